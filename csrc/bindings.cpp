@@ -1,0 +1,65 @@
+// Python bindings of the sm_100a kernel library (module graspo_b200._C).
+#include <torch/extension.h>
+
+namespace gb {
+void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
+             c10::optional<torch::Tensor> B2, torch::Tensor C, c10::optional<torch::Tensor> R,
+             c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> targets,
+             c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
+             c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
+             int64_t splits, torch::Tensor err, int64_t max_ctas);
+void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta, c10::optional<torch::Tensor> h_out,
+                 torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> rstd,
+                 c10::optional<torch::Tensor> lora_a, c10::optional<torch::Tensor> lora_u, double scale,
+                 double eps);
+void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> rstd,
+                 c10::optional<torch::Tensor> dres, torch::Tensor dx, double eps);
+void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
+                  torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
+                  c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
+                  int64_t nq, int64_t nkv, int64_t page_size, double eps);
+void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
+                      torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq, torch::Tensor pos,
+                      torch::Tensor dqkv, int64_t nq, int64_t nkv, double eps);
+void swiglu_bwd(torch::Tensor gu, torch::Tensor dh, torch::Tensor dgu);
+void lora_down(torch::Tensor x, torch::Tensor A, torch::Tensor U, double scale);
+void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
+void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
+                            torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
+                            torch::Tensor out, double scale);
+void sample_append(torch::Tensor logits, double temperature, double top_p, int64_t seed,
+                   torch::Tensor next_ids, torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len,
+                   torch::Tensor finished, torch::Tensor out_tokens, int64_t prompt_slots,
+                   int64_t eos_id, int64_t pad_id, bool ignore_eos, c10::optional<torch::Tensor> active);
+void lse_combine(torch::Tensor partials, torch::Tensor tgt, torch::Tensor lse, torch::Tensor logp);
+void grpo_loss(torch::Tensor logp, torch::Tensor old_logp, torch::Tensor adv, torch::Tensor mask,
+               double clip_eps, double grad_scale, torch::Tensor loss, torch::Tensor dlogp,
+               c10::optional<torch::Tensor> stats);
+void dropout(torch::Tensor x, torch::Tensor y, double p, int64_t seed, int64_t stream_id,
+             c10::optional<torch::Tensor> add);
+void grad_sumsq(torch::Tensor g, torch::Tensor out);
+void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, double lr, double b1,
+           double b2, double eps, double wd, int64_t step, torch::Tensor sumsq, double max_norm,
+           c10::optional<torch::Tensor> loss, c10::optional<torch::Tensor> skipped);
+void transpose_bf16(torch::Tensor in, torch::Tensor out);
+}  // namespace gb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "graspo_b200 sm_100a kernels";
+  m.def("gemm_tc", &gb::gemm_tc, "tcgen05 GEMM with fused epilogues");
+  m.def("add_rmsnorm", &gb::add_rmsnorm);
+  m.def("rmsnorm_bwd", &gb::rmsnorm_bwd);
+  m.def("qk_norm_rope", &gb::qk_norm_rope);
+  m.def("qk_norm_rope_bwd", &gb::qk_norm_rope_bwd);
+  m.def("swiglu_bwd", &gb::swiglu_bwd);
+  m.def("lora_down", &gb::lora_down);
+  m.def("embedding", &gb::embedding);
+  m.def("paged_decode_attention", &gb::paged_decode_attention);
+  m.def("sample_append", &gb::sample_append);
+  m.def("lse_combine", &gb::lse_combine);
+  m.def("grpo_loss", &gb::grpo_loss);
+  m.def("dropout", &gb::dropout);
+  m.def("grad_sumsq", &gb::grad_sumsq);
+  m.def("adamw", &gb::adamw);
+  m.def("transpose_bf16", &gb::transpose_bf16);
+}

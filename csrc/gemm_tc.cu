@@ -1,0 +1,129 @@
+// Host entry of the tcgen05 GEMM: argument checks, tensor-map encoding and
+// dispatch to the instantiation for the requested tile width / epilogue.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_tc.cuh"
+
+namespace gb {
+
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Tensor map for a row-major bf16 matrix [rows, cols] with row stride `ld`
+// elements, loaded in boxes of [box_rows, 64] with the 128-byte swizzle.
+CUtensorMap make_tmap_bf16(const void* ptr, long rows, long cols, long ld, int box_rows) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return map;
+}
+
+static void check_operand(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16, name, " must be a CUDA bf16 tensor");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+}
+
+// Generic entry: see module docstring for the meaning of each epilogue.
+void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
+             c10::optional<torch::Tensor> B2, torch::Tensor C, c10::optional<torch::Tensor> R,
+             c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> targets,
+             c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
+             c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
+             int64_t splits, torch::Tensor err, int64_t max_ctas) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  TORCH_CHECK(A.size(1) == B.size(1), "A and B must share K");
+  // K need not be a multiple of 64: TMA zero-fills the tail of the last K-block.
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int device = A.get_device();
+  GemmArgs args{};
+  args.M = static_cast<int>(A.size(0));
+  args.N = static_cast<int>(B.size(0));
+  args.kb_main = static_cast<int>((A.size(1) + BK - 1) / BK);
+  args.kb_ext = 0;
+  args.splits = static_cast<int>(std::max<int64_t>(splits, 1));
+  args.C = C.data_ptr();
+  args.ldc = C.stride(0);
+  args.err = err.data_ptr<int>();
+  const int box_a = BM;
+  const int box_b = static_cast<int>(bn);
+  CUtensorMap ta = make_tmap_bf16(A.data_ptr(), A.size(0), A.size(1), A.stride(0), box_a);
+  CUtensorMap tb = make_tmap_bf16(B.data_ptr(), B.size(0), B.size(1), B.stride(0), box_b);
+  CUtensorMap ta2 = ta, tb2 = tb;
+  if (A2.has_value() && A2->defined()) {
+    TORCH_CHECK(B2.has_value() && B2->defined(), "A2 requires B2");
+    check_operand(*A2, "A2");
+    check_operand(*B2, "B2");
+    TORCH_CHECK(A2->size(1) == B2->size(1), "extension K must match");
+    TORCH_CHECK(A2->size(0) == A.size(0) && B2->size(0) == B.size(0), "extension operands must match M and N");
+    args.kb_ext = static_cast<int>((A2->size(1) + BK - 1) / BK);
+    ta2 = make_tmap_bf16(A2->data_ptr(), A2->size(0), A2->size(1), A2->stride(0), box_a);
+    tb2 = make_tmap_bf16(B2->data_ptr(), B2->size(0), B2->size(1), B2->stride(0), box_b);
+  }
+  if (R.has_value() && R->defined()) {
+    args.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    args.ldr = R->stride(0);
+  }
+  if (aux.has_value() && aux->defined()) {
+    args.aux = aux->data_ptr();
+    args.ldaux = aux->stride(0);
+    if (epilogue == kLSE) args.ldaux = aux->stride(0) / 2;  // float2 units
+  }
+  if (targets.has_value() && targets->defined()) args.targets = targets->data_ptr<int64_t>();
+  if (tgt_logit.has_value() && tgt_logit->defined()) args.tgt_logit = tgt_logit->data_ptr<float>();
+  if (row_lse.has_value() && row_lse->defined()) args.row_lse = row_lse->data_ptr<float>();
+  if (row_scale.has_value() && row_scale->defined()) args.row_scale = row_scale->data_ptr<float>();
+  if (epilogue == kLSE || epilogue == kSoftmaxGrad)
+    TORCH_CHECK(args.targets != nullptr, "log-prob epilogues need targets");
+  if (epilogue == kLSE) TORCH_CHECK(args.tgt_logit != nullptr && args.aux != nullptr, "LSE epilogue needs aux and tgt_logit");
+  if (epilogue == kSoftmaxGrad) TORCH_CHECK(args.row_lse != nullptr && args.row_scale != nullptr, "softmax-grad epilogue needs lse and scale");
+  TORCH_CHECK(epilogue == kAtomicF32 || args.splits == 1, "split-K requires the atomic epilogue");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int mc = static_cast<int>(max_ctas);
+  TORCH_CHECK(!swap || (epilogue != kLSE && epilogue != kSoftmaxGrad), "log-prob epilogues are not available in swap mode");
+  GemmLauncher fn = nullptr;
+  if (swap) {
+    fn = gemm_launcher_swap(static_cast<int>(bn), static_cast<int>(epilogue));
+  } else if (bn == 256) {
+    fn = gemm_launcher_n256(static_cast<int>(epilogue));
+  } else if (bn == 128) {
+    fn = gemm_launcher_n128(static_cast<int>(epilogue));
+  } else if (bn == 64) {
+    fn = gemm_launcher_n64(static_cast<int>(epilogue));
+  }
+  TORCH_CHECK(fn != nullptr, "no GEMM instantiation for bn=", bn, " swap=", swap, " epilogue=", epilogue);
+  fn(ta, tb, ta2, tb2, args, mc, stream, device);
+}
+
+}  // namespace gb

@@ -1,0 +1,496 @@
+#pragma once
+// Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+//
+//   C[M, N] = A[M, K] * B[N, K]^T  (+ A2[M, K2] * B2[N, K2]^T)   fp32 accumulate
+//
+// Both operands are K-major (row-major with K contiguous).  The optional
+// second pair (A2, B2) extends the reduction: this is how a rank-r LoRA update
+// s * (x A^T) B^T is folded into the frozen base GEMM x W^T -- the caller passes
+// U = s * x A^T as A2 and the LoRA B factor as B2, so the adapter costs one or
+// two extra K-blocks of MMA instead of a separate GEMM and an extra pass over
+// the output.
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0      TMA producer: streams 128x64 A tiles and BNx64 B tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle).
+//   warp 1      TMEM allocator + MMA issuer: one elected thread issues
+//               tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
+//               accumulators and commits completion to mbarriers.
+//   warps 2-5   epilogue: tcgen05.ld the finished accumulator (each warp owns
+//               its 32-lane TMEM quarter), apply the fused epilogue, store.
+// Double-buffered accumulators let the epilogue of tile i overlap the
+// main loop of tile i+1.  Work units are (tile, K-split) pairs walked in a
+// grouped raster so concurrently running CTAs share A and B tiles in L2.
+//
+// Epilogues:
+//   kStoreBF16     C = acc (+ R)                        bf16
+//   kSwiGLU        B rows interleave (gate_j, up_j): C[:, j] = silu(g) * u,
+//                  optionally also stores the raw (g, u) pairs to `aux`
+//   kAtomicF32     C += acc (fp32 red.add; split-K partial sums)
+//   kLSE           per row: (max, sum exp) of this tile's columns < N into
+//                  aux[row, n_block]; logit of targets[row] if it falls here
+//   kStoreF32      C = acc fp32
+//   kSoftmaxGrad   C = g[row] * (onehot(targets[row]) - exp(acc - lse[row]))  bf16;
+//                  the gradient of selected-token log-probs w.r.t. the logits,
+//                  produced without materialising the logits
+// SWAP=true stores the transpose (C[n, m]); used for small-M decode GEMMs
+// that run "swap-AB" (weights as the 128-row operand, tokens as N).
+//
+// No TMA multicast is used anywhere (every CTA loads its own tiles).
+
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <algorithm>
+
+#include "sm100_common.cuh"
+
+namespace gb {
+
+enum Epilogue : int { kStoreBF16 = 0, kSwiGLU = 1, kAtomicF32 = 2, kLSE = 3, kStoreF32 = 4, kSoftmaxGrad = 5 };
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 8;
+
+struct GemmArgs {
+  int M, N;
+  int kb_main;   // K-blocks from (A, B)
+  int kb_ext;    // K-blocks from (A2, B2)
+  int splits;    // split-K factor (kAtomicF32 only)
+  void* C;
+  long ldc;
+  const __nv_bfloat16* R;  // optional residual for kStoreBF16
+  long ldr;
+  void* aux;
+  long ldaux;
+  const int64_t* targets;  // kLSE, kSoftmaxGrad
+  float* tgt_logit;        // kLSE
+  const float* row_lse;    // kSoftmaxGrad
+  const float* row_scale;  // kSoftmaxGrad
+  int* err;
+};
+
+template <int BN_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct Unit {
+  int m_block, n_block, kb_begin, kb_end;
+};
+
+__device__ __forceinline__ Unit decode_unit(int u, int num_m, int num_n, int splits, int kb_total) {
+  const int tile = u / splits;
+  const int split = u - tile * splits;
+  const int group = kGroupM * num_n;
+  const int g = tile / group;
+  const int first_m = g * kGroupM;
+  const int gm = min(num_m - first_m, kGroupM);
+  const int in_group = tile - g * group;
+  Unit r;
+  r.m_block = first_m + in_group % gm;
+  r.n_block = in_group / gm;
+  const int per = (kb_total + splits - 1) / splits;
+  r.kb_begin = split * per;
+  r.kb_end = min(kb_total, r.kb_begin + per);
+  return r;
+}
+
+template <int BN, int EPI, bool SWAP>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
+  using C_ = Cfg<BN>;
+  constexpr int STAGES = C_::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment is required by the 128-byte swizzle atoms.
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + STAGES * C_::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int num_m = (args.M + BM - 1) / BM;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int kb_total = args.kb_main + args.kb_ext;
+  const int units = num_m * num_n * args.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 128);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C_::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      if (args.kb_ext > 0) {
+        tma_prefetch_desc(&tmA2);
+        tma_prefetch_desc(&tmB2);
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrSmemEmptyTimeout)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+          uint8_t* a_dst = smA + stage * C_::A_BYTES;
+          uint8_t* b_dst = smB + stage * C_::B_BYTES;
+          if (kb < args.kb_main) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, w.m_block * BM);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, w.n_block * BN);
+          } else {
+            const int ke = kb - args.kb_main;
+            tma_load_2d(a_dst, &tmA2, &full[stage], ke * BK, w.m_block * BM);
+            tma_load_2d(b_dst, &tmB2, &full[stage], ke * BK, w.n_block * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: wait (bounded) until every stage we filled has been consumed so
+      // no TMA write into this CTA's shared memory is still in flight at exit.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrSmemEmptyTimeout)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc_iter = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+        if (w.kb_end <= w.kb_begin) continue;
+        const int acc = acc_iter & 1;
+        const uint32_t acc_phase = (acc_iter >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, args.err, kErrTmemEmptyTimeout)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrTmaFullTimeout)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a_desc = umma_desc_k_sw128(smem_addr(smA + stage * C_::A_BYTES));
+          const uint64_t b_desc = umma_desc_k_sw128(smem_addr(smB + stage * C_::B_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 elements (32 bytes) along K inside the swizzled row
+            umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc,
+                      (kb > w.kb_begin || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        ++acc_iter;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;          // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc_iter = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+      if (w.kb_end <= w.kb_begin) continue;
+      const int acc = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrTmemFullTimeout)) break;
+      tc_fence_after();
+      const int m = w.m_block * BM + row_in_tile;
+      const int n0 = w.n_block * BN;
+      const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      float run_max = -INFINITY, run_sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(t_row + c * 32, v);
+        const int nc = n0 + c * 32;
+        if constexpr (SWAP) {
+          // lane <-> output feature m, column <-> token n; store C[n, m]
+          if constexpr (EPI == kAtomicF32) {
+            float* C = static_cast<float*>(args.C);
+            if (m < args.M) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) atomicAdd(C + static_cast<long>(nc + j) * args.ldc + m, v[j]);
+            }
+          } else if constexpr (EPI == kStoreBF16) {
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C);
+            if (m < args.M) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (nc + j < args.N) {
+                  float x = v[j];
+                  if (args.R != nullptr) x += __bfloat162float(args.R[static_cast<long>(nc + j) * args.ldr + m]);
+                  C[static_cast<long>(nc + j) * args.ldc + m] = __float2bfloat16(x);
+                }
+              }
+            }
+          } else if constexpr (EPI == kSwiGLU) {
+            // adjacent lanes hold (gate_j, up_j); even lanes write silu(g)*u
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float partner = __shfl_xor_sync(0xffffffffu, v[j], 1);
+              if ((lane & 1) == 0 && m < args.M && nc + j < args.N) {
+                C[static_cast<long>(nc + j) * args.ldc + (m >> 1)] =
+                    __float2bfloat16(silu_f(v[j]) * partner);
+              }
+            }
+          } else if constexpr (EPI == kStoreF32) {
+            float* C = static_cast<float*>(args.C);
+            if (m < args.M) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) C[static_cast<long>(nc + j) * args.ldc + m] = v[j];
+            }
+          }
+        } else {
+          if (m >= args.M) {
+            if constexpr (EPI == kLSE) { /* keep tcgen05.ld convergent; nothing to write */ }
+            continue;
+          }
+          const bool full_chunk = (nc + 32 <= args.N);
+          if constexpr (EPI == kStoreBF16) {
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C) + static_cast<long>(m) * args.ldc + nc;
+            if (args.R != nullptr) {
+              const __nv_bfloat16* R = args.R + static_cast<long>(m) * args.ldr + nc;
+              if (full_chunk) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  uint4 rv = *reinterpret_cast<const uint4*>(R + q * 8);
+                  const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) v[q * 8 + e] += __bfloat162float(rb[e]);
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (nc + j < args.N) v[j] += __bfloat162float(R[j]);
+              }
+            }
+            if (full_chunk) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 pk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(C + q * 8) = pk;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) C[j] = __float2bfloat16(v[j]);
+            }
+          } else if constexpr (EPI == kStoreF32) {
+            float* C = static_cast<float*>(args.C) + static_cast<long>(m) * args.ldc + nc;
+            if (full_chunk) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                *reinterpret_cast<float4*>(C + q * 4) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) C[j] = v[j];
+            }
+          } else if constexpr (EPI == kAtomicF32) {
+            float* C = static_cast<float*>(args.C) + static_cast<long>(m) * args.ldc + nc;
+            for (int j = 0; j < 32; ++j)
+              if (nc + j < args.N) atomicAdd(C + j, v[j]);
+          } else if constexpr (EPI == kSwiGLU) {
+            // columns (2i, 2i+1) = (gate_i, up_i) -> out column (nc/2 + i)
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C) + static_cast<long>(m) * args.ldc + (nc >> 1);
+            if (args.aux != nullptr) {
+              __nv_bfloat16* G = static_cast<__nv_bfloat16*>(args.aux) + static_cast<long>(m) * args.ldaux + nc;
+              if (full_chunk) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  uint4 pk;
+                  __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                  *reinterpret_cast<uint4*>(G + q * 8) = pk;
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (nc + j < args.N) G[j] = __float2bfloat16(v[j]);
+              }
+            }
+            if (full_chunk) {
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                uint4 pk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int i0 = q * 16 + 4 * e;
+                  // the GEMM accumulates in fp32; the activation is applied to
+                  // the bf16-rounded pre-activations so forward and backward see
+                  // the same (g, u) values that are stored to `aux`
+                  const float g0 = __bfloat162float(__float2bfloat16(v[i0]));
+                  const float u0 = __bfloat162float(__float2bfloat16(v[i0 + 1]));
+                  const float g1 = __bfloat162float(__float2bfloat16(v[i0 + 2]));
+                  const float u1 = __bfloat162float(__float2bfloat16(v[i0 + 3]));
+                  p2[e] = __floats2bfloat162_rn(silu_f(g0) * u0, silu_f(g1) * u1);
+                }
+                *reinterpret_cast<uint4*>(C + q * 8) = pk;
+              }
+            } else {
+              for (int j = 0; j + 1 < 32; j += 2)
+                if (nc + j + 1 < args.N) {
+                  const float g = __bfloat162float(__float2bfloat16(v[j]));
+                  const float uu = __bfloat162float(__float2bfloat16(v[j + 1]));
+                  C[j >> 1] = __float2bfloat16(silu_f(g) * uu);
+                }
+            }
+          } else if constexpr (EPI == kSoftmaxGrad) {
+            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C) + static_cast<long>(m) * args.ldc + nc;
+            const float l = args.row_lse[m];
+            const float gs = args.row_scale[m];
+            const long tgt = args.targets[m];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gs * (((nc + j) == tgt ? 1.f : 0.f) - __expf(v[j] - l));
+            if (full_chunk) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 pk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(C + q * 8) = pk;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) C[j] = __float2bfloat16(v[j]);
+            }
+          } else if constexpr (EPI == kLSE) {
+            float cmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (nc + j < args.N) cmax = fmaxf(cmax, v[j]);
+            if (cmax > -INFINITY) {
+              const float new_max = fmaxf(run_max, cmax);
+              float s = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (nc + j < args.N) s += __expf(v[j] - new_max);
+              run_sum = run_sum * __expf(run_max - new_max) + s;
+              run_max = new_max;
+            }
+            const long tgt = args.targets[m];
+            if (tgt >= nc && tgt < nc + 32) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (tgt == nc + j) args.tgt_logit[m] = v[j];
+            }
+          }
+        }
+      }
+      if constexpr (EPI == kLSE && !SWAP) {
+        if (m < args.M) {
+          float2* P = static_cast<float2*>(args.aux) + static_cast<long>(m) * args.ldaux + w.n_block;
+          *P = make_float2(run_max, run_sum);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      ++acc_iter;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+inline int num_sms(int device) {
+  static int cached[64] = {0};
+  if (cached[device] == 0) {
+    cudaDeviceGetAttribute(&cached[device], cudaDevAttrMultiProcessorCount, device);
+  }
+  return cached[device];
+}
+
+template <int BN, int EPI, bool SWAP>
+void launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2,
+                        const CUtensorMap& b2, const GemmArgs& args, int max_ctas,
+                        cudaStream_t stream, int device) {
+  auto kern = gemm_tc_kernel<BN, EPI, SWAP>;
+  static bool configured[64] = {false};
+  if (!configured[device]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
+    configured[device] = true;
+  }
+  const int num_m = (args.M + BM - 1) / BM;
+  const int num_n = (args.N + BN - 1) / BN;
+  const int units = num_m * num_n * args.splits;
+  int grid = std::min(units, num_sms(device));
+  if (max_ctas > 0) grid = std::min(grid, max_ctas);
+  grid = std::max(grid, 1);
+  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, stream>>>(a, b, a2, b2, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+using GemmLauncher = void (*)(const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                              const GemmArgs&, int, cudaStream_t, int);
+
+// Defined in the gemm_inst_*.cu translation units (compiled in parallel).
+GemmLauncher gemm_launcher_n256(int epi);
+GemmLauncher gemm_launcher_n128(int epi);
+GemmLauncher gemm_launcher_n64(int epi);
+GemmLauncher gemm_launcher_swap(int bn, int epi);
+
+}  // namespace gb

@@ -1,0 +1,149 @@
+"""Kernel micro-benchmarks: CUDA-event timing, warm-up, L2 flush between runs.
+
+``python -m graspo_b200.bench.kernels gemm`` times the tcgen05 GEMM on the
+Qwen3-8B projection shapes next to ``torch.matmul`` (cuBLAS) on the same
+inputs and prints one JSON line per case with achieved TFLOP/s and the
+fraction of the measured bf16 peak.  ``decode`` times the swap-AB decode GEMMs
+and the paged decode attention as bytes/s against the measured copy bandwidth.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def measured_peaks() -> dict:
+    path = Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "fallback": True}
+
+
+class Timer:
+    def __init__(self, warmup: int = 3, iters: int = 10, flush: bool = True) -> None:
+        self.warmup, self.iters, self.flush = warmup, iters, flush
+        self._buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda") if flush else None
+
+    def __call__(self, fn) -> float:
+        """Median milliseconds of ``fn()`` over ``iters`` runs."""
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(self.iters):
+            if self._buf is not None:
+                self._buf.zero_()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            torch.cuda.synchronize()
+            times.append(start.elapsed_time(end))
+        times.sort()
+        return times[len(times) // 2]
+
+
+def bench_gemm(args) -> None:
+    from graspo_b200.ops._ext import check_errors
+    from graspo_b200.ops.gemm import gemm
+
+    peaks = measured_peaks()
+    timer = Timer(iters=args.iters)
+    shapes = [
+        ("qkv", 8192, 6144, 4096),
+        ("o", 8192, 4096, 4096),
+        ("gate_up", 8192, 24576, 4096),
+        ("down", 8192, 4096, 12288),
+        ("train_qkv", 24576, 6144, 4096),
+        ("train_gate_up", 24576, 24576, 4096),
+        ("lm_head", 8192, 151936, 4096),
+    ]
+    for name, m, n, k in shapes:
+        a = torch.randn(m, k, device="cuda").bfloat16()
+        b = torch.randn(n, k, device="cuda").bfloat16()
+        c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        flops = 2.0 * m * n * k
+        ours = timer(lambda: gemm(a, b, c))
+        ref = timer(lambda: torch.matmul(a, b.T, out=c))
+        check_errors()
+        print(json.dumps({
+            "kernel": "gemm_tc", "case": name, "m": m, "n": n, "k": k,
+            "ms": round(ours, 4), "tflops": round(flops / ours / 1e9, 1),
+            "frac_of_measured_bf16": round(flops / ours / 1e9 / peaks["bf16_tflops"], 3),
+            "cublas_ms": round(ref, 4), "cublas_tflops": round(flops / ref / 1e9, 1),
+            "speedup_vs_cublas": round(ref / ours, 3),
+        }), flush=True)
+        del a, b, c
+
+
+def bench_decode(args) -> None:
+    from graspo_b200.ops._ext import check_errors, ext
+    from graspo_b200.ops.gemm import gemm
+
+    peaks = measured_peaks()
+    timer = Timer(iters=args.iters)
+    T = args.tokens
+    for name, n, k, splits in [("qkv", 6144, 4096, 3), ("o", 4096, 4096, 4), ("gate_up", 24576, 4096, 1),
+                               ("down", 4096, 12288, 4), ("lm_head", 151936, 4096, 1)]:
+        w = torch.randn(n, k, device="cuda").bfloat16()
+        x = torch.randn(T, k, device="cuda").bfloat16()
+        if splits > 1:
+            out = torch.zeros(T, n, device="cuda")
+            fn = lambda: gemm(w, x, out, swap=True, epilogue="atomic", splits=splits)  # noqa: E731
+        else:
+            out = torch.empty(T, n, device="cuda", dtype=torch.float32 if name == "lm_head" else torch.bfloat16)
+            epi = "store_f32" if name == "lm_head" else "store"
+            fn = lambda: gemm(w, x, out, swap=True, epilogue=epi)  # noqa: E731
+        ms = timer(fn)
+        ref = timer(lambda: torch.matmul(x, w.T))
+        check_errors()
+        nbytes = n * k * 2 + T * k * 2
+        print(json.dumps({
+            "kernel": "gemm_tc_swap", "case": name, "tokens": T, "n": n, "k": k, "splits": splits,
+            "ms": round(ms, 4), "GBps": round(nbytes / ms / 1e6, 1),
+            "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
+            "cublas_ms": round(ref, 4),
+        }), flush=True)
+    # paged decode attention: rows x context
+    nq, nkv, D, page = 32, 8, 128, 64
+    for ctx in (1024, 2048, 3072):
+        rows = T
+        pages_per_row = math.ceil(ctx / page)
+        num_pages = rows * pages_per_row
+        kp = torch.randn(num_pages, nkv, page, D, device="cuda").bfloat16()
+        vp = torch.randn_like(kp)
+        bt = torch.arange(num_pages, device="cuda", dtype=torch.int32).view(rows, pages_per_row)
+        q = torch.randn(rows, nq, D, device="cuda").bfloat16()
+        start = torch.zeros(rows, device="cuda", dtype=torch.int32)
+        ln = torch.full((rows,), ctx, device="cuda", dtype=torch.int32)
+        out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+        ms = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D)))
+        nbytes = 2 * rows * ctx * nkv * D * 2
+        print(json.dumps({
+            "kernel": "paged_decode_attention", "rows": rows, "ctx": ctx, "ms": round(ms, 4),
+            "GBps": round(nbytes / ms / 1e6, 1),
+            "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
+        }), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("what", choices=["gemm", "decode", "all"])
+    parser.add_argument("--iters", type=int, default=10)
+    parser.add_argument("--tokens", type=int, default=64)
+    args = parser.parse_args()
+    if args.what in ("gemm", "all"):
+        bench_gemm(args)
+    if args.what in ("decode", "all"):
+        bench_decode(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,330 @@
+"""Fused sm_100a execution of the Qwen3 decoder (forward, backward, log-probs).
+
+Per decoder layer the forward is ~10 kernels:
+
+    add_rmsnorm -> [dropout] -> U = x A^T (tcgen05, N=64) -> QKV GEMM with the
+    LoRA update folded into its K loop -> qk_norm_rope -> attention ->
+    O GEMM (+LoRA, + residual in the epilogue) -> add_rmsnorm ->
+    gate/up GEMM (+LoRA, SwiGLU epilogue) -> down GEMM (+LoRA, + residual)
+
+Training uses whole-layer recomputation: the forward keeps only each layer's
+input; the backward re-runs the layer keeping its intermediates, then runs
+the backward kernels.  LoRA gradients are tensor-core reductions over tokens
+(``dB = dY^T U``, ``dA = s * dU^T X``) written straight into the adapter's
+flat fp32 gradient buffer.  Under tensor parallelism the input gradients of
+column-parallel projections are all-reduced over the TP group (the conjugate
+of the forward all-reduce after row-parallel projections).
+
+The selected-token log-prob never materialises logits: the LM-head GEMM's
+epilogue emits per-tile (max, sum-exp) partials, a small kernel merges them
+(and, with a vocab-parallel head, an all-reduce merges the TP shards); the
+backward recomputes each logit tile and writes ``g * (onehot - softmax)``
+directly from the epilogue.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from graspo_b200.models.qwen3 import LayerWeights, Qwen3Model
+from graspo_b200.ops import attention as attn_ops
+from graspo_b200.ops._ext import ext
+from graspo_b200.ops.gemm import gemm
+
+# dropout stream ids: layer * 8 + site
+_DROP_SITES = {"qkv": 0, "o": 1, "gu": 2, "down": 3}
+
+
+def _tp_all_reduce(x: torch.Tensor, group) -> torch.Tensor:
+    if group is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(x, group=group)
+    return x
+
+
+def _t(x: torch.Tensor) -> torch.Tensor:
+    """K-major transpose for token-reduction GEMMs (row stride padded to 8)."""
+    rows, cols = x.shape
+    buf = torch.empty(cols, (rows + 7) // 8 * 8, dtype=x.dtype, device=x.device)
+    out = buf[:, :rows]
+    ext().transpose_bf16(x, out)
+    return out
+
+
+@dataclass
+class AttnMeta:
+    """Token layout of a padded batch: B sequences of S tokens, flattened."""
+
+    B: int
+    S: int
+    key_mask: torch.Tensor      # [B, S] bool, valid tokens
+    pos: torch.Tensor           # [B*S] int64 rope positions
+
+    @staticmethod
+    def from_mask(mask: torch.Tensor) -> "AttnMeta":
+        m = mask.bool()
+        pos = (m.long().cumsum(-1) - 1).masked_fill(~m, 0)
+        return AttnMeta(B=m.shape[0], S=m.shape[1], key_mask=m, pos=pos.reshape(-1).contiguous())
+
+
+class LayerSaved:
+    __slots__ = ("x", "xn", "rstd1", "xd", "u_qkv", "qkv", "q", "k", "v", "attn", "attn_d", "u_o",
+                 "x1", "xn2", "rstd2", "xd2", "u_gu", "gu", "act", "act_d", "u_d", "attn_ctx")
+
+
+class FusedQwen3:
+    def __init__(self, model: Qwen3Model) -> None:
+        self.m = model
+        self.C = ext()
+        self.eps = model.cfg.rms_norm_eps
+        self.scale = 1.0 / math.sqrt(model.D)
+
+    # ------------------------------------------------------------ helpers
+    def _dropout(self, x, site: str, layer: int, seed: int, train: bool):
+        p = self.m.lora.dropout
+        if not train or p <= 0:
+            return x
+        y = torch.empty_like(x)
+        self.C.dropout(x, y, p, seed, layer * 8 + _DROP_SITES[site], None)
+        return y
+
+    def _dropout_add(self, x, base, site, layer, seed):
+        """base + mask(x) with the forward's mask (in place into base)."""
+        self.C.dropout(x, base, self.m.lora.dropout, seed, layer * 8 + _DROP_SITES[site], base)
+
+    def _layouts(self, lw: LayerWeights):
+        return self.m.lora.layer_layouts(lw.index, self.m.sizes)
+
+    # ------------------------------------------------------------ forward
+    def layer_forward(self, lw: LayerWeights, x: torch.Tensor, meta: AttnMeta, *, train: bool = False,
+                      seed: int = 0, save: bool = False, kv_sink=None):
+        m, C, L = self.m, self.C, self._layouts(lw)
+        tp_group = m.ps.tp_group
+        tp = m.ps.tp_size
+        T, H = x.shape
+        s = LayerSaved() if save else None
+        xn = torch.empty_like(x)
+        rstd1 = torch.empty(T, device=x.device, dtype=torch.float32)
+        C.add_rmsnorm(x, None, None, lw.ln1, xn, rstd1, None, None, 1.0, self.eps)
+        ext_qkv = None
+        if "a_qkv" in L:
+            xd = self._dropout(xn, "qkv", lw.index, seed, train)
+            u_qkv = gemm(xd, L["a_qkv"], bn=64)
+            ext_qkv = (u_qkv, L["b_qkv"])
+        qkv = gemm(xn, lw.w_qkv, ext_ab=ext_qkv)
+        q = torch.empty(T, m.nq, m.D, device=x.device, dtype=x.dtype)
+        k = torch.empty(T, m.nkv, m.D, device=x.device, dtype=x.dtype)
+        v = torch.empty_like(k)
+        C.qk_norm_rope(qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, q, k, v, None, None, m.nq, m.nkv, 0, self.eps)
+        if kv_sink is not None:
+            kv_sink(lw.index, k, v)
+        attn, ctx = attn_ops.attention_forward(q, k, v, meta, self.scale, need_ctx=save)
+        ext_o = None
+        if "a_o" in L:
+            attn_d = self._dropout(attn, "o", lw.index, seed, train)
+            u_o = gemm(attn_d, L["a_o"], bn=64)
+            ext_o = (u_o, L["b_o"])
+        x1 = torch.empty_like(x)
+        xn2 = torch.empty_like(x)
+        rstd2 = torch.empty(T, device=x.device, dtype=torch.float32)
+        if tp == 1:
+            gemm(attn, lw.w_o, x1, ext_ab=ext_o, residual=x)
+            C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
+        else:
+            o = gemm(attn, lw.w_o, ext_ab=ext_o)
+            _tp_all_reduce(o, tp_group)
+            C.add_rmsnorm(x, o, x1, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
+        ext_gu = None
+        if "a_gu" in L:
+            xd2 = self._dropout(xn2, "gu", lw.index, seed, train)
+            u_gu = gemm(xd2, L["a_gu"], bn=64)
+            ext_gu = (u_gu, L["b_gu"])
+        gu = torch.empty(T, 2 * m.inter_local, device=x.device, dtype=x.dtype) if save else None
+        act = gemm(xn2, lw.w_gu, ext_ab=ext_gu, epilogue="swiglu", aux=gu)
+        ext_d = None
+        if "a_down" in L:
+            act_d = self._dropout(act, "down", lw.index, seed, train)
+            u_d = gemm(act_d, L["a_down"], bn=64)
+            ext_d = (u_d, L["b_down"])
+        if tp == 1:
+            x2 = gemm(act, lw.w_down, ext_ab=ext_d, residual=x1)
+        else:
+            d = gemm(act, lw.w_down, ext_ab=ext_d)
+            _tp_all_reduce(d, tp_group)
+            x2 = (x1.float() + d.float()).to(x.dtype)
+        if save:
+            s.x, s.xn, s.rstd1, s.qkv, s.q, s.k, s.v, s.attn = x, xn, rstd1, qkv, q, k, v, attn
+            s.x1, s.xn2, s.rstd2, s.gu, s.act, s.attn_ctx = x1, xn2, rstd2, gu, act, ctx
+            s.xd = xd if ext_qkv else None
+            s.u_qkv = ext_qkv[0] if ext_qkv else None
+            s.attn_d = attn_d if ext_o else None
+            s.u_o = ext_o[0] if ext_o else None
+            s.xd2 = xd2 if ext_gu else None
+            s.u_gu = ext_gu[0] if ext_gu else None
+            s.act_d = act_d if ext_d else None
+            s.u_d = ext_d[0] if ext_d else None
+        return x2, s
+
+    # ------------------------------------------------------------ backward
+    def _lora_linear_backward(self, dy, w_t, saved_u, saved_xd, b_ext, a_ext, site, layer, seed, train):
+        """d(input) of y = x W^T + U B^T with U = drop(x) (sA)^T, plus LoRA grads.
+
+        Returns (dx, db_full [N, 64k] fp32, da_full [64k, K] fp32) -- the
+        gradient w.r.t. the padded layouts (caller scatters into parameters).
+        """
+        if saved_u is None:
+            return gemm(dy, w_t), None, None
+        b_t = b_ext.t().contiguous()                      # [64k, N]
+        du = gemm(dy, b_t, bn=64)                          # [T, 64k]
+        a_t = a_ext.t().contiguous()                      # [K, 64k]
+        p = self.m.lora.dropout
+        if train and p > 0:
+            dx = gemm(dy, w_t)
+            tmp = gemm(du, a_t)
+            self._dropout_add(tmp, dx, site, layer, seed)
+        else:
+            dx = gemm(dy, w_t, ext_ab=(du, a_t))
+        db = gemm(_t(dy), _t(saved_u), epilogue="store_f32", bn=64)      # [N, 64k]
+        da = gemm(_t(du), _t(saved_xd), epilogue="store_f32")             # [64k, K]
+        return dx, db, da
+
+    def _scatter_grads(self, layer: int, group: str, db, da) -> None:
+        ad = self.m.lora
+        r, s = ad.r, ad.scaling
+        if group == "qkv":
+            rows = [("q", self.m.q_local), ("k", self.m.kv_local), ("v", self.m.kv_local)]
+            row = 0
+            for slot, (kind, n) in enumerate(rows):
+                mod = ad.module(layer, kind)
+                if mod is not None:
+                    mod.b_grad += db[row : row + n, slot * r : (slot + 1) * r]
+                    mod.a_grad += s * da[slot * r : (slot + 1) * r]
+                row += n
+        elif group == "gu":
+            for slot, kind in enumerate(("gate", "up")):
+                mod = ad.module(layer, kind)
+                if mod is not None:
+                    mod.b_grad += db[slot::2, slot * r : (slot + 1) * r]
+                    mod.a_grad += s * da[slot * r : (slot + 1) * r]
+        else:
+            mod = ad.module(layer, group)
+            if mod is not None:
+                mod.b_grad += db[:, :r]
+                mod.a_grad += s * da[:r]
+
+    def layer_backward(self, lw: LayerWeights, s: LayerSaved, dx2: torch.Tensor, meta: AttnMeta, *,
+                       train: bool, seed: int) -> torch.Tensor:
+        m, C, L = self.m, self.C, self._layouts(lw)
+        tp_group = m.ps.tp_group
+        li = lw.index
+        # --- down projection
+        dact, db, da = self._lora_linear_backward(dx2, lw.w_down_t, s.u_d, s.act_d, L.get("b_down"),
+                                                  L.get("a_down"), "down", li, seed, train)
+        if db is not None:
+            self._scatter_grads(li, "down", db, da)
+        # --- SwiGLU
+        dgu = torch.empty_like(s.gu)
+        C.swiglu_bwd(s.gu, dact, dgu)
+        del dact
+        # --- gate/up
+        dxn2, db, da = self._lora_linear_backward(dgu, lw.w_gu_t, s.u_gu, s.xd2, L.get("b_gu"), L.get("a_gu"),
+                                                  "gu", li, seed, train)
+        if db is not None:
+            self._scatter_grads(li, "gu", db, da)
+        del dgu
+        _tp_all_reduce(dxn2, tp_group)
+        dx1 = torch.empty_like(dx2)
+        C.rmsnorm_bwd(dxn2, s.x1, lw.ln2, s.rstd2, dx2, dx1, self.eps)
+        # --- o projection
+        dattn, db, da = self._lora_linear_backward(dx1, lw.w_o_t, s.u_o, s.attn_d, L.get("b_o"), L.get("a_o"),
+                                                   "o", li, seed, train)
+        if db is not None:
+            self._scatter_grads(li, "o", db, da)
+        # --- attention
+        dq, dk, dv = attn_ops.attention_backward(dattn, s.q, s.k, s.v, s.attn, s.attn_ctx, meta, self.scale)
+        dqkv = torch.empty_like(s.qkv)
+        C.qk_norm_rope_bwd(dq, dk, dv, s.qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, dqkv, m.nq, m.nkv, self.eps)
+        del dq, dk, dv
+        # --- qkv projection
+        dxn, db, da = self._lora_linear_backward(dqkv, lw.w_qkv_t, s.u_qkv, s.xd, L.get("b_qkv"), L.get("a_qkv"),
+                                                 "qkv", li, seed, train)
+        if db is not None:
+            self._scatter_grads(li, "qkv", db, da)
+        _tp_all_reduce(dxn, tp_group)
+        dx = torch.empty_like(dx2)
+        C.rmsnorm_bwd(dxn, s.x, lw.ln1, s.rstd1, dx1, dx, self.eps)
+        return dx
+
+    # ------------------------------------------------------------ stages
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        out = torch.empty(ids.numel(), self.m.cfg.hidden_size, device=ids.device, dtype=self.m.dtype)
+        self.C.embedding(ids.reshape(-1).contiguous(), self.m.embed, out)
+        return out
+
+    def stage_forward(self, x: torch.Tensor, meta: AttnMeta, *, train=False, seed=0, keep_inputs=False):
+        """Run this rank's layers; returns (out, [layer inputs] if keep_inputs)."""
+        inputs = []
+        for lw in self.m.layers:
+            if keep_inputs:
+                inputs.append(x)
+            x, _ = self.layer_forward(lw, x, meta, train=train, seed=seed)
+        return x, inputs
+
+    def stage_backward(self, inputs, dout: torch.Tensor, meta: AttnMeta, *, train=True, seed=0):
+        """Recompute-and-backprop through this rank's layers; returns d(input)."""
+        g = dout
+        for lw, x in zip(reversed(self.m.layers), reversed(inputs), strict=True):
+            _, saved = self.layer_forward(lw, x, meta, train=train, seed=seed, save=True)
+            g = self.layer_backward(lw, saved, g, meta, train=train, seed=seed)
+            del saved
+        return g
+
+    # ------------------------------------------------------------ head
+    def final_norm(self, x: torch.Tensor):
+        xn = torch.empty_like(x)
+        rstd = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
+        self.C.add_rmsnorm(x, None, None, self.m.norm, xn, rstd, None, None, 1.0, self.eps)
+        return xn, rstd
+
+    def token_logprobs(self, h: torch.Tensor, targets: torch.Tensor):
+        """log p(targets) from normed hidden h [T, H] -> (logp [T], lse [T])."""
+        m = self.m
+        T = h.shape[0]
+        bn = 256
+        nblk = (m.vocab_local + bn - 1) // bn
+        local_t = (targets - m.vocab_start).contiguous()
+        part = torch.empty(T, nblk, 2, device=h.device, dtype=torch.float32)
+        tl = torch.zeros(T, device=h.device, dtype=torch.float32)
+        gemm(h, m.lm_head, torch.empty(0, device=h.device), epilogue="lse", aux=part.view(T, nblk * 2),
+             targets=local_t, tgt_logit=tl, bn=bn)
+        lse = torch.empty(T, device=h.device, dtype=torch.float32)
+        logp = torch.empty(T, device=h.device, dtype=torch.float32)
+        self.C.lse_combine(part, tl, lse, logp)
+        group = m.ps.tp_group
+        if m.ps.tp_size > 1:
+            # merge vocab shards: lse = log sum_r exp(lse_r); target logit lives on one shard
+            lses = torch.empty(m.ps.tp_size, T, device=h.device, dtype=torch.float32)
+            dist.all_gather_into_tensor(lses, lse, group=group)
+            _tp_all_reduce(tl, group)
+            lse = torch.logsumexp(lses, 0)
+            logp = tl - lse
+        return logp, lse
+
+    def token_logprobs_backward(self, h: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
+                                g: torch.Tensor, chunk_tokens: int = 32768) -> torch.Tensor:
+        """d(normed hidden) for upstream grads g [T] of the selected log-probs."""
+        m = self.m
+        T, H = h.shape
+        dh = torch.empty_like(h)
+        local_t = (targets - m.vocab_start).contiguous()
+        for t0 in range(0, T, chunk_tokens):
+            t1 = min(T, t0 + chunk_tokens)
+            dlog = gemm(h[t0:t1], m.lm_head, epilogue="softmax_grad", targets=local_t[t0:t1],
+                        row_lse=lse[t0:t1].contiguous(), row_scale=g[t0:t1].contiguous())
+            gemm(dlog, m.lm_head_t, dh[t0:t1])
+            del dlog
+        _tp_all_reduce(dh, m.ps.tp_group)
+        return dh

@@ -1,0 +1,87 @@
+"""Python face of the tcgen05 GEMM (csrc/gemm_tc.cu).
+
+``gemm(a, b)`` computes ``a @ b.T`` for row-major bf16 ``a [M, K]`` and
+``b [N, K]`` with fp32 accumulation, plus optional fused pieces:
+
+* ``ext=(a2, b2)``: extends the reduction with ``a2 @ b2.T`` (LoRA: ``a2`` is
+  ``s * x A^T`` zero-padded to a multiple of 64 columns, ``b2`` the padded B).
+* ``residual``: adds a bf16 tensor to the result.
+* ``epilogue``: ``store`` (bf16), ``store_f32``, ``atomic`` (fp32 +=, allows
+  split-K), ``swiglu`` (b rows interleave gate/up; output N/2 columns),
+  ``lse`` (row log-sum-exp partials + target logits), ``softmax_grad``.
+* ``swap=True``: ``a`` is the weight ``[N_out, K]`` and ``b`` the activations
+  ``[T, K]``; the result is stored as ``[T, N_out]``.  This is the decode
+  shape: tokens fill the narrow N side of the tensor-core tile.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from graspo_b200.ops._ext import err_word, ext
+
+EPILOGUES = {"store": 0, "swiglu": 1, "atomic": 2, "lse": 3, "store_f32": 4, "softmax_grad": 5}
+
+
+def pick_bn(n: int, swap: bool) -> int:
+    if swap:
+        if n <= 32:
+            return 32
+        if n <= 64:
+            return 64
+        return 128
+    if n >= 1024:
+        return 256
+    if n >= 128:
+        return 128
+    return 64
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor | None = None,
+    *,
+    ext_ab: tuple[torch.Tensor, torch.Tensor] | None = None,
+    residual: torch.Tensor | None = None,
+    epilogue: str = "store",
+    aux: torch.Tensor | None = None,
+    targets: torch.Tensor | None = None,
+    tgt_logit: torch.Tensor | None = None,
+    row_lse: torch.Tensor | None = None,
+    row_scale: torch.Tensor | None = None,
+    swap: bool = False,
+    bn: int | None = None,
+    splits: int = 1,
+    max_ctas: int = 0,
+) -> torch.Tensor:
+    epi = EPILOGUES[epilogue]
+    if swap:
+        tokens, n_out = b.shape[0], a.shape[0]
+        out_shape = (tokens, n_out // 2 if epilogue == "swiglu" else n_out)
+        narrow = tokens
+    else:
+        out_shape = (a.shape[0], b.shape[0] // 2 if epilogue == "swiglu" else b.shape[0])
+        narrow = b.shape[0]
+    if out is None:
+        dtype = torch.float32 if epilogue in ("atomic", "store_f32") else torch.bfloat16
+        if epilogue == "lse":
+            out = torch.empty(0, device=a.device, dtype=torch.float32)
+        else:
+            out = (torch.zeros if epilogue == "atomic" else torch.empty)(out_shape, device=a.device, dtype=dtype)
+    a2 = b2 = None
+    if ext_ab is not None:
+        a2, b2 = ext_ab
+        if swap:
+            # the extension pairs with (a, b) in the same roles
+            pass
+    bn = bn or pick_bn(narrow, swap)
+    ext().gemm_tc(
+        a, b, a2, b2, out, residual, aux, targets, tgt_logit, row_lse, row_scale,
+        epi, swap, bn, splits, err_word(a.device), max_ctas,
+    )
+    return out
+
+
+def lse_partials_shape(m: int, n: int, bn: int = 256) -> tuple[int, int, int]:
+    return (m, (n + bn - 1) // bn, 2)

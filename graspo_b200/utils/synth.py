@@ -1,0 +1,191 @@
+"""Synthetic, seeded inputs: random-init HF checkpoints and JSON-extraction data.
+
+* ``write_qwen3_checkpoint`` writes a Hugging Face style directory
+  (``config.json`` with ``model_type: qwen3``, sharded ``*.safetensors`` with an
+  index, an offline tokenizer) whose weights are N(0, 0.02) from a seed and
+  whose norm weights are ones.  Both this framework and the reference load
+  it, so the two run identical models.
+* ``synthetic_json_records`` produces the seeded JSON-extraction prompts of
+  the benchmark configs: a system message and a user message holding 2-4
+  random snake_case keys, each with a random lowercase 3-8 character value or
+  an 11-digit number; the target is the dict of those pairs.
+"""
+
+from __future__ import annotations
+
+import json
+import random
+import string
+from pathlib import Path
+
+import torch
+
+QWEN3_8B = dict(
+    vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+    num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+)
+DENSE_32B = dict(
+    vocab_size=151936, hidden_size=5120, intermediate_size=25600, num_hidden_layers=64,
+    num_attention_heads=64, num_key_value_heads=8, head_dim=128,
+)
+TINY = dict(
+    vocab_size=2048, hidden_size=128, intermediate_size=384, num_hidden_layers=2,
+    num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+)
+
+
+def qwen3_config_dict(dims: dict, *, rms_norm_eps: float = 1e-6, rope_theta: float = 1e6) -> dict:
+    return {
+        "architectures": ["Qwen3ForCausalLM"],
+        "model_type": "qwen3",
+        "hidden_act": "silu",
+        "rms_norm_eps": rms_norm_eps,
+        "rope_theta": rope_theta,
+        "max_position_embeddings": 40960,
+        "tie_word_embeddings": False,
+        "attention_bias": False,
+        "torch_dtype": "bfloat16",
+        "bos_token_id": None,
+        "eos_token_id": 151643 if dims["vocab_size"] >= 151654 else dims["vocab_size"] - 4,
+        **dims,
+    }
+
+
+def _qwen3_tensor_specs(dims: dict) -> list[tuple[str, tuple[int, ...], str]]:
+    H, I, V = dims["hidden_size"], dims["intermediate_size"], dims["vocab_size"]
+    q = dims["num_attention_heads"] * dims["head_dim"]
+    kv = dims["num_key_value_heads"] * dims["head_dim"]
+    D = dims["head_dim"]
+    specs = [("model.embed_tokens.weight", (V, H), "normal")]
+    for i in range(dims["num_hidden_layers"]):
+        p = f"model.layers.{i}"
+        specs += [
+            (f"{p}.input_layernorm.weight", (H,), "ones"),
+            (f"{p}.post_attention_layernorm.weight", (H,), "ones"),
+            (f"{p}.self_attn.q_proj.weight", (q, H), "normal"),
+            (f"{p}.self_attn.k_proj.weight", (kv, H), "normal"),
+            (f"{p}.self_attn.v_proj.weight", (kv, H), "normal"),
+            (f"{p}.self_attn.o_proj.weight", (H, q), "normal"),
+            (f"{p}.self_attn.q_norm.weight", (D,), "ones"),
+            (f"{p}.self_attn.k_norm.weight", (D,), "ones"),
+            (f"{p}.mlp.gate_proj.weight", (I, H), "normal"),
+            (f"{p}.mlp.up_proj.weight", (I, H), "normal"),
+            (f"{p}.mlp.down_proj.weight", (H, I), "normal"),
+        ]
+    specs += [("model.norm.weight", (H,), "ones"), ("lm_head.weight", (V, H), "normal")]
+    return specs
+
+
+def write_qwen3_checkpoint(
+    output_dir: str | Path,
+    dims: dict,
+    *,
+    seed: int = 0,
+    dtype: torch.dtype = torch.bfloat16,
+    std: float = 0.02,
+    shard_bytes: int = 4 << 30,
+    device: str | None = None,
+    with_tokenizer: bool = True,
+) -> Path:
+    """Write a random-init Qwen3 checkpoint (skipped if a complete one exists)."""
+    from safetensors.torch import save_file
+
+    out = Path(output_dir)
+    marker = out / ".complete"
+    config = qwen3_config_dict(dims)
+    if marker.exists() and json.loads((out / "config.json").read_text())["hidden_size"] == dims["hidden_size"]:
+        return out
+    out.mkdir(parents=True, exist_ok=True)
+    dev = device or ("cuda" if torch.cuda.is_available() else "cpu")
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    weight_map: dict[str, str] = {}
+    shard: dict[str, torch.Tensor] = {}
+    size = 0
+    index = 0
+
+    def flush() -> None:
+        nonlocal shard, size, index
+        if not shard:
+            return
+        index += 1
+        name = f"model-{index:05d}.safetensors"
+        save_file(shard, str(out / name), metadata={"format": "pt"})
+        for key in shard:
+            weight_map[key] = name
+        shard, size = {}, 0
+
+    for name, shape, kind in _qwen3_tensor_specs(dims):
+        if kind == "ones":
+            t = torch.ones(shape, dtype=dtype)
+        else:
+            t = (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(dtype).cpu()
+        nbytes = t.numel() * t.element_size()
+        if size and size + nbytes > shard_bytes:
+            flush()
+        shard[name] = t.contiguous()
+        size += nbytes
+    flush()
+    total = sum((out / f).stat().st_size for f in set(weight_map.values()))
+    (out / "model.safetensors.index.json").write_text(
+        json.dumps({"metadata": {"total_size": total}, "weight_map": weight_map}, indent=2)
+    )
+    (out / "config.json").write_text(json.dumps(config, indent=2))
+    (out / "generation_config.json").write_text(json.dumps({"eos_token_id": config["eos_token_id"]}))
+    if with_tokenizer:
+        from graspo_b200.utils.tokenizer import build_tokenizer
+
+        build_tokenizer(out, dims["vocab_size"])
+    marker.write_text("ok")
+    return out
+
+
+def _snake_key(rng: random.Random) -> str:
+    words = ["".join(rng.choice(string.ascii_lowercase) for _ in range(rng.randint(3, 7))) for _ in range(rng.randint(1, 3))]
+    return "_".join(words)
+
+
+def synthetic_json_records(
+    count: int, *, seed: int = 0, pad_words_to: int | None = None
+) -> list[dict]:
+    """Seeded JSON-extraction records in the JSONL schema.
+
+    ``pad_words_to`` appends filler words to the user message so prompts reach
+    a target length (used by the 1024-token benchmark prompts).
+    """
+    rng = random.Random(seed)
+    records = []
+    for idx in range(count):
+        fields: dict[str, object] = {}
+        for _ in range(rng.randint(2, 4)):
+            key = _snake_key(rng)
+            if rng.random() < 0.5:
+                fields[key] = "".join(rng.choice(string.ascii_lowercase) for _ in range(rng.randint(3, 8)))
+            else:
+                fields[key] = rng.randint(10**10, 10**11 - 1)
+        facts = "; ".join(f"{k.replace('_', ' ')} is {v}" for k, v in fields.items())
+        text = f"Extract the following fields as JSON with keys {list(fields)}: {facts}."
+        if pad_words_to:
+            filler = []
+            while len(filler) < pad_words_to:
+                filler.append("".join(rng.choice(string.ascii_lowercase) for _ in range(rng.randint(2, 9))))
+            text += " Context: " + " ".join(filler)
+        records.append(
+            {
+                "id": f"synthetic-{idx}",
+                "messages": [
+                    {"role": "system", "content": "You extract structured data. Answer with a ```json fenced object."},
+                    {"role": "user", "content": text},
+                ],
+                "targets": [{"id": f"t{idx}", "output": {"content": fields}}],
+            }
+        )
+    return records
+
+
+def write_jsonl_records(records: list[dict], path: str | Path) -> Path:
+    out = Path(path)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    with out.open("w", encoding="utf-8") as handle:
+        for rec in records:
+            handle.write(json.dumps(rec, ensure_ascii=False) + "\n")
+    return out

@@ -1,0 +1,35 @@
+"""Build the sm_100a kernel library in-tree: ``python setup.py build_ext --inplace``.
+
+Produces ``graspo_b200/_C*.so``.  Only Blackwell datacenter parts (sm_100a)
+are targeted; there is no fallback architecture.
+"""
+
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+sources = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + [os.path.join("csrc", "bindings.cpp")]
+
+setup(
+    name="graspo_b200",
+    version="0.1.0",
+    packages=[],
+    ext_modules=[
+        CUDAExtension(
+            name="graspo_b200._C",
+            sources=sources,
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={
+                "cxx": ["-O3", "-std=c++17"],
+                "nvcc": ARCH + ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
+                                "-Xptxas=-v" if os.environ.get("GRASPO_PTXAS_VERBOSE") else "-Xptxas=-O3"],
+            },
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

@@ -1,0 +1,330 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from graspo_b200.ops._ext import ext
+
+    return ext()
+
+
+def _rand(*shape, scale=1.0, dtype=torch.bfloat16):
+    return (torch.randn(*shape, device="cuda") * scale).to(dtype)
+
+
+def _close(out, ref, tol):
+    err = (out.float() - ref.float()).abs().max().item()
+    den = ref.float().abs().max().item() + 1e-6
+    assert err / den < tol, f"max rel err {err / den:.3e} (abs {err:.3e})"
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+    yield
+    from graspo_b200.ops._ext import check_errors
+
+    torch.cuda.synchronize()
+    check_errors()
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (300, 520, 512), (1000, 1536, 1024), (64, 4096, 4096)])
+def test_gemm_store(m, n, k):
+    from graspo_b200.ops.gemm import gemm
+
+    a, b = _rand(m, k), _rand(n, k)
+    out = gemm(a, b)
+    _close(out, a.float() @ b.float().T, 2e-2)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tile_widths_and_residual(bn):
+    from graspo_b200.ops.gemm import gemm
+
+    a, b, r = _rand(384, 256), _rand(640, 256), _rand(384, 640)
+    out = gemm(a, b, residual=r, bn=bn)
+    _close(out, a.float() @ b.float().T + r.float(), 2e-2)
+
+
+def test_gemm_lora_extension():
+    from graspo_b200.ops.gemm import gemm
+
+    m, n, k, r = 257, 384, 512, 48
+    x, w = _rand(m, k), _rand(n, k)
+    A, B = _rand(r, k, scale=0.05), _rand(n, r, scale=0.05)
+    s = 2.0
+    u = torch.zeros(m, 64, device="cuda", dtype=torch.bfloat16)
+    u[:, :r] = ((x.float() @ A.float().T) * s).bfloat16()
+    bpad = torch.zeros(n, 64, device="cuda", dtype=torch.bfloat16)
+    bpad[:, :r] = B
+    out = gemm(x, w, ext_ab=(u, bpad))
+    ref = x.float() @ w.float().T + u[:, :r].float() @ B.float().T
+    _close(out, ref, 2e-2)
+
+
+def test_gemm_swiglu():
+    from graspo_b200.ops.gemm import gemm
+
+    m, i, k = 200, 384, 256
+    x, wg, wu = _rand(m, k), _rand(i, k, scale=0.1), _rand(i, k, scale=0.1)
+    inter = torch.stack([wg, wu], dim=1).reshape(2 * i, k).contiguous()
+    aux = torch.empty(m, 2 * i, device="cuda", dtype=torch.bfloat16)
+    out = gemm(x, inter, epilogue="swiglu", aux=aux)
+    g, u = x.float() @ wg.float().T, x.float() @ wu.float().T
+    _close(out, torch.nn.functional.silu(g) * u, 3e-2)
+    _close(aux.view(m, i, 2)[..., 0], g, 2e-2)
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+def test_gemm_atomic_split_k(splits):
+    from graspo_b200.ops.gemm import gemm
+
+    a, b = _rand(130, 768), _rand(300, 768)
+    out = gemm(a, b, epilogue="atomic", splits=splits)
+    _close(out, a.float() @ b.float().T, 1e-2)
+
+
+@pytest.mark.parametrize("tokens", [8, 64, 100])
+@pytest.mark.parametrize("epilogue", ["store", "atomic", "store_f32"])
+def test_gemm_swap(tokens, epilogue):
+    from graspo_b200.ops.gemm import gemm
+
+    w, x = _rand(384, 512), _rand(tokens, 512)
+    out = gemm(w, x, swap=True, epilogue=epilogue, splits=2 if epilogue == "atomic" else 1)
+    _close(out, x.float() @ w.float().T, 2e-2)
+
+
+def test_gemm_swap_swiglu_and_residual():
+    from graspo_b200.ops.gemm import gemm
+
+    i, k, t = 256, 256, 40
+    wg, wu, x = _rand(i, k, scale=0.1), _rand(i, k, scale=0.1), _rand(t, k)
+    inter = torch.stack([wg, wu], dim=1).reshape(2 * i, k).contiguous()
+    out = gemm(inter, x, swap=True, epilogue="swiglu")
+    ref = torch.nn.functional.silu(x.float() @ wg.float().T) * (x.float() @ wu.float().T)
+    _close(out, ref, 3e-2)
+    w, r = _rand(384, k), _rand(t, 384)
+    _close(gemm(w, x, swap=True, residual=r), x.float() @ w.float().T + r.float(), 2e-2)
+
+
+def test_gemm_lse_and_softmax_grad():
+    from graspo_b200.ops.gemm import gemm
+
+    t, v, h = 300, 1000, 256
+    x, w = _rand(t, h), _rand(v, h, scale=0.2)
+    tgt = torch.randint(0, v, (t,), device="cuda")
+    nblk = (v + 255) // 256
+    part = torch.empty(t, nblk, 2, device="cuda")
+    tl = torch.empty(t, device="cuda")
+    gemm(x, w, epilogue="lse", aux=part.view(t, nblk * 2), targets=tgt, tgt_logit=tl, bn=256)
+    lse, logp = torch.empty(t, device="cuda"), torch.empty(t, device="cuda")
+    _ext().lse_combine(part, tl, lse, logp)
+    logits = x.float() @ w.float().T
+    ref = torch.log_softmax(logits, -1).gather(1, tgt[:, None]).squeeze(1)
+    assert (logp - ref).abs().max().item() < 2e-2
+    g = torch.randn(t, device="cuda")
+    dl = gemm(x, w, epilogue="softmax_grad", targets=tgt, row_lse=lse, row_scale=g)
+    ref_dl = g[:, None] * (torch.nn.functional.one_hot(tgt, v).float() - torch.softmax(logits, -1))
+    _close(dl, ref_dl, 3e-2)
+
+
+def _rmsnorm_ref(x, w, eps):
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+
+@pytest.mark.parametrize("delta_dtype", [None, torch.bfloat16, torch.float32])
+def test_add_rmsnorm(delta_dtype):
+    h, w = _rand(37, 4096), _rand(4096, scale=0.1) + 1
+    y = torch.empty_like(h)
+    hout = torch.empty_like(h)
+    A = _rand(48, 4096, scale=0.02)
+    U = torch.empty(37, 64, device="cuda", dtype=torch.bfloat16)
+    delta = None if delta_dtype is None else _rand(37, 4096).to(delta_dtype)
+    ref_in = h.float() + (delta.float() if delta is not None else 0)
+    ref_in = ref_in.bfloat16()
+    dcopy = delta.clone() if delta is not None else None
+    _ext().add_rmsnorm(h, delta, hout if delta is not None else None, w, y, None, A, U, 2.0, 1e-6)
+    ref = _rmsnorm_ref(ref_in, w, 1e-6)
+    _close(y, ref, 2e-2)
+    _close(U[:, :48], 2.0 * ref.bfloat16().float() @ A.float().T, 3e-2)
+    assert U[:, 48:].abs().max().item() == 0
+    if delta_dtype is torch.float32:
+        assert delta.abs().max().item() == 0, "fp32 workspace must be zeroed after use"
+    if dcopy is not None:
+        _close(hout, ref_in, 1e-2)
+
+
+def test_rmsnorm_bwd():
+    x = _rand(19, 1024).requires_grad_(False)
+    w = _rand(1024, scale=0.1) + 1
+    dy = _rand(19, 1024)
+    xf = x.float().requires_grad_(True)
+    _rmsnorm_ref(xf, w, 1e-6).backward(dy.float())
+    dx = torch.empty_like(x)
+    _ext().rmsnorm_bwd(dy, x, w, None, None, dx, 1e-6)
+    _close(dx, xf.grad, 2e-2)
+
+
+def _rope_ref(x, pos, inv_freq):
+    f = pos.float()[:, None] * inv_freq[None, :]
+    emb = torch.cat([f, f], -1)
+    cos, sin = emb.cos()[:, None, :], emb.sin()[:, None, :]
+    x1, x2 = x[..., :64], x[..., 64:]
+    rot = torch.cat([-x2, x1], -1)
+    return x * cos + rot * sin
+
+
+def test_qk_norm_rope_and_bwd():
+    T, nq, nkv, D = 23, 4, 2, 128
+    qkv = _rand(T, (nq + 2 * nkv) * D)
+    qw, kw = _rand(D, scale=0.1) + 1, _rand(D, scale=0.1) + 1
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    pos = torch.randint(0, 3000, (T,), device="cuda")
+    q = torch.empty(T, nq, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.empty(T, nkv, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.empty_like(k)
+    _ext().qk_norm_rope(qkv, qw, kw, inv_freq, pos, q, k, v, None, None, nq, nkv, 64, 1e-6)
+    x = qkv.float().view(T, nq + 2 * nkv, D).requires_grad_(True)
+    qr = _rope_ref(_rmsnorm_ref(x[:, :nq], qw, 1e-6), pos, inv_freq)
+    kr = _rope_ref(_rmsnorm_ref(x[:, nq:nq + nkv], kw, 1e-6), pos, inv_freq)
+    _close(q, qr, 2e-2)
+    _close(k, kr, 2e-2)
+    _close(v, x[:, nq + nkv:], 1e-2)
+    dq, dk, dv = _rand(T, nq, D), _rand(T, nkv, D), _rand(T, nkv, D)
+    (qr * dq.float()).sum().add_((kr * dk.float()).sum()).add_((x[:, nq + nkv:] * dv.float()).sum()).backward()
+    dqkv = torch.empty_like(qkv)
+    _ext().qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, inv_freq, pos, dqkv, nq, nkv, 1e-6)
+    _close(dqkv, x.grad.view(T, -1), 3e-2)
+
+
+def test_swiglu_bwd_lora_down_embedding_transpose():
+    gu, dh = _rand(33, 2 * 96), _rand(33, 96)
+    dgu = torch.empty_like(gu)
+    _ext().swiglu_bwd(gu, dh, dgu)
+    x = gu.float().view(33, 96, 2).requires_grad_(True)
+    (torch.nn.functional.silu(x[..., 0]) * x[..., 1] * dh.float()).sum().backward()
+    _close(dgu, x.grad.view(33, -1), 2e-2)
+
+    xx, A = _rand(10, 3072), _rand(40, 3072, scale=0.05)
+    U = torch.empty(10, 64, device="cuda", dtype=torch.bfloat16)
+    _ext().lora_down(xx, A, U, 0.5)
+    _close(U[:, :40], 0.5 * xx.float() @ A.float().T, 2e-2)
+
+    table, ids = _rand(100, 64), torch.randint(0, 100, (17,), device="cuda")
+    out = torch.empty(17, 64, device="cuda", dtype=torch.bfloat16)
+    _ext().embedding(ids, table, out)
+    assert torch.equal(out, table[ids])
+
+    m = _rand(70, 45)
+    t = torch.empty(45, 70, device="cuda", dtype=torch.bfloat16)
+    _ext().transpose_bf16(m, t)
+    assert torch.equal(t, m.T)
+
+
+def test_paged_decode_attention():
+    rows, nq, nkv, D, page = 6, 8, 2, 128, 16
+    lens = torch.tensor([5, 16, 17, 40, 33, 64], device="cuda", dtype=torch.int32)
+    starts = torch.tensor([0, 3, 0, 7, 1, 0], device="cuda", dtype=torch.int32)
+    max_pages = 4
+    num_pages = rows * max_pages
+    perm = torch.randperm(num_pages, device="cuda").int().view(rows, max_pages)
+    kp, vp = _rand(num_pages, nkv, page, D), _rand(num_pages, nkv, page, D)
+    q = _rand(rows, nq, D)
+    out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    _ext().paged_decode_attention(q, kp, vp, perm, starts, lens, out, scale)
+    for r in range(rows):
+        L = int(lens[r])
+        s0 = int(starts[r])
+        keys = torch.cat([kp[perm[r, p]] for p in range(max_pages)], dim=1)[:, s0:L]  # [nkv, L, D]
+        vals = torch.cat([vp[perm[r, p]] for p in range(max_pages)], dim=1)[:, s0:L]
+        kk = keys.float().repeat_interleave(nq // nkv, 0)
+        vv = vals.float().repeat_interleave(nq // nkv, 0)
+        att = torch.softmax(q[r].float()[:, None, :] @ kk.transpose(1, 2) * scale, -1) @ vv
+        _close(out[r].view(nq, D), att.squeeze(1), 2e-2)
+
+
+def test_sample_append_greedy_and_distribution():
+    rows, V = 4, 50
+    logits = torch.randn(rows, V, device="cuda")
+    state = dict(
+        next_ids=torch.zeros(rows, dtype=torch.long, device="cuda"),
+        slot=torch.full((rows,), 9, dtype=torch.long, device="cuda"),
+        pos=torch.zeros(rows, dtype=torch.long, device="cuda"),
+        kv_len=torch.zeros(rows, dtype=torch.int32, device="cuda"),
+        finished=torch.zeros(rows, dtype=torch.uint8, device="cuda"),
+        out=torch.zeros(rows, 4, dtype=torch.long, device="cuda"),
+    )
+    _ext().sample_append(logits, 0.0, 1.0, 1, state["next_ids"], state["slot"], state["pos"], state["kv_len"],
+                         state["finished"], state["out"], 10, -1, 0, False, None)
+    assert torch.equal(state["next_ids"], logits.argmax(-1))
+    assert torch.equal(state["out"][:, 0], logits.argmax(-1))
+    assert int(state["slot"][0]) == 10 and int(state["kv_len"][0]) == 11
+    # distribution: many independent rows of the same logits
+    n = 4000
+    lg = torch.log(torch.tensor([0.5, 0.3, 0.15, 0.05], device="cuda")).repeat(n, 1)
+    ids = torch.zeros(n, dtype=torch.long, device="cuda")
+    slot = torch.zeros(n, dtype=torch.long, device="cuda")
+    _ext().sample_append(lg, 1.0, 1.0, 123, ids, slot, torch.zeros_like(slot), torch.zeros(n, dtype=torch.int32, device="cuda"),
+                         torch.zeros(n, dtype=torch.uint8, device="cuda"), torch.zeros(n, 1, dtype=torch.long, device="cuda"),
+                         1, -1, 0, False, None)
+    freq = torch.bincount(ids, minlength=4).float() / n
+    assert (freq - torch.tensor([0.5, 0.3, 0.15, 0.05], device="cuda")).abs().max() < 0.03
+    # top-p 0.7 keeps only the two most likely tokens
+    _ext().sample_append(lg, 1.0, 0.7, 7, ids, slot, torch.zeros_like(slot), torch.zeros(n, dtype=torch.int32, device="cuda"),
+                         torch.zeros(n, dtype=torch.uint8, device="cuda"), torch.zeros(n, 1, dtype=torch.long, device="cuda"),
+                         1, -1, 0, False, None)
+    assert int(ids.max()) <= 1
+
+
+def test_grpo_loss_matches_reference():
+    from graspo_b200.core.loss import GRASPOLoss
+
+    B, S = 5, 37
+    lp = (torch.randn(B, S, device="cuda") * 0.1 - 2).requires_grad_(True)
+    old = lp.detach() + torch.randn(B, S, device="cuda") * 0.3
+    adv = torch.randn(B, 1, device="cuda").expand(B, S).contiguous()
+    mask = torch.rand(B, S, device="cuda") > 0.3
+    ref = GRASPOLoss(0.2)(lp, old, adv, mask)
+    ref.backward()
+    loss = torch.zeros(1, device="cuda")
+    dlp = torch.empty(B, S, device="cuda")
+    _ext().grpo_loss(lp.detach(), old, adv, mask.to(torch.uint8), 0.2, 1.0, loss, dlp, None)
+    assert abs(loss.item() - ref.item()) < 1e-5
+    _close(dlp, lp.grad, 1e-4)
+
+
+def test_adamw_matches_torch():
+    n = 1000
+    p0 = torch.randn(n, device="cuda")
+    grads = [torch.randn(n, device="cuda") * 3 for _ in range(3)]
+    ref = p0.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([ref], lr=1e-3, weight_decay=0.01)
+    p, m, v = p0.clone(), torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    for step, g in enumerate(grads, start=1):
+        ref.grad = g.clone()
+        torch.nn.utils.clip_grad_norm_([ref], 1.0)
+        opt.step()
+        ss = torch.zeros(1, device="cuda")
+        _ext().grad_sumsq(g, ss)
+        _ext().adamw(p, g, m, v, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, ss, 1.0, None, None)
+    _close(p, ref.detach(), 1e-5)
+
+
+def test_dropout_statistics():
+    x = torch.ones(100000, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty_like(x)
+    _ext().dropout(x, y, 0.1, 5, 3, None)
+    kept = (y != 0).float().mean().item()
+    assert abs(kept - 0.9) < 0.01
+    assert abs(y[y != 0].float().mean().item() - 1 / 0.9) < 1e-2
+    y2 = torch.empty_like(x)
+    _ext().dropout(x, y2, 0.1, 5, 3, None)
+    assert torch.equal(y, y2), "same seed and stream must regenerate the same mask"
