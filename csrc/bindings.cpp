@@ -17,7 +17,7 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::option
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
-                  int64_t nq, int64_t nkv, int64_t page_size, double eps);
+                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps);
 void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
                       torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq, torch::Tensor pos,
                       torch::Tensor dqkv, int64_t nq, int64_t nkv, double eps);
@@ -26,7 +26,8 @@ void lora_down(torch::Tensor x, torch::Tensor A, torch::Tensor U, double scale);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
-                            torch::Tensor out, double scale);
+                            torch::Tensor out, double scale, int64_t splits,
+                            c10::optional<torch::Tensor> scratch);
 void sample_append(torch::Tensor logits, double temperature, double top_p, int64_t seed,
                    torch::Tensor next_ids, torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len,
                    torch::Tensor finished, torch::Tensor out_tokens, int64_t prompt_slots,

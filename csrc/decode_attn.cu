@@ -1,17 +1,26 @@
-// Decode-step attention over the paged KV cache.
+// Decode-step attention over the paged KV cache (flash-decoding).
 //
 // Cache layout: k_pool / v_pool [num_pages, n_kv_heads, page_size, 128] bf16,
 // block_table [rows, max_pages] maps a row's logical page to a physical page.
 // Rows that share a prompt (the G completions of one GRASPO group) point at
-// the same physical prompt pages, so the prompt KV is stored once per group.
-// A row attends to key positions [start[row], len[row]) (left padding is
-// skipped, the newest token at len-1 is included).
+// the same physical prompt pages, so the prompt KV is stored once per group;
+// CTAs of one group are launched next to each other, so those pages are
+// read from DRAM once and served from L2 to the other rows.  A row attends to
+// key positions [start[row], len[row]).
 //
-// One CTA per (row, kv_head) handles all G = nq / nkv query heads of that KV
-// head (GQA packing: every K/V element is read once for the whole group).  Each
-// of the 4 warps walks a quarter of every page; a lane owns 4 of the 128 head
-// dims; per-warp online-softmax states are merged through shared memory at the
-// end.  This kernel is bandwidth-bound: the figure of merit is KV bytes / time.
+// Grid: (split, kv head, row), row fastest.  A CTA handles all G = nq / nkv
+// query heads of one KV head (GQA packing) over one contiguous slice of the
+// key range.  Inside a CTA each warp walks 32-key chunks:
+//   * QK: lane t owns key t of the chunk and computes its G dot products
+//     (q broadcast from shared memory) -- no per-key shuffles;
+//   * online softmax per head with one warp max / sum per chunk;
+//   * PV: lane l owns head dims [4l, 4l+4); probabilities are broadcast by
+//     shuffle, V rows are read coalesced.
+// With more than one split, every CTA writes its (max, sum, acc) partial to a
+// scratch buffer and bumps a per-(row, kv head) counter; the CTA that arrives
+// last merges the partials and writes the output (no CTA ever waits on
+// another).  The counter is reset by that last CTA, so the scratch buffer is
+// reusable by the next launch without clearing.
 
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -24,28 +33,47 @@ namespace gb {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kMaxGroup = 8;
+constexpr int kWarps = 4;
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;       // [rows, nq, D]
+  const __nv_bfloat16* k_pool;  // [pages, nkv, page, D]
+  const __nv_bfloat16* v_pool;
+  const int* block_table;       // [rows, max_pages]
+  const int* start;             // [rows]
+  const int* len;               // [rows]
+  __nv_bfloat16* out;           // [rows, nq * D]
+  float* part_acc;              // [rows, nq, splits, D]    (splits > 1)
+  float* part_ml;               // [rows, nq, splits, 2]
+  int* counters;                // [rows, nkv]
+  int nq, nkv, page_size, max_pages, splits, keys_per_split;
+  float scale_log2;
+};
 
 template <int G>
-__global__ void __launch_bounds__(128) paged_decode_attn_kernel(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_pool,
-    const __nv_bfloat16* __restrict__ v_pool, const int* __restrict__ block_table,
-    const int* __restrict__ start, const int* __restrict__ len, __nv_bfloat16* __restrict__ out,
-    int nq, int nkv, int page_size, int max_pages, float scale_log2) {
-  const int row = blockIdx.x / nkv;
-  const int kvh = blockIdx.x - row * nkv;
+__global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAttnArgs a) {
+  const int rows_total = gridDim.x / (a.nkv * a.splits);
+  const int row = blockIdx.x % rows_total;
+  const int rest = blockIdx.x / rows_total;
+  const int kvh = rest % a.nkv;
+  const int split = rest / a.nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int s0 = start[row], s1 = len[row];
 
-  float qv[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const __nv_bfloat16* qp = q + (static_cast<long>(row) * nq + kvh * G + g) * kD + lane * 4;
-    uint2 raw = *reinterpret_cast<const uint2*>(qp);
-    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) qv[g][e] = __bfloat162float(b[e]) * scale_log2;
+  __shared__ __align__(16) float q_s[G][kD];
+  __shared__ float m_s[kWarps][G], l_s[kWarps][G];
+  __shared__ float acc_s[kWarps][G][kD];
+  __shared__ int is_last;
+
+  for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
+    const int g = i / kD, d = i - g * kD;
+    q_s[g][d] = __bfloat162float(a.q[(static_cast<long>(row) * a.nq + kvh * G + g) * kD + d]) * a.scale_log2;
   }
+  __syncthreads();
+
+  const int s0 = a.start[row], s1 = a.len[row];
+  const int k_begin = max(s0, split * a.keys_per_split);
+  const int k_end = min(s1, (split + 1) * a.keys_per_split);
+
   float m[G], l[G], acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -55,80 +83,160 @@ __global__ void __launch_bounds__(128) paged_decode_attn_kernel(
     for (int e = 0; e < 4; ++e) acc[g][e] = 0.f;
   }
 
-  const int first_page = s0 / page_size;
-  const int last_page = (s1 - 1) / page_size;
-  const int per_warp = page_size / 4;
-  for (int lp = first_page; lp <= last_page && s1 > s0; ++lp) {
-    const int phys = block_table[static_cast<long>(row) * max_pages + lp];
-    const long page_base = (static_cast<long>(phys) * nkv + kvh) * page_size;
-    const int t_begin = lp * page_size + warp * per_warp;
-#pragma unroll 2
-    for (int i = 0; i < per_warp; ++i) {
-      const int t = t_begin + i;
-      if (t < s0 || t >= s1) continue;  // uniform across the warp
-      const long off = (page_base + (t - lp * page_size)) * kD + lane * 4;
-      uint2 kr = *reinterpret_cast<const uint2*>(k_pool + off);
-      uint2 vr = *reinterpret_cast<const uint2*>(v_pool + off);
-      const __nv_bfloat16* kb = reinterpret_cast<const __nv_bfloat16*>(&kr);
-      const __nv_bfloat16* vb = reinterpret_cast<const __nv_bfloat16*>(&vr);
-      float kf[4], vf[4];
+  const int* bt = a.block_table + static_cast<long>(row) * a.max_pages;
+  // chunks of 32 keys, aligned to 32; warps take chunks round-robin
+  const int first_chunk = k_begin >> 5;
+  const int last_chunk = (k_end - 1) >> 5;
+  for (int c = first_chunk + warp; c <= last_chunk && k_end > k_begin; c += kWarps) {
+    const int t = c * 32 + lane;
+    const bool valid = t >= k_begin && t < k_end;
+    const int page = valid ? bt[t / a.page_size] : bt[(c * 32) / a.page_size];
+    const long kv_off = ((static_cast<long>(page) * a.nkv + kvh) * a.page_size + (t % a.page_size)) * kD;
+    float s[G];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        kf[e] = __bfloat162float(kb[e]);
-        vf[e] = __bfloat162float(vb[e]);
+    for (int g = 0; g < G; ++g) s[g] = 0.f;
+    if (valid) {
+      const uint4* kr = reinterpret_cast<const uint4*>(a.k_pool + kv_off);
+#pragma unroll 4
+      for (int q8 = 0; q8 < kD / 8; ++q8) {
+        const uint4 raw = kr[q8];
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = __bfloat1622float2(k2[e]);
+          kf[2 * e] = f2.x;
+          kf[2 * e + 1] = f2.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&q_s[g][q8 * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&q_s[g][q8 * 8 + 4]);
+          s[g] = fmaf(qa.x, kf[0], s[g]);
+          s[g] = fmaf(qa.y, kf[1], s[g]);
+          s[g] = fmaf(qa.z, kf[2], s[g]);
+          s[g] = fmaf(qa.w, kf[3], s[g]);
+          s[g] = fmaf(qb.x, kf[4], s[g]);
+          s[g] = fmaf(qb.y, kf[5], s[g]);
+          s[g] = fmaf(qb.z, kf[6], s[g]);
+          s[g] = fmaf(qb.w, kf[7], s[g]);
+        }
       }
+    }
+    float p[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float sv = valid ? s[g] : -INFINITY;
+      const float cmax = warp_max(sv);
+      const float mn = fmaxf(m[g], cmax);
+      const float corr = exp2f(m[g] - mn);  // m = -inf at first: exp2(-inf) = 0
+      p[g] = valid ? exp2f(sv - mn) : 0.f;
+      l[g] = l[g] * corr + warp_sum(p[g]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[g][e] *= corr;
+      m[g] = mn;
+    }
+    // PV: lane owns dims [4*lane, 4*lane+4)
+    const int n_valid_hi = min(32, k_end - c * 32);
+    const int n_valid_lo = max(0, k_begin - c * 32);
+    for (int j = n_valid_lo; j < n_valid_hi; ++j) {
+      const int tj = c * 32 + j;
+      const int pg = bt[tj / a.page_size];
+      const long off = ((static_cast<long>(pg) * a.nkv + kvh) * a.page_size + (tj % a.page_size)) * kD + lane * 4;
+      const uint2 vr = *reinterpret_cast<const uint2*>(a.v_pool + off);
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vr);
+      const float2 v01 = __bfloat1622float2(v2[0]);
+      const float2 v23 = __bfloat1622float2(v2[1]);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float s = qv[g][0] * kf[0] + qv[g][1] * kf[1] + qv[g][2] * kf[2] + qv[g][3] * kf[3];
-        s = warp_sum(s);
-        const float mn = fmaxf(m[g], s);
-        const float corr = exp2f(m[g] - mn);
-        const float p = exp2f(s - mn);
-        l[g] = l[g] * corr + p;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] = acc[g][e] * corr + p * vf[e];
-        m[g] = mn;
+        const float pj = __shfl_sync(0xffffffffu, p[g], j);
+        acc[g][0] = fmaf(pj, v01.x, acc[g][0]);
+        acc[g][1] = fmaf(pj, v01.y, acc[g][1]);
+        acc[g][2] = fmaf(pj, v23.x, acc[g][2]);
+        acc[g][3] = fmaf(pj, v23.y, acc[g][3]);
       }
     }
   }
 
-  // merge the 4 warps
-  __shared__ float sm_m[4][kMaxGroup], sm_l[4][kMaxGroup];
-  __shared__ float sm_acc[4][kMaxGroup][kD];
+  // ---- merge warps
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     if (lane == 0) {
-      sm_m[warp][g] = m[g];
-      sm_l[warp][g] = l[g];
+      m_s[warp][g] = m[g];
+      l_s[warp][g] = l[g];
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) sm_acc[warp][g][lane * 4 + e] = acc[g][e];
+    for (int e = 0; e < 4; ++e) acc_s[warp][g][lane * 4 + e] = acc[g][e];
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
-    const int g = idx / kD, d = idx - g * kD;
+  const long head_base = static_cast<long>(row) * a.nq + kvh * G;
+  for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
+    const int g = i / kD, d = i - g * kD;
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm_m[w][g]);
-    float lsum = 0.f, o = 0.f;
+    for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, m_s[w][g]);
+    float ls = 0.f, o = 0.f;
     if (mx > -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float c = exp2f(sm_m[w][g] - mx);
-        lsum += sm_l[w][g] * c;
-        o += sm_acc[w][g][d] * c;
+      for (int w = 0; w < kWarps; ++w) {
+        const float cf = exp2f(m_s[w][g] - mx);
+        ls += l_s[w][g] * cf;
+        o += acc_s[w][g][d] * cf;
       }
     }
-    const float res = lsum > 0.f ? o / lsum : 0.f;
-    out[(static_cast<long>(row) * nq + kvh * G + g) * kD + d] = __float2bfloat16(res);
+    if (a.splits == 1) {
+      a.out[(head_base + g) * kD + d] = __float2bfloat16(ls > 0.f ? o / ls : 0.f);
+    } else {
+      const long pidx = (head_base + g) * a.splits + split;
+      a.part_acc[pidx * kD + d] = o;
+      if (d == 0) {
+        a.part_ml[pidx * 2] = mx;
+        a.part_ml[pidx * 2 + 1] = ls;
+      }
+    }
+  }
+  if (a.splits == 1) return;
+
+  // ---- last CTA of this (row, kv head) merges the splits
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = a.counters + static_cast<long>(row) * a.nkv + kvh;
+    const int prev = atomicAdd(ctr, 1);
+    is_last = (prev == a.splits - 1);
+    if (is_last) *ctr = 0;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
+    const int g = i / kD, d = i - g * kD;
+    const long pbase = (head_base + g) * a.splits;
+    float mx = -INFINITY;
+    for (int sp = 0; sp < a.splits; ++sp) mx = fmaxf(mx, __ldcg(a.part_ml + (pbase + sp) * 2));
+    float ls = 0.f, o = 0.f;
+    if (mx > -INFINITY) {
+      for (int sp = 0; sp < a.splits; ++sp) {
+        const float ms = __ldcg(a.part_ml + (pbase + sp) * 2);
+        if (ms == -INFINITY) continue;
+        const float cf = exp2f(ms - mx);
+        ls += __ldcg(a.part_ml + (pbase + sp) * 2 + 1) * cf;
+        o += __ldcg(a.part_acc + (pbase + sp) * kD + d) * cf;
+      }
+    }
+    a.out[(head_base + g) * kD + d] = __float2bfloat16(ls > 0.f ? o / ls : 0.f);
   }
 }
 
 }  // namespace
 
+// scratch: optional fp32 buffer of at least rows*nq*splits*(D+2) floats plus
+// rows*nkv ints for the counters (zero-initialised once); required when the
+// launch is split.
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
-                            torch::Tensor out, double scale) {
+                            torch::Tensor out, double scale, int64_t splits,
+                            c10::optional<torch::Tensor> scratch) {
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.is_contiguous(), "q must be contiguous bf16");
   TORCH_CHECK(k_pool.dim() == 4 && k_pool.size(3) == kD, "k_pool must be [pages, nkv, page, 128]");
@@ -136,28 +244,46 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
   const int nq = static_cast<int>(q.size(1));
   const int nkv = static_cast<int>(k_pool.size(1));
   const int page = static_cast<int>(k_pool.size(2));
-  TORCH_CHECK(page % 4 == 0, "page size must be a multiple of 4");
   TORCH_CHECK(nq % nkv == 0, "nq must be a multiple of nkv");
   const int G = nq / nkv;
-  const float scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
-  auto stream = at::cuda::getCurrentCUDAStream();
-  const int blocks = rows * nkv;
+  const int max_pages = static_cast<int>(block_table.size(1));
+  DecodeAttnArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k_pool = reinterpret_cast<const __nv_bfloat16*>(k_pool.data_ptr());
+  a.v_pool = reinterpret_cast<const __nv_bfloat16*>(v_pool.data_ptr());
+  a.block_table = block_table.data_ptr<int>();
+  a.start = start.data_ptr<int>();
+  a.len = len.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.nq = nq;
+  a.nkv = nkv;
+  a.page_size = page;
+  a.max_pages = max_pages;
+  a.splits = static_cast<int>(std::max<int64_t>(1, splits));
+  const int capacity = max_pages * page;
+  a.keys_per_split = ((capacity + a.splits - 1) / a.splits + 31) / 32 * 32;
+  a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
+  if (a.splits > 1) {
+    TORCH_CHECK(scratch.has_value() && scratch->defined() && scratch->scalar_type() == torch::kFloat32,
+                "split decode attention needs an fp32 scratch buffer");
+    const long need_f = static_cast<long>(rows) * nq * a.splits * (kD + 2);
+    const long need = need_f + static_cast<long>(rows) * nkv;
+    TORCH_CHECK(scratch->numel() >= need, "decode-attention scratch too small: need ", need, " floats");
+    float* base = scratch->data_ptr<float>();
+    a.part_acc = base;
+    a.part_ml = base + static_cast<long>(rows) * nq * a.splits * kD;
+    a.counters = reinterpret_cast<int*>(base + need_f);
+  }
+  const int blocks = rows * nkv * a.splits;
   if (blocks == 0) return;
-#define GB_ATT(GV)                                                                                   \
-  paged_decode_attn_kernel<GV><<<blocks, 128, 0, stream>>>(                                          \
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),                                          \
-      reinterpret_cast<const __nv_bfloat16*>(k_pool.data_ptr()),                                     \
-      reinterpret_cast<const __nv_bfloat16*>(v_pool.data_ptr()), block_table.data_ptr<int>(),        \
-      start.data_ptr<int>(), len.data_ptr<int>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), \
-      nq, nkv, page, static_cast<int>(block_table.size(1)), scale_log2)
+  auto stream = at::cuda::getCurrentCUDAStream();
   switch (G) {
-    case 1: GB_ATT(1); break;
-    case 2: GB_ATT(2); break;
-    case 4: GB_ATT(4); break;
-    case 8: GB_ATT(8); break;
+    case 1: paged_decode_attn_kernel<1><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    case 2: paged_decode_attn_kernel<2><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    case 4: paged_decode_attn_kernel<4><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    case 8: paged_decode_attn_kernel<8><<<blocks, kWarps * 32, 0, stream>>>(a); break;
     default: TORCH_CHECK(false, "unsupported GQA group size ", G);
   }
-#undef GB_ATT
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -242,6 +242,8 @@ struct RopeArgs {
   int max_pages;
   int page_size;
   const int64_t* row_of_token;  // token -> cache row (paged)
+  const int64_t* slot;          // token -> cache slot (paged); the rope position differs
+                                // from the slot when the row is left-padded
   int T, nq, nkv;
   float eps;
 };
@@ -281,7 +283,7 @@ __global__ void qk_norm_rope_kernel(RopeArgs a) {
     __nv_bfloat16* pool = is_k ? a.k_out : a.v_out;
     if (a.block_table != nullptr) {
       const long row = a.row_of_token[t];
-      const long p = a.pos[t];
+      const long p = a.slot[t];
       const int page = a.block_table[row * a.max_pages + p / a.page_size];
       const int off = static_cast<int>(p % a.page_size);
       dst = pool + ((static_cast<long>(page) * a.nkv + kvh) * a.page_size + off) * D;
@@ -526,7 +528,7 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::option
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
-                  int64_t nq, int64_t nkv, int64_t page_size, double eps) {
+                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps) {
   const c10::cuda::CUDAGuard guard(qkv.device());
   TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D row-major");
   RopeArgs a{};
@@ -543,7 +545,9 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
   if (block_table.has_value() && block_table->defined()) {
     a.block_table = block_table->data_ptr<int>();
     a.max_pages = static_cast<int>(block_table->size(1));
+    TORCH_CHECK(row_of_token.has_value() && slot.has_value(), "paged KV write needs row_of_token and slot");
     a.row_of_token = row_of_token->data_ptr<int64_t>();
+    a.slot = slot->data_ptr<int64_t>();
     a.page_size = static_cast<int>(page_size);
   }
   a.T = static_cast<int>(qkv.size(0));

@@ -124,10 +124,15 @@ def bench_decode(args) -> None:
         start = torch.zeros(rows, device="cuda", dtype=torch.int32)
         ln = torch.full((rows,), ctx, device="cuda", dtype=torch.int32)
         out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
-        ms = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D)))
+        from graspo_b200.engine.rollout import decode_attention_splits
+
+        splits = decode_attention_splits(rows, nkv, ctx)
+        scratch = torch.zeros(rows * nq * splits * (D + 2) + rows * nkv, device="cuda")
+        ms = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), splits,
+                                                        scratch))
         nbytes = 2 * rows * ctx * nkv * D * 2
         print(json.dumps({
-            "kernel": "paged_decode_attention", "rows": rows, "ctx": ctx, "ms": round(ms, 4),
+            "kernel": "paged_decode_attention", "rows": rows, "ctx": ctx, "splits": splits, "ms": round(ms, 4),
             "GBps": round(nbytes / ms / 1e6, 1),
             "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
         }), flush=True)

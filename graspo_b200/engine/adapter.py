@@ -1,0 +1,504 @@
+"""Qwen3 adapter: model setup, rollout, log-probs, GRASPO/SFT optimisation, checkpoints.
+
+One adapter per rank.  ``setup()`` initialises the TP x PP x DP process
+groups, the tokenizer, the model shard (with LoRA targets resolved against the
+family's canonical names, an optional PEFT warm start) and the optimizer.
+Execution is the fused sm_100a path on a GPU (``graspoflow.kernel_backend:
+fused``) and the plain-PyTorch path otherwise (CPU / gloo, or ``eager``).
+
+Optimisation semantics follow the reference (qwen3/adapter.py:367-476,
+qwen35_36/training.py:352-481): ``optimize_iterations_per_step`` passes over
+the replay data in a seeded shuffle, micro-batches of
+``optimize_prompt_batch_size`` completions, one clipped AdamW step per
+micro-batch, a step is skipped when the loss or gradient norm is not finite.
+Differences: the shuffle is computed identically on every rank instead of
+being broadcast; data-parallel replicas average their LoRA gradients before
+each step; the global gradient norm spans all TP/PP ranks; TP input
+gradients of column-parallel projections are all-reduced.
+"""
+
+from __future__ import annotations
+
+import json
+import math
+import random
+import time
+from pathlib import Path
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from graspo_b200.core.buffer import Experience
+from graspo_b200.core.chat_template import render_messages
+from graspo_b200.core.completion import ParsedCompletion
+from graspo_b200.core.lora_targets import resolve_lora_target_modules
+from graspo_b200.core.loss import GRASPOLoss
+from graspo_b200.core.tool_parser import parse_qwen_tool_completion
+from graspo_b200.engine.optim import FlatAdamW, lr_lambda
+from graspo_b200.engine.runtime import NativeGeneration
+from graspo_b200.models.config import load_decoder_config, lora_available_targets
+from graspo_b200.models.loader import SafetensorIndex
+from graspo_b200.models.qwen3 import EagerLoRA, Qwen3Model, eager_stage_forward, eager_token_logprobs
+from graspo_b200.parallel import state as pstate
+from graspo_b200.parallel.placement import build_placement_plan, placement_summary
+
+
+def _dtype(name: str) -> torch.dtype:
+    n = str(name).lower()
+    return {"bf16": torch.bfloat16, "bfloat16": torch.bfloat16, "fp16": torch.float16, "float16": torch.float16,
+            "fp32": torch.float32, "float32": torch.float32}[n]
+
+
+def collate(items: list[Experience], device: torch.device, pad_id: int):
+    """Right-pad experiences to a common length and move them to ``device``."""
+    S = max(int(e.sequences.shape[0]) for e in items)
+    B = len(items)
+    seq = torch.full((B, S), pad_id, dtype=torch.long)
+    att = torch.zeros((B, S), dtype=torch.bool)
+    old = torch.zeros((B, S - 1), dtype=torch.float32)
+    adv = torch.zeros((B, S - 1), dtype=torch.float32)
+    act = torch.zeros((B, S - 1), dtype=torch.bool)
+    for i, e in enumerate(items):
+        n = int(e.sequences.shape[0])
+        seq[i, :n] = e.sequences
+        att[i, :n] = e.attention_mask.bool()
+        old[i, : n - 1] = e.old_log_probs
+        adv[i, : n - 1] = e.advantages
+        act[i, : n - 1] = e.action_mask.bool()
+    pin = device.type == "cuda"
+    move = (lambda t: t.pin_memory().to(device, non_blocking=True)) if pin else (lambda t: t.to(device))
+    return move(seq), move(att), move(old), move(adv), move(act)
+
+
+class Qwen3Adapter:
+    completion_parser_name = "qwen_tool_call"
+
+    def __init__(self, config: Any) -> None:
+        self.config = config
+        self.ps: pstate.ParallelState | None = None
+        self.model: Qwen3Model | None = None
+        self.tokenizer = None
+        self.optimizer: FlatAdamW | None = None
+        self.placement = None
+        self._train_batch_call_index = 0
+        self.loss_fn = GRASPOLoss(config.training.policy_ratio_clip_eps)
+
+    # ------------------------------------------------------------ properties
+    @property
+    def rank(self) -> int:
+        return self.ps.rank if self.ps else 0
+
+    @property
+    def tp_rank(self) -> int:
+        return self.ps.tp_rank if self.ps else 0
+
+    @property
+    def device(self) -> torch.device:
+        return self.ps.device if self.ps else torch.device("cpu")
+
+    @property
+    def fused(self) -> bool:
+        return self.device.type == "cuda" and self.config.graspoflow.kernel_backend == "fused"
+
+    def is_primary(self) -> bool:
+        return self.rank == 0
+
+    # ------------------------------------------------------------ setup
+    def setup(self) -> None:
+        cfg = self.config
+        flow = cfg.graspoflow
+        self.ps = pstate.initialize(flow.tp_size, flow.pp_size, flow.dp_size, timeout_sec=flow.pg_timeout_sec)
+        if self.ps.pp_size > 1:
+            raise NotImplementedError("pipeline-parallel execution is provided by PipelineQwen3Adapter")
+        model_path = Path(cfg.model.model_path)
+        if not model_path.exists():
+            raise FileNotFoundError(f"model.model_path does not exist: {model_path}")
+        from graspo_b200.utils.tokenizer import load_tokenizer
+
+        self.tokenizer = load_tokenizer(model_path)
+        hf = load_decoder_config(model_path)
+        if hf.family != "qwen3":
+            raise ValueError(f"Qwen3Adapter serves the dense qwen3 family; got {hf.family}")
+        targets = resolve_lora_target_modules(
+            cfg.lora.target_modules or (cfg.lora.target_preset,), available=lora_available_targets(hf)
+        )
+        self.placement = build_placement_plan(
+            strategy=flow.placement_strategy, model_family=hf.family, num_hidden_layers=hf.num_hidden_layers,
+            tp_size=self.ps.tp_size, pp_size=self.ps.pp_size, tp_rank=self.ps.tp_rank, pp_rank=self.ps.pp_rank,
+            layer_types=hf.layer_types, manual_ranges=flow.layer_ranges,
+        )
+        dtype = _dtype(cfg.model.torch_dtype)
+        if self.device.type == "cpu" and dtype != torch.float32:
+            dtype = torch.float32
+        loader = SafetensorIndex(model_path)
+        self.model = Qwen3Model(
+            hf, loader, ps=self.ps, local_layers=list(self.placement.local_layer_indices),
+            include_embed=self.placement.include_embeddings, include_head=self.placement.include_lm_head,
+            lora_targets=set(targets.resolved), lora_r=cfg.lora.r, lora_alpha=cfg.lora.alpha,
+            lora_dropout=cfg.lora.dropout, dtype=dtype, device=self.device, seed=cfg.training.seed,
+            gradient_checkpointing=cfg.model.gradient_checkpointing,
+        )
+        loader.close()
+        missing = sorted(set(targets.resolved) - set(self.model.enabled_lora_target_names()))
+        if missing:
+            raise ValueError("Resolved LoRA target(s) are not implemented by this model: " + ", ".join(missing))
+        if cfg.lora.adapter_path:
+            from graspo_b200.models.lora_io import load_peft_adapter
+
+            load_peft_adapter(self.model, cfg.lora.adapter_path)
+        self._build_optimizer()
+        self._engine = None
+        self._fused = None
+        if self.fused:
+            from graspo_b200.engine.rollout import FusedRolloutEngine
+            from graspo_b200.models.fused import FusedQwen3
+
+            self.model.ensure_transposed()
+            self._fused = FusedQwen3(self.model)
+            self._engine = FusedRolloutEngine(self.model, self._fused, page_size=flow.kv_page_size,
+                                              use_graph=flow.cuda_graph_decode)
+        else:
+            from graspo_b200.engine.rollout import EagerRolloutEngine
+
+            self._engine = EagerRolloutEngine(self.model)
+        self._print_rank0({
+            "event": "adapter_ready", "rank": self.rank, "tp_rank": self.tp_rank, "tp_size": self.ps.tp_size,
+            "dp_size": self.ps.dp_size, "pp_size": self.ps.pp_size, "backend": "fused" if self.fused else "eager",
+            "trainable_parameters_local": int(self.model.lora.numel),
+            "lora_target_modules": sorted(targets.resolved),
+            "lora_target_signature": self.model.lora_target_signature(),
+            "placement": placement_summary(self.placement),
+        })
+
+    def _build_optimizer(self) -> None:
+        tr = self.config.training
+        sched = tr.lr_scheduler
+        fn = None
+        if sched.type != "constant":
+            if int(tr.max_steps) <= 0:
+                raise ValueError("lr_scheduler.type other than constant requires training.max_steps > 0")
+            total = int(tr.max_steps) * int(tr.optimize_iterations_per_step) * int(tr.rollout_group_size)
+            if total <= int(sched.warmup_steps):
+                raise ValueError(f"lr_scheduler: total steps ({total}) must exceed warmup_steps ({sched.warmup_steps})")
+            fn = lr_lambda(sched.type, int(sched.warmup_steps), total, float(sched.min_lr_ratio))
+        self.optimizer = FlatAdamW(self.model.lora, lr=tr.learning_rate, weight_decay=tr.weight_decay,
+                                   schedule=fn, ps=self.ps)
+
+    def _print_rank0(self, payload: dict) -> None:
+        if self.rank == 0:
+            print(json.dumps(payload, ensure_ascii=False, default=str), flush=True)
+
+    # ------------------------------------------------------------ prompts
+    def format_messages(self, messages, chat_template_kwargs=None, *, tools=None) -> str:
+        return render_messages(self.tokenizer, messages, chat_template_kwargs, tools=tools)
+
+    def encode_prompts(self, message_batches, tool_batches, max_prompt_length, chat_template_kwargs) -> list[list[int]]:
+        tool_batches = tool_batches or [None] * len(message_batches)
+        texts = [self.format_messages(msgs, chat_template_kwargs, tools=tools)
+                 for msgs, tools in zip(message_batches, tool_batches, strict=True)]
+        enc = self.tokenizer(texts, truncation=True, max_length=int(max_prompt_length), padding=False,
+                             add_special_tokens=False)
+        return [list(ids) for ids in enc["input_ids"]]
+
+    # ------------------------------------------------------------ rollout
+    def generate_from_token_ids(self, prompts: list[list[int]], *, rollout_group_size: int, max_new_tokens: int,
+                                temperature: float, top_p: float, seed: int | None = None):
+        tok = self.tokenizer
+        eos = int(tok.eos_token_id)
+        pad = int(tok.pad_token_id if tok.pad_token_id is not None else eos)
+        flow = self.config.graspoflow
+        seed = int(self.config.training.seed) * 1_000_003 + self._train_batch_call_index if seed is None else seed
+        # every TP rank must draw the same tokens: derive the seed from the DP replica only
+        seed += 7919 * (self.ps.dp_rank if self.ps else 0)
+        return self._engine.generate(prompts, group_size=rollout_group_size, max_new_tokens=max_new_tokens,
+                                     temperature=temperature, top_p=top_p, eos_id=eos, pad_id=pad,
+                                     ignore_eos=bool(flow.benchmark_ignore_eos), seed=seed)
+
+    def generate_groups(self, *, message_batches=None, tool_batches=None, rollout_group_size: int,
+                        max_new_tokens: int, max_prompt_length: int | None = None, temperature: float = 1.0,
+                        top_p: float = 1.0, chat_template_kwargs: dict | None = None, **_: Any) -> list[NativeGeneration]:
+        if not message_batches:
+            return []
+        t0 = time.monotonic()
+        max_len = int(max_prompt_length or self.config.data.max_prompt_length)
+        prompts = self.encode_prompts(message_batches, tool_batches, max_len, chat_template_kwargs)
+        tokenize_sec = time.monotonic() - t0
+        res = self.generate_from_token_ids(prompts, rollout_group_size=rollout_group_size,
+                                           max_new_tokens=max_new_tokens, temperature=temperature, top_p=top_p)
+        return self._generations(res, tokenize_sec, time.monotonic() - t0)
+
+    def generate_sample_groups(self, *, samples: list[Any], **kwargs: Any) -> list[NativeGeneration]:
+        if any(getattr(s, "media", None) for s in samples):
+            raise NotImplementedError("image/video samples need the multimodal adapter (VisionQwen3Adapter)")
+        return self.generate_groups(message_batches=[s.messages for s in samples],
+                                    tool_batches=[s.tools for s in samples], **kwargs)
+
+    def generate_group(self, *, messages, tools=None, **kwargs) -> NativeGeneration:
+        return self.generate_groups(message_batches=[messages], tool_batches=[tools], **kwargs)[0]
+
+    def _generations(self, res, tokenize_sec: float, elapsed: float) -> list[NativeGeneration]:
+        tok = self.tokenizer
+        pad = int(tok.pad_token_id if tok.pad_token_id is not None else tok.eos_token_id)
+        n, P = res.prompt_ids.shape
+        G = res.group_size
+        max_new = res.tokens.shape[1]
+        seqs = torch.cat([res.prompt_ids.repeat_interleave(G, 0), res.tokens], dim=1)
+        attn = seqs.ne(pad)
+        action = torch.zeros((seqs.shape[0], seqs.shape[1] - 1), dtype=torch.bool)
+        action[:, P - 1:] = True
+        action &= attn[:, 1:]
+        texts = tok.batch_decode(
+            [row[:length].tolist() for row, length in zip(res.tokens, res.gen_lens, strict=True)],
+            skip_special_tokens=True,
+        )
+        decode_tokens = int(sum(res.gen_lens))
+        out = []
+        for i in range(n):
+            sl = slice(i * G, (i + 1) * G)
+            out.append(NativeGeneration(
+                sequences=seqs[sl], attention_mask=attn[sl], action_mask=action[sl], completions=texts[sl],
+                prompt_len=P,
+                metadata={
+                    "adapter": "graspoflow", "rollout_group_size": G, "prefill_len": P,
+                    "prompt_lens": [res.prompt_lens[i]], "generated_tokens_max": max_new,
+                    "rollout_use_kv_cache": True, "rollout_paged_kv": self.fused,
+                    "tokenize_sec": round(tokenize_sec / n, 6), "prefill_sec": round(res.prefill_sec / n, 6),
+                    "decode_sec": round(res.decode_sec / n, 6), "decode_tokens": decode_tokens // n,
+                    "decode_steps": res.decode_steps, "rollout_elapsed_sec": round(elapsed, 6),
+                    "tp_rank": self.tp_rank, "tp_size": self.ps.tp_size,
+                },
+            ))
+        return out
+
+    def parse_completion(self, completion: str, sample: Any | None = None) -> ParsedCompletion:
+        return parse_qwen_tool_completion(
+            completion, expect_tool_calls=bool(getattr(sample, "expects_tool_calls", False)),
+            tools=getattr(sample, "tools", None),
+        )
+
+    # ------------------------------------------------------------ log-probs
+    def _token_budget_chunks(self, B: int, S: int, budget: int = 65536) -> list[slice]:
+        per = max(1, budget // max(S, 1))
+        return [slice(i, min(B, i + per)) for i in range(0, B, per)]
+
+    @torch.no_grad()
+    def sequence_log_probs(self, sequences, attention_mask, metadata: Any | None = None) -> torch.Tensor:
+        dev = self.device
+        seq = sequences.to(dev)
+        mask = attention_mask.to(dev).bool()
+        outs = []
+        for sl in self._token_budget_chunks(seq.shape[0], seq.shape[1]):
+            outs.append(self._logprobs(seq[sl], mask[sl], train=False)[0])
+        return torch.cat(outs, 0)
+
+    def _logprobs(self, seq, mask, *, train: bool, seed: int = 0, targets=None):
+        """log p(targets) per position, [B, S-1] fp32 (targets default to seq[:, 1:]).
+
+        In training the second return value carries what the backward needs.
+        """
+        B, S = seq.shape
+        tgt = seq[:, 1:] if targets is None else targets
+        if self.fused:
+            from graspo_b200.models.fused import AttnMeta
+
+            f = self._fused
+            meta = AttnMeta.from_mask(mask)
+            xL, inputs = f.stage_forward(f.embed(seq), meta, train=train, seed=seed, keep_inputs=train)
+            hn, rstd = f.final_norm(xL)
+            full = torch.zeros_like(seq)
+            full[:, :-1] = tgt
+            full = full.reshape(-1)
+            logp_full, lse = f.token_logprobs(hn, full)
+            logp = logp_full.view(B, S)[:, :-1].contiguous()
+            return logp, ((meta, inputs, xL, hn, rstd, full, lse) if train else None)
+        lora = EagerLoRA(self.model.lora, requires_grad=train)
+        with torch.set_grad_enabled(train):
+            hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train)
+            logp = eager_token_logprobs(self.model, hidden[:, :-1], tgt)
+        return logp, lora
+
+    def _fused_backward_from_logp_grad(self, ctx, dlogp: torch.Tensor, seed: int) -> None:
+        """Backprop d(loss)/d(logp) [B, S-1] through the head and all layers."""
+        from graspo_b200.ops._ext import ext
+
+        meta, inputs, xL, hn, rstd, full_targets, lse = ctx
+        B, S = meta.B, meta.S
+        g = torch.zeros(B, S, device=dlogp.device, dtype=torch.float32)
+        g[:, :-1] = dlogp
+        dhn = self._fused.token_logprobs_backward(hn, full_targets, lse, g.view(-1))
+        dxL = torch.empty_like(xL)
+        ext().rmsnorm_bwd(dhn, xL, self.model.norm, rstd, None, dxL, self.model.cfg.rms_norm_eps)
+        del dhn
+        self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed)
+
+    # ------------------------------------------------------------ training
+    def _dp_average_grads(self) -> None:
+        ps = self.ps
+        g = self.model.lora.grads
+        if ps.dp_size > 1 and ps.distributed:
+            dist.all_reduce(g, group=ps.dp_group)
+            g.div_(ps.dp_size)
+
+    def _tp_sync_replicated_grads(self) -> None:
+        ps = self.ps
+        rep = self.model.lora.replicated_numel
+        if ps.tp_size > 1 and ps.distributed and rep:
+            dist.all_reduce(self.model.lora.grads[:rep], group=ps.tp_group)
+
+    def _backward_grpo(self, seq, mask, old, adv, act, clip_eps: float, seed: int):
+        """Forward + GRPO loss + backward into the flat grad buffer; returns loss (device)."""
+        B, S = seq.shape
+        if self.fused:
+            from graspo_b200.ops._ext import ext
+
+            logp, ctx = self._logprobs(seq, mask, train=True, seed=seed)
+            loss = torch.zeros(1, device=seq.device, dtype=torch.float32)
+            dlogp = torch.empty_like(logp)
+            ext().grpo_loss(logp, old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous(), clip_eps,
+                            1.0, loss, dlogp, None)
+            self._fused_backward_from_logp_grad(ctx, dlogp, seed)
+            return loss
+        logp, lora = self._logprobs(seq, mask, train=True)
+        self.loss_fn.policy_ratio_clip_eps = clip_eps
+        loss = self.loss_fn(logp, old, adv, act)
+        if torch.isfinite(loss):
+            loss.backward()
+            lora.accumulate_grads()
+        return loss.detach().reshape(1)
+
+    def _shared_training_indices(self, count: int, optimize_round: int) -> list[int]:
+        seed = int(self.config.training.seed) + self._train_batch_call_index * 1_000_003 + int(optimize_round)
+        idx = list(range(count))
+        random.Random(seed).shuffle(idx)
+        return idx
+
+    def train_batch(self, experiences: list[Experience], *, policy_ratio_clip_eps: float,
+                    optimize_iterations_per_step: int, max_grad_norm: float) -> dict[str, Any]:
+        tok = self.tokenizer
+        pad = int(tok.pad_token_id if tok.pad_token_id is not None else tok.eos_token_id)
+        bs = int(self.config.training.optimize_prompt_batch_size)
+        t0 = time.monotonic()
+        lora_before = self.model.lora.parameter_norm()
+        losses, norms = [], []
+        steps = 0
+        for rnd in range(int(optimize_iterations_per_step)):
+            idx = self._shared_training_indices(len(experiences), rnd)
+            for start in range(0, len(idx) - bs + 1, bs):
+                batch = [experiences[i] for i in idx[start : start + bs]]
+                seq, att, old, adv, act = collate(batch, self.device, pad)
+                self.optimizer.zero_grad()
+                seed = (int(self.config.training.seed) << 20) ^ (self._train_batch_call_index << 10) ^ steps
+                loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed)
+                self._tp_sync_replicated_grads()
+                self._dp_average_grads()
+                norm = self.optimizer.step(max_grad_norm, loss)
+                losses.append(loss)
+                norms.append(norm)
+                steps += 1
+        self._train_batch_call_index += 1
+        loss_vals = [float(x) for x in torch.cat(losses).cpu()] if losses else []
+        norm_vals = [float(x) for x in torch.cat([n.reshape(1) for n in norms]).cpu()] if norms else []
+        skipped = int(self.optimizer.skipped.item())
+        finite = [v for v in loss_vals if math.isfinite(v)]
+        lora_after = self.model.lora.parameter_norm()
+        metrics = {
+            "optimized": steps > 0,
+            "replay_buffer_trainable_completion_count": len(experiences),
+            "optimizer_steps": steps,
+            "skipped_nonfinite": skipped,
+            "loss_mean": sum(finite) / len(finite) if finite else None,
+            "grad_norm_mean": sum(norm_vals) / len(norm_vals) if norm_vals else None,
+            "nonzero_grad_count": int((self.model.lora.grads != 0).any().item()) * len(self.model.lora.modules),
+            "lora_norm_before": lora_before,
+            "lora_norm_after": lora_after,
+            "lora_norm_delta": lora_after - lora_before,
+            "train_batch_total_sec": time.monotonic() - t0,
+            "micro_batch_count": steps,
+            "current_lr": self.optimizer.lr,
+            "activation_checkpointing_enabled": bool(self.model.gradient_checkpointing),
+        }
+        return self._aggregate_rank_metrics(metrics)
+
+    def train_batch_sft(self, sft_batches: list[dict[str, Any]], *, optimize_iterations_per_step: int,
+                        max_grad_norm: float) -> dict[str, Any]:
+        """Supervised steps on tokenized batches (labels -100 on the prompt)."""
+        tok = self.tokenizer
+        pad = int(tok.pad_token_id if tok.pad_token_id is not None else tok.eos_token_id)
+        fbs = int(self.config.graspoflow.forward_batch_size)
+        losses, steps = [], 0
+        t0 = time.monotonic()
+        for _ in range(int(optimize_iterations_per_step)):
+            for start in range(0, len(sft_batches), fbs):
+                chunk = sft_batches[start : start + fbs]
+                S = max(int(b["input_ids"].shape[0]) for b in chunk)
+                ids = torch.full((len(chunk), S), pad, dtype=torch.long)
+                labels = torch.full((len(chunk), S), -100, dtype=torch.long)
+                mask = torch.zeros((len(chunk), S), dtype=torch.bool)
+                for i, b in enumerate(chunk):
+                    n = int(b["input_ids"].shape[0])
+                    ids[i, :n], labels[i, :n], mask[i, :n] = b["input_ids"], b["labels"], True
+                ids, labels, mask = ids.to(self.device), labels.to(self.device), mask.to(self.device)
+                self.optimizer.zero_grad()
+                loss = self._backward_sft(ids, mask, labels, steps)
+                self._tp_sync_replicated_grads()
+                self._dp_average_grads()
+                self.optimizer.step(max_grad_norm, loss)
+                losses.append(loss)
+                steps += 1
+        vals = [float(x) for x in torch.cat(losses).cpu()] if losses else []
+        return self._aggregate_rank_metrics({
+            "optimized": steps > 0, "optimizer_steps": steps,
+            "loss_mean": sum(vals) / len(vals) if vals else None,
+            "train_batch_total_sec": time.monotonic() - t0, "current_lr": self.optimizer.lr,
+        })
+
+    def _backward_sft(self, ids, mask, labels, step: int):
+        """Token cross-entropy = -mean log p(label) over labelled positions
+        (the quantity of core.loss.sft_cross_entropy_loss, without logits)."""
+        tgt = labels[:, 1:]
+        valid = tgt.ne(-100)
+        denom = valid.sum().clamp_min(1)
+        safe = torch.where(valid, tgt, torch.zeros_like(tgt))
+        if self.fused:
+            logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe)
+            loss = -(logp * valid).sum() / denom
+            self._fused_backward_from_logp_grad(ctx, -(valid.float() / denom), step)
+            return loss.detach().reshape(1)
+        logp, lora = self._logprobs(ids, mask, train=True, targets=safe)
+        loss = -(logp * valid).sum() / denom
+        loss.backward()
+        lora.accumulate_grads()
+        return loss.detach().reshape(1)
+
+    def _aggregate_rank_metrics(self, metrics: dict[str, Any]) -> dict[str, Any]:
+        local = {"rank": self.rank, "tp_rank": self.tp_rank, **metrics}
+        if not self.ps.distributed:
+            return {**metrics, "rank": self.rank, "tp_rank": self.tp_rank, "rank_metrics": [local]}
+        gathered: list[Any] = [None] * self.ps.world_size
+        dist.all_gather_object(gathered, local)
+        ranks = [g for g in gathered if g is not None]
+
+        def mean(key):
+            vals = [float(r[key]) for r in ranks if r.get(key) is not None]
+            return sum(vals) / len(vals) if vals else None
+
+        return {**metrics, "rank": self.rank, "tp_rank": self.tp_rank, "rank_metrics": ranks,
+                "global_optimizer_steps_sum": sum(int(r.get("optimizer_steps") or 0) for r in ranks),
+                "global_loss_mean": mean("loss_mean"), "global_grad_norm_mean": mean("grad_norm_mean"),
+                "global_lora_norm_delta_mean": mean("lora_norm_delta")}
+
+    # ------------------------------------------------------------ checkpoints
+    def save_checkpoint(self, path: str | Path, *, trainer_state: dict[str, Any] | None = None) -> None:
+        from graspo_b200.train.checkpoint import save_rank_checkpoint
+
+        save_rank_checkpoint(self, Path(path), trainer_state=trainer_state)
+
+    def load_checkpoint(self, path: str | Path) -> dict[str, Any] | None:
+        from graspo_b200.train.checkpoint import load_rank_checkpoint
+
+        return load_rank_checkpoint(self, Path(path))
+
+    def close(self) -> None:
+        self._engine = None
+        pstate.destroy()

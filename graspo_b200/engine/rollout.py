@@ -1,0 +1,481 @@
+"""Group rollout: prefill once per prompt, decode G completions per prompt.
+
+GRASPO samples ``G`` completions of every prompt.  The reference repeats each
+prompt G times and prefills all copies (reference: qwen3/adapter.py:190-230),
+grows its KV cache with ``torch.cat`` every token and synchronises with the
+host after every token to test for EOS (generation.py:249-276).  This engine:
+
+* prefills each *unique* prompt once and writes its K/V into pages that the G
+  rows of the group share through their block tables (prefix sharing: 1/G
+  of the prompt KV memory and prefill FLOPs);
+* keeps K/V in a preallocated paged pool ``[layers, pages, kv_heads, page, 128]``
+  and writes each new token's K/V in place from the QK-norm/RoPE kernel;
+* runs a decode step as one CUDA graph (embedding -> 36 x [norm + LoRA-down,
+  QKV GEMM, QK-norm/RoPE/KV-write, paged attention, O GEMM, norm, gate/up
+  GEMM with SwiGLU, down GEMM] -> LM head -> sampling + state update), with
+  all per-row state (next token, cache slot, position, length, finished) on
+  the device, and checks for "all rows finished" only every few steps.
+
+The decode GEMMs are "swap-AB": weights fill the 128-row side of the
+tensor-core tile and the decode batch the narrow side; the QKV / O / down
+projections split K across CTAs and accumulate fp32 partial sums that the
+next kernel consumes (and re-zeroes).
+
+``EagerRolloutEngine`` is the plain-PyTorch counterpart (CPU / tests).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from graspo_b200.models.qwen3 import (
+    EagerLoRA,
+    Qwen3Model,
+    _linear_lora,
+    apply_rope,
+    rmsnorm,
+)
+from graspo_b200.parallel.tp import copy_to_tp, reduce_from_tp
+
+
+@dataclass
+class RolloutResult:
+    prompt_ids: torch.Tensor      # [n, P] left-padded prompts (host)
+    prompt_lens: list[int]
+    tokens: torch.Tensor          # [rows, max_new] generated ids (host), pad after finish
+    gen_lens: list[int]           # generated tokens per row (up to and including EOS)
+    group_size: int
+    prefill_sec: float = 0.0
+    decode_sec: float = 0.0
+    decode_steps: int = 0
+
+
+def _sync(dev: torch.device) -> None:
+    if dev.type == "cuda":
+        torch.cuda.synchronize(dev)
+
+
+def decode_attention_splits(rows: int, nkv: int, capacity: int, sms: int = 148) -> int:
+    """Key-range splits so decode attention launches about 4 CTAs per SM."""
+    ctas = rows * nkv
+    want = max(1, -(-4 * sms // max(ctas, 1)))
+    return int(max(1, min(want, capacity // 128, 16)))
+
+
+def _round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def _gen_lengths(tokens: torch.Tensor, eos_id: int, ignore_eos: bool) -> list[int]:
+    if ignore_eos:
+        return [tokens.shape[1]] * tokens.shape[0]
+    lens = []
+    for row in tokens.tolist():
+        n = len(row)
+        for i, t in enumerate(row):
+            if t == eos_id:
+                n = i + 1
+                break
+        lens.append(n)
+    return lens
+
+
+class FusedRolloutEngine:
+    def __init__(self, model: Qwen3Model, fused, *, page_size: int = 64, use_graph: bool = True,
+                 graph_chunk: int = 16) -> None:
+        from graspo_b200.ops._ext import ext
+
+        self.m = model
+        self.f = fused
+        self.C = ext()
+        self.page = page_size
+        self.use_graph = use_graph
+        self.graph_chunk = graph_chunk
+        self._pool_shape = None
+        self.k_pool = self.v_pool = None
+
+    def _ensure_pool(self, num_pages: int) -> None:
+        m = self.m
+        shape = (len(m.layers), num_pages, m.nkv, self.page, m.D)
+        if self._pool_shape is None or self._pool_shape[1] < num_pages:
+            self.k_pool = self.v_pool = None
+            if m.device.type == "cuda":
+                torch.cuda.empty_cache()
+            self.k_pool = torch.empty(shape, device=m.device, dtype=m.dtype)
+            self.v_pool = torch.empty(shape, device=m.device, dtype=m.dtype)
+            self._pool_shape = shape
+
+    def _vocab_gather(self, local: torch.Tensor) -> torch.Tensor:
+        ps = self.m.ps
+        if ps.tp_size == 1:
+            return local
+        parts = torch.empty((ps.tp_size, *local.shape), device=local.device, dtype=local.dtype)
+        dist.all_gather_into_tensor(parts, local.contiguous(), group=ps.tp_group)
+        return parts.permute(1, 0, 2).reshape(local.shape[0], -1).contiguous()
+
+    def _lm_logits(self, xn: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from graspo_b200.ops.gemm import gemm
+
+        m = self.m
+        rows = xn.shape[0]
+        if rows <= 128:
+            local = gemm(m.lm_head, xn, out, swap=True, epilogue="store_f32")
+        else:
+            local = gemm(xn, m.lm_head, out, epilogue="store_f32")
+        return self._vocab_gather(local)
+
+    @torch.no_grad()
+    def generate(
+        self,
+        prompts: list[list[int]],
+        *,
+        group_size: int,
+        max_new_tokens: int,
+        temperature: float,
+        top_p: float,
+        eos_id: int,
+        pad_id: int,
+        ignore_eos: bool = False,
+        seed: int = 0,
+    ) -> RolloutResult:
+        import time
+
+        from graspo_b200.models.fused import AttnMeta
+        from graspo_b200.ops._ext import check_errors
+        from graspo_b200.ops.gemm import gemm
+
+        m, f, C = self.m, self.f, self.C
+        dev = m.device
+        n, G = len(prompts), int(group_size)
+        rows = n * G
+        lens = [max(1, len(p)) for p in prompts]
+        P = _round_up(max(lens), self.page)
+        prompt_pages = P // self.page
+        gen_pages = math.ceil(max_new_tokens / self.page)
+        num_pages = n * prompt_pages + rows * gen_pages
+        self._ensure_pool(num_pages)
+
+        ids = torch.full((n, P), pad_id, dtype=torch.long)
+        mask = torch.zeros((n, P), dtype=torch.bool)
+        for i, p in enumerate(prompts):
+            row = list(p) or [pad_id]
+            ids[i, P - len(row):] = torch.tensor(row, dtype=torch.long)
+            mask[i, P - len(row):] = True
+        ids_d = ids.to(dev, non_blocking=True)
+        mask_d = mask.to(dev, non_blocking=True)
+
+        bt = torch.empty(rows, prompt_pages + gen_pages, dtype=torch.int32)
+        for r in range(rows):
+            i = r // G
+            bt[r, :prompt_pages] = torch.arange(i * prompt_pages, (i + 1) * prompt_pages)
+            base = n * prompt_pages + r * gen_pages
+            bt[r, prompt_pages:] = torch.arange(base, base + gen_pages)
+        bt_d = bt.to(dev)
+
+        _sync(dev)
+        t0 = time.perf_counter()
+        # ---------------- prefill (unique prompts)
+        meta = AttnMeta.from_mask(mask_d)
+        kp, vp = self.k_pool, self.v_pool
+
+        def sink(layer_idx: int, k: torch.Tensor, v: torch.Tensor) -> None:
+            li = m.local_layers.index(layer_idx)
+            shape = (n, prompt_pages, self.page, m.nkv, m.D)
+            kp[li, : n * prompt_pages] = k.view(shape).permute(0, 1, 3, 2, 4).reshape(-1, m.nkv, self.page, m.D)
+            vp[li, : n * prompt_pages] = v.view(shape).permute(0, 1, 3, 2, 4).reshape(-1, m.nkv, self.page, m.D)
+
+        x = f.embed(ids_d)
+        for lw in m.layers:
+            x, _ = f.layer_forward(lw, x, meta, kv_sink=sink)
+        last = x.view(n, P, -1)[:, -1].contiguous()
+        xn, _ = f.final_norm(last)
+        logits0 = self._lm_logits(xn)
+        logits_rows = logits0.repeat_interleave(G, dim=0).contiguous()
+
+        # ---------------- decode state
+        st = {
+            "next_ids": torch.zeros(rows, dtype=torch.long, device=dev),
+            "slot": torch.full((rows,), P - 1, dtype=torch.long, device=dev),
+            "pos": torch.tensor([lens[r // G] - 1 for r in range(rows)], dtype=torch.long, device=dev),
+            "kv_len": torch.full((rows,), P, dtype=torch.int32, device=dev),
+            "finished": torch.zeros(rows, dtype=torch.uint8, device=dev),
+            "out": torch.full((rows, max_new_tokens), pad_id, dtype=torch.long, device=dev),
+            "start": torch.tensor([P - lens[r // G] for r in range(rows)], dtype=torch.int32, device=dev),
+        }
+        C.sample_append(logits_rows, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"],
+                        st["pos"], st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)
+        del logits0, logits_rows, x, last
+        _sync(dev)
+        t1 = time.perf_counter()
+
+        # ---------------- decode loop
+        steps = max_new_tokens - 1
+        bufs = self._decode_buffers(rows)
+        cap = (prompt_pages + gen_pages) * self.page
+        self._splits = decode_attention_splits(rows, m.nkv, cap)
+        bufs["attn_scratch"] = torch.zeros(rows * m.nq * self._splits * (m.D + 2) + rows * m.nkv,
+                                           device=dev, dtype=torch.float32)
+        row_ids = torch.arange(rows, dtype=torch.long, device=dev)
+
+        def step() -> None:
+            self._decode_step(st, bufs, bt_d, row_ids, P, temperature, top_p, seed, eos_id, pad_id, ignore_eos)
+
+        done = 0
+        if steps > 0:
+            if self.use_graph and dev.type == "cuda":
+                saved = {k: v.clone() for k, v in st.items()}
+                step()  # warm-up outside capture (sets kernel attributes, allocator pools)
+                for k, v in saved.items():
+                    st[k].copy_(v)
+                for ws in ("qkv_ws", "o_ws", "d_ws"):
+                    bufs[ws].zero_()
+                from graspo_b200.ops._ext import launches
+
+                graph = torch.cuda.CUDAGraph()
+                before = launches.count
+                with torch.cuda.graph(graph):
+                    step()
+                per_step = launches.count - before
+                launches.count = before
+                while done < steps:
+                    chunk = min(self.graph_chunk, steps - done)
+                    for _ in range(chunk):
+                        graph.replay()
+                    launches.add(per_step * chunk)
+                    done += chunk
+                    if not ignore_eos and bool(st["finished"].all()):
+                        break
+                del graph
+            else:
+                while done < steps:
+                    step()
+                    done += 1
+                    if not ignore_eos and done % self.graph_chunk == 0 and bool(st["finished"].all()):
+                        break
+        _sync(dev)
+        t2 = time.perf_counter()
+        check_errors(dev)
+        tokens = st["out"].cpu()
+        return RolloutResult(
+            prompt_ids=ids, prompt_lens=lens, tokens=tokens, gen_lens=_gen_lengths(tokens, eos_id, ignore_eos),
+            group_size=G, prefill_sec=t1 - t0, decode_sec=t2 - t1, decode_steps=done + 1,
+        )
+
+    def _decode_buffers(self, rows: int) -> dict[str, torch.Tensor]:
+        m = self.m
+        dev, dt = m.device, m.dtype
+        H = m.cfg.hidden_size
+        f32 = torch.float32
+        nqkv = m.q_local + 2 * m.kv_local
+        return {
+            "x_a": torch.empty(rows, H, device=dev, dtype=dt),
+            "x_b": torch.empty(rows, H, device=dev, dtype=dt),
+            "xn": torch.empty(rows, H, device=dev, dtype=dt),
+            "qkv_ws": torch.zeros(rows, nqkv, device=dev, dtype=f32),
+            "q": torch.empty(rows, m.nq, m.D, device=dev, dtype=dt),
+            "attn": torch.empty(rows, m.q_local, device=dev, dtype=dt),
+            "o_ws": torch.zeros(rows, H, device=dev, dtype=f32),
+            "act": torch.empty(rows, m.inter_local, device=dev, dtype=dt),
+            "d_ws": torch.zeros(rows, H, device=dev, dtype=f32),
+            "logits": torch.empty(rows, m.vocab_local, device=dev, dtype=f32),
+        }
+
+    @staticmethod
+    def _u(b: dict, name: str, rows: int, width: int, like: torch.Tensor) -> torch.Tensor:
+        key = f"{name}_{width}"
+        buf = b.get(key)
+        if buf is None:
+            buf = torch.zeros(rows, width, device=like.device, dtype=like.dtype)
+            b[key] = buf
+        return buf
+
+    def _decode_step(self, st, b, bt, row_ids, P, temperature, top_p, seed, eos_id, pad_id, ignore_eos) -> None:
+        from graspo_b200.ops.gemm import gemm
+
+        m, C = self.m, self.C
+        eps = m.cfg.rms_norm_eps
+        tp_group = m.ps.tp_group
+        tp = m.ps.tp_size
+        rows = row_ids.shape[0]
+        C.embedding(st["next_ids"], m.embed, b["x_a"])
+        scale = 1.0 / math.sqrt(m.D)
+        for li, lw in enumerate(m.layers):
+            L = m.lora.layer_layouts(lw.index, m.sizes)
+            first = li == 0
+            a_qkv = L.get("a_qkv")
+            uq = self._u(b, "u", rows, a_qkv.shape[0], b["xn"]) if a_qkv is not None else None
+            # x_a holds the residual stream; the previous layer's down-projection
+            # partial sums (d_ws) are added here and the sum stored back to x_a.
+            C.add_rmsnorm(b["x_b"] if not first else b["x_a"], None if first else b["d_ws"],
+                          None if first else b["x_a"], lw.ln1, b["xn"], None, a_qkv, uq, 1.0, eps)
+            gemm(lw.w_qkv, b["xn"], b["qkv_ws"], ext_ab=(L["b_qkv"], uq) if a_qkv is not None else None,
+                 swap=True, epilogue="atomic", splits=3)
+            if tp > 1:
+                pass  # column-parallel: no reduction needed for q/k/v
+            C.qk_norm_rope(b["qkv_ws"], lw.q_norm, lw.k_norm, m.inv_freq, st["pos"], b["q"], self.k_pool[li],
+                           self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps)
+            C.paged_decode_attention(b["q"], self.k_pool[li], self.v_pool[li], bt, st["start"], st["kv_len"],
+                                     b["attn"], scale, self._splits, b["attn_scratch"])
+            ext_o = None
+            if "a_o" in L:
+                uo = self._u(b, "u2", rows, L["a_o"].shape[0], b["xn"])
+                C.lora_down(b["attn"], L["a_o"], uo, 1.0)
+                ext_o = (L["b_o"], uo)
+            gemm(lw.w_o, b["attn"], b["o_ws"], ext_ab=ext_o, swap=True, epilogue="atomic", splits=4)
+            if tp > 1:
+                dist.all_reduce(b["o_ws"], group=tp_group)
+            a_gu = L.get("a_gu")
+            ug = self._u(b, "u", rows, a_gu.shape[0], b["xn"]) if a_gu is not None else None
+            C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None, a_gu, ug, 1.0, eps)
+            gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
+                 swap=True, epilogue="swiglu")
+            ext_d = None
+            if "a_down" in L:
+                ud = self._u(b, "u2", rows, L["a_down"].shape[0], b["xn"])
+                C.lora_down(b["act"], L["a_down"], ud, 1.0)
+                ext_d = (L["b_down"], ud)
+            gemm(lw.w_down, b["act"], b["d_ws"], ext_ab=ext_d, swap=True, epilogue="atomic", splits=4)
+            if tp > 1:
+                dist.all_reduce(b["d_ws"], group=tp_group)
+        C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps)
+        logits = self._lm_logits(b["xn"], b["logits"])
+        C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"], st["pos"],
+                        st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)
+
+
+# ======================================================================= eager
+class EagerRolloutEngine:
+    """Plain-PyTorch rollout with a contiguous KV cache (CPU / reference path)."""
+
+    def __init__(self, model: Qwen3Model) -> None:
+        self.m = model
+
+    def _layer(self, lw, x, pos, key_mask, cache, cur, lora):
+        m = self.m
+        cfg = m.cfg
+        ad = m.lora
+        group = m.ps.tp_group
+        B, s_new, _ = x.shape
+        mod = {k: ad.module(lw.index, k) for k in ("q", "k", "v", "o", "gate", "up", "down")}
+        h = copy_to_tp(rmsnorm(x, lw.ln1, cfg.rms_norm_eps), group)
+        q_end, k_end = m.q_local, m.q_local + m.kv_local
+        q = _linear_lora(h, lw.w_qkv[:q_end], mod["q"], lora, ad.scaling, 0.0, False)
+        k = _linear_lora(h, lw.w_qkv[q_end:k_end], mod["k"], lora, ad.scaling, 0.0, False)
+        v = _linear_lora(h, lw.w_qkv[k_end:], mod["v"], lora, ad.scaling, 0.0, False)
+        q = apply_rope(rmsnorm(q.view(B, s_new, m.nq, m.D), lw.q_norm, cfg.rms_norm_eps), pos, m.inv_freq)
+        k = apply_rope(rmsnorm(k.view(B, s_new, m.nkv, m.D), lw.k_norm, cfg.rms_norm_eps), pos, m.inv_freq)
+        kc, vc = cache
+        kc[:, cur : cur + s_new] = k
+        vc[:, cur : cur + s_new] = v.view(B, s_new, m.nkv, m.D)
+        total = cur + s_new
+        keys = kc[:, :total].float().transpose(1, 2).repeat_interleave(m.nq // m.nkv, 1)
+        vals = vc[:, :total].float().transpose(1, 2).repeat_interleave(m.nq // m.nkv, 1)
+        scores = (q.float().transpose(1, 2) @ keys.transpose(-1, -2)) / math.sqrt(m.D)
+        qpos = torch.arange(cur, total, device=x.device)[:, None]
+        kpos = torch.arange(total, device=x.device)[None, :]
+        allowed = (kpos <= qpos)[None, None] & key_mask[:, None, None, :total]
+        scores = scores.masked_fill(~allowed, float("-inf"))
+        probs = torch.nan_to_num(torch.softmax(scores, -1), nan=0.0)
+        attn = (probs @ vals).transpose(1, 2).reshape(B, s_new, -1).to(x.dtype)
+        o = _linear_lora(attn, lw.w_o, mod["o"], lora, ad.scaling, 0.0, False)
+        x = x + reduce_from_tp(o, group)
+        h2 = copy_to_tp(rmsnorm(x, lw.ln2, cfg.rms_norm_eps), group)
+        g = _linear_lora(h2, lw.w_gu[0::2], mod["gate"], lora, ad.scaling, 0.0, False)
+        u = _linear_lora(h2, lw.w_gu[1::2], mod["up"], lora, ad.scaling, 0.0, False)
+        d = _linear_lora(F.silu(g) * u, lw.w_down, mod["down"], lora, ad.scaling, 0.0, False)
+        return x + reduce_from_tp(d, group)
+
+    def _logits(self, h):
+        m = self.m
+        local = F.linear(rmsnorm(h, m.norm, m.cfg.rms_norm_eps).float(), m.lm_head.float())
+        ps = m.ps
+        if ps.tp_size > 1:
+            parts = [torch.empty_like(local) for _ in range(ps.tp_size)]
+            dist.all_gather(parts, local.contiguous(), group=ps.tp_group)
+            local = torch.cat(parts, -1)
+        return local
+
+    @torch.no_grad()
+    def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
+                 ignore_eos=False, seed=0) -> RolloutResult:
+        import time
+
+        m = self.m
+        dev = m.device
+        n, G = len(prompts), int(group_size)
+        rows = n * G
+        lens = [max(1, len(p)) for p in prompts]
+        P = max(lens)
+        ids = torch.full((n, P), pad_id, dtype=torch.long)
+        mask = torch.zeros((n, P), dtype=torch.bool)
+        for i, p in enumerate(prompts):
+            row = list(p) or [pad_id]
+            ids[i, P - len(row):] = torch.tensor(row)
+            mask[i, P - len(row):] = True
+        ids_r = ids.repeat_interleave(G, 0).to(dev)
+        key_mask = torch.zeros(rows, P + max_new_tokens, dtype=torch.bool, device=dev)
+        key_mask[:, :P] = mask.repeat_interleave(G, 0).to(dev)
+        pos = (key_mask[:, :P].long().cumsum(-1) - 1).clamp(min=0)
+        caches = [
+            (torch.zeros(rows, P + max_new_tokens, m.nkv, m.D, dtype=m.dtype, device=dev),
+             torch.zeros(rows, P + max_new_tokens, m.nkv, m.D, dtype=m.dtype, device=dev))
+            for _ in m.layers
+        ]
+        lora = EagerLoRA(m.lora, requires_grad=False)
+        gen = torch.Generator(device="cpu").manual_seed(int(seed))
+        t0 = time.perf_counter()
+        x = F.embedding(ids_r, m.embed)
+        for lw, cache in zip(m.layers, caches, strict=True):
+            x = self._layer(lw, x, pos, key_mask, cache, 0, lora)
+        logits = self._logits(x[:, -1])
+        out = torch.full((rows, max_new_tokens), pad_id, dtype=torch.long)
+        finished = torch.zeros(rows, dtype=torch.bool)
+        next_pos = pos[:, -1] + 1
+        t1 = time.perf_counter()
+        steps = 0
+        for step in range(max_new_tokens):
+            tok = self._sample(logits.cpu(), temperature, top_p, gen)
+            tok = torch.where(finished, torch.full_like(tok, pad_id), tok)
+            if m.ps.tp_size > 1:
+                tok_d = tok.to(dev)
+                dist.broadcast(tok_d, src=m.ps.tp_ranks[0], group=m.ps.tp_group)
+                tok = tok_d.cpu()
+            out[:, step] = tok
+            steps += 1
+            if not ignore_eos:
+                finished |= tok == eos_id
+            if step == max_new_tokens - 1 or (not ignore_eos and bool(finished.all())):
+                break
+            key_mask[:, P + step] = True
+            x = F.embedding(tok.to(dev)[:, None], m.embed)
+            cur = P + step
+            for lw, cache in zip(m.layers, caches, strict=True):
+                x = self._layer(lw, x, next_pos[:, None], key_mask, cache, cur, lora)
+            next_pos = next_pos + 1
+            logits = self._logits(x[:, -1])
+        t2 = time.perf_counter()
+        return RolloutResult(
+            prompt_ids=ids, prompt_lens=lens, tokens=out, gen_lens=_gen_lengths(out, eos_id, ignore_eos),
+            group_size=G, prefill_sec=t1 - t0, decode_sec=t2 - t1, decode_steps=steps,
+        )
+
+    @staticmethod
+    def _sample(logits: torch.Tensor, temperature: float, top_p: float, gen: torch.Generator) -> torch.Tensor:
+        if temperature <= 0:
+            return logits.argmax(-1)
+        scaled = logits.float() / max(temperature, 1e-6)
+        if 0 < top_p < 1:
+            probs = torch.softmax(scaled, -1)
+            sp, si = torch.sort(probs, descending=True, dim=-1)
+            cum = sp.cumsum(-1)
+            drop = cum - sp > top_p
+            sp = sp.masked_fill(drop, 0.0)
+            choice = torch.multinomial(sp / sp.sum(-1, keepdim=True), 1, generator=gen).squeeze(-1)
+            return si.gather(-1, choice[:, None]).squeeze(-1)
+        u = torch.rand(scaled.shape, generator=gen).clamp_(1e-20, 1 - 1e-7)
+        return (scaled - torch.log(-torch.log(u))).argmax(-1)

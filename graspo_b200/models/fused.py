@@ -118,7 +118,8 @@ class FusedQwen3:
         q = torch.empty(T, m.nq, m.D, device=x.device, dtype=x.dtype)
         k = torch.empty(T, m.nkv, m.D, device=x.device, dtype=x.dtype)
         v = torch.empty_like(k)
-        C.qk_norm_rope(qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, q, k, v, None, None, m.nq, m.nkv, 0, self.eps)
+        C.qk_norm_rope(qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, q, k, v, None, None, None, m.nq, m.nkv, 0,
+                       self.eps)
         if kv_sink is not None:
             kv_sink(lw.index, k, v)
         attn, ctx = attn_ops.attention_forward(q, k, v, meta, self.scale, need_ctx=save)

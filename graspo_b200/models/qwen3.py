@@ -343,7 +343,13 @@ def eager_stage_forward(
     lora: EagerLoRA | None = None,
     training: bool = False,
 ) -> torch.Tensor:
-    """Token ids (first stage) or hidden states -> hidden states after local layers."""
+    """Token ids (first stage) or hidden states -> hidden states after local layers.
+
+    The adapter is always applied; pass ``lora`` (with ``requires_grad``) to
+    collect its gradients.
+    """
+    if lora is None:
+        lora = EagerLoRA(model.lora, requires_grad=False)
     if model.include_embed:
         x = F.embedding(inputs, model.embed)
     else:

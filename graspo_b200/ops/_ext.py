@@ -28,6 +28,45 @@ class KernelTimeout(RuntimeError):
     """A kernel's bounded wait expired; the kernel exited without finishing."""
 
 
+class LaunchCounter:
+    """Counts launches of this library's kernels (each entry point launches one).
+
+    Kernels replayed from a CUDA graph are added by the code that replays the
+    graph (``add``), since no Python call happens on replay.
+    """
+
+    def __init__(self) -> None:
+        self.count = 0
+
+    def add(self, n: int) -> None:
+        self.count += int(n)
+
+    def reset(self) -> int:
+        value, self.count = self.count, 0
+        return value
+
+
+launches = LaunchCounter()
+
+
+class _Counting:
+    def __init__(self, module) -> None:
+        self._module = module
+        self._cache: dict[str, object] = {}
+
+    def __getattr__(self, name: str):
+        fn = self._cache.get(name)
+        if fn is None:
+            raw = getattr(self._module, name)
+
+            def fn(*args, _raw=raw, **kwargs):
+                launches.count += 1
+                return _raw(*args, **kwargs)
+
+            self._cache[name] = fn
+        return fn
+
+
 def ext():
     """The loaded extension module; raises if it has not been built."""
     global _C
@@ -39,7 +78,7 @@ def ext():
                 "graspo_b200._C (the sm_100a kernel library) is not built; run "
                 "`python setup.py build_ext --inplace` in the repository root"
             ) from exc
-        _C = module
+        _C = _Counting(module)
     return _C
 
 
@@ -52,6 +91,11 @@ def available() -> bool:
 
 
 def err_word(device: torch.device | int | None = None) -> torch.Tensor:
+    if isinstance(device, torch.device) and device.type == "cpu":
+        word = _ERR.get(-1)
+        if word is None:
+            word = _ERR[-1] = torch.zeros(4, dtype=torch.int32)
+        return word
     if device is None:
         device = torch.cuda.current_device()
     index = device if isinstance(device, int) else (device.index if device.index is not None else torch.cuda.current_device())

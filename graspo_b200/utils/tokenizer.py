@@ -71,19 +71,19 @@ def build_tokenizer(output_dir: str | Path, vocab_size: int = 151936) -> Path:
             continue
         text = "".join(b2u[b] for b in f"<t{i}>".encode())
         vocab[text] = i
+    for text, idx in specials.items():
+        vocab[text] = idx
     model = models.BPE(vocab=vocab, merges=[], fuse_unk=False)
     tok = Tokenizer(model)
-    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=True)
+    # no merges exist, so every byte is its own token and no split pattern is needed
+    tok.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False, use_regex=False)
     tok.decoder = decoders.ByteLevel()
-    from tokenizers import AddedToken
-
-    tok.add_special_tokens([AddedToken(t, special=True, normalized=False) for t in specials])
-    # the added tokens take the next free ids; remap them onto the reserved ones
     data = json.loads(tok.to_str())
-    for entry in data["added_tokens"]:
-        entry["id"] = specials[entry["content"]]
-    for text, idx in specials.items():
-        data["model"]["vocab"][text] = idx
+    data["added_tokens"] = [
+        {"id": idx, "content": text, "single_word": False, "lstrip": False, "rstrip": False,
+         "normalized": False, "special": True}
+        for text, idx in specials.items()
+    ]
     (out / "tokenizer.json").write_text(json.dumps(data, ensure_ascii=False), encoding="utf-8")
     config = {
         "tokenizer_class": "PreTrainedTokenizerFast",

@@ -1,0 +1,117 @@
+"""The fused sm_100a decoder agrees with the eager PyTorch oracle (log-probs,
+LoRA gradients, paged-KV rollout)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(vocab_size=4096, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+             num_attention_heads=4, num_key_value_heads=2, head_dim=128)
+
+
+@pytest.fixture(scope="module")
+def small_model(tmp_path_factory):
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import Qwen3Model
+    from graspo_b200.parallel.state import ParallelState
+    from graspo_b200.utils.synth import write_qwen3_checkpoint
+
+    path = write_qwen3_checkpoint(tmp_path_factory.mktemp("small"), SMALL, seed=3, std=0.05)
+    cfg = load_decoder_config(path)
+    ps = ParallelState(device=torch.device("cuda", 0))
+    targets = {"language.self_attn.q_proj", "language.self_attn.k_proj", "language.self_attn.v_proj",
+               "language.self_attn.o_proj", "language.mlp.gate_proj", "language.mlp.up_proj",
+               "language.mlp.down_proj"}
+    model = Qwen3Model(cfg, SafetensorIndex(path), ps=ps, lora_targets=targets, lora_r=8, lora_alpha=16,
+                       lora_dropout=0.0, dtype=torch.bfloat16, device=ps.device, seed=1)
+    # give the adapters non-zero B so the LoRA path is exercised
+    with torch.no_grad():
+        model.lora.params.copy_(torch.randn_like(model.lora.params) * 0.02)
+    model.ensure_transposed()
+    return model
+
+
+def _batch(B=3, S=96, vocab=4096):
+    g = torch.Generator().manual_seed(0)
+    seq = torch.randint(0, vocab - 8, (B, S), generator=g)
+    mask = torch.ones(B, S, dtype=torch.bool)
+    mask[1, :17] = False  # left padding
+    mask[2, -9:] = False  # right padding
+    return seq.cuda(), mask.cuda()
+
+
+def test_fused_logprobs_match_eager(small_model):
+    from graspo_b200.models.fused import AttnMeta, FusedQwen3
+    from graspo_b200.models.qwen3 import eager_sequence_logprobs
+
+    m = small_model
+    seq, mask = _batch()
+    ref = eager_sequence_logprobs(m, seq, mask)
+    f = FusedQwen3(m)
+    meta = AttnMeta.from_mask(mask)
+    x, _ = f.stage_forward(f.embed(seq), meta)
+    hn, _ = f.final_norm(x)
+    tgt = torch.zeros_like(seq)
+    tgt[:, :-1] = seq[:, 1:]
+    lp, _ = f.token_logprobs(hn, tgt.reshape(-1))
+    lp = lp.view(seq.shape)[:, :-1]
+    valid = mask[:, :-1] & mask[:, 1:]
+    err = (lp - ref).abs()[valid].max().item()
+    assert err < 0.08, f"max |logp diff| {err}"
+
+
+def test_fused_lora_grads_match_eager(small_model):
+    from graspo_b200.models.fused import AttnMeta, FusedQwen3
+    from graspo_b200.models.qwen3 import EagerLoRA, eager_stage_forward, eager_token_logprobs
+
+    m = small_model
+    seq, mask = _batch()
+    B, S = seq.shape
+    w = torch.randn(B, S - 1, device="cuda") * (mask[:, :-1] & mask[:, 1:])
+    # eager
+    m.lora.grads.zero_()
+    lora = EagerLoRA(m.lora, requires_grad=True)
+    hidden = eager_stage_forward(m, seq, mask, lora=lora, training=True)
+    (eager_token_logprobs(m, hidden[:, :-1], seq[:, 1:]) * w).sum().backward()
+    lora.accumulate_grads()
+    ref = m.lora.grads.clone()
+    # fused
+    m.lora.grads.zero_()
+    f = FusedQwen3(m)
+    meta = AttnMeta.from_mask(mask)
+    x, inputs = f.stage_forward(f.embed(seq), meta, train=True, keep_inputs=True)
+    hn, rstd = f.final_norm(x)
+    tgt = torch.zeros_like(seq)
+    tgt[:, :-1] = seq[:, 1:]
+    _, lse = f.token_logprobs(hn, tgt.reshape(-1))
+    g = torch.zeros(B, S, device="cuda")
+    g[:, :-1] = w
+    dhn = f.token_logprobs_backward(hn, tgt.reshape(-1), lse, g.view(-1))
+    dx = torch.empty_like(x)
+    from graspo_b200.ops._ext import ext
+
+    ext().rmsnorm_bwd(dhn, x, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
+    f.stage_backward(inputs, dx, meta, train=True)
+    got = m.lora.grads
+    cos = torch.nn.functional.cosine_similarity(got, ref, dim=0).item()
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert cos > 0.99 and rel < 0.15, f"cos {cos:.4f} rel {rel:.4f}"
+
+
+def test_paged_rollout_matches_eager_greedy(small_model):
+    from graspo_b200.engine.rollout import EagerRolloutEngine, FusedRolloutEngine
+    from graspo_b200.models.fused import FusedQwen3
+
+    m = small_model
+    prompts = [[5, 6, 7, 8, 9, 10, 11], list(range(20, 90)), [300, 301]]
+    kw = dict(group_size=2, max_new_tokens=12, temperature=0.0, top_p=1.0, eos_id=4095, pad_id=4095,
+              ignore_eos=True, seed=0)
+    fused = FusedRolloutEngine(m, FusedQwen3(m), page_size=16).generate(prompts, **kw)
+    eager = EagerRolloutEngine(m).generate(prompts, **kw)
+    agree = (fused.tokens == eager.tokens).float().mean().item()
+    # bf16 kernels vs eager bf16 ops can flip a near-tie argmax; most tokens must agree
+    assert agree > 0.8, f"greedy agreement {agree:.2f}\n{fused.tokens}\n{eager.tokens}"
+    # identical rows within a group under greedy decoding
+    assert torch.equal(fused.tokens[0], fused.tokens[1])

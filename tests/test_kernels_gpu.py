@@ -190,7 +190,7 @@ def test_qk_norm_rope_and_bwd():
     q = torch.empty(T, nq, D, device="cuda", dtype=torch.bfloat16)
     k = torch.empty(T, nkv, D, device="cuda", dtype=torch.bfloat16)
     v = torch.empty_like(k)
-    _ext().qk_norm_rope(qkv, qw, kw, inv_freq, pos, q, k, v, None, None, nq, nkv, 64, 1e-6)
+    _ext().qk_norm_rope(qkv, qw, kw, inv_freq, pos, q, k, v, None, None, None, nq, nkv, 64, 1e-6)
     x = qkv.float().view(T, nq + 2 * nkv, D).requires_grad_(True)
     qr = _rope_ref(_rmsnorm_ref(x[:, :nq], qw, 1e-6), pos, inv_freq)
     kr = _rope_ref(_rmsnorm_ref(x[:, nq:nq + nkv], kw, 1e-6), pos, inv_freq)
@@ -239,7 +239,12 @@ def test_paged_decode_attention():
     q = _rand(rows, nq, D)
     out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
     scale = 1 / math.sqrt(D)
-    _ext().paged_decode_attention(q, kp, vp, perm, starts, lens, out, scale)
+    _ext().paged_decode_attention(q, kp, vp, perm, starts, lens, out, scale, 1, None)
+    scratch = torch.zeros(rows * nq * 3 * (D + 2) + rows * nkv, device="cuda")
+    out3 = torch.empty_like(out)
+    for _ in range(2):  # the split path resets its counters: a second launch must agree
+        _ext().paged_decode_attention(q, kp, vp, perm, starts, lens, out3, scale, 3, scratch)
+        _close(out3, out, 1e-2)
     for r in range(rows):
         L = int(lens[r])
         s0 = int(starts[r])
