@@ -100,18 +100,31 @@ def test_fused_lora_grads_match_eager(small_model):
     assert cos > 0.99 and rel < 0.15, f"cos {cos:.4f} rel {rel:.4f}"
 
 
-def test_paged_rollout_matches_eager_greedy(small_model):
-    from graspo_b200.engine.rollout import EagerRolloutEngine, FusedRolloutEngine
+def test_paged_rollout_greedy_is_argmax_under_eager(small_model):
+    """Every greedy token of the paged-KV engine is (up to bf16 noise) the
+    argmax of the eager model's logits for the same prefix (teacher forcing);
+    exact token equality is not required because bf16 near-ties can flip."""
+    import torch.nn.functional as F
+
+    from graspo_b200.engine.rollout import FusedRolloutEngine
     from graspo_b200.models.fused import FusedQwen3
+    from graspo_b200.models.qwen3 import eager_stage_forward, rmsnorm
 
     m = small_model
     prompts = [[5, 6, 7, 8, 9, 10, 11], list(range(20, 90)), [300, 301]]
-    kw = dict(group_size=2, max_new_tokens=12, temperature=0.0, top_p=1.0, eos_id=4095, pad_id=4095,
-              ignore_eos=True, seed=0)
-    fused = FusedRolloutEngine(m, FusedQwen3(m), page_size=16).generate(prompts, **kw)
-    eager = EagerRolloutEngine(m).generate(prompts, **kw)
-    agree = (fused.tokens == eager.tokens).float().mean().item()
-    # bf16 kernels vs eager bf16 ops can flip a near-tie argmax; most tokens must agree
-    assert agree > 0.8, f"greedy agreement {agree:.2f}\n{fused.tokens}\n{eager.tokens}"
-    # identical rows within a group under greedy decoding
-    assert torch.equal(fused.tokens[0], fused.tokens[1])
+    res = FusedRolloutEngine(m, FusedQwen3(m), page_size=16).generate(
+        prompts, group_size=2, max_new_tokens=12, temperature=0.0, top_p=1.0, eos_id=4095, pad_id=4095,
+        ignore_eos=True, seed=0)
+    G, P = 2, res.prompt_ids.shape[1]
+    seq = torch.cat([res.prompt_ids.repeat_interleave(G, 0), res.tokens], 1).cuda()
+    mask = torch.ones_like(seq, dtype=torch.bool)
+    for i, p in enumerate(prompts):
+        mask[i * G : (i + 1) * G, : P - len(p)] = False
+    hidden = eager_stage_forward(m, seq, mask)
+    logits = F.linear(rmsnorm(hidden, m.norm, m.cfg.rms_norm_eps).float(), m.lm_head.float())
+    steps = logits[:, P - 1 : P - 1 + res.tokens.shape[1]]
+    chosen = steps.gather(-1, res.tokens.cuda()[..., None]).squeeze(-1)
+    gap = (steps.max(-1).values - chosen).max().item()
+    assert gap < 0.25, f"a greedy token is {gap:.3f} logits below the eager argmax"
+    for i in range(0, 6, 2):  # identical rows within a group under greedy decoding
+        assert torch.equal(res.tokens[i], res.tokens[i + 1])
