@@ -26,6 +26,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <mutex>
+
 #include "sm100_common.cuh"
 
 namespace gb {
@@ -288,3 +290,146 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
 }
 
 }  // namespace gb
+
+// ===========================================================================
+// Allocation-free entry point (C ABI).
+//
+// This entry point has no counterpart in the reference implementation.
+//
+// Some callers cannot allocate device memory when they call into this library:
+// a serving process whose whole HBM budget is carved up up front by its own
+// arena allocator (and which forbids any other cudaMalloc), C or C++ hosts that
+// have no PyTorch caching allocator to borrow a scratch tensor from, and code
+// on a latency-critical path where cudaMalloc's implicit device
+// synchronisation is unacceptable.  For them the split decode attention can
+// run with its scratch (per-split partial results plus the per-(row, kv head)
+// arrival counters) taken from a fixed array compiled into this library
+// instead of from a caller-provided buffer.
+//
+// Limits and contract:
+//  * The array holds kNoAllocScratchFloats floats (4 MiB) and
+//    kNoAllocMaxCounters counters (32 KiB); every GPU that loads this library
+//    keeps that memory until the process exits.  A call whose
+//    rows * nq * splits * (128 + 2) floats or rows * nkv counters do not fit is
+//    rejected with GB_NOALLOC_TOO_LARGE before anything is launched.
+//  * The caller passes inputs and outputs as device pointers plus the stream.
+//    Nothing is allocated: no cudaMalloc / cudaFree, no library allocator.
+//  * The first call on a device looks up the array's device address with
+//    cudaGetSymbolAddress (host code cannot use the array's name as a device
+//    address).  Make that first call on each device before any stream capture.
+//  * Every call uses the same array and the array keeps the last call's
+//    contents; the counters are cleared (cudaMemsetAsync on the call's stream)
+//    before each launch.  Calls that can overlap on the GPU (different streams
+//    without ordering) race on the array and must not be issued.
+// ===========================================================================
+
+constexpr long kNoAllocScratchFloats = 1L << 20;
+constexpr int kNoAllocMaxCounters = 8192;
+
+// File-scope scratch for the allocation-free entry point (see above).  In host
+// code these names are host-side stand-ins, not device addresses: the device
+// addresses come from cudaGetSymbolAddress.
+static __device__ __align__(256) float g_decode_attn_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_decode_attn_counters[kNoAllocMaxCounters];
+
+namespace gb {
+namespace noalloc {
+
+struct DeviceSlots {
+  float* scratch = nullptr;
+  int* counters = nullptr;
+  bool ready = false;
+};
+
+static DeviceSlots g_slots[64];
+static std::mutex g_slots_mutex;
+
+// Resolve the device addresses of the two arrays for the current device.
+static int resolve_slots(int device, DeviceSlots** out) {
+  if (device < 0 || device >= 64) return 5;
+  std::lock_guard<std::mutex> lock(g_slots_mutex);
+  DeviceSlots& s = g_slots[device];
+  if (!s.ready) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_attn_scratch) != cudaSuccess || p == nullptr) return 3;
+    s.scratch = static_cast<float*>(p);
+    p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_attn_counters) != cudaSuccess || p == nullptr) return 3;
+    s.counters = static_cast<int*>(p);
+    s.ready = true;
+  }
+  *out = &s;
+  return 0;
+}
+
+}  // namespace noalloc
+}  // namespace gb
+
+enum GbNoAllocStatus : int {
+  GB_NOALLOC_OK = 0,
+  GB_NOALLOC_TOO_LARGE = 1,
+  GB_NOALLOC_BAD_ARGUMENT = 2,
+  GB_NOALLOC_SETUP_FAILED = 3,
+  GB_NOALLOC_LAUNCH_FAILED = 4,
+  GB_NOALLOC_BAD_DEVICE = 5,
+};
+
+// Paged decode attention, split over the key range, scratch from the library's
+// fixed array.  Same layouts and semantics as paged_decode_attention():
+//   q [rows, nq, 128] bf16, k_pool / v_pool [pages, nkv, page_size, 128] bf16,
+//   block_table [rows, max_pages] int32, start / len [rows] int32,
+//   out [rows, nq * 128] bf16.
+// Returns a GbNoAllocStatus; nothing is launched unless it returns GB_NOALLOC_OK.
+extern "C" int graspo_paged_decode_attention_noalloc(const void* q, const void* k_pool, const void* v_pool,
+                                                     const int* block_table, const int* start, const int* len,
+                                                     void* out, int rows, int nq, int nkv, int page_size,
+                                                     int max_pages, int splits, float scale, cudaStream_t stream) {
+  using namespace gb;
+  if (q == nullptr || k_pool == nullptr || v_pool == nullptr || block_table == nullptr || start == nullptr ||
+      len == nullptr || out == nullptr || rows <= 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || page_size <= 0 ||
+      max_pages <= 0 || splits < 2) {
+    return GB_NOALLOC_BAD_ARGUMENT;
+  }
+  const int G = nq / nkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return GB_NOALLOC_BAD_ARGUMENT;
+  const long need_floats = static_cast<long>(rows) * nq * splits * (kD + 2);
+  const long need_counters = static_cast<long>(rows) * nkv;
+  if (need_floats > kNoAllocScratchFloats || need_counters > kNoAllocMaxCounters) {
+    return GB_NOALLOC_TOO_LARGE;
+  }
+  int device = -1;
+  if (cudaGetDevice(&device) != cudaSuccess) return GB_NOALLOC_BAD_DEVICE;
+  noalloc::DeviceSlots* slots = nullptr;
+  const int rc = noalloc::resolve_slots(device, &slots);
+  if (rc != 0) return rc;
+  if (cudaMemsetAsync(slots->counters, 0, need_counters * sizeof(int), stream) != cudaSuccess) {
+    return GB_NOALLOC_LAUNCH_FAILED;
+  }
+  DecodeAttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k_pool = static_cast<const __nv_bfloat16*>(k_pool);
+  a.v_pool = static_cast<const __nv_bfloat16*>(v_pool);
+  a.block_table = block_table;
+  a.start = start;
+  a.len = len;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.part_acc = slots->scratch;
+  a.part_ml = slots->scratch + static_cast<long>(rows) * nq * splits * kD;
+  a.counters = slots->counters;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.splits = splits;
+  const int capacity = max_pages * page_size;
+  a.keys_per_split = ((capacity + splits - 1) / splits + 31) / 32 * 32;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int blocks = rows * nkv * splits;
+  switch (G) {
+    case 1: paged_decode_attn_kernel<1><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    case 2: paged_decode_attn_kernel<2><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    case 4: paged_decode_attn_kernel<4><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+    default: paged_decode_attn_kernel<8><<<blocks, kWarps * 32, 0, stream>>>(a); break;
+  }
+  return cudaGetLastError() == cudaSuccess ? GB_NOALLOC_OK : GB_NOALLOC_LAUNCH_FAILED;
+}
