@@ -119,6 +119,11 @@ class PhaseTimer:
         self.cuda = cuda
         self.device_ms = 0.0
         self.total_ms = 0.0
+        self.phases: dict[str, float] = {}
+
+    def add(self, name: str, ms: float) -> None:
+        self.device_ms += ms
+        self.phases[name] = self.phases.get(name, 0.0) + ms
 
     def event(self):
         if self.cuda:
@@ -145,7 +150,11 @@ def grpo_step(api, samples, reward, *, group: int, max_new: int, prompt_len: int
         temperature=1.0, top_p=1.0, chat_template_kwargs={},
     )
     b = timer.event()
-    timer.device_ms += timer.elapsed(a, b)
+    timer.add("rollout", timer.elapsed(a, b))
+    meta = gens[0].metadata or {}
+    n = len(gens)
+    timer.phases["prefill_s"] = timer.phases.get("prefill_s", 0.0) + float(meta.get("prefill_sec", 0.0)) * n
+    timer.phases["decode_s"] = timer.phases.get("decode_s", 0.0) + float(meta.get("decode_sec", 0.0)) * n
     tokens = 0
     experiences = []
     for sample, gen in zip(samples, gens, strict=True):
@@ -161,7 +170,7 @@ def grpo_step(api, samples, reward, *, group: int, max_new: int, prompt_len: int
         old = api.sequence_log_probs(gen.sequences, gen.attention_mask)
         old = old.detach().float().cpu()
         b = timer.event()
-        timer.device_ms += timer.elapsed(a, b)
+        timer.add("old_logprob", timer.elapsed(a, b))
         counters["h2d"] += seqs.numel() * seqs.element_size() + gen.attention_mask.numel()
         counters["d2h"] += old.numel() * 4
         prompt_len_tok = int(gen.prompt_len)
@@ -177,7 +186,7 @@ def grpo_step(api, samples, reward, *, group: int, max_new: int, prompt_len: int
     metrics = api.train_batch(experiences, policy_ratio_clip_eps=0.2, optimize_iterations_per_step=iters,
                               max_grad_norm=1.0)
     b = timer.event()
-    timer.device_ms += timer.elapsed(a, b)
+    timer.add("train", timer.elapsed(a, b))
     for e in experiences:
         counters["h2d"] += (e.sequences.numel() * 8 + e.old_log_probs.numel() * 4 + e.advantages.numel() * 4
                             + e.attention_mask.numel() + e.action_mask.numel()) * iters
@@ -251,9 +260,11 @@ def run(args) -> dict:
     kw = dict(group=args.group, max_new=args.max_new, prompt_len=args.prompt_len, iters=args.iters,
               reward_cls_adv=adv_fn, experience_cls=Experience)
     for w in range(args.warmup):
-        grpo_step(api, step_samples(w), reward, timer=PhaseTimer(cuda), counters={"h2d": 0, "d2h": 0}, **kw)
+        wt = PhaseTimer(cuda)
+        grpo_step(api, step_samples(w), reward, timer=wt, counters={"h2d": 0, "d2h": 0}, **kw)
         if rank == 0:
-            print(f"[bench] warm-up step {w + 1}/{args.warmup} done", file=sys.stderr, flush=True)
+            phases = {k: round(v / 1e3 if not k.endswith("_s") else v, 2) for k, v in wt.phases.items()}
+            print(f"[bench] warm-up step {w + 1}/{args.warmup}: {phases}", file=sys.stderr, flush=True)
 
     from graspo_b200.bench.clocks import ClockSampler
 
@@ -273,6 +284,9 @@ def run(args) -> dict:
     if dist.is_available() and dist.is_initialized():
         dist.barrier()
     gpu_launches = launches.reset() if launches is not None else 0
+    if rank == 0:
+        phases = {k: round(v / 1e3 if not k.endswith("_s") else v, 2) for k, v in timer.phases.items()}
+        print(f"[bench] timed phases (s): {phases}", file=sys.stderr, flush=True)
     stats = torch.tensor([timer.device_ms, timer.total_ms, float(tokens), float(gpu_launches)],
                          dtype=torch.float64, device="cuda" if cuda else "cpu")
     if dist.is_available() and dist.is_initialized():

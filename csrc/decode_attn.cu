@@ -230,6 +230,277 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Tensor-core variant for page_size % 64 == 0.  Per CTA and 64-key tile:
+// K and V tiles are copied to shared memory with cp.async (double buffered,
+// 16-byte chunks XOR-swizzled by row so ldmatrix reads are conflict-free);
+// each of the 4 warps owns 16 keys of the tile.  S = Q K^T uses
+// mma.sync.m16n8k16 (bf16 in, fp32 out) with the G query heads as the first G
+// of 16 MMA rows; P (the softmax numerators, re-packed to bf16 in registers)
+// multiplies V loaded with ldmatrix.trans.  Per-warp online-softmax states are
+// merged exactly as in the CUDA-core kernel.
+constexpr int kTile = 64;
+constexpr int kRowBytes = kD * 2;                    // 256 B per key row
+constexpr int kTileBytes = kTile * kRowBytes;         // 16 KiB per K or V tile
+constexpr int kTcSmem = 2 * 2 * kTileBytes;           // 2 stages x (K, V)
+
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  // byte offset of 16-byte chunk `chunk` (0..15) of key row `row` in a tile
+  return static_cast<uint32_t>(row * kRowBytes + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(DecodeAttnArgs a) {
+  extern __shared__ __align__(128) uint8_t tc_smem[];
+  __shared__ float m_s[kWarps][16], l_s[kWarps][16];
+  __shared__ float acc_s[kWarps][G][kD];
+  __shared__ int is_last;
+  const int rows_total = gridDim.x / (a.nkv * a.splits);
+  const int row = blockIdx.x % rows_total;
+  const int rest = blockIdx.x / rows_total;
+  const int kvh = rest % a.nkv;
+  const int split = rest / a.nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = (lane & 3) * 2;
+
+  const int s0 = a.start[row], s1 = a.len[row];
+  const int k_begin = max(s0, split * a.keys_per_split);
+  const int k_end = min(s1, (split + 1) * a.keys_per_split);
+  const int t_first = k_begin / kTile, t_last = (k_end - 1) / kTile;
+  const int* bt = a.block_table + static_cast<long>(row) * a.max_pages;
+  const uint32_t sbase = smem_addr(tc_smem);
+
+  // Q fragments (A operand, rows = heads; rows >= G are zero), pre-scaled
+  uint32_t qa[8][4];
+  {
+    const __nv_bfloat16* qr = a.q + (static_cast<long>(row) * a.nq + kvh * G) * kD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      if (g < G) {
+        const int d0 = ks * 16 + c;
+        v[0] = __bfloat162float(qr[g * kD + d0]) * a.scale_log2;
+        v[1] = __bfloat162float(qr[g * kD + d0 + 1]) * a.scale_log2;
+        v[4] = __bfloat162float(qr[g * kD + d0 + 8]) * a.scale_log2;
+        v[5] = __bfloat162float(qr[g * kD + d0 + 9]) * a.scale_log2;
+      }
+      qa[ks][0] = pack_bf16(v[0], v[1]);
+      qa[ks][1] = pack_bf16(v[2], v[3]);  // row g + 8: zero
+      qa[ks][2] = pack_bf16(v[4], v[5]);
+      qa[ks][3] = pack_bf16(v[6], v[7]);  // row g + 8: zero
+    }
+  }
+
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = tile * kTile;
+    const int phys = bt[t0 / a.page_size];
+    const long base = ((static_cast<long>(phys) * a.nkv + kvh) * a.page_size + (t0 % a.page_size)) * kD;
+    const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.k_pool + base);
+    const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.v_pool + base);
+    const uint32_t kdst = sbase + stage * 2 * kTileBytes;
+    const uint32_t vdst = kdst + kTileBytes;
+#pragma unroll
+    for (int i = 0; i < (kTileBytes / 16) / (kWarps * 32); ++i) {
+      const int chunk_id = threadIdx.x + i * kWarps * 32;  // 0..1023
+      const int r = chunk_id >> 4, ch = chunk_id & 15;
+      cp_async16(kdst + swz(r, ch), ksrc + r * kRowBytes + ch * 16);
+      cp_async16(vdst + swz(r, ch), vsrc + r * kRowBytes + ch * 16);
+    }
+    cp_async_commit();
+  };
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // for row g (rows g+8 are padding)
+
+  if (k_end > k_begin) load_tile(t_first, 0);
+  for (int tile = t_first; tile <= t_last && k_end > k_begin; ++tile) {
+    const int stage = (tile - t_first) & 1;
+    if (tile < t_last) {
+      load_tile(tile + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t kt = sbase + stage * 2 * kTileBytes;
+    const uint32_t vt = kt + kTileBytes;
+    const int key0 = warp * 16;  // this warp's 16 keys inside the tile
+    // ---- S = Q K^T for 16 keys (two n-tiles of 8)
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      // matrices: (keys 0-7, dims 0-7), (keys 0-7, dims 8-15), (keys 8-15, dims 0-7), (keys 8-15, dims 8-15)
+      const int mi = lane >> 3, rr = lane & 7;
+      const int key = key0 + rr + ((mi >> 1) << 3);
+      const int chunk = ks * 2 + (mi & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + swz(key, chunk), b0, b1, b2, b3);
+      mma_bf16(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      mma_bf16(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+    }
+    // ---- mask keys outside [k_begin, k_end)
+    const int tbase = tile * kTile + key0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tbase + j * 8 + c + e;
+        if (t < k_begin || t >= k_end) s[j][e] = -INFINITY;
+        s[j][2 + e] = -INFINITY;  // padding rows
+      }
+    }
+    // ---- online softmax for row g over this warp's 16 keys
+    float mx = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    float p[2][2];
+    float corr = 1.f;
+    if (m_new == -INFINITY) {
+      p[0][0] = p[0][1] = p[1][0] = p[1][1] = 0.f;
+    } else {
+      corr = exp2f(m_run - m_new);
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) p[j][e] = exp2f(s[j][e] - m_new);
+    }
+    float ps = p[0][0] + p[0][1] + p[1][0] + p[1][1];
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    l_run = l_run * corr + ps;
+    m_run = m_new;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= corr;
+      o[n][1] *= corr;
+    }
+    // ---- O += P V  (P: 16 rows x 16 keys as the A operand)
+    const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]);
+    const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]);
+    const uint32_t zero = 0u;
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      // matrices: (keys 0-7, dims 16nd..+7), (keys 8-15, dims 16nd..), (keys 0-7, dims 16nd+8..), (keys 8-15, ...)
+      const int mi = lane >> 3, rr = lane & 7;
+      const int key = key0 + rr + ((mi & 1) << 3);
+      const int chunk = nd * 2 + (mi >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vt + swz(key, chunk), b0, b1, b2, b3);
+      mma_bf16(o[2 * nd], pa0, zero, pa2, zero, b0, b1);
+      mma_bf16(o[2 * nd + 1], pa0, zero, pa2, zero, b2, b3);
+    }
+    __syncthreads();  // this stage is overwritten by the load issued next iteration
+  }
+
+  // ---- merge warps (rows g < G hold data)
+  if ((lane & 3) == 0 && g < G) {
+    m_s[warp][g] = m_run;
+    l_s[warp][g] = l_run;
+  }
+  if (g < G) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      acc_s[warp][g][n * 8 + c] = o[n][0];
+      acc_s[warp][g][n * 8 + c + 1] = o[n][1];
+    }
+  }
+  __syncthreads();
+  const long head_base = static_cast<long>(row) * a.nq + kvh * G;
+  for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
+    const int gg = i / kD, d = i - gg * kD;
+    float mxx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mxx = fmaxf(mxx, m_s[w][gg]);
+    float ls = 0.f, ov = 0.f;
+    if (mxx > -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        if (m_s[w][gg] == -INFINITY) continue;
+        const float cf = exp2f(m_s[w][gg] - mxx);
+        ls += l_s[w][gg] * cf;
+        ov += acc_s[w][gg][d] * cf;
+      }
+    }
+    if (a.splits == 1) {
+      a.out[(head_base + gg) * kD + d] = __float2bfloat16(ls > 0.f ? ov / ls : 0.f);
+    } else {
+      const long pidx = (head_base + gg) * a.splits + split;
+      a.part_acc[pidx * kD + d] = ov;
+      if (d == 0) {
+        a.part_ml[pidx * 2] = mxx;
+        a.part_ml[pidx * 2 + 1] = ls;
+      }
+    }
+  }
+  if (a.splits == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* ctr = a.counters + static_cast<long>(row) * a.nkv + kvh;
+    const int prev = atomicAdd(ctr, 1);
+    is_last = (prev == a.splits - 1);
+    if (is_last) *ctr = 0;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
+    const int gg = i / kD, d = i - gg * kD;
+    const long pbase = (head_base + gg) * a.splits;
+    float mxx = -INFINITY;
+    for (int sp = 0; sp < a.splits; ++sp) mxx = fmaxf(mxx, __ldcg(a.part_ml + (pbase + sp) * 2));
+    float ls = 0.f, ov = 0.f;
+    if (mxx > -INFINITY) {
+      for (int sp = 0; sp < a.splits; ++sp) {
+        const float ms = __ldcg(a.part_ml + (pbase + sp) * 2);
+        if (ms == -INFINITY) continue;
+        const float cf = exp2f(ms - mxx);
+        ls += __ldcg(a.part_ml + (pbase + sp) * 2 + 1) * cf;
+        ov += __ldcg(a.part_acc + (pbase + sp) * kD + d) * cf;
+      }
+    }
+    a.out[(head_base + gg) * kD + d] = __float2bfloat16(ls > 0.f ? ov / ls : 0.f);
+  }
+}
+
 }  // namespace
 
 // scratch: optional fp32 buffer of at least rows*nq*splits*(D+2) floats plus
@@ -263,7 +534,9 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
   a.max_pages = max_pages;
   a.splits = static_cast<int>(std::max<int64_t>(1, splits));
   const int capacity = max_pages * page;
-  a.keys_per_split = ((capacity + a.splits - 1) / a.splits + 31) / 32 * 32;
+  const bool use_tc = (page % kTile) == 0 && G <= 8;
+  const int align = use_tc ? kTile : 32;
+  a.keys_per_split = ((capacity + a.splits - 1) / a.splits + align - 1) / align * align;
   a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
   if (a.splits > 1) {
     TORCH_CHECK(scratch.has_value() && scratch->defined() && scratch->scalar_type() == torch::kFloat32,
@@ -279,6 +552,26 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
   const int blocks = rows * nkv * a.splits;
   if (blocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (use_tc) {
+    static bool configured[64][4] = {};
+    const int dev = q.get_device();
+#define GB_TC(GV, IDX)                                                                                       \
+  if (!configured[dev][IDX]) {                                                                               \
+    cudaFuncSetAttribute(paged_decode_attn_tc_kernel<GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem); \
+    configured[dev][IDX] = true;                                                                             \
+  }                                                                                                          \
+  paged_decode_attn_tc_kernel<GV><<<blocks, kWarps * 32, kTcSmem, stream>>>(a)
+    switch (G) {
+      case 1: GB_TC(1, 0); break;
+      case 2: GB_TC(2, 1); break;
+      case 4: GB_TC(4, 2); break;
+      case 8: GB_TC(8, 3); break;
+      default: TORCH_CHECK(false, "unsupported GQA group size ", G);
+    }
+#undef GB_TC
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   switch (G) {
     case 1: paged_decode_attn_kernel<1><<<blocks, kWarps * 32, 0, stream>>>(a); break;
     case 2: paged_decode_attn_kernel<2><<<blocks, kWarps * 32, 0, stream>>>(a); break;

@@ -106,8 +106,11 @@ class FusedRolloutEngine:
             self.k_pool = self.v_pool = None
             if m.device.type == "cuda":
                 torch.cuda.empty_cache()
-            self.k_pool = torch.empty(shape, device=m.device, dtype=m.dtype)
-            self.v_pool = torch.empty(shape, device=m.device, dtype=m.dtype)
+            # zero-filled: slots never written (beyond a row's length) still enter
+            # the tensor-core attention tiles, multiplied by zero probabilities,
+            # so they must hold finite values
+            self.k_pool = torch.zeros(shape, device=m.device, dtype=m.dtype)
+            self.v_pool = torch.zeros(shape, device=m.device, dtype=m.dtype)
             self._pool_shape = shape
 
     def _vocab_gather(self, local: torch.Tensor) -> torch.Tensor:

@@ -228,10 +228,12 @@ def test_swiglu_bwd_lora_down_embedding_transpose():
     assert torch.equal(t, m.T)
 
 
-def test_paged_decode_attention():
-    rows, nq, nkv, D, page = 6, 8, 2, 128, 16
-    lens = torch.tensor([5, 16, 17, 40, 33, 64], device="cuda", dtype=torch.int32)
-    starts = torch.tensor([0, 3, 0, 7, 1, 0], device="cuda", dtype=torch.int32)
+@pytest.mark.parametrize("page,G", [(16, 4), (64, 4), (64, 8), (128, 2)])
+def test_paged_decode_attention(page, G):
+    rows, nkv, D = 6, 2, 128
+    nq = nkv * G
+    lens = torch.tensor([5, 16, 17, 40, 33, 64], device="cuda", dtype=torch.int32) * (page // 16)
+    starts = torch.tensor([0, 3, 0, 7, 1, 0], device="cuda", dtype=torch.int32) * (page // 16)
     max_pages = 4
     num_pages = rows * max_pages
     perm = torch.randperm(num_pages, device="cuda").int().view(rows, max_pages)
