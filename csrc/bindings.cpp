@@ -11,19 +11,25 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
 void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta, c10::optional<torch::Tensor> h_out,
                  torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> lora_a, c10::optional<torch::Tensor> lora_u, double scale,
-                 double eps);
+                 double eps, c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r);
 void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> dres, torch::Tensor dx, double eps);
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
-                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps);
+                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps,
+                  c10::optional<torch::Tensor> lora_b, int64_t lora_r);
 void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
                       torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq, torch::Tensor pos,
                       torch::Tensor dqkv, int64_t nq, int64_t nkv, double eps);
 void swiglu_bwd(torch::Tensor gu, torch::Tensor dh, torch::Tensor dgu);
 void lora_down(torch::Tensor x, torch::Tensor A, torch::Tensor U, double scale);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
+void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                    torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale);
+void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
+                    torch::Tensor end, int64_t B, int64_t S, double scale);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
@@ -48,14 +54,21 @@ void transpose_bf16(torch::Tensor in, torch::Tensor out);
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "graspo_b200 sm_100a kernels";
   m.def("gemm_tc", &gb::gemm_tc, "tcgen05 GEMM with fused epilogues");
-  m.def("add_rmsnorm", &gb::add_rmsnorm);
+  m.def("add_rmsnorm", &gb::add_rmsnorm, py::arg("h"), py::arg("delta"), py::arg("h_out"), py::arg("w"),
+        py::arg("y"), py::arg("rstd"), py::arg("lora_a"), py::arg("lora_u"), py::arg("scale"), py::arg("eps"),
+        py::arg("delta_lora_b") = py::none(), py::arg("delta_lora_r") = 0);
   m.def("rmsnorm_bwd", &gb::rmsnorm_bwd);
-  m.def("qk_norm_rope", &gb::qk_norm_rope);
+  m.def("qk_norm_rope", &gb::qk_norm_rope, py::arg("qkv"), py::arg("q_w"), py::arg("k_w"), py::arg("inv_freq"),
+        py::arg("pos"), py::arg("q_out"), py::arg("k_out"), py::arg("v_out"), py::arg("block_table"),
+        py::arg("row_of_token"), py::arg("slot"), py::arg("nq"), py::arg("nkv"), py::arg("page_size"),
+        py::arg("eps"), py::arg("lora_b") = py::none(), py::arg("lora_r") = 0);
   m.def("qk_norm_rope_bwd", &gb::qk_norm_rope_bwd);
   m.def("swiglu_bwd", &gb::swiglu_bwd);
   m.def("lora_down", &gb::lora_down);
   m.def("embedding", &gb::embedding);
   m.def("paged_decode_attention", &gb::paged_decode_attention);
+  m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
+  m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
   m.def("sample_append", &gb::sample_append);
   m.def("lse_combine", &gb::lse_combine);
   m.def("grpo_loss", &gb::grpo_loss);

@@ -57,12 +57,26 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
                                    __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out,
                                    const __nv_bfloat16* __restrict__ lora_a,
                                    __nv_bfloat16* __restrict__ lora_u, int H, int R, int ldu,
-                                   float scale, float eps) {
+                                   float scale, float eps, long ldd,
+                                   const __nv_bfloat16* __restrict__ dlb, int ldb, int dlr) {
   constexpr int MAXC = 4;  // chunks of 8 per thread: H <= 256*8*4 = 8192
   __shared__ float red[32];
   __shared__ float ured[8][64];
+  __shared__ float dus[64];
   const long row = blockIdx.x;
   const __nv_bfloat16* hr = h + row * H;
+  if constexpr (HAS_DELTA && DELTA_F32) {
+    // U = s * A x of the producing GEMM sits after the H delta columns; take it
+    // and zero it (the workspace is accumulated by atomics on the next step)
+    if (dlb != nullptr) {
+      float* ur = static_cast<float*>(const_cast<void*>(delta)) + row * ldd + H;
+      if (threadIdx.x < dlr) {
+        dus[threadIdx.x] = ur[threadIdx.x];
+        ur[threadIdx.x] = 0.f;
+      }
+      __syncthreads();
+    }
+  }
   float x[MAXC][8];
   float ss = 0.f;
 #pragma unroll
@@ -75,15 +89,29 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
       for (int e = 0; e < 8; ++e) x[c][e] = __bfloat162float(b[e]);
       if constexpr (HAS_DELTA) {
         if constexpr (DELTA_F32) {
-          float* d = static_cast<float*>(const_cast<void*>(delta)) + row * H + col;
+          float* d = static_cast<float*>(const_cast<void*>(delta)) + row * ldd + col;
           float4 d0 = *reinterpret_cast<float4*>(d);
           float4 d1 = *reinterpret_cast<float4*>(d + 4);
           x[c][0] += d0.x; x[c][1] += d0.y; x[c][2] += d0.z; x[c][3] += d0.w;
           x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
+          if (dlb != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const uint4* br = reinterpret_cast<const uint4*>(dlb + static_cast<long>(col + e) * ldb);
+              float acc = 0.f;
+              for (int j8 = 0; j8 < dlr; j8 += 8) {
+                const uint4 raw = __ldg(br + j8 / 8);
+                const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc += __bfloat162float(bb[q]) * dus[j8 + q];
+              }
+              x[c][e] += acc;
+            }
+          }
           *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
           *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
         } else {
-          const __nv_bfloat16* d = static_cast<const __nv_bfloat16*>(delta) + row * H + col;
+          const __nv_bfloat16* d = static_cast<const __nv_bfloat16*>(delta) + row * ldd + col;
           uint4 draw = *reinterpret_cast<const uint4*>(d);
           const __nv_bfloat16* db = reinterpret_cast<const __nv_bfloat16*>(&draw);
 #pragma unroll
@@ -127,21 +155,31 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int j0 = 0; j0 < R; j0 += 64) {
       const int jn = min(64, R - j0);
-      for (int j = 0; j < jn; ++j) {
-        const __nv_bfloat16* arow = lora_a + static_cast<long>(j0 + j) * H;
-        float p = 0.f;
+      for (int j = 0; j < jn; j += 8) {
+        // 8 rank rows per pass: their loads are issued together
+        float p[8];
 #pragma unroll
-        for (int c = 0; c < MAXC; ++c) {
-          const int col = (threadIdx.x + c * kNormThreads) * 8;
-          if (col < H) {
-            uint4 araw = *reinterpret_cast<const uint4*>(arow + col);
-            const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&araw);
+        for (int jj = 0; jj < 8; ++jj) {
+          p[jj] = 0.f;
+          if (j + jj < jn) {
+            const __nv_bfloat16* arow = lora_a + static_cast<long>(j0 + j + jj) * H;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) p += x[c][e] * __bfloat162float(ab[e]);
+            for (int c = 0; c < MAXC; ++c) {
+              const int col = (threadIdx.x + c * kNormThreads) * 8;
+              if (col < H) {
+                uint4 araw = __ldg(reinterpret_cast<const uint4*>(arow + col));
+                const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&araw);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) p[jj] += x[c][e] * __bfloat162float(ab[e]);
+              }
+            }
           }
         }
-        p = warp_sum(p);
-        if (lane == 0) ured[warp][j] = p;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const float v = warp_sum(p[jj]);
+          if (lane == 0 && j + jj < jn) ured[warp][j + jj] = v;
+        }
       }
       __syncthreads();
       if (threadIdx.x < jn) {
@@ -246,16 +284,32 @@ struct RopeArgs {
                                 // from the slot when the row is left-padded
   int T, nq, nkv;
   float eps;
+  // LoRA on q/k/v computed by the projection GEMM itself: the fp32 workspace
+  // row holds, after the (nq + 2 nkv) * D projection columns, U = s * A x in
+  // u_width columns (q, k, v blocks of lora_r each); this kernel adds B U
+  // (B block-diagonal [(nq + 2 nkv) * D, ldb]) and zeroes U for the next step.
+  const __nv_bfloat16* lora_b;
+  int ldb, lora_r, u_width;
 };
 
-__global__ void qk_norm_rope_kernel(RopeArgs a) {
+// One CTA (8 warps) per token; warps loop over the token's heads.
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
   constexpr int D = 128;
-  const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  __shared__ float us[192];
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = a.nq + 2 * a.nkv;
-  if (warp_global >= a.T * heads) return;
-  const int t = warp_global / heads;
-  const int hd = warp_global - t * heads;
+  const bool lora = a.qkv_f32 && a.lora_b != nullptr;
+  if (lora) {
+    float* ur = static_cast<float*>(const_cast<void*>(a.qkv)) + static_cast<long>(t) * a.ld_qkv +
+                static_cast<long>(heads) * D;
+    for (int j = threadIdx.x; j < a.u_width; j += blockDim.x) {
+      if (j < 192) us[j] = ur[j];
+      ur[j] = 0.f;
+    }
+    __syncthreads();
+  }
+  for (int hd = warp; hd < heads; hd += 8) {
   float x[4];
   const long base = static_cast<long>(t) * a.ld_qkv + static_cast<long>(hd) * D + lane * 4;
   if (a.qkv_f32) {
@@ -264,6 +318,23 @@ __global__ void qk_norm_rope_kernel(RopeArgs a) {
     x[0] = f.x; x[1] = f.y; x[2] = f.z; x[3] = f.w;
     *reinterpret_cast<float4*>(src) = make_float4(0.f, 0.f, 0.f, 0.f);
     // round like a bf16 GEMM output would be
+    if (lora) {
+      const int blk = hd < a.nq ? 0 : (hd < a.nq + a.nkv ? 1 : 2);
+      const float* u = us + blk * a.lora_r;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint4* br = reinterpret_cast<const uint4*>(
+            a.lora_b + static_cast<long>(hd * D + lane * 4 + e) * a.ldb + blk * a.lora_r);
+        float acc = 0.f;
+        for (int j8 = 0; j8 < a.lora_r; j8 += 8) {
+          const uint4 raw = __ldg(br + j8 / 8);
+          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc += __bfloat162float(bb[q]) * u[j8 + q];
+        }
+        x[e] += acc;
+      }
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(__float2bfloat16(x[e]));
   } else {
@@ -318,6 +389,7 @@ __global__ void qk_norm_rope_kernel(RopeArgs a) {
 #pragma unroll
   for (int e = 0; e < 4; ++e) ob[e] = __float2bfloat16(x[e]);
   *reinterpret_cast<uint2*>(dst + lane * 4) = out;
+  }
 }
 
 // Backward: inputs dq [T,nq,D], dk/dv [T,nkv,D], the pre-norm qkv [T, ...] (bf16);
@@ -411,34 +483,66 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
 }
 
 // U[row, j] = scale * x[row, :] . A[j, :]  for j < R (zero-padded to ldu).
-// One CTA per row, K <= 256 * 8 * 8.
-__global__ void lora_down_kernel(const __nv_bfloat16* __restrict__ x, long ldx,
-                                 const __nv_bfloat16* __restrict__ A,
-                                 __nv_bfloat16* __restrict__ U, int K, int R, int ldu,
-                                 float scale) {
+// One CTA per row; the first 16384 columns of x are held in registers.
+__global__ void __launch_bounds__(256) lora_down_kernel(const __nv_bfloat16* __restrict__ x, long ldx,
+                                                         const __nv_bfloat16* __restrict__ A,
+                                                         __nv_bfloat16* __restrict__ U, int K, int R, int ldu,
+                                                         float scale) {
+  constexpr int MAXC = 8;  // chunks of 8 per thread: K <= 256 * 8 * 8
   __shared__ float part[8][64];
   const long row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float xv[MAXC][8];
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int col = (threadIdx.x + c * 256) * 8;
+    if (col < K) {
+      uint4 xr = *reinterpret_cast<const uint4*>(x + row * ldx + col);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xr);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xv[c][e] = __bfloat162float(xb[e]);
+    }
+  }
   for (int j0 = 0; j0 < R; j0 += 64) {
     const int jn = min(64, R - j0);
-    for (int j = 0; j < jn; ++j) {
-      const __nv_bfloat16* arow = A + static_cast<long>(j0 + j) * K;
-      float p = 0.f;
-      for (int col = threadIdx.x * 8; col < K; col += blockDim.x * 8) {
-        uint4 xr = *reinterpret_cast<const uint4*>(x + row * ldx + col);
-        uint4 ar = *reinterpret_cast<const uint4*>(arow + col);
-        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xr);
-        const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&ar);
+    for (int j = 0; j < jn; j += 4) {
+      float p[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) p += __bfloat162float(xb[e]) * __bfloat162float(ab[e]);
+      for (int jj = 0; jj < 4; ++jj) {
+        p[jj] = 0.f;
+        if (j + jj < jn) {
+          const __nv_bfloat16* arow = A + static_cast<long>(j0 + j + jj) * K;
+#pragma unroll
+          for (int c = 0; c < MAXC; ++c) {
+            const int col = (threadIdx.x + c * 256) * 8;
+            if (col < K) {
+              uint4 ar = __ldg(reinterpret_cast<const uint4*>(arow + col));
+              const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&ar);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) p[jj] += xv[c][e] * __bfloat162float(ab[e]);
+            }
+          }
+          // columns beyond the register-held prefix (K > 16384)
+          for (int col = (threadIdx.x + MAXC * 256) * 8; col < K; col += 256 * 8) {
+            uint4 xr = *reinterpret_cast<const uint4*>(x + row * ldx + col);
+            uint4 ar = __ldg(reinterpret_cast<const uint4*>(arow + col));
+            const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xr);
+            const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&ar);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p[jj] += __bfloat162float(xb[e]) * __bfloat162float(ab[e]);
+          }
+        }
       }
-      p = warp_sum(p);
-      if (lane == 0) part[warp][j] = p;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const float v = warp_sum(p[jj]);
+        if (lane == 0 && j + jj < jn) part[warp][j + jj] = v;
+      }
     }
     __syncthreads();
     if (threadIdx.x < jn) {
       float s = 0.f;
-      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) s += part[wi][threadIdx.x];
+      for (int wi = 0; wi < 8; ++wi) s += part[wi][threadIdx.x];
       U[row * ldu + j0 + threadIdx.x] = __float2bfloat16(s * scale);
     }
     __syncthreads();
@@ -467,7 +571,8 @@ static void check_bf16(const torch::Tensor& t, const char* n) {
 void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
                  c10::optional<torch::Tensor> h_out, torch::Tensor w, torch::Tensor y,
                  c10::optional<torch::Tensor> rstd, c10::optional<torch::Tensor> lora_a,
-                 c10::optional<torch::Tensor> lora_u, double scale, double eps) {
+                 c10::optional<torch::Tensor> lora_u, double scale, double eps,
+                 c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r) {
   check_bf16(h, "h");
   check_bf16(y, "y");
   const c10::cuda::CUDAGuard guard(h.device());
@@ -491,10 +596,28 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
   auto hp = reinterpret_cast<const __nv_bfloat16*>(h.data_ptr());
   auto wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  long ldd = H;
+  if (has_delta) {
+    TORCH_CHECK(delta->stride(-1) == 1 && delta->numel() / delta->size(-1) == rows && delta->size(-1) >= H,
+                "delta must be row-major [rows, >= H]");
+    ldd = delta->stride(0);
+  }
+  const __nv_bfloat16* dlb = nullptr;
+  int ldb = 0, dlr = 0;
+  if (delta_lora_b.has_value() && delta_lora_b->defined()) {
+    TORCH_CHECK(delta_f32, "the LoRA B.U term needs an fp32 delta workspace");
+    check_bf16(*delta_lora_b, "delta_lora_b");
+    dlb = reinterpret_cast<const __nv_bfloat16*>(delta_lora_b->data_ptr());
+    ldb = static_cast<int>(delta_lora_b->size(1));
+    dlr = static_cast<int>(delta_lora_r);
+    TORCH_CHECK(delta_lora_b->size(0) == H && dlr % 8 == 0 && dlr <= 64 && dlr <= ldb && ldb % 8 == 0 &&
+                    delta->size(-1) >= H + dlr,
+                "delta LoRA: B must be [H, >= r], r a multiple of 8 and <= 64, U after the H delta columns");
+  }
 #define GB_LAUNCH_NORM(DF, HD, LR)                                                              \
   add_rmsnorm_kernel<DF, HD, LR><<<rows, kNormThreads, 0, stream>>>(hp, dptr, hout, wp, yp, rp, ap, \
                                                                     up, H, R, ldu, (float)scale, \
-                                                                    (float)eps)
+                                                                    (float)eps, ldd, dlb, ldb, dlr)
   if (!has_delta) {
     if (lora) GB_LAUNCH_NORM(false, false, true); else GB_LAUNCH_NORM(false, false, false);
   } else if (delta_f32) {
@@ -528,7 +651,8 @@ void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::option
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
-                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps) {
+                  c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps,
+                  c10::optional<torch::Tensor> lora_b, int64_t lora_r) {
   const c10::cuda::CUDAGuard guard(qkv.device());
   TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D row-major");
   RopeArgs a{};
@@ -555,10 +679,18 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
   a.nkv = static_cast<int>(nkv);
   a.eps = static_cast<float>(eps);
   TORCH_CHECK(qkv.size(1) >= (nq + 2 * nkv) * 128, "qkv width / head_dim mismatch (head_dim must be 128)");
-  const long warps = static_cast<long>(a.T) * (nq + 2 * nkv);
-  const int threads = 256;
-  const long blocks = (warps * 32 + threads - 1) / threads;
-  if (blocks > 0) qk_norm_rope_kernel<<<blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  if (lora_b.has_value() && lora_b->defined()) {
+    TORCH_CHECK(a.qkv_f32, "the LoRA B.U term applies to the fp32 split-K workspace");
+    check_bf16(*lora_b, "lora_b");
+    a.lora_b = reinterpret_cast<const __nv_bfloat16*>(lora_b->data_ptr());
+    a.ldb = static_cast<int>(lora_b->size(1));
+    a.lora_r = static_cast<int>(lora_r);
+    a.u_width = static_cast<int>(qkv.size(1) - (nq + 2 * nkv) * 128);
+    TORCH_CHECK(lora_r % 8 == 0 && 3 * lora_r <= a.u_width && 3 * lora_r <= 192 && a.ldb % 8 == 0,
+                "LoRA rank must be a multiple of 8, at most 64, with U columns after the projection");
+    TORCH_CHECK(lora_b->size(0) == (nq + 2 * nkv) * 128, "lora_b rows must match the projection width");
+  }
+  if (a.T > 0) qk_norm_rope_kernel<<<a.T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -5,6 +5,11 @@ Qwen3-8B projection shapes next to ``torch.matmul`` (cuBLAS) on the same
 inputs and prints one JSON line per case with achieved TFLOP/s and the
 fraction of the measured bf16 peak.  ``decode`` times the swap-AB decode GEMMs
 and the paged decode attention as bytes/s against the measured copy bandwidth.
+``step`` runs the rollout engine on a Qwen3-8B-shaped model with fewer layers
+(every layer has the 8B shapes, so per-layer figures carry over) and reports
+the decode-step time per layer with and without the CUDA graph; its eager
+decode steps sit in NVTX ranges named ``decode_step`` so that a profiler can
+select exactly those launches.
 """
 
 from __future__ import annotations
@@ -138,16 +143,59 @@ def bench_decode(args) -> None:
         }), flush=True)
 
 
+def bench_step(args) -> None:
+    from graspo_b200.engine.rollout import FusedRolloutEngine
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.fused import FusedQwen3
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import Qwen3Model
+    from graspo_b200.parallel.state import ParallelState
+    from graspo_b200.utils.synth import QWEN3_8B, write_qwen3_checkpoint
+
+    dims = dict(QWEN3_8B, num_hidden_layers=args.layers)
+    path = write_qwen3_checkpoint(Path(args.ckpt) / f"qwen3-8b-{args.layers}l", dims, seed=7, device="cuda",
+                                  with_tokenizer=False)
+    ps = ParallelState(device=torch.device("cuda", 0))
+    targets = {f"language.{m}" for m in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                                          "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")}
+    model = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=targets, lora_r=16,
+                       lora_alpha=32, lora_dropout=0.0, dtype=torch.bfloat16, device=ps.device, seed=1)
+    model.ensure_transposed()
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, 150000, (args.prompt_len,), generator=g).tolist() for _ in range(args.prompts)]
+    for graph in (True, False):
+        eng = FusedRolloutEngine(model, FusedQwen3(model), page_size=64, use_graph=graph)
+        eng.nvtx = not graph
+        kw = dict(group_size=args.group, max_new_tokens=args.new, temperature=1.0, top_p=1.0, eos_id=0, pad_id=0,
+                  ignore_eos=True, seed=1)
+        eng.generate(prompts, **kw)  # warm-up (pools, kernel attributes)
+        res = eng.generate(prompts, **kw)
+        ms = res.decode_sec * 1e3 / max(1, res.decode_steps - 1)
+        print(json.dumps({
+            "kernel": "decode_step", "graph": graph, "layers": args.layers, "rows": args.prompts * args.group,
+            "prompt_len": args.prompt_len, "new_tokens": args.new, "ms_per_step": round(ms, 3),
+            "ms_per_layer": round(ms / args.layers, 4), "prefill_s": round(res.prefill_sec, 3),
+        }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "step", "all"])
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
+    parser.add_argument("--layers", type=int, default=4)
+    parser.add_argument("--prompts", type=int, default=8)
+    parser.add_argument("--group", type=int, default=8)
+    parser.add_argument("--prompt-len", type=int, default=1024)
+    parser.add_argument("--new", type=int, default=64)
+    parser.add_argument("--ckpt", default="/tmp/graspo_b200_bench")
     args = parser.parse_args()
     if args.what in ("gemm", "all"):
         bench_gemm(args)
     if args.what in ("decode", "all"):
         bench_decode(args)
+    if args.what == "step":
+        bench_step(args)
 
 
 if __name__ == "__main__":

@@ -98,6 +98,7 @@ class FusedRolloutEngine:
         self.graph_chunk = graph_chunk
         self._pool_shape = None
         self.k_pool = self.v_pool = None
+        self.nvtx = False  # wrap eager decode steps in NVTX ranges "decode_step"
 
     def _ensure_pool(self, num_pages: int) -> None:
         m = self.m
@@ -218,7 +219,8 @@ class FusedRolloutEngine:
 
         # ---------------- decode loop
         steps = max_new_tokens - 1
-        bufs = self._decode_buffers(rows)
+        tails = self._refresh_lora_rows()
+        bufs = self._decode_buffers(rows, tails)
         cap = (prompt_pages + gen_pages) * self.page
         self._splits = decode_attention_splits(rows, m.nkv, cap)
         bufs["attn_scratch"] = torch.zeros(rows * m.nq * self._splits * (m.D + 2) + rows * m.nkv,
@@ -256,7 +258,11 @@ class FusedRolloutEngine:
                 del graph
             else:
                 while done < steps:
+                    if self.nvtx:
+                        torch.cuda.nvtx.range_push("decode_step")
                     step()
+                    if self.nvtx:
+                        torch.cuda.nvtx.range_pop()
                     done += 1
                     if not ignore_eos and done % self.graph_chunk == 0 and bool(st["finished"].all()):
                         break
@@ -269,7 +275,30 @@ class FusedRolloutEngine:
             group_size=G, prefill_sec=t1 - t0, decode_sec=t2 - t1, decode_steps=done + 1,
         )
 
-    def _decode_buffers(self, rows: int) -> dict[str, torch.Tensor]:
+    def _lora_tails(self) -> dict[str, int]:
+        """Spare weight rows per projection: the width of its scaled LoRA A layout."""
+        m = self.m
+        if not m.layers:
+            return {}
+        L = m.lora.layer_layouts(m.layers[0].index, m.sizes)
+        return {"w_qkv": L["a_qkv"].shape[0] if "a_qkv" in L else 0,
+                "w_o": L["a_o"].shape[0] if "a_o" in L else 0,
+                "w_down": L["a_down"].shape[0] if "a_down" in L else 0}
+
+    def _refresh_lora_rows(self) -> dict[str, int]:
+        """Write the current (scaled) LoRA A factors into the weights' spare rows."""
+        m = self.m
+        tails = self._lora_tails()
+        m.ensure_tail_rows(tails)
+        for lw in m.layers:
+            L = m.lora.layer_layouts(lw.index, m.sizes)
+            for name, key in (("w_qkv", "a_qkv"), ("w_o", "a_o"), ("w_down", "a_down")):
+                if key in L:
+                    ext = getattr(lw, f"{name}_ext")
+                    ext[getattr(lw, name).shape[0]:].copy_(L[key])
+        return tails
+
+    def _decode_buffers(self, rows: int, tails: dict[str, int]) -> dict[str, torch.Tensor]:
         m = self.m
         dev, dt = m.device, m.dtype
         H = m.cfg.hidden_size
@@ -279,12 +308,13 @@ class FusedRolloutEngine:
             "x_a": torch.empty(rows, H, device=dev, dtype=dt),
             "x_b": torch.empty(rows, H, device=dev, dtype=dt),
             "xn": torch.empty(rows, H, device=dev, dtype=dt),
-            "qkv_ws": torch.zeros(rows, nqkv, device=dev, dtype=f32),
+            # fp32 split-K workspaces: projection columns, then U = s A x
+            "qkv_ws": torch.zeros(rows, nqkv + tails.get("w_qkv", 0), device=dev, dtype=f32),
             "q": torch.empty(rows, m.nq, m.D, device=dev, dtype=dt),
             "attn": torch.empty(rows, m.q_local, device=dev, dtype=dt),
-            "o_ws": torch.zeros(rows, H, device=dev, dtype=f32),
+            "o_ws": torch.zeros(rows, H + tails.get("w_o", 0), device=dev, dtype=f32),
             "act": torch.empty(rows, m.inter_local, device=dev, dtype=dt),
-            "d_ws": torch.zeros(rows, H, device=dev, dtype=f32),
+            "d_ws": torch.zeros(rows, H + tails.get("w_down", 0), device=dev, dtype=f32),
             "logits": torch.empty(rows, m.vocab_local, device=dev, dtype=f32),
         }
 
@@ -298,54 +328,60 @@ class FusedRolloutEngine:
         return buf
 
     def _decode_step(self, st, b, bt, row_ids, P, temperature, top_p, seed, eos_id, pad_id, ignore_eos) -> None:
+        """One token for every row: embedding, the decoder layers, LM head, sampling.
+
+        LoRA: q/k/v, o and down compute U = s A x inside their base GEMM (A sits
+        in spare weight rows, U lands after the projection columns of the fp32
+        workspace) and the consuming kernel adds B U -- qk_norm_rope for q/k/v,
+        the next residual-add + RMSNorm for o and down.  gate/up keep the
+        K-extension (SwiGLU in the epilogue needs the complete sum): its U is
+        computed by the RMSNorm kernel that produces the GEMM input.
+        """
         from graspo_b200.ops.gemm import gemm
 
         m, C = self.m, self.C
         eps = m.cfg.rms_norm_eps
         tp_group = m.ps.tp_group
         tp = m.ps.tp_size
+        r = m.lora.r
         rows = row_ids.shape[0]
         C.embedding(st["next_ids"], m.embed, b["x_a"])
         scale = 1.0 / math.sqrt(m.D)
+        b_down_prev = None
         for li, lw in enumerate(m.layers):
             L = m.lora.layer_layouts(lw.index, m.sizes)
             first = li == 0
-            a_qkv = L.get("a_qkv")
-            uq = self._u(b, "u", rows, a_qkv.shape[0], b["xn"]) if a_qkv is not None else None
             # x_a holds the residual stream; the previous layer's down-projection
-            # partial sums (d_ws) are added here and the sum stored back to x_a.
+            # partial sums (d_ws, with its LoRA U) are added here, the sum stored to x_a
             C.add_rmsnorm(b["x_b"] if not first else b["x_a"], None if first else b["d_ws"],
-                          None if first else b["x_a"], lw.ln1, b["xn"], None, a_qkv, uq, 1.0, eps)
-            gemm(lw.w_qkv, b["xn"], b["qkv_ws"], ext_ab=(L["b_qkv"], uq) if a_qkv is not None else None,
-                 swap=True, epilogue="atomic", splits=3)
-            if tp > 1:
-                pass  # column-parallel: no reduction needed for q/k/v
+                          None if first else b["x_a"], lw.ln1, b["xn"], None, None, None, 1.0, eps,
+                          b_down_prev, r if b_down_prev is not None else 0)
+            has_qkv = "a_qkv" in L
+            gemm(lw.w_qkv_ext if has_qkv else lw.w_qkv, b["xn"], b["qkv_ws"], swap=True, epilogue="atomic",
+                 splits=3)
             C.qk_norm_rope(b["qkv_ws"], lw.q_norm, lw.k_norm, m.inv_freq, st["pos"], b["q"], self.k_pool[li],
-                           self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps)
+                           self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps,
+                           L.get("b_qkv"), r if has_qkv else 0)
             C.paged_decode_attention(b["q"], self.k_pool[li], self.v_pool[li], bt, st["start"], st["kv_len"],
                                      b["attn"], scale, self._splits, b["attn_scratch"])
-            ext_o = None
-            if "a_o" in L:
-                uo = self._u(b, "u2", rows, L["a_o"].shape[0], b["xn"])
-                C.lora_down(b["attn"], L["a_o"], uo, 1.0)
-                ext_o = (L["b_o"], uo)
-            gemm(lw.w_o, b["attn"], b["o_ws"], ext_ab=ext_o, swap=True, epilogue="atomic", splits=4)
+            has_o = "a_o" in L
+            gemm(lw.w_o_ext if has_o else lw.w_o, b["attn"], b["o_ws"], swap=True, epilogue="atomic", splits=4)
             if tp > 1:
                 dist.all_reduce(b["o_ws"], group=tp_group)
             a_gu = L.get("a_gu")
             ug = self._u(b, "u", rows, a_gu.shape[0], b["xn"]) if a_gu is not None else None
-            C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None, a_gu, ug, 1.0, eps)
+            C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None, a_gu, ug, 1.0, eps,
+                          L.get("b_o"), r if has_o else 0)
             gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
                  swap=True, epilogue="swiglu")
-            ext_d = None
-            if "a_down" in L:
-                ud = self._u(b, "u2", rows, L["a_down"].shape[0], b["xn"])
-                C.lora_down(b["act"], L["a_down"], ud, 1.0)
-                ext_d = (L["b_down"], ud)
-            gemm(lw.w_down, b["act"], b["d_ws"], ext_ab=ext_d, swap=True, epilogue="atomic", splits=4)
+            has_d = "a_down" in L
+            gemm(lw.w_down_ext if has_d else lw.w_down, b["act"], b["d_ws"], swap=True, epilogue="atomic",
+                 splits=4)
             if tp > 1:
                 dist.all_reduce(b["d_ws"], group=tp_group)
-        C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps)
+            b_down_prev = L.get("b_down")
+        C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps,
+                      b_down_prev, r if b_down_prev is not None else 0)
         logits = self._lm_logits(b["xn"], b["logits"])
         C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"], st["pos"],
                         st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)

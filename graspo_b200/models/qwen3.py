@@ -73,6 +73,11 @@ class LayerWeights:
     w_o_t: torch.Tensor | None = None
     w_gu_t: torch.Tensor | None = None
     w_down_t: torch.Tensor | None = None
+    # the same weights followed by spare rows holding a LoRA A factor (decode
+    # GEMMs compute W x and s A x in one pass); w_qkv / w_o / w_down are views
+    w_qkv_ext: torch.Tensor | None = None
+    w_o_ext: torch.Tensor | None = None
+    w_down_ext: torch.Tensor | None = None
 
 
 class Qwen3Model:
@@ -218,6 +223,26 @@ class Qwen3Model:
                 lw.w_down_t = lw.w_down.t().contiguous()
         if self.include_head and self.lm_head_t is None:
             self.lm_head_t = self.lm_head.t().contiguous()
+
+    def ensure_tail_rows(self, tails: dict[str, int]) -> None:
+        """Give ``w_qkv`` / ``w_o`` / ``w_down`` ``tails[name]`` spare rows.
+
+        The weight moves into a buffer of ``rows + tail`` rows; the layer keeps
+        a view of the first ``rows`` (so every other user is unaffected) and
+        ``<name>_ext`` names the whole buffer.  The rollout engine writes the
+        scaled LoRA A factor into the spare rows before decoding.
+        """
+        for lw in self.layers:
+            for name, tail in tails.items():
+                ext = getattr(lw, f"{name}_ext")
+                w = getattr(lw, name)
+                if tail <= 0 or (ext is not None and ext.shape[0] == w.shape[0] + tail):
+                    continue
+                buf = torch.zeros(w.shape[0] + tail, w.shape[1], device=w.device, dtype=w.dtype)
+                buf[: w.shape[0]].copy_(w)
+                setattr(lw, name, buf[: w.shape[0]])
+                setattr(lw, f"{name}_ext", buf)
+                del w
 
     def estimate_kv_cache_bytes(self, *, batch_size: int, sequence_len: int) -> int:
         return batch_size * len(self.local_layers) * 2 * self.nkv * self.D * sequence_len * self.dtype.itemsize

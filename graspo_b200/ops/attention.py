@@ -1,59 +1,71 @@
-"""Prefill / training attention over padded batches.
+"""Prefill / training attention over padded batches (sm_100a flash attention).
 
 Layout: q [T, nq, D], k/v [T, nkv, D] with T = B*S tokens; ``meta.key_mask``
-marks valid tokens (left padding before the prompt, right padding after
-EOS).  Each valid query attends causally to valid keys of its own row.  A
-padding query attends only to itself, so every softmax row is non-empty; its
-output is never consumed (loss masks exclude it, and no valid query attends
-to padding keys).
+marks valid tokens.  A row's valid tokens form one contiguous range
+[start, end) -- left padding before the prompt, right padding after EOS --
+and each valid query attends causally to the valid keys of its own row.
+Padding queries produce zero output and receive zero gradient; nothing
+downstream consumes them (loss masks exclude them and no valid query attends
+to a padding key).
 
-This module currently runs the attention through
-``torch.nn.functional.scaled_dot_product_attention`` (a library kernel) while
-the sm_100a flash-attention kernel is developed; the decode-time attention
-over the paged cache is already a hand-written kernel.
+The forward kernel also returns the per-(token, head) log-sum-exp (log2
+domain, fp32), which the backward kernel uses to rebuild the probabilities
+without a second softmax pass (FlashAttention-2, Dao 2023).  GQA is handled
+inside the kernels: a query head reads KV head ``h // (nq // nkv)``, and the
+backward kernel sums the G query heads' contributions to dK/dV in registers.
+Head dim 128 (every Qwen3 size) is the supported kernel shape.
 """
 
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
+
+from graspo_b200.ops._ext import ext
 
 
-def _mask(meta) -> torch.Tensor:
-    cached = getattr(meta, "_sdpa_mask", None)
+def row_ranges(meta) -> tuple[torch.Tensor, torch.Tensor]:
+    """int32 [B] start / end of each row's valid range, computed on device once per meta."""
+    cached = getattr(meta, "_row_ranges", None)
     if cached is not None:
         return cached
-    S = meta.S
-    dev = meta.key_mask.device
-    causal = torch.ones(S, S, dtype=torch.bool, device=dev).tril()
-    allowed = causal[None] & meta.key_mask[:, None, :]
-    allowed |= torch.eye(S, dtype=torch.bool, device=dev)[None]
-    mask = allowed[:, None]
-    object.__setattr__(meta, "_sdpa_mask", mask)
-    return mask
+    m = meta.key_mask.bool()
+    S = m.shape[1]
+    any_ = m.any(-1)
+    first = m.int().argmax(-1)
+    last = S - 1 - m.flip(-1).int().argmax(-1)
+    start = torch.where(any_, first, torch.zeros_like(first)).int().contiguous()
+    end = torch.where(any_, last + 1, torch.zeros_like(last)).int().contiguous()
+    object.__setattr__(meta, "_row_ranges", (start, end))
+    return start, end
 
 
-def _heads(x: torch.Tensor, B: int, S: int) -> torch.Tensor:
-    return x.view(B, S, x.shape[1], x.shape[2]).transpose(1, 2)
+def _check(q: torch.Tensor) -> None:
+    if q.is_cuda and q.shape[-1] != 128:
+        raise NotImplementedError(f"flash attention kernel supports head_dim 128, got {q.shape[-1]}")
 
 
 def attention_forward(q, k, v, meta, scale: float, need_ctx: bool = False):
-    B, S = meta.B, meta.S
-    out = F.scaled_dot_product_attention(
-        _heads(q, B, S), _heads(k, B, S), _heads(v, B, S), attn_mask=_mask(meta), scale=scale,
-        enable_gqa=q.shape[1] != k.shape[1],
-    )
-    return out.transpose(1, 2).reshape(B * S, -1), None
+    """Returns (out [T, nq*D], lse [T, nq] or None)."""
+    _check(q)
+    T, nq, D = q.shape
+    start, end = row_ranges(meta)
+    out = torch.empty(T, nq * D, device=q.device, dtype=q.dtype)
+    lse = torch.empty(T, nq, device=q.device, dtype=torch.float32)
+    ext().flash_attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
+                         meta.B, meta.S, float(scale))
+    return out, (lse if need_ctx else None)
 
 
 def attention_backward(dout, q, k, v, out, ctx, meta, scale: float):
-    B, S = meta.B, meta.S
-    with torch.enable_grad():
-        qh = _heads(q, B, S).detach().requires_grad_(True)
-        kh = _heads(k, B, S).detach().requires_grad_(True)
-        vh = _heads(v, B, S).detach().requires_grad_(True)
-        o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=_mask(meta), scale=scale,
-                                           enable_gqa=q.shape[1] != k.shape[1])
-        dq, dk, dv = torch.autograd.grad(o, (qh, kh, vh), dout.view(B, S, -1, q.shape[2]).transpose(1, 2))
-    return (dq.transpose(1, 2).reshape_as(q).contiguous(), dk.transpose(1, 2).reshape_as(k).contiguous(),
-            dv.transpose(1, 2).reshape_as(v).contiguous())
+    """dout / out [T, nq*D]; ctx is the forward's log-sum-exp.  Returns dq, dk, dv."""
+    _check(q)
+    T, nq, D = q.shape
+    start, end = row_ranges(meta)
+    if ctx is None:
+        _, ctx = attention_forward(q, k, v, meta, scale, need_ctx=True)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    ext().flash_attn_bwd(dout.contiguous().view(T, nq, D), q.contiguous(), k.contiguous(), v.contiguous(),
+                         out.contiguous().view(T, nq, D), ctx, dq, dk, dv, start, end, meta.B, meta.S, float(scale))
+    return dq, dk, dv

@@ -66,10 +66,15 @@ def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epi
         raise ValueError(epilogue)
 
 
-def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps):
+def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps, delta_lora_b=None, delta_lora_r=0):
     x = _f(h)
+    H = h.shape[-1]
     if delta is not None:
-        x = x + _f(delta)
+        d = _f(delta[..., :H])
+        if delta_lora_b is not None:
+            u = _f(delta[..., H : H + delta_lora_r])
+            d = d + u @ _f(delta_lora_b[:, :delta_lora_r]).T
+        x = x + d
         x = x.to(torch.bfloat16).float() if h.dtype == torch.bfloat16 else x
         h_out.copy_(x.to(h_out.dtype))
         if delta.dtype == torch.float32:
@@ -108,10 +113,15 @@ def _head_norm(x, w, eps):
 
 
 def qk_norm_rope(qkv, q_w, k_w, inv_freq, pos, q_out, k_out, v_out, block_table, row_of_token, slot, nq, nkv,
-                 page_size, eps):
+                 page_size, eps, lora_b=None, lora_r=0):
     T = qkv.shape[0]
     D = q_out.shape[-1]
-    x = _f(qkv[:, : (nq + 2 * nkv) * D]).view(T, nq + 2 * nkv, D)
+    W = (nq + 2 * nkv) * D
+    x = _f(qkv[:, :W])
+    if lora_b is not None:
+        u = _f(qkv[:, W : W + 3 * lora_r])
+        x = x + u @ _f(lora_b[:, : 3 * lora_r]).T
+    x = x.view(T, nq + 2 * nkv, D)
     if qkv.dtype == torch.float32:
         x = x.to(torch.bfloat16).float()
         qkv.zero_()
@@ -180,6 +190,58 @@ def paged_decode_attention(q, k_pool, v_pool, block_table, start, length, out, s
 class _Gen:
     def __init__(self, seed):
         self.g = torch.Generator().manual_seed(int(seed) & ((1 << 62) - 1))
+
+
+def _flash_scores(q, k, start, end, B, S, scale):
+    T, nq, D = q.shape
+    G = nq // k.shape[1]
+    qh = _f(q).view(B, S, nq, D).transpose(1, 2)
+    kh = _f(k).view(B, S, -1, D).transpose(1, 2).repeat_interleave(G, 1)
+    idx = torch.arange(S, device=q.device)
+    st, en = start.long()[:, None], end.long()[:, None]
+    valid = (idx[None] >= st) & (idx[None] < en)                      # [B, S]
+    allowed = valid[:, None, :] & (idx[None, :, None] >= idx[None, None, :]) & valid[:, :, None]
+    s = (qh @ kh.transpose(-1, -2)) * scale
+    return s.masked_fill(~allowed[:, None], float("-inf")), valid
+
+
+def flash_attn_fwd(q, k, v, out, lse, start, end, B, S, scale):
+    T, nq, D = q.shape
+    G = nq // k.shape[1]
+    s, valid = _flash_scores(q, k, start, end, B, S, scale)
+    m = s.amax(-1, keepdim=True).clamp_min(-1e30)
+    p = torch.exp(s - m)
+    z = p.sum(-1, keepdim=True)
+    vh = _f(v).view(B, S, -1, D).transpose(1, 2).repeat_interleave(G, 1)
+    o = (p / z.clamp_min(1e-30)) @ vh                                  # [B, nq, S, D]
+    o = o * valid[:, None, :, None]
+    out.copy_(o.transpose(1, 2).reshape(T, nq, D).to(out.dtype))
+    l2 = ((m + torch.log(z.clamp_min(1e-30))) / math.log(2.0)).squeeze(-1)  # log2 domain, [B, nq, S]
+    l2 = torch.where(valid[:, None], l2, torch.zeros_like(l2))
+    lse.copy_(l2.transpose(1, 2).reshape(T, nq))
+
+
+def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, start, end, B, S, scale):
+    T, nq, D = q.shape
+    nkv = k.shape[1]
+    G = nq // nkv
+    s, valid = _flash_scores(q, k, start, end, B, S, scale)
+    l2 = lse.view(B, S, nq).transpose(1, 2)[..., None] * math.log(2.0)
+    p = torch.exp(s - l2).masked_fill(~valid[:, None, :, None], 0.0)
+    doh = _f(dout).view(B, S, nq, D).transpose(1, 2)
+    oh = _f(out).view(B, S, nq, D).transpose(1, 2)
+    vh = _f(v).view(B, S, nkv, D).transpose(1, 2).repeat_interleave(G, 1)
+    qh = _f(q).view(B, S, nq, D).transpose(1, 2)
+    kh = _f(k).view(B, S, nkv, D).transpose(1, 2).repeat_interleave(G, 1)
+    dvh = p.transpose(-1, -2) @ doh
+    dp = doh @ vh.transpose(-1, -2)
+    dd = (doh * oh).sum(-1, keepdim=True)
+    ds = p * (dp - dd) * scale
+    dqh = ds @ kh
+    dkh = ds.transpose(-1, -2) @ qh
+    dq.copy_(dqh.transpose(1, 2).reshape(T, nq, D).to(dq.dtype))
+    dk.copy_(dkh.view(B, nkv, G, S, D).sum(2).transpose(1, 2).reshape(T, nkv, D).to(dk.dtype))
+    dv.copy_(dvh.view(B, nkv, G, S, D).sum(2).transpose(1, 2).reshape(T, nkv, D).to(dv.dtype))
 
 
 def sample_append(logits, temperature, top_p, seed, next_ids, slot, pos, kv_len, finished, out_tokens, prompt_slots,
