@@ -221,7 +221,8 @@ def run(args) -> dict:
         from graspo_b200.ops._ext import launches
 
         cfg_dict = base_config(args, tp, dp, model_path, out_dir, per_replica)
-        cfg_dict["graspoflow"].update({"dp_size": dp, "benchmark_ignore_eos": True, "advantage_eps": 1e-8})
+        cfg_dict["graspoflow"].update({"dp_size": dp, "benchmark_ignore_eos": True, "advantage_eps": 1e-8,
+                                       "pg_timeout_sec": 300.0})
         cfg = GraspoConfig.from_dict(cfg_dict)
         api = GraspoFlowRuntime.from_config(cfg)
         api.setup()
