@@ -2,16 +2,23 @@
 #include <torch/extension.h>
 
 namespace gb {
+bool& pdl_enabled();
 void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              c10::optional<torch::Tensor> B2, torch::Tensor C, c10::optional<torch::Tensor> R,
              c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> targets,
              c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
              c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
-             int64_t splits, torch::Tensor err, int64_t max_ctas);
+             int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
+             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout);
+std::vector<torch::Tensor> symm_alloc(int64_t nbytes, int64_t device);
+int64_t symm_open(torch::Tensor handle, int64_t device);
+void symm_close(int64_t ptr, int64_t device);
 void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta, c10::optional<torch::Tensor> h_out,
                  torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> lora_a, c10::optional<torch::Tensor> lora_u, double scale,
-                 double eps, c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r);
+                 double eps, c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r,
+                 c10::optional<torch::Tensor> peer_src, c10::optional<torch::Tensor> peer_sync,
+                 int64_t peer_expected, c10::optional<torch::Tensor> err);
 void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> dres, torch::Tensor dx, double eps);
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
@@ -33,7 +40,8 @@ void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch:
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
-                            c10::optional<torch::Tensor> scratch);
+                            c10::optional<torch::Tensor> scratch, int64_t prefix_len, int64_t group_rows,
+                            int64_t prefix_splits);
 void sample_append(torch::Tensor logits, double temperature, double top_p, int64_t seed,
                    torch::Tensor next_ids, torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len,
                    torch::Tensor finished, torch::Tensor out_tokens, int64_t prompt_slots,
@@ -53,10 +61,21 @@ void transpose_bf16(torch::Tensor in, torch::Tensor out);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "graspo_b200 sm_100a kernels";
-  m.def("gemm_tc", &gb::gemm_tc, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_tc", &gb::gemm_tc, "tcgen05 GEMM with fused epilogues", py::arg("A"), py::arg("B"), py::arg("A2"),
+        py::arg("B2"), py::arg("C"), py::arg("R"), py::arg("aux"), py::arg("targets"), py::arg("tgt_logit"),
+        py::arg("row_lse"), py::arg("row_scale"), py::arg("epilogue"), py::arg("swap"), py::arg("bn"),
+        py::arg("splits"), py::arg("err"), py::arg("max_ctas"), py::arg("push_dst") = py::none(),
+        py::arg("push_flag") = py::none(), py::arg("tile_ctr") = py::none(), py::arg("layout") = 0);
+  m.def("symm_alloc", &gb::symm_alloc, "zeroed device buffer + its CUDA IPC handle");
+  m.def("symm_open", &gb::symm_open, "map a peer's buffer from its IPC handle; returns the device address");
+  m.def("symm_close", &gb::symm_close);
+  m.def("set_pdl", [](bool on) { gb::pdl_enabled() = on; },
+        "launch the decode-chain kernels with programmatic dependent launch (default on)");
+  m.def("pdl_enabled", []() { return gb::pdl_enabled(); });
   m.def("add_rmsnorm", &gb::add_rmsnorm, py::arg("h"), py::arg("delta"), py::arg("h_out"), py::arg("w"),
         py::arg("y"), py::arg("rstd"), py::arg("lora_a"), py::arg("lora_u"), py::arg("scale"), py::arg("eps"),
-        py::arg("delta_lora_b") = py::none(), py::arg("delta_lora_r") = 0);
+        py::arg("delta_lora_b") = py::none(), py::arg("delta_lora_r") = 0, py::arg("peer_src") = py::none(),
+        py::arg("peer_sync") = py::none(), py::arg("peer_expected") = 0, py::arg("err") = py::none());
   m.def("rmsnorm_bwd", &gb::rmsnorm_bwd);
   m.def("qk_norm_rope", &gb::qk_norm_rope, py::arg("qkv"), py::arg("q_w"), py::arg("k_w"), py::arg("inv_freq"),
         py::arg("pos"), py::arg("q_out"), py::arg("k_out"), py::arg("v_out"), py::arg("block_table"),
@@ -66,7 +85,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &gb::swiglu_bwd);
   m.def("lora_down", &gb::lora_down);
   m.def("embedding", &gb::embedding);
-  m.def("paged_decode_attention", &gb::paged_decode_attention);
+  m.def("paged_decode_attention", &gb::paged_decode_attention, py::arg("q"), py::arg("k_pool"), py::arg("v_pool"),
+        py::arg("block_table"), py::arg("start"), py::arg("len"), py::arg("out"), py::arg("scale"),
+        py::arg("splits"), py::arg("scratch"), py::arg("prefix_len") = 0, py::arg("group_rows") = 1,
+        py::arg("prefix_splits") = 1);
   m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
   m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
   m.def("sample_append", &gb::sample_append);

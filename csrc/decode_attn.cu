@@ -50,6 +50,12 @@ struct DecodeAttnArgs {
   int* counters;                // [rows, nkv]
   int nq, nkv, page_size, max_pages, splits, keys_per_split;
   float scale_log2;
+  // Shared-prefix mode (prefix_len > 0): consecutive groups of group_rows rows
+  // share the pages of key positions [start, prefix_len).  Those keys are
+  // handled by paged_prefix_attn_kernel for all rows of a group at once
+  // (prefix_splits key slices, 4 partial slots each); the split kernels then
+  // cover [prefix_len, len) and merge prefix_slots + splits partials per row.
+  int prefix_len, group_rows, prefix_splits, prefix_kps, prefix_slots;
 };
 
 template <int G>
@@ -280,6 +286,201 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Shared-prefix decode attention.  CTA = (group, kv head, prefix split); its
+// 4 * MT warps take the group's R rows x G query heads (R * G <= 16 * MT) as MT
+// MMA row tiles of 16 -- the prompt K/V tiles are loaded once for the whole
+// group instead of once per row, and the MMA rows are full instead of G of 16.
+// Warp w handles row tile w / 4 and keys [16 (w % 4), +16) of each 64-key
+// tile, and writes its own partial (max, sum, acc) into slot
+// split * 4 + w % 4 of every (row, head) it holds; the split kernel that runs
+// next merges them with the partials of the generated keys.
+template <int G, int MT>
+__global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAttnArgs a) {
+  extern __shared__ __align__(128) uint8_t tc_smem[];
+  constexpr int kThreadsP = MT * 4 * 32;
+  const int groups = gridDim.x / (a.nkv * a.prefix_splits);
+  const int grp = blockIdx.x % groups;
+  const int rest = blockIdx.x / groups;
+  const int kvh = rest % a.nkv;
+  const int split = rest / a.nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = warp >> 2, kw = warp & 3;
+  const int g = lane >> 2, c = (lane & 3) * 2;
+  pdl_trigger();
+  pdl_wait();
+  const int R = a.group_rows;
+  const int row0 = grp * R;
+  const int s0 = a.start[row0];
+  const int k_begin = max(s0, split * a.prefix_kps);
+  const int k_end = min(a.prefix_len, (split + 1) * a.prefix_kps);
+  const int* bt = a.block_table + static_cast<long>(row0) * a.max_pages;
+  const uint32_t sbase = smem_addr(tc_smem);
+  const int total = a.prefix_slots + a.splits;
+
+  // this thread's two MMA rows (g and g + 8 of row tile mt) -> (row, head)
+  const int qr0 = mt * 16 + g, qr1 = qr0 + 8;
+  const bool ok0 = qr0 < R * G, ok1 = qr1 < R * G;
+  uint32_t qa[8][4];
+  {
+    const __nv_bfloat16* q0 = a.q + ((static_cast<long>(row0 + qr0 / G)) * a.nq + kvh * G + qr0 % G) * kD;
+    const __nv_bfloat16* q1 = a.q + ((static_cast<long>(row0 + qr1 / G)) * a.nq + kvh * G + qr1 % G) * kD;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int d0 = ks * 16 + c;
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      if (ok0) {
+        v[0] = __bfloat162float(q0[d0]) * a.scale_log2;
+        v[1] = __bfloat162float(q0[d0 + 1]) * a.scale_log2;
+        v[4] = __bfloat162float(q0[d0 + 8]) * a.scale_log2;
+        v[5] = __bfloat162float(q0[d0 + 9]) * a.scale_log2;
+      }
+      if (ok1) {
+        v[2] = __bfloat162float(q1[d0]) * a.scale_log2;
+        v[3] = __bfloat162float(q1[d0 + 1]) * a.scale_log2;
+        v[6] = __bfloat162float(q1[d0 + 8]) * a.scale_log2;
+        v[7] = __bfloat162float(q1[d0 + 9]) * a.scale_log2;
+      }
+      qa[ks][0] = pack_bf16(v[0], v[1]);
+      qa[ks][1] = pack_bf16(v[2], v[3]);
+      qa[ks][2] = pack_bf16(v[4], v[5]);
+      qa[ks][3] = pack_bf16(v[6], v[7]);
+    }
+  }
+
+  auto load_tile = [&](int tile, int stage) {
+    const int t0 = tile * kTile;
+    const int phys = bt[t0 / a.page_size];
+    const long base = ((static_cast<long>(phys) * a.nkv + kvh) * a.page_size + (t0 % a.page_size)) * kD;
+    const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.k_pool + base);
+    const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.v_pool + base);
+    const uint32_t kdst = sbase + stage * 2 * kTileBytes;
+    const uint32_t vdst = kdst + kTileBytes;
+#pragma unroll
+    for (int i = 0; i < (kTileBytes / 16) / kThreadsP; ++i) {
+      const int chunk_id = threadIdx.x + i * kThreadsP;
+      const int r = chunk_id >> 4, ch = chunk_id & 15;
+      cp_async16(kdst + swz(r, ch), ksrc + r * kRowBytes + ch * 16);
+      cp_async16(vdst + swz(r, ch), vsrc + r * kRowBytes + ch * 16);
+    }
+    cp_async_commit();
+  };
+
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const bool any = k_end > k_begin;
+  const int t_first = any ? k_begin / kTile : 0, t_last = any ? (k_end - 1) / kTile : -1;
+  if (any) load_tile(t_first, 0);
+  for (int tile = t_first; tile <= t_last; ++tile) {
+    const int stage = (tile - t_first) & 1;
+    if (tile < t_last) {
+      load_tile(tile + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t kt = sbase + stage * 2 * kTileBytes;
+    const uint32_t vt = kt + kTileBytes;
+    const int key0 = kw * 16;
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int key = key0 + rr + ((mi >> 1) << 3);
+      const int chunk = ks * 2 + (mi & 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + swz(key, chunk), b0, b1, b2, b3);
+      mma_bf16(s[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      mma_bf16(s[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+    }
+    const int tbase = tile * kTile + key0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = tbase + j * 8 + c + e;
+        if (t < k_begin || t >= k_end) {
+          s[j][e] = -INFINITY;
+          s[j][2 + e] = -INFINITY;
+        }
+      }
+    }
+    // online softmax, rows g (elements 0,1) and g + 8 (elements 2,3)
+    float mx0 = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    float mx1 = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float c0 = n0 == -INFINITY ? 1.f : exp2f(m0 - n0);
+    const float c1 = n1 == -INFINITY ? 1.f : exp2f(m1 - n1);
+    float p[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[j][e] = n0 == -INFINITY ? 0.f : exp2f(s[j][e] - n0);
+        p[j][2 + e] = n1 == -INFINITY ? 0.f : exp2f(s[j][2 + e] - n1);
+      }
+    }
+    float ps0 = p[0][0] + p[0][1] + p[1][0] + p[1][1];
+    float ps1 = p[0][2] + p[0][3] + p[1][2] + p[1][3];
+    ps0 += __shfl_xor_sync(0xffffffffu, ps0, 1);
+    ps0 += __shfl_xor_sync(0xffffffffu, ps0, 2);
+    ps1 += __shfl_xor_sync(0xffffffffu, ps1, 1);
+    ps1 += __shfl_xor_sync(0xffffffffu, ps1, 2);
+    l0 = l0 * c0 + ps0;
+    l1 = l1 * c1 + ps1;
+    m0 = n0;
+    m1 = n1;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= c0;
+      o[n][1] *= c0;
+      o[n][2] *= c1;
+      o[n][3] *= c1;
+    }
+    const uint32_t pa0 = pack_bf16(p[0][0], p[0][1]), pa1 = pack_bf16(p[0][2], p[0][3]);
+    const uint32_t pa2 = pack_bf16(p[1][0], p[1][1]), pa3 = pack_bf16(p[1][2], p[1][3]);
+#pragma unroll
+    for (int nd = 0; nd < 8; ++nd) {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int key = key0 + rr + ((mi & 1) << 3);
+      const int chunk = nd * 2 + (mi >> 1);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vt + swz(key, chunk), b0, b1, b2, b3);
+      mma_bf16(o[2 * nd], pa0, pa1, pa2, pa3, b0, b1);
+      mma_bf16(o[2 * nd + 1], pa0, pa1, pa2, pa3, b2, b3);
+    }
+    __syncthreads();
+  }
+  // partial of this warp for its two rows
+  const int slot = split * 4 + kw;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int qr = h ? qr1 : qr0;
+    if (!(h ? ok1 : ok0)) continue;
+    const long head_idx = static_cast<long>(row0 + qr / G) * a.nq + kvh * G + qr % G;
+    const long pidx = head_idx * total + slot;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      a.part_acc[pidx * kD + n * 8 + c] = o[n][2 * h];
+      a.part_acc[pidx * kD + n * 8 + c + 1] = o[n][2 * h + 1];
+    }
+    if ((lane & 3) == 0) {
+      a.part_ml[pidx * 2] = h ? m1 : m0;
+      a.part_ml[pidx * 2 + 1] = h ? l1 : l0;
+    }
+  }
+}
+
 template <int G>
 __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(DecodeAttnArgs a) {
   extern __shared__ __align__(128) uint8_t tc_smem[];
@@ -293,10 +494,14 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
   const int split = rest / a.nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = (lane & 3) * 2;
+  pdl_trigger();
+  pdl_wait();
 
   const int s0 = a.start[row], s1 = a.len[row];
-  const int k_begin = max(s0, split * a.keys_per_split);
-  const int k_end = min(s1, (split + 1) * a.keys_per_split);
+  const int P = a.prefix_len;  // 0 unless the shared prefix is handled separately
+  const int total = a.prefix_slots + a.splits;
+  const int k_begin = max(max(s0, P), P + split * a.keys_per_split);
+  const int k_end = min(s1, P + (split + 1) * a.keys_per_split);
   const int t_first = k_begin / kTile, t_last = (k_end - 1) / kTile;
   const int* bt = a.block_table + static_cast<long>(row) * a.max_pages;
   const uint32_t sbase = smem_addr(tc_smem);
@@ -459,10 +664,10 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
         ov += acc_s[w][gg][d] * cf;
       }
     }
-    if (a.splits == 1) {
+    if (total == 1) {
       a.out[(head_base + gg) * kD + d] = __float2bfloat16(ls > 0.f ? ov / ls : 0.f);
     } else {
-      const long pidx = (head_base + gg) * a.splits + split;
+      const long pidx = (head_base + gg) * total + a.prefix_slots + split;
       a.part_acc[pidx * kD + d] = ov;
       if (d == 0) {
         a.part_ml[pidx * 2] = mxx;
@@ -470,7 +675,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
       }
     }
   }
-  if (a.splits == 1) return;
+  if (total == 1) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -484,12 +689,12 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
   __threadfence();
   for (int i = threadIdx.x; i < G * kD; i += blockDim.x) {
     const int gg = i / kD, d = i - gg * kD;
-    const long pbase = (head_base + gg) * a.splits;
+    const long pbase = (head_base + gg) * total;
     float mxx = -INFINITY;
-    for (int sp = 0; sp < a.splits; ++sp) mxx = fmaxf(mxx, __ldcg(a.part_ml + (pbase + sp) * 2));
+    for (int sp = 0; sp < total; ++sp) mxx = fmaxf(mxx, __ldcg(a.part_ml + (pbase + sp) * 2));
     float ls = 0.f, ov = 0.f;
     if (mxx > -INFINITY) {
-      for (int sp = 0; sp < a.splits; ++sp) {
+      for (int sp = 0; sp < total; ++sp) {
         const float ms = __ldcg(a.part_ml + (pbase + sp) * 2);
         if (ms == -INFINITY) continue;
         const float cf = exp2f(ms - mxx);
@@ -509,7 +714,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
-                            c10::optional<torch::Tensor> scratch) {
+                            c10::optional<torch::Tensor> scratch, int64_t prefix_len, int64_t group_rows,
+                            int64_t prefix_splits) {
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.is_contiguous(), "q must be contiguous bf16");
   TORCH_CHECK(k_pool.dim() == 4 && k_pool.size(3) == kD, "k_pool must be [pages, nkv, page, 128]");
@@ -536,22 +742,69 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
   const int capacity = max_pages * page;
   const bool use_tc = (page % kTile) == 0 && G <= 8;
   const int align = use_tc ? kTile : 32;
-  a.keys_per_split = ((capacity + a.splits - 1) / a.splits + align - 1) / align * align;
+  const int P = static_cast<int>(prefix_len);
+  int MT = 0;
+  if (P > 0) {
+    const int R = static_cast<int>(group_rows);
+    TORCH_CHECK(use_tc, "shared-prefix decode attention needs pages that are a multiple of 64 keys");
+    TORCH_CHECK(R > 0 && rows % R == 0 && R * G <= 64, "rows must form groups of group_rows with R * G <= 64");
+    TORCH_CHECK(P % kTile == 0 && P <= capacity && prefix_splits > 0, "prefix length must be 64-aligned");
+    MT = (R * G + 15) / 16;
+    MT = MT <= 1 ? 1 : (MT <= 2 ? 2 : 4);
+    a.prefix_len = P;
+    a.group_rows = R;
+    a.prefix_splits = static_cast<int>(prefix_splits);
+    a.prefix_kps = ((P + a.prefix_splits - 1) / a.prefix_splits + kTile - 1) / kTile * kTile;
+    a.prefix_slots = 4 * a.prefix_splits;
+  }
+  a.keys_per_split = ((capacity - P + a.splits - 1) / a.splits + align - 1) / align * align;
   a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
-  if (a.splits > 1) {
+  const int total = a.prefix_slots + a.splits;
+  if (total > 1) {
     TORCH_CHECK(scratch.has_value() && scratch->defined() && scratch->scalar_type() == torch::kFloat32,
                 "split decode attention needs an fp32 scratch buffer");
-    const long need_f = static_cast<long>(rows) * nq * a.splits * (kD + 2);
+    const long need_f = static_cast<long>(rows) * nq * total * (kD + 2);
     const long need = need_f + static_cast<long>(rows) * nkv;
     TORCH_CHECK(scratch->numel() >= need, "decode-attention scratch too small: need ", need, " floats");
     float* base = scratch->data_ptr<float>();
     a.part_acc = base;
-    a.part_ml = base + static_cast<long>(rows) * nq * a.splits * kD;
+    a.part_ml = base + static_cast<long>(rows) * nq * total * kD;
     a.counters = reinterpret_cast<int*>(base + need_f);
   }
   const int blocks = rows * nkv * a.splits;
   if (blocks == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (P > 0) {
+    static bool pconf[64][4][3] = {};
+    const int dev = q.get_device();
+    const int pblocks = (rows / a.group_rows) * nkv * a.prefix_splits;
+    const int gi = G == 1 ? 0 : (G == 2 ? 1 : (G == 4 ? 2 : 3));
+    const int mi = MT == 1 ? 0 : (MT == 2 ? 1 : 2);
+#define GB_PF(GV, MV)                                                                                         \
+  do {                                                                                                        \
+    if (!pconf[dev][gi][mi]) {                                                                                \
+      cudaFuncSetAttribute(paged_prefix_attn_kernel<GV, MV>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                           kTcSmem);                                                                          \
+      pconf[dev][gi][mi] = true;                                                                              \
+    }                                                                                                         \
+    C10_CUDA_CHECK(launch_kernel(paged_prefix_attn_kernel<GV, MV>, dim3(pblocks), dim3(MV * 128), kTcSmem,   \
+                                 stream, a));                                                                 \
+  } while (0)
+#define GB_PF_G(GV)                   \
+  switch (MT) {                       \
+    case 1: GB_PF(GV, 1); break;      \
+    case 2: GB_PF(GV, 2); break;      \
+    default: GB_PF(GV, 4); break;     \
+  }
+    switch (G) {
+      case 1: GB_PF_G(1); break;
+      case 2: GB_PF_G(2); break;
+      case 4: GB_PF_G(4); break;
+      default: GB_PF_G(8); break;
+    }
+#undef GB_PF_G
+#undef GB_PF
+  }
   if (use_tc) {
     static bool configured[64][4] = {};
     const int dev = q.get_device();
@@ -560,7 +813,7 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
     cudaFuncSetAttribute(paged_decode_attn_tc_kernel<GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem); \
     configured[dev][IDX] = true;                                                                             \
   }                                                                                                          \
-  paged_decode_attn_tc_kernel<GV><<<blocks, kWarps * 32, kTcSmem, stream>>>(a)
+  C10_CUDA_CHECK(launch_kernel(paged_decode_attn_tc_kernel<GV>, dim3(blocks), dim3(kWarps * 32), kTcSmem, stream, a))
     switch (G) {
       case 1: GB_TC(1, 0); break;
       case 2: GB_TC(2, 1); break;

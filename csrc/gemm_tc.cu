@@ -11,6 +11,14 @@
 
 namespace gb {
 
+bool& pdl_enabled() {
+  // Off by default: on the decode loop (captured in a CUDA graph) it measured
+  // slower than plain stream order.  GRASPO_PDL=1 turns it on.
+  static bool on = false;
+  return on;
+}
+
+
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -60,17 +68,23 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              c10::optional<torch::Tensor> aux, c10::optional<torch::Tensor> targets,
              c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
              c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
-             int64_t splits, torch::Tensor err, int64_t max_ctas) {
+             int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
+             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout) {
   check_operand(A, "A");
   check_operand(B, "B");
-  TORCH_CHECK(A.size(1) == B.size(1), "A and B must share K");
+  // layout bit 1: A given as [K, M] (MN-major); bit 0: B given as [K, N]
+  const bool a_mn = (layout & 2) != 0, b_mn = (layout & 1) != 0;
+  const int64_t Ka = a_mn ? A.size(0) : A.size(1), Kb = b_mn ? B.size(0) : B.size(1);
+  const int64_t Mdim = a_mn ? A.size(1) : A.size(0), Ndim = b_mn ? B.size(1) : B.size(0);
+  TORCH_CHECK(Ka == Kb, "A and B must share K");
+  TORCH_CHECK(!b_mn || bn % 64 == 0, "MN-major B needs an N tile that is a multiple of 64");
   // K need not be a multiple of 64: TMA zero-fills the tail of the last K-block.
   const c10::cuda::CUDAGuard guard(A.device());
   const int device = A.get_device();
   GemmArgs args{};
-  args.M = static_cast<int>(A.size(0));
-  args.N = static_cast<int>(B.size(0));
-  args.kb_main = static_cast<int>((A.size(1) + BK - 1) / BK);
+  args.M = static_cast<int>(Mdim);
+  args.N = static_cast<int>(Ndim);
+  args.kb_main = static_cast<int>((Ka + BK - 1) / BK);
   args.kb_ext = 0;
   args.splits = static_cast<int>(std::max<int64_t>(splits, 1));
   args.C = C.data_ptr();
@@ -78,18 +92,25 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
   args.err = err.data_ptr<int>();
   const int box_a = BM;
   const int box_b = static_cast<int>(bn);
-  CUtensorMap ta = make_tmap_bf16(A.data_ptr(), A.size(0), A.size(1), A.stride(0), box_a);
-  CUtensorMap tb = make_tmap_bf16(B.data_ptr(), B.size(0), B.size(1), B.stride(0), box_b);
+  // MN-major operands are loaded as [64 K-rows, 64 MN] boxes
+  CUtensorMap ta = a_mn ? make_tmap_bf16(A.data_ptr(), A.size(0), A.size(1), A.stride(0), 64)
+                        : make_tmap_bf16(A.data_ptr(), A.size(0), A.size(1), A.stride(0), box_a);
+  CUtensorMap tb = b_mn ? make_tmap_bf16(B.data_ptr(), B.size(0), B.size(1), B.stride(0), 64)
+                        : make_tmap_bf16(B.data_ptr(), B.size(0), B.size(1), B.stride(0), box_b);
   CUtensorMap ta2 = ta, tb2 = tb;
   if (A2.has_value() && A2->defined()) {
     TORCH_CHECK(B2.has_value() && B2->defined(), "A2 requires B2");
     check_operand(*A2, "A2");
     check_operand(*B2, "B2");
-    TORCH_CHECK(A2->size(1) == B2->size(1), "extension K must match");
-    TORCH_CHECK(A2->size(0) == A.size(0) && B2->size(0) == B.size(0), "extension operands must match M and N");
-    args.kb_ext = static_cast<int>((A2->size(1) + BK - 1) / BK);
-    ta2 = make_tmap_bf16(A2->data_ptr(), A2->size(0), A2->size(1), A2->stride(0), box_a);
-    tb2 = make_tmap_bf16(B2->data_ptr(), B2->size(0), B2->size(1), B2->stride(0), box_b);
+    const int64_t K2a = a_mn ? A2->size(0) : A2->size(1), K2b = b_mn ? B2->size(0) : B2->size(1);
+    const int64_t M2 = a_mn ? A2->size(1) : A2->size(0), N2 = b_mn ? B2->size(1) : B2->size(0);
+    TORCH_CHECK(K2a == K2b, "extension K must match");
+    TORCH_CHECK(M2 == Mdim && N2 == Ndim, "extension operands must match M and N");
+    args.kb_ext = static_cast<int>((K2a + BK - 1) / BK);
+    ta2 = a_mn ? make_tmap_bf16(A2->data_ptr(), A2->size(0), A2->size(1), A2->stride(0), 64)
+               : make_tmap_bf16(A2->data_ptr(), A2->size(0), A2->size(1), A2->stride(0), box_a);
+    tb2 = b_mn ? make_tmap_bf16(B2->data_ptr(), B2->size(0), B2->size(1), B2->stride(0), 64)
+               : make_tmap_bf16(B2->data_ptr(), B2->size(0), B2->size(1), B2->stride(0), box_b);
   }
   if (R.has_value() && R->defined()) {
     args.R = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
@@ -109,11 +130,38 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
   if (epilogue == kLSE) TORCH_CHECK(args.tgt_logit != nullptr && args.aux != nullptr, "LSE epilogue needs aux and tgt_logit");
   if (epilogue == kSoftmaxGrad) TORCH_CHECK(args.row_lse != nullptr && args.row_scale != nullptr, "softmax-grad epilogue needs lse and scale");
   TORCH_CHECK(epilogue == kAtomicF32 || args.splits == 1, "split-K requires the atomic epilogue");
+  if (push_dst.has_value() && push_dst->defined()) {
+    TORCH_CHECK(swap && epilogue == kAtomicF32, "tile push needs the swap atomic epilogue");
+    TORCH_CHECK(push_flag.has_value() && tile_ctr.has_value(), "tile push needs flags and tile counters");
+    TORCH_CHECK(push_dst->device().is_cpu() && push_dst->scalar_type() == torch::kInt64 &&
+                    push_flag->device().is_cpu() && push_flag->scalar_type() == torch::kInt64 &&
+                    push_dst->numel() == push_flag->numel() && push_dst->numel() <= kMaxPeers,
+                "push_dst / push_flag: CPU int64 address tables of equal length <= 8");
+    const int np = static_cast<int>(push_dst->numel());
+    auto pd = push_dst->contiguous();
+    auto pf = push_flag->contiguous();
+    for (int q = 0; q < np; ++q) {
+      args.push_dst[q] = reinterpret_cast<float*>(pd.data_ptr<int64_t>()[q]);
+      args.push_flag[q] = reinterpret_cast<int*>(pf.data_ptr<int64_t>()[q]);
+    }
+    args.npeers = np;
+    const int num_tiles = static_cast<int>(((Mdim + BM - 1) / BM) * ((Ndim + bn - 1) / bn));
+    TORCH_CHECK(tile_ctr->scalar_type() == torch::kInt32 && tile_ctr->is_cuda() && tile_ctr->numel() >= num_tiles,
+                "tile_ctr must be a zeroed int32 CUDA tensor with one entry per output tile");
+    args.tile_ctr = tile_ctr->data_ptr<int>();
+    const int kb_total = args.kb_main + args.kb_ext;
+    const int per = (kb_total + args.splits - 1) / args.splits;
+    args.nonempty_splits = (kb_total + per - 1) / per;
+    TORCH_CHECK(layout == 0 && C.scalar_type() == torch::kFloat32 && C.size(0) == Ndim && C.size(1) == Mdim,
+                "tile push writes C [tokens, features] in full");
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
   const int mc = static_cast<int>(max_ctas);
   TORCH_CHECK(!swap || (epilogue != kLSE && epilogue != kSoftmaxGrad), "log-prob epilogues are not available in swap mode");
   GemmLauncher fn = nullptr;
-  if (swap) {
+  if (layout != 0) {
+    fn = gemm_launcher_mn(static_cast<int>(bn), static_cast<int>(epilogue), swap, static_cast<int>(layout));
+  } else if (swap) {
     fn = gemm_launcher_swap(static_cast<int>(bn), static_cast<int>(epilogue));
   } else if (bn == 256) {
     fn = gemm_launcher_n256(static_cast<int>(epilogue));
@@ -122,7 +170,8 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
   } else if (bn == 64) {
     fn = gemm_launcher_n64(static_cast<int>(epilogue));
   }
-  TORCH_CHECK(fn != nullptr, "no GEMM instantiation for bn=", bn, " swap=", swap, " epilogue=", epilogue);
+  TORCH_CHECK(fn != nullptr, "no GEMM instantiation for bn=", bn, " swap=", swap, " epilogue=", epilogue,
+              " layout=", layout);
   fn(ta, tb, ta2, tb2, args, mc, stream, device);
 }
 

@@ -54,6 +54,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kGroupM = 8;
+constexpr int kMaxPeers = 8;
 
 struct GemmArgs {
   int M, N;
@@ -71,6 +72,16 @@ struct GemmArgs {
   const float* row_lse;    // kSoftmaxGrad
   const float* row_scale;  // kSoftmaxGrad
   int* err;
+  // Tensor-parallel all-reduce inside a swap kAtomicF32 GEMM: when the last
+  // split of an output tile has added its partial sums, the complete fp32 tile
+  // is stored into every peer's receive slot (push_dst[q], same layout as C)
+  // and push_flag[q] (the peer's arrival counter) grows by the tile's element
+  // count.  tile_ctr counts finished splits per tile (zeroed by the last).
+  float* push_dst[kMaxPeers];
+  int* push_flag[kMaxPeers];
+  int npeers;              // ranks in the group (0: no push)
+  int* tile_ctr;
+  int nonempty_splits;     // splits that own at least one K-block
 };
 
 template <int BN_>
@@ -105,11 +116,68 @@ __device__ __forceinline__ Unit decode_unit(int u, int num_m, int num_n, int spl
   return r;
 }
 
-template <int BN, int EPI, bool SWAP>
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Called by the 128 epilogue threads after they issued a unit's atomics
+// (swap layout: thread <-> output feature m, C[n, m] with n = token).
+template <int BN>
+__device__ __forceinline__ void push_tile_impl(const GemmArgs& args, const Unit& w, int num_n, int m, int row_in_tile) {
+  __shared__ int last_split;
+  __threadfence();
+  epi_bar();
+  const int tile = w.m_block * num_n + w.n_block;
+  if (row_in_tile == 0) {
+    const int prev = atomicAdd(args.tile_ctr + tile, 1);
+    const int last = prev == args.nonempty_splits - 1;
+    if (last) args.tile_ctr[tile] = 0;
+    last_split = last;
+  }
+  epi_bar();
+  const bool last = last_split != 0;
+  if (last) {
+    __threadfence();
+    const int n0 = w.n_block * BN;
+    const int nn = min(BN, args.N - n0);
+    if (m < args.M) {
+      // 32 loads in flight per batch, then the stores to every peer
+      const float* __restrict__ src = static_cast<const float*>(args.C);
+      for (int j0 = 0; j0 < nn; j0 += 32) {
+        float v[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+          v[jj] = (j0 + jj < nn) ? __ldcg(src + static_cast<long>(n0 + j0 + jj) * args.ldc + m) : 0.f;
+        for (int q = 0; q < args.npeers; ++q) {
+          float* __restrict__ dst = args.push_dst[q];
+          if (dst == nullptr) continue;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj)
+            if (j0 + jj < nn) __stcg(dst + static_cast<long>(n0 + j0 + jj) * args.ldc + m, v[jj]);
+        }
+      }
+    }
+    __threadfence_system();
+    epi_bar();
+    if (row_in_tile == 0) {
+      const int mm = min(BM, args.M - w.m_block * BM);
+      for (int q = 0; q < args.npeers; ++q)
+        if (args.push_flag[q] != nullptr)
+          asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(args.push_flag[q]), "r"(mm * nn) : "memory");
+    }
+  }
+  epi_bar();  // last_split is rewritten by the next unit
+}
+
+// LAYOUT bit 0: B (and B2) are MN-major -- given as [K, N] row-major; bit 1:
+// A (and A2) are MN-major -- given as [K, M].  MN-major tiles are loaded as
+// 64-wide column blocks of 64 K-rows (one swizzle atom column each).
+constexpr int kMnAtomBytes = 64 * 64 * 2;
+
+template <int BN, int EPI, bool SWAP, int LAYOUT = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB2, GemmArgs args) {
+  static_assert((LAYOUT & 1) == 0 || BN % 64 == 0, "MN-major B needs whole 64-wide atom columns");
   using C_ = Cfg<BN>;
   constexpr int STAGES = C_::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -148,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -158,26 +227,74 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tmA2);
         tma_prefetch_desc(&tmB2);
       }
+      constexpr bool A_MN = (LAYOUT & 2) != 0;
+      constexpr bool B_MN = (LAYOUT & 1) != 0;
+      auto load_a = [&](uint8_t* dst, const CUtensorMap* map, int kc, int m_block, uint64_t* bar) {
+        if constexpr (A_MN) {
+#pragma unroll
+          for (int j = 0; j < BM / 64; ++j) tma_load_2d(dst + j * kMnAtomBytes, map, bar, m_block * BM + j * 64, kc);
+        } else {
+          tma_load_2d(dst, map, bar, kc, m_block * BM);
+        }
+      };
+      auto load_b = [&](uint8_t* dst, const CUtensorMap* map, int kc, int n_block, uint64_t* bar) {
+        if constexpr (B_MN) {
+#pragma unroll
+          for (int j = 0; j < (BN + 63) / 64; ++j)
+            tma_load_2d(dst + j * kMnAtomBytes, map, bar, n_block * BN + j * 64, kc);
+        } else {
+          tma_load_2d(dst, map, bar, kc, n_block * BN);
+        }
+      };
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // Swap (decode) GEMMs: the A operand is a frozen weight that no kernel
+      // writes, so the first ring stages are filled with it before waiting on
+      // the preceding kernel; their B halves follow after the wait.
+      int early = 0;
+      if constexpr (SWAP) {
+        if (blockIdx.x < units) {
+          const Unit w = decode_unit(blockIdx.x, num_m, num_n, args.splits, kb_total);
+          for (int kb = w.kb_begin; kb < w.kb_end && early < STAGES; ++kb, ++early) {
+            mbar_arrive_expect_tx(&full[early], C_::STAGE_BYTES);
+            uint8_t* a_dst = smA + early * C_::A_BYTES;
+            if (kb < args.kb_main) {
+              load_a(a_dst, &tmA, kb * BK, w.m_block, &full[early]);
+            } else {
+              load_a(a_dst, &tmA2, (kb - args.kb_main) * BK, w.m_block, &full[early]);
+            }
+          }
+        }
+      }
+      pdl_wait();
+      int issued = 0;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
-        for (int kb = w.kb_begin; kb < w.kb_end; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrSmemEmptyTimeout)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+        for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++issued) {
           uint8_t* a_dst = smA + stage * C_::A_BYTES;
           uint8_t* b_dst = smB + stage * C_::B_BYTES;
-          if (kb < args.kb_main) {
-            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, w.m_block * BM);
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, w.n_block * BN);
+          if (issued < early) {
+            // A half already in flight on this stage
+            if (kb < args.kb_main) {
+              load_b(b_dst, &tmB, kb * BK, w.n_block, &full[stage]);
+            } else {
+              load_b(b_dst, &tmB2, (kb - args.kb_main) * BK, w.n_block, &full[stage]);
+            }
           } else {
-            const int ke = kb - args.kb_main;
-            tma_load_2d(a_dst, &tmA2, &full[stage], ke * BK, w.m_block * BM);
-            tma_load_2d(b_dst, &tmB2, &full[stage], ke * BK, w.n_block * BN);
+            if (!mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrSmemEmptyTimeout)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+            if (kb < args.kb_main) {
+              load_a(a_dst, &tmA, kb * BK, w.m_block, &full[stage]);
+              load_b(b_dst, &tmB, kb * BK, w.n_block, &full[stage]);
+            } else {
+              const int ke = kb - args.kb_main;
+              load_a(a_dst, &tmA2, ke * BK, w.m_block, &full[stage]);
+              load_b(b_dst, &tmB2, ke * BK, w.n_block, &full[stage]);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -198,7 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+      constexpr bool A_MN = (LAYOUT & 2) != 0;
+      constexpr bool B_MN = (LAYOUT & 1) != 0;
+      constexpr uint32_t idesc = umma_idesc_bf16(BM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc_iter = 0;
@@ -217,12 +336,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t a_desc = umma_desc_k_sw128(smem_addr(smA + stage * C_::A_BYTES));
-          const uint64_t b_desc = umma_desc_k_sw128(smem_addr(smB + stage * C_::B_BYTES));
+          const uint32_t a_addr = smem_addr(smA + stage * C_::A_BYTES);
+          const uint32_t b_addr = smem_addr(smB + stage * C_::B_BYTES);
+          const uint64_t a_desc = A_MN ? umma_desc_mn_sw128(a_addr, kMnAtomBytes, 1024) : umma_desc_k_sw128(a_addr);
+          const uint64_t b_desc = B_MN ? umma_desc_mn_sw128(b_addr, kMnAtomBytes, 1024) : umma_desc_k_sw128(b_addr);
+          // K-step of 16: +32 bytes inside a K-major swizzled row, or two
+          // 8-row atoms (2048 bytes) down an MN-major atom column
+          constexpr uint64_t a_step = A_MN ? (2048 >> 4) : 2;
+          constexpr uint64_t b_step = B_MN ? (2048 >> 4) : 2;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // advance 16 elements (32 bytes) along K inside the swizzled row
-            umma_bf16(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc,
+            umma_bf16(d_tmem, a_desc + a_step * k, b_desc + b_step * k, idesc,
                       (kb > w.kb_begin || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
@@ -239,20 +364,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;          // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
+    pdl_wait();  // outputs (and residual / target inputs) belong to neighbouring kernels
     int acc_iter = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
       if (w.kb_end <= w.kb_begin) continue;
       const int acc = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrTmemFullTimeout)) break;
+      // on a timeout the unit is skipped but the loop goes on, so every
+      // epilogue warp reaches the same named barriers of the tile push
+      const bool have_acc = mbar_wait(&tfull[acc], acc_phase, args.err, kErrTmemFullTimeout);
       tc_fence_after();
       const int m = w.m_block * BM + row_in_tile;
       const int n0 = w.n_block * BN;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       float run_max = -INFINITY, run_sum = 0.f;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < (have_acc ? BN / 32 : 0); ++c) {
         float v[32];
         tmem_ld32(t_row + c * 32, v);
         const int nc = n0 + c * 32;
@@ -436,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if constexpr (EPI == kLSE && !SWAP) {
-        if (m < args.M) {
+        if (m < args.M && have_acc) {
           float2* P = static_cast<float2*>(args.aux) + static_cast<long>(m) * args.ldaux + w.n_block;
           *P = make_float2(run_max, run_sum);
         }
@@ -444,6 +572,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       ++acc_iter;
+      if constexpr (SWAP && EPI == kAtomicF32) {
+        if (args.npeers > 1) push_tile_impl<BN>(args, w, num_n, m, row_in_tile);
+      }
     }
   }
 
@@ -463,14 +594,18 @@ inline int num_sms(int device) {
   return cached[device];
 }
 
-template <int BN, int EPI, bool SWAP>
+template <int BN, int EPI, bool SWAP, int LAYOUT = 0>
 void launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2,
                         const CUtensorMap& b2, const GemmArgs& args, int max_ctas,
                         cudaStream_t stream, int device) {
-  auto kern = gemm_tc_kernel<BN, EPI, SWAP>;
+  auto kern = gemm_tc_kernel<BN, EPI, SWAP, LAYOUT>;
+  // MN-major instantiations get 16 KiB of unused tail so that every address a
+  // stage descriptor can reach stays inside the allocation
+  constexpr int smem = Cfg<BN>::SMEM_BYTES + (LAYOUT != 0 ? 16384 : 0);
+  static_assert(smem <= 227 * 1024, "shared memory budget");
   static bool configured[64] = {false};
   if (!configured[device]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured[device] = true;
   }
   const int num_m = (args.M + BM - 1) / BM;
@@ -479,8 +614,7 @@ void launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& 
   int grid = std::min(units, num_sms(device));
   if (max_ctas > 0) grid = std::min(grid, max_ctas);
   grid = std::max(grid, 1);
-  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, stream>>>(a, b, a2, b2, args);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  C10_CUDA_CHECK(launch_kernel(kern, dim3(grid), dim3(kThreads), smem, stream, a, b, a2, b2, args));
 }
 
 
@@ -492,5 +626,6 @@ GemmLauncher gemm_launcher_n256(int epi);
 GemmLauncher gemm_launcher_n128(int epi);
 GemmLauncher gemm_launcher_n64(int epi);
 GemmLauncher gemm_launcher_swap(int bn, int epi);
+GemmLauncher gemm_launcher_mn(int bn, int epi, bool swap, int layout);
 
 }  // namespace gb

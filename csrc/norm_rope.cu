@@ -50,6 +50,64 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // One CTA per row; H <= 8 * 256 * 8 (each thread holds up to 8 chunks of 8).
+// Tensor-parallel sum of an fp32 delta whose peer partials were pushed into
+// this rank's receive slots by the producing GEMM (see GemmArgs::push_dst).
+struct PeerSum {
+  const float* src[8];  // per rank: receive slot, or nullptr for this rank (the local delta)
+  int n;                // ranks (<= 1: the local delta alone)
+  int* arrivals;        // grows by the pushed element count; this kernel takes `expected` back off
+  int* done;            // CTAs finished (the last resets it)
+  int expected;
+  int* err;
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait (about 10 s) for the peers' pushes of this step.
+__device__ __forceinline__ void peer_wait(const PeerSum& ps) {
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    while (ld_acquire_sys(ps.arrivals) < ps.expected) {
+      if (clock64() - t0 > 10 * kSpinLimitCycles) {
+        record_error(ps.err, kErrPeerTimeout);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void peer_release(const PeerSum& ps) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(ps.done, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      *ps.done = 0;
+      atomicSub_system(ps.arrivals, ps.expected);
+    }
+  }
+}
+
+// Row `row` of the tensor-parallel sum at columns [col, col + 8): partials
+// added in rank order, so every rank gets the same bits.
+__device__ __forceinline__ void peer_sum8(const PeerSum& ps, const float* local, long off, float (&d)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) d[e] = 0.f;
+  for (int q = 0; q < ps.n; ++q) {
+    const float* src = ps.src[q] != nullptr ? ps.src[q] + off : local + off;
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
+    d[0] += a.x; d[1] += a.y; d[2] += a.z; d[3] += a.w;
+    d[4] += b.x; d[5] += b.y; d[6] += b.z; d[7] += b.w;
+  }
+}
+
 template <bool DELTA_F32, bool HAS_DELTA, bool LORA>
 __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const void* delta,
                                    __nv_bfloat16* __restrict__ h_out,
@@ -58,23 +116,35 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
                                    const __nv_bfloat16* __restrict__ lora_a,
                                    __nv_bfloat16* __restrict__ lora_u, int H, int R, int ldu,
                                    float scale, float eps, long ldd,
-                                   const __nv_bfloat16* __restrict__ dlb, int ldb, int dlr) {
+                                   const __nv_bfloat16* __restrict__ dlb, int ldb, int dlr, PeerSum ps) {
   constexpr int MAXC = 4;  // chunks of 8 per thread: H <= 256*8*4 = 8192
   __shared__ float red[32];
   __shared__ float ured[8][64];
   __shared__ float dus[64];
   const long row = blockIdx.x;
   const __nv_bfloat16* hr = h + row * H;
+  pdl_trigger();
+  pdl_wait();
+  const bool peers = HAS_DELTA && DELTA_F32 && ps.n > 1;
+  if (peers) peer_wait(ps);
   if constexpr (HAS_DELTA && DELTA_F32) {
     // U = s * A x of the producing GEMM sits after the H delta columns; take it
     // and zero it (the workspace is accumulated by atomics on the next step)
     if (dlb != nullptr) {
       float* ur = static_cast<float*>(const_cast<void*>(delta)) + row * ldd + H;
       if (threadIdx.x < dlr) {
-        dus[threadIdx.x] = ur[threadIdx.x];
-        ur[threadIdx.x] = 0.f;
+        float u = 0.f;
+        if (peers) {
+          for (int q = 0; q < ps.n; ++q)
+            u += __ldcg((ps.src[q] != nullptr ? ps.src[q] + row * ldd + H : ur) + threadIdx.x);
+        } else {
+          u = ur[threadIdx.x];
+        }
+        dus[threadIdx.x] = u;
       }
       __syncthreads();
+      // the whole U region (padding columns included) starts the next step at zero
+      for (long j = threadIdx.x; j < ldd - H; j += blockDim.x) ur[j] = 0.f;
     }
   }
   float x[MAXC][8];
@@ -90,10 +160,17 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
       if constexpr (HAS_DELTA) {
         if constexpr (DELTA_F32) {
           float* d = static_cast<float*>(const_cast<void*>(delta)) + row * ldd + col;
-          float4 d0 = *reinterpret_cast<float4*>(d);
-          float4 d1 = *reinterpret_cast<float4*>(d + 4);
-          x[c][0] += d0.x; x[c][1] += d0.y; x[c][2] += d0.z; x[c][3] += d0.w;
-          x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
+          if (peers) {
+            float ds[8];
+            peer_sum8(ps, static_cast<const float*>(delta), row * ldd + col, ds);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[c][e] += ds[e];
+          } else {
+            float4 d0 = *reinterpret_cast<float4*>(d);
+            float4 d1 = *reinterpret_cast<float4*>(d + 4);
+            x[c][0] += d0.x; x[c][1] += d0.y; x[c][2] += d0.z; x[c][3] += d0.w;
+            x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
+          }
           if (dlb != nullptr) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -191,6 +268,7 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
     }
     for (int j = R + threadIdx.x; j < ldu; j += blockDim.x) lora_u[row * ldu + j] = __float2bfloat16(0.f);
   }
+  if (peers) peer_release(ps);
 }
 
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
@@ -300,6 +378,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = a.nq + 2 * a.nkv;
   const bool lora = a.qkv_f32 && a.lora_b != nullptr;
+  pdl_trigger();
+  pdl_wait();
   if (lora) {
     float* ur = static_cast<float*>(const_cast<void*>(a.qkv)) + static_cast<long>(t) * a.ld_qkv +
                 static_cast<long>(heads) * D;
@@ -553,6 +633,8 @@ __global__ void __launch_bounds__(256) lora_down_kernel(const __nv_bfloat16* __r
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                                  __nv_bfloat16* __restrict__ out, int H, long vocab) {
   const long row = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   long id = ids[row];
   if (id < 0 || id >= vocab) id = 0;
   const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
@@ -572,7 +654,9 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
                  c10::optional<torch::Tensor> h_out, torch::Tensor w, torch::Tensor y,
                  c10::optional<torch::Tensor> rstd, c10::optional<torch::Tensor> lora_a,
                  c10::optional<torch::Tensor> lora_u, double scale, double eps,
-                 c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r) {
+                 c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r,
+                 c10::optional<torch::Tensor> peer_src, c10::optional<torch::Tensor> peer_sync,
+                 int64_t peer_expected, c10::optional<torch::Tensor> err) {
   check_bf16(h, "h");
   check_bf16(y, "y");
   const c10::cuda::CUDAGuard guard(h.device());
@@ -614,10 +698,27 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
                     delta->size(-1) >= H + dlr,
                 "delta LoRA: B must be [H, >= r], r a multiple of 8 and <= 64, U after the H delta columns");
   }
-#define GB_LAUNCH_NORM(DF, HD, LR)                                                              \
-  add_rmsnorm_kernel<DF, HD, LR><<<rows, kNormThreads, 0, stream>>>(hp, dptr, hout, wp, yp, rp, ap, \
-                                                                    up, H, R, ldu, (float)scale, \
-                                                                    (float)eps, ldd, dlb, ldb, dlr)
+  PeerSum ps{};
+  if (peer_src.has_value() && peer_src->defined()) {
+    TORCH_CHECK(delta_f32, "the tensor-parallel sum needs an fp32 delta workspace");
+    TORCH_CHECK(peer_src->device().is_cpu() && peer_src->scalar_type() == torch::kInt64 && peer_src->numel() <= 8,
+                "peer_src must be a CPU int64 address table (<= 8 ranks)");
+    TORCH_CHECK(peer_sync.has_value() && peer_sync->device().is_cpu() && peer_sync->numel() == 2,
+                "peer_sync must hold the arrival and done counter addresses");
+    auto src = peer_src->contiguous();
+    auto sy = peer_sync->contiguous();
+    ps.n = static_cast<int>(src.numel());
+    for (int q = 0; q < ps.n; ++q) ps.src[q] = reinterpret_cast<const float*>(src.data_ptr<int64_t>()[q]);
+    ps.arrivals = reinterpret_cast<int*>(sy.data_ptr<int64_t>()[0]);
+    ps.done = reinterpret_cast<int*>(sy.data_ptr<int64_t>()[1]);
+    ps.expected = static_cast<int>(peer_expected);
+    ps.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
+    TORCH_CHECK(ldd % 4 == 0, "peer sum needs 16-byte aligned rows");
+  }
+#define GB_LAUNCH_NORM(DF, HD, LR)                                                                       \
+  C10_CUDA_CHECK(launch_kernel(add_rmsnorm_kernel<DF, HD, LR>, dim3(rows), dim3(kNormThreads), 0, stream, hp, \
+                               dptr, hout, wp, yp, rp, ap, up, H, R, ldu, (float)scale, (float)eps, ldd, dlb, \
+                               ldb, dlr, ps))
   if (!has_delta) {
     if (lora) GB_LAUNCH_NORM(false, false, true); else GB_LAUNCH_NORM(false, false, false);
   } else if (delta_f32) {
@@ -690,7 +791,8 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
                 "LoRA rank must be a multiple of 8, at most 64, with U columns after the projection");
     TORCH_CHECK(lora_b->size(0) == (nq + 2 * nkv) * 128, "lora_b rows must match the projection width");
   }
-  if (a.T > 0) qk_norm_rope_kernel<<<a.T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  if (a.T > 0)
+    C10_CUDA_CHECK(launch_kernel(qk_norm_rope_kernel, dim3(a.T), dim3(256), 0, at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -754,10 +856,11 @@ void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
   const int H = static_cast<int>(table.size(1));
   TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
   if (rows == 0) return;
-  embedding_kernel<<<rows, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(launch_kernel(embedding_kernel, dim3(rows), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, table.size(0));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H, table.size(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
 
 }  // namespace gb

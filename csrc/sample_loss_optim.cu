@@ -151,6 +151,8 @@ struct SampleArgs {
 
 __global__ void sample_append_kernel(SampleArgs a) {
   const int row = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
   const float* lg = a.logits + static_cast<long>(row) * a.ld;
   const int64_t slot = a.slot[row];
   float thresh = -INFINITY;  // in units of logit/T
@@ -379,7 +381,7 @@ void sample_append(torch::Tensor logits, double temperature, double top_p, int64
   a.active = (active.has_value() && active->defined()) ? active->data_ptr<uint8_t>() : nullptr;
   const int rows = static_cast<int>(logits.size(0));
   if (rows == 0) return;
-  sample_append_kernel<<<rows, 1024, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_CHECK(launch_kernel(sample_append_kernel, dim3(rows), dim3(1024), 0, at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

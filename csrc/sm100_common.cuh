@@ -14,7 +14,38 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace gb {
+
+// ------------------------------------------- programmatic dependent launch
+// Kernels of the decode chain are launched with programmatic stream
+// serialisation: the next kernel may start (allocate TMEM, initialise
+// barriers, stream frozen weights into shared memory) while this one drains.
+// Contract for every kernel launched through `launch_kernel`: it calls
+// `pdl_wait()` before it reads or writes any global memory that another
+// kernel produces or consumes.  Without the launch attribute both
+// instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool& pdl_enabled();  // process-wide switch, defined in gemm_tc.cu
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ~1 s at 2 GHz; far above any legitimate wait inside one kernel.
 constexpr long long kSpinLimitCycles = 2000000000LL;
@@ -177,12 +208,28 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_byte_addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
-// K-major, tile M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+// Shared-memory descriptor for an MN-major operand in 128-byte-swizzled
+// atoms: each atom is 8 K-rows of 128 bytes (64 MN elements); atoms follow
+// each other every `sbo` bytes along K and every `lbo` bytes along MN.  A
+// K-step of 16 elements spans two atoms along K (advance 2 * sbo).
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_byte_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_byte_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, tile
+// M x N; each operand K-major unless its MN-major flag is set.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n, bool a_mn = false, bool b_mn = false) {
   return (1u << 4)                                   // D format: f32
          | (1u << 7)                                 // A format: bf16
          | (1u << 10)                                // B format: bf16
+         | (static_cast<uint32_t>(a_mn ? 1 : 0) << 15)  // A major-ness
+         | (static_cast<uint32_t>(b_mn ? 1 : 0) << 16)  // B major-ness
          | (static_cast<uint32_t>(n >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }

@@ -145,22 +145,9 @@ def bench_decode(args) -> None:
 
 def bench_step(args) -> None:
     from graspo_b200.engine.rollout import FusedRolloutEngine
-    from graspo_b200.models.config import load_decoder_config
     from graspo_b200.models.fused import FusedQwen3
-    from graspo_b200.models.loader import SafetensorIndex
-    from graspo_b200.models.qwen3 import Qwen3Model
-    from graspo_b200.parallel.state import ParallelState
-    from graspo_b200.utils.synth import QWEN3_8B, write_qwen3_checkpoint
 
-    dims = dict(QWEN3_8B, num_hidden_layers=args.layers)
-    path = write_qwen3_checkpoint(Path(args.ckpt) / f"qwen3-8b-{args.layers}l", dims, seed=7, device="cuda",
-                                  with_tokenizer=False)
-    ps = ParallelState(device=torch.device("cuda", 0))
-    targets = {f"language.{m}" for m in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
-                                          "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")}
-    model = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=targets, lora_r=16,
-                       lora_alpha=32, lora_dropout=0.0, dtype=torch.bfloat16, device=ps.device, seed=1)
-    model.ensure_transposed()
+    model = _step_model(args)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 150000, (args.prompt_len,), generator=g).tolist() for _ in range(args.prompts)]
     for graph in (True, False):
@@ -178,9 +165,92 @@ def bench_step(args) -> None:
         }), flush=True)
 
 
+def _step_model(args):
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import Qwen3Model
+    from graspo_b200.parallel.state import ParallelState
+    from graspo_b200.utils.synth import QWEN3_8B, write_qwen3_checkpoint
+
+    dims = dict(QWEN3_8B, num_hidden_layers=args.layers)
+    path = write_qwen3_checkpoint(Path(args.ckpt) / f"qwen3-8b-{args.layers}l", dims, seed=7, device="cuda",
+                                  with_tokenizer=False)
+    ps = ParallelState(device=torch.device("cuda", 0))
+    targets = {f"language.{m}" for m in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                                          "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")}
+    model = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=targets, lora_r=16,
+                       lora_alpha=32, lora_dropout=args.dropout, dtype=torch.bfloat16, device=ps.device, seed=1)
+    model.ensure_transposed()
+    return model
+
+
+def bench_train(args) -> None:
+    """One GRASPO micro-batch (forward with saved inputs, log-probs, backward
+    with recompute) on ``--rows`` x ``--seq`` tokens, timed per phase; the
+    timed iterations sit in NVTX ranges named ``train_step``."""
+    from graspo_b200.models.fused import AttnMeta, FusedQwen3
+    from graspo_b200.ops._ext import check_errors, ext
+
+    model = _step_model(args)
+    f = FusedQwen3(model)
+    B, S = args.rows, args.seq
+    g = torch.Generator().manual_seed(0)
+    seq = torch.randint(0, 150000, (B, S), generator=g).cuda()
+    mask = torch.ones(B, S, dtype=torch.bool, device="cuda")
+    for b in range(B):  # left padding in half the rows, right padding in the others
+        if b % 2:
+            mask[b, : 37 * b] = False
+        else:
+            mask[b, S - 53 * (b + 1):] = False
+    tgt = torch.zeros_like(seq)
+    tgt[:, :-1] = seq[:, 1:]
+    tgt = tgt.reshape(-1)
+    w = torch.randn(B * S, device="cuda") * 1e-3
+
+    def fwd():
+        meta = AttnMeta.from_mask(mask)
+        x, inputs = f.stage_forward(f.embed(seq), meta, train=True, seed=1, keep_inputs=True)
+        hn, rstd = f.final_norm(x)
+        lp, lse = f.token_logprobs(hn, tgt)
+        return meta, x, inputs, hn, rstd, lse
+
+    def bwd(state):
+        meta, x, inputs, hn, rstd, lse = state
+        dhn = f.token_logprobs_backward(hn, tgt, lse, w)
+        dx = torch.empty_like(x)
+        ext().rmsnorm_bwd(dhn, x, model.norm, rstd, None, dx, model.cfg.rms_norm_eps)
+        f.stage_backward(inputs, dx, meta, train=True, seed=1)
+
+    for _ in range(2):
+        bwd(fwd())
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    times = []
+    for _ in range(args.iters):
+        torch.cuda.nvtx.range_push("train_step")
+        ev[0].record()
+        st = fwd()
+        ev[1].record()
+        bwd(st)
+        ev[2].record()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        times.append((ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])))
+    check_errors()
+    times.sort(key=lambda t: t[0] + t[1])
+    fw, bw = times[len(times) // 2]
+    tokens = B * S
+    print(json.dumps({
+        "kernel": "train_microbatch", "layers": args.layers, "rows": B, "seq": S, "dropout": args.dropout,
+        "fwd_ms": round(fw, 2), "bwd_ms": round(bw, 2),
+        "fwd_ms_per_layer": round(fw / args.layers, 3), "bwd_ms_per_layer": round(bw / args.layers, 3),
+        "tokens": tokens,
+    }), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "step", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "step", "train", "all"])
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
     parser.add_argument("--layers", type=int, default=4)
@@ -189,6 +259,9 @@ def main() -> None:
     parser.add_argument("--prompt-len", type=int, default=1024)
     parser.add_argument("--new", type=int, default=64)
     parser.add_argument("--ckpt", default="/tmp/graspo_b200_bench")
+    parser.add_argument("--rows", type=int, default=8)
+    parser.add_argument("--seq", type=int, default=3072)
+    parser.add_argument("--dropout", type=float, default=0.1)
     args = parser.parse_args()
     if args.what in ("gemm", "all"):
         bench_gemm(args)
@@ -196,6 +269,8 @@ def main() -> None:
         bench_decode(args)
     if args.what == "step":
         bench_step(args)
+    if args.what == "train":
+        bench_train(args)
 
 
 if __name__ == "__main__":

@@ -125,6 +125,10 @@ class GraspoFlowConfig(BaseModel):
       engine (0 = all rows of the prompt queue at once).
     * ``pg_timeout_sec`` – process-group timeout so a dead peer ends collectives
       with an error instead of a hang.
+    * ``decode_tp_allreduce`` – ``"fused"``: the decode loop's tensor-parallel
+      all-reduces run inside the o_proj / down_proj GEMMs (tile push into the
+      peers' memory over NVLink) and the following RMSNorm kernel; ``"nccl"``:
+      an NCCL all-reduce after each of those GEMMs.
     """
 
     model_config = _STRICT
@@ -154,6 +158,7 @@ class GraspoFlowConfig(BaseModel):
     kv_page_size: int = 64
     cuda_graph_decode: bool = True
     pg_timeout_sec: float = 600.0
+    decode_tp_allreduce: Literal["fused", "nccl"] = "fused"
 
     @field_validator("adapter")
     @classmethod

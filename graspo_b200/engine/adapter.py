@@ -157,7 +157,8 @@ class Qwen3Adapter:
             self.model.ensure_transposed()
             self._fused = FusedQwen3(self.model)
             self._engine = FusedRolloutEngine(self.model, self._fused, page_size=flow.kv_page_size,
-                                              use_graph=flow.cuda_graph_decode)
+                                              use_graph=flow.cuda_graph_decode,
+                                              fused_tp_allreduce=flow.decode_tp_allreduce == "fused")
         else:
             from graspo_b200.engine.rollout import EagerRolloutEngine
 

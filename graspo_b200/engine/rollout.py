@@ -87,7 +87,7 @@ def _gen_lengths(tokens: torch.Tensor, eos_id: int, ignore_eos: bool) -> list[in
 
 class FusedRolloutEngine:
     def __init__(self, model: Qwen3Model, fused, *, page_size: int = 64, use_graph: bool = True,
-                 graph_chunk: int = 16) -> None:
+                 graph_chunk: int = 16, fused_tp_allreduce: bool = True) -> None:
         from graspo_b200.ops._ext import ext
 
         self.m = model
@@ -99,6 +99,10 @@ class FusedRolloutEngine:
         self._pool_shape = None
         self.k_pool = self.v_pool = None
         self.nvtx = False  # wrap eager decode steps in NVTX ranges "decode_step"
+        # tensor-parallel all-reduce of the decode loop inside the GEMM / RMSNorm
+        # kernels (peer-memory tile push) instead of NCCL calls
+        self.fused_tp = bool(fused_tp_allreduce) and model.ps.tp_size > 1 and model.device.type == "cuda"
+        self._peer_sites: dict[tuple, object] = {}
 
     def _ensure_pool(self, num_pages: int) -> None:
         m = self.m
@@ -221,9 +225,23 @@ class FusedRolloutEngine:
         steps = max_new_tokens - 1
         tails = self._refresh_lora_rows()
         bufs = self._decode_buffers(rows, tails)
+        if self.fused_tp:
+            H = m.cfg.hidden_size
+            self._sites = {"o": self._peer_site("o", rows, H + tails.get("w_o", 0)),
+                           "d": self._peer_site("d", rows, H + tails.get("w_down", 0))}
+        else:
+            self._sites = {}
         cap = (prompt_pages + gen_pages) * self.page
-        self._splits = decode_attention_splits(rows, m.nkv, cap)
-        bufs["attn_scratch"] = torch.zeros(rows * m.nq * self._splits * (m.D + 2) + rows * m.nkv,
+        # shared-prefix attention: the prompt keys of a group are attended once for
+        # all G rows (full tensor-core tiles), the generated keys per row
+        heads_per_kv = m.nq // m.nkv
+        self._prefix = (P if dev.type == "cuda" and self.page % 64 == 0 and G > 1 and G * heads_per_kv <= 64
+                        else 0)
+        self._group = G
+        self._prefix_splits = (max(1, min(P // 64, round(2 * 148 / max(1, n * m.nkv)))) if self._prefix else 1)
+        self._splits = decode_attention_splits(rows, m.nkv, cap - self._prefix)
+        slots = self._splits + (4 * self._prefix_splits if self._prefix else 0)
+        bufs["attn_scratch"] = torch.zeros(rows * m.nq * slots * (m.D + 2) + rows * m.nkv,
                                            device=dev, dtype=torch.float32)
         row_ids = torch.arange(rows, dtype=torch.long, device=dev)
 
@@ -283,13 +301,14 @@ class FusedRolloutEngine:
         L = m.lora.layer_layouts(m.layers[0].index, m.sizes)
         return {"w_qkv": L["a_qkv"].shape[0] if "a_qkv" in L else 0,
                 "w_o": L["a_o"].shape[0] if "a_o" in L else 0,
-                "w_down": L["a_down"].shape[0] if "a_down" in L else 0}
+                "w_down": L["a_down"].shape[0] if "a_down" in L else 0,
+                "u_gu": L["a_gu"].shape[0] if "a_gu" in L else 0}
 
     def _refresh_lora_rows(self) -> dict[str, int]:
         """Write the current (scaled) LoRA A factors into the weights' spare rows."""
         m = self.m
         tails = self._lora_tails()
-        m.ensure_tail_rows(tails)
+        m.ensure_tail_rows({k: v for k, v in tails.items() if k.startswith("w_")})
         for lw in m.layers:
             L = m.lora.layer_layouts(lw.index, m.sizes)
             for name, key in (("w_qkv", "a_qkv"), ("w_o", "a_o"), ("w_down", "a_down")):
@@ -297,6 +316,19 @@ class FusedRolloutEngine:
                     ext = getattr(lw, f"{name}_ext")
                     ext[getattr(lw, name).shape[0]:].copy_(L[key])
         return tails
+
+    def _peer_site(self, name: str, rows: int, width: int):
+        """The fused all-reduce site ``name`` for ``rows`` x ``width`` partials (kept across calls)."""
+        key = (name, rows, width)
+        site = self._peer_sites.get(key)
+        if site is None:
+            from graspo_b200.parallel.symm import PeerReduce
+
+            for k in [k for k in self._peer_sites if k[0] == name]:
+                self._peer_sites.pop(k).close()
+            site = PeerReduce(rows, width, self.m.ps.tp_group, self.m.device)
+            self._peer_sites[key] = site
+        return site
 
     def _decode_buffers(self, rows: int, tails: dict[str, int]) -> dict[str, torch.Tensor]:
         m = self.m
@@ -313,29 +345,23 @@ class FusedRolloutEngine:
             "q": torch.empty(rows, m.nq, m.D, device=dev, dtype=dt),
             "attn": torch.empty(rows, m.q_local, device=dev, dtype=dt),
             "o_ws": torch.zeros(rows, H + tails.get("w_o", 0), device=dev, dtype=f32),
+            # U = s A xn of the gate/up LoRA (the K-extension operand of that GEMM)
+            "u_gu": torch.zeros(rows, max(tails.get("u_gu", 0), 1), device=dev, dtype=dt),
             "act": torch.empty(rows, m.inter_local, device=dev, dtype=dt),
             "d_ws": torch.zeros(rows, H + tails.get("w_down", 0), device=dev, dtype=f32),
             "logits": torch.empty(rows, m.vocab_local, device=dev, dtype=f32),
         }
-
-    @staticmethod
-    def _u(b: dict, name: str, rows: int, width: int, like: torch.Tensor) -> torch.Tensor:
-        key = f"{name}_{width}"
-        buf = b.get(key)
-        if buf is None:
-            buf = torch.zeros(rows, width, device=like.device, dtype=like.dtype)
-            b[key] = buf
-        return buf
 
     def _decode_step(self, st, b, bt, row_ids, P, temperature, top_p, seed, eos_id, pad_id, ignore_eos) -> None:
         """One token for every row: embedding, the decoder layers, LM head, sampling.
 
         LoRA: q/k/v, o and down compute U = s A x inside their base GEMM (A sits
         in spare weight rows, U lands after the projection columns of the fp32
-        workspace) and the consuming kernel adds B U -- qk_norm_rope for q/k/v,
-        the next residual-add + RMSNorm for o and down.  gate/up keep the
-        K-extension (SwiGLU in the epilogue needs the complete sum): its U is
-        computed by the RMSNorm kernel that produces the GEMM input.
+        split-K workspace) and the consuming kernel adds B U -- qk_norm_rope
+        for q/k/v, the next residual-add + RMSNorm for o and down.  gate/up
+        keep the K-extension, because SwiGLU in the GEMM epilogue needs the
+        complete pre-activation: the RMSNorm kernel that produces the GEMM
+        input also computes its U.
         """
         from graspo_b200.ops.gemm import gemm
 
@@ -345,6 +371,9 @@ class FusedRolloutEngine:
         tp = m.ps.tp_size
         r = m.lora.r
         rows = row_ids.shape[0]
+        so, sd = self._sites.get("o"), self._sites.get("d")
+        o_norm = so.norm_kwargs() if so is not None else {}
+        d_norm = sd.norm_kwargs() if sd is not None else {}
         C.embedding(st["next_ids"], m.embed, b["x_a"])
         scale = 1.0 / math.sqrt(m.D)
         b_down_prev = None
@@ -355,7 +384,7 @@ class FusedRolloutEngine:
             # partial sums (d_ws, with its LoRA U) are added here, the sum stored to x_a
             C.add_rmsnorm(b["x_b"] if not first else b["x_a"], None if first else b["d_ws"],
                           None if first else b["x_a"], lw.ln1, b["xn"], None, None, None, 1.0, eps,
-                          b_down_prev, r if b_down_prev is not None else 0)
+                          b_down_prev, r if b_down_prev is not None else 0, **({} if first else d_norm))
             has_qkv = "a_qkv" in L
             gemm(lw.w_qkv_ext if has_qkv else lw.w_qkv, b["xn"], b["qkv_ws"], swap=True, epilogue="atomic",
                  splits=3)
@@ -363,25 +392,27 @@ class FusedRolloutEngine:
                            self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps,
                            L.get("b_qkv"), r if has_qkv else 0)
             C.paged_decode_attention(b["q"], self.k_pool[li], self.v_pool[li], bt, st["start"], st["kv_len"],
-                                     b["attn"], scale, self._splits, b["attn_scratch"])
+                                     b["attn"], scale, self._splits, b["attn_scratch"], self._prefix, self._group,
+                                     self._prefix_splits)
             has_o = "a_o" in L
-            gemm(lw.w_o_ext if has_o else lw.w_o, b["attn"], b["o_ws"], swap=True, epilogue="atomic", splits=4)
-            if tp > 1:
+            gemm(lw.w_o_ext if has_o else lw.w_o, b["attn"], b["o_ws"], swap=True, epilogue="atomic", splits=4,
+                 push=so)
+            if tp > 1 and so is None:
                 dist.all_reduce(b["o_ws"], group=tp_group)
             a_gu = L.get("a_gu")
-            ug = self._u(b, "u", rows, a_gu.shape[0], b["xn"]) if a_gu is not None else None
+            ug = b["u_gu"] if a_gu is not None else None
             C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None, a_gu, ug, 1.0, eps,
-                          L.get("b_o"), r if has_o else 0)
+                          L.get("b_o"), r if has_o else 0, **o_norm)
             gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
                  swap=True, epilogue="swiglu")
             has_d = "a_down" in L
             gemm(lw.w_down_ext if has_d else lw.w_down, b["act"], b["d_ws"], swap=True, epilogue="atomic",
-                 splits=4)
-            if tp > 1:
+                 splits=4, push=sd)
+            if tp > 1 and sd is None:
                 dist.all_reduce(b["d_ws"], group=tp_group)
             b_down_prev = L.get("b_down")
         C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps,
-                      b_down_prev, r if b_down_prev is not None else 0)
+                      b_down_prev, r if b_down_prev is not None else 0, **d_norm)
         logits = self._lm_logits(b["xn"], b["logits"])
         C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"], st["pos"],
                         st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)

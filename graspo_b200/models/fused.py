@@ -45,13 +45,10 @@ def _tp_all_reduce(x: torch.Tensor, group) -> torch.Tensor:
     return x
 
 
-def _t(x: torch.Tensor) -> torch.Tensor:
-    """K-major transpose for token-reduction GEMMs (row stride padded to 8)."""
-    rows, cols = x.shape
-    buf = torch.empty(cols, (rows + 7) // 8 * 8, dtype=x.dtype, device=x.device)
-    out = buf[:, :rows]
-    ext().transpose_bf16(x, out)
-    return out
+def _grad_splits(rows: int, sms: int = 148) -> int:
+    """Split-K factor for a token-contracted LoRA gradient with ``rows`` output rows."""
+    tiles = max(1, -(-rows // 128))
+    return max(1, min(16, round(2 * sms / tiles)))
 
 
 @dataclass
@@ -170,26 +167,32 @@ class FusedQwen3:
         return x2, s
 
     # ------------------------------------------------------------ backward
-    def _lora_linear_backward(self, dy, w_t, saved_u, saved_xd, b_ext, a_ext, site, layer, seed, train):
+    def _lora_linear_backward(self, dy, w, saved_u, saved_xd, b_ext, a_ext, site, layer, seed, train):
         """d(input) of y = x W^T + U B^T with U = drop(x) (sA)^T, plus LoRA grads.
 
+        Every operand is read as stored: ``W`` [N, K], ``B`` [N, 64k] and ``sA``
+        [64k, K] are the MN-major B operand of ``dy @ W`` / ``dy @ B`` /
+        ``du @ sA``, and the gradients contract over tokens with both operands
+        MN-major (split-K fp32 atomics), so no transposed copy is made.
         Returns (dx, db_full [N, 64k] fp32, da_full [64k, K] fp32) -- the
         gradient w.r.t. the padded layouts (caller scatters into parameters).
         """
         if saved_u is None:
-            return gemm(dy, w_t), None, None
-        b_t = b_ext.t().contiguous()                      # [64k, N]
-        du = gemm(dy, b_t, bn=64)                          # [T, 64k]
-        a_t = a_ext.t().contiguous()                      # [K, 64k]
+            return gemm(dy, w, b_mn=True), None, None
+        du = gemm(dy, b_ext, b_mn=True, bn=64)            # [T, 64k]
         p = self.m.lora.dropout
         if train and p > 0:
-            dx = gemm(dy, w_t)
-            tmp = gemm(du, a_t)
+            dx = gemm(dy, w, b_mn=True)
+            tmp = gemm(du, a_ext, b_mn=True)
             self._dropout_add(tmp, dx, site, layer, seed)
         else:
-            dx = gemm(dy, w_t, ext_ab=(du, a_t))
-        db = gemm(_t(dy), _t(saved_u), epilogue="store_f32", bn=64)      # [N, 64k]
-        da = gemm(_t(du), _t(saved_xd), epilogue="store_f32")             # [64k, K]
+            dx = gemm(dy, w, b_mn=True, ext_ab=(du, a_ext))
+        n_out, width, k_in = dy.shape[1], saved_u.shape[1], saved_xd.shape[1]
+        db = torch.zeros(n_out, width, device=dy.device, dtype=torch.float32)
+        gemm(dy, saved_u, db, epilogue="atomic", a_mn=True, b_mn=True, bn=64, splits=_grad_splits(n_out))
+        da = torch.zeros(width, k_in, device=dy.device, dtype=torch.float32)
+        gemm(saved_xd, du, da, epilogue="atomic", a_mn=True, b_mn=True, bn=64, swap=True,
+             splits=_grad_splits(k_in))
         return dx, db, da
 
     def _scatter_grads(self, layer: int, group: str, db, da) -> None:
@@ -222,7 +225,7 @@ class FusedQwen3:
         tp_group = m.ps.tp_group
         li = lw.index
         # --- down projection
-        dact, db, da = self._lora_linear_backward(dx2, lw.w_down_t, s.u_d, s.act_d, L.get("b_down"),
+        dact, db, da = self._lora_linear_backward(dx2, lw.w_down, s.u_d, s.act_d, L.get("b_down"),
                                                   L.get("a_down"), "down", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "down", db, da)
@@ -231,7 +234,7 @@ class FusedQwen3:
         C.swiglu_bwd(s.gu, dact, dgu)
         del dact
         # --- gate/up
-        dxn2, db, da = self._lora_linear_backward(dgu, lw.w_gu_t, s.u_gu, s.xd2, L.get("b_gu"), L.get("a_gu"),
+        dxn2, db, da = self._lora_linear_backward(dgu, lw.w_gu, s.u_gu, s.xd2, L.get("b_gu"), L.get("a_gu"),
                                                   "gu", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "gu", db, da)
@@ -240,7 +243,7 @@ class FusedQwen3:
         dx1 = torch.empty_like(dx2)
         C.rmsnorm_bwd(dxn2, s.x1, lw.ln2, s.rstd2, dx2, dx1, self.eps)
         # --- o projection
-        dattn, db, da = self._lora_linear_backward(dx1, lw.w_o_t, s.u_o, s.attn_d, L.get("b_o"), L.get("a_o"),
+        dattn, db, da = self._lora_linear_backward(dx1, lw.w_o, s.u_o, s.attn_d, L.get("b_o"), L.get("a_o"),
                                                    "o", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "o", db, da)
@@ -250,7 +253,7 @@ class FusedQwen3:
         C.qk_norm_rope_bwd(dq, dk, dv, s.qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, dqkv, m.nq, m.nkv, self.eps)
         del dq, dk, dv
         # --- qkv projection
-        dxn, db, da = self._lora_linear_backward(dqkv, lw.w_qkv_t, s.u_qkv, s.xd, L.get("b_qkv"), L.get("a_qkv"),
+        dxn, db, da = self._lora_linear_backward(dqkv, lw.w_qkv, s.u_qkv, s.xd, L.get("b_qkv"), L.get("a_qkv"),
                                                  "qkv", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "qkv", db, da)
@@ -325,7 +328,7 @@ class FusedQwen3:
             t1 = min(T, t0 + chunk_tokens)
             dlog = gemm(h[t0:t1], m.lm_head, epilogue="softmax_grad", targets=local_t[t0:t1],
                         row_lse=lse[t0:t1].contiguous(), row_scale=g[t0:t1].contiguous())
-            gemm(dlog, m.lm_head_t, dh[t0:t1])
+            gemm(dlog, m.lm_head, dh[t0:t1], b_mn=True)
             del dlog
         _tp_all_reduce(dh, m.ps.tp_group)
         return dh

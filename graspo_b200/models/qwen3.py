@@ -69,10 +69,6 @@ class LayerWeights:
     w_o: torch.Tensor
     w_gu: torch.Tensor
     w_down: torch.Tensor
-    w_qkv_t: torch.Tensor | None = None
-    w_o_t: torch.Tensor | None = None
-    w_gu_t: torch.Tensor | None = None
-    w_down_t: torch.Tensor | None = None
     # the same weights followed by spare rows holding a LoRA A factor (decode
     # GEMMs compute W x and s A x in one pass); w_qkv / w_o / w_down are views
     w_qkv_ext: torch.Tensor | None = None
@@ -201,7 +197,6 @@ class Qwen3Model:
         else:
             self.norm = None
             self.lm_head = None
-        self.lm_head_t: torch.Tensor | None = None
         self.lora = LoRAAdapter(
             modules, r=lora_r, alpha=lora_alpha, dropout=lora_dropout, device=dev, seed=seed, tp_rank=tr
         )
@@ -214,15 +209,9 @@ class Qwen3Model:
         return self.layers[self.local_layers.index(idx)]
 
     def ensure_transposed(self) -> None:
-        """Build the K-major transposed weight copies used by backward GEMMs."""
-        for lw in self.layers:
-            if lw.w_qkv_t is None:
-                lw.w_qkv_t = lw.w_qkv.t().contiguous()
-                lw.w_o_t = lw.w_o.t().contiguous()
-                lw.w_gu_t = lw.w_gu.t().contiguous()
-                lw.w_down_t = lw.w_down.t().contiguous()
-        if self.include_head and self.lm_head_t is None:
-            self.lm_head_t = self.lm_head.t().contiguous()
+        """Kept for callers of earlier versions: backward GEMMs read every weight
+        MN-major as stored, so no transposed copies are built."""
+        return None
 
     def ensure_tail_rows(self, tails: dict[str, int]) -> None:
         """Give ``w_qkv`` / ``w_o`` / ``w_down`` ``tails[name]`` spare rows.

@@ -78,6 +78,9 @@ def ext():
                 "graspo_b200._C (the sm_100a kernel library) is not built; run "
                 "`python setup.py build_ext --inplace` in the repository root"
             ) from exc
+        import os
+
+        module.set_pdl(os.environ.get("GRASPO_PDL", "0") == "1")
         _C = _Counting(module)
     return _C
 

@@ -24,10 +24,17 @@ def _f(x):
 
 
 def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epilogue, swap, bn, splits, err,
-            max_ctas):
-    acc = _f(A) @ _f(B).T
+            max_ctas, push_dst=None, push_flag=None, tile_ctr=None, layout=0):
+    if push_dst is not None:
+        raise NotImplementedError("the peer-memory tile push needs GPUs")
+    a_mn, b_mn = bool(layout & 2), bool(layout & 1)
+
+    def op(a, b):
+        return (_f(a).T if a_mn else _f(a)) @ (_f(b) if b_mn else _f(b).T)
+
+    acc = op(A, B)
     if A2 is not None:
-        acc = acc + _f(A2) @ _f(B2).T
+        acc = acc + op(A2, B2)
     if swap:
         acc = acc.T  # [tokens, features]
     M, N = acc.shape
@@ -66,7 +73,10 @@ def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epi
         raise ValueError(epilogue)
 
 
-def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps, delta_lora_b=None, delta_lora_r=0):
+def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps, delta_lora_b=None, delta_lora_r=0,
+                peer_src=None, peer_sync=None, peer_expected=0, err=None):
+    if peer_src is not None:
+        raise NotImplementedError("the peer-memory sum needs GPUs")
     x = _f(h)
     H = h.shape[-1]
     if delta is not None:
@@ -173,7 +183,8 @@ def embedding(ids, table, out):
     out.copy_(table[ids.long().clamp(0, table.shape[0] - 1)])
 
 
-def paged_decode_attention(q, k_pool, v_pool, block_table, start, length, out, scale, splits, scratch):
+def paged_decode_attention(q, k_pool, v_pool, block_table, start, length, out, scale, splits, scratch,
+                           prefix_len=0, group_rows=1, prefix_splits=1):
     rows, nq, D = q.shape
     nkv, page = k_pool.shape[1], k_pool.shape[2]
     G = nq // nkv

@@ -12,6 +12,11 @@
 * ``swap=True``: ``a`` is the weight ``[N_out, K]`` and ``b`` the activations
   ``[T, K]``; the result is stored as ``[T, N_out]``.  This is the decode
   shape: tokens fill the narrow N side of the tensor-core tile.
+* ``b_mn=True``: ``b`` is given as ``[K, N]`` (read MN-major by the tensor
+  cores, no transpose) -- e.g. ``gemm(dy, W, b_mn=True)`` is ``dy @ W`` for
+  the frozen weight as stored; ``a_mn=True`` likewise takes ``a`` as
+  ``[K, M]`` (with both set the product contracts over the shared leading
+  dimension, e.g. LoRA gradients over tokens).
 """
 
 from __future__ import annotations
@@ -54,15 +59,18 @@ def gemm(
     bn: int | None = None,
     splits: int = 1,
     max_ctas: int = 0,
+    push=None,
+    a_mn: bool = False,
+    b_mn: bool = False,
 ) -> torch.Tensor:
     epi = EPILOGUES[epilogue]
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
     if swap:
-        tokens, n_out = b.shape[0], a.shape[0]
-        out_shape = (tokens, n_out // 2 if epilogue == "swiglu" else n_out)
-        narrow = tokens
+        out_shape = (N, M // 2 if epilogue == "swiglu" else M)
     else:
-        out_shape = (a.shape[0], b.shape[0] // 2 if epilogue == "swiglu" else b.shape[0])
-        narrow = b.shape[0]
+        out_shape = (M, N // 2 if epilogue == "swiglu" else N)
+    narrow = N
     if out is None:
         dtype = torch.float32 if epilogue in ("atomic", "store_f32") else torch.bfloat16
         if epilogue == "lse":
@@ -76,9 +84,13 @@ def gemm(
             # the extension pairs with (a, b) in the same roles
             pass
     bn = bn or pick_bn(narrow, swap)
+    if b_mn:
+        bn = max(bn, 64)
+    kw = push.gemm_kwargs() if push is not None else {}
+    layout = (2 if a_mn else 0) | (1 if b_mn else 0)
     ext().gemm_tc(
         a, b, a2, b2, out, residual, aux, targets, tgt_logit, row_lse, row_scale,
-        epi, swap, bn, splits, err_word(a.device), max_ctas,
+        epi, swap, bn, splits, err_word(a.device), max_ctas, **kw, layout=layout,
     )
     return out
 

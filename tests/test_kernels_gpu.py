@@ -90,6 +90,31 @@ def test_gemm_atomic_split_k(splits):
     _close(out, a.float() @ b.float().T, 1e-2)
 
 
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_b_mn_major(bn):
+    """dY @ W with the weight read as stored ([N_out, K_in], MN-major B), with and without a K-extension."""
+    from graspo_b200.ops.gemm import gemm
+
+    dy, w = _rand(300, 448), _rand(448, 200)
+    out = gemm(dy, w, b_mn=True, bn=bn)
+    _close(out, dy.float() @ w.float(), 1e-2)
+    du, a = _rand(300, 64), _rand(64, 200)
+    out2 = gemm(dy, w, b_mn=True, bn=bn, ext_ab=(du, a))
+    _close(out2, dy.float() @ w.float() + du.float() @ a.float(), 1e-2)
+
+
+@pytest.mark.parametrize("swap", [False, True])
+def test_gemm_both_mn_major_split_k(swap):
+    """Contraction over the shared leading (token) dimension: A^T B, fp32 split-K atomics."""
+    from graspo_b200.ops.gemm import gemm
+
+    x, du = _rand(1000, 320), _rand(1000, 64)
+    ref = x.float().T @ du.float()                       # [320, 64]
+    out = torch.zeros(64, 320, device="cuda") if swap else torch.zeros(320, 64, device="cuda")
+    gemm(x, du, out, epilogue="atomic", splits=3, a_mn=True, b_mn=True, swap=swap)
+    _close(out, ref.T if swap else ref, 1e-2)
+
+
 @pytest.mark.parametrize("tokens", [8, 64, 100])
 @pytest.mark.parametrize("epilogue", ["store", "atomic", "store_f32"])
 def test_gemm_swap(tokens, epilogue):
@@ -254,6 +279,46 @@ def test_paged_decode_attention(page, G):
         vals = torch.cat([vp[perm[r, p]] for p in range(max_pages)], dim=1)[:, s0:L]
         kk = keys.float().repeat_interleave(nq // nkv, 0)
         vv = vals.float().repeat_interleave(nq // nkv, 0)
+        att = torch.softmax(q[r].float()[:, None, :] @ kk.transpose(1, 2) * scale, -1) @ vv
+        _close(out[r].view(nq, D), att.squeeze(1), 2e-2)
+
+
+@pytest.mark.parametrize("G,R", [(4, 4), (4, 8), (8, 8), (2, 3)])
+def test_paged_decode_attention_shared_prefix(G, R):
+    """Prompt pages shared by the R rows of a group, attended once per group."""
+    nkv, D, page, P = 2, 128, 64, 192
+    nq = nkv * G
+    groups = 2
+    rows = groups * R
+    gen_pages = 3
+    prompt_pages = P // page
+    num_pages = groups * prompt_pages + rows * gen_pages
+    kp, vp = _rand(num_pages, nkv, page, D), _rand(num_pages, nkv, page, D)
+    bt = torch.empty(rows, prompt_pages + gen_pages, dtype=torch.int32)
+    for r in range(rows):
+        grp = r // R
+        bt[r, :prompt_pages] = torch.arange(grp * prompt_pages, (grp + 1) * prompt_pages)
+        base = groups * prompt_pages + r * gen_pages
+        bt[r, prompt_pages:] = torch.arange(base, base + gen_pages)
+    bt = bt.cuda()
+    start = torch.tensor([7] * R + [0] * R, device="cuda", dtype=torch.int32)
+    lens = torch.tensor([P + 1 + 37 * r for r in range(rows)], device="cuda", dtype=torch.int32)
+    q = _rand(rows, nq, D)
+    scale = 1 / math.sqrt(D)
+    splits = 2
+    ref = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+    scratch = torch.zeros(rows * nq * 3 * (D + 2) + rows * nkv, device="cuda")
+    _ext().paged_decode_attention(q, kp, vp, bt, start, lens, ref, scale, 3, scratch)
+    out = torch.empty_like(ref)
+    pscr = torch.zeros(rows * nq * (splits + 4 * 2) * (D + 2) + rows * nkv, device="cuda")
+    for _ in range(2):
+        _ext().paged_decode_attention(q, kp, vp, bt, start, lens, out, scale, splits, pscr, P, R, 2)
+        _close(out, ref, 1e-2)
+    for r in range(rows):
+        keys = torch.cat([kp[bt[r, p]] for p in range(bt.shape[1])], dim=1)[:, int(start[r]) : int(lens[r])]
+        vals = torch.cat([vp[bt[r, p]] for p in range(bt.shape[1])], dim=1)[:, int(start[r]) : int(lens[r])]
+        kk = keys.float().repeat_interleave(G, 0)
+        vv = vals.float().repeat_interleave(G, 0)
         att = torch.softmax(q[r].float()[:, None, :] @ kk.transpose(1, 2) * scale, -1) @ vv
         _close(out[r].view(nq, D), att.squeeze(1), 2e-2)
 

@@ -97,6 +97,54 @@ def _worker(rank, world, path):
     pstate.destroy()
 
 
+def _peer_reduce_worker(rank, world):
+    from graspo_b200.ops._ext import check_errors, ext
+    from graspo_b200.ops.gemm import gemm
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.symm import PeerReduce
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ps = pstate.initialize(2, 1, 0, timeout_sec=120)
+    C = ext()
+    rows, H, tail, K = 96, 1024, 64, 768
+    site = PeerReduce(rows, H + tail, ps.tp_group, ps.device)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    shared = torch.Generator(device="cuda").manual_seed(7)
+    h = torch.randn(rows, H, device="cuda", generator=shared).bfloat16()
+    w = (torch.rand(H, device="cuda", generator=shared) + 0.5).bfloat16()
+    lb = (torch.randn(H, 64, device="cuda", generator=shared) * 0.1).bfloat16()
+    ws = torch.zeros(rows, H + tail, device="cuda")
+    for it in range(3):  # counters must come back to their start state every step
+        W = (torch.randn(H + tail, K, device="cuda", generator=g) * 0.05).bfloat16()
+        x = torch.randn(rows, K, device="cuda", generator=g).bfloat16()
+        gemm(W, x, ws, swap=True, epilogue="atomic", splits=3, push=site)
+        h_out = torch.empty_like(h)
+        y = torch.empty_like(h)
+        C.add_rmsnorm(h, ws, h_out, w, y, None, None, None, 1.0, 1e-6, lb, 16, **site.norm_kwargs())
+        torch.cuda.synchronize()
+        check_errors()
+        part = x.float() @ W.float().T
+        parts = [torch.empty_like(part) for _ in range(2)]
+        torch.distributed.all_gather(parts, part, group=ps.tp_group)
+        tot = parts[0] + parts[1]
+        d = tot[:, :H] + tot[:, H : H + 16] @ lb[:, :16].float().T
+        xr = (h.float() + d).bfloat16().float()
+        ref = (xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).bfloat16()
+        err = (y.float() - ref.float()).abs().max().item()
+        assert err < 0.05 * ref.float().abs().max().item(), f"step {it}: max err {err}"
+        assert torch.count_nonzero(ws).item() == 0, "workspace must be zeroed by the consumer"
+        other = y.clone()
+        torch.distributed.broadcast(other, src=0, group=ps.tp_group)
+        assert torch.equal(y, other), "ranks must hold bit-identical sums"
+    site.close()
+    pstate.destroy()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_tp_allreduce_matches_nccl():
+    run_world(2, _peer_reduce_worker, timeout=300)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tp2_fused_matches_tp1(tmp_path):
     from graspo_b200.utils.synth import write_qwen3_checkpoint
