@@ -80,7 +80,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
 
   const int s0 = a.start[row], s1 = a.len[row];
   const int k_begin = max(s0, split * a.keys_per_split);
-  const int k_end = min(s1, (split + 1) * a.keys_per_split);
+  // keys beyond the row's block table are never read, whatever len says
+  const int k_end = min(min(s1, a.max_pages * a.page_size), (split + 1) * a.keys_per_split);
 
   float m[G], l[G], acc[G][4];
 #pragma unroll
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
   const int row0 = grp * R;
   const int s0 = a.start[row0];
   const int k_begin = max(s0, split * a.prefix_kps);
-  const int k_end = min(a.prefix_len, (split + 1) * a.prefix_kps);
+  const int k_end = min(min(a.prefix_len, a.max_pages * a.page_size), (split + 1) * a.prefix_kps);
   const int* bt = a.block_table + static_cast<long>(row0) * a.max_pages;
   const uint32_t sbase = smem_addr(tc_smem);
   const int total = a.prefix_slots + a.splits;
@@ -501,7 +502,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
   const int P = a.prefix_len;  // 0 unless the shared prefix is handled separately
   const int total = a.prefix_slots + a.splits;
   const int k_begin = max(max(s0, P), P + split * a.keys_per_split);
-  const int k_end = min(s1, P + (split + 1) * a.keys_per_split);
+  // keys beyond the row's block table are never read, whatever len says
+  const int k_end = min(min(s1, a.max_pages * a.page_size), P + (split + 1) * a.keys_per_split);
   const int t_first = k_begin / kTile, t_last = (k_end - 1) / kTile;
   const int* bt = a.block_table + static_cast<long>(row) * a.max_pages;
   const uint32_t sbase = smem_addr(tc_smem);

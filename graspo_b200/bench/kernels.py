@@ -248,9 +248,76 @@ def bench_train(args) -> None:
     }), flush=True)
 
 
+def bench_profile(args) -> None:
+    """Small, fixed launches of one kernel family for an ncu capture (no timing).
+
+    ``--kernel``: ``gemm`` (training gate/up projection with the SwiGLU
+    epilogue, 8192 tokens), ``gemm_mn`` (dgrad against the stored weight,
+    MN-major B), ``decode_attn`` (64 rows, 2048 keys, shared 1024-key prompt
+    per group of 8), ``flash_fwd`` / ``flash_bwd`` (4 x 3072 tokens, 32/8 heads).
+    """
+    from graspo_b200.ops._ext import check_errors, ext
+    from graspo_b200.ops.gemm import gemm
+
+    k = args.kernel
+    runs = []
+    if k == "gemm":
+        x, w = torch.randn(8192, 4096, device="cuda").bfloat16(), torch.randn(24576, 4096, device="cuda").bfloat16()
+        runs.append(lambda: gemm(x, w, epilogue="swiglu"))
+    elif k == "gemm_mn":
+        dy, w = torch.randn(8192, 24576, device="cuda").bfloat16(), torch.randn(24576, 4096, device="cuda").bfloat16()
+        runs.append(lambda: gemm(dy, w, b_mn=True))
+    elif k == "decode_attn":
+        rows, nq, nkv, D, page, P, ctx, G = 64, 32, 8, 128, 64, 1024, 2048, 8
+        n = rows // G
+        pp, gp = P // page, (ctx - P) // page
+        num_pages = n * pp + rows * gp
+        kp = torch.randn(num_pages, nkv, page, D, device="cuda").bfloat16()
+        vp = torch.randn_like(kp)
+        bt = torch.empty(rows, pp + gp, dtype=torch.int32)
+        for r in range(rows):
+            bt[r, :pp] = torch.arange((r // G) * pp, (r // G + 1) * pp)
+            bt[r, pp:] = torch.arange(n * pp + r * gp, n * pp + (r + 1) * gp)
+        bt = bt.cuda()
+        q = torch.randn(rows, nq, D, device="cuda").bfloat16()
+        start = torch.zeros(rows, device="cuda", dtype=torch.int32)
+        ln = torch.full((rows,), ctx, device="cuda", dtype=torch.int32)
+        out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+        scratch = torch.zeros(rows * nq * 12 * (D + 2) + rows * nkv, device="cuda")
+        runs.append(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), 4, scratch,
+                                                         P, G, 2))
+    elif k in ("flash_fwd", "flash_bwd"):
+        B, S, nq, nkv, D = 4, 3072, 32, 8, 128
+        T = B * S
+        q = torch.randn(T, nq, D, device="cuda").bfloat16()
+        kk = torch.randn(T, nkv, D, device="cuda").bfloat16()
+        v = torch.randn(T, nkv, D, device="cuda").bfloat16()
+        start = torch.zeros(B, device="cuda", dtype=torch.int32)
+        end = torch.full((B,), S, device="cuda", dtype=torch.int32)
+        o = torch.empty_like(q)
+        lse = torch.empty(T, nq, device="cuda")
+        ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D))
+        if k == "flash_fwd":
+            runs.append(lambda: ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D)))
+        else:
+            do = torch.randn_like(q)
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)
+            runs.append(lambda: ext().flash_attn_bwd(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
+                                                     1 / math.sqrt(D)))
+    else:
+        raise SystemExit(f"unknown kernel {k}")
+    for _ in range(args.iters):
+        for fn in runs:
+            fn()
+    torch.cuda.synchronize()
+    check_errors()
+    print(json.dumps({"profile": k, "launches": args.iters * len(runs)}), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "step", "train", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "step", "train", "profile", "all"])
+    parser.add_argument("--kernel", default="gemm")
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
     parser.add_argument("--layers", type=int, default=4)
@@ -271,6 +338,8 @@ def main() -> None:
         bench_step(args)
     if args.what == "train":
         bench_train(args)
+    if args.what == "profile":
+        bench_profile(args)
 
 
 if __name__ == "__main__":

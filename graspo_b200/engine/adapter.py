@@ -109,8 +109,11 @@ class Qwen3Adapter:
         cfg = self.config
         flow = cfg.graspoflow
         self.ps = pstate.initialize(flow.tp_size, flow.pp_size, flow.dp_size, timeout_sec=flow.pg_timeout_sec)
-        if self.ps.pp_size > 1:
-            raise NotImplementedError("pipeline-parallel execution is provided by PipelineQwen3Adapter")
+        from graspo_b200.parallel.p2p import StageComm
+
+        self._comm = StageComm(self.ps)
+        if self.ps.pp_size > 1 and not self.fused:
+            raise NotImplementedError("pipeline parallelism runs on the fused sm_100a kernels (GPUs)")
         model_path = Path(cfg.model.model_path)
         if not model_path.exists():
             raise FileNotFoundError(f"model.model_path does not exist: {model_path}")
@@ -158,7 +161,8 @@ class Qwen3Adapter:
             self._fused = FusedQwen3(self.model)
             self._engine = FusedRolloutEngine(self.model, self._fused, page_size=flow.kv_page_size,
                                               use_graph=flow.cuda_graph_decode,
-                                              fused_tp_allreduce=flow.decode_tp_allreduce == "fused")
+                                              fused_tp_allreduce=flow.decode_tp_allreduce == "fused",
+                                              comm=self._comm)
         else:
             from graspo_b200.engine.rollout import EagerRolloutEngine
 
@@ -288,6 +292,10 @@ class Qwen3Adapter:
         dev = self.device
         seq = sequences.to(dev)
         mask = attention_mask.to(dev).bool()
+        if self.ps.pp_size > 1:
+            from graspo_b200.engine.pipeline import pp_logprobs
+
+            return pp_logprobs(self._fused, self._comm, seq, mask, seq[:, 1:], chunk_rows=self._pp_chunk_rows(seq))
         outs = []
         for sl in self._token_budget_chunks(seq.shape[0], seq.shape[1]):
             outs.append(self._logprobs(seq[sl], mask[sl], train=False)[0])
@@ -347,9 +355,30 @@ class Qwen3Adapter:
         if ps.tp_size > 1 and ps.distributed and rep:
             dist.all_reduce(self.model.lora.grads[:rep], group=ps.tp_group)
 
+    def _pp_chunk_rows(self, seq) -> int:
+        """Rows per pipeline micro-batch (graspoflow.pp_micro_batch_size, bounded by a token budget)."""
+        rows = max(1, int(self.config.graspoflow.pp_micro_batch_size))
+        return max(1, min(rows, 65536 // max(1, seq.shape[1])))
+
     def _backward_grpo(self, seq, mask, old, adv, act, clip_eps: float, seed: int):
         """Forward + GRPO loss + backward into the flat grad buffer; returns loss (device)."""
         B, S = seq.shape
+        if self.ps.pp_size > 1:
+            from graspo_b200.engine.pipeline import pp_train
+            from graspo_b200.ops._ext import ext
+
+            old_c, adv_c, act_c = old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous()
+
+            def loss_fn(logp_c, sl):
+                rows = sl.stop - sl.start
+                loss = torch.zeros(1, device=seq.device, dtype=torch.float32)
+                dlogp = torch.empty_like(logp_c)
+                ext().grpo_loss(logp_c.contiguous(), old_c[sl], adv_c[sl], act_c[sl], clip_eps, rows / B, loss,
+                                dlogp, None)
+                return loss * (rows / B), dlogp
+
+            return pp_train(self._fused, self._comm, seq, mask, seq[:, 1:], loss_fn, seed=seed,
+                            chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule)
         if self.fused:
             from graspo_b200.ops._ext import ext
 
@@ -461,6 +490,15 @@ class Qwen3Adapter:
         valid = tgt.ne(-100)
         denom = valid.sum().clamp_min(1)
         safe = torch.where(valid, tgt, torch.zeros_like(tgt))
+        if self.ps.pp_size > 1:
+            from graspo_b200.engine.pipeline import pp_train
+
+            def loss_fn(logp_c, sl):
+                v = valid[sl].float()
+                return -(logp_c * v).sum().reshape(1) / denom, -(v / denom)
+
+            return pp_train(self._fused, self._comm, ids, mask, safe, loss_fn, seed=step,
+                            chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule)
         if self.fused:
             logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe)
             loss = -(logp * valid).sum() / denom

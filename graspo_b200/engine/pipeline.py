@@ -1,0 +1,125 @@
+"""Pipeline-parallel forward / backward of the fused decoder.
+
+A batch of rows is cut into micro-batches of ``chunk_rows`` rows.  Stage 0
+embeds, every stage runs its local layers, the last stage normalises and
+computes the selected-token log-probs (and the loss); hidden states travel
+forward and their gradients backward between neighbouring stages over
+``StageComm`` (NCCL p2p on GPUs).
+
+* ``pp_logprobs``: forward only (old log-probs), GPipe order; the last stage
+  broadcasts the log-probs to its pipeline column so every rank returns them
+  (reference: backends/graspoflow/models/qwen35_36/logprobs.py:65-121).
+* ``pp_train``: one optimizer step's forward + backward under the configured
+  schedule (``one_f_one_b`` by default: warm-up forwards, then alternating
+  forward / backward, then the drain -- parallel/schedule.py).  The loss of a
+  micro-batch is weighted by its share of the rows, so the accumulated
+  gradient equals the unchunked one (reference: training.py:727-1043).
+  Backward recomputes each stage's layers from their saved inputs.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+from graspo_b200.models.fused import AttnMeta, FusedQwen3
+from graspo_b200.ops._ext import ext
+from graspo_b200.parallel.p2p import StageComm
+from graspo_b200.parallel.schedule import PipelineAction, get_scheduler
+
+# the fused layers produce bf16 activations (the GEMMs store bf16)
+ACT_DTYPE = torch.bfloat16
+
+
+def _chunks(B: int, rows: int) -> list[slice]:
+    rows = max(1, int(rows))
+    return [slice(i, min(B, i + rows)) for i in range(0, B, rows)]
+
+
+def _full_targets(tgt: torch.Tensor) -> torch.Tensor:
+    B, S1 = tgt.shape
+    full = torch.zeros(B, S1 + 1, dtype=torch.long, device=tgt.device)
+    full[:, :-1] = tgt
+    return full
+
+
+def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor,
+                targets: torch.Tensor, *, chunk_rows: int) -> torch.Tensor:
+    """log p(targets) [B, S-1] on every stage of the column (forward only)."""
+    m, ps = f.m, comm.ps
+    B, S = seq.shape
+    H = m.cfg.hidden_size
+    full = _full_targets(targets)
+    outs = []
+    for sl in _chunks(B, chunk_rows):
+        rows = sl.stop - sl.start
+        meta = AttnMeta.from_mask(mask[sl])
+        x = f.embed(seq[sl]) if ps.is_first_stage else comm.recv_prev((rows * S, H), ACT_DTYPE)
+        xL, _ = f.stage_forward(x, meta)
+        if ps.is_last_stage:
+            hn, _ = f.final_norm(xL)
+            lp, _ = f.token_logprobs(hn, full[sl].reshape(-1))
+            outs.append(lp.view(rows, S)[:, :-1])
+        else:
+            comm.send_next(xL)
+    comm.flush()
+    logp = torch.cat(outs, 0).contiguous() if ps.is_last_stage else torch.empty(B, S - 1, device=seq.device)
+    return comm.broadcast_from_last(logp)
+
+
+LossFn = Callable[[torch.Tensor, slice], tuple[torch.Tensor, torch.Tensor]]
+
+
+def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
+             loss_fn: LossFn, *, seed: int, chunk_rows: int, schedule: str = "one_f_one_b") -> torch.Tensor:
+    """Forward + backward of one optimizer step into the LoRA gradient buffer.
+
+    ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
+    returns (loss contribution [1], d loss / d logp_chunk); contributions must
+    already carry the chunk's weight.  Returns the summed loss on every stage.
+    """
+    m, ps = f.m, comm.ps
+    C = ext()
+    B, S = seq.shape
+    H = m.cfg.hidden_size
+    full = _full_targets(targets)
+    chunks = _chunks(B, chunk_rows)
+    plan = get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank).plan(len(chunks))
+    saved: dict[int, tuple] = {}
+    total = torch.zeros(1, device=seq.device, dtype=torch.float32)
+    for step in plan:
+        c = step.microbatch_idx
+        sl = chunks[c]
+        rows = sl.stop - sl.start
+        if step.action == PipelineAction.FORWARD:
+            meta = AttnMeta.from_mask(mask[sl])
+            x = f.embed(seq[sl]) if ps.is_first_stage else comm.recv_prev((rows * S, H), ACT_DTYPE)
+            xL, inputs = f.stage_forward(x, meta, train=True, seed=seed, keep_inputs=True)
+            if ps.is_last_stage:
+                hn, rstd = f.final_norm(xL)
+                fc = full[sl].reshape(-1).contiguous()
+                lp, lse = f.token_logprobs(hn, fc)
+                loss_c, dlogp = loss_fn(lp.view(rows, S)[:, :-1], sl)
+                total += loss_c.reshape(1)
+                saved[c] = (meta, inputs, xL, hn, rstd, fc, lse, dlogp)
+            else:
+                comm.send_next(xL)
+                saved[c] = (meta, inputs)
+        else:
+            if ps.is_last_stage:
+                meta, inputs, xL, hn, rstd, fc, lse, dlogp = saved.pop(c)
+                g = torch.zeros(rows, S, device=seq.device, dtype=torch.float32)
+                g[:, :-1] = dlogp
+                dhn = f.token_logprobs_backward(hn, fc, lse, g.view(-1))
+                dx = torch.empty_like(xL)
+                C.rmsnorm_bwd(dhn, xL, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
+                del dhn, hn, xL
+            else:
+                meta, inputs = saved.pop(c)
+                dx = comm.recv_next((rows * S, H), ACT_DTYPE)
+            dx_in = f.stage_backward(inputs, dx, meta, train=True, seed=seed)
+            if not ps.is_first_stage:
+                comm.send_prev(dx_in)
+    comm.flush()
+    return comm.broadcast_from_last(total)

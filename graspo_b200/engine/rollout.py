@@ -87,7 +87,7 @@ def _gen_lengths(tokens: torch.Tensor, eos_id: int, ignore_eos: bool) -> list[in
 
 class FusedRolloutEngine:
     def __init__(self, model: Qwen3Model, fused, *, page_size: int = 64, use_graph: bool = True,
-                 graph_chunk: int = 16, fused_tp_allreduce: bool = True) -> None:
+                 graph_chunk: int = 16, fused_tp_allreduce: bool = True, comm=None) -> None:
         from graspo_b200.ops._ext import ext
 
         self.m = model
@@ -103,6 +103,10 @@ class FusedRolloutEngine:
         # kernels (peer-memory tile push) instead of NCCL calls
         self.fused_tp = bool(fused_tp_allreduce) and model.ps.tp_size > 1 and model.device.type == "cuda"
         self._peer_sites: dict[tuple, object] = {}
+        # pipeline parallelism: each stage runs its local layers on every step;
+        # hidden states go forward by p2p, the last stage samples and broadcasts
+        # the tokens to its column (no CUDA graph across the p2p boundary)
+        self.comm = comm if (comm is not None and comm.active) else None
 
     def _ensure_pool(self, num_pages: int) -> None:
         m = self.m
@@ -197,13 +201,14 @@ class FusedRolloutEngine:
             kp[li, : n * prompt_pages] = k.view(shape).permute(0, 1, 3, 2, 4).reshape(-1, m.nkv, self.page, m.D)
             vp[li, : n * prompt_pages] = v.view(shape).permute(0, 1, 3, 2, 4).reshape(-1, m.nkv, self.page, m.D)
 
-        x = f.embed(ids_d)
+        comm, ps = self.comm, m.ps
+        H = m.cfg.hidden_size
+        x = f.embed(ids_d) if m.include_embed else comm.recv_prev((n * P, H), torch.bfloat16)
         for lw in m.layers:
             x, _ = f.layer_forward(lw, x, meta, kv_sink=sink)
-        last = x.view(n, P, -1)[:, -1].contiguous()
-        xn, _ = f.final_norm(last)
-        logits0 = self._lm_logits(xn)
-        logits_rows = logits0.repeat_interleave(G, dim=0).contiguous()
+        if not m.include_head:
+            comm.send_next(x)
+            comm.flush()
 
         # ---------------- decode state
         st = {
@@ -215,9 +220,16 @@ class FusedRolloutEngine:
             "out": torch.full((rows, max_new_tokens), pad_id, dtype=torch.long, device=dev),
             "start": torch.tensor([P - lens[r // G] for r in range(rows)], dtype=torch.int32, device=dev),
         }
-        C.sample_append(logits_rows, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"],
-                        st["pos"], st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)
-        del logits0, logits_rows, x, last
+        if m.include_head:
+            last = x.view(n, P, -1)[:, -1].contiguous()
+            xn, _ = f.final_norm(last)
+            logits_rows = self._lm_logits(xn).repeat_interleave(G, dim=0).contiguous()
+            C.sample_append(logits_rows, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"],
+                            st["pos"], st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos),
+                            None)
+            del logits_rows, last
+        self._sync_stages(st)
+        del x
         _sync(dev)
         t1 = time.perf_counter()
 
@@ -250,7 +262,7 @@ class FusedRolloutEngine:
 
         done = 0
         if steps > 0:
-            if self.use_graph and dev.type == "cuda":
+            if self.use_graph and dev.type == "cuda" and comm is None:
                 saved = {k: v.clone() for k, v in st.items()}
                 step()  # warm-up outside capture (sets kernel attributes, allocator pools)
                 for k, v in saved.items():
@@ -284,6 +296,8 @@ class FusedRolloutEngine:
                     done += 1
                     if not ignore_eos and done % self.graph_chunk == 0 and bool(st["finished"].all()):
                         break
+        if comm is not None:
+            comm.broadcast_from_last(st["out"])
         _sync(dev)
         t2 = time.perf_counter()
         check_errors(dev)
@@ -292,6 +306,19 @@ class FusedRolloutEngine:
             prompt_ids=ids, prompt_lens=lens, tokens=tokens, gen_lens=_gen_lengths(tokens, eos_id, ignore_eos),
             group_size=G, prefill_sec=t1 - t0, decode_sec=t2 - t1, decode_steps=done + 1,
         )
+
+    def _sync_stages(self, st) -> None:
+        """Pipeline: the last stage's sampled tokens (and finished flags) reach
+        every stage; the other stages advance their cache bookkeeping the way
+        the sampler does (slot, position and key count grow by one)."""
+        if self.comm is None:
+            return
+        self.comm.broadcast_from_last(st["next_ids"])
+        self.comm.broadcast_from_last(st["finished"])
+        if not self.m.include_head:
+            st["slot"] += 1
+            st["pos"] += 1
+            st["kv_len"].copy_(st["slot"] + 1)
 
     def _lora_tails(self) -> dict[str, int]:
         """Spare weight rows per projection: the width of its scaled LoRA A layout."""
@@ -349,7 +376,9 @@ class FusedRolloutEngine:
             "u_gu": torch.zeros(rows, max(tails.get("u_gu", 0), 1), device=dev, dtype=dt),
             "act": torch.empty(rows, m.inter_local, device=dev, dtype=dt),
             "d_ws": torch.zeros(rows, H + tails.get("w_down", 0), device=dev, dtype=f32),
-            "logits": torch.empty(rows, m.vocab_local, device=dev, dtype=f32),
+            "logits": (torch.empty(rows, m.vocab_local, device=dev, dtype=f32) if m.include_head
+                       else torch.empty(0, device=dev)),
+            "ones": torch.ones(H, device=dev, dtype=dt),
         }
 
     def _decode_step(self, st, b, bt, row_ids, P, temperature, top_p, seed, eos_id, pad_id, ignore_eos) -> None:
@@ -374,7 +403,10 @@ class FusedRolloutEngine:
         so, sd = self._sites.get("o"), self._sites.get("d")
         o_norm = so.norm_kwargs() if so is not None else {}
         d_norm = sd.norm_kwargs() if sd is not None else {}
-        C.embedding(st["next_ids"], m.embed, b["x_a"])
+        if m.include_embed:
+            C.embedding(st["next_ids"], m.embed, b["x_a"])
+        else:
+            self.comm.recv_prev(b["x_a"].shape, b["x_a"].dtype, out=b["x_a"])
         scale = 1.0 / math.sqrt(m.D)
         b_down_prev = None
         for li, lw in enumerate(m.layers):
@@ -411,11 +443,26 @@ class FusedRolloutEngine:
             if tp > 1 and sd is None:
                 dist.all_reduce(b["d_ws"], group=tp_group)
             b_down_prev = L.get("b_down")
-        C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps,
-                      b_down_prev, r if b_down_prev is not None else 0, **d_norm)
+        ran = len(m.layers) > 0  # a stage may hold only the LM head
+        if not m.include_head:
+            # stage boundary: materialise the residual stream (x_b + down output)
+            # in x_a and hand it to the next stage (the norm output is unused)
+            if ran:
+                C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], b["ones"], b["xn"], None, None, None, 1.0, eps,
+                              b_down_prev, r if b_down_prev is not None else 0, **d_norm)
+            self.comm.send_next(b["x_a"])
+            self.comm.flush()
+            self._sync_stages(st)
+            return
+        if ran:
+            C.add_rmsnorm(b["x_b"], b["d_ws"], b["x_a"], m.norm, b["xn"], None, None, None, 1.0, eps,
+                          b_down_prev, r if b_down_prev is not None else 0, **d_norm)
+        else:
+            C.add_rmsnorm(b["x_a"], None, None, m.norm, b["xn"], None, None, None, 1.0, eps)
         logits = self._lm_logits(b["xn"], b["logits"])
         C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"], st["pos"],
                         st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)
+        self._sync_stages(st)
 
 
 # ======================================================================= eager

@@ -302,7 +302,10 @@ def test_paged_decode_attention_shared_prefix(G, R):
         bt[r, prompt_pages:] = torch.arange(base, base + gen_pages)
     bt = bt.cuda()
     start = torch.tensor([7] * R + [0] * R, device="cuda", dtype=torch.int32)
-    lens = torch.tensor([P + 1 + 37 * r for r in range(rows)], device="cuda", dtype=torch.int32)
+    # every row's keys fit its block table (prompt pages + gen_pages)
+    lens = torch.tensor([P + 1 + (gen_pages * page - 1) * r // (rows - 1) for r in range(rows)], device="cuda",
+                        dtype=torch.int32)
+    assert int(lens.max()) <= bt.shape[1] * page
     q = _rand(rows, nq, D)
     scale = 1 / math.sqrt(D)
     splits = 2
