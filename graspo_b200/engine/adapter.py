@@ -157,9 +157,12 @@ class Qwen3Adapter:
             from graspo_b200.engine.rollout import FusedRolloutEngine
             from graspo_b200.models.fused import FusedQwen3
 
-            self.model.ensure_transposed()
-            self._fused = FusedQwen3(self.model)
-            self._engine = FusedRolloutEngine(self.model, self._fused, page_size=flow.kv_page_size,
+            if flow.sequence_parallel and self.ps.pp_size > 1:
+                raise NotImplementedError("sequence parallelism together with pipeline stages is not supported")
+            # training / log-prob passes (optionally sequence-parallel); the rollout
+            # engine keeps whole-sequence prefill
+            self._fused = FusedQwen3(self.model, sequence_parallel=flow.sequence_parallel)
+            self._engine = FusedRolloutEngine(self.model, FusedQwen3(self.model), page_size=flow.kv_page_size,
                                               use_graph=flow.cuda_graph_decode,
                                               fused_tp_allreduce=flow.decode_tp_allreduce == "fused",
                                               comm=self._comm)
@@ -312,15 +315,26 @@ class Qwen3Adapter:
             from graspo_b200.models.fused import AttnMeta
 
             f = self._fused
+            S_in = S
+            if f.sp and (B * S) % self.ps.tp_size:
+                # sequence parallelism splits the B*S tokens evenly over the TP ranks:
+                # pad the sequence dimension with masked pad tokens
+                while (B * S) % self.ps.tp_size:
+                    S += 1
+                pad = S - S_in
+                seq = torch.cat([seq, seq.new_zeros(B, pad)], 1)
+                mask = torch.cat([mask, mask.new_zeros(B, pad)], 1)
+                tgt = torch.cat([tgt, tgt.new_zeros(B, pad)], 1)
             meta = AttnMeta.from_mask(mask)
-            xL, inputs = f.stage_forward(f.embed(seq), meta, train=train, seed=seed, keep_inputs=train)
+            xL, inputs = f.stage_forward(f.sp_shard(f.embed(seq)), meta, train=train, seed=seed, keep_inputs=train)
             hn, rstd = f.final_norm(xL)
+            hn_all = f.sp_gather(hn)
             full = torch.zeros_like(seq)
             full[:, :-1] = tgt
             full = full.reshape(-1)
-            logp_full, lse = f.token_logprobs(hn, full)
-            logp = logp_full.view(B, S)[:, :-1].contiguous()
-            return logp, ((meta, inputs, xL, hn, rstd, full, lse) if train else None)
+            logp_full, lse = f.token_logprobs(hn_all, full)
+            logp = logp_full.view(B, S)[:, : S_in - 1].contiguous()
+            return logp, ((meta, inputs, xL, hn_all, rstd, full, lse) if train else None)
         lora = EagerLoRA(self.model.lora, requires_grad=train)
         with torch.set_grad_enabled(train):
             hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train)
@@ -334,7 +348,7 @@ class Qwen3Adapter:
         meta, inputs, xL, hn, rstd, full_targets, lse = ctx
         B, S = meta.B, meta.S
         g = torch.zeros(B, S, device=dlogp.device, dtype=torch.float32)
-        g[:, :-1] = dlogp
+        g[:, : dlogp.shape[1]] = dlogp
         dhn = self._fused.token_logprobs_backward(hn, full_targets, lse, g.view(-1))
         dxL = torch.empty_like(xL)
         ext().rmsnorm_bwd(dhn, xL, self.model.norm, rstd, None, dxL, self.model.cfg.rms_norm_eps)

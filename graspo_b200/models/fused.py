@@ -45,6 +45,22 @@ def _tp_all_reduce(x: torch.Tensor, group) -> torch.Tensor:
     return x
 
 
+def _sp_gather(x: torch.Tensor, group) -> torch.Tensor:
+    """All-gather token shards [T/tp, ...] -> [T, ...] (sequence parallel)."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world * x.shape[0], *x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+    return out
+
+
+def _sp_scatter(x: torch.Tensor, group) -> torch.Tensor:
+    """Reduce-scatter partial sums [T, ...] -> this rank's token shard [T/tp, ...]."""
+    world = dist.get_world_size(group)
+    out = torch.empty((x.shape[0] // world, *x.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.reduce_scatter_tensor(out, x.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    return out
+
+
 def _grad_splits(rows: int, sms: int = 148) -> int:
     """Split-K factor for a token-contracted LoRA gradient with ``rows`` output rows."""
     tiles = max(1, -(-rows // 128))
@@ -73,11 +89,33 @@ class LayerSaved:
 
 
 class FusedQwen3:
-    def __init__(self, model: Qwen3Model) -> None:
+    """Kernel-path forward / backward of the Qwen3 decoder.
+
+    With ``sequence_parallel`` (and TP > 1) the residual stream, the norms and
+    the residual adds hold 1/tp of the tokens on each TP rank: the input of a
+    column-parallel projection is all-gathered over the tokens, the output of a
+    row-parallel projection is reduce-scattered (instead of all-reduced), and
+    the backward pass mirrors both (Megatron sequence parallelism).
+    """
+
+    def __init__(self, model: Qwen3Model, sequence_parallel: bool = False) -> None:
         self.m = model
         self.C = ext()
         self.eps = model.cfg.rms_norm_eps
         self.scale = 1.0 / math.sqrt(model.D)
+        self.sp = bool(sequence_parallel) and model.ps.tp_size > 1
+
+    # ------------------------------------------------------------ sequence parallel
+    def sp_shard(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's token shard of a replicated [T, ...] tensor (identity without SP)."""
+        if not self.sp:
+            return x
+        tp, r = self.m.ps.tp_size, self.m.ps.tp_rank
+        n = x.shape[0] // tp
+        return x[r * n : (r + 1) * n].contiguous()
+
+    def sp_gather(self, x: torch.Tensor) -> torch.Tensor:
+        return _sp_gather(x, self.m.ps.tp_group) if self.sp else x
 
     # ------------------------------------------------------------ helpers
     def _dropout(self, x, site: str, layer: int, seed: int, train: bool):
@@ -101,19 +139,22 @@ class FusedQwen3:
         m, C, L = self.m, self.C, self._layouts(lw)
         tp_group = m.ps.tp_group
         tp = m.ps.tp_size
-        T, H = x.shape
+        sp = self.sp
         s = LayerSaved() if save else None
         xn = torch.empty_like(x)
-        rstd1 = torch.empty(T, device=x.device, dtype=torch.float32)
+        rstd1 = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
         C.add_rmsnorm(x, None, None, lw.ln1, xn, rstd1, None, None, 1.0, self.eps)
+        if sp:
+            xn = _sp_gather(xn, tp_group)
+        T = xn.shape[0]
         ext_qkv = None
         if "a_qkv" in L:
             xd = self._dropout(xn, "qkv", lw.index, seed, train)
             u_qkv = gemm(xd, L["a_qkv"], bn=64)
             ext_qkv = (u_qkv, L["b_qkv"])
         qkv = gemm(xn, lw.w_qkv, ext_ab=ext_qkv)
-        q = torch.empty(T, m.nq, m.D, device=x.device, dtype=x.dtype)
-        k = torch.empty(T, m.nkv, m.D, device=x.device, dtype=x.dtype)
+        q = torch.empty(T, m.nq, m.D, device=x.device, dtype=xn.dtype)
+        k = torch.empty(T, m.nkv, m.D, device=x.device, dtype=xn.dtype)
         v = torch.empty_like(k)
         C.qk_norm_rope(qkv, lw.q_norm, lw.k_norm, m.inv_freq, meta.pos, q, k, v, None, None, None, m.nq, m.nkv, 0,
                        self.eps)
@@ -127,20 +168,22 @@ class FusedQwen3:
             ext_o = (u_o, L["b_o"])
         x1 = torch.empty_like(x)
         xn2 = torch.empty_like(x)
-        rstd2 = torch.empty(T, device=x.device, dtype=torch.float32)
+        rstd2 = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
         if tp == 1:
             gemm(attn, lw.w_o, x1, ext_ab=ext_o, residual=x)
             C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
         else:
             o = gemm(attn, lw.w_o, ext_ab=ext_o)
-            _tp_all_reduce(o, tp_group)
+            o = _sp_scatter(o, tp_group) if sp else _tp_all_reduce(o, tp_group)
             C.add_rmsnorm(x, o, x1, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
+        if sp:
+            xn2 = _sp_gather(xn2, tp_group)
         ext_gu = None
         if "a_gu" in L:
             xd2 = self._dropout(xn2, "gu", lw.index, seed, train)
             u_gu = gemm(xd2, L["a_gu"], bn=64)
             ext_gu = (u_gu, L["b_gu"])
-        gu = torch.empty(T, 2 * m.inter_local, device=x.device, dtype=x.dtype) if save else None
+        gu = torch.empty(T, 2 * m.inter_local, device=x.device, dtype=xn2.dtype) if save else None
         act = gemm(xn2, lw.w_gu, ext_ab=ext_gu, epilogue="swiglu", aux=gu)
         ext_d = None
         if "a_down" in L:
@@ -151,7 +194,7 @@ class FusedQwen3:
             x2 = gemm(act, lw.w_down, ext_ab=ext_d, residual=x1)
         else:
             d = gemm(act, lw.w_down, ext_ab=ext_d)
-            _tp_all_reduce(d, tp_group)
+            d = _sp_scatter(d, tp_group) if sp else _tp_all_reduce(d, tp_group)
             x2 = (x1.float() + d.float()).to(x.dtype)
         if save:
             s.x, s.xn, s.rstd1, s.qkv, s.q, s.k, s.v, s.attn = x, xn, rstd1, qkv, q, k, v, attn
@@ -224,8 +267,10 @@ class FusedQwen3:
         m, C, L = self.m, self.C, self._layouts(lw)
         tp_group = m.ps.tp_group
         li = lw.index
-        # --- down projection
-        dact, db, da = self._lora_linear_backward(dx2, lw.w_down, s.u_d, s.act_d, L.get("b_down"),
+        sp = self.sp
+        # --- down projection (SP: its output gradient is gathered over the tokens)
+        dy2 = _sp_gather(dx2, tp_group) if sp else dx2
+        dact, db, da = self._lora_linear_backward(dy2, lw.w_down, s.u_d, s.act_d, L.get("b_down"),
                                                   L.get("a_down"), "down", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "down", db, da)
@@ -238,12 +283,13 @@ class FusedQwen3:
                                                   "gu", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "gu", db, da)
-        del dgu
-        _tp_all_reduce(dxn2, tp_group)
+        del dgu, dy2
+        dxn2 = _sp_scatter(dxn2, tp_group) if sp else _tp_all_reduce(dxn2, tp_group)
         dx1 = torch.empty_like(dx2)
         C.rmsnorm_bwd(dxn2, s.x1, lw.ln2, s.rstd2, dx2, dx1, self.eps)
         # --- o projection
-        dattn, db, da = self._lora_linear_backward(dx1, lw.w_o, s.u_o, s.attn_d, L.get("b_o"), L.get("a_o"),
+        dy1 = _sp_gather(dx1, tp_group) if sp else dx1
+        dattn, db, da = self._lora_linear_backward(dy1, lw.w_o, s.u_o, s.attn_d, L.get("b_o"), L.get("a_o"),
                                                    "o", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "o", db, da)
@@ -257,7 +303,7 @@ class FusedQwen3:
                                                  "qkv", li, seed, train)
         if db is not None:
             self._scatter_grads(li, "qkv", db, da)
-        _tp_all_reduce(dxn, tp_group)
+        dxn = _sp_scatter(dxn, tp_group) if sp else _tp_all_reduce(dxn, tp_group)
         dx = torch.empty_like(dx2)
         C.rmsnorm_bwd(dxn, s.x, lw.ln1, s.rstd1, dx1, dx, self.eps)
         return dx
@@ -310,8 +356,9 @@ class FusedQwen3:
         group = m.ps.tp_group
         if m.ps.tp_size > 1:
             # merge vocab shards: lse = log sum_r exp(lse_r); target logit lives on one shard
-            lses = torch.empty(m.ps.tp_size, T, device=h.device, dtype=torch.float32)
-            dist.all_gather_into_tensor(lses, lse, group=group)
+            lses = torch.empty(m.ps.tp_size * T, device=h.device, dtype=torch.float32)
+            dist.all_gather_into_tensor(lses, lse.contiguous(), group=group)
+            lses = lses.view(m.ps.tp_size, T)
             _tp_all_reduce(tl, group)
             lse = torch.logsumexp(lses, 0)
             logp = tl - lse
@@ -319,7 +366,10 @@ class FusedQwen3:
 
     def token_logprobs_backward(self, h: torch.Tensor, targets: torch.Tensor, lse: torch.Tensor,
                                 g: torch.Tensor, chunk_tokens: int = 32768) -> torch.Tensor:
-        """d(normed hidden) for upstream grads g [T] of the selected log-probs."""
+        """d(normed hidden) for upstream grads g [T] of the selected log-probs.
+
+        ``h`` holds every token; with SP the result is this rank's token shard
+        (reduce-scattered instead of all-reduced over the vocabulary shards)."""
         m = self.m
         T, H = h.shape
         dh = torch.empty_like(h)
@@ -330,5 +380,7 @@ class FusedQwen3:
                         row_lse=lse[t0:t1].contiguous(), row_scale=g[t0:t1].contiguous())
             gemm(dlog, m.lm_head, dh[t0:t1], b_mn=True)
             del dlog
+        if self.sp:
+            return _sp_scatter(dh, m.ps.tp_group)
         _tp_all_reduce(dh, m.ps.tp_group)
         return dh
