@@ -31,6 +31,8 @@ void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torc
                       torch::Tensor dqkv, int64_t nq, int64_t nkv, double eps);
 void swiglu_bwd(torch::Tensor gu, torch::Tensor dh, torch::Tensor dgu);
 void lora_down(torch::Tensor x, torch::Tensor A, torch::Tensor U, double scale);
+void gated_delta_step(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                      torch::Tensor state, torch::Tensor out);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale);
@@ -84,6 +86,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_bwd", &gb::qk_norm_rope_bwd);
   m.def("swiglu_bwd", &gb::swiglu_bwd);
   m.def("lora_down", &gb::lora_down);
+  m.def("gated_delta_step", &gb::gated_delta_step, "one decoding step of the gated delta rule");
   m.def("embedding", &gb::embedding);
   m.def("paged_decode_attention", &gb::paged_decode_attention, py::arg("q"), py::arg("k_pool"), py::arg("v_pool"),
         py::arg("block_table"), py::arg("start"), py::arg("len"), py::arg("out"), py::arg("scale"),

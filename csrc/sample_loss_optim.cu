@@ -462,3 +462,75 @@ void adamw(torch::Tensor p, torch::Tensor g, torch::Tensor m, torch::Tensor v, d
 }
 
 }  // namespace gb
+
+// ---------------------------------------------------------------------------
+// One decoding step of the gated delta rule (Gated DeltaNet, Yang et al. 2024)
+// for every (row, head):
+//   S <- exp(g) S;  u = beta (v - S^T k);  S <- S + k u^T;  o = S^T q
+// S [dk, dv] fp32 is read twice (the second pass mostly from cache) and
+// written once.  One CTA per (row, head); thread j owns column j of S, so
+// S^T k and S^T q are thread-local dot products and the rank-1 update needs
+// no communication; a warp touches 32 consecutive columns (coalesced).
+namespace gb {
+namespace {
+template <int DK>
+__global__ void __launch_bounds__(128) gated_delta_step_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                               const float* __restrict__ v, const float* __restrict__ g,
+                                                               const float* __restrict__ beta, float* __restrict__ state,
+                                                               float* __restrict__ out, int dv) {
+  __shared__ float ks[DK], qs[DK];
+  const long bh = blockIdx.x;
+  for (int i = threadIdx.x; i < DK; i += blockDim.x) {
+    ks[i] = k[bh * DK + i];
+    qs[i] = q[bh * DK + i];
+  }
+  __syncthreads();
+  const float decay = __expf(g[bh]);
+  const float b = beta[bh];
+  for (int j = threadIdx.x; j < dv; j += blockDim.x) {
+    float* col = state + bh * DK * dv + j;
+    float mem = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < DK; ++i) mem += col[static_cast<long>(i) * dv] * ks[i];
+    const float u = b * (v[bh * dv + j] - mem * decay);
+    float o = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < DK; ++i) {
+      const float sn = col[static_cast<long>(i) * dv] * decay + ks[i] * u;
+      col[static_cast<long>(i) * dv] = sn;
+      o += sn * qs[i];
+    }
+    out[bh * dv + j] = o;
+  }
+}
+}  // namespace
+
+void gated_delta_step(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                      torch::Tensor state, torch::Tensor out) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(state.scalar_type() == torch::kFloat32 && state.is_contiguous() && state.dim() == 4,
+              "state must be contiguous fp32 [B, h, dk, dv]");
+  const int dk = static_cast<int>(state.size(2)), dv = static_cast<int>(state.size(3));
+  const long bh = state.size(0) * state.size(1);
+  for (auto* t : {&q, &k, &v, &g, &beta, &out})
+    TORCH_CHECK(t->scalar_type() == torch::kFloat32 && t->is_contiguous(), "fp32 contiguous operands");
+  TORCH_CHECK(q.numel() == bh * dk && k.numel() == bh * dk && v.numel() == bh * dv && g.numel() == bh &&
+                  beta.numel() == bh && out.numel() == bh * dv,
+              "shape mismatch");
+  if (bh == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+#define GB_GDS(DKV)                                                                                        \
+  gated_delta_step_kernel<DKV><<<bh, 128, 0, stream>>>(q.data_ptr<float>(), k.data_ptr<float>(),           \
+                                                       v.data_ptr<float>(), g.data_ptr<float>(),           \
+                                                       beta.data_ptr<float>(), state.data_ptr<float>(),    \
+                                                       out.data_ptr<float>(), dv)
+  switch (dk) {
+    case 64: GB_GDS(64); break;
+    case 128: GB_GDS(128); break;
+    case 256: GB_GDS(256); break;
+    default: TORCH_CHECK(false, "gated_delta_step supports key head dims 64, 128, 256");
+  }
+#undef GB_GDS
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+}  // namespace gb

@@ -150,16 +150,18 @@ def bench_step(args) -> None:
     model = _step_model(args)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 150000, (args.prompt_len,), generator=g).tolist() for _ in range(args.prompts)]
-    for graph in (True, False):
+    for graph, prefix in ((True, True), (True, False), (False, True)):
         eng = FusedRolloutEngine(model, FusedQwen3(model), page_size=64, use_graph=graph)
         eng.nvtx = not graph
+        eng.prefix_attention = prefix
         kw = dict(group_size=args.group, max_new_tokens=args.new, temperature=1.0, top_p=1.0, eos_id=0, pad_id=0,
                   ignore_eos=True, seed=1)
         eng.generate(prompts, **kw)  # warm-up (pools, kernel attributes)
         res = eng.generate(prompts, **kw)
         ms = res.decode_sec * 1e3 / max(1, res.decode_steps - 1)
         print(json.dumps({
-            "kernel": "decode_step", "graph": graph, "layers": args.layers, "rows": args.prompts * args.group,
+            "kernel": "decode_step", "graph": graph, "prefix_attention": prefix, "layers": args.layers,
+            "rows": args.prompts * args.group,
             "prompt_len": args.prompt_len, "new_tokens": args.new, "ms_per_step": round(ms, 3),
             "ms_per_layer": round(ms / args.layers, 4), "prefill_s": round(res.prefill_sec, 3),
         }), flush=True)

@@ -107,6 +107,9 @@ class FusedRolloutEngine:
         # hidden states go forward by p2p, the last stage samples and broadcasts
         # the tokens to its column (no CUDA graph across the p2p boundary)
         self.comm = comm if (comm is not None and comm.active) else None
+        # attend the prompt keys once per group (shared-prefix kernel); False
+        # runs every row over its whole key range
+        self.prefix_attention = True
 
     def _ensure_pool(self, num_pages: int) -> None:
         m = self.m
@@ -247,8 +250,8 @@ class FusedRolloutEngine:
         # shared-prefix attention: the prompt keys of a group are attended once for
         # all G rows (full tensor-core tiles), the generated keys per row
         heads_per_kv = m.nq // m.nkv
-        self._prefix = (P if dev.type == "cuda" and self.page % 64 == 0 and G > 1 and G * heads_per_kv <= 64
-                        else 0)
+        self._prefix = (P if self.prefix_attention and dev.type == "cuda" and self.page % 64 == 0 and G > 1
+                        and G * heads_per_kv <= 64 else 0)
         self._group = G
         self._prefix_splits = (max(1, min(P // 64, round(2 * 148 / max(1, n * m.nkv)))) if self._prefix else 1)
         self._splits = decode_attention_splits(rows, m.nkv, cap - self._prefix)

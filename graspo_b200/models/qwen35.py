@@ -1,0 +1,445 @@
+"""Qwen3.5 / 3.6 hybrid decoder (``qwen3_5_text``): gated DeltaNet + gated attention.
+
+Layer kinds come from ``layer_types`` (reference:
+backends/graspoflow/models/common/layers.py:31-133):
+
+* ``linear_attention`` -- Gated DeltaNet (Yang, Kautz, Hatamizadeh 2024):
+  ``in_proj_qkv`` -> causal depthwise conv1d (kernel K) + SiLU -> split q, k, v;
+  q, k L2-normalised per head (q also scaled by 1/sqrt(d_k)); per head a
+  decay ``g = -exp(A_log) * softplus(a + dt_bias)`` and a write strength
+  ``beta = sigmoid(b)``; the state S [d_k, d_v] evolves as
+  ``S <- exp(g) S;  S <- S + k (beta (v - S^T k))^T;  o = S^T q``; the output
+  passes a gated RMSNorm with ``z = in_proj_z(x)`` (``w * norm(o) * silu(z)``)
+  and ``out_proj`` (reference layers.py:358-633, tensor_utils.py:509-646).
+* ``full_attention`` -- ``q_proj`` emits (query, gate) per head; QK-norm,
+  partial rotary embedding, GQA attention, output ``o * sigmoid(gate)`` into
+  ``o_proj`` (layers.py:145-355).
+
+RMSNorms use the ``(1 + w)`` parametrisation (layers.py:636-651); the MLP is
+SwiGLU.  The whole-sequence DeltaNet uses the chunked form (chunk 64): the
+in-chunk triangular system is solved with one batched ``solve_triangular``
+(not a loop over rows), the chunks are chained by the recurrent state.  The
+one-token decode step of the recurrence runs in the ``gated_delta_step``
+kernel on GPUs.  LoRA is applied on the reference's targets
+(``language.full_attn.*``, ``language.linear_attn.{q,k,v}_proj`` (row blocks of
+``in_proj_qkv``), ``in_proj_z``, ``out_proj``, ``language.mlp.*``).  This family
+runs with TP = 1 (one process per pipeline / data replica).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from graspo_b200.core.lora_targets import lora_target_enabled
+from graspo_b200.models.config import DecoderConfig
+from graspo_b200.models.loader import SafetensorIndex
+from graspo_b200.models.lora import LoRAAdapter, LoRAModule
+from graspo_b200.models.qwen3 import EagerLoRA
+from graspo_b200.parallel.state import ParallelState
+
+CHUNK = 64
+
+
+def norm1p(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm with the (1 + w) weight, fp32 statistics."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (y * (1.0 + w.float())).to(x.dtype)
+
+
+def gated_norm(x: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+    return (w * y * F.silu(z.float())).to(x.dtype)
+
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    return x / x.norm(dim=-1, keepdim=True).clamp_min(eps)
+
+
+def chunk_gated_delta(q, k, v, g, beta, state=None):
+    """Whole-sequence gated delta rule. q, k [B, S, h, dk]; v [B, S, h, dv];
+    g, beta [B, S, h] (g = log decay).  q, k must be L2-normalised and q scaled.
+    Returns (o [B, S, h, dv], final state [B, h, dk, dv]); fp32 math."""
+    B, S, h, dk = k.shape
+    dv = v.shape[-1]
+    pad = (-S) % CHUNK
+    q, k, v, g, beta = (t.float().transpose(1, 2) for t in (q, k, v, g, beta))   # [B, h, S, .]
+    if pad:
+        q, k, v = (F.pad(t, (0, 0, 0, pad)) for t in (q, k, v))
+        g, beta = F.pad(g, (0, pad)), F.pad(beta, (0, pad))
+    n = (S + pad) // CHUNK
+    q, k, v = (t.reshape(B, h, n, CHUNK, t.shape[-1]) for t in (q, k, v))
+    g = g.reshape(B, h, n, CHUNK).cumsum(-1)                                      # within-chunk cumulative log decay
+    beta = beta.reshape(B, h, n, CHUNK)
+    idx = torch.arange(CHUNK, device=q.device)
+    lower = idx[:, None] > idx[None, :]
+    decay = torch.exp((g[..., :, None] - g[..., None, :]).masked_fill(~(idx[:, None] >= idx[None, :]), -math.inf))
+    kb = k * beta[..., None]
+    # W-representation: (I + strictly-lower(beta K K^T . decay)) u = beta v, w likewise for k exp(g)
+    A = (kb @ k.transpose(-1, -2)) * decay
+    A = A.masked_fill(~lower, 0.0) + torch.eye(CHUNK, device=q.device)
+    rhs = torch.cat([v * beta[..., None], kb * g.exp()[..., None]], -1)
+    sol = torch.linalg.solve_triangular(A, rhs, upper=False, unitriangular=True)
+    u, w = sol[..., :dv], sol[..., dv:]
+    S_t = torch.zeros(B, h, dk, dv, device=q.device, dtype=torch.float32) if state is None else state.float()
+    attn = (q @ k.transpose(-1, -2)) * decay                                      # [B, h, n, C, C] (causal)
+    outs = []
+    for c in range(n):
+        u_c = u[:, :, c] - w[:, :, c] @ S_t                                       # new values after the state
+        outs.append((q[:, :, c] * g[:, :, c].exp()[..., None]) @ S_t + attn[:, :, c] @ u_c)
+        last = g[:, :, c, -1]
+        S_t = S_t * last.exp()[..., None, None] + \
+            (k[:, :, c] * (last[..., None] - g[:, :, c]).exp()[..., None]).transpose(-1, -2) @ u_c
+    o = torch.stack(outs, 2).reshape(B, h, n * CHUNK, dv)[:, :, :S]
+    return o.transpose(1, 2), S_t
+
+
+def recurrent_gated_delta(q, k, v, g, beta, state):
+    """One-token step (PyTorch): q, k [B, h, dk]; v [B, h, dv]; g, beta [B, h]; state [B, h, dk, dv] (updated)."""
+    state.mul_(g.float().exp()[..., None, None])
+    mem = (state * k.float()[..., None]).sum(-2)
+    delta = (v.float() - mem) * beta.float()[..., None]
+    state.add_(k.float()[..., None] * delta[..., None, :])
+    return (state * q.float()[..., None]).sum(-2)
+
+
+@dataclass
+class HybridLayer:
+    index: int
+    kind: str
+    ln1: torch.Tensor
+    ln2: torch.Tensor
+    w: dict[str, torch.Tensor] = field(default_factory=dict)
+
+
+_TARGETS = {
+    "fq": ("language.full_attn.q_proj", "self_attn.q_proj"),
+    "fk": ("language.full_attn.k_proj", "self_attn.k_proj"),
+    "fv": ("language.full_attn.v_proj", "self_attn.v_proj"),
+    "fo": ("language.full_attn.o_proj", "self_attn.o_proj"),
+    "lq": ("language.linear_attn.q_proj", "linear_attn.in_proj_qkv"),
+    "lk": ("language.linear_attn.k_proj", "linear_attn.in_proj_qkv"),
+    "lv": ("language.linear_attn.v_proj", "linear_attn.in_proj_qkv"),
+    "lz": ("language.linear_attn.in_proj_z", "linear_attn.in_proj_z"),
+    "lo": ("language.linear_attn.out_proj", "linear_attn.out_proj"),
+    "gate": ("language.mlp.gate_proj", "mlp.gate_proj"),
+    "up": ("language.mlp.up_proj", "mlp.up_proj"),
+    "down": ("language.mlp.down_proj", "mlp.down_proj"),
+}
+
+
+class Qwen35Model:
+    """Weights and LoRA state of the hybrid decoder (TP = 1)."""
+
+    supports_kv_cache = True
+
+    def __init__(self, cfg: DecoderConfig, loader: SafetensorIndex, *, ps: ParallelState,
+                 local_layers: list[int] | None = None, include_embed: bool = True, include_head: bool = True,
+                 lora_targets=frozenset(), lora_r: int = 8, lora_alpha: float = 16, lora_dropout: float = 0.0,
+                 dtype: torch.dtype = torch.bfloat16, device: torch.device = torch.device("cpu"), seed: int = 42,
+                 gradient_checkpointing: bool = True) -> None:
+        if ps.tp_size != 1:
+            raise NotImplementedError("the qwen3_5_text family runs with tp_size=1")
+        t = cfg.extra["text_config"]
+        self.cfg, self.ps, self.dtype, self.device = cfg, ps, dtype, device
+        self.gradient_checkpointing = gradient_checkpointing
+        self.local_layers = list(range(cfg.num_hidden_layers)) if local_layers is None else list(local_layers)
+        self.include_embed, self.include_head = include_embed, include_head
+        self.lora_targets = frozenset(lora_targets)
+        self.nq, self.nkv, self.D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        rp = dict(t.get("rope_parameters") or {})
+        self.rotary_dim = int(self.D * float(rp.get("partial_rotary_factor", t.get("partial_rotary_factor", 1.0))))
+        theta = float(rp.get("rope_theta", t.get("rope_theta", 1e6)))
+        self.inv_freq = (1.0 / theta ** (torch.arange(0, self.rotary_dim, 2, dtype=torch.float32) / self.rotary_dim)
+                         ).to(device)
+        self.lk_heads, self.lv_heads = int(t["linear_num_key_heads"]), int(t["linear_num_value_heads"])
+        self.dk, self.dv = int(t["linear_key_head_dim"]), int(t["linear_value_head_dim"])
+        self.conv_k = int(t["linear_conv_kernel_dim"])
+        self.key_dim, self.value_dim = self.lk_heads * self.dk, self.lv_heads * self.dv
+        pre = cfg.key_prefix
+        dev, dt = device, dtype
+
+        def load(name):
+            return loader.get(name).to(device=dev, dtype=dt)
+
+        self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
+        self.vocab_local, self.vocab_start = cfg.vocab_size, 0
+        self.layers: list[HybridLayer] = []
+        modules: list[LoRAModule] = []
+        for idx in self.local_layers:
+            p = f"{pre}.layers.{idx}"
+            kind = cfg.layer_kind(idx)
+            lay = HybridLayer(idx, kind, load(f"{p}.input_layernorm.weight"), load(f"{p}.post_attention_layernorm.weight"))
+            if kind == "full_attention":
+                for n in ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"):
+                    lay.w[n] = load(f"{p}.self_attn.{n}.weight")
+                sizes = {"fq": (cfg.hidden_size, 2 * self.nq * self.D), "fk": (cfg.hidden_size, self.nkv * self.D),
+                         "fv": (cfg.hidden_size, self.nkv * self.D), "fo": (self.nq * self.D, cfg.hidden_size)}
+            else:
+                for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+                    lay.w[n] = load(f"{p}.linear_attn.{n}.weight")
+                lay.w["conv"] = load(f"{p}.linear_attn.conv1d.weight").reshape(-1, self.conv_k)
+                lay.w["dt_bias"] = loader.get(f"{p}.linear_attn.dt_bias").float().to(dev)
+                lay.w["A_log"] = loader.get(f"{p}.linear_attn.A_log").float().to(dev)
+                lay.w["norm"] = load(f"{p}.linear_attn.norm.weight")
+                H = cfg.hidden_size
+                sizes = {"lq": (H, self.key_dim), "lk": (H, self.key_dim), "lv": (H, self.value_dim),
+                         "lz": (H, self.value_dim), "lo": (self.value_dim, H)}
+            for n in ("gate_proj", "up_proj", "down_proj"):
+                lay.w[n] = load(f"{p}.mlp.{n}.weight")
+            sizes.update({"gate": (cfg.hidden_size, cfg.intermediate_size), "up": (cfg.hidden_size, cfg.intermediate_size),
+                          "down": (cfg.intermediate_size, cfg.hidden_size)})
+            self.layers.append(lay)
+            for k, (fan_in, fan_out) in sizes.items():
+                target, sub = _TARGETS[k]
+                if not lora_target_enabled(self.lora_targets, target):
+                    continue
+                modules.append(LoRAModule(
+                    module_name=f"layers.{idx}.{k}", target_name=target, hf_module_path=f"{p}.{sub}", layer=idx,
+                    kind=k, shard_kind="none", in_full=fan_in, out_full=fan_out, in_local=fan_in, out_local=fan_out,
+                    row_start=0, row_stop=fan_out, col_start=0, col_stop=fan_in))
+        if include_head:
+            self.norm = load(f"{pre}.norm.weight")
+            name = "lm_head.weight" if loader.has("lm_head.weight") else f"{pre}.embed_tokens.weight"
+            self.lm_head = load(name)
+        else:
+            self.norm = self.lm_head = None
+        self.lora = LoRAAdapter(modules, r=lora_r, alpha=lora_alpha, dropout=lora_dropout, device=dev, seed=seed)
+        self._mods = {(m.layer, m.kind): m for m in modules}
+
+    # ---------------------------------------------------------------- api parity
+    def ensure_transposed(self) -> None:
+        return None
+
+    def lora_state_dict(self):
+        return self.lora.state_dict()
+
+    def lora_tensor_metadata(self):
+        return self.lora.metadata()
+
+    def lora_target_signature(self):
+        return self.lora.signature()
+
+    def enabled_lora_target_names(self):
+        return self.lora.target_names()
+
+    def estimate_kv_cache_bytes(self, *, batch_size: int, sequence_len: int) -> int:
+        full = sum(1 for lay in self.layers if lay.kind == "full_attention")
+        lin = len(self.layers) - full
+        kv = batch_size * full * 2 * self.nkv * self.D * sequence_len * self.dtype.itemsize
+        state = batch_size * lin * (self.lv_heads * self.dk * self.dv * 4
+                                    + (2 * self.key_dim + self.value_dim) * self.conv_k * self.dtype.itemsize)
+        return kv + state
+
+    # ---------------------------------------------------------------- pieces
+    def _lin(self, x, w, lay, kind, lora, training):
+        y = F.linear(x, w)
+        mod = self._mods.get((lay.index, kind))
+        if mod is None or lora is None:
+            return y
+        a, b = lora.leaves[mod.module_name]
+        ad = self.lora
+        xin = F.dropout(x, ad.dropout, training) if (training and ad.dropout > 0) else x
+        return y + (F.linear(F.linear(xin.to(a.dtype), a), b) * ad.scaling).to(y.dtype)
+
+    def _rope(self, x, pos):
+        """Partial rotary embedding (rotate-half on the first rotary_dim dims). x [B, S, h, D]; pos [B, S]."""
+        rd = self.rotary_dim
+        f = pos.float()[..., None] * self.inv_freq                     # [B, S, rd/2]
+        cos, sin = torch.cat([f, f], -1).cos()[:, :, None], torch.cat([f, f], -1).sin()[:, :, None]
+        xr, xp = x[..., :rd].float(), x[..., rd:]
+        half = rd // 2
+        rot = torch.cat([-xr[..., half:], xr[..., :half]], -1)
+        return torch.cat([(xr * cos + rot * sin).to(x.dtype), xp], -1)
+
+    def _full_attn(self, lay, h, pos, key_mask, lora, training, cache=None):
+        B, S, _ = h.shape
+        D = self.D
+        qg = self._lin(h, lay.w["q_proj"], lay, "fq", lora, training).view(B, S, self.nq, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(B, S, self.nq * D)
+        k = self._lin(h, lay.w["k_proj"], lay, "fk", lora, training).view(B, S, self.nkv, D)
+        v = self._lin(h, lay.w["v_proj"], lay, "fv", lora, training).view(B, S, self.nkv, D)
+        q = self._rope(norm1p(q, lay.w["q_norm"], self.cfg.rms_norm_eps), pos)
+        k = self._rope(norm1p(k, lay.w["k_norm"], self.cfg.rms_norm_eps), pos)
+        if cache is not None:
+            if "k" in cache:
+                k = torch.cat([cache["k"], k], 1)
+                v = torch.cat([cache["v"], v], 1)
+            cache["k"], cache["v"] = k, v
+        Sk = k.shape[1]
+        G = self.nq // self.nkv
+        qh = q.transpose(1, 2)
+        kh = k.transpose(1, 2).repeat_interleave(G, 1)
+        vh = v.transpose(1, 2).repeat_interleave(G, 1)
+        qpos = torch.arange(Sk - S, Sk, device=h.device)
+        kpos = torch.arange(Sk, device=h.device)
+        allowed = (qpos[:, None] >= kpos[None])[None] & key_mask[:, None, :]
+        # a padding query attends to itself, so no softmax row is empty
+        allowed = allowed | (qpos[:, None] == kpos[None])[None]
+        o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=allowed[:, None], scale=1.0 / math.sqrt(D))
+        o = o.transpose(1, 2).reshape(B, S, self.nq * D)
+        return self._lin(o * torch.sigmoid(gate), lay.w["o_proj"], lay, "fo", lora, training)
+
+    def _linear_attn(self, lay, h, key_mask, lora, training, cache=None):
+        B, S, _ = h.shape
+        h = h * key_mask[:, -S:, None].to(h.dtype)
+        W = lay.w["in_proj_qkv"]
+        kd, vd = self.key_dim, self.value_dim
+        q = self._lin(h, W[:kd], lay, "lq", lora, training)
+        k = self._lin(h, W[kd : 2 * kd], lay, "lk", lora, training)
+        v = self._lin(h, W[2 * kd :], lay, "lv", lora, training)
+        mixed = torch.cat([q, k, v], -1).transpose(1, 2)                   # [B, C, S]
+        K = self.conv_k
+        prev = cache.get("conv") if cache is not None else None
+        ext = torch.cat([prev, mixed], -1) if prev is not None else F.pad(mixed, (K - 1, 0))
+        if cache is not None:
+            cache["conv"] = ext[..., -(K - 1):].detach().clone()
+        conv = F.conv1d(ext, lay.w["conv"][:, None, :], groups=mixed.shape[1])
+        mixed = F.silu(conv).transpose(1, 2)                               # [B, S, C]
+        q, k, v = mixed[..., :kd], mixed[..., kd : 2 * kd], mixed[..., 2 * kd :]
+        q = q.reshape(B, S, self.lk_heads, self.dk)
+        k = k.reshape(B, S, self.lk_heads, self.dk)
+        v = v.reshape(B, S, self.lv_heads, self.dv)
+        z = self._lin(h, lay.w["in_proj_z"], lay, "lz", lora, training).reshape(B, S, self.lv_heads, self.dv)
+        beta = torch.sigmoid(F.linear(h, lay.w["in_proj_b"]).float())
+        g = -lay.w["A_log"].exp() * F.softplus(F.linear(h, lay.w["in_proj_a"]).float() + lay.w["dt_bias"])
+        rep = self.lv_heads // self.lk_heads
+        if rep > 1:
+            q, k = q.repeat_interleave(rep, 2), k.repeat_interleave(rep, 2)
+        q = l2norm(q.float()) / math.sqrt(self.dk)
+        k = l2norm(k.float())
+        state = cache.get("state") if cache is not None else None
+        if cache is not None and state is not None and S == 1:
+            o = gated_delta_step(q[:, 0], k[:, 0], v[:, 0], g[:, 0], beta[:, 0], state)[:, None]
+        else:
+            o, fin = chunk_gated_delta(q, k, v, g, beta, state)
+            if cache is not None:
+                cache["state"] = fin.detach().clone()
+        o = gated_norm(o.to(h.dtype).reshape(-1, self.dv), z.reshape(-1, self.dv), lay.w["norm"],
+                       self.cfg.rms_norm_eps).reshape(B, S, vd)
+        return self._lin(o, lay.w["out_proj"], lay, "lo", lora, training)
+
+    def layer(self, lay, x, pos, key_mask, lora=None, training=False, cache=None):
+        eps = self.cfg.rms_norm_eps
+        h = norm1p(x, lay.ln1, eps)
+        if lay.kind == "full_attention":
+            x = x + self._full_attn(lay, h, pos, key_mask, lora, training, cache)
+        else:
+            x = x + self._linear_attn(lay, h, key_mask, lora, training, cache)
+        h2 = norm1p(x, lay.ln2, eps)
+        gate = self._lin(h2, lay.w["gate_proj"], lay, "gate", lora, training)
+        up = self._lin(h2, lay.w["up_proj"], lay, "up", lora, training)
+        return x + self._lin(F.silu(gate) * up, lay.w["down_proj"], lay, "down", lora, training)
+
+    def forward(self, ids, mask, *, lora=None, training=False, caches=None, pos=None, key_mask=None):
+        """[B, S] ids -> final hidden [B, S, H] (whole-sequence; caches fill for decoding)."""
+        x = F.embedding(ids, self.embed)
+        pos = (mask.long().cumsum(-1) - 1).clamp_min(0) if pos is None else pos
+        key_mask = mask if key_mask is None else key_mask
+        for i, lay in enumerate(self.layers):
+            c = caches[i] if caches is not None else None
+            if training and self.gradient_checkpointing and c is None:
+                x = torch.utils.checkpoint.checkpoint(self.layer, lay, x, pos, key_mask, lora, training,
+                                                      use_reentrant=False)
+            else:
+                x = self.layer(lay, x, pos, key_mask, lora, training, c)
+        return x
+
+    def logits(self, hidden):
+        return F.linear(norm1p(hidden, self.norm, self.cfg.rms_norm_eps).float(), self.lm_head.float())
+
+    def token_logprobs(self, hidden, targets, chunk: int = 8192):
+        """log p(targets) from final hidden states, computed in token chunks."""
+        hn = norm1p(hidden, self.norm, self.cfg.rms_norm_eps)
+        flat, tg = hn.reshape(-1, hn.shape[-1]), targets.reshape(-1)
+        out = []
+        for i in range(0, flat.shape[0], chunk):
+            lg = F.linear(flat[i : i + chunk].float(), self.lm_head.float())
+            out.append(lg.gather(-1, tg[i : i + chunk, None]).squeeze(-1) - torch.logsumexp(lg, -1))
+        return torch.cat(out).view(targets.shape)
+
+    def sequence_logprobs(self, seq, mask, *, lora=None, training=False, targets=None):
+        hidden = self.forward(seq, mask, lora=lora, training=training)
+        tgt = seq[:, 1:] if targets is None else targets
+        return self.token_logprobs(hidden[:, :-1], tgt)
+
+
+def gated_delta_step(q, k, v, g, beta, state):
+    """One decoding step of the recurrence; the sm_100a kernel on GPUs (state updated in place)."""
+    if state.is_cuda:
+        from graspo_b200.ops._ext import ext
+
+        out = torch.empty(v.shape, device=v.device, dtype=torch.float32)
+        ext().gated_delta_step(q.float().contiguous(), k.float().contiguous(), v.float().contiguous(),
+                               g.float().contiguous(), beta.float().contiguous(), state, out)
+        return out
+    return recurrent_gated_delta(q, k, v, g, beta, state)
+
+
+class HybridRolloutEngine:
+    """Grouped sampling for the hybrid decoder: each prompt is prefilled once,
+    its caches (KV for attention layers, conv + recurrent state for DeltaNet
+    layers) are copied to its G rows, then tokens are decoded one at a time."""
+
+    def __init__(self, model: Qwen35Model) -> None:
+        self.m = model
+
+    @torch.no_grad()
+    def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
+                 ignore_eos=False, seed=0):
+        import time
+
+        from graspo_b200.engine.rollout import EagerRolloutEngine, RolloutResult, _gen_lengths
+
+        m, dev = self.m, self.m.device
+        n, G = len(prompts), int(group_size)
+        lens = [max(1, len(p)) for p in prompts]
+        P = max(lens)
+        ids = torch.full((n, P), pad_id, dtype=torch.long)
+        mask = torch.zeros((n, P), dtype=torch.bool)
+        for i, p in enumerate(prompts):
+            row = list(p) or [pad_id]
+            ids[i, P - len(row):] = torch.tensor(row)
+            mask[i, P - len(row):] = True
+        t0 = time.perf_counter()
+        ids_d, mask_d = ids.to(dev), mask.to(dev)
+        caches = [dict() for _ in m.layers]
+        hidden = m.forward(ids_d, mask_d, caches=caches)
+        for c in caches:
+            for key, val in list(c.items()):
+                c[key] = val.repeat_interleave(G, 0)
+        key_mask = mask_d.repeat_interleave(G, 0)
+        pos = (mask_d.long().sum(-1) - 1).repeat_interleave(G, 0)
+        logits = m.logits(hidden[:, -1]).repeat_interleave(G, 0)
+        gen = torch.Generator(device=dev).manual_seed(int(seed))
+        rows = n * G
+        out = torch.full((rows, max_new_tokens), pad_id, dtype=torch.long, device=dev)
+        finished = torch.zeros(rows, dtype=torch.bool, device=dev)
+        t1 = time.perf_counter()
+        steps = 0
+        for t in range(max_new_tokens):
+            tok = EagerRolloutEngine._sample(logits, temperature, top_p, gen)
+            tok = torch.where(finished, torch.full_like(tok, pad_id), tok)
+            out[:, t] = tok
+            if not ignore_eos:
+                finished |= tok == eos_id
+            steps += 1
+            if t + 1 == max_new_tokens or (not ignore_eos and bool(finished.all())):
+                break
+            key_mask = torch.cat([key_mask, torch.ones(rows, 1, dtype=torch.bool, device=dev)], 1)
+            pos = pos + 1
+            x = m.forward(tok[:, None], key_mask[:, -1:], caches=caches, pos=pos[:, None], key_mask=key_mask)
+            logits = m.logits(x[:, -1])
+        tokens = out.cpu()
+        return RolloutResult(prompt_ids=ids, prompt_lens=lens, tokens=tokens,
+                             gen_lens=_gen_lengths(tokens, eos_id, ignore_eos), group_size=G,
+                             prefill_sec=t1 - t0, decode_sec=time.perf_counter() - t1, decode_steps=steps)
+
+
+__all__ = ["Qwen35Model", "HybridRolloutEngine", "chunk_gated_delta", "recurrent_gated_delta", "gated_delta_step",
+           "EagerLoRA"]
