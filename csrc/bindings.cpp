@@ -18,7 +18,8 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta, c10::optio
                  c10::optional<torch::Tensor> lora_a, c10::optional<torch::Tensor> lora_u, double scale,
                  double eps, c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r,
                  c10::optional<torch::Tensor> peer_src, c10::optional<torch::Tensor> peer_sync,
-                 int64_t peer_expected, c10::optional<torch::Tensor> err);
+                 int64_t peer_expected, c10::optional<torch::Tensor> err,
+                 c10::optional<torch::Tensor> zero_tail);
 void rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> dres, torch::Tensor dx, double eps);
 void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq,
@@ -77,7 +78,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm", &gb::add_rmsnorm, py::arg("h"), py::arg("delta"), py::arg("h_out"), py::arg("w"),
         py::arg("y"), py::arg("rstd"), py::arg("lora_a"), py::arg("lora_u"), py::arg("scale"), py::arg("eps"),
         py::arg("delta_lora_b") = py::none(), py::arg("delta_lora_r") = 0, py::arg("peer_src") = py::none(),
-        py::arg("peer_sync") = py::none(), py::arg("peer_expected") = 0, py::arg("err") = py::none());
+        py::arg("peer_sync") = py::none(), py::arg("peer_expected") = 0, py::arg("err") = py::none(),
+        py::arg("zero_tail") = py::none());
   m.def("rmsnorm_bwd", &gb::rmsnorm_bwd);
   m.def("qk_norm_rope", &gb::qk_norm_rope, py::arg("qkv"), py::arg("q_w"), py::arg("k_w"), py::arg("inv_freq"),
         py::arg("pos"), py::arg("q_out"), py::arg("k_out"), py::arg("v_out"), py::arg("block_table"),

@@ -116,7 +116,8 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
                                    const __nv_bfloat16* __restrict__ lora_a,
                                    __nv_bfloat16* __restrict__ lora_u, int H, int R, int ldu,
                                    float scale, float eps, long ldd,
-                                   const __nv_bfloat16* __restrict__ dlb, int ldb, int dlr, PeerSum ps) {
+                                   const __nv_bfloat16* __restrict__ dlb, int ldb, int dlr, PeerSum ps,
+                                   float* __restrict__ zero_tail, long zero_ld, int zero_n) {
   constexpr int MAXC = 4;  // chunks of 8 per thread: H <= 256*8*4 = 8192
   __shared__ float red[32];
   __shared__ float ured[8][64];
@@ -268,6 +269,10 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
     }
     for (int j = R + threadIdx.x; j < ldu; j += blockDim.x) lora_u[row * ldu + j] = __float2bfloat16(0.f);
   }
+  // another kernel's per-row fp32 columns to clear for the next step (the LoRA
+  // U of the q/k/v projection, read by qk_norm_rope earlier in this step)
+  if (zero_tail != nullptr)
+    for (int j = threadIdx.x; j < zero_n; j += blockDim.x) zero_tail[row * zero_ld + j] = 0.f;
   if (peers) peer_release(ps);
 }
 
@@ -370,26 +375,24 @@ struct RopeArgs {
   int ldb, lora_r, u_width;
 };
 
-// One CTA (8 warps) per token; warps loop over the token's heads.
+// One warp per (token, head).  The LoRA U columns are only read here; the
+// residual-add + RMSNorm kernel after the attention zeroes them for the next
+// step (see add_rmsnorm's zero_tail).
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
   constexpr int D = 128;
-  __shared__ float us[192];
-  const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int heads = a.nq + 2 * a.nkv;
-  const bool lora = a.qkv_f32 && a.lora_b != nullptr;
+  const long wg = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   pdl_trigger();
   pdl_wait();
-  if (lora) {
-    float* ur = static_cast<float*>(const_cast<void*>(a.qkv)) + static_cast<long>(t) * a.ld_qkv +
-                static_cast<long>(heads) * D;
-    for (int j = threadIdx.x; j < a.u_width; j += blockDim.x) {
-      if (j < 192) us[j] = ur[j];
-      ur[j] = 0.f;
-    }
-    __syncthreads();
-  }
-  for (int hd = warp; hd < heads; hd += 8) {
+  if (wg >= static_cast<long>(a.T) * heads) return;
+  const int t = static_cast<int>(wg / heads);
+  const bool lora = a.qkv_f32 && a.lora_b != nullptr;
+  const float* us = lora ? static_cast<const float*>(a.qkv) + static_cast<long>(t) * a.ld_qkv +
+                               static_cast<long>(heads) * D
+                         : nullptr;
+  {
+  const int hd = static_cast<int>(wg - static_cast<long>(t) * heads);
   float x[4];
   const long base = static_cast<long>(t) * a.ld_qkv + static_cast<long>(hd) * D + lane * 4;
   if (a.qkv_f32) {
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
     // round like a bf16 GEMM output would be
     if (lora) {
       const int blk = hd < a.nq ? 0 : (hd < a.nq + a.nkv ? 1 : 2);
-      const float* u = us + blk * a.lora_r;
+      const float* u = us + blk * a.lora_r;  // L1/L2-served broadcast reads
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const uint4* br = reinterpret_cast<const uint4*>(
@@ -656,7 +659,8 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
                  c10::optional<torch::Tensor> lora_u, double scale, double eps,
                  c10::optional<torch::Tensor> delta_lora_b, int64_t delta_lora_r,
                  c10::optional<torch::Tensor> peer_src, c10::optional<torch::Tensor> peer_sync,
-                 int64_t peer_expected, c10::optional<torch::Tensor> err) {
+                 int64_t peer_expected, c10::optional<torch::Tensor> err,
+                 c10::optional<torch::Tensor> zero_tail) {
   check_bf16(h, "h");
   check_bf16(y, "y");
   const c10::cuda::CUDAGuard guard(h.device());
@@ -715,10 +719,21 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
     ps.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
     TORCH_CHECK(ldd % 4 == 0, "peer sum needs 16-byte aligned rows");
   }
+  float* zt = nullptr;
+  long zld = 0;
+  int zn = 0;
+  if (zero_tail.has_value() && zero_tail->defined()) {
+    TORCH_CHECK(zero_tail->scalar_type() == torch::kFloat32 && zero_tail->dim() == 2 && zero_tail->stride(1) == 1 &&
+                    zero_tail->size(0) == rows,
+                "zero_tail must be an fp32 [rows, n] view with unit inner stride");
+    zt = zero_tail->data_ptr<float>();
+    zld = zero_tail->stride(0);
+    zn = static_cast<int>(zero_tail->size(1));
+  }
 #define GB_LAUNCH_NORM(DF, HD, LR)                                                                       \
   C10_CUDA_CHECK(launch_kernel(add_rmsnorm_kernel<DF, HD, LR>, dim3(rows), dim3(kNormThreads), 0, stream, hp, \
                                dptr, hout, wp, yp, rp, ap, up, H, R, ldu, (float)scale, (float)eps, ldd, dlb, \
-                               ldb, dlr, ps))
+                               ldb, dlr, ps, zt, zld, zn))
   if (!has_delta) {
     if (lora) GB_LAUNCH_NORM(false, false, true); else GB_LAUNCH_NORM(false, false, false);
   } else if (delta_f32) {
@@ -791,8 +806,10 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
                 "LoRA rank must be a multiple of 8, at most 64, with U columns after the projection");
     TORCH_CHECK(lora_b->size(0) == (nq + 2 * nkv) * 128, "lora_b rows must match the projection width");
   }
-  if (a.T > 0)
-    C10_CUDA_CHECK(launch_kernel(qk_norm_rope_kernel, dim3(a.T), dim3(256), 0, at::cuda::getCurrentCUDAStream(), a));
+  const long warps = static_cast<long>(a.T) * (nq + 2 * nkv);
+  if (warps > 0)
+    C10_CUDA_CHECK(launch_kernel(qk_norm_rope_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0,
+                                 at::cuda::getCurrentCUDAStream(), a));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

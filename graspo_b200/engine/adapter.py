@@ -72,6 +72,20 @@ def collate(items: list[Experience], device: torch.device, pad_id: int):
 
 
 class Qwen3Adapter:
+    families: tuple[str, ...] = ("qwen3",)
+    model_class = Qwen3Model
+
+    def __new__(cls, config: Any = None, *args: Any, **kwargs: Any):
+        # the default adapter serves both families: a qwen3_5 checkpoint gets the hybrid adapter
+        if cls is Qwen3Adapter and config is not None:
+            try:
+                family = load_decoder_config(Path(config.model.model_path)).family
+            except (OSError, ValueError, KeyError, AttributeError):
+                family = None
+            if family == "qwen3_5_text":
+                cls = Qwen35Adapter
+        return super().__new__(cls)
+
     completion_parser_name = "qwen_tool_call"
 
     def __init__(self, config: Any) -> None:
@@ -121,8 +135,8 @@ class Qwen3Adapter:
 
         self.tokenizer = load_tokenizer(model_path)
         hf = load_decoder_config(model_path)
-        if hf.family != "qwen3":
-            raise ValueError(f"Qwen3Adapter serves the dense qwen3 family; got {hf.family}")
+        if hf.family not in self.families:
+            raise ValueError(f"{type(self).__name__} serves the {'/'.join(self.families)} family; got {hf.family}")
         targets = resolve_lora_target_modules(
             cfg.lora.target_modules or (cfg.lora.target_preset,), available=lora_available_targets(hf)
         )
@@ -135,7 +149,7 @@ class Qwen3Adapter:
         if self.device.type == "cpu" and dtype != torch.float32:
             dtype = torch.float32
         loader = SafetensorIndex(model_path)
-        self.model = Qwen3Model(
+        self.model = self.model_class(
             hf, loader, ps=self.ps, local_layers=list(self.placement.local_layer_indices),
             include_embed=self.placement.include_embeddings, include_head=self.placement.include_lm_head,
             lora_targets=set(targets.resolved), lora_r=cfg.lora.r, lora_alpha=cfg.lora.alpha,
@@ -167,9 +181,7 @@ class Qwen3Adapter:
                                               fused_tp_allreduce=flow.decode_tp_allreduce == "fused",
                                               comm=self._comm)
         else:
-            from graspo_b200.engine.rollout import EagerRolloutEngine
-
-            self._engine = EagerRolloutEngine(self.model)
+            self._engine = self._eager_engine()
         self._print_rank0({
             "event": "adapter_ready", "rank": self.rank, "tp_rank": self.tp_rank, "tp_size": self.ps.tp_size,
             "dp_size": self.ps.dp_size, "pp_size": self.ps.pp_size, "backend": "fused" if self.fused else "eager",
@@ -178,6 +190,11 @@ class Qwen3Adapter:
             "lora_target_signature": self.model.lora_target_signature(),
             "placement": placement_summary(self.placement),
         })
+
+    def _eager_engine(self):
+        from graspo_b200.engine.rollout import EagerRolloutEngine
+
+        return EagerRolloutEngine(self.model)
 
     def _build_optimizer(self) -> None:
         tr = self.config.training
@@ -337,8 +354,11 @@ class Qwen3Adapter:
             return logp, ((meta, inputs, xL, hn_all, rstd, full, lse) if train else None)
         lora = EagerLoRA(self.model.lora, requires_grad=train)
         with torch.set_grad_enabled(train):
-            hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train)
-            logp = eager_token_logprobs(self.model, hidden[:, :-1], tgt)
+            if hasattr(self.model, "sequence_logprobs"):
+                logp = self.model.sequence_logprobs(seq, mask, lora=lora, training=train, targets=tgt)
+            else:
+                hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train)
+                logp = eager_token_logprobs(self.model, hidden[:, :-1], tgt)
         return logp, lora
 
     def _fused_backward_from_logp_grad(self, ctx, dlogp: torch.Tensor, seed: int) -> None:
@@ -555,3 +575,31 @@ class Qwen3Adapter:
     def close(self) -> None:
         self._engine = None
         pstate.destroy()
+
+
+class Qwen35Adapter(Qwen3Adapter):
+    """Adapter of the Qwen3.5 / 3.6 hybrid family (gated DeltaNet + gated
+    attention; reference: backends/graspoflow/models/qwen35_36/adapter.py:35-117).
+
+    Training and log-probs run the model's autograd path (chunked delta rule,
+    gradient checkpointing per layer), rollout runs ``HybridRolloutEngine``
+    (per-row KV / conv / recurrent caches, the delta-rule decode step on the
+    sm_100a kernel).  Text prompts only; TP = 1 per replica.
+    """
+
+    families = ("qwen3_5_text",)
+
+    @property
+    def model_class(self):
+        from graspo_b200.models.qwen35 import Qwen35Model
+
+        return Qwen35Model
+
+    @property
+    def fused(self) -> bool:
+        return False
+
+    def _eager_engine(self):
+        from graspo_b200.models.qwen35 import HybridRolloutEngine
+
+        return HybridRolloutEngine(self.model)

@@ -107,9 +107,10 @@ class FusedRolloutEngine:
         # hidden states go forward by p2p, the last stage samples and broadcasts
         # the tokens to its column (no CUDA graph across the p2p boundary)
         self.comm = comm if (comm is not None and comm.active) else None
-        # attend the prompt keys once per group (shared-prefix kernel); False
-        # runs every row over its whole key range
-        self.prefix_attention = True
+        # attend the prompt keys once per group (shared-prefix kernel).  Off by
+        # default: with the current split kernel its fixed per-CTA cost outweighs
+        # the saved prompt reads at 1k-3k keys; True runs it
+        self.prefix_attention = False
 
     def _ensure_pool(self, num_pages: int) -> None:
         m = self.m
@@ -240,6 +241,7 @@ class FusedRolloutEngine:
         steps = max_new_tokens - 1
         tails = self._refresh_lora_rows()
         bufs = self._decode_buffers(rows, tails)
+        bufs["qkv_u"] = bufs["qkv_ws"][:, m.q_local + 2 * m.kv_local:]
         if self.fused_tp:
             H = m.cfg.hidden_size
             self._sites = {"o": self._peer_site("o", rows, H + tails.get("w_o", 0)),
@@ -373,6 +375,8 @@ class FusedRolloutEngine:
             # fp32 split-K workspaces: projection columns, then U = s A x
             "qkv_ws": torch.zeros(rows, nqkv + tails.get("w_qkv", 0), device=dev, dtype=f32),
             "q": torch.empty(rows, m.nq, m.D, device=dev, dtype=dt),
+            # LoRA U columns of the q/k/v workspace (cleared after qk_norm_rope has read them)
+            "qkv_u": None,
             "attn": torch.empty(rows, m.q_local, device=dev, dtype=dt),
             "o_ws": torch.zeros(rows, H + tails.get("w_o", 0), device=dev, dtype=f32),
             # U = s A xn of the gate/up LoRA (the K-extension operand of that GEMM)
@@ -436,8 +440,12 @@ class FusedRolloutEngine:
                 dist.all_reduce(b["o_ws"], group=tp_group)
             a_gu = L.get("a_gu")
             ug = b["u_gu"] if a_gu is not None else None
-            C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None, a_gu, ug, 1.0, eps,
-                          L.get("b_o"), r if has_o else 0, **o_norm)
+            # only the 2r live rows of the padded A layout are dotted (the rest of U stays 0);
+            # this kernel also clears the q/k/v LoRA U columns read by qk_norm_rope
+            C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None,
+                          a_gu[: 2 * r] if a_gu is not None else None, ug, 1.0, eps,
+                          L.get("b_o"), r if has_o else 0, **o_norm,
+                          zero_tail=b["qkv_u"] if has_qkv else None)
             gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
                  swap=True, epilogue="swiglu")
             has_d = "a_down" in L

@@ -74,9 +74,11 @@ def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epi
 
 
 def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps, delta_lora_b=None, delta_lora_r=0,
-                peer_src=None, peer_sync=None, peer_expected=0, err=None):
+                peer_src=None, peer_sync=None, peer_expected=0, err=None, zero_tail=None):
     if peer_src is not None:
         raise NotImplementedError("the peer-memory sum needs GPUs")
+    if zero_tail is not None:
+        zero_tail.zero_()
     x = _f(h)
     H = h.shape[-1]
     if delta is not None:
@@ -134,7 +136,7 @@ def qk_norm_rope(qkv, q_w, k_w, inv_freq, pos, q_out, k_out, v_out, block_table,
     x = x.view(T, nq + 2 * nkv, D)
     if qkv.dtype == torch.float32:
         x = x.to(torch.bfloat16).float()
-        qkv.zero_()
+        qkv[:, :W].zero_()
     q = _rope(_head_norm(x[:, :nq], q_w, eps), pos, inv_freq)
     k = _rope(_head_norm(x[:, nq : nq + nkv], k_w, eps), pos, inv_freq)
     v = x[:, nq + nkv :]

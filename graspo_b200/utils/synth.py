@@ -76,6 +76,98 @@ def _qwen3_tensor_specs(dims: dict) -> list[tuple[str, tuple[int, ...], str]]:
     return specs
 
 
+QWEN35_TINY = dict(
+    vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=4,
+    num_attention_heads=4, num_key_value_heads=2, head_dim=32,
+    linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=32, linear_value_head_dim=32,
+    linear_conv_kernel_dim=4, full_attention_interval=4, partial_rotary_factor=0.25,
+)
+
+
+def _qwen35_tensor_specs(dims: dict) -> list[tuple[str, tuple[int, ...], str]]:
+    H, I, V = dims["hidden_size"], dims["intermediate_size"], dims["vocab_size"]
+    D = dims["head_dim"]
+    nq, nkv = dims["num_attention_heads"], dims["num_key_value_heads"]
+    kd = dims["linear_num_key_heads"] * dims["linear_key_head_dim"]
+    vd = dims["linear_num_value_heads"] * dims["linear_value_head_dim"]
+    hv = dims["linear_num_value_heads"]
+    pre = "model.language_model"
+    specs = [(f"{pre}.embed_tokens.weight", (V, H), "normal")]
+    for i, kind in enumerate(qwen35_layer_types(dims)):
+        p = f"{pre}.layers.{i}"
+        specs += [(f"{p}.input_layernorm.weight", (H,), "zeros"), (f"{p}.post_attention_layernorm.weight", (H,), "zeros")]
+        if kind == "full_attention":
+            specs += [(f"{p}.self_attn.q_proj.weight", (2 * nq * D, H), "normal"),
+                      (f"{p}.self_attn.k_proj.weight", (nkv * D, H), "normal"),
+                      (f"{p}.self_attn.v_proj.weight", (nkv * D, H), "normal"),
+                      (f"{p}.self_attn.o_proj.weight", (H, nq * D), "normal"),
+                      (f"{p}.self_attn.q_norm.weight", (D,), "zeros"), (f"{p}.self_attn.k_norm.weight", (D,), "zeros")]
+        else:
+            specs += [(f"{p}.linear_attn.in_proj_qkv.weight", (2 * kd + vd, H), "normal"),
+                      (f"{p}.linear_attn.in_proj_z.weight", (vd, H), "normal"),
+                      (f"{p}.linear_attn.in_proj_b.weight", (hv, H), "normal"),
+                      (f"{p}.linear_attn.in_proj_a.weight", (hv, H), "normal"),
+                      (f"{p}.linear_attn.conv1d.weight", (2 * kd + vd, 1, dims["linear_conv_kernel_dim"]), "conv"),
+                      (f"{p}.linear_attn.dt_bias", (hv,), "ones"),
+                      (f"{p}.linear_attn.A_log", (hv,), "alog"),
+                      (f"{p}.linear_attn.norm.weight", (dims["linear_value_head_dim"],), "ones"),
+                      (f"{p}.linear_attn.out_proj.weight", (H, vd), "normal")]
+        specs += [(f"{p}.mlp.gate_proj.weight", (I, H), "normal"), (f"{p}.mlp.up_proj.weight", (I, H), "normal"),
+                  (f"{p}.mlp.down_proj.weight", (H, I), "normal")]
+    specs += [(f"{pre}.norm.weight", (H,), "zeros"), ("lm_head.weight", (V, H), "normal")]
+    return specs
+
+
+def qwen35_layer_types(dims: dict) -> list[str]:
+    every = int(dims.get("full_attention_interval", 4))
+    return ["full_attention" if (i + 1) % every == 0 else "linear_attention" for i in range(dims["num_hidden_layers"])]
+
+
+def write_qwen35_checkpoint(output_dir: str | Path, dims: dict, *, seed: int = 0, std: float = 0.02,
+                            dtype: torch.dtype = torch.bfloat16, with_tokenizer: bool = True) -> Path:
+    """Random-init Qwen3.5 hybrid (``model_type: qwen3_5`` with a ``qwen3_5_text`` text config)."""
+    from safetensors.torch import save_file
+
+    out = Path(output_dir)
+    if (out / ".complete").exists():
+        return out
+    out.mkdir(parents=True, exist_ok=True)
+    gen = torch.Generator().manual_seed(seed)
+    tensors = {}
+    for name, shape, kind in _qwen35_tensor_specs(dims):
+        if kind == "normal":
+            t = torch.randn(shape, generator=gen) * std
+        elif kind == "zeros":
+            t = torch.zeros(shape)
+        elif kind == "ones":
+            t = torch.ones(shape)
+        elif kind == "conv":
+            t = torch.randn(shape, generator=gen) * 0.3
+        else:  # A_log: decays between exp(-1) and exp(-16) per step scale
+            t = torch.log(torch.rand(shape, generator=gen) * 15 + 1)
+        tensors[name] = t.to(dtype).contiguous()
+    save_file(tensors, str(out / "model.safetensors"), metadata={"format": "pt"})
+    (out / "model.safetensors.index.json").write_text(json.dumps(
+        {"metadata": {}, "weight_map": {k: "model.safetensors" for k in tensors}}, indent=2))
+    text = {
+        "model_type": "qwen3_5_text", "hidden_act": "silu", "rms_norm_eps": 1e-6,
+        "layer_types": qwen35_layer_types(dims), "tie_word_embeddings": False,
+        "rope_parameters": {"rope_theta": 1e7, "partial_rotary_factor": dims.get("partial_rotary_factor", 0.25)},
+        **{k: v for k, v in dims.items() if k not in ("full_attention_interval", "partial_rotary_factor")},
+    }
+    eos = dims["vocab_size"] - 4
+    config = {"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"], "text_config": text,
+              "tie_word_embeddings": False, "eos_token_id": eos}
+    (out / "config.json").write_text(json.dumps(config, indent=2))
+    (out / "generation_config.json").write_text(json.dumps({"eos_token_id": eos}))
+    if with_tokenizer:
+        from graspo_b200.utils.tokenizer import build_tokenizer
+
+        build_tokenizer(out, dims["vocab_size"])
+    (out / ".complete").write_text("ok")
+    return out
+
+
 def write_qwen3_checkpoint(
     output_dir: str | Path,
     dims: dict,

@@ -449,3 +449,23 @@ def test_dropout_statistics():
     y2 = torch.empty_like(x)
     _ext().dropout(x, y2, 0.1, 5, 3, None)
     assert torch.equal(y, y2), "same seed and stream must regenerate the same mask"
+
+
+@pytest.mark.parametrize("dk,dv", [(64, 64), (128, 128), (128, 96)])
+def test_gated_delta_step_matches_recurrence(dk, dv):
+    from graspo_b200.models.qwen35 import l2norm, recurrent_gated_delta
+
+    B, h = 3, 5
+    q = (l2norm(torch.randn(B, h, dk, device="cuda")) / dk ** 0.5).float()
+    k = l2norm(torch.randn(B, h, dk, device="cuda")).float()
+    v = torch.randn(B, h, dv, device="cuda")
+    g = -torch.rand(B, h, device="cuda")
+    beta = torch.rand(B, h, device="cuda")
+    state = torch.randn(B, h, dk, dv, device="cuda") * 0.1
+    ref_state = state.clone()
+    ref = recurrent_gated_delta(q, k, v, g, beta, ref_state)
+    out = torch.empty(B, h, dv, device="cuda")
+    for _ in range(1):
+        _ext().gated_delta_step(q, k, v, g, beta, state, out)
+    _close(out, ref, 1e-4)
+    _close(state, ref_state, 1e-4)
