@@ -255,9 +255,86 @@ class Qwen3Adapter:
 
     def generate_sample_groups(self, *, samples: list[Any], **kwargs: Any) -> list[NativeGeneration]:
         if any(getattr(s, "media", None) for s in samples):
-            raise NotImplementedError("image/video samples need the multimodal adapter (VisionQwen3Adapter)")
+            return self._generate_multimodal(samples, **kwargs)
         return self.generate_groups(message_batches=[s.messages for s in samples],
                                     tool_batches=[s.tools for s in samples], **kwargs)
+
+    # ------------------------------------------------------------ images
+    @property
+    def _vision_pad_id(self) -> int:
+        return int(self.tokenizer.convert_tokens_to_ids("<|vision_pad|>"))
+
+    def _image_features(self, media_rows: list[list[dict]]):
+        """Vision-tower features of every image of every row, rows in order (cached per image path)."""
+        from graspo_b200.models.vision import load_image, preprocess
+
+        vt = getattr(self.model, "vision", None)
+        if vt is None:
+            raise NotImplementedError("this checkpoint has no vision tower (config.json vision_config)")
+        cache = self.__dict__.setdefault("_image_cache", {})
+        if len(cache) > 512:
+            cache.clear()
+        feats = []
+        for media in media_rows:
+            for item in media or []:
+                if item.get("type") != "image":
+                    raise NotImplementedError("video inputs are not supported")
+                path = item["path"]
+                if path not in cache:
+                    patches, grid = preprocess(load_image(path), vt.cfg)
+                    cache[path] = vt.encode([patches], [grid])
+                feats.append(cache[path])
+        return torch.cat(feats, 0) if feats else None
+
+    def _image_hook(self, media_rows: list[list[dict]]):
+        """embed_hook placing image features on the image placeholder tokens."""
+        from graspo_b200.models.vision import scatter_image_features
+
+        feats = self._image_features(media_rows)
+        if feats is None:
+            return None
+        pad = self._vision_pad_id
+        return lambda ids, x: scatter_image_features(x, ids, pad, feats)
+
+    def _generate_multimodal(self, samples, *, rollout_group_size: int, max_new_tokens: int,
+                             max_prompt_length: int | None = None, temperature: float = 1.0, top_p: float = 1.0,
+                             chat_template_kwargs: dict | None = None, **_: Any) -> list[NativeGeneration]:
+        from graspo_b200.models.vision import expand_image_placeholders, load_image, merged_tokens, preprocess
+
+        vt = getattr(self.model, "vision", None)
+        if vt is None:
+            raise NotImplementedError("this checkpoint has no vision tower (config.json vision_config)")
+        t0 = time.monotonic()
+        max_len = int(max_prompt_length or self.config.data.max_prompt_length)
+        texts = [self.format_messages(s.messages, chat_template_kwargs, tools=s.tools) for s in samples]
+        enc = self.tokenizer(texts, padding=False, add_special_tokens=False)
+        pad = self._vision_pad_id
+        prompts, media_rows = [], []
+        for s, ids in zip(samples, enc["input_ids"], strict=True):
+            media = [m for m in (s.media or []) if m.get("type") == "image"]
+            counts = [merged_tokens(preprocess(load_image(m["path"]), vt.cfg)[1], vt.cfg) for m in media]
+            ids = expand_image_placeholders(list(ids), pad, counts)
+            if len(ids) > max_len:
+                # keep the image tokens: drop text from the front of the prompt
+                ids = ids[len(ids) - max_len:]
+                if ids.count(pad) != sum(counts):
+                    raise ValueError("max_prompt_length cuts into the image tokens of a prompt")
+            prompts.append(ids)
+            media_rows.append(media)
+        tok = self.tokenizer
+        eos = int(tok.eos_token_id)
+        pad_tok = int(tok.pad_token_id if tok.pad_token_id is not None else eos)
+        seed = int(self.config.training.seed) * 1_000_003 + self._train_batch_call_index
+        seed += 7919 * (self.ps.dp_rank if self.ps else 0)
+        res = self._engine.generate(prompts, group_size=rollout_group_size, max_new_tokens=max_new_tokens,
+                                    temperature=temperature, top_p=top_p, eos_id=eos, pad_id=pad_tok,
+                                    ignore_eos=bool(self.config.graspoflow.benchmark_ignore_eos), seed=seed,
+                                    embed_hook=self._image_hook(media_rows))
+        gens = self._generations(res, 0.0, time.monotonic() - t0)
+        G = res.group_size
+        for g, media in zip(gens, media_rows, strict=True):
+            g.metadata["_media_rows"] = [media] * G
+        return gens
 
     def generate_group(self, *, messages, tools=None, **kwargs) -> NativeGeneration:
         return self.generate_groups(message_batches=[messages], tool_batches=[tools], **kwargs)[0]
@@ -312,6 +389,9 @@ class Qwen3Adapter:
         dev = self.device
         seq = sequences.to(dev)
         mask = attention_mask.to(dev).bool()
+        media_rows = (metadata or {}).get("_media_rows") if isinstance(metadata, dict) else None
+        if media_rows and any(media_rows):
+            return self._logprobs(seq, mask, train=False, embed_hook=self._image_hook(media_rows))[0]
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_logprobs
 
@@ -321,7 +401,7 @@ class Qwen3Adapter:
             outs.append(self._logprobs(seq[sl], mask[sl], train=False)[0])
         return torch.cat(outs, 0)
 
-    def _logprobs(self, seq, mask, *, train: bool, seed: int = 0, targets=None):
+    def _logprobs(self, seq, mask, *, train: bool, seed: int = 0, targets=None, embed_hook=None):
         """log p(targets) per position, [B, S-1] fp32 (targets default to seq[:, 1:]).
 
         In training the second return value carries what the backward needs.
@@ -343,7 +423,10 @@ class Qwen3Adapter:
                 mask = torch.cat([mask, mask.new_zeros(B, pad)], 1)
                 tgt = torch.cat([tgt, tgt.new_zeros(B, pad)], 1)
             meta = AttnMeta.from_mask(mask)
-            xL, inputs = f.stage_forward(f.sp_shard(f.embed(seq)), meta, train=train, seed=seed, keep_inputs=train)
+            x0 = f.embed(seq)
+            if embed_hook is not None:
+                x0 = embed_hook(seq, x0)
+            xL, inputs = f.stage_forward(f.sp_shard(x0), meta, train=train, seed=seed, keep_inputs=train)
             hn, rstd = f.final_norm(xL)
             hn_all = f.sp_gather(hn)
             full = torch.zeros_like(seq)
@@ -357,7 +440,7 @@ class Qwen3Adapter:
             if hasattr(self.model, "sequence_logprobs"):
                 logp = self.model.sequence_logprobs(seq, mask, lora=lora, training=train, targets=tgt)
             else:
-                hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train)
+                hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train, embed_hook=embed_hook)
                 logp = eager_token_logprobs(self.model, hidden[:, :-1], tgt)
         return logp, lora
 
@@ -394,13 +477,15 @@ class Qwen3Adapter:
         rows = max(1, int(self.config.graspoflow.pp_micro_batch_size))
         return max(1, min(rows, 65536 // max(1, seq.shape[1])))
 
-    def _backward_grpo(self, seq, mask, old, adv, act, clip_eps: float, seed: int):
+    def _backward_grpo(self, seq, mask, old, adv, act, clip_eps: float, seed: int, embed_hook=None):
         """Forward + GRPO loss + backward into the flat grad buffer; returns loss (device)."""
         B, S = seq.shape
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
             from graspo_b200.ops._ext import ext
 
+            if embed_hook is not None:
+                raise NotImplementedError("image inputs with pipeline stages are not supported")
             old_c, adv_c, act_c = old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous()
 
             def loss_fn(logp_c, sl):
@@ -416,14 +501,14 @@ class Qwen3Adapter:
         if self.fused:
             from graspo_b200.ops._ext import ext
 
-            logp, ctx = self._logprobs(seq, mask, train=True, seed=seed)
+            logp, ctx = self._logprobs(seq, mask, train=True, seed=seed, embed_hook=embed_hook)
             loss = torch.zeros(1, device=seq.device, dtype=torch.float32)
             dlogp = torch.empty_like(logp)
             ext().grpo_loss(logp, old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous(), clip_eps,
                             1.0, loss, dlogp, None)
             self._fused_backward_from_logp_grad(ctx, dlogp, seed)
             return loss
-        logp, lora = self._logprobs(seq, mask, train=True)
+        logp, lora = self._logprobs(seq, mask, train=True, embed_hook=embed_hook)
         self.loss_fn.policy_ratio_clip_eps = clip_eps
         loss = self.loss_fn(logp, old, adv, act)
         if torch.isfinite(loss):
@@ -453,7 +538,9 @@ class Qwen3Adapter:
                 seq, att, old, adv, act = collate(batch, self.device, pad)
                 self.optimizer.zero_grad()
                 seed = (int(self.config.training.seed) << 20) ^ (self._train_batch_call_index << 10) ^ steps
-                loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed)
+                media_rows = [((e.metadata or {}).get("_media") or []) for e in batch]
+                hook = self._image_hook(media_rows) if any(media_rows) else None
+                loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed, embed_hook=hook)
                 self._tp_sync_replicated_grads()
                 self._dp_average_grads()
                 norm = self.optimizer.step(max_grad_norm, loss)

@@ -158,7 +158,10 @@ class FusedRolloutEngine:
         pad_id: int,
         ignore_eos: bool = False,
         seed: int = 0,
+        embed_hook=None,
     ) -> RolloutResult:
+        """``embed_hook(ids [n, P], x [n * P, H]) -> x`` may replace prompt token
+        embeddings (image features) before the prefill."""
         import time
 
         from graspo_b200.models.fused import AttnMeta
@@ -208,6 +211,8 @@ class FusedRolloutEngine:
         comm, ps = self.comm, m.ps
         H = m.cfg.hidden_size
         x = f.embed(ids_d) if m.include_embed else comm.recv_prev((n * P, H), torch.bfloat16)
+        if embed_hook is not None and m.include_embed:
+            x = embed_hook(ids_d, x)
         for lw in m.layers:
             x, _ = f.layer_forward(lw, x, meta, kv_sink=sink)
         if not m.include_head:
@@ -530,7 +535,7 @@ class EagerRolloutEngine:
 
     @torch.no_grad()
     def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
-                 ignore_eos=False, seed=0) -> RolloutResult:
+                 ignore_eos=False, seed=0, embed_hook=None) -> RolloutResult:
         import time
 
         m = self.m
@@ -558,6 +563,10 @@ class EagerRolloutEngine:
         gen = torch.Generator(device="cpu").manual_seed(int(seed))
         t0 = time.perf_counter()
         x = F.embedding(ids_r, m.embed)
+        if embed_hook is not None:
+            xu = F.embedding(ids.to(dev), m.embed)
+            xu = embed_hook(ids.to(dev), xu.reshape(-1, xu.shape[-1]).clone()).view_as(xu)
+            x = xu.repeat_interleave(G, 0)
         for lw, cache in zip(m.layers, caches, strict=True):
             x = self._layer(lw, x, pos, key_mask, cache, 0, lora)
         logits = self._logits(x[:, -1])

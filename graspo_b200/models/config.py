@@ -78,7 +78,11 @@ def load_decoder_config(model_path: str | Path) -> DecoderConfig:
     raw = json.loads((Path(model_path) / "config.json").read_text(encoding="utf-8"))
     model_type = str(raw.get("model_type") or "")
     if model_type == "qwen3":
-        return _from_values(raw, "qwen3", "model", {})
+        extra = {}
+        if raw.get("vision_config"):
+            # a dense Qwen3 decoder with a vision tower (weights under model.visual.)
+            extra = {"vision_config": dict(raw["vision_config"]), "image_token_id": raw.get("image_token_id")}
+        return _from_values(raw, "qwen3", "model", extra)
     text = dict(raw.get("text_config") or {})
     if model_type == "qwen3_5" and text.get("model_type") == "qwen3_5_text":
         extra = {

@@ -134,6 +134,14 @@ class Qwen3Model:
             return loader.get_cols(name, a, b).to(device=dev, dtype=dt)
 
         self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
+        # frozen vision tower on the stage that embeds the tokens
+        self.vision = None
+        if include_embed and cfg.has_vision:
+            from graspo_b200.models.vision import VisionConfig, VisionTower
+
+            vc = dict(cfg.extra["vision_config"])
+            vc.setdefault("out_hidden_size", cfg.hidden_size)
+            self.vision = VisionTower(VisionConfig.from_dict(vc), loader, "model.visual", dtype=dtype, device=self.device)
         self.layers: list[LayerWeights] = []
         modules: list[LoRAModule] = []
         H = cfg.hidden_size
@@ -356,16 +364,20 @@ def eager_stage_forward(
     *,
     lora: EagerLoRA | None = None,
     training: bool = False,
+    embed_hook=None,
 ) -> torch.Tensor:
     """Token ids (first stage) or hidden states -> hidden states after local layers.
 
     The adapter is always applied; pass ``lora`` (with ``requires_grad``) to
-    collect its gradients.
+    collect its gradients.  ``embed_hook(ids, x)`` may edit the token
+    embeddings in place (image features).
     """
     if lora is None:
         lora = EagerLoRA(model.lora, requires_grad=False)
     if model.include_embed:
         x = F.embedding(inputs, model.embed)
+        if embed_hook is not None:
+            x = embed_hook(inputs, x.reshape(-1, x.shape[-1]).clone()).view_as(x)
     else:
         x = inputs
     pos = position_ids_from_mask(attention_mask)

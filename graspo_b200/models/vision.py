@@ -1,0 +1,192 @@
+"""Vision tower: native ViT + 2x2 patch merger feeding image features to the decoder.
+
+Architecture of the Qwen3.5 / Qwen3-VL vision encoder (the reference runs the
+Hugging Face module; reference: backends/graspoflow/models/qwen3/model.py:170-232,
+qwen35_36/model.py:263-286), written here as plain tensor code:
+
+* patch embedding: each image is cut into 16 x 16 patches of 3 channels and 2
+  (duplicated) frames; the 3-D convolution with kernel == stride is a single
+  linear map of the flattened 1536-value patch (one GEMM);
+* a learned position table on a 48 x 48 grid, bilinearly resampled to the
+  image's patch grid;
+* 2-D rotary embedding on the attention heads (row and column frequencies);
+* ``depth`` pre-LayerNorm blocks: bidirectional multi-head attention inside
+  each image (QKV / output projections with bias), GELU(tanh) MLP;
+* merger: LayerNorm, every 2 x 2 block of neighbouring patches concatenated,
+  Linear -> GELU -> Linear into the decoder's hidden size.
+
+Patches are kept in merge-block order (rows of 2 x 2 blocks), so the merger's
+concatenation is a reshape.  ``preprocess`` turns an RGB uint8 image into
+that patch layout (CLIP mean / std normalisation, sides rounded to a multiple
+of 32 pixels).  The decoder receives one feature per merged block in place of
+each image placeholder token (``scatter_image_features``).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+MEAN = (0.48145466, 0.4578275, 0.40821073)
+STD = (0.26862954, 0.26130258, 0.27577711)
+
+
+@dataclass
+class VisionConfig:
+    depth: int = 27
+    hidden_size: int = 1152
+    intermediate_size: int = 4304
+    num_heads: int = 16
+    in_channels: int = 3
+    patch_size: int = 16
+    spatial_merge_size: int = 2
+    temporal_patch_size: int = 2
+    out_hidden_size: int = 4096
+    num_position_embeddings: int = 2304
+
+    @staticmethod
+    def from_dict(d: dict) -> "VisionConfig":
+        keys = VisionConfig.__dataclass_fields__.keys()
+        return VisionConfig(**{k: d[k] for k in keys if k in d})
+
+    @property
+    def patch_dim(self) -> int:
+        return self.in_channels * self.temporal_patch_size * self.patch_size ** 2
+
+
+def preprocess(image: torch.Tensor, cfg: VisionConfig) -> tuple[torch.Tensor, tuple[int, int, int]]:
+    """uint8 [H, W, 3] -> (patches [gh * gw, patch_dim] in merge-block order, (1, gh, gw))."""
+    unit = cfg.patch_size * cfg.spatial_merge_size
+    img = image.permute(2, 0, 1).float()[None] / 255.0                       # [1, 3, H, W]
+    H, W = img.shape[-2:]
+    h2, w2 = max(unit, round(H / unit) * unit), max(unit, round(W / unit) * unit)
+    if (h2, w2) != (H, W):
+        img = F.interpolate(img, size=(h2, w2), mode="bicubic", align_corners=False)
+    mean = torch.tensor(MEAN).view(1, 3, 1, 1)
+    std = torch.tensor(STD).view(1, 3, 1, 1)
+    img = ((img - mean) / std)[0]                                             # [3, h2, w2]
+    p, m, t = cfg.patch_size, cfg.spatial_merge_size, cfg.temporal_patch_size
+    gh, gw = h2 // p, w2 // p
+    frames = img[None].expand(t, -1, -1, -1)                                  # an image is t equal frames
+    x = frames.reshape(t, 3, gh // m, m, p, gw // m, m, p)
+    x = x.permute(2, 5, 3, 6, 1, 0, 4, 7)                                     # (bh, bw, mh, mw, C, t, p, p)
+    return x.reshape(gh * gw, cfg.patch_dim).contiguous(), (1, gh, gw)
+
+
+def load_image(path: str) -> torch.Tensor:
+    from PIL import Image
+
+    with Image.open(path) as im:
+        return torch.from_numpy(__import__("numpy").asarray(im.convert("RGB"), dtype="uint8").copy())
+
+
+class VisionTower:
+    """Frozen vision encoder (weights under ``<prefix>.``)."""
+
+    def __init__(self, cfg: VisionConfig, loader, prefix: str, *, dtype: torch.dtype, device: torch.device) -> None:
+        self.cfg, self.dtype, self.device = cfg, dtype, device
+
+        def load(name):
+            return loader.get(f"{prefix}.{name}").to(device=device, dtype=dtype)
+
+        self.patch_w = load("patch_embed.proj.weight").reshape(cfg.hidden_size, cfg.patch_dim)
+        self.patch_b = load("patch_embed.proj.bias")
+        self.pos_table = load("pos_embed.weight")
+        self.blocks = []
+        for i in range(cfg.depth):
+            b = f"blocks.{i}"
+            self.blocks.append({n: load(f"{b}.{n}") for n in (
+                "norm1.weight", "norm1.bias", "norm2.weight", "norm2.bias", "attn.qkv.weight", "attn.qkv.bias",
+                "attn.proj.weight", "attn.proj.bias", "mlp.linear_fc1.weight", "mlp.linear_fc1.bias",
+                "mlp.linear_fc2.weight", "mlp.linear_fc2.bias")})
+        self.merger = {n: load(f"merger.{n}") for n in (
+            "norm.weight", "norm.bias", "linear_fc1.weight", "linear_fc1.bias", "linear_fc2.weight", "linear_fc2.bias")}
+        hd = cfg.hidden_size // cfg.num_heads
+        self.head_dim = hd
+        quarter = hd // 2
+        self.rot_inv = (1.0 / (10000.0 ** (torch.arange(0, quarter, 2, dtype=torch.float32) / quarter))).to(device)
+
+    def _pos_embed(self, gh: int, gw: int) -> torch.Tensor:
+        n = int(math.isqrt(self.cfg.num_position_embeddings))
+        table = self.pos_table.float().view(n, n, -1).permute(2, 0, 1)[None]   # [1, C, n, n]
+        grid = F.interpolate(table, size=(gh, gw), mode="bilinear", align_corners=True)[0]  # [C, gh, gw]
+        m = self.cfg.spatial_merge_size
+        grid = grid.permute(1, 2, 0).reshape(gh // m, m, gw // m, m, -1).permute(0, 2, 1, 3, 4)
+        return grid.reshape(gh * gw, -1)
+
+    def _rotary(self, gh: int, gw: int) -> tuple[torch.Tensor, torch.Tensor]:
+        m = self.cfg.spatial_merge_size
+        rows = torch.arange(gh, device=self.device).view(gh // m, 1, m, 1).expand(gh // m, gw // m, m, m)
+        cols = torch.arange(gw, device=self.device).view(1, gw // m, 1, m).expand(gh // m, gw // m, m, m)
+        fr = rows.reshape(-1, 1).float() * self.rot_inv
+        fc = cols.reshape(-1, 1).float() * self.rot_inv
+        emb = torch.cat([fr, fc], -1)
+        emb = torch.cat([emb, emb], -1)                                         # [N, head_dim]
+        return emb.cos(), emb.sin()
+
+    @staticmethod
+    def _rope(x, cos, sin):
+        half = x.shape[-1] // 2
+        rot = torch.cat([-x[..., half:], x[..., :half]], -1)
+        return x * cos[:, None] + rot * sin[:, None]
+
+    @torch.no_grad()
+    def encode(self, patches: list[torch.Tensor], grids: list[tuple[int, int, int]]) -> torch.Tensor:
+        """Per-image patches -> merged features [sum(gh * gw / 4), out_hidden], images in order."""
+        cfg = self.cfg
+        outs = []
+        for pt, (_, gh, gw) in zip(patches, grids, strict=True):
+            x = F.linear(pt.to(self.device, self.dtype), self.patch_w, self.patch_b)
+            x = (x.float() + self._pos_embed(gh, gw)).to(self.dtype)
+            cos, sin = self._rotary(gh, gw)
+            N = x.shape[0]
+            for blk in self.blocks:
+                h = F.layer_norm(x, (cfg.hidden_size,), blk["norm1.weight"], blk["norm1.bias"], 1e-6)
+                qkv = F.linear(h, blk["attn.qkv.weight"], blk["attn.qkv.bias"]).view(N, 3, cfg.num_heads, -1)
+                q = self._rope(qkv[:, 0].float(), cos, sin).to(self.dtype)
+                k = self._rope(qkv[:, 1].float(), cos, sin).to(self.dtype)
+                v = qkv[:, 2]
+                o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
+                                                   v.transpose(0, 1)[None])[0].transpose(0, 1).reshape(N, -1)
+                x = x + F.linear(o, blk["attn.proj.weight"], blk["attn.proj.bias"])
+                h = F.layer_norm(x, (cfg.hidden_size,), blk["norm2.weight"], blk["norm2.bias"], 1e-6)
+                h = F.gelu(F.linear(h, blk["mlp.linear_fc1.weight"], blk["mlp.linear_fc1.bias"]), approximate="tanh")
+                x = x + F.linear(h, blk["mlp.linear_fc2.weight"], blk["mlp.linear_fc2.bias"])
+            mg = self.merger
+            h = F.layer_norm(x, (cfg.hidden_size,), mg["norm.weight"], mg["norm.bias"], 1e-6)
+            h = h.reshape(-1, cfg.hidden_size * cfg.spatial_merge_size ** 2)
+            h = F.gelu(F.linear(h, mg["linear_fc1.weight"], mg["linear_fc1.bias"]))
+            outs.append(F.linear(h, mg["linear_fc2.weight"], mg["linear_fc2.bias"]))
+        return torch.cat(outs, 0)
+
+
+def merged_tokens(grid: tuple[int, int, int], cfg: VisionConfig) -> int:
+    t, gh, gw = grid
+    return t * (gh // cfg.spatial_merge_size) * (gw // cfg.spatial_merge_size)
+
+
+def expand_image_placeholders(ids: list[int], pad_id: int, counts: list[int]) -> list[int]:
+    """Replace the k-th image placeholder token with counts[k] copies of it."""
+    out, k = [], 0
+    for t in ids:
+        if t == pad_id and k < len(counts):
+            out.extend([pad_id] * counts[k])
+            k += 1
+        else:
+            out.append(t)
+    if k != len(counts):
+        raise ValueError(f"prompt has {k} image placeholders for {len(counts)} images")
+    return out
+
+
+def scatter_image_features(x: torch.Tensor, ids: torch.Tensor, pad_id: int, feats: torch.Tensor) -> torch.Tensor:
+    """x [T, H] token embeddings of ids [T]: placeholder rows take the image features in order."""
+    sel = ids.reshape(-1) == pad_id
+    n = int(sel.sum())
+    if n != feats.shape[0]:
+        raise ValueError(f"{n} image placeholder tokens for {feats.shape[0]} image features")
+    x[sel] = feats.to(x.dtype)
+    return x

@@ -394,7 +394,10 @@ class GraspoTrainer:
                     sequences=gen.sequences[j].detach().cpu(), old_log_probs=old[j],
                     advantages=torch.full_like(old[j], float(adv[j])),
                     attention_mask=gen.attention_mask[j].detach().cpu(), action_mask=gen.action_mask[j].detach().cpu(),
-                    rewards=torch.tensor(rewards[j]), metadata=None,
+                    rewards=torch.tensor(rewards[j]),
+                    # image references travel with the experience so training re-encodes them
+                    metadata=({"_media": gen.metadata["_media_rows"][j]}
+                              if (gen.metadata or {}).get("_media_rows") else None),
                 ))
             self.replay_buffer.append_many(items)
             self.stats.trainable += 1

@@ -274,6 +274,74 @@ def synthetic_json_records(
     return records
 
 
+VIT_27L = dict(depth=27, hidden_size=1152, intermediate_size=4304, num_heads=16, in_channels=3, patch_size=16,
+               spatial_merge_size=2, temporal_patch_size=2, num_position_embeddings=2304)
+VIT_TINY = dict(depth=2, hidden_size=64, intermediate_size=128, num_heads=4, in_channels=3, patch_size=16,
+                spatial_merge_size=2, temporal_patch_size=2, num_position_embeddings=64)
+
+
+def add_vision_tower(model_dir: str | Path, vdims: dict, *, seed: int = 0, std: float = 0.02,
+                     dtype: torch.dtype = torch.bfloat16) -> Path:
+    """Add a random-init vision tower (``model.visual.*``) to a synthetic Qwen3 checkpoint."""
+    from safetensors.torch import save_file
+
+    out = Path(model_dir)
+    config = json.loads((out / "config.json").read_text())
+    if config.get("vision_config"):
+        return out
+    Hd, I = vdims["hidden_size"], vdims["intermediate_size"]
+    pdim = vdims["in_channels"] * vdims["temporal_patch_size"] * vdims["patch_size"] ** 2
+    merged = Hd * vdims["spatial_merge_size"] ** 2
+    out_h = config["hidden_size"]
+    gen = torch.Generator().manual_seed(seed)
+    specs = [("patch_embed.proj.weight", (Hd, vdims["in_channels"], vdims["temporal_patch_size"], vdims["patch_size"],
+                                          vdims["patch_size"]), "n"),
+             ("patch_embed.proj.bias", (Hd,), "z"), ("pos_embed.weight", (vdims["num_position_embeddings"], Hd), "n")]
+    for i in range(vdims["depth"]):
+        b = f"blocks.{i}"
+        specs += [(f"{b}.norm1.weight", (Hd,), "o"), (f"{b}.norm1.bias", (Hd,), "z"), (f"{b}.norm2.weight", (Hd,), "o"),
+                  (f"{b}.norm2.bias", (Hd,), "z"), (f"{b}.attn.qkv.weight", (3 * Hd, Hd), "n"),
+                  (f"{b}.attn.qkv.bias", (3 * Hd,), "z"), (f"{b}.attn.proj.weight", (Hd, Hd), "n"),
+                  (f"{b}.attn.proj.bias", (Hd,), "z"), (f"{b}.mlp.linear_fc1.weight", (I, Hd), "n"),
+                  (f"{b}.mlp.linear_fc1.bias", (I,), "z"), (f"{b}.mlp.linear_fc2.weight", (Hd, I), "n"),
+                  (f"{b}.mlp.linear_fc2.bias", (Hd,), "z")]
+    specs += [("merger.norm.weight", (Hd,), "o"), ("merger.norm.bias", (Hd,), "z"),
+              ("merger.linear_fc1.weight", (merged, merged), "n"), ("merger.linear_fc1.bias", (merged,), "z"),
+              ("merger.linear_fc2.weight", (out_h, merged), "n"), ("merger.linear_fc2.bias", (out_h,), "z")]
+    tensors = {}
+    for name, shape, kind in specs:
+        t = torch.randn(shape, generator=gen) * std if kind == "n" else (torch.ones(shape) if kind == "o"
+                                                                         else torch.zeros(shape))
+        tensors[f"model.visual.{name}"] = t.to(dtype).contiguous()
+    save_file(tensors, str(out / "model-vision.safetensors"), metadata={"format": "pt"})
+    index = json.loads((out / "model.safetensors.index.json").read_text())
+    index["weight_map"].update({k: "model-vision.safetensors" for k in tensors})
+    (out / "model.safetensors.index.json").write_text(json.dumps(index, indent=2))
+    config["vision_config"] = {**vdims, "out_hidden_size": out_h}
+    (out / "config.json").write_text(json.dumps(config, indent=2))
+    return out
+
+
+def synthetic_image_records(count: int, image_dir: str | Path, *, seed: int = 0, size: int = 448,
+                            text_words: int = 40) -> list[dict]:
+    """Seeded multimodal JSON-extraction records: one uniform-random uint8 RGB
+    image (PNG) plus a text instruction per record."""
+    import numpy as np
+    from PIL import Image
+
+    image_dir = Path(image_dir)
+    image_dir.mkdir(parents=True, exist_ok=True)
+    base = synthetic_json_records(count, seed=seed, pad_words_to=text_words)
+    rs = np.random.RandomState(seed)
+    for i, rec in enumerate(base):
+        path = image_dir / f"img_{seed}_{i}.png"
+        if not path.exists():
+            Image.fromarray(rs.randint(0, 256, (size, size, 3), dtype=np.uint8)).save(path)
+        text = rec["messages"][1]["content"]
+        rec["messages"][1]["content"] = [{"type": "image", "image": str(path)}, {"type": "text", "text": text}]
+    return base
+
+
 def write_jsonl_records(records: list[dict], path: str | Path) -> Path:
     out = Path(path)
     out.parent.mkdir(parents=True, exist_ok=True)
