@@ -250,7 +250,10 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
 constexpr int kTile = 64;
 constexpr int kRowBytes = kD * 2;                    // 256 B per key row
 constexpr int kTileBytes = kTile * kRowBytes;         // 16 KiB per K or V tile
-constexpr int kTcSmem = 2 * 2 * kTileBytes;           // 2 stages x (K, V)
+constexpr int kTcSmem = 2 * 2 * kTileBytes;           // 2 stages x (K, V) (prefix kernel)
+constexpr int kTcStages = 3;                            // split kernel: 3 tiles in flight
+constexpr int kTcSmemSplit = kTcStages * 2 * kTileBytes;
+constexpr int kBtCache = 128;                           // block-table entries kept in shared memory
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
   // byte offset of 16-byte chunk `chunk` (0..15) of key row `row` in a tile
@@ -531,9 +534,20 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
     }
   }
 
+  // block-table entries of this split's pages, read once
+  __shared__ int bt_s[kBtCache];
+  const int page_first = k_end > k_begin ? (t_first * kTile) / a.page_size : 0;
+  const int page_count = k_end > k_begin ? ((t_last + 1) * kTile - 1) / a.page_size - page_first + 1 : 0;
+  for (int i = threadIdx.x; i < min(page_count, kBtCache); i += blockDim.x) bt_s[i] = bt[page_first + i];
+  __syncthreads();
+  auto page_of = [&](int t0) {
+    const int pg = t0 / a.page_size - page_first;
+    return pg < kBtCache ? bt_s[pg] : bt[page_first + pg];
+  };
+
   auto load_tile = [&](int tile, int stage) {
     const int t0 = tile * kTile;
-    const int phys = bt[t0 / a.page_size];
+    const int phys = page_of(t0);
     const long base = ((static_cast<long>(phys) * a.nkv + kvh) * a.page_size + (t0 % a.page_size)) * kD;
     const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.k_pool + base);
     const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.v_pool + base);
@@ -546,7 +560,6 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
       cp_async16(kdst + swz(r, ch), ksrc + r * kRowBytes + ch * 16);
       cp_async16(vdst + swz(r, ch), vsrc + r * kRowBytes + ch * 16);
     }
-    cp_async_commit();
   };
 
   float o[16][4];
@@ -554,15 +567,16 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;  // for row g (rows g+8 are padding)
 
-  if (k_end > k_begin) load_tile(t_first, 0);
-  for (int tile = t_first; tile <= t_last && k_end > k_begin; ++tile) {
-    const int stage = (tile - t_first) & 1;
-    if (tile < t_last) {
-      load_tile(tile + 1, stage ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+  // kTcStages-deep cp.async ring: one commit group per tile (empty groups past the end)
+  const bool any_keys = k_end > k_begin;
+#pragma unroll
+  for (int sidx = 0; sidx < kTcStages - 1; ++sidx) {
+    if (any_keys && t_first + sidx <= t_last) load_tile(t_first + sidx, sidx);
+    cp_async_commit();
+  }
+  for (int tile = t_first; tile <= t_last && any_keys; ++tile) {
+    const int stage = (tile - t_first) % kTcStages;
+    cp_async_wait<kTcStages - 2>();
     __syncthreads();
     const uint32_t kt = sbase + stage * 2 * kTileBytes;
     const uint32_t vt = kt + kTileBytes;
@@ -634,8 +648,11 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
       mma_bf16(o[2 * nd], pa0, zero, pa2, zero, b0, b1);
       mma_bf16(o[2 * nd + 1], pa0, zero, pa2, zero, b2, b3);
     }
-    __syncthreads();  // this stage is overwritten by the load issued next iteration
+    __syncthreads();  // the stage read above is refilled below
+    if (tile + kTcStages - 1 <= t_last) load_tile(tile + kTcStages - 1, (tile + kTcStages - 1 - t_first) % kTcStages);
+    cp_async_commit();
   }
+  cp_async_wait<0>();
 
   // ---- merge warps (rows g < G hold data)
   if ((lane & 3) == 0 && g < G) {
@@ -812,10 +829,10 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
     const int dev = q.get_device();
 #define GB_TC(GV, IDX)                                                                                       \
   if (!configured[dev][IDX]) {                                                                               \
-    cudaFuncSetAttribute(paged_decode_attn_tc_kernel<GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem); \
+    cudaFuncSetAttribute(paged_decode_attn_tc_kernel<GV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemSplit); \
     configured[dev][IDX] = true;                                                                             \
   }                                                                                                          \
-  C10_CUDA_CHECK(launch_kernel(paged_decode_attn_tc_kernel<GV>, dim3(blocks), dim3(kWarps * 32), kTcSmem, stream, a))
+  C10_CUDA_CHECK(launch_kernel(paged_decode_attn_tc_kernel<GV>, dim3(blocks), dim3(kWarps * 32), kTcSmemSplit, stream, a))
     switch (G) {
       case 1: GB_TC(1, 0); break;
       case 2: GB_TC(2, 1); break;

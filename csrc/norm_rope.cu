@@ -173,17 +173,13 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
             x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
           }
           if (dlb != nullptr) {
+            // B^T [r, H]: rank row j holds the 8 columns of this chunk contiguously
+            for (int j = 0; j < dlr; ++j) {
+              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(dlb + static_cast<long>(j) * ldb + col));
+              const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+              const float u = dus[j];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const uint4* br = reinterpret_cast<const uint4*>(dlb + static_cast<long>(col + e) * ldb);
-              float acc = 0.f;
-              for (int j8 = 0; j8 < dlr; j8 += 8) {
-                const uint4 raw = __ldg(br + j8 / 8);
-                const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) acc += __bfloat162float(bb[q]) * dus[j8 + q];
-              }
-              x[c][e] += acc;
+              for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(bb[e]) * u;
             }
           }
           *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -233,11 +229,11 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int j0 = 0; j0 < R; j0 += 64) {
       const int jn = min(64, R - j0);
-      for (int j = 0; j < jn; j += 8) {
-        // 8 rank rows per pass: their loads are issued together
-        float p[8];
+      for (int j = 0; j < jn; j += 16) {
+        // 16 rank rows per pass: their loads are issued together
+        float p[16];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < 16; ++jj) {
           p[jj] = 0.f;
           if (j + jj < jn) {
             const __nv_bfloat16* arow = lora_a + static_cast<long>(j0 + j + jj) * H;
@@ -254,7 +250,7 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
           }
         }
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
+        for (int jj = 0; jj < 16; ++jj) {
           const float v = warp_sum(p[jj]);
           if (lane == 0 && j + jj < jn) ured[warp][j + jj] = v;
         }
@@ -370,7 +366,7 @@ struct RopeArgs {
   // LoRA on q/k/v computed by the projection GEMM itself: the fp32 workspace
   // row holds, after the (nq + 2 nkv) * D projection columns, U = s * A x in
   // u_width columns (q, k, v blocks of lora_r each); this kernel adds B U
-  // (B block-diagonal [(nq + 2 nkv) * D, ldb]) and zeroes U for the next step.
+  // (lora_b = B^T [3 r, (nq + 2 nkv) * D] of the block-diagonal q/k/v B).
   const __nv_bfloat16* lora_b;
   int ldb, lora_r, u_width;
 };
@@ -404,18 +400,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
     if (lora) {
       const int blk = hd < a.nq ? 0 : (hd < a.nq + a.nkv ? 1 : 2);
       const float* u = us + blk * a.lora_r;  // L1/L2-served broadcast reads
+      // B^T [3r, W]: rank row (blk r + j) holds this lane's 4 columns contiguously
+      for (int j = 0; j < a.lora_r; ++j) {
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(
+            a.lora_b + static_cast<long>(blk * a.lora_r + j) * a.ldb + hd * D + lane * 4));
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+        const float uj = u[j];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint4* br = reinterpret_cast<const uint4*>(
-            a.lora_b + static_cast<long>(hd * D + lane * 4 + e) * a.ldb + blk * a.lora_r);
-        float acc = 0.f;
-        for (int j8 = 0; j8 < a.lora_r; j8 += 8) {
-          const uint4 raw = __ldg(br + j8 / 8);
-          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) acc += __bfloat162float(bb[q]) * u[j8 + q];
-        }
-        x[e] += acc;
+        for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]) * uj;
       }
     }
 #pragma unroll
@@ -698,9 +690,9 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
     dlb = reinterpret_cast<const __nv_bfloat16*>(delta_lora_b->data_ptr());
     ldb = static_cast<int>(delta_lora_b->size(1));
     dlr = static_cast<int>(delta_lora_r);
-    TORCH_CHECK(delta_lora_b->size(0) == H && dlr % 8 == 0 && dlr <= 64 && dlr <= ldb && ldb % 8 == 0 &&
+    TORCH_CHECK(delta_lora_b->size(1) == H && delta_lora_b->size(0) >= dlr && dlr <= 64 && ldb % 8 == 0 &&
                     delta->size(-1) >= H + dlr,
-                "delta LoRA: B must be [H, >= r], r a multiple of 8 and <= 64, U after the H delta columns");
+                "delta LoRA: B^T must be [>= r, H] with r <= 64, U after the H delta columns");
   }
   PeerSum ps{};
   if (peer_src.has_value() && peer_src->defined()) {
@@ -802,9 +794,10 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
     a.ldb = static_cast<int>(lora_b->size(1));
     a.lora_r = static_cast<int>(lora_r);
     a.u_width = static_cast<int>(qkv.size(1) - (nq + 2 * nkv) * 128);
-    TORCH_CHECK(lora_r % 8 == 0 && 3 * lora_r <= a.u_width && 3 * lora_r <= 192 && a.ldb % 8 == 0,
-                "LoRA rank must be a multiple of 8, at most 64, with U columns after the projection");
-    TORCH_CHECK(lora_b->size(0) == (nq + 2 * nkv) * 128, "lora_b rows must match the projection width");
+    TORCH_CHECK(3 * lora_r <= a.u_width && lora_r <= 64 && a.ldb % 4 == 0,
+                "LoRA rank at most 64, with U columns after the projection");
+    TORCH_CHECK(lora_b->size(1) == (nq + 2 * nkv) * 128 && lora_b->size(0) >= 3 * lora_r,
+                "lora_b must be B^T [3r, projection width]");
   }
   const long warps = static_cast<long>(a.T) * (nq + 2 * nkv);
   if (warps > 0)

@@ -61,10 +61,11 @@ def _sync(dev: torch.device) -> None:
 
 
 def decode_attention_splits(rows: int, nkv: int, capacity: int, sms: int = 148) -> int:
-    """Key-range splits so decode attention launches about 4 CTAs per SM."""
+    """Key-range splits so the split kernel (two resident CTAs per SM) fills the GPU
+    once; each split keeps at least four 64-key tiles."""
     ctas = rows * nkv
-    want = max(1, -(-4 * sms // max(ctas, 1)))
-    return int(max(1, min(want, capacity // 128, 16)))
+    want = max(1, -(-2 * sms // max(ctas, 1)))
+    return int(max(1, min(want, capacity // 256, 16)))
 
 
 def _round_up(x: int, m: int) -> int:
@@ -346,12 +347,20 @@ class FusedRolloutEngine:
         m = self.m
         tails = self._lora_tails()
         m.ensure_tail_rows({k: v for k, v in tails.items() if k.startswith("w_")})
+        r = m.lora.r
+        self._bt = {}
         for lw in m.layers:
             L = m.lora.layer_layouts(lw.index, m.sizes)
             for name, key in (("w_qkv", "a_qkv"), ("w_o", "a_o"), ("w_down", "a_down")):
                 if key in L:
                     ext = getattr(lw, f"{name}_ext")
                     ext[getattr(lw, name).shape[0]:].copy_(L[key])
+            # B^T layouts for the consumer kernels' B U (rank rows contiguous over features)
+            self._bt[lw.index] = {
+                "qkv": L["b_qkv"][:, : 3 * r].t().contiguous() if "b_qkv" in L else None,
+                "o": L["b_o"][:, :r].t().contiguous() if "b_o" in L else None,
+                "down": L["b_down"][:, :r].t().contiguous() if "b_down" in L else None,
+            }
         return tails
 
     def _peer_site(self, name: str, rows: int, width: int):
@@ -423,6 +432,7 @@ class FusedRolloutEngine:
         b_down_prev = None
         for li, lw in enumerate(m.layers):
             L = m.lora.layer_layouts(lw.index, m.sizes)
+            BT = self._bt[lw.index]
             first = li == 0
             # x_a holds the residual stream; the previous layer's down-projection
             # partial sums (d_ws, with its LoRA U) are added here, the sum stored to x_a
@@ -434,7 +444,7 @@ class FusedRolloutEngine:
                  splits=3)
             C.qk_norm_rope(b["qkv_ws"], lw.q_norm, lw.k_norm, m.inv_freq, st["pos"], b["q"], self.k_pool[li],
                            self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps,
-                           L.get("b_qkv"), r if has_qkv else 0)
+                           BT["qkv"], r if has_qkv else 0)
             C.paged_decode_attention(b["q"], self.k_pool[li], self.v_pool[li], bt, st["start"], st["kv_len"],
                                      b["attn"], scale, self._splits, b["attn_scratch"], self._prefix, self._group,
                                      self._prefix_splits)
@@ -449,7 +459,7 @@ class FusedRolloutEngine:
             # this kernel also clears the q/k/v LoRA U columns read by qk_norm_rope
             C.add_rmsnorm(b["x_a"], b["o_ws"], b["x_b"], lw.ln2, b["xn"], None,
                           a_gu[: 2 * r] if a_gu is not None else None, ug, 1.0, eps,
-                          L.get("b_o"), r if has_o else 0, **o_norm,
+                          BT["o"], r if has_o else 0, **o_norm,
                           zero_tail=b["qkv_u"] if has_qkv else None)
             gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
                  swap=True, epilogue="swiglu")
@@ -458,7 +468,7 @@ class FusedRolloutEngine:
                  splits=4, push=sd)
             if tp > 1 and sd is None:
                 dist.all_reduce(b["d_ws"], group=tp_group)
-            b_down_prev = L.get("b_down")
+            b_down_prev = BT["down"]
         ran = len(m.layers) > 0  # a stage may hold only the LM head
         if not m.include_head:
             # stage boundary: materialise the residual stream (x_b + down output)

@@ -83,9 +83,9 @@ def add_rmsnorm(h, delta, h_out, w, y, rstd, lora_a, lora_u, scale, eps, delta_l
     H = h.shape[-1]
     if delta is not None:
         d = _f(delta[..., :H])
-        if delta_lora_b is not None:
+        if delta_lora_b is not None:  # B^T [r, H]
             u = _f(delta[..., H : H + delta_lora_r])
-            d = d + u @ _f(delta_lora_b[:, :delta_lora_r]).T
+            d = d + u @ _f(delta_lora_b[:delta_lora_r])
         x = x + d
         x = x.to(torch.bfloat16).float() if h.dtype == torch.bfloat16 else x
         h_out.copy_(x.to(h_out.dtype))
@@ -130,9 +130,9 @@ def qk_norm_rope(qkv, q_w, k_w, inv_freq, pos, q_out, k_out, v_out, block_table,
     D = q_out.shape[-1]
     W = (nq + 2 * nkv) * D
     x = _f(qkv[:, :W])
-    if lora_b is not None:
+    if lora_b is not None:  # B^T [3r, W] of the block-diagonal B
         u = _f(qkv[:, W : W + 3 * lora_r])
-        x = x + u @ _f(lora_b[:, : 3 * lora_r]).T
+        x = x + u @ _f(lora_b[: 3 * lora_r])
     x = x.view(T, nq + 2 * nkv, D)
     if qkv.dtype == torch.float32:
         x = x.to(torch.bfloat16).float()
