@@ -37,6 +37,8 @@ void gated_delta_step(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale);
+void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err);
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
                     torch::Tensor end, int64_t B, int64_t S, double scale);
@@ -96,6 +98,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("prefix_splits") = 1);
   m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
   m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
+  m.def("flash_attn_fwd_tc", &gb::flash_attn_fwd_tc, "causal flash attention forward on tcgen05 / TMEM");
   m.def("sample_append", &gb::sample_append);
   m.def("lse_combine", &gb::lse_combine);
   m.def("grpo_loss", &gb::grpo_loss);

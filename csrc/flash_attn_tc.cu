@@ -1,0 +1,365 @@
+// Flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same contract as flash_attn_fwd (csrc/flash_attn.cu): q [T, nq, 128], k / v
+// [T, nkv, 128] bf16, T = B * S tokens, row b attends causally inside its
+// valid range [start[b], end[b]); outputs O (bf16) and the row log-sum-exp
+// (log2 domain).  CTA = 128 query rows of one head, key tiles of 128.
+//
+// Warp roles (192 threads):
+//   warp 0     TMA producer: Q once, then K and V tiles into 2-stage rings;
+//   warp 1     TMEM owner (512 columns: S double buffer at 0 / 128, O at 256)
+//              and MMA issuer: S_j = Q K_j^T (M=128, N=128, K=128) into
+//              S[j % 2], then O += P_{j-1} V_{j-1} (A = P from shared memory,
+//              B = V read MN-major) -- so QK^T of tile j overlaps the softmax
+//              of tile j-1;
+//   warps 2-5  softmax: thread = query row (its TMEM lane): load the S row,
+//              mask, online max / sum in the log2 domain, write P (bf16) into a
+//              128B-swizzled K-major tile; O is rescaled in TMEM only when the
+//              running max grows by more than 2^8 (otherwise the stale max is
+//              kept: P stays <= 256, exact in fp32 accumulation), and
+//              normalised once at the end.
+// Every wait is bounded (an error word is set and the kernel drains).
+
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "sm100_common.cuh"
+
+namespace gb {
+
+CUtensorMap make_tmap_bf16(const void* ptr, long rows, long cols, long ld, int box_rows);
+
+namespace {
+
+constexpr int kBM = 128;           // query rows per CTA
+constexpr int kBN = 128;           // keys per tile
+constexpr int kHD = 128;           // head dim
+constexpr int kAtom = kBM * 128;   // one 128-row x 128-byte swizzle-atom column: 16 KiB
+constexpr int kTile = 2 * kAtom;   // 128 rows x 128 bf16: 32 KiB
+constexpr int kStages = 2;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;
+
+// smem layout (offsets from a 1024-aligned base)
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTile;
+constexpr int kOffV = kOffK + kStages * kTile;
+constexpr int kOffP = kOffV + kStages * kTile;
+constexpr int kOffBar = kOffP + kTile;
+constexpr int kSmem = kOffBar + 256 + 1024;
+
+struct FwdTcArgs {
+  __nv_bfloat16* o;
+  float* lse;
+  const int *start, *end;
+  int S, nq, nkv;
+  float scale_log2;
+  int* err;
+};
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, FwdTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kOffBar);
+  uint64_t* q_full = bar + 0;
+  uint64_t* k_full = bar + 1;    // [2]
+  uint64_t* k_empty = bar + 3;   // [2]
+  uint64_t* v_full = bar + 5;    // [2]
+  uint64_t* v_empty = bar + 7;   // [2]
+  uint64_t* s_full = bar + 9;    // [2]
+  uint64_t* s_free = bar + 11;   // [2]
+  uint64_t* p_full = bar + 13;
+  uint64_t* o_done = bar + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // heaviest (latest) query blocks first
+  const int qb = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int G = a.nq / a.nkv, hk = h / G;
+  const int q0 = qb * kBM;
+  const int s0 = a.start[b], s1 = a.end[b];
+  const int q_last = min(q0 + kBM, s1) - 1;
+  const bool any = q_last >= s0 && q0 < s1;
+  const int j_first = any ? s0 / kBN : 0;
+  const int j_last = any ? q_last / kBN : -1;
+  const int n_tiles = j_last - j_first + 1;
+  const long tok0 = static_cast<long>(b) * a.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(k_full + i, 1);
+      mbar_init(k_empty + i, 1);
+      mbar_init(v_full + i, 1);
+      mbar_init(v_empty + i, 1);
+      mbar_init(s_full + i, 1);
+      mbar_init(s_free + i, 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_addr(sm + kOffQ), sK = smem_addr(sm + kOffK), sV = smem_addr(sm + kOffV),
+                 sP = smem_addr(sm + kOffP);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, kTile);
+      for (int c = 0; c < 2; ++c)
+        tma_load_2d(sm + kOffQ + c * kAtom, &tmQ, q_full, h * kHD + c * 64, static_cast<int>(tok0 + q0));
+      for (int i = 0; i < n_tiles; ++i) {
+        const int st = i & 1;
+        const int key0 = (j_first + i) * kBN;
+        if (i >= 2 && !mbar_wait(k_empty + st, ((i - 2) >> 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(k_full + st, kTile);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sm + kOffK + st * kTile + c * kAtom, &tmK, k_full + st, hk * kHD + c * 64,
+                      static_cast<int>(tok0 + key0));
+        if (i >= 2 && !mbar_wait(v_empty + st, ((i - 2) >> 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(v_full + st, kTile);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sm + kOffV + st * kTile + c * kAtom, &tmV, v_full + st, hk * kHD + c * 64,
+                      static_cast<int>(tok0 + key0));
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_qk = umma_idesc_bf16(kBM, kBN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(kBM, kHD, false, true);
+      const uint32_t o_tmem = tmem + 256;
+      bool ok = mbar_wait(q_full, 0, a.err, kErrTmaFullTimeout);
+      auto mma_pv = [&](int t) {
+        if (!ok) return;
+        ok = mbar_wait(p_full, t & 1, a.err, kErrTmaFullTimeout) &&
+             mbar_wait(v_full + (t & 1), (t >> 1) & 1, a.err, kErrTmaFullTimeout);
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t vbase = sV + (t & 1) * kTile;
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          // A = P (K-major: key atom k / 4, +32 B per 16 keys inside it)
+          const uint64_t pd = umma_desc_k_sw128(sP + (k >> 2) * kAtom) + 2 * (k & 3);
+          // B = V (MN-major: head-dim atom columns 16 KiB apart, 16-key step = two 8-row groups)
+          const uint64_t vd = umma_desc_mn_sw128(vbase + k * 2048, kAtom, 1024);
+          umma_bf16(o_tmem, pd, vd, idesc_pv, (t > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(v_empty + (t & 1));
+        umma_commit(o_done);
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int st = i & 1;
+        ok = mbar_wait(k_full + st, (i >> 1) & 1, a.err, kErrTmaFullTimeout);
+        if (ok && i >= 2) ok = mbar_wait(s_free + st, ((i - 2) >> 1) & 1, a.err, kErrTmemEmptyTimeout);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t kbase = sK + st * kTile;
+#pragma unroll
+        for (int k = 0; k < kHD / 16; ++k) {
+          const uint64_t qd = umma_desc_k_sw128(sQ + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t kd = umma_desc_k_sw128(kbase + (k >> 2) * kAtom) + 2 * (k & 3);
+          umma_bf16(tmem + st * kBN, qd, kd, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(k_empty + st);
+        umma_commit(s_full + st);
+        if (i >= 1) mma_pv(i - 1);
+      }
+      mma_pv(n_tiles - 1);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;          // query row inside the tile (TMEM lane)
+    const int qi = q0 + r;
+    const bool row_ok = qi >= s0 && qi < s1 && qi < a.S;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n_tiles && ok; ++i) {
+      const int st = i & 1;
+      const int key0 = (j_first + i) * kBN;
+      // warp-uniform decisions: tcgen05.ld / st are warp-collective
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, a.err, kErrTmemFullTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + st * kBN + c * 32, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[c * 32 + e] = v[e];
+      }
+      tc_fence_before();
+      mbar_arrive(s_free + st);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < kBN; ++e) {
+        const int kj = key0 + e;
+        const bool keep = row_ok && kj >= s0 && kj < s1 && kj <= qi;
+        s[e] = keep ? s[e] * a.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[e]);
+      }
+      const float m_new = fmaxf(m, mx);
+      float alpha = 1.f;
+      const bool need = m != -INFINITY && m_new > m + kRescaleLog2;
+      if (m == -INFINITY) {
+        m = m_new;                               // first finite max: nothing accumulated yet
+      } else if (need) {
+        alpha = exp2f(m - m_new);
+        m = m_new;
+      }
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float ps = 0.f;
+#pragma unroll
+      for (int e = 0; e < kBN; ++e) {
+        s[e] = (m == -INFINITY) ? 0.f : exp2f(s[e] - m);
+        ps += s[e];
+      }
+      l = l * alpha + ps;
+      // P(i) overwrites P(i-1) and O may be rescaled: O += P(i-1) V(i-1) must be done
+      if (i >= 1) {
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1, a.err, kErrTmemFullTimeout));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (rescale && i >= 1) {
+#pragma unroll
+        for (int c = 0; c < kHD / 32; ++c) {
+          float v[32];
+          tmem_ld32(tmem + lane_off + 256 + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= alpha;
+          tmem_st32(tmem + lane_off + 256 + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      // P row -> K-major 128B-swizzled tile (two 64-key atom columns)
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c) {
+        const int atom = c >> 3, ch = c & 7;
+        const uint32_t addr = sP + atom * kAtom + (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4);
+        const uint32_t w0 = pack2(s[c * 8 + 0], s[c * 8 + 1]), w1 = pack2(s[c * 8 + 2], s[c * 8 + 3]);
+        const uint32_t w2 = pack2(s[c * 8 + 4], s[c * 8 + 5]), w3 = pack2(s[c * 8 + 6], s[c * 8 + 7]);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                     : "memory");
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- epilogue: O / l -> bf16, log-sum-exp
+    if (n_tiles > 0 && ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, a.err, kErrTmemFullTimeout));
+      tc_fence_after();
+    }
+    const bool valid = row_ok && n_tiles > 0 && ok && l > 0.f;
+    const float inv = valid ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = a.o + ((tok0 + min(qi, a.S - 1)) * a.nq + h) * kHD;
+#pragma unroll
+    for (int c = 0; c < kHD / 32; ++c) {
+      float v[32];
+      if (n_tiles > 0 && ok) {
+        tmem_ld32(tmem + lane_off + 256 + c * 32, v);   // every lane of the warp takes part
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0.f;
+      }
+      if (qi < a.S) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 pkt;
+          pkt.x = pack2(valid ? v[q4 * 8 + 0] * inv : 0.f, valid ? v[q4 * 8 + 1] * inv : 0.f);
+          pkt.y = pack2(valid ? v[q4 * 8 + 2] * inv : 0.f, valid ? v[q4 * 8 + 3] * inv : 0.f);
+          pkt.z = pack2(valid ? v[q4 * 8 + 4] * inv : 0.f, valid ? v[q4 * 8 + 5] * inv : 0.f);
+          pkt.w = pack2(valid ? v[q4 * 8 + 6] * inv : 0.f, valid ? v[q4 * 8 + 7] * inv : 0.f);
+          *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = pkt;
+        }
+      }
+    }
+    if (qi < a.S) a.lse[(tok0 + qi) * a.nq + h] = valid ? m + log2f(l) : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
+                       torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && out.is_contiguous(), "contiguous inputs");
+  TORCH_CHECK(q.size(-1) == kHD && q.scalar_type() == torch::kBFloat16, "bf16 q/k/v with head_dim 128");
+  const long T = q.size(0);
+  const int nq = static_cast<int>(q.size(1)), nkv = static_cast<int>(k.size(1));
+  FwdTcArgs a{};
+  a.o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.start = start.data_ptr<int>();
+  a.end = end.data_ptr<int>();
+  a.S = static_cast<int>(S);
+  a.nq = nq;
+  a.nkv = nkv;
+  a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
+  a.err = err.data_ptr<int>();
+  CUtensorMap tq = make_tmap_bf16(q.data_ptr(), T, static_cast<long>(nq) * kHD, static_cast<long>(nq) * kHD, kBM);
+  CUtensorMap tk = make_tmap_bf16(k.data_ptr(), T, static_cast<long>(nkv) * kHD, static_cast<long>(nkv) * kHD, kBN);
+  CUtensorMap tv = make_tmap_bf16(v.data_ptr(), T, static_cast<long>(nkv) * kHD, static_cast<long>(nkv) * kHD, kBN);
+  static bool configured[64] = {};
+  const int dev = q.get_device();
+  if (!configured[dev]) {
+    cudaFuncSetAttribute(flash_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    configured[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((S + kBM - 1) / kBM), static_cast<unsigned>(nq), static_cast<unsigned>(B));
+  flash_fwd_tc_kernel<<<grid, kThreads, kSmem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace gb

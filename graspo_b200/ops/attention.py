@@ -8,8 +8,10 @@ Padding queries produce zero output and receive zero gradient; nothing
 downstream consumes them (loss masks exclude them and no valid query attends
 to a padding key).
 
-The forward kernel also returns the per-(token, head) log-sum-exp (log2
-domain, fp32), which the backward kernel uses to rebuild the probabilities
+The forward runs on the tcgen05 kernel (csrc/flash_attn_tc.cu: S, P and O in
+TMEM / swizzled shared memory, TMA-fed K/V rings); the backward on the
+mma.sync kernel (csrc/flash_attn.cu).  The forward also returns the
+per-(token, head) log-sum-exp (log2 domain, fp32), which the backward kernel uses to rebuild the probabilities
 without a second softmax pass (FlashAttention-2, Dao 2023).  GQA is handled
 inside the kernels: a query head reads KV head ``h // (nq // nkv)``, and the
 backward kernel sums the G query heads' contributions to dK/dV in registers.
@@ -20,7 +22,12 @@ from __future__ import annotations
 
 import torch
 
-from graspo_b200.ops._ext import ext
+import os
+
+from graspo_b200.ops._ext import err_word, ext
+
+# forward on the tcgen05 kernel (S / P / O in TMEM); GRASPO_FA_TC=0 selects the mma.sync kernel
+USE_TC_FORWARD = os.environ.get("GRASPO_FA_TC", "1") != "0"
 
 
 def row_ranges(meta) -> tuple[torch.Tensor, torch.Tensor]:
@@ -51,8 +58,12 @@ def attention_forward(q, k, v, meta, scale: float, need_ctx: bool = False):
     start, end = row_ranges(meta)
     out = torch.empty(T, nq * D, device=q.device, dtype=q.dtype)
     lse = torch.empty(T, nq, device=q.device, dtype=torch.float32)
-    ext().flash_attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
-                         meta.B, meta.S, float(scale))
+    if USE_TC_FORWARD and q.is_cuda:
+        ext().flash_attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
+                                meta.B, meta.S, float(scale), err_word(q.device))
+    else:
+        ext().flash_attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
+                             meta.B, meta.S, float(scale))
     return out, (lse if need_ctx else None)
 
 

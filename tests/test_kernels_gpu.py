@@ -337,6 +337,27 @@ def _attn_reference(q, k, v, start, end, B, S, scale):
     return out, lse
 
 
+@pytest.mark.parametrize("S,G", [(96, 2), (300, 4), (64, 1), (520, 8)])
+def test_flash_attention_forward_tcgen05(S, G):
+    from graspo_b200.ops._ext import check_errors, err_word
+
+    B, nkv, D = 3, 2, 128
+    nq = nkv * G
+    T = B * S
+    q, k, v = _rand(T, nq, D), _rand(T, nkv, D), _rand(T, nkv, D)
+    start = torch.tensor([0, 17, 5], device="cuda", dtype=torch.int32)
+    end = torch.tensor([S, S, S - 23], device="cuda", dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    out = torch.empty(T, nq, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(T, nq, device="cuda")
+    _ext().flash_attn_fwd_tc(q, k, v, out, lse, start, end, B, S, scale, err_word(q.device))
+    torch.cuda.synchronize()
+    check_errors()
+    ref, ref_lse = _attn_reference(q, k, v, start, end, B, S, scale)
+    _close(out, ref, 2e-2)
+    assert (lse - ref_lse).abs().max().item() < 2e-2
+
+
 @pytest.mark.parametrize("S,G", [(96, 2), (200, 4), (64, 1)])
 def test_flash_attention_forward_backward(S, G):
     B, nkv, D = 3, 2, 128
