@@ -150,7 +150,7 @@ def bench_step(args) -> None:
     model = _step_model(args)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 150000, (args.prompt_len,), generator=g).tolist() for _ in range(args.prompts)]
-    for graph, prefix in ((True, True), (True, False), (False, True)):
+    for graph, prefix in ((True, False), (True, True), (False, False)):
         eng = FusedRolloutEngine(model, FusedQwen3(model), page_size=64, use_graph=graph)
         eng.nvtx = not graph
         eng.prefix_attention = prefix
@@ -288,7 +288,7 @@ def bench_profile(args) -> None:
         scratch = torch.zeros(rows * nq * 12 * (D + 2) + rows * nkv, device="cuda")
         runs.append(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), 4, scratch,
                                                          P, G, 2))
-    elif k in ("flash_fwd", "flash_bwd"):
+    elif k in ("flash_fwd", "flash_bwd", "flash_fwd_tc"):
         B, S, nq, nkv, D = 4, 3072, 32, 8, 128
         T = B * S
         q = torch.randn(T, nq, D, device="cuda").bfloat16()
@@ -301,6 +301,11 @@ def bench_profile(args) -> None:
         ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D))
         if k == "flash_fwd":
             runs.append(lambda: ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D)))
+        elif k == "flash_fwd_tc":
+            from graspo_b200.ops._ext import err_word
+
+            runs.append(lambda: ext().flash_attn_fwd_tc(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D),
+                                                        err_word(q.device)))
         else:
             do = torch.randn_like(q)
             dq, dk, dv = torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)

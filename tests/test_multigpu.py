@@ -151,3 +151,59 @@ def test_tp2_fused_matches_tp1(tmp_path):
 
     path = write_qwen3_checkpoint(tmp_path / "small", SMALL, seed=4, std=0.05, with_tokenizer=False)
     run_world(2, _worker, path, timeout=600)
+
+
+def _pp_worker(rank, world, path):
+    from graspo_b200.engine.pipeline import pp_logprobs
+    from graspo_b200.engine.rollout import FusedRolloutEngine
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.fused import FusedQwen3
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import Qwen3Model
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.p2p import StageComm
+    from graspo_b200.parallel.state import ParallelState
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ps = pstate.initialize(1, 2, 0, timeout_sec=120)
+    comm = StageComm(ps)
+
+    def build(ps_, layers, embed, head):
+        return Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps_, local_layers=layers,
+                          include_embed=embed, include_head=head, lora_targets=TARGETS, lora_r=8, lora_alpha=16,
+                          lora_dropout=0.0, dtype=torch.bfloat16, device=ps.device, seed=3)
+
+    stage = build(ps, [0] if rank == 0 else [1], rank == 0, rank == 1)
+    ref = build(ParallelState(device=ps.device), [0, 1], True, True)
+    g = torch.Generator().manual_seed(0)
+    seq = torch.randint(0, 4088, (3, 96), generator=g).cuda()
+    mask = torch.ones(3, 96, dtype=torch.bool, device="cuda")
+    mask[1, :17] = False
+    lp = pp_logprobs(FusedQwen3(stage), comm, seq, mask, seq[:, 1:], chunk_rows=1)
+    f = FusedQwen3(ref)
+    from graspo_b200.models.fused import AttnMeta
+
+    x, _ = f.stage_forward(f.embed(seq), AttnMeta.from_mask(mask))
+    hn, _ = f.final_norm(x)
+    tgt = torch.zeros_like(seq)
+    tgt[:, :-1] = seq[:, 1:]
+    lp_ref = f.token_logprobs(hn, tgt.reshape(-1))[0].view(seq.shape)[:, :-1]
+    valid = mask[:, :-1] & mask[:, 1:]
+    assert (lp - lp_ref).abs()[valid].max().item() < 0.08
+    kw = dict(group_size=2, max_new_tokens=12, temperature=1.0, top_p=1.0, eos_id=4095, pad_id=4095,
+              ignore_eos=True, seed=7)
+    prompts = [[5, 6, 7], list(range(20, 90))]
+    got = FusedRolloutEngine(stage, FusedQwen3(stage), page_size=64, comm=comm).generate(prompts, **kw)
+    toks = got.tokens.cuda()
+    other = toks.clone()
+    torch.distributed.broadcast(other, src=1)
+    assert torch.equal(toks, other), "pipeline stages disagree on the sampled tokens"
+    pstate.destroy()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_pipeline_two_stages_on_gpus(tmp_path):
+    from graspo_b200.utils.synth import write_qwen3_checkpoint
+
+    path = write_qwen3_checkpoint(tmp_path / "pp", SMALL, seed=4, std=0.05, with_tokenizer=False)
+    run_world(2, _pp_worker, path, timeout=600)
