@@ -225,12 +225,23 @@ def load_jsonl(path: str | Path) -> list[Sample]:
     return samples
 
 
+def sample_to_record(sample: Sample) -> dict[str, Any]:
+    """The JSONL record that ``sample_from_record`` turns back into ``sample``:
+    metadata keys return to the top level and media (derived from the
+    messages) is not written."""
+    record: dict[str, Any] = {"messages": sample.messages, "targets": sample.targets}
+    if sample.tools is not None:
+        record["tools"] = sample.tools
+    record.update(sample.metadata or {})
+    return record
+
+
 def write_jsonl(samples: list[Sample], path: str | Path) -> None:
     out = Path(path)
     out.parent.mkdir(parents=True, exist_ok=True)
     with out.open("w", encoding="utf-8") as handle:
         for sample in samples:
-            handle.write(sample.to_json() + "\n")
+            handle.write(json.dumps(sample_to_record(sample), ensure_ascii=False) + "\n")
 
 
 # --------------------------------------------------------------------------
