@@ -88,6 +88,23 @@ class LayerSaved:
                  "x1", "xn2", "rstd2", "xd2", "u_gu", "gu", "act", "act_d", "u_d", "attn_ctx")
 
 
+class AttnCache:
+    """A layer's q/k/v projection output, attention output and log-sum-exp kept
+    from the training forward, so the backward's recompute skips the q/k/v GEMM
+    and the flash-attention forward (they are the same values)."""
+
+    __slots__ = ("qkv", "attn", "lse")
+
+    def __init__(self) -> None:
+        self.qkv = self.attn = self.lse = None
+
+
+def _cache_attention_mode() -> str:
+    import os
+
+    return os.environ.get("GRASPO_CACHE_ATTN", "auto").strip().lower()
+
+
 class FusedQwen3:
     """Kernel-path forward / backward of the Qwen3 decoder.
 
@@ -135,7 +152,12 @@ class FusedQwen3:
 
     # ------------------------------------------------------------ forward
     def layer_forward(self, lw: LayerWeights, x: torch.Tensor, meta: AttnMeta, *, train: bool = False,
-                      seed: int = 0, save: bool = False, kv_sink=None):
+                      seed: int = 0, save: bool = False, kv_sink=None, keep: AttnCache | None = None,
+                      cache: AttnCache | None = None, need_out: bool = True):
+        """One decoder layer.  ``keep`` receives this forward's attention values;
+        ``cache`` supplies them instead of recomputing (backward recompute);
+        ``need_out=False`` skips the down projection, whose output the backward
+        does not read (its inputs are saved)."""
         m, C, L = self.m, self.C, self._layouts(lw)
         tp_group = m.ps.tp_group
         tp = m.ps.tp_size
@@ -152,7 +174,7 @@ class FusedQwen3:
             xd = self._dropout(xn, "qkv", lw.index, seed, train)
             u_qkv = gemm(xd, L["a_qkv"], bn=64)
             ext_qkv = (u_qkv, L["b_qkv"])
-        qkv = gemm(xn, lw.w_qkv, ext_ab=ext_qkv)
+        qkv = cache.qkv if cache is not None else gemm(xn, lw.w_qkv, ext_ab=ext_qkv)
         q = torch.empty(T, m.nq, m.D, device=x.device, dtype=xn.dtype)
         k = torch.empty(T, m.nkv, m.D, device=x.device, dtype=xn.dtype)
         v = torch.empty_like(k)
@@ -160,7 +182,12 @@ class FusedQwen3:
                        self.eps)
         if kv_sink is not None:
             kv_sink(lw.index, k, v)
-        attn, ctx = attn_ops.attention_forward(q, k, v, meta, self.scale, need_ctx=save)
+        if cache is not None:
+            attn, ctx = cache.attn, cache.lse
+        else:
+            attn, ctx = attn_ops.attention_forward(q, k, v, meta, self.scale, need_ctx=save or keep is not None)
+        if keep is not None:
+            keep.qkv, keep.attn, keep.lse = qkv, attn, ctx
         ext_o = None
         if "a_o" in L:
             attn_d = self._dropout(attn, "o", lw.index, seed, train)
@@ -190,7 +217,9 @@ class FusedQwen3:
             act_d = self._dropout(act, "down", lw.index, seed, train)
             u_d = gemm(act_d, L["a_down"], bn=64)
             ext_d = (u_d, L["b_down"])
-        if tp == 1:
+        if not need_out:
+            x2 = None  # every TP rank skips the same GEMM and collective
+        elif tp == 1:
             x2 = gemm(act, lw.w_down, ext_ab=ext_d, residual=x1)
         else:
             d = gemm(act, lw.w_down, ext_ab=ext_d)
@@ -314,22 +343,61 @@ class FusedQwen3:
         self.C.embedding(ids.reshape(-1).contiguous(), self.m.embed, out)
         return out
 
+    def attention_cache_bytes(self, tokens: int) -> int:
+        """Device bytes that caching every local layer's attention values costs
+        for ``tokens`` (this rank's q/k/v width and query heads)."""
+        m = self.m
+        qkv_w = (m.nq + 2 * m.nkv) * m.D
+        per_token = 2 * qkv_w + 2 * m.nq * m.D + 4 * m.nq
+        return len(m.layers) * tokens * per_token
+
+    def _cache_attention(self, tokens: int, device: torch.device) -> bool:
+        mode = _cache_attention_mode()
+        if mode in ("0", "off", "false") or not self.m.layers:
+            return False
+        if mode in ("1", "on", "true"):
+            return True
+        if device.type != "cuda":
+            return False
+        free, _ = torch.cuda.mem_get_info(device)
+        free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+        m = self.m
+        # head-room for one layer's backward: its saved activations and gradients
+        per_layer_bwd = tokens * 2 * (6 * m.cfg.hidden_size + 4 * (m.nq + 2 * m.nkv) * m.D + 6 * m.inter_local)
+        return free > self.attention_cache_bytes(tokens) + 2 * per_layer_bwd + (4 << 30)
+
     def stage_forward(self, x: torch.Tensor, meta: AttnMeta, *, train=False, seed=0, keep_inputs=False):
-        """Run this rank's layers; returns (out, [layer inputs] if keep_inputs)."""
+        """Run this rank's layers; returns (out, [per-layer (input, AttnCache or None)] if keep_inputs).
+
+        With ``keep_inputs`` the attention values are kept for the backward's
+        recompute when they fit in free device memory (``GRASPO_CACHE_ATTN``:
+        ``auto`` (default), ``1`` always, ``0`` never)."""
         inputs = []
+        T = x.shape[0] * (self.m.ps.tp_size if self.sp else 1)
+        cache = keep_inputs and self._cache_attention(T, x.device)
         for lw in self.m.layers:
+            keep = AttnCache() if cache else None
+            x_in = x
+            x, _ = self.layer_forward(lw, x, meta, train=train, seed=seed, keep=keep)
             if keep_inputs:
-                inputs.append(x)
-            x, _ = self.layer_forward(lw, x, meta, train=train, seed=seed)
+                inputs.append((x_in, keep))
         return x, inputs
 
     def stage_backward(self, inputs, dout: torch.Tensor, meta: AttnMeta, *, train=True, seed=0):
-        """Recompute-and-backprop through this rank's layers; returns d(input)."""
+        """Recompute-and-backprop through this rank's layers; returns d(input).
+
+        ``inputs`` (from ``stage_forward``) is consumed: each layer's entry is
+        released once its backward ran."""
         g = dout
-        for lw, x in zip(reversed(self.m.layers), reversed(inputs), strict=True):
-            _, saved = self.layer_forward(lw, x, meta, train=train, seed=seed, save=True)
+        for lw in reversed(self.m.layers):
+            x, cache = inputs.pop()
+            _, saved = self.layer_forward(lw, x, meta, train=train, seed=seed, save=True, cache=cache,
+                                          need_out=False)
+            del x, cache
             g = self.layer_backward(lw, saved, g, meta, train=train, seed=seed)
             del saved
+        if inputs:
+            raise ValueError("stage_backward: more saved inputs than local layers")
         return g
 
     # ------------------------------------------------------------ head

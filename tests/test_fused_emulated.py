@@ -105,3 +105,33 @@ def test_emulated_paged_rollout_matches_eager(model):
     with use_emulation():
         fused = FusedRolloutEngine(model, FusedQwen3(model), page_size=16, use_graph=False).generate(prompts, **kw)
     assert torch.equal(fused.tokens, eager.tokens)
+
+
+def _fused_grads(model, monkeypatch, mode):
+    from graspo_b200.ops._ext import ext
+
+    monkeypatch.setenv("GRASPO_CACHE_ATTN", mode)
+    seq, mask = _batch()
+    B, S = seq.shape
+    w = torch.randn(B, S - 1, generator=torch.Generator().manual_seed(1)) * (mask[:, :-1] & mask[:, 1:])
+    model.lora.grads.zero_()
+    with use_emulation():
+        _, (f, meta, inputs, x, hn, rstd, tgt, lse) = _fused_logprobs(model, seq, mask, train=True)
+        cached = [c is not None for _, c in inputs]
+        g = torch.zeros(B, S)
+        g[:, :-1] = w
+        dhn = f.token_logprobs_backward(hn, tgt.reshape(-1), lse, g.view(-1))
+        dx = torch.empty_like(x)
+        ext().rmsnorm_bwd(dhn, x, model.norm, rstd, None, dx, model.cfg.rms_norm_eps)
+        dx0 = f.stage_backward(inputs, dx, meta, train=True)
+    assert inputs == []  # consumed layer by layer
+    return model.lora.grads.clone(), dx0, cached
+
+
+def test_attention_cache_gives_the_recompute_values(model, monkeypatch):
+    """Keeping q/k/v, attention output and LSE from the forward (instead of
+    recomputing them in the backward) changes no gradient."""
+    ref, dref, cached_ref = _fused_grads(model, monkeypatch, "0")
+    got, dgot, cached = _fused_grads(model, monkeypatch, "1")
+    assert not any(cached_ref) and all(cached)
+    assert torch.equal(got, ref) and torch.equal(dgot, dref)
