@@ -5,20 +5,29 @@
 // valid range [start[b], end[b]); outputs O (bf16) and the row log-sum-exp
 // (log2 domain).  CTA = 128 query rows of one head, key tiles of 128.
 //
-// Warp roles (192 threads):
+// Warp roles (320 threads):
 //   warp 0     TMA producer: Q once, then K and V tiles into 2-stage rings;
 //   warp 1     TMEM owner (512 columns: S double buffer at 0 / 128, O at 256)
 //              and MMA issuer: S_j = Q K_j^T (M=128, N=128, K=128) into
 //              S[j % 2], then O += P_{j-1} V_{j-1} (A = P from shared memory,
 //              B = V read MN-major) -- so QK^T of tile j overlaps the softmax
 //              of tile j-1;
-//   warps 2-5  softmax: thread = query row (its TMEM lane): load the S row,
-//              mask, online max / sum in the log2 domain, write P (bf16) into a
-//              128B-swizzled K-major tile; O is rescaled in TMEM only when the
-//              running max grows by more than 2^8 (otherwise the stale max is
-//              kept: P stays <= 256, exact in fp32 accumulation), and
-//              normalised once at the end.
-// Every wait is bounded (an error word is set and the kernel drains).
+//   warps 2-9  softmax, two threads per query row: warps w and w + 4 read the
+//              same TMEM lanes (row = their lane) and take 64 of the 128 key
+//              columns each (and 64 of the 128 head-dim columns of O).  The
+//              pair swaps its partial row maxima through shared memory
+//              (barrier.red also agrees on the error state), then each thread
+//              computes p = 2^(s * scale - m) for its half, keeps its own
+//              partial row sum (both halves see the same rescale factors, so
+//              the sums add at the end) and writes its 64-key atom column of P
+//              (bf16, 128B-swizzled K-major).  Only tiles that touch a range
+//              boundary or the causal diagonal evaluate the mask.  O is
+//              rescaled in TMEM only when the running max grows by more than
+//              2^8 (otherwise the stale max is kept: P stays <= 256, exact in
+//              fp32 accumulation), and normalised once at the end.
+// Every wait is bounded (an error word is set and the kernel drains); the
+// pair barriers are reached the same number of times by both warps of a pair
+// on every path.
 
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -38,7 +47,8 @@ constexpr int kHD = 128;           // head dim
 constexpr int kAtom = kBM * 128;   // one 128-row x 128-byte swizzle-atom column: 16 KiB
 constexpr int kTile = 2 * kAtom;   // 128 rows x 128 bf16: 32 KiB
 constexpr int kStages = 2;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;
 
@@ -48,7 +58,8 @@ constexpr int kOffK = kOffQ + kTile;
 constexpr int kOffV = kOffK + kStages * kTile;
 constexpr int kOffP = kOffV + kStages * kTile;
 constexpr int kOffBar = kOffP + kTile;
-constexpr int kSmem = kOffBar + 256 + 1024;
+constexpr int kOffX = kOffBar + 256;          // pair exchange: [2 parity][2 half][128 rows] fp32
+constexpr int kSmem = kOffX + 2 * 2 * kBM * 4 + 1024;
 
 struct FwdTcArgs {
   __nv_bfloat16* o;
@@ -80,6 +91,25 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// barrier over the 64 threads of a softmax warp pair that also ANDs a predicate
+__device__ __forceinline__ bool pair_and(int id, bool p) {
+  uint32_t out;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n"
+      " barrier.red.and.pred po, %2, 64, pi;\n selp.u32 %0, 1, 0, po;\n}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(p)), "r"(id)
+      : "memory");
+  return out != 0;
+}
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = +0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -126,9 +156,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(v_full + i, 1);
       mbar_init(v_empty + i, 1);
       mbar_init(s_full + i, 1);
-      mbar_init(s_free + i, 128);
+      mbar_init(s_free + i, kSoftmaxThreads);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kSoftmaxThreads);
     mbar_init(o_done, 1);
     fence_mbar_init();
   }
@@ -210,77 +240,95 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax / epilogue
+    const int half = (warp - 2) >> 2;           // key / head-dim columns [64 half, 64 half + 64)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;          // query row inside the tile (TMEM lane)
     const int qi = q0 + r;
     const bool row_ok = qi >= s0 && qi < s1 && qi < a.S;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t col0 = static_cast<uint32_t>(half * 64);
+    const int pair_bar = 1 + quarter;           // named barrier of warps (w, w + 4)
+    float* xch = reinterpret_cast<float*>(sm + kOffX);
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int i = 0; i < n_tiles && ok; ++i) {
+    for (int i = 0; i < n_tiles; ++i) {
       const int st = i & 1;
       const int key0 = (j_first + i) * kBN;
-      // warp-uniform decisions: tcgen05.ld / st are warp-collective
-      ok = __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, a.err, kErrTmemFullTimeout));
-      if (!ok) break;
-      tc_fence_after();
-      float s[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        float v[32];
-        tmem_ld32(tmem + lane_off + st * kBN + c * 32, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = v[e];
-      }
-      tc_fence_before();
-      mbar_arrive(s_free + st);
+      // every key of the tile valid and causal for every row of the CTA: no mask
+      // (rows outside the valid range compute values that are never stored)
+      const bool interior = key0 >= s0 && key0 + kBN <= s1 && key0 + kBN - 1 <= q0;
+      bool got = ok && __all_sync(0xffffffffu, mbar_wait(s_full + st, (i >> 1) & 1, a.err, kErrTmemFullTimeout));
+      float s[64];
       float mx = -INFINITY;
+      if (got) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_off + st * kBN + col0, *reinterpret_cast<float(*)[32]>(s));
+        tmem_ld32(tmem + lane_off + st * kBN + col0 + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+        tc_fence_before();
+        mbar_arrive(s_free + st);
+        if (!interior) {
+          const int kb = key0 + half * 64;
 #pragma unroll
-      for (int e = 0; e < kBN; ++e) {
-        const int kj = key0 + e;
-        const bool keep = row_ok && kj >= s0 && kj < s1 && kj <= qi;
-        s[e] = keep ? s[e] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[e]);
+          for (int e = 0; e < 64; ++e) {
+            const int kj = kb + e;
+            if (!(row_ok && kj >= s0 && kj < s1 && kj <= qi)) s[e] = -INFINITY;
+          }
+        }
+        float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int e = 4; e < 64; ++e) m4[e & 3] = fmaxf(m4[e & 3], s[e]);
+        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       }
-      const float m_new = fmaxf(m, mx);
+      xch[((i & 1) * 2 + half) * kBM + r] = mx;
+      ok = pair_and(pair_bar, got);
+      if (!ok) break;
+      mx = fmaxf(mx, xch[((i & 1) * 2 + (half ^ 1)) * kBM + r]);
+      // the log2-domain max is max * scale (scale > 0); both threads of a row
+      // take identical decisions from identical inputs
+      const float m_new = fmaxf(m, mx * a.scale_log2);
       float alpha = 1.f;
       const bool need = m != -INFINITY && m_new > m + kRescaleLog2;
       if (m == -INFINITY) {
         m = m_new;                               // first finite max: nothing accumulated yet
       } else if (need) {
-        alpha = exp2f(m - m_new);
+        alpha = ex2(m - m_new);
         m = m_new;
       }
       const bool rescale = __any_sync(0xffffffffu, need);
-      float ps = 0.f;
+      // a row with no valid key so far has m = -inf and only -inf scores: p = 2^-inf = 0
+      const float neg_m = m == -INFINITY ? 0.f : -m;
+      float p4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < kBN; ++e) {
-        s[e] = (m == -INFINITY) ? 0.f : exp2f(s[e] - m);
-        ps += s[e];
+      for (int e = 0; e < 64; ++e) {
+        s[e] = ex2(fmaf(s[e], a.scale_log2, neg_m));
+        p4[e & 3] += s[e];
       }
-      l = l * alpha + ps;
+      l = l * alpha + ((p4[0] + p4[1]) + (p4[2] + p4[3]));
       // P(i) overwrites P(i-1) and O may be rescaled: O += P(i-1) V(i-1) must be done
+      bool ready = true;
       if (i >= 1) {
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1, a.err, kErrTmemFullTimeout));
-        if (!ok) break;
+        ready = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1, a.err, kErrTmemFullTimeout));
         tc_fence_after();
+      }
+      if (!ready) {
+        ok = false;                              // reported at the next pair barrier (or the epilogue's)
+        continue;
       }
       if (rescale && i >= 1) {
 #pragma unroll
-        for (int c = 0; c < kHD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float v[32];
-          tmem_ld32(tmem + lane_off + 256 + c * 32, v);
+          tmem_ld32(tmem + lane_off + 256 + col0 + c * 32, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] *= alpha;
-          tmem_st32(tmem + lane_off + 256 + c * 32, v);
+          tmem_st32(tmem + lane_off + 256 + col0 + c * 32, v);
         }
         tmem_wait_st();
       }
-      // P row -> K-major 128B-swizzled tile (two 64-key atom columns)
+      // this thread's 64 keys are atom column `half` of the K-major P tile
 #pragma unroll
-      for (int c = 0; c < kBN / 8; ++c) {
-        const int atom = c >> 3, ch = c & 7;
-        const uint32_t addr = sP + atom * kAtom + (r >> 3) * 1024 + (r & 7) * 128 + ((ch ^ (r & 7)) << 4);
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t addr = sP + half * kAtom + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
         const uint32_t w0 = pack2(s[c * 8 + 0], s[c * 8 + 1]), w1 = pack2(s[c * 8 + 2], s[c * 8 + 3]);
         const uint32_t w2 = pack2(s[c * 8 + 4], s[c * 8 + 5]), w3 = pack2(s[c * 8 + 6], s[c * 8 + 7]);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2), "r"(w3)
@@ -290,19 +338,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
-    // ---- epilogue: O / l -> bf16, log-sum-exp
-    if (n_tiles > 0 && ok) {
-      ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, a.err, kErrTmemFullTimeout));
+    // ---- epilogue: O / l -> bf16, log-sum-exp (the pair adds its partial sums)
+    bool got = ok;
+    if (n_tiles > 0 && got) {
+      got = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, a.err, kErrTmemFullTimeout));
       tc_fence_after();
     }
-    const bool valid = row_ok && n_tiles > 0 && ok && l > 0.f;
-    const float inv = valid ? 1.f / l : 0.f;
-    __nv_bfloat16* orow = a.o + ((tok0 + min(qi, a.S - 1)) * a.nq + h) * kHD;
+    xch[((n_tiles & 1) * 2 + half) * kBM + r] = l;
+    got = pair_and(pair_bar, got);
+    const float l_tot = l + xch[((n_tiles & 1) * 2 + (half ^ 1)) * kBM + r];
+    const bool valid = row_ok && n_tiles > 0 && got && l_tot > 0.f;
+    const float inv = valid ? 1.f / l_tot : 0.f;
+    __nv_bfloat16* orow = a.o + ((tok0 + min(qi, a.S - 1)) * a.nq + h) * kHD + col0;
 #pragma unroll
-    for (int c = 0; c < kHD / 32; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float v[32];
-      if (n_tiles > 0 && ok) {
-        tmem_ld32(tmem + lane_off + 256 + c * 32, v);   // every lane of the warp takes part
+      if (n_tiles > 0 && got) {
+        tmem_ld32(tmem + lane_off + 256 + col0 + c * 32, v);   // every lane of the warp takes part
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = 0.f;
@@ -319,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (qi < a.S) a.lse[(tok0 + qi) * a.nq + h] = valid ? m + log2f(l) : 0.f;
+    if (qi < a.S && half == 0) a.lse[(tok0 + qi) * a.nq + h] = valid ? m + log2f(l_tot) : 0.f;
   }
   tc_fence_before();
   __syncthreads();

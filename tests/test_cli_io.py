@@ -148,3 +148,31 @@ def test_fault_injector(monkeypatch):
     inj = FaultInjector(rank=0)
     inj.hit("optimize")
     inj.hit("optimize")  # other rank: never fires
+
+
+def test_every_shipped_config_loads_and_plans(tmp_path, monkeypatch):
+    """Each YAML under configs/ validates against the strict schema and gives a
+    launch plan whose world matches tp x pp x dp (paths made to exist here)."""
+
+    root = Path(__file__).resolve().parents[1] / "configs"
+    files = sorted(root.glob("*.yaml"))
+    assert len(files) >= 6
+    monkeypatch.chdir(tmp_path)
+    data = tmp_path / "train.jsonl"
+    data.write_text(json.dumps({"messages": [{"role": "user", "content": "x"}],
+                                "targets": [{"output": {"content": {"a": 1}}}]}) + "\n")
+    for f in files:
+        raw = yaml.safe_load(f.read_text())
+        raw["data"]["train_path"] = str(data)
+        raw["training"]["output_dir"] = str(tmp_path / "out" / f.stem)
+        raw.setdefault("launch", {}).pop("gpus", None)
+        path = tmp_path / f.name
+        path.write_text(yaml.safe_dump(raw))
+        cfg = GraspoConfig.from_yaml(path)
+        plan = build_launch_plan(path, cfg)
+        flow = cfg.graspoflow
+        cell = flow.tp_size * flow.pp_size
+        assert plan.nproc_per_node % cell == 0, f.name
+        if flow.dp_size:
+            assert plan.nproc_per_node == cell * flow.dp_size, f.name
+        assert plan.uses_torchrun == (plan.nproc_per_node > 1), f.name
