@@ -42,6 +42,9 @@ void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
 void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                     torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
                     torch::Tensor end, int64_t B, int64_t S, double scale);
+void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                       torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
+                       torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err);
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
@@ -99,6 +102,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
   m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
   m.def("flash_attn_fwd_tc", &gb::flash_attn_fwd_tc, "causal flash attention forward on tcgen05 / TMEM");
+  m.def("flash_attn_bwd_tc", &gb::flash_attn_bwd_tc, "causal flash attention backward on tcgen05 / TMEM");
   m.def("sample_append", &gb::sample_append);
   m.def("lse_combine", &gb::lse_combine);
   m.def("grpo_loss", &gb::grpo_loss);

@@ -414,4 +414,422 @@ void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch:
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+
+// ===========================================================================
+// Flash attention backward on tcgen05.
+//
+// CTA = one tile of 128 keys of one KV head; it walks every (query head of the
+// GQA group, 128-query tile) pair j that can see those keys and accumulates
+// dK and dV in TMEM.  Products (rows = TMEM lanes):
+//   S^T_j  = K Q_j^T            [keys x queries]   TMEM cols [0, 128)
+//   dP^T_j = V dO_j^T           [keys x queries]   same columns, after S^T_j is read
+//   P^T = 2^(S^T * scale - lse_q), dS^T = scale * P^T (dP^T - delta_q)  (registers,
+//         two threads per key row, 64 query columns each; written to shared
+//         memory as bf16 128B-swizzled K-major tiles)
+//   dV += P^T dO_j             cols [256, 384)   (dO read MN-major)
+//   dK += dS^T Q_j             cols [384, 512)   (Q read MN-major)
+//   dQ_j = dS K                cols [128, 256)   (the dS^T tile read MN-major is dS;
+//                                                 K read MN-major), then added to
+//                                                 the fp32 dQ buffer with vector
+//                                                 atomics by the softmax warps.
+// Warp 0: TMA (K, V once; Q_j + lse_j and dO_j + delta_j per step); warp 1: TMEM
+// owner and MMA issuer; warps 2-9: elementwise work, dQ drain and the dK / dV
+// epilogue.  lse and delta arrive as [B * nq, S_pad] rows (bulk copies of 512 B).
+// Every wait is bounded.
+// ===========================================================================
+namespace {
+
+constexpr int kBOffK = 0;
+constexpr int kBOffV = kBOffK + kTile;
+constexpr int kBOffQ = kBOffV + kTile;
+constexpr int kBOffDO = kBOffQ + kTile;
+constexpr int kBOffP = kBOffDO + kTile;
+constexpr int kBOffDS = kBOffP + kTile;
+constexpr int kBOffLse = kBOffDS + kTile;     // 128 fp32
+constexpr int kBOffDel = kBOffLse + 512;      // 128 fp32
+constexpr int kBOffBar = kBOffDel + 512;
+constexpr int kBSmem = kBOffBar + 256 + 1024;
+
+struct BwdTcArgs {
+  const float *lse_t, *delta_t;   // [B * nq, S_pad]
+  float* dq;                      // fp32 [T, nq, 128], accumulated
+  __nv_bfloat16 *dk, *dv;         // [T, nkv, 128]
+  const int *start, *end;
+  int S, S_pad, nq, nkv;
+  float scale_log2, scale;
+  int* err;
+};
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                        BwdTcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_addr(smem_raw);
+  uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBOffBar);
+  uint64_t* kv_full = bar + 0;
+  uint64_t* q_full = bar + 1;
+  uint64_t* q_empty = bar + 2;
+  uint64_t* do_full = bar + 3;
+  uint64_t* do_empty = bar + 4;
+  uint64_t* s_full = bar + 5;
+  uint64_t* s_loaded = bar + 6;
+  uint64_t* dp_full = bar + 7;
+  uint64_t* dp_loaded = bar + 8;
+  uint64_t* ds_ready = bar + 9;
+  uint64_t* dq_full = bar + 10;
+  uint64_t* dq_free = bar + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int G = a.nq / a.nkv;
+  const int k0 = kb * kBN;
+  const int s0 = a.start[b], s1 = a.end[b];
+  const long tok0 = static_cast<long>(b) * a.S;
+  // query tiles that can see a key of this tile (queries >= keys, both in [s0, s1))
+  const bool live = k0 < s1 && k0 + kBN > s0;
+  const int qt_first = max(kb, s0 / kBM);
+  const int qt_last = live ? (s1 - 1) / kBM : qt_first - 1;
+  const int n_qt = max(0, qt_last - qt_first + 1);
+  const int n_steps = G * n_qt;                 // j = head_in_group * n_qt + (qt - qt_first)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 12; ++i) mbar_init(bar + i, 1);
+    mbar_init(s_loaded, kSoftmaxThreads);
+    mbar_init(dp_loaded, kSoftmaxThreads);
+    mbar_init(ds_ready, kSoftmaxThreads);
+    mbar_init(dq_free, kSoftmaxThreads);
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = smem_addr(sm + kBOffK), sV = smem_addr(sm + kBOffV), sQ = smem_addr(sm + kBOffQ),
+                 sDO = smem_addr(sm + kBOffDO), sP = smem_addr(sm + kBOffP), sDS = smem_addr(sm + kBOffDS);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_steps > 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmDO);
+      mbar_arrive_expect_tx(kv_full, 2 * kTile);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(sm + kBOffK + c * kAtom, &tmK, kv_full, hk * kHD + c * 64, static_cast<int>(tok0 + k0));
+        tma_load_2d(sm + kBOffV + c * kAtom, &tmV, kv_full, hk * kHD + c * 64, static_cast<int>(tok0 + k0));
+      }
+      for (int j = 0; j < n_steps; ++j) {
+        const int h = hk * G + j / n_qt;
+        const int q0 = (qt_first + j % n_qt) * kBM;
+        const long vec = (static_cast<long>(b) * a.nq + h) * a.S_pad + q0;
+        if (j >= 1 && !mbar_wait(q_empty, (j - 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(q_full, kTile + 512);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sm + kBOffQ + c * kAtom, &tmQ, q_full, h * kHD + c * 64, static_cast<int>(tok0 + q0));
+        bulk_load(smem_addr(sm + kBOffLse), a.lse_t + vec, 512, q_full);
+        if (j >= 1 && !mbar_wait(do_empty, (j - 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(do_full, kTile + 512);
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sm + kBOffDO + c * kAtom, &tmDO, do_full, h * kHD + c * 64, static_cast<int>(tok0 + q0));
+        bulk_load(smem_addr(sm + kBOffDel), a.delta_t + vec, 512, do_full);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_steps > 0) {
+      constexpr uint32_t id_kk = umma_idesc_bf16(kBN, kBM, false, false);   // S^T, dP^T
+      constexpr uint32_t id_kmn = umma_idesc_bf16(kBN, kHD, false, true);   // dV, dK: B MN-major
+      constexpr uint32_t id_mnmn = umma_idesc_bf16(kBM, kHD, true, true);   // dQ: A and B MN-major
+      const uint32_t t_sd = tmem, t_dq = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
+      bool ok = mbar_wait(kv_full, 0, a.err, kErrTmaFullTimeout);
+      for (int j = 0; j < n_steps && ok; ++j) {
+        const uint32_t par = j & 1;
+        ok = mbar_wait(q_full, par, a.err, kErrTmaFullTimeout);
+        if (ok && j >= 1) ok = mbar_wait(dp_loaded, par ^ 1u, a.err, kErrTmemEmptyTimeout);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kHD / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(sK + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t bd = umma_desc_k_sw128(sQ + (k >> 2) * kAtom) + 2 * (k & 3);
+          umma_bf16(t_sd, ad, bd, id_kk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        ok = mbar_wait(do_full, par, a.err, kErrTmaFullTimeout) &&
+             mbar_wait(s_loaded, par, a.err, kErrTmemEmptyTimeout);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kHD / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(sV + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t bd = umma_desc_k_sw128(sDO + (k >> 2) * kAtom) + 2 * (k & 3);
+          umma_bf16(t_sd, ad, bd, id_kk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(dp_full);
+        ok = mbar_wait(ds_ready, par, a.err, kErrTmaFullTimeout);
+        if (!ok) break;
+        tc_fence_after();
+        // dV += P^T dO  (K = queries: 16 per step, +32 B in the K-major P^T row, two 8-row groups down dO)
+#pragma unroll
+        for (int k = 0; k < kBM / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(sP + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t bd = umma_desc_mn_sw128(sDO + k * 2048, kAtom, 1024);
+          umma_bf16(t_dv, ad, bd, id_kmn, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(do_empty);
+        // dK += dS^T Q
+#pragma unroll
+        for (int k = 0; k < kBM / 16; ++k) {
+          const uint64_t ad = umma_desc_k_sw128(sDS + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t bd = umma_desc_mn_sw128(sQ + k * 2048, kAtom, 1024);
+          umma_bf16(t_dk, ad, bd, id_kmn, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(q_empty);
+        // dQ_j = dS K  (K = keys: the dS^T tile read MN-major, K read MN-major)
+        if (j >= 1) ok = mbar_wait(dq_free, par ^ 1u, a.err, kErrTmemEmptyTimeout);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kBN / 16; ++k) {
+          const uint64_t ad = umma_desc_mn_sw128(sDS + k * 2048, kAtom, 1024);
+          const uint64_t bd = umma_desc_mn_sw128(sK + k * 2048, kAtom, 1024);
+          umma_bf16(t_dq, ad, bd, id_mnmn, k > 0 ? 1u : 0u);
+        }
+        umma_commit(dq_full);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ elementwise / drains / epilogue
+    const int half = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;          // TMEM lane: key row (S^T, dP^T, dK, dV) or query row (dQ)
+    const int kr = k0 + r;
+    const bool key_ok = kr >= s0 && kr < s1;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t col0 = static_cast<uint32_t>(half * 64);
+    const float* lse_s = reinterpret_cast<const float*>(sm + kBOffLse) + half * 64;
+    const float* del_s = reinterpret_cast<const float*>(sm + kBOffDel) + half * 64;
+    bool ok = true;
+    for (int j = 0; j < n_steps && ok; ++j) {
+      const uint32_t par = j & 1;
+      const int h = hk * G + j / n_qt;
+      const int q0 = (qt_first + j % n_qt) * kBM;
+      const bool interior = k0 >= s0 && q0 >= s0 && q0 + kBM <= s1 && q0 >= k0 + kBN - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, a.err, kErrTmemFullTimeout) &&
+                                       mbar_wait(q_full, par, a.err, kErrTmaFullTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      float p[64];
+      tmem_ld32(tmem + lane_off + col0, *reinterpret_cast<float(*)[32]>(p));
+      tmem_ld32(tmem + lane_off + col0 + 32, *reinterpret_cast<float(*)[32]>(p + 32));
+      tc_fence_before();
+      mbar_arrive(s_loaded);
+      const int qc = q0 + half * 64;            // first query column of this thread
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const float v = ex2(fmaf(p[e], a.scale_log2, -lse_s[e]));
+        const int qq = qc + e;
+        p[e] = (interior || (key_ok && qq >= kr && qq < s1)) ? v : 0.f;
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(dp_full, par, a.err, kErrTmemFullTimeout) &&
+                                       mbar_wait(do_full, par, a.err, kErrTmaFullTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      float d[64];
+      tmem_ld32(tmem + lane_off + col0, *reinterpret_cast<float(*)[32]>(d));
+      tmem_ld32(tmem + lane_off + col0 + 32, *reinterpret_cast<float(*)[32]>(d + 32));
+      tc_fence_before();
+      mbar_arrive(dp_loaded);
+#pragma unroll
+      for (int e = 0; e < 64; ++e) d[e] = p[e] != 0.f ? p[e] * (d[e] - del_s[e]) * a.scale : 0.f;
+      // P^T and dS^T rows: this thread's 64 queries are atom column `half`
+      // (the previous step's MMAs finished reading both tiles: dq_full(j - 1) was awaited)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = half * kAtom + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off),
+                     "r"(pack2(p[c * 8 + 0], p[c * 8 + 1])), "r"(pack2(p[c * 8 + 2], p[c * 8 + 3])),
+                     "r"(pack2(p[c * 8 + 4], p[c * 8 + 5])), "r"(pack2(p[c * 8 + 6], p[c * 8 + 7]))
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off),
+                     "r"(pack2(d[c * 8 + 0], d[c * 8 + 1])), "r"(pack2(d[c * 8 + 2], d[c * 8 + 3])),
+                     "r"(pack2(d[c * 8 + 4], d[c * 8 + 5])), "r"(pack2(d[c * 8 + 6], d[c * 8 + 7]))
+                     : "memory");
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+      // dQ_j rows (lane = query row): add into the fp32 buffer
+      ok = __all_sync(0xffffffffu, mbar_wait(dq_full, par, a.err, kErrTmemFullTimeout));
+      if (!ok) break;
+      tc_fence_after();
+      const int qr = q0 + r;
+      const bool q_ok = qr >= s0 && qr < s1;
+      float* dst = a.dq + ((tok0 + min(qr, a.S - 1)) * a.nq + h) * kHD + col0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        tmem_ld32(tmem + lane_off + 128 + col0 + c * 32, v);
+        if (q_ok) {
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4)
+            red_add_v4(dst + c * 32 + q4 * 4, v[q4 * 4 + 0], v[q4 * 4 + 1], v[q4 * 4 + 2], v[q4 * 4 + 3]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    // ---- epilogue: dK, dV rows (zero where the key is outside the valid range);
+    // the TMEM loads are warp-uniform, only the stores depend on the row
+    const bool have = n_steps > 0 && ok;
+    const bool keep = have && key_ok;
+    const long row = (tok0 + min(kr, a.S - 1)) * a.nkv + hk;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      __nv_bfloat16* out = (which == 0 ? a.dv : a.dk) + row * kHD + col0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float v[32];
+        if (have) {
+          tmem_ld32(tmem + lane_off + (which == 0 ? 256 : 384) + col0 + c * 32, v);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0.f;
+        }
+        if (kr < a.S) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 pkt;
+            pkt.x = pack2(keep ? v[q4 * 8 + 0] : 0.f, keep ? v[q4 * 8 + 1] : 0.f);
+            pkt.y = pack2(keep ? v[q4 * 8 + 2] : 0.f, keep ? v[q4 * 8 + 3] : 0.f);
+            pkt.z = pack2(keep ? v[q4 * 8 + 4] : 0.f, keep ? v[q4 * 8 + 5] : 0.f);
+            pkt.w = pack2(keep ? v[q4 * 8 + 6] : 0.f, keep ? v[q4 * 8 + 7] : 0.f);
+            *reinterpret_cast<uint4*>(out + c * 32 + q4 * 8) = pkt;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// delta[b, h, s] = sum_d dO * O and lse copied into [B * nq, S_pad] rows (one warp per (t, h))
+__global__ void flash_bwd_tc_pre_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                                        const float* __restrict__ lse, float* __restrict__ delta_t,
+                                        float* __restrict__ lse_t, long n_rows, int nq, int S, int S_pad) {
+  const long w = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n_rows) return;
+  const uint2 ov = *reinterpret_cast<const uint2*>(o + w * kHD + lane * 4);
+  const uint2 dv = *reinterpret_cast<const uint2*>(dout + w * kHD + lane * 4);
+  const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&ov);
+  const __nv_bfloat16* db = reinterpret_cast<const __nv_bfloat16*>(&dv);
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) s += __bfloat162float(ob[e]) * __bfloat162float(db[e]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) {
+    const long t = w / nq;
+    const int h = static_cast<int>(w - t * nq);
+    const long b = t / S, pos = t - b * S;
+    const long dst = (b * nq + h) * S_pad + pos;
+    delta_t[dst] = s;
+    lse_t[dst] = lse[w];
+  }
+}
+
+__global__ void dq_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long n) {
+  const long i = (blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(src + i);
+    uint2 out;
+    out.x = pack2(v.x, v.y);
+    out.y = pack2(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + i) = out;
+  } else {
+    for (long k = i; k < n; ++k) dst[k] = __float2bfloat16(src[k]);
+  }
+}
+
+}  // namespace
+
+void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
+                       torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
+                       torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(dout.is_contiguous() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous() &&
+                  out.is_contiguous() && lse.is_contiguous(), "contiguous inputs");
+  TORCH_CHECK(q.size(-1) == kHD && q.scalar_type() == torch::kBFloat16, "bf16 q/k/v with head_dim 128");
+  const long T = q.size(0);
+  TORCH_CHECK(T == B * S, "q must hold B * S tokens");
+  const int nq = static_cast<int>(q.size(1)), nkv = static_cast<int>(k.size(1));
+  TORCH_CHECK(nq % nkv == 0, "query heads must be a multiple of KV heads");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto opts = q.options().dtype(torch::kFloat32);
+  const int S_pad = static_cast<int>((S + kBM - 1) / kBM * kBM);
+  // padding columns (positions >= S) are read by boundary tiles and masked: keep them finite
+  torch::Tensor delta_t = torch::zeros({B * nq, S_pad}, opts);
+  torch::Tensor lse_t = torch::zeros({B * nq, S_pad}, opts);
+  torch::Tensor dq32 = torch::zeros({T, nq, kHD}, opts);
+  const long rows = T * nq;
+  flash_bwd_tc_pre_kernel<<<(rows * 32 + 255) / 256, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+      lse.data_ptr<float>(), delta_t.data_ptr<float>(), lse_t.data_ptr<float>(), rows, nq, static_cast<int>(S), S_pad);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  BwdTcArgs a{};
+  a.lse_t = lse_t.data_ptr<float>();
+  a.delta_t = delta_t.data_ptr<float>();
+  a.dq = dq32.data_ptr<float>();
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  a.start = start.data_ptr<int>();
+  a.end = end.data_ptr<int>();
+  a.S = static_cast<int>(S);
+  a.S_pad = S_pad;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.scale = static_cast<float>(scale);
+  a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;
+  a.err = err.data_ptr<int>();
+  CUtensorMap tq = make_tmap_bf16(q.data_ptr(), T, static_cast<long>(nq) * kHD, static_cast<long>(nq) * kHD, kBM);
+  CUtensorMap tdo = make_tmap_bf16(dout.data_ptr(), T, static_cast<long>(nq) * kHD, static_cast<long>(nq) * kHD, kBM);
+  CUtensorMap tk = make_tmap_bf16(k.data_ptr(), T, static_cast<long>(nkv) * kHD, static_cast<long>(nkv) * kHD, kBN);
+  CUtensorMap tv = make_tmap_bf16(v.data_ptr(), T, static_cast<long>(nkv) * kHD, static_cast<long>(nkv) * kHD, kBN);
+  static bool configured[64] = {};
+  const int dev = q.get_device();
+  if (!configured[dev]) {
+    cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBSmem);
+    configured[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(S_pad / kBN), static_cast<unsigned>(nkv), static_cast<unsigned>(B));
+  flash_bwd_tc_kernel<<<grid, kThreads, kBSmem, stream>>>(tq, tk, tv, tdo, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const long n = dq32.numel();
+  dq_to_bf16_kernel<<<(n / 4 + 255) / 256 + 1, 256, 0, stream>>>(dq32.data_ptr<float>(),
+                                                                  reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace gb

@@ -288,7 +288,7 @@ def bench_profile(args) -> None:
         scratch = torch.zeros(rows * nq * 12 * (D + 2) + rows * nkv, device="cuda")
         runs.append(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), 4, scratch,
                                                          P, G, 2))
-    elif k in ("flash_fwd", "flash_bwd", "flash_fwd_tc"):
+    elif k in ("flash_fwd", "flash_bwd", "flash_fwd_tc", "flash_bwd_tc"):
         B, S, nq, nkv, D = 4, 3072, 32, 8, 128
         T = B * S
         q = torch.randn(T, nq, D, device="cuda").bfloat16()
@@ -309,8 +309,14 @@ def bench_profile(args) -> None:
         else:
             do = torch.randn_like(q)
             dq, dk, dv = torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)
-            runs.append(lambda: ext().flash_attn_bwd(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
-                                                     1 / math.sqrt(D)))
+            if k == "flash_bwd_tc":
+                from graspo_b200.ops._ext import err_word
+
+                runs.append(lambda: ext().flash_attn_bwd_tc(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
+                                                            1 / math.sqrt(D), err_word(q.device)))
+            else:
+                runs.append(lambda: ext().flash_attn_bwd(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
+                                                         1 / math.sqrt(D)))
     else:
         raise SystemExit(f"unknown kernel {k}")
     for _ in range(args.iters):

@@ -8,26 +8,28 @@ Padding queries produce zero output and receive zero gradient; nothing
 downstream consumes them (loss masks exclude them and no valid query attends
 to a padding key).
 
-The forward runs on the tcgen05 kernel (csrc/flash_attn_tc.cu: S, P and O in
-TMEM / swizzled shared memory, TMA-fed K/V rings); the backward on the
-mma.sync kernel (csrc/flash_attn.cu).  The forward also returns the
-per-(token, head) log-sum-exp (log2 domain, fp32), which the backward kernel uses to rebuild the probabilities
-without a second softmax pass (FlashAttention-2, Dao 2023).  GQA is handled
-inside the kernels: a query head reads KV head ``h // (nq // nkv)``, and the
-backward kernel sums the G query heads' contributions to dK/dV in registers.
+Both directions run on tcgen05 kernels (csrc/flash_attn_tc.cu): the forward
+keeps S and O in TMEM and P in swizzled shared memory; the backward walks, per
+128-key tile, every query tile and head of the GQA group with S^T / dP^T, dQ,
+dK and dV in TMEM (dQ is added into an fp32 buffer with vector atomics).  The
+forward also returns the per-(token, head) log-sum-exp (log2 domain, fp32),
+which the backward uses to rebuild the probabilities without a second softmax
+pass (FlashAttention-2, Dao 2023).  GQA is handled inside the kernels: a query
+head reads KV head ``h // (nq // nkv)``.  ``GRASPO_FA_TC=0`` / ``GRASPO_FA_TC_BWD=0``
+select the mma.sync kernels (csrc/flash_attn.cu) instead.
 Head dim 128 (every Qwen3 size) is the supported kernel shape.
 """
 
 from __future__ import annotations
 
-import torch
-
 import os
+
+import torch
 
 from graspo_b200.ops._ext import err_word, ext
 
-# forward on the tcgen05 kernel (S / P / O in TMEM); GRASPO_FA_TC=0 selects the mma.sync kernel
 USE_TC_FORWARD = os.environ.get("GRASPO_FA_TC", "1") != "0"
+USE_TC_BACKWARD = os.environ.get("GRASPO_FA_TC_BWD", "1") != "0"
 
 
 def row_ranges(meta) -> tuple[torch.Tensor, torch.Tensor]:
@@ -77,6 +79,10 @@ def attention_backward(dout, q, k, v, out, ctx, meta, scale: float):
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    ext().flash_attn_bwd(dout.contiguous().view(T, nq, D), q.contiguous(), k.contiguous(), v.contiguous(),
-                         out.contiguous().view(T, nq, D), ctx, dq, dk, dv, start, end, meta.B, meta.S, float(scale))
+    args = (dout.contiguous().view(T, nq, D), q.contiguous(), k.contiguous(), v.contiguous(),
+            out.contiguous().view(T, nq, D), ctx.contiguous(), dq, dk, dv, start, end, meta.B, meta.S, float(scale))
+    if USE_TC_BACKWARD and q.is_cuda:
+        ext().flash_attn_bwd_tc(*args, err_word(q.device))
+    else:
+        ext().flash_attn_bwd(*args)
     return dq, dk, dv

@@ -50,7 +50,7 @@ def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epi
         pre = acc.to(torch.bfloat16).float()
         g, u = pre[:, 0::2], pre[:, 1::2]
         C.copy_((torch.nn.functional.silu(g) * u).to(C.dtype))
-        if aux is not None:
+        if aux is not None and not (swap and splits > 1):  # split-K swap: aux is the kernel's workspace
             aux.copy_(acc.to(aux.dtype))
     elif epilogue == EPI_LSE:
         nblk = math.ceil(N / bn)
@@ -236,6 +236,10 @@ def flash_attn_fwd(q, k, v, out, lse, start, end, B, S, scale):
 
 def flash_attn_fwd_tc(q, k, v, out, lse, start, end, B, S, scale, err):
     flash_attn_fwd(q, k, v, out, lse, start, end, B, S, scale)
+
+
+def flash_attn_bwd_tc(dout, q, k, v, out, lse, dq, dk, dv, start, end, B, S, scale, err):
+    flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, start, end, B, S, scale)
 
 
 def flash_attn_bwd(dout, q, k, v, out, lse, dq, dk, dv, start, end, B, S, scale):

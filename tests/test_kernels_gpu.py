@@ -138,6 +138,28 @@ def test_gemm_swap_swiglu_and_residual():
     _close(gemm(w, x, swap=True, residual=r), x.float() @ w.float().T + r.float(), 2e-2)
 
 
+@pytest.mark.parametrize("t,splits", [(64, 3), (40, 2), (100, 4)])
+def test_gemm_swap_swiglu_split_k(t, splits):
+    """Split-K SwiGLU: per-split fp32 partial tiles, the last split of each tile
+    applies the activation; counters are left zeroed for the next call."""
+    from graspo_b200.ops.gemm import gemm
+
+    i, k = 640, 1024
+    wg, wu, x = _rand(i, k, scale=0.05), _rand(i, k, scale=0.05), _rand(t, k)
+    a2, b2 = _rand(2 * i, 64, scale=0.05), _rand(t, 64, scale=0.5)    # LoRA-style K extension
+    inter = torch.stack([wg, wu], dim=1).reshape(2 * i, k).contiguous()
+    full = x.float() @ inter.float().T + b2.float() @ a2.float().T
+    ref = torch.nn.functional.silu(full[:, 0::2]) * full[:, 1::2]
+    ws = torch.empty(splits * t * 2 * i, device="cuda")
+    ctr = torch.zeros(-(-2 * i // 128) * -(-t // 64), device="cuda", dtype=torch.int32)
+    for _ in range(3):
+        out = gemm(inter, x, swap=True, epilogue="swiglu", ext_ab=(a2, b2), splits=splits, aux=ws, tile_ctr=ctr)
+        _close(out, ref, 3e-2)
+        assert int(ctr.abs().sum()) == 0
+    one = gemm(inter, x, swap=True, epilogue="swiglu", ext_ab=(a2, b2))
+    _close(out, one.float(), 2e-2)
+
+
 def test_gemm_lse_and_softmax_grad():
     from graspo_b200.ops.gemm import gemm
 
@@ -391,6 +413,50 @@ def test_flash_attention_forward_backward(S, G):
     _close(dq, qf.grad, 3e-2)
     _close(dk, kf.grad, 3e-2)
     _close(dv, vf.grad, 3e-2)
+
+
+def _attn_grads_reference(q, k, v, dout, start, end, B, S, G, scale):
+    """Autograd of the fp32 reference: (dq, dk, dv)."""
+    T, nq, D = q.shape
+    nkv = k.shape[1]
+    qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+    idx = torch.arange(S, device="cuda")
+    valid = (idx[None] >= start[:, None]) & (idx[None] < end[:, None])
+    allowed = valid[:, None, :] & valid[:, :, None] & (idx[:, None] >= idx[None, :])[None]
+    qh = qf.view(B, S, nq, D).transpose(1, 2)
+    kh = kf.view(B, S, nkv, D).transpose(1, 2).repeat_interleave(G, 1)
+    vh = vf.view(B, S, nkv, D).transpose(1, 2).repeat_interleave(G, 1)
+    s = (qh @ kh.transpose(-1, -2) * scale).masked_fill(~allowed[:, None], float("-inf"))
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    o = (p @ vh) * valid[:, None, :, None]
+    o.transpose(1, 2).reshape(T, nq, D).mul(dout.float()).sum().backward()
+    return qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("S,G", [(96, 2), (300, 4), (64, 1), (520, 8), (384, 4)])
+def test_flash_attention_backward_tcgen05(S, G):
+    from graspo_b200.ops._ext import check_errors, err_word
+
+    B, nkv, D = 3, 2, 128
+    nq = nkv * G
+    T = B * S
+    q, k, v = _rand(T, nq, D), _rand(T, nkv, D), _rand(T, nkv, D)
+    start = torch.tensor([0, 17, 5], device="cuda", dtype=torch.int32)
+    end = torch.tensor([S, S, S - 23], device="cuda", dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    out = torch.empty(T, nq, D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(T, nq, device="cuda")
+    _ext().flash_attn_fwd_tc(q, k, v, out, lse, start, end, B, S, scale, err_word(q.device))
+    dout = _rand(T, nq, D)
+    rq, rk, rv = _attn_grads_reference(q, k, v, dout, start, end, B, S, G, scale)
+    dq, dk, dv = torch.full_like(q, float("nan")), torch.full_like(k, float("nan")), torch.full_like(v, float("nan"))
+    for _ in range(2):  # a second run must not depend on leftovers of the first
+        _ext().flash_attn_bwd_tc(dout, q, k, v, out, lse, dq, dk, dv, start, end, B, S, scale, err_word(q.device))
+        torch.cuda.synchronize()
+        check_errors()
+        _close(dq, rq, 3e-2)
+        _close(dk, rk, 3e-2)
+        _close(dv, rv, 3e-2)
 
 
 def test_sample_append_greedy_and_distribution():
