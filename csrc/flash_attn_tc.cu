@@ -441,14 +441,15 @@ namespace {
 
 constexpr int kBOffK = 0;
 constexpr int kBOffV = kBOffK + kTile;
-constexpr int kBOffQ = kBOffV + kTile;
-constexpr int kBOffDO = kBOffQ + kTile;
+constexpr int kBOffQ = kBOffV + kTile;        // 2 buffers: Q_{j+1} loads while step j runs
+constexpr int kBOffDO = kBOffQ + 2 * kTile;
 constexpr int kBOffP = kBOffDO + kTile;
 constexpr int kBOffDS = kBOffP + kTile;
-constexpr int kBOffLse = kBOffDS + kTile;     // 128 fp32
-constexpr int kBOffDel = kBOffLse + 512;      // 128 fp32
+constexpr int kBOffLse = kBOffDS + kTile;     // 2 x 128 fp32 (with the Q buffers)
+constexpr int kBOffDel = kBOffLse + 1024;     // 128 fp32
 constexpr int kBOffBar = kBOffDel + 512;
 constexpr int kBSmem = kBOffBar + 256 + 1024;
+static_assert(kBSmem <= 227 * 1024, "backward shared memory budget");
 
 struct BwdTcArgs {
   const float *lse_t, *delta_t;   // [B * nq, S_pad]
@@ -480,18 +481,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sm = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBOffBar);
   uint64_t* kv_full = bar + 0;
-  uint64_t* q_full = bar + 1;
-  uint64_t* q_empty = bar + 2;
-  uint64_t* do_full = bar + 3;
-  uint64_t* do_empty = bar + 4;
-  uint64_t* s_full = bar + 5;
-  uint64_t* s_loaded = bar + 6;
-  uint64_t* dp_full = bar + 7;
-  uint64_t* dp_loaded = bar + 8;
-  uint64_t* ds_ready = bar + 9;
-  uint64_t* dq_full = bar + 10;
-  uint64_t* dq_free = bar + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 12);
+  uint64_t* q_full = bar + 1;     // [2]
+  uint64_t* q_empty = bar + 3;    // [2]
+  uint64_t* do_full = bar + 5;
+  uint64_t* do_empty = bar + 6;
+  uint64_t* s_full = bar + 7;
+  uint64_t* s_loaded = bar + 8;
+  uint64_t* dp_full = bar + 9;
+  uint64_t* dp_loaded = bar + 10;
+  uint64_t* ds_ready = bar + 11;
+  uint64_t* dq_full = bar + 12;
+  uint64_t* dq_free = bar + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -507,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_steps = G * n_qt;                 // j = head_in_group * n_qt + (qt - qt_first)
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) mbar_init(bar + i, 1);
+    for (int i = 0; i < 14; ++i) mbar_init(bar + i, 1);
     mbar_init(s_loaded, kSoftmaxThreads);
     mbar_init(dp_loaded, kSoftmaxThreads);
     mbar_init(ds_ready, kSoftmaxThreads);
@@ -538,11 +539,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = hk * G + j / n_qt;
         const int q0 = (qt_first + j % n_qt) * kBM;
         const long vec = (static_cast<long>(b) * a.nq + h) * a.S_pad + q0;
-        if (j >= 1 && !mbar_wait(q_empty, (j - 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
-        mbar_arrive_expect_tx(q_full, kTile + 512);
+        const int qs = j & 1;
+        if (j >= 2 && !mbar_wait(q_empty + qs, ((j - 2) >> 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
+        mbar_arrive_expect_tx(q_full + qs, kTile + 512);
         for (int c = 0; c < 2; ++c)
-          tma_load_2d(sm + kBOffQ + c * kAtom, &tmQ, q_full, h * kHD + c * 64, static_cast<int>(tok0 + q0));
-        bulk_load(smem_addr(sm + kBOffLse), a.lse_t + vec, 512, q_full);
+          tma_load_2d(sm + kBOffQ + qs * kTile + c * kAtom, &tmQ, q_full + qs, h * kHD + c * 64,
+                      static_cast<int>(tok0 + q0));
+        bulk_load(smem_addr(sm + kBOffLse + qs * 512), a.lse_t + vec, 512, q_full + qs);
         if (j >= 1 && !mbar_wait(do_empty, (j - 1) & 1, a.err, kErrSmemEmptyTimeout)) break;
         mbar_arrive_expect_tx(do_full, kTile + 512);
         for (int c = 0; c < 2; ++c)
@@ -560,14 +563,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = mbar_wait(kv_full, 0, a.err, kErrTmaFullTimeout);
       for (int j = 0; j < n_steps && ok; ++j) {
         const uint32_t par = j & 1;
-        ok = mbar_wait(q_full, par, a.err, kErrTmaFullTimeout);
+        const uint32_t sQj = sQ + (j & 1) * kTile;
+        ok = mbar_wait(q_full + (j & 1), (j >> 1) & 1, a.err, kErrTmaFullTimeout);
         if (ok && j >= 1) ok = mbar_wait(dp_loaded, par ^ 1u, a.err, kErrTmemEmptyTimeout);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < kHD / 16; ++k) {
           const uint64_t ad = umma_desc_k_sw128(sK + (k >> 2) * kAtom) + 2 * (k & 3);
-          const uint64_t bd = umma_desc_k_sw128(sQ + (k >> 2) * kAtom) + 2 * (k & 3);
+          const uint64_t bd = umma_desc_k_sw128(sQj + (k >> 2) * kAtom) + 2 * (k & 3);
           umma_bf16(t_sd, ad, bd, id_kk, k > 0 ? 1u : 0u);
         }
         umma_commit(s_full);
@@ -597,10 +601,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < kBM / 16; ++k) {
           const uint64_t ad = umma_desc_k_sw128(sDS + (k >> 2) * kAtom) + 2 * (k & 3);
-          const uint64_t bd = umma_desc_mn_sw128(sQ + k * 2048, kAtom, 1024);
+          const uint64_t bd = umma_desc_mn_sw128(sQj + k * 2048, kAtom, 1024);
           umma_bf16(t_dk, ad, bd, id_kmn, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(q_empty);
+        umma_commit(q_empty + (j & 1));
         // dQ_j = dS K  (K = keys: the dS^T tile read MN-major, K read MN-major)
         if (j >= 1) ok = mbar_wait(dq_free, par ^ 1u, a.err, kErrTmemEmptyTimeout);
         if (!ok) break;
@@ -632,7 +636,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q0 = (qt_first + j % n_qt) * kBM;
       const bool interior = k0 >= s0 && q0 >= s0 && q0 + kBM <= s1 && q0 >= k0 + kBN - 1;
       ok = __all_sync(0xffffffffu, mbar_wait(s_full, par, a.err, kErrTmemFullTimeout) &&
-                                       mbar_wait(q_full, par, a.err, kErrTmaFullTimeout));
+                                       mbar_wait(q_full + (j & 1), (j >> 1) & 1, a.err, kErrTmaFullTimeout));
+      const float* lse_j = lse_s + (j & 1) * 128;
       if (!ok) break;
       tc_fence_after();
       float p[64];
@@ -643,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int qc = q0 + half * 64;            // first query column of this thread
 #pragma unroll
       for (int e = 0; e < 64; ++e) {
-        const float v = ex2(fmaf(p[e], a.scale_log2, -lse_s[e]));
+        const float v = ex2(fmaf(p[e], a.scale_log2, -lse_j[e]));
         const int qq = qc + e;
         p[e] = (interior || (key_ok && qq >= kr && qq < s1)) ? v : 0.f;
       }

@@ -129,7 +129,41 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
     TORCH_CHECK(args.targets != nullptr, "log-prob epilogues need targets");
   if (epilogue == kLSE) TORCH_CHECK(args.tgt_logit != nullptr && args.aux != nullptr, "LSE epilogue needs aux and tgt_logit");
   if (epilogue == kSoftmaxGrad) TORCH_CHECK(args.row_lse != nullptr && args.row_scale != nullptr, "softmax-grad epilogue needs lse and scale");
-  TORCH_CHECK(epilogue == kAtomicF32 || args.splits == 1, "split-K requires the atomic epilogue");
+  const bool split_swiglu = epilogue == kSwiGLU && swap && args.splits > 1;
+  TORCH_CHECK(epilogue == kAtomicF32 || args.splits == 1 || split_swiglu,
+              "split-K requires the atomic epilogue (or the swap SwiGLU epilogue with a workspace)");
+  {
+    const int kb_total = args.kb_main + args.kb_ext;
+    const int per = (kb_total + args.splits - 1) / args.splits;
+    args.nonempty_splits = (kb_total + per - 1) / per;
+  }
+  if (split_swiglu) {
+    TORCH_CHECK(args.splits <= 4, "split-K SwiGLU supports at most 4 splits");
+    // Only the tiles of the persistent grid's last (partial) wave are split: the
+    // first full waves run whole-K tiles with the SwiGLU epilogue directly.
+    const int tiles = static_cast<int>(((Mdim + BM - 1) / BM) * ((Ndim + bn - 1) / bn));
+    int ctas = num_sms(device);
+    if (max_ctas > 0) ctas = std::min<int>(ctas, static_cast<int>(max_ctas));
+    const int full = tiles / ctas * ctas;
+    const int rem = tiles - full;
+    args.full_tiles = full;
+    args.splits = rem == 0 ? 1 : std::max(1, std::min(args.splits, ctas / rem));
+    if (args.splits == 1) args.full_tiles = 0;
+    {
+      const int kb_total = args.kb_main + args.kb_ext;
+      const int per = (kb_total + args.splits - 1) / args.splits;
+      args.nonempty_splits = (kb_total + per - 1) / per;
+    }
+    TORCH_CHECK(aux.has_value() && aux->defined() && aux->scalar_type() == torch::kFloat32 && aux->is_contiguous() &&
+                    aux->numel() >= static_cast<int64_t>(args.splits) * Mdim * Ndim,
+                "split-K SwiGLU needs an fp32 workspace of splits x tokens x features");
+    TORCH_CHECK(tile_ctr.has_value() && tile_ctr->defined() && tile_ctr->scalar_type() == torch::kInt32 &&
+                    tile_ctr->numel() >= ((Mdim + BM - 1) / BM) * ((Ndim + bn - 1) / bn),
+                "split-K SwiGLU needs a zeroed int32 tile counter per output tile");
+    TORCH_CHECK(layout == 0, "split-K SwiGLU takes K-major operands");
+    args.ldaux = Mdim;
+    args.tile_ctr = tile_ctr->data_ptr<int>();
+  }
   if (push_dst.has_value() && push_dst->defined()) {
     TORCH_CHECK(swap && epilogue == kAtomicF32, "tile push needs the swap atomic epilogue");
     TORCH_CHECK(push_flag.has_value() && tile_ctr.has_value(), "tile push needs flags and tile counters");
@@ -149,9 +183,6 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
     TORCH_CHECK(tile_ctr->scalar_type() == torch::kInt32 && tile_ctr->is_cuda() && tile_ctr->numel() >= num_tiles,
                 "tile_ctr must be a zeroed int32 CUDA tensor with one entry per output tile");
     args.tile_ctr = tile_ctr->data_ptr<int>();
-    const int kb_total = args.kb_main + args.kb_ext;
-    const int per = (kb_total + args.splits - 1) / args.splits;
-    args.nonempty_splits = (kb_total + per - 1) / per;
     TORCH_CHECK(layout == 0 && C.scalar_type() == torch::kFloat32 && C.size(0) == Ndim && C.size(1) == Mdim,
                 "tile push writes C [tokens, features] in full");
   }

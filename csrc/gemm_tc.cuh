@@ -82,6 +82,10 @@ struct GemmArgs {
   int npeers;              // ranks in the group (0: no push)
   int* tile_ctr;
   int nonempty_splits;     // splits that own at least one K-block
+  // Tiles [0, full_tiles) run with the whole K range (one unit each); only the
+  // remaining tiles are split `splits` ways (split-K SwiGLU: the last wave of a
+  // persistent grid is filled without splitting every tile).  0: all tiles split.
+  int full_tiles;
 };
 
 template <int BN_>
@@ -97,11 +101,27 @@ struct Cfg {
 
 struct Unit {
   int m_block, n_block, kb_begin, kb_end;
+  int split;      // K-split index inside its tile
+  bool partial;   // the tile is split (its units write partial results)
 };
 
-__device__ __forceinline__ Unit decode_unit(int u, int num_m, int num_n, int splits, int kb_total) {
-  const int tile = u / splits;
-  const int split = u - tile * splits;
+__host__ __device__ __forceinline__ int unit_count(int tiles, int splits, int full_tiles) {
+  return full_tiles + (tiles - full_tiles) * splits;
+}
+
+__device__ __forceinline__ Unit decode_unit(int u, int num_m, int num_n, int splits, int kb_total,
+                                            int full_tiles = 0) {
+  int tile, split, nsplit;
+  if (u < full_tiles) {
+    tile = u;
+    split = 0;
+    nsplit = 1;
+  } else {
+    const int v = u - full_tiles;
+    tile = full_tiles + v / splits;
+    split = v - (v / splits) * splits;
+    nsplit = splits;
+  }
   const int group = kGroupM * num_n;
   const int g = tile / group;
   const int first_m = g * kGroupM;
@@ -110,9 +130,11 @@ __device__ __forceinline__ Unit decode_unit(int u, int num_m, int num_n, int spl
   Unit r;
   r.m_block = first_m + in_group % gm;
   r.n_block = in_group / gm;
-  const int per = (kb_total + splits - 1) / splits;
+  const int per = (kb_total + nsplit - 1) / nsplit;
   r.kb_begin = split * per;
   r.kb_end = min(kb_total, r.kb_begin + per);
+  r.split = split;
+  r.partial = nsplit > 1;
   return r;
 }
 
@@ -167,6 +189,60 @@ __device__ __forceinline__ void push_tile_impl(const GemmArgs& args, const Unit&
   epi_bar();  // last_split is rewritten by the next unit
 }
 
+// Split-K SwiGLU (swap layout): every split stores its fp32 partial tile into
+// its own slice of the workspace `aux` ([splits][N][ldaux]); the split that
+// finishes last (tile counter) sums the slices, applies silu(gate) * up and
+// writes the bf16 output -- no atomics and no workspace clearing.
+constexpr int kMaxSwigluSplits = 4;
+
+template <int BN>
+__device__ __forceinline__ void swiglu_fixup_impl(const GemmArgs& args, const Unit& w, int num_n, int m,
+                                                  int row_in_tile) {
+  __shared__ int last_split_sw;
+  // the 128 epilogue threads' partial stores are ordered before one thread's
+  // acq_rel arrival by the named barrier (release is cumulative); the last
+  // arrival's acquire orders the slice reads of every thread after the next barrier
+  epi_bar();
+  const int tile = w.m_block * num_n + w.n_block;
+  if (row_in_tile == 0) {
+    int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(args.tile_ctr + tile) : "memory");
+    const int last = prev == args.nonempty_splits - 1;
+    if (last) args.tile_ctr[tile] = 0;
+    last_split_sw = last;
+  }
+  epi_bar();
+  if (last_split_sw != 0) {
+    const int n0 = w.n_block * BN;
+    const int nn = min(BN, args.N - n0);
+    const float* __restrict__ ws = static_cast<const float*>(args.aux);
+    const long slice = args.ldaux * static_cast<long>(args.N);
+    __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C);
+    const int lane = threadIdx.x & 31;
+    const bool live = m < args.M;
+    const int ns = args.nonempty_splits;
+    for (int j0 = 0; j0 < nn; j0 += 32) {
+      // 32 token rows x every split: all loads in flight together
+      float part[kMaxSwigluSplits][32];
+#pragma unroll
+      for (int q = 0; q < kMaxSwigluSplits; ++q)
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+          part[q][jj] = (live && q < ns && j0 + jj < nn)
+                            ? __ldcg(ws + q * slice + static_cast<long>(n0 + j0 + jj) * args.ldaux + m)
+                            : 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const float acc = (part[0][jj] + part[1][jj]) + (part[2][jj] + part[3][jj]);
+        const float partner = __shfl_xor_sync(0xffffffffu, acc, 1);  // (gate, up) sit in adjacent lanes
+        if ((lane & 1) == 0 && live && j0 + jj < nn)
+          C[static_cast<long>(n0 + j0 + jj) * args.ldc + (m >> 1)] = __float2bfloat16(silu_f(acc) * partner);
+      }
+    }
+  }
+  epi_bar();  // last_split_sw is rewritten by the next unit
+}
+
 // LAYOUT bit 0: B (and B2) are MN-major -- given as [K, N] row-major; bit 1:
 // A (and A2) are MN-major -- given as [K, M].  MN-major tiles are loaded as
 // 64-wide column blocks of 64 K-rows (one swizzle atom column each).
@@ -198,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_m = (args.M + BM - 1) / BM;
   const int num_n = (args.N + BN - 1) / BN;
   const int kb_total = args.kb_main + args.kb_ext;
-  const int units = num_m * num_n * args.splits;
+  const int units = unit_count(num_m * num_n, args.splits, args.full_tiles);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -255,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int early = 0;
       if constexpr (SWAP) {
         if (blockIdx.x < units) {
-          const Unit w = decode_unit(blockIdx.x, num_m, num_n, args.splits, kb_total);
+          const Unit w = decode_unit(blockIdx.x, num_m, num_n, args.splits, kb_total, args.full_tiles);
           for (int kb = w.kb_begin; kb < w.kb_end && early < STAGES; ++kb, ++early) {
             mbar_arrive_expect_tx(&full[early], C_::STAGE_BYTES);
             uint8_t* a_dst = smA + early * C_::A_BYTES;
@@ -270,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       pdl_wait();
       int issued = 0;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total, args.full_tiles);
         for (int kb = w.kb_begin; kb < w.kb_end; ++kb, ++issued) {
           uint8_t* a_dst = smA + stage * C_::A_BYTES;
           uint8_t* b_dst = smB + stage * C_::B_BYTES;
@@ -323,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc_iter = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+        const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total, args.full_tiles);
         if (w.kb_end <= w.kb_begin) continue;
         const int acc = acc_iter & 1;
         const uint32_t acc_phase = (acc_iter >> 1) & 1;
@@ -367,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();  // outputs (and residual / target inputs) belong to neighbouring kernels
     int acc_iter = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total);
+      const Unit w = decode_unit(u, num_m, num_n, args.splits, kb_total, args.full_tiles);
       if (w.kb_end <= w.kb_begin) continue;
       const int acc = acc_iter & 1;
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
@@ -406,14 +482,25 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           } else if constexpr (EPI == kSwiGLU) {
-            // adjacent lanes hold (gate_j, up_j); even lanes write silu(g)*u
-            __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C);
+            if (w.partial) {
+              // split-K: the partial tile goes to this split's workspace slice
+              float* P = static_cast<float*>(args.aux) +
+                         static_cast<long>(w.split) * args.ldaux * static_cast<long>(args.N);
+              if (m < args.M) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float partner = __shfl_xor_sync(0xffffffffu, v[j], 1);
-              if ((lane & 1) == 0 && m < args.M && nc + j < args.N) {
-                C[static_cast<long>(nc + j) * args.ldc + (m >> 1)] =
-                    __float2bfloat16(silu_f(v[j]) * partner);
+                for (int j = 0; j < 32; ++j)
+                  if (nc + j < args.N) __stcg(P + static_cast<long>(nc + j) * args.ldaux + m, v[j]);
+              }
+            } else {
+              // adjacent lanes hold (gate_j, up_j); even lanes write silu(g)*u
+              __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float partner = __shfl_xor_sync(0xffffffffu, v[j], 1);
+                if ((lane & 1) == 0 && m < args.M && nc + j < args.N) {
+                  C[static_cast<long>(nc + j) * args.ldc + (m >> 1)] =
+                      __float2bfloat16(silu_f(v[j]) * partner);
+                }
               }
             }
           } else if constexpr (EPI == kStoreF32) {
@@ -575,6 +662,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (SWAP && EPI == kAtomicF32) {
         if (args.npeers > 1) push_tile_impl<BN>(args, w, num_n, m, row_in_tile);
       }
+      if constexpr (SWAP && EPI == kSwiGLU) {
+        if (w.partial) swiglu_fixup_impl<BN>(args, w, num_n, m, row_in_tile);
+      }
     }
   }
 
@@ -610,7 +700,7 @@ void launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& 
   }
   const int num_m = (args.M + BM - 1) / BM;
   const int num_n = (args.N + BN - 1) / BN;
-  const int units = num_m * num_n * args.splits;
+  const int units = unit_count(num_m * num_n, args.splits, args.full_tiles);
   int grid = std::min(units, num_sms(device));
   if (max_ctas > 0) grid = std::min(grid, max_ctas);
   grid = std::max(grid, 1);

@@ -107,6 +107,18 @@ def bench_decode(args) -> None:
             epi = "store_f32" if name == "lm_head" else "store"
             fn = lambda: gemm(w, x, out, swap=True, epilogue=epi)  # noqa: E731
         ms = timer(fn)
+        if name == "gate_up":
+            # the decode step runs gate/up as split-K 3 with a last-split SwiGLU
+            act = torch.empty(T, n // 2, device="cuda", dtype=torch.bfloat16)
+            ws = torch.empty(4 * T * n, device="cuda")
+            ctr = torch.zeros(-(-n // 128) * -(-T // 64), device="cuda", dtype=torch.int32)
+            for sp in (1, 2, 3, 4):
+                kw = dict(aux=ws, tile_ctr=ctr) if sp > 1 else {}
+                ms_s = timer(lambda: gemm(w, x, act, swap=True, epilogue="swiglu", splits=sp, **kw))  # noqa: B023
+                print(json.dumps({"kernel": "gemm_tc_swap_swiglu", "tokens": T, "n": n, "k": k, "splits": sp,
+                                  "ms": round(ms_s, 4),
+                                  "frac_of_measured_hbm": round(n * k * 2 / ms_s / 1e6 / peaks["hbm_gbs"], 3)}),
+                      flush=True)
         ref = timer(lambda: torch.matmul(x, w.T))
         check_errors()
         nbytes = n * k * 2 + T * k * 2
@@ -266,6 +278,15 @@ def bench_profile(args) -> None:
     if k == "gemm":
         x, w = torch.randn(8192, 4096, device="cuda").bfloat16(), torch.randn(24576, 4096, device="cuda").bfloat16()
         runs.append(lambda: gemm(x, w, epilogue="swiglu"))
+    elif k in ("gemm_gu_decode", "gemm_gu_decode_s1"):
+        # decode gate/up: 64 tokens, swap layout, SwiGLU epilogue, split-K 3 (or 1)
+        splits = 1 if k.endswith("_s1") else 3
+        w, x = torch.randn(24576, 4096, device="cuda").bfloat16(), torch.randn(64, 4096, device="cuda").bfloat16()
+        out = torch.empty(64, 12288, device="cuda", dtype=torch.bfloat16)
+        ws = torch.empty(splits * 64 * 24576, device="cuda")
+        ctr = torch.zeros(192, device="cuda", dtype=torch.int32)
+        kw = dict(aux=ws, tile_ctr=ctr) if splits > 1 else {}
+        runs.append(lambda: gemm(w, x, out, swap=True, epilogue="swiglu", splits=splits, **kw))
     elif k == "gemm_mn":
         dy, w = torch.randn(8192, 24576, device="cuda").bfloat16(), torch.randn(24576, 4096, device="cuda").bfloat16()
         runs.append(lambda: gemm(dy, w, b_mn=True))

@@ -68,6 +68,19 @@ def decode_attention_splits(rows: int, nkv: int, capacity: int, sms: int = 148) 
     return int(max(1, min(want, capacity // 256, 16)))
 
 
+def swap_gemm_splits(out_features: int, rows: int, sms: int = 148, max_splits: int = 4) -> int:
+    """Split-K factor for a swap-layout decode GEMM: the fewest splits that
+    minimise the time of the last wave (units = 128-feature tiles x splits,
+    persistent CTAs, one per SM), each split costing 1/splits of a tile."""
+    tiles = -(-out_features // 128) * -(-rows // 64)
+    best, best_t = 1, float("inf")
+    for s in range(1, max_splits + 1):
+        t = -(-tiles * s // sms) / s
+        if t < best_t - 1e-9:
+            best, best_t = s, t
+    return best
+
+
 def _round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
@@ -376,6 +389,15 @@ class FusedRolloutEngine:
             self._peer_sites[key] = site
         return site
 
+    def _gu_splits(self, rows: int) -> int:
+        """Split-K for gate/up only when its tiles fill less than half of the
+        SMs (TP >= 4 shards): the split partials' fixup through L2 measured
+        slower than a partial last wave on the full-width projection."""
+        if self.m.device.type != "cuda":
+            return 1
+        tiles = -(-2 * self.m.inter_local // 128) * -(-rows // 64)
+        return swap_gemm_splits(2 * self.m.inter_local, rows) if 2 * tiles <= 148 else 1
+
     def _decode_buffers(self, rows: int, tails: dict[str, int]) -> dict[str, torch.Tensor]:
         m = self.m
         dev, dt = m.device, m.dtype
@@ -396,6 +418,9 @@ class FusedRolloutEngine:
             # U = s A xn of the gate/up LoRA (the K-extension operand of that GEMM)
             "u_gu": torch.zeros(rows, max(tails.get("u_gu", 0), 1), device=dev, dtype=dt),
             "act": torch.empty(rows, m.inter_local, device=dev, dtype=dt),
+            # split-K gate/up: per-split fp32 partial tiles and per-tile arrival counters
+            "gu_ws": torch.empty(self._gu_splits(rows) * rows * 2 * m.inter_local, device=dev, dtype=f32),
+            "gu_ctr": torch.zeros(-(-2 * m.inter_local // 128) * -(-rows // 64), device=dev, dtype=torch.int32),
             "d_ws": torch.zeros(rows, H + tails.get("w_down", 0), device=dev, dtype=f32),
             "logits": (torch.empty(rows, m.vocab_local, device=dev, dtype=f32) if m.include_head
                        else torch.empty(0, device=dev)),
@@ -461,8 +486,10 @@ class FusedRolloutEngine:
                           a_gu[: 2 * r] if a_gu is not None else None, ug, 1.0, eps,
                           BT["o"], r if has_o else 0, **o_norm,
                           zero_tail=b["qkv_u"] if has_qkv else None)
+            gu_splits = self._gu_splits(rows)
             gemm(lw.w_gu, b["xn"], b["act"], ext_ab=(L["b_gu"], ug) if a_gu is not None else None,
-                 swap=True, epilogue="swiglu")
+                 swap=True, epilogue="swiglu", splits=gu_splits,
+                 aux=b["gu_ws"] if gu_splits > 1 else None, tile_ctr=b["gu_ctr"] if gu_splits > 1 else None)
             has_d = "a_down" in L
             gemm(lw.w_down_ext if has_d else lw.w_down, b["act"], b["d_ws"], swap=True, epilogue="atomic",
                  splits=4, push=sd)

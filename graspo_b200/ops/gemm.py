@@ -9,6 +9,10 @@
 * ``epilogue``: ``store`` (bf16), ``store_f32``, ``atomic`` (fp32 +=, allows
   split-K), ``swiglu`` (b rows interleave gate/up; output N/2 columns),
   ``lse`` (row log-sum-exp partials + target logits), ``softmax_grad``.
+* ``splits`` > 1 with ``swiglu`` in swap mode: split-K whose partial tiles go to
+  ``aux`` (fp32, ``splits x tokens x features``) and whose last split per
+  tile applies the activation; ``tile_ctr`` is a zeroed int32 counter per
+  output tile (left zeroed by the kernel).
 * ``swap=True``: ``a`` is the weight ``[N_out, K]`` and ``b`` the activations
   ``[T, K]``; the result is stored as ``[T, N_out]``.  This is the decode
   shape: tokens fill the narrow N side of the tensor-core tile.
@@ -60,6 +64,7 @@ def gemm(
     splits: int = 1,
     max_ctas: int = 0,
     push=None,
+    tile_ctr: torch.Tensor | None = None,
     a_mn: bool = False,
     b_mn: bool = False,
 ) -> torch.Tensor:
@@ -87,6 +92,8 @@ def gemm(
     if b_mn:
         bn = max(bn, 64)
     kw = push.gemm_kwargs() if push is not None else {}
+    if tile_ctr is not None:
+        kw["tile_ctr"] = tile_ctr
     layout = (2 if a_mn else 0) | (1 if b_mn else 0)
     ext().gemm_tc(
         a, b, a2, b2, out, residual, aux, targets, tgt_logit, row_lse, row_scale,

@@ -138,13 +138,14 @@ def test_gemm_swap_swiglu_and_residual():
     _close(gemm(w, x, swap=True, residual=r), x.float() @ w.float().T + r.float(), 2e-2)
 
 
-@pytest.mark.parametrize("t,splits", [(64, 3), (40, 2), (100, 4)])
-def test_gemm_swap_swiglu_split_k(t, splits):
+@pytest.mark.parametrize("t,splits,i", [(64, 3, 640), (40, 2, 640), (100, 4, 640), (64, 3, 10000)])
+def test_gemm_swap_swiglu_split_k(t, splits, i):
     """Split-K SwiGLU: per-split fp32 partial tiles, the last split of each tile
-    applies the activation; counters are left zeroed for the next call."""
+    applies the activation; counters are left zeroed for the next call.  With
+    more tiles than SMs (i = 10000) only the last wave's tiles are split."""
     from graspo_b200.ops.gemm import gemm
 
-    i, k = 640, 1024
+    k = 1024
     wg, wu, x = _rand(i, k, scale=0.05), _rand(i, k, scale=0.05), _rand(t, k)
     a2, b2 = _rand(2 * i, 64, scale=0.05), _rand(t, 64, scale=0.5)    # LoRA-style K extension
     inter = torch.stack([wg, wu], dim=1).reshape(2 * i, k).contiguous()
