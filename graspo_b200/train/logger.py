@@ -3,7 +3,8 @@
 File names follow the reference layout (backends/graspoflow/logger.py):
 ``rollouts.readable.jsonl`` (compact per-group view), ``rollouts.raw.jsonl``
 (everything, tensors as lists), ``train_batches.readable.jsonl``,
-``timing_events.jsonl``, ``error.log`` (invalid groups, failures) and
+``timing_events.jsonl``, ``error.log`` (invalid groups, failures), ``events.jsonl``
+(every stdout event of the primary rank, for post-run analysis) and
 ``rank_metrics.rank_NNNNN.jsonl`` (per-rank memory/metrics events).
 """
 
@@ -123,3 +124,11 @@ class RolloutLogger:
 
     def write_error(self, payload: dict[str, Any]) -> None:
         self._append(self.error_path, to_jsonable(payload))
+
+
+def append_event(output_dir: str | Path, payload: dict[str, Any]) -> None:
+    """Append one stdout event to ``<output_dir>/logs/events.jsonl``."""
+    path = Path(output_dir) / "logs" / "events.jsonl"
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with path.open("a", encoding="utf-8") as handle:
+        handle.write(json.dumps(payload, ensure_ascii=False, default=str) + "\n")

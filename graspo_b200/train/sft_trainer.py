@@ -19,6 +19,7 @@ from pathlib import Path
 
 from graspo_b200.core.data import load_jsonl, sft_tokenize
 from graspo_b200.core.logging import setup_logging
+from graspo_b200.train.logger import append_event
 from graspo_b200.engine.runtime import GraspoFlowRuntime
 
 log = logging.getLogger("graspo.sft")
@@ -33,6 +34,7 @@ class SFTTrainer:
     def _emit(self, payload: dict) -> None:
         if self.runtime.is_primary():
             print(json.dumps(payload, ensure_ascii=False, default=str), flush=True)
+            append_event(self.config.training.output_dir, payload)
 
     def _checkpoint(self, path: Path, epoch: int) -> None:
         state = {"format": "graspoflow-trainer-state", "version": 1, "global_step": self.global_step,

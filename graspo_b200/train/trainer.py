@@ -41,7 +41,7 @@ from graspo_b200.core.logging import setup_logging
 from graspo_b200.core.reward import GraspoReward
 from graspo_b200.core.schema import GraspoConfig
 from graspo_b200.engine.runtime import GraspoFlowRuntime, validate_graspoflow_runtime_config
-from graspo_b200.train.logger import RolloutLogger
+from graspo_b200.train.logger import RolloutLogger, append_event
 from graspo_b200.train.summary import (
     compact_batch_summary,
     compact_decisions,
@@ -181,6 +181,7 @@ class GraspoTrainer:
     def _emit(self, payload: dict[str, Any]) -> None:
         if self._is_primary():
             print(json.dumps(payload, ensure_ascii=False, default=str), flush=True)
+            append_event(self.config.training.output_dir, payload)
 
     def _dp(self) -> tuple[int, int]:
         ps = self.ps
