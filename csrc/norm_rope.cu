@@ -173,22 +173,13 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
             x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
           }
           if (dlb != nullptr) {
-            // B^T [r, H]: rank row j holds the 8 columns of this chunk contiguously;
-            // 8 rank rows per pass so their loads are in flight together
-            for (int j0 = 0; j0 < dlr; j0 += 8) {
-              uint4 raw[8];
+            // B^T [r, H]: rank row j holds the 8 columns of this chunk contiguously
+            for (int j = 0; j < dlr; ++j) {
+              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(dlb + static_cast<long>(j) * ldb + col));
+              const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+              const float u = dus[j];
 #pragma unroll
-              for (int jj = 0; jj < 8; ++jj)
-                raw[jj] = j0 + jj < dlr
-                              ? __ldg(reinterpret_cast<const uint4*>(dlb + static_cast<long>(j0 + jj) * ldb + col))
-                              : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw[jj]);
-                const float u = j0 + jj < dlr ? dus[j0 + jj] : 0.f;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(bb[e]) * u;
-              }
+              for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(bb[e]) * u;
             }
           }
           *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -410,22 +401,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
       const int blk = hd < a.nq ? 0 : (hd < a.nq + a.nkv ? 1 : 2);
       const float* u = us + blk * a.lora_r;  // L1/L2-served broadcast reads
       // B^T [3r, W]: rank row (blk r + j) holds this lane's 4 columns contiguously
-      // 8 rank rows per pass so their loads are in flight together
-      for (int j0 = 0; j0 < a.lora_r; j0 += 8) {
-        uint2 raw[8];
+      for (int j = 0; j < a.lora_r; ++j) {
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(
+            a.lora_b + static_cast<long>(blk * a.lora_r + j) * a.ldb + hd * D + lane * 4));
+        const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+        const float uj = u[j];
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj)
-          raw[jj] = j0 + jj < a.lora_r
-                        ? __ldg(reinterpret_cast<const uint2*>(
-                              a.lora_b + static_cast<long>(blk * a.lora_r + j0 + jj) * a.ldb + hd * D + lane * 4))
-                        : make_uint2(0u, 0u);
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw[jj]);
-          const float uj = j0 + jj < a.lora_r ? u[j0 + jj] : 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]) * uj;
-        }
+        for (int e = 0; e < 4; ++e) x[e] += __bfloat162float(bb[e]) * uj;
       }
     }
 #pragma unroll
