@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import json
 import math
+import os
 import random
 import time
 from pathlib import Path
@@ -459,6 +460,20 @@ class Qwen3Adapter:
         self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed)
 
     # ------------------------------------------------------------ training
+    def check_replicas(self) -> None:
+        """Debug check (``GRASPO_CHECK_REPLICAS=1``, after every optimize call):
+        the LoRA parameters are bit-identical across data-parallel replicas and
+        their TP-replicated part is identical across the tensor-parallel group."""
+        from graspo_b200.parallel.state import replica_mismatches
+
+        ps, lora = self.ps, self.model.lora
+        bad = replica_mismatches(lora.params, ps.dp_group if ps.dp_size > 1 else None, name="lora (dp)")
+        rep = lora.replicated_numel
+        if rep:
+            bad += replica_mismatches(lora.params[:rep], ps.tp_group if ps.tp_size > 1 else None, name="lora (tp)")
+        if bad:
+            raise RuntimeError("replicated LoRA state diverged: " + "; ".join(bad))
+
     def _dp_average_grads(self) -> None:
         ps = self.ps
         g = self.model.lora.grads
@@ -548,6 +563,8 @@ class Qwen3Adapter:
                 norms.append(norm)
                 steps += 1
         self._train_batch_call_index += 1
+        if os.environ.get("GRASPO_CHECK_REPLICAS", "0") == "1":
+            self.check_replicas()
         loss_vals = [float(x) for x in torch.cat(losses).cpu()] if losses else []
         norm_vals = [float(x) for x in torch.cat([n.reshape(1) for n in norms]).cpu()] if norms else []
         skipped = int(self.optimizer.skipped.item())

@@ -161,3 +161,25 @@ def destroy() -> None:
         finally:
             dist.destroy_process_group()
     _STATE = None
+
+
+def replica_mismatches(tensor: torch.Tensor, group, *, name: str = "tensor") -> list[str]:
+    """Debug check that a tensor meant to be replicated over ``group`` holds the
+    same bits on every member: all-gathers a 64-bit digest of its bytes and
+    returns one message per rank that disagrees with the group's first rank
+    (empty when consistent or when the group has one member)."""
+    if group is None or not dist.is_available() or not dist.is_initialized():
+        return []
+    n = dist.get_world_size(group)
+    if n <= 1:
+        return []
+    flat = tensor.detach().contiguous().view(-1)
+    words = flat.view(torch.int32) if flat.element_size() == 4 else flat.float().view(torch.int32)
+    w = words.to(torch.int64)
+    idx = torch.arange(w.numel(), device=w.device, dtype=torch.int64)
+    digest = torch.stack([(w * (idx % 8191 + 1)).sum(), (w ^ (idx * 2654435761 % (1 << 31))).sum()])
+    gathered = [torch.empty_like(digest) for _ in range(n)]
+    dist.all_gather(gathered, digest, group=group)
+    ranks = dist.get_process_group_ranks(group)
+    return [f"{name}: rank {ranks[i]} differs from rank {ranks[0]}" for i in range(1, n)
+            if not torch.equal(gathered[i], gathered[0])]

@@ -141,3 +141,83 @@ def test_tp2_lora_grads_equal_tp1(tmp_path):
     ref_file = tmp_path / "ref.pt"
     torch.save({"grads": {k: (v[0], v[1]) for k, v in grads.items()}, "lp": lp}, ref_file)
     run_world(2, _tp2_worker, path, (seq, mask), ref_file)
+
+
+def _dp2_worker(rank, world, path, batch, ref_file):
+    """DP = 2: each replica takes half the rows; the mean-loss gradients averaged
+    over the replicas (the adapter's DP step) equal the single-replica gradients
+    of the whole batch, and the replica check passes."""
+    from types import SimpleNamespace
+
+    from graspo_b200.engine.adapter import Qwen3Adapter
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import EagerLoRA, Qwen3Model, eager_stage_forward, eager_token_logprobs
+    from graspo_b200.parallel import state as pstate
+
+    ps = pstate.initialize(1, 1, 2, timeout_sec=60, device="cpu")
+    assert ps.dp_size == 2 and ps.tp_size == 1
+    m = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=TINY_TARGETS, lora_r=4,
+                   lora_alpha=8, lora_dropout=0.0, dtype=torch.float32, device=ps.device, seed=3)
+    with torch.no_grad():
+        m.lora.params.copy_(torch.load(ref_file)["params"])
+    seq, mask = batch
+    half = seq.shape[0] // 2
+    rows = slice(rank * half, (rank + 1) * half)
+    lora = EagerLoRA(m.lora, requires_grad=True)
+    hidden = eager_stage_forward(m, seq[rows], mask[rows], lora=lora, training=True)
+    lp = eager_token_logprobs(m, hidden[:, :-1], seq[rows, 1:])
+    w = mask[rows, 1:].float()
+    ((lp * w).sum() / w.sum()).backward()
+    lora.accumulate_grads()
+    fake = SimpleNamespace(ps=ps, model=m)
+    Qwen3Adapter._dp_average_grads(fake)
+    ref = torch.load(ref_file)["grads"]
+    assert torch.allclose(m.lora.grads, ref, atol=1e-6, rtol=1e-4), (m.lora.grads - ref).abs().max()
+    Qwen3Adapter.check_replicas(fake)   # identical parameters on both replicas
+    if rank == 1:
+        with torch.no_grad():
+            m.lora.params[0] += 1.0
+    try:
+        Qwen3Adapter.check_replicas(fake)
+    except RuntimeError as exc:
+        assert "lora (dp)" in str(exc)
+    else:
+        raise AssertionError("a diverged replica was not reported")
+    torch.distributed.destroy_process_group()
+
+
+@pytest.mark.slow
+def test_dp2_grads_equal_dp1_and_replica_check(tmp_path):
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import EagerLoRA, Qwen3Model, eager_stage_forward, eager_token_logprobs
+    from graspo_b200.parallel import state as pstate
+
+    path = _tiny_ckpt(tmp_path / "ckpt")
+    g = torch.Generator().manual_seed(1)
+    seq = torch.randint(0, 2040, (4, 20), generator=g)
+    mask = torch.ones(4, 20, dtype=torch.bool)
+    mask[0, :4] = False
+    mask[3, -3:] = False
+    os.environ.pop("WORLD_SIZE", None)
+    ps = pstate.initialize(1, 1, timeout_sec=60, device="cpu")
+    m = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=TINY_TARGETS, lora_r=4,
+                   lora_alpha=8, lora_dropout=0.0, dtype=torch.float32, device=ps.device, seed=3)
+    with torch.no_grad():
+        m.lora.params.normal_(0, 0.05)
+    # the reference: mean over each half, averaged (equal-size halves, per-replica normalisation)
+    grads = torch.zeros_like(m.lora.grads)
+    for rows in (slice(0, 2), slice(2, 4)):
+        m.lora.grads.zero_()
+        lora = EagerLoRA(m.lora, requires_grad=True)
+        hidden = eager_stage_forward(m, seq[rows], mask[rows], lora=lora, training=True)
+        lp = eager_token_logprobs(m, hidden[:, :-1], seq[rows, 1:])
+        w = mask[rows, 1:].float()
+        ((lp * w).sum() / w.sum()).backward()
+        lora.accumulate_grads()
+        grads += m.lora.grads / 2
+    ref_file = tmp_path / "ref.pt"
+    torch.save({"grads": grads, "params": m.lora.params.clone()}, ref_file)
+    pstate.destroy()
+    run_world(2, _dp2_worker, path, (seq, mask), ref_file)
