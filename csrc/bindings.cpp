@@ -26,7 +26,7 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
                   c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps,
-                  c10::optional<torch::Tensor> lora_b, int64_t lora_r);
+                  c10::optional<torch::Tensor> lora_b, int64_t lora_r, c10::optional<torch::Tensor> err);
 void qk_norm_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv,
                       torch::Tensor q_w, torch::Tensor k_w, torch::Tensor inv_freq, torch::Tensor pos,
                       torch::Tensor dqkv, int64_t nq, int64_t nkv, double eps);
@@ -35,6 +35,7 @@ void lora_down(torch::Tensor x, torch::Tensor A, torch::Tensor U, double scale);
 void gated_delta_step(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                       torch::Tensor state, torch::Tensor out);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
+bool kernel_checks();
 void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                     torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale);
 void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
@@ -49,7 +50,7 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
                             c10::optional<torch::Tensor> scratch, int64_t prefix_len, int64_t group_rows,
-                            int64_t prefix_splits);
+                            int64_t prefix_splits, c10::optional<torch::Tensor> err);
 void sample_append(torch::Tensor logits, double temperature, double top_p, int64_t seed,
                    torch::Tensor next_ids, torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len,
                    torch::Tensor finished, torch::Tensor out_tokens, int64_t prompt_slots,
@@ -89,16 +90,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope", &gb::qk_norm_rope, py::arg("qkv"), py::arg("q_w"), py::arg("k_w"), py::arg("inv_freq"),
         py::arg("pos"), py::arg("q_out"), py::arg("k_out"), py::arg("v_out"), py::arg("block_table"),
         py::arg("row_of_token"), py::arg("slot"), py::arg("nq"), py::arg("nkv"), py::arg("page_size"),
-        py::arg("eps"), py::arg("lora_b") = py::none(), py::arg("lora_r") = 0);
+        py::arg("eps"), py::arg("lora_b") = py::none(), py::arg("lora_r") = 0, py::arg("err") = py::none());
   m.def("qk_norm_rope_bwd", &gb::qk_norm_rope_bwd);
   m.def("swiglu_bwd", &gb::swiglu_bwd);
   m.def("lora_down", &gb::lora_down);
   m.def("gated_delta_step", &gb::gated_delta_step, "one decoding step of the gated delta rule");
   m.def("embedding", &gb::embedding);
+  m.def("kernel_checks", &gb::kernel_checks, "true when built with GRASPO_KERNEL_CHECKS (index checks)");
   m.def("paged_decode_attention", &gb::paged_decode_attention, py::arg("q"), py::arg("k_pool"), py::arg("v_pool"),
         py::arg("block_table"), py::arg("start"), py::arg("len"), py::arg("out"), py::arg("scale"),
         py::arg("splits"), py::arg("scratch"), py::arg("prefix_len") = 0, py::arg("group_rows") = 1,
-        py::arg("prefix_splits") = 1);
+        py::arg("prefix_splits") = 1, py::arg("err") = py::none());
   m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
   m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
   m.def("flash_attn_fwd_tc", &gb::flash_attn_fwd_tc, "causal flash attention forward on tcgen05 / TMEM");

@@ -56,6 +56,8 @@ struct DecodeAttnArgs {
   // (prefix_splits key slices, 4 partial slots each); the split kernels then
   // cover [prefix_len, len) and merge prefix_slots + splits partials per row.
   int prefix_len, group_rows, prefix_splits, prefix_kps, prefix_slots;
+  int num_pages;  // pages in the pools (kernel-checks builds validate block-table entries)
+  int* err;
 };
 
 template <int G>
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
   for (int c = first_chunk + warp; c <= last_chunk && k_end > k_begin; c += kWarps) {
     const int t = c * 32 + lane;
     const bool valid = t >= k_begin && t < k_end;
-    const int page = valid ? bt[t / a.page_size] : bt[(c * 32) / a.page_size];
+    const int page = checked_index(valid ? bt[t / a.page_size] : bt[(c * 32) / a.page_size], a.num_pages, a.err);
     const long kv_off = ((static_cast<long>(page) * a.nkv + kvh) * a.page_size + (t % a.page_size)) * kD;
     float s[G];
 #pragma unroll
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
     const int n_valid_lo = max(0, k_begin - c * 32);
     for (int j = n_valid_lo; j < n_valid_hi; ++j) {
       const int tj = c * 32 + j;
-      const int pg = bt[tj / a.page_size];
+      const int pg = checked_index(bt[tj / a.page_size], a.num_pages, a.err);
       const long off = ((static_cast<long>(pg) * a.nkv + kvh) * a.page_size + (tj % a.page_size)) * kD + lane * 4;
       const uint2 vr = *reinterpret_cast<const uint2*>(a.v_pool + off);
       const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vr);
@@ -355,7 +357,7 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
 
   auto load_tile = [&](int tile, int stage) {
     const int t0 = tile * kTile;
-    const int phys = bt[t0 / a.page_size];
+    const int phys = checked_index(bt[t0 / a.page_size], a.num_pages, a.err);
     const long base = ((static_cast<long>(phys) * a.nkv + kvh) * a.page_size + (t0 % a.page_size)) * kD;
     const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.k_pool + base);
     const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.v_pool + base);
@@ -547,7 +549,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
 
   auto load_tile = [&](int tile, int stage) {
     const int t0 = tile * kTile;
-    const int phys = page_of(t0);
+    const int phys = checked_index(page_of(t0), a.num_pages, a.err);
     const long base = ((static_cast<long>(phys) * a.nkv + kvh) * a.page_size + (t0 % a.page_size)) * kD;
     const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(a.k_pool + base);
     const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(a.v_pool + base);
@@ -730,11 +732,13 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
 // scratch: optional fp32 buffer of at least rows*nq*splits*(D+2) floats plus
 // rows*nkv ints for the counters (zero-initialised once); required when the
 // launch is split.
+bool kernel_checks() { return kKernelChecks; }
+
 void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
                             torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
                             torch::Tensor out, double scale, int64_t splits,
                             c10::optional<torch::Tensor> scratch, int64_t prefix_len, int64_t group_rows,
-                            int64_t prefix_splits) {
+                            int64_t prefix_splits, c10::optional<torch::Tensor> err) {
   const c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.is_contiguous(), "q must be contiguous bf16");
   TORCH_CHECK(k_pool.dim() == 4 && k_pool.size(3) == kD, "k_pool must be [pages, nkv, page, 128]");
@@ -746,6 +750,8 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
   const int G = nq / nkv;
   const int max_pages = static_cast<int>(block_table.size(1));
   DecodeAttnArgs a{};
+  a.num_pages = static_cast<int>(k_pool.size(0));
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   a.k_pool = reinterpret_cast<const __nv_bfloat16*>(k_pool.data_ptr());
   a.v_pool = reinterpret_cast<const __nv_bfloat16*>(v_pool.data_ptr());
@@ -971,6 +977,7 @@ extern "C" int graspo_paged_decode_attention_noalloc(const void* q, const void* 
     return GB_NOALLOC_LAUNCH_FAILED;
   }
   DecodeAttnArgs a{};
+  a.num_pages = 0x7fffffff;  // the C entry point has no pool size: block-table entries are trusted
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k_pool = static_cast<const __nv_bfloat16*>(k_pool);
   a.v_pool = static_cast<const __nv_bfloat16*>(v_pool);

@@ -29,6 +29,8 @@ namespace gb {
 namespace {
 
 constexpr int kNormThreads = 256;
+constexpr int kStageBytes = 64 * 1024;   // one slot of the LoRA weight-row ring
+constexpr int kMaxLoraRows = 128;        // LoRA-down outputs per row (2 r for gate/up, r <= 64)
 
 template <int VEC>
 struct BF16Vec {
@@ -120,10 +122,50 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
                                    float* __restrict__ zero_tail, long zero_ld, int zero_n) {
   constexpr int MAXC = 4;  // chunks of 8 per thread: H <= 256*8*4 = 8192
   __shared__ float red[32];
-  __shared__ float ured[8][64];
+  __shared__ float ured[8][kMaxLoraRows];
   __shared__ float dus[64];
+  __shared__ uint64_t stage_bar[2];
+  extern __shared__ __align__(16) uint8_t stage_smem[];   // 2 x kStageBytes when LoRA rows are staged
   const long row = blockIdx.x;
   const __nv_bfloat16* hr = h + row * H;
+  // LoRA weight rows (B^T of the delta's LoRA, then A of this norm's LoRA-down)
+  // stream through a two-slot shared-memory ring as 1-D bulk copies of whole
+  // rows: every thread then reads its columns from shared memory instead of
+  // waiting on one global load per rank row.
+  const int pass_rows = kStageBytes / (H * 2);
+  const int b_rows = (HAS_DELTA && DELTA_F32 && dlb != nullptr) ? dlr : 0;
+  const int a_rows = LORA ? R : 0;
+  const int b_passes = (b_rows + pass_rows - 1) / pass_rows;
+  const int n_passes = b_passes + (a_rows + pass_rows - 1) / pass_rows;
+  auto pass_src = [&](int k, int& r0, int& nr) -> const __nv_bfloat16* {
+    if (k < b_passes) {
+      r0 = k * pass_rows;
+      nr = min(pass_rows, b_rows - r0);
+      return dlb + static_cast<long>(r0) * H;
+    }
+    r0 = (k - b_passes) * pass_rows;
+    nr = min(pass_rows, a_rows - r0);
+    return lora_a + static_cast<long>(r0) * H;
+  };
+  auto issue = [&](int k) {
+    if (threadIdx.x == 0 && k < n_passes) {
+      int r0, nr;
+      const __nv_bfloat16* src = pass_src(k, r0, nr);
+      const uint32_t bytes = static_cast<uint32_t>(nr) * H * 2;
+      mbar_arrive_expect_tx(&stage_bar[k & 1], bytes);
+      bulk_copy_g2s(stage_smem + (k & 1) * kStageBytes, src, bytes, &stage_bar[k & 1]);
+    }
+  };
+  if (n_passes > 0) {
+    if (threadIdx.x == 0) {
+      mbar_init(&stage_bar[0], 1);
+      mbar_init(&stage_bar[1], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    issue(0);  // frozen weights: fetched before waiting on the producing kernel
+    issue(1);
+  }
   pdl_trigger();
   pdl_wait();
   const bool peers = HAS_DELTA && DELTA_F32 && ps.n > 1;
@@ -172,16 +214,6 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
             x[c][0] += d0.x; x[c][1] += d0.y; x[c][2] += d0.z; x[c][3] += d0.w;
             x[c][4] += d1.x; x[c][5] += d1.y; x[c][6] += d1.z; x[c][7] += d1.w;
           }
-          if (dlb != nullptr) {
-            // B^T [r, H]: rank row j holds the 8 columns of this chunk contiguously
-            for (int j = 0; j < dlr; ++j) {
-              const uint4 raw = __ldg(reinterpret_cast<const uint4*>(dlb + static_cast<long>(j) * ldb + col));
-              const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
-              const float u = dus[j];
-#pragma unroll
-              for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(bb[e]) * u;
-            }
-          }
           *reinterpret_cast<float4*>(d) = make_float4(0.f, 0.f, 0.f, 0.f);
           *reinterpret_cast<float4*>(d + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
         } else {
@@ -191,6 +223,37 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
 #pragma unroll
           for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(db[e]);
         }
+      }
+    }
+  }
+  // B^T [r, H] rows (rank row j holds every column): x += B U, in rank order
+  bool staged_ok = true;
+  for (int k = 0; k < b_passes; ++k) {
+    int r0, nr;
+    pass_src(k, r0, nr);
+    staged_ok = staged_ok && mbar_wait(&stage_bar[k & 1], (k >> 1) & 1, ps.err, kErrTmaFullTimeout);
+    const uint8_t* st = stage_smem + (k & 1) * kStageBytes;
+    for (int jj = 0; jj < nr && staged_ok; ++jj) {
+      const float u = dus[r0 + jj];
+#pragma unroll
+      for (int c = 0; c < MAXC; ++c) {
+        const int col = (threadIdx.x + c * kNormThreads) * 8;
+        if (col < H) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(st + (static_cast<long>(jj) * H + col) * 2);
+          const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[c][e] += __bfloat162float(bb[e]) * u;
+        }
+      }
+    }
+    __syncthreads();  // slot k & 1 is free again
+    if (staged_ok) issue(k + 2);
+  }
+#pragma unroll
+  for (int c = 0; c < MAXC; ++c) {
+    const int col = (threadIdx.x + c * kNormThreads) * 8;
+    if (col < H) {
+      if constexpr (HAS_DELTA) {
         // the residual stream is stored in bf16: round the sum once
         uint4 out;
         __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(&out);
@@ -227,41 +290,33 @@ __global__ void add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ h, const vo
   if constexpr (LORA) {
     // U[row, j] = scale * sum_k y[k] * A[j, k]   for j < R; zero for R <= j < ldu
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int j0 = 0; j0 < R; j0 += 64) {
-      const int jn = min(64, R - j0);
-      for (int j = 0; j < jn; j += 16) {
-        // 16 rank rows per pass: their loads are issued together
-        float p[16];
+    for (int k = b_passes; k < n_passes; ++k) {
+      int r0, nr;
+      pass_src(k, r0, nr);
+      staged_ok = staged_ok && mbar_wait(&stage_bar[k & 1], (k >> 1) & 1, ps.err, kErrTmaFullTimeout);
+      const uint8_t* st = stage_smem + (k & 1) * kStageBytes;
+      for (int jj = 0; jj < nr && staged_ok; ++jj) {
+        float p = 0.f;
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          p[jj] = 0.f;
-          if (j + jj < jn) {
-            const __nv_bfloat16* arow = lora_a + static_cast<long>(j0 + j + jj) * H;
+        for (int c = 0; c < MAXC; ++c) {
+          const int col = (threadIdx.x + c * kNormThreads) * 8;
+          if (col < H) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(st + (static_cast<long>(jj) * H + col) * 2);
+            const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-            for (int c = 0; c < MAXC; ++c) {
-              const int col = (threadIdx.x + c * kNormThreads) * 8;
-              if (col < H) {
-                uint4 araw = __ldg(reinterpret_cast<const uint4*>(arow + col));
-                const __nv_bfloat16* ab = reinterpret_cast<const __nv_bfloat16*>(&araw);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) p[jj] += x[c][e] * __bfloat162float(ab[e]);
-              }
-            }
+            for (int e = 0; e < 8; ++e) p += x[c][e] * __bfloat162float(ab[e]);
           }
         }
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const float v = warp_sum(p[jj]);
-          if (lane == 0 && j + jj < jn) ured[warp][j + jj] = v;
-        }
+        p = warp_sum(p);
+        if (lane == 0) ured[warp][r0 + jj] = p;
       }
-      __syncthreads();
-      if (threadIdx.x < jn) {
-        float s = 0.f;
-        for (int wi = 0; wi < kNormThreads / 32; ++wi) s += ured[wi][threadIdx.x];
-        lora_u[row * ldu + j0 + threadIdx.x] = __float2bfloat16(s * scale);
-      }
-      __syncthreads();
+      __syncthreads();  // slot k & 1 is free again; ured rows of this pass are complete
+      if (staged_ok) issue(k + 2);
+    }
+    for (int j = threadIdx.x; j < R; j += blockDim.x) {
+      float s = 0.f;
+      for (int wi = 0; wi < kNormThreads / 32; ++wi) s += ured[wi][j];
+      lora_u[row * ldu + j] = __float2bfloat16(staged_ok ? s * scale : 0.f);
     }
     for (int j = R + threadIdx.x; j < ldu; j += blockDim.x) lora_u[row * ldu + j] = __float2bfloat16(0.f);
   }
@@ -358,6 +413,8 @@ struct RopeArgs {
   const int* block_table;   // [rows, max_pages]
   int max_pages;
   int page_size;
+  int num_pages;            // pool pages (kernel-checks builds validate block-table entries)
+  int* err;
   const int64_t* row_of_token;  // token -> cache row (paged)
   const int64_t* slot;          // token -> cache slot (paged); the rope position differs
                                 // from the slot when the row is left-padded
@@ -430,7 +487,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(RopeArgs a) {
     if (a.block_table != nullptr) {
       const long row = a.row_of_token[t];
       const long p = a.slot[t];
-      const int page = a.block_table[row * a.max_pages + p / a.page_size];
+      const int page = checked_index(a.block_table[row * a.max_pages + p / a.page_size], a.num_pages, a.err);
       const int off = static_cast<int>(p % a.page_size);
       dst = pool + ((static_cast<long>(page) * a.nkv + kvh) * a.page_size + off) * D;
     } else {
@@ -708,9 +765,10 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
     ps.arrivals = reinterpret_cast<int*>(sy.data_ptr<int64_t>()[0]);
     ps.done = reinterpret_cast<int*>(sy.data_ptr<int64_t>()[1]);
     ps.expected = static_cast<int>(peer_expected);
-    ps.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
     TORCH_CHECK(ldd % 4 == 0, "peer sum needs 16-byte aligned rows");
   }
+  // error word for the bounded waits (peer sums, staged LoRA rows)
+  ps.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
   float* zt = nullptr;
   long zld = 0;
   int zn = 0;
@@ -722,10 +780,28 @@ void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta,
     zld = zero_tail->stride(0);
     zn = static_cast<int>(zero_tail->size(1));
   }
-#define GB_LAUNCH_NORM(DF, HD, LR)                                                                       \
-  C10_CUDA_CHECK(launch_kernel(add_rmsnorm_kernel<DF, HD, LR>, dim3(rows), dim3(kNormThreads), 0, stream, hp, \
-                               dptr, hout, wp, yp, rp, ap, up, H, R, ldu, (float)scale, (float)eps, ldd, dlb, \
-                               ldb, dlr, ps, zt, zld, zn))
+  const bool staged = dlb != nullptr || lora;
+  TORCH_CHECK(R <= kMaxLoraRows && (!lora || ldu >= R), "LoRA-down: at most 128 rows, U at least that wide");
+  const int dyn_smem = staged ? 2 * kStageBytes : 0;
+  if (staged) {
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(dlb) % 16 == 0 && reinterpret_cast<uintptr_t>(ap) % 16 == 0,
+                "LoRA weight rows must be 16-byte aligned");
+    TORCH_CHECK(dlb == nullptr || ldb == H, "B^T rows must be contiguous [r, H]");
+    TORCH_CHECK(!lora || (lora_a->stride(0) == H && lora_a->stride(1) == 1), "LoRA A rows must be contiguous [R, H]");
+  }
+#define GB_LAUNCH_NORM(DF, HD, LR)                                                                           \
+  do {                                                                                                       \
+    static bool configured[64] = {};                                                                         \
+    const int dev = h.get_device();                                                                          \
+    if (!configured[dev]) {                                                                                  \
+      C10_CUDA_CHECK(cudaFuncSetAttribute(add_rmsnorm_kernel<DF, HD, LR>,                                    \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * kStageBytes));   \
+      configured[dev] = true;                                                                                \
+    }                                                                                                        \
+    C10_CUDA_CHECK(launch_kernel(add_rmsnorm_kernel<DF, HD, LR>, dim3(rows), dim3(kNormThreads), dyn_smem,  \
+                                 stream, hp, dptr, hout, wp, yp, rp, ap, up, H, R, ldu, (float)scale,        \
+                                 (float)eps, ldd, dlb, ldb, dlr, ps, zt, zld, zn));                          \
+  } while (0)
   if (!has_delta) {
     if (lora) GB_LAUNCH_NORM(false, false, true); else GB_LAUNCH_NORM(false, false, false);
   } else if (delta_f32) {
@@ -760,10 +836,12 @@ void qk_norm_rope(torch::Tensor qkv, torch::Tensor q_w, torch::Tensor k_w, torch
                   torch::Tensor pos, torch::Tensor q_out, torch::Tensor k_out, torch::Tensor v_out,
                   c10::optional<torch::Tensor> block_table, c10::optional<torch::Tensor> row_of_token,
                   c10::optional<torch::Tensor> slot, int64_t nq, int64_t nkv, int64_t page_size, double eps,
-                  c10::optional<torch::Tensor> lora_b, int64_t lora_r) {
+                  c10::optional<torch::Tensor> lora_b, int64_t lora_r, c10::optional<torch::Tensor> err) {
   const c10::cuda::CUDAGuard guard(qkv.device());
   TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1, "qkv must be 2-D row-major");
   RopeArgs a{};
+  a.err = (err.has_value() && err->defined()) ? err->data_ptr<int>() : nullptr;
+  a.num_pages = static_cast<int>(k_out.size(0));
   a.qkv = qkv.data_ptr();
   a.ld_qkv = qkv.stride(0);
   a.qkv_f32 = qkv.scalar_type() == torch::kFloat32 ? 1 : 0;

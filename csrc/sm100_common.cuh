@@ -58,6 +58,7 @@ enum ErrorCode : int {
   kErrTmemEmptyTimeout = 4,
   kErrPeerTimeout = 5,
   kErrBadShape = 6,
+  kErrBadIndex = 7,   // kernel-checks builds: an index outside its table (the access is clamped)
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -66,6 +67,25 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 
 __device__ __forceinline__ void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// Bounds checks compiled in with -DGRASPO_KERNEL_CHECKS (GRASPO_KERNEL_CHECKS=1
+// at build time): an index outside its table records kErrBadIndex in the error
+// word and the access is clamped to a valid entry instead of faulting.
+#if defined(GRASPO_KERNEL_CHECKS)
+constexpr bool kKernelChecks = true;
+#else
+constexpr bool kKernelChecks = false;
+#endif
+
+__device__ __forceinline__ int checked_index(int idx, int limit, int* err) {
+  if constexpr (kKernelChecks) {
+    if (idx < 0 || idx >= limit) {
+      record_error(err, kErrBadIndex);
+      return 0;
+    }
+  }
+  return idx;
 }
 
 // ---------------------------------------------------------------- mbarrier
@@ -129,6 +149,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// 1-D bulk copy global -> shared completing on `bar` (both addresses 16-byte
+// aligned, bytes a multiple of 16).  No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

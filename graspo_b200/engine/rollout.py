@@ -438,6 +438,7 @@ class FusedRolloutEngine:
         complete pre-activation: the RMSNorm kernel that produces the GEMM
         input also computes its U.
         """
+        from graspo_b200.ops._ext import err_word
         from graspo_b200.ops.gemm import gemm
 
         m, C = self.m, self.C
@@ -447,8 +448,10 @@ class FusedRolloutEngine:
         r = m.lora.r
         rows = row_ids.shape[0]
         so, sd = self._sites.get("o"), self._sites.get("d")
-        o_norm = so.norm_kwargs() if so is not None else {}
-        d_norm = sd.norm_kwargs() if sd is not None else {}
+        # the norm kernels' bounded waits (peer sums, staged LoRA rows) report into the error word
+        ew = {"err": err_word(m.device)}
+        o_norm = so.norm_kwargs() if so is not None else ew
+        d_norm = sd.norm_kwargs() if sd is not None else ew
         if m.include_embed:
             C.embedding(st["next_ids"], m.embed, b["x_a"])
         else:
@@ -469,10 +472,10 @@ class FusedRolloutEngine:
                  splits=3)
             C.qk_norm_rope(b["qkv_ws"], lw.q_norm, lw.k_norm, m.inv_freq, st["pos"], b["q"], self.k_pool[li],
                            self.v_pool[li], bt, row_ids, st["slot"], m.nq, m.nkv, self.page, eps,
-                           BT["qkv"], r if has_qkv else 0)
+                           BT["qkv"], r if has_qkv else 0, **ew)
             C.paged_decode_attention(b["q"], self.k_pool[li], self.v_pool[li], bt, st["start"], st["kv_len"],
                                      b["attn"], scale, self._splits, b["attn_scratch"], self._prefix, self._group,
-                                     self._prefix_splits)
+                                     self._prefix_splits, **ew)
             has_o = "a_o" in L
             gemm(lw.w_o_ext if has_o else lw.w_o, b["attn"], b["o_ws"], swap=True, epilogue="atomic", splits=4,
                  push=so)

@@ -209,6 +209,35 @@ def test_add_rmsnorm(delta_dtype):
         _close(hout, ref_in, 1e-2)
 
 
+@pytest.mark.parametrize("r,R", [(16, 32), (64, 128), (5, 7)])
+def test_add_rmsnorm_lora_b_u_and_down(r, R):
+    """fp32 split-K delta with U columns after H: x' = h + delta + B U, then the
+    norm and U' = s y A^T; LoRA rows stream through the shared-memory ring."""
+    from graspo_b200.ops._ext import check_errors, err_word
+
+    rows, H = 37, 4096
+    h, w = _rand(rows, H), _rand(H, scale=0.1) + 1
+    bt = _rand(r, H, scale=0.05)                       # B^T [r, H]
+    u = torch.randn(rows, r, device="cuda")
+    delta = torch.zeros(rows, H + 64, device="cuda")
+    delta[:, :H] = torch.randn(rows, H, device="cuda")
+    delta[:, H:H + r] = u
+    ref_in = (h.float() + delta[:, :H] + u @ bt.float()).bfloat16()
+    A = _rand(R, H, scale=0.02)
+    U = torch.full((rows, 128), 7.0, device="cuda", dtype=torch.bfloat16)
+    zt = torch.ones(rows, 24, device="cuda")
+    y, hout = torch.empty_like(h), torch.empty_like(h)
+    _ext().add_rmsnorm(h, delta, hout, w, y, None, A, U, 2.0, 1e-6, bt, r, err=err_word(h.device), zero_tail=zt)
+    torch.cuda.synchronize()
+    check_errors()
+    _close(hout, ref_in, 1e-2)
+    ref = _rmsnorm_ref(ref_in, w, 1e-6)
+    _close(y, ref, 2e-2)
+    _close(U[:, :R], 2.0 * ref.bfloat16().float() @ A.float().T, 3e-2)
+    assert R == U.shape[1] or U[:, R:].abs().max().item() == 0
+    assert delta.abs().max().item() == 0 and zt.abs().max().item() == 0
+
+
 def test_rmsnorm_bwd():
     x = _rand(19, 1024).requires_grad_(False)
     w = _rand(1024, scale=0.1) + 1
@@ -557,3 +586,23 @@ def test_gated_delta_step_matches_recurrence(dk, dv):
         _ext().gated_delta_step(q, k, v, g, beta, state, out)
     _close(out, ref, 1e-4)
     _close(state, ref_state, 1e-4)
+
+
+def test_kernel_checks_flag_and_decode_attention_with_error_word():
+    """The loaded build reports whether index checks are compiled in; the decode
+    attention accepts the error word either way and leaves it clear on valid input."""
+    from graspo_b200.ops._ext import check_errors, err_word
+
+    assert isinstance(_ext().kernel_checks(), bool)
+    rows, nq, nkv, D, page = 4, 8, 2, 128, 64
+    kp = _rand(8, nkv, page, D)
+    vp = _rand(8, nkv, page, D)
+    bt = torch.arange(8, device="cuda", dtype=torch.int32).view(rows, 2)
+    q = _rand(rows, nq, D)
+    start = torch.zeros(rows, device="cuda", dtype=torch.int32)
+    ln = torch.full((rows,), 100, device="cuda", dtype=torch.int32)
+    out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+    scratch = torch.zeros(rows * nq * 2 * (D + 2) + rows * nkv, device="cuda")
+    _ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), 2, scratch, err=err_word(q.device))
+    torch.cuda.synchronize()
+    check_errors()
