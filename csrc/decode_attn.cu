@@ -53,7 +53,7 @@ struct DecodeAttnArgs {
   // Shared-prefix mode (prefix_len > 0): consecutive groups of group_rows rows
   // share the pages of key positions [start, prefix_len).  Those keys are
   // handled by paged_prefix_attn_kernel for all rows of a group at once
-  // (prefix_splits key slices, 4 partial slots each); the split kernels then
+  // (prefix_splits key slices, one partial slot each); the split kernels then
   // cover [prefix_len, len) and merge prefix_slots + splits partials per row.
   int prefix_len, group_rows, prefix_splits, prefix_kps, prefix_slots;
   int num_pages;  // pages in the pools (kernel-checks builds validate block-table entries)
@@ -467,23 +467,54 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
     }
     __syncthreads();
   }
-  // partial of this warp for its two rows
-  const int slot = split * 4 + kw;
+  // ---- the four key-warps of each row tile merge inside the CTA (their K/V
+  // staging memory holds the exchange), so each split leaves one partial slot
+  __shared__ float xm[2][4][16], xl[2][4][16];
+  float* xo = reinterpret_cast<float*>(tc_smem);          // [2 tiles][4 key-warps][16 rows][kD]
+  __syncthreads();                                        // no warp reads K / V any more
+  for (int mt0 = 0; mt0 < MT; mt0 += 2) {
+    if (mt >= mt0 && mt < mt0 + 2) {
+      const int lt = mt - mt0;
+      float* dst = xo + static_cast<long>((lt * 4 + kw) * 16) * kD;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int qr = h ? qr1 : qr0;
-    if (!(h ? ok1 : ok0)) continue;
-    const long head_idx = static_cast<long>(row0 + qr / G) * a.nq + kvh * G + qr % G;
-    const long pidx = head_idx * total + slot;
+      for (int n = 0; n < 16; ++n) {
+        dst[g * kD + n * 8 + c] = o[n][0];
+        dst[g * kD + n * 8 + c + 1] = o[n][1];
+        dst[(g + 8) * kD + n * 8 + c] = o[n][2];
+        dst[(g + 8) * kD + n * 8 + c + 1] = o[n][3];
+      }
+      if ((lane & 3) == 0) {
+        xm[lt][kw][g] = m0;
+        xl[lt][kw][g] = l0;
+        xm[lt][kw][g + 8] = m1;
+        xl[lt][kw][g + 8] = l1;
+      }
+    }
+    __syncthreads();
+    const int nlt = min(2, MT - mt0);
+    for (int i = threadIdx.x; i < nlt * 16 * kD; i += kThreadsP) {
+      const int lt = i / (16 * kD), rr = (i / kD) % 16, d = i % kD;
+      const int qr = (mt0 + lt) * 16 + rr;
+      if (qr >= R * G) continue;
+      float mm = -INFINITY;
 #pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      a.part_acc[pidx * kD + n * 8 + c] = o[n][2 * h];
-      a.part_acc[pidx * kD + n * 8 + c + 1] = o[n][2 * h + 1];
+      for (int k = 0; k < 4; ++k) mm = fmaxf(mm, xm[lt][k][rr]);
+      float ll = 0.f, oo = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float w = mm == -INFINITY ? 0.f : exp2f(xm[lt][k][rr] - mm);
+        ll += xl[lt][k][rr] * w;
+        oo += xo[static_cast<long>((lt * 4 + k) * 16 + rr) * kD + d] * w;
+      }
+      const long head_idx = static_cast<long>(row0 + qr / G) * a.nq + kvh * G + qr % G;
+      const long pidx = head_idx * total + split;
+      a.part_acc[pidx * kD + d] = oo;
+      if (d == 0) {
+        a.part_ml[pidx * 2] = mm;
+        a.part_ml[pidx * 2 + 1] = ll;
+      }
     }
-    if ((lane & 3) == 0) {
-      a.part_ml[pidx * 2] = h ? m1 : m0;
-      a.part_ml[pidx * 2 + 1] = h ? l1 : l0;
-    }
+    __syncthreads();
   }
 }
 
@@ -780,7 +811,7 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
     a.group_rows = R;
     a.prefix_splits = static_cast<int>(prefix_splits);
     a.prefix_kps = ((P + a.prefix_splits - 1) / a.prefix_splits + kTile - 1) / kTile * kTile;
-    a.prefix_slots = 4 * a.prefix_splits;
+    a.prefix_slots = a.prefix_splits;
   }
   a.keys_per_split = ((capacity - P + a.splits - 1) / a.splits + align - 1) / align * align;
   a.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;

@@ -162,7 +162,9 @@ def bench_step(args) -> None:
     model = _step_model(args)
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, 150000, (args.prompt_len,), generator=g).tolist() for _ in range(args.prompts)]
-    for graph, prefix in ((True, False), (True, True), (False, False)):
+    configs = {"gn": (True, False), "gp": (True, True), "en": (False, False), "ep": (False, True)}
+    for name in args.configs.split(","):
+        graph, prefix = configs[name]
         eng = FusedRolloutEngine(model, FusedQwen3(model), page_size=64, use_graph=graph)
         eng.nvtx = not graph
         eng.prefix_attention = prefix
@@ -359,6 +361,7 @@ def main() -> None:
     parser.add_argument("--group", type=int, default=8)
     parser.add_argument("--prompt-len", type=int, default=1024)
     parser.add_argument("--new", type=int, default=64)
+    parser.add_argument("--configs", default="gn,gp,en", help="decode-step configs: g/e = graph/eager, n/p = no prefix / shared-prefix attention")
     parser.add_argument("--ckpt", default="/tmp/graspo_b200_bench")
     parser.add_argument("--rows", type=int, default=8)
     parser.add_argument("--seq", type=int, default=3072)

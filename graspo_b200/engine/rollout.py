@@ -276,7 +276,7 @@ class FusedRolloutEngine:
         self._group = G
         self._prefix_splits = (max(1, min(P // 64, round(2 * 148 / max(1, n * m.nkv)))) if self._prefix else 1)
         self._splits = decode_attention_splits(rows, m.nkv, cap - self._prefix)
-        slots = self._splits + (4 * self._prefix_splits if self._prefix else 0)
+        slots = self._splits + (self._prefix_splits if self._prefix else 0)
         bufs["attn_scratch"] = torch.zeros(rows * m.nq * slots * (m.D + 2) + rows * m.nkv,
                                            device=dev, dtype=torch.float32)
         row_ids = torch.arange(rows, dtype=torch.long, device=dev)
