@@ -252,7 +252,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_kernel(DecodeAt
 constexpr int kTile = 64;
 constexpr int kRowBytes = kD * 2;                    // 256 B per key row
 constexpr int kTileBytes = kTile * kRowBytes;         // 16 KiB per K or V tile
-constexpr int kTcSmem = 2 * 2 * kTileBytes;           // 2 stages x (K, V) (prefix kernel)
+constexpr int kPrefStages = 4;                          // prefix kernel: 3 tiles in flight
+constexpr int kTcSmem = kPrefStages * 2 * kTileBytes;   // stages x (K, V) (prefix kernel)
 constexpr int kTcStages = 3;                            // split kernel: 3 tiles in flight
 constexpr int kTcSmemSplit = kTcStages * 2 * kTileBytes;
 constexpr int kBtCache = 128;                           // block-table entries kept in shared memory
@@ -370,7 +371,6 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
       cp_async16(kdst + swz(r, ch), ksrc + r * kRowBytes + ch * 16);
       cp_async16(vdst + swz(r, ch), vsrc + r * kRowBytes + ch * 16);
     }
-    cp_async_commit();
   };
 
   float o[16][4];
@@ -379,15 +379,15 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
   const bool any = k_end > k_begin;
   const int t_first = any ? k_begin / kTile : 0, t_last = any ? (k_end - 1) / kTile : -1;
-  if (any) load_tile(t_first, 0);
+  // kPrefStages-deep cp.async ring: one commit group per tile (empty groups past the end)
+#pragma unroll
+  for (int sidx = 0; sidx < kPrefStages - 1; ++sidx) {
+    if (t_first + sidx <= t_last) load_tile(t_first + sidx, sidx);
+    cp_async_commit();
+  }
   for (int tile = t_first; tile <= t_last; ++tile) {
-    const int stage = (tile - t_first) & 1;
-    if (tile < t_last) {
-      load_tile(tile + 1, stage ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    const int stage = (tile - t_first) % kPrefStages;
+    cp_async_wait<kPrefStages - 2>();
     __syncthreads();
     const uint32_t kt = sbase + stage * 2 * kTileBytes;
     const uint32_t vt = kt + kTileBytes;
@@ -465,8 +465,12 @@ __global__ void __launch_bounds__(MT * 4 * 32) paged_prefix_attn_kernel(DecodeAt
       mma_bf16(o[2 * nd], pa0, pa1, pa2, pa3, b0, b1);
       mma_bf16(o[2 * nd + 1], pa0, pa1, pa2, pa3, b2, b3);
     }
-    __syncthreads();
+    __syncthreads();  // the stage read above is refilled below
+    if (tile + kPrefStages - 1 <= t_last)
+      load_tile(tile + kPrefStages - 1, (tile + kPrefStages - 1 - t_first) % kPrefStages);
+    cp_async_commit();
   }
+  cp_async_wait<0>();
   // ---- the four key-warps of each row tile merge inside the CTA (their K/V
   // staging memory holds the exchange), so each split leaves one partial slot
   __shared__ float xm[2][4][16], xl[2][4][16];
@@ -718,6 +722,28 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
     }
     if (total == 1) {
       a.out[(head_base + gg) * kD + d] = __float2bfloat16(ls > 0.f ? ov / ls : 0.f);
+    } else if (a.splits == 1) {
+      // one key split besides the shared-prefix slots, which the prefix kernel
+      // (earlier in stream order) has completed: merge them here directly
+      const long pbase = (head_base + gg) * total;
+      float mm = mxx;
+      for (int sp = 0; sp < a.prefix_slots; ++sp) mm = fmaxf(mm, __ldcg(a.part_ml + (pbase + sp) * 2));
+      float lt = 0.f, ot = 0.f;
+      if (mm > -INFINITY) {
+        if (mxx > -INFINITY) {
+          const float cf = exp2f(mxx - mm);
+          lt = ls * cf;
+          ot = ov * cf;
+        }
+        for (int sp = 0; sp < a.prefix_slots; ++sp) {
+          const float ms = __ldcg(a.part_ml + (pbase + sp) * 2);
+          if (ms == -INFINITY) continue;
+          const float cf = exp2f(ms - mm);
+          lt += __ldcg(a.part_ml + (pbase + sp) * 2 + 1) * cf;
+          ot += __ldcg(a.part_acc + (pbase + sp) * kD + d) * cf;
+        }
+      }
+      a.out[(head_base + gg) * kD + d] = __float2bfloat16(lt > 0.f ? ot / lt : 0.f);
     } else {
       const long pidx = (head_base + gg) * total + a.prefix_slots + split;
       a.part_acc[pidx * kD + d] = ov;
@@ -727,7 +753,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_attn_tc_kernel(Decod
       }
     }
   }
-  if (total == 1) return;
+  if (total == 1 || a.splits == 1) return;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -274,7 +274,7 @@ class FusedRolloutEngine:
         self._prefix = (P if self.prefix_attention and dev.type == "cuda" and self.page % 64 == 0 and G > 1
                         and G * heads_per_kv <= 64 else 0)
         self._group = G
-        self._prefix_splits = (max(1, min(P // 64, round(2 * 148 / max(1, n * m.nkv)))) if self._prefix else 1)
+        self._prefix_splits = (max(1, min(P // 64, round(148 / max(1, n * m.nkv)))) if self._prefix else 1)
         self._splits = decode_attention_splits(rows, m.nkv, cap - self._prefix)
         slots = self._splits + (self._prefix_splits if self._prefix else 0)
         bufs["attn_scratch"] = torch.zeros(rows * m.nq * slots * (m.D + 2) + rows * m.nkv,
