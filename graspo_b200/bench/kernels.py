@@ -76,6 +76,7 @@ def bench_gemm(args) -> None:
         c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
         flops = 2.0 * m * n * k
         ours = timer(lambda: gemm(a, b, c))
+        ours128 = timer(lambda: gemm(a, b, c, bn=128))
         ref = timer(lambda: torch.matmul(a, b.T, out=c))
         check_errors()
         print(json.dumps({
@@ -83,7 +84,7 @@ def bench_gemm(args) -> None:
             "ms": round(ours, 4), "tflops": round(flops / ours / 1e9, 1),
             "frac_of_measured_bf16": round(flops / ours / 1e9 / peaks["bf16_tflops"], 3),
             "cublas_ms": round(ref, 4), "cublas_tflops": round(flops / ref / 1e9, 1),
-            "speedup_vs_cublas": round(ref / ours, 3),
+            "speedup_vs_cublas": round(ref / ours, 3), "ms_bn128": round(ours128, 4),
         }), flush=True)
         del a, b, c
 
