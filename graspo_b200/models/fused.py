@@ -89,14 +89,21 @@ class LayerSaved:
 
 
 class AttnCache:
-    """A layer's q/k/v projection output, attention output and log-sum-exp kept
-    from the training forward, so the backward's recompute skips the q/k/v GEMM
-    and the flash-attention forward (they are the same values)."""
+    """Values of a layer's training forward kept for the backward's recompute.
 
-    __slots__ = ("qkv", "attn", "lse")
+    Level 1: the q/k/v projection output, the attention output and its
+    log-sum-exp (the recompute skips the q/k/v GEMM and the flash-attention
+    forward).  Level 2 adds the residual after attention and the gate/up
+    pre-activations with the SwiGLU output (it also skips the o and gate/up
+    GEMMs).  Cached values are the forward's own tensors, so the gradients do
+    not change."""
 
-    def __init__(self) -> None:
+    __slots__ = ("qkv", "attn", "lse", "x1", "gu", "act", "mlp")
+
+    def __init__(self, mlp: bool = False) -> None:
         self.qkv = self.attn = self.lse = None
+        self.x1 = self.gu = self.act = None
+        self.mlp = mlp
 
 
 def _cache_attention_mode() -> str:
@@ -188,6 +195,7 @@ class FusedQwen3:
             attn, ctx = attn_ops.attention_forward(q, k, v, meta, self.scale, need_ctx=save or keep is not None)
         if keep is not None:
             keep.qkv, keep.attn, keep.lse = qkv, attn, ctx
+        mlp_cached = cache is not None and cache.x1 is not None
         ext_o = None
         if "a_o" in L:
             attn_d = self._dropout(attn, "o", lw.index, seed, train)
@@ -196,7 +204,11 @@ class FusedQwen3:
         x1 = torch.empty_like(x)
         xn2 = torch.empty_like(x)
         rstd2 = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
-        if tp == 1:
+        if mlp_cached:
+            # every TP rank takes this branch (the cache level is agreed across the group)
+            x1 = cache.x1
+            C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
+        elif tp == 1:
             gemm(attn, lw.w_o, x1, ext_ab=ext_o, residual=x)
             C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
         else:
@@ -210,8 +222,15 @@ class FusedQwen3:
             xd2 = self._dropout(xn2, "gu", lw.index, seed, train)
             u_gu = gemm(xd2, L["a_gu"], bn=64)
             ext_gu = (u_gu, L["b_gu"])
-        gu = torch.empty(T, 2 * m.inter_local, device=x.device, dtype=xn2.dtype) if save else None
-        act = gemm(xn2, lw.w_gu, ext_ab=ext_gu, epilogue="swiglu", aux=gu)
+        keep_mlp = keep is not None and keep.mlp
+        if mlp_cached:
+            gu, act = cache.gu, cache.act
+        else:
+            gu = (torch.empty(T, 2 * m.inter_local, device=x.device, dtype=xn2.dtype) if save or keep_mlp
+                  else None)
+            act = gemm(xn2, lw.w_gu, ext_ab=ext_gu, epilogue="swiglu", aux=gu)
+        if keep_mlp:
+            keep.x1, keep.gu, keep.act = x1, gu, act
         ext_d = None
         if "a_down" in L:
             act_d = self._dropout(act, "down", lw.index, seed, train)
@@ -343,40 +362,61 @@ class FusedQwen3:
         self.C.embedding(ids.reshape(-1).contiguous(), self.m.embed, out)
         return out
 
-    def attention_cache_bytes(self, tokens: int) -> int:
-        """Device bytes that caching every local layer's attention values costs
-        for ``tokens`` (this rank's q/k/v width and query heads)."""
+    def attention_cache_bytes(self, tokens: int, level: int = 1) -> int:
+        """Device bytes that caching every local layer's values at ``level``
+        (1: attention, 2: attention and MLP) costs for ``tokens``."""
         m = self.m
         qkv_w = (m.nq + 2 * m.nkv) * m.D
         per_token = 2 * qkv_w + 2 * m.nq * m.D + 4 * m.nq
+        if level >= 2:
+            per_token += 2 * (m.cfg.hidden_size + 3 * m.inter_local)
         return len(m.layers) * tokens * per_token
 
-    def _cache_attention(self, tokens: int, device: torch.device) -> bool:
+    def _cache_level(self, tokens: int, device: torch.device) -> int:
+        """0, 1 or 2 (``GRASPO_CACHE_ATTN``: ``auto`` picks the highest level
+        that leaves room for one layer's backward; ``1`` / ``2`` force a level,
+        ``0`` disables).  TP ranks agree on the lowest level any of them picked,
+        because level 2 skips the row-parallel projections and their collectives."""
         mode = _cache_attention_mode()
         if mode in ("0", "off", "false") or not self.m.layers:
-            return False
-        if mode in ("1", "on", "true"):
-            return True
-        if device.type != "cuda":
-            return False
-        free, _ = torch.cuda.mem_get_info(device)
-        free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
-        m = self.m
-        # head-room for one layer's backward: its saved activations and gradients
-        per_layer_bwd = tokens * 2 * (6 * m.cfg.hidden_size + 4 * (m.nq + 2 * m.nkv) * m.D + 6 * m.inter_local)
-        return free > self.attention_cache_bytes(tokens) + 2 * per_layer_bwd + (4 << 30)
+            level = 0
+        elif mode in ("1", "on", "true"):
+            level = 1
+        elif mode in ("2", "full", "mlp"):
+            level = 2
+        elif device.type != "cuda":
+            level = 0
+        else:
+            free, _ = torch.cuda.mem_get_info(device)
+            free += torch.cuda.memory_reserved(device) - torch.cuda.memory_allocated(device)
+            m = self.m
+            # head-room for one layer's backward: its saved activations and gradients
+            per_layer_bwd = tokens * 2 * (6 * m.cfg.hidden_size + 4 * (m.nq + 2 * m.nkv) * m.D + 6 * m.inter_local)
+            room = free - 2 * per_layer_bwd - (4 << 30)
+            level = 2 if room > self.attention_cache_bytes(tokens, 2) else (
+                1 if room > self.attention_cache_bytes(tokens, 1) else 0)
+        ps = self.m.ps
+        if ps.tp_size > 1 and dist.is_available() and dist.is_initialized():
+            t = torch.tensor([level], device=ps.device, dtype=torch.int32)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=ps.tp_group)
+            level = int(t.item())
+        return level
+
+    def _cache_attention(self, tokens: int, device: torch.device) -> bool:
+        return self._cache_level(tokens, device) > 0
 
     def stage_forward(self, x: torch.Tensor, meta: AttnMeta, *, train=False, seed=0, keep_inputs=False):
         """Run this rank's layers; returns (out, [per-layer (input, AttnCache or None)] if keep_inputs).
 
-        With ``keep_inputs`` the attention values are kept for the backward's
+        With ``keep_inputs`` forward values are kept for the backward's
         recompute when they fit in free device memory (``GRASPO_CACHE_ATTN``:
-        ``auto`` (default), ``1`` always, ``0`` never)."""
+        ``auto`` (default), ``1`` attention values, ``2`` attention and MLP
+        values, ``0`` none; see ``AttnCache``)."""
         inputs = []
         T = x.shape[0] * (self.m.ps.tp_size if self.sp else 1)
-        cache = keep_inputs and self._cache_attention(T, x.device)
+        level = self._cache_level(T, x.device) if keep_inputs else 0
         for lw in self.m.layers:
-            keep = AttnCache() if cache else None
+            keep = AttnCache(mlp=level >= 2) if level else None
             x_in = x
             x, _ = self.layer_forward(lw, x, meta, train=train, seed=seed, keep=keep)
             if keep_inputs:

@@ -132,6 +132,8 @@ def test_attention_cache_gives_the_recompute_values(model, monkeypatch):
     """Keeping q/k/v, attention output and LSE from the forward (instead of
     recomputing them in the backward) changes no gradient."""
     ref, dref, cached_ref = _fused_grads(model, monkeypatch, "0")
-    got, dgot, cached = _fused_grads(model, monkeypatch, "1")
-    assert not any(cached_ref) and all(cached)
-    assert torch.equal(got, ref) and torch.equal(dgot, dref)
+    assert not any(cached_ref)
+    for mode in ("1", "2"):   # attention values; attention and MLP values
+        got, dgot, cached = _fused_grads(model, monkeypatch, mode)
+        assert all(cached), mode
+        assert torch.equal(got, ref) and torch.equal(dgot, dref), mode
