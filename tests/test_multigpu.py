@@ -120,7 +120,9 @@ def _peer_reduce_worker(rank, world):
         gemm(W, x, ws, swap=True, epilogue="atomic", splits=3, push=site)
         h_out = torch.empty_like(h)
         y = torch.empty_like(h)
-        C.add_rmsnorm(h, ws, h_out, w, y, None, None, None, 1.0, 1e-6, lb, 16, **site.norm_kwargs())
+        # the norm kernel takes the LoRA B factor transposed: B^T [r, H]
+        lbt = lb[:, :16].T.contiguous()
+        C.add_rmsnorm(h, ws, h_out, w, y, None, None, None, 1.0, 1e-6, lbt, 16, **site.norm_kwargs())
         torch.cuda.synchronize()
         check_errors()
         part = x.float() @ W.float().T
