@@ -53,3 +53,57 @@ def test_replay_buffer():
     assert [e.sequences for e in limited.items] == [3, 4]
     buf.clear()
     assert len(buf) == 0
+
+
+# (rewards, content scores, retry_count, rollout_max_retries, extra flags) -> decision.
+# Priority order exercised: perfect skip (lower median at the threshold) > max correct >
+# unparseable-best retry/discard > preference gap (max above the lower median) > retry while
+# attempts remain > invalid filters (no variance, uniform partial content) > no preference gap.
+_SCENARIOS = [
+    ([1.0, 1.0, 1.0, 0.5], [1.0, 1.0, 1.0, 0.5], 0, 5, {}, GroupDecision.PERFECT_SKIP),
+    ([1.0, 1.0, 1.0, 1.0], [1.0] * 4, 1, 5, {}, GroupDecision.PERFECT_SKIP),
+    ([0.5, 0.5, 0.5, 1.0], [0.5, 0.5, 0.5, 1.0], 1, 5, {}, GroupDecision.TRAINABLE_MAX_CORRECT),
+    ([0.1, 1.0], [0.1, 1.0], 1, 5, {}, GroupDecision.TRAINABLE_MAX_CORRECT),
+    ([0.2, 0.2], [0.2, 0.2], 0, 1, {}, GroupDecision.RETRY),
+    ([0.2, 0.2], [0.2, 0.2], 1, 1, {}, GroupDecision.INVALID),
+    ([0.1, 0.2], [0.1, 0.2], 0, 5, {}, GroupDecision.TRAINABLE_NOT_CORRECT),
+    ([0.1, 0.2, 0.2, 0.2], [0.0, 0.8, 0.8, 0.8], 5, 5, {}, GroupDecision.INVALID_NO_PREFERENCE_GAP),
+    ([0.1, 0.2, 0.2, 0.3], [0.0, 0.8, 0.8, 0.9], 5, 5, {}, GroupDecision.TRAINABLE_NOT_CORRECT),
+    # a preference gap trains even when every completion has the same partial content score
+    ([0.1, 0.2, 0.2, 0.3], [0.8] * 4, 5, 5, {}, GroupDecision.TRAINABLE_NOT_CORRECT),
+    # no reward variance is invalid, ahead of "no preference gap"
+    ([0.2] * 4, [0.5] * 4, 5, 5, {}, GroupDecision.INVALID),
+    ([0.1, 0.2], [0.1, 0.2], 0, 5, {"best_completion_has_parse_error": True}, GroupDecision.RETRY),
+    ([0.1, 0.2], [0.1, 0.2], 5, 5, {"best_completion_has_parse_error": True}, GroupDecision.INVALID),
+    ([0.1, 0.2], [0.1, 0.2], 5, 5, {"best_completion_has_parse_error": True, "reject_unparseable_groups": False},
+     GroupDecision.TRAINABLE_NOT_CORRECT),
+    # a lower perfect-skip threshold moves the boundary
+    ([0.8, 0.9, 0.9], [0.8, 0.9, 0.9], 0, 5, {"perfect_skip_reward_threshold": 0.85}, GroupDecision.PERFECT_SKIP),
+]
+
+
+@pytest.mark.parametrize("rewards,content,retry,max_retries,flags,expected", _SCENARIOS)
+def test_decision_priority(rewards, content, retry, max_retries, flags, expected):
+    d = classify_group(rewards, content, retry_count=retry, rollout_max_retries=max_retries, **flags)
+    assert d.decision == expected
+    assert d.should_train == (expected in (GroupDecision.TRAINABLE_MAX_CORRECT, GroupDecision.TRAINABLE_NOT_CORRECT))
+    assert d.should_retry == (expected == GroupDecision.RETRY)
+    assert d.reward_max_median_gap == pytest.approx(max(rewards) - lower_median(rewards))
+
+
+def test_invalid_filters():
+    from graspo_b200.core.decisions import is_invalid_group, is_uniform_partial_content
+
+    assert is_invalid_group([0.0, 0.0], [0.0, 0.0])
+    assert is_invalid_group([0.2, 0.8], [0.5, 0.5])           # uniform partial content
+    assert not is_invalid_group([0.1, 0.2, 0.2, 0.2], [0.0, 0.8, 0.8, 0.8])
+    assert is_uniform_partial_content([0.5, 0.5, 0.5])
+    assert not is_uniform_partial_content([0.0, 0.0]) and not is_uniform_partial_content([1.0, 1.0])
+    assert not is_uniform_partial_content([])
+
+
+def test_replay_threshold_is_prompts_times_group():
+    from graspo_b200.core.decisions import replay_buffer_optimize_threshold
+
+    assert replay_buffer_optimize_threshold(4, 8) == 32
+    assert replay_ready(32, 4, 8) and not replay_ready(31, 4, 8)
