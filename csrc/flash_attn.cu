@@ -1,4 +1,6 @@
 // Flash attention for prefill and training (forward + backward), head_dim 128.
+// Reference counterpart: SDPA with a boolean mask (src/graspo/backends/graspoflow/models/
+// common/layers_qwen3.py:252-257); this mma.sync version is the fallback of csrc/flash_attn_tc.cu.
 //
 // Layout: q [T, nq, 128], k / v [T, nkv, 128] bf16 with T = B * S tokens of a
 // padded batch.  Row b's valid tokens are the contiguous range

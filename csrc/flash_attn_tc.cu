@@ -1,4 +1,7 @@
 // Flash attention forward on the 5th-generation tensor cores (tcgen05 + TMEM).
+// Reference counterpart: SDPA with an explicit boolean causal + padding mask and
+// repeat_interleave for GQA (src/graspo/backends/graspoflow/models/common/layers_qwen3.py:252-257,
+// src/graspo/backends/graspoflow/tensor_utils.py:452-468).
 //
 // Same contract as flash_attn_fwd (csrc/flash_attn.cu): q [T, nq, 128], k / v
 // [T, nkv, 128] bf16, T = B * S tokens, row b attends causally inside its

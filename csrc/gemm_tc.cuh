@@ -1,5 +1,8 @@
 #pragma once
 // Persistent, warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+// Reference counterparts: the LoRA linears (src/graspo/backends/graspoflow/lora.py:208-213,
+// models/common/layers_qwen3.py:148-192, 287-316, 333-335), SwiGLU (layers_qwen3.py:334),
+// the LM head and selected-token log-prob (tensor_utils.py:167-186) -- cuBLAS + ATen there.
 //
 //   C[M, N] = A[M, K] * B[N, K]^T  (+ A2[M, K2] * B2[N, K2]^T)   fp32 accumulate
 //

@@ -1,4 +1,10 @@
 // Normalisation, rotary-embedding and small fused elementwise kernels.
+// Reference counterparts (all ATen eager there), under src/graspo/backends/graspoflow/:
+//   RMSNorm            models/common/layers_qwen3.py:338-351
+//   QK-norm            models/common/layers_qwen3.py:193-204, 231-236
+//   RoPE cache + apply tensor_utils.py:361-374, 403-449
+//   SwiGLU             models/common/layers_qwen3.py:334
+//   embedding          models/qwen3/model.py:262-269
 //
 // * add_rmsnorm      h' = h + delta (bf16 or fp32 delta; an fp32 delta is a
 //                    split-K workspace and is zeroed after it is read), then

@@ -1,4 +1,8 @@
 // Sampling, log-prob reductions, the GRPO loss, dropout and the fused AdamW.
+// Reference counterparts, under src/graspo/backends/graspoflow/ unless noted: sampling
+// tensor_utils.py:649-683, selected-token log-prob tensor_utils.py:167-186, GRPO loss
+// src/graspo/core/graspo_loss.py:45-63, clip + AdamW models/qwen35_36/training.py:435-441,
+// recurrent gated delta rule tensor_utils.py:592-646.
 //
 // Random numbers come from Philox4x32-10 (Salmon, Moraes, Dror, Shaw:
 // "Parallel random numbers: as easy as 1, 2, 3", SC'11), implemented here

@@ -1,4 +1,6 @@
 // Symmetric device buffers for in-kernel collectives over NVLink.
+// Reference counterpart: the TP all-reduce after row-parallel projections, an NCCL call
+// (src/graspo/backends/graspoflow/tensor_utils.py:146-164).
 //
 // Every rank of a tensor-parallel group allocates a buffer of the same size
 // with cudaMalloc, exports a CUDA IPC handle, and opens the handles of its

@@ -1,4 +1,7 @@
-"""Parsed view of one generated completion (think text, tool calls, leftovers)."""
+"""Parsed view of one generated completion (think text, tool calls, leftovers).
+
+Same fields and defaults as the reference record (src/graspo/core/completion.py).
+"""
 
 from __future__ import annotations
 

@@ -1,4 +1,5 @@
-"""The ``graspo`` standard-library logging channel.
+"""The ``graspo`` standard-library logging channel (reference: ``logs/training.log``,
+README.md:491-513).
 
 Console output (INFO) on every rank; ``<output_dir>/logs/training.log`` (DEBUG)
 on rank 0.  Calling it again for the same directory is harmless.

@@ -1,5 +1,9 @@
 """Fused sm_100a execution of the Qwen3 decoder (forward, backward, log-probs).
 
+Reference counterpart: the Qwen3 layer stack and its checkpointed recompute
+(src/graspo/backends/graspoflow/models/common/layers_qwen3.py, models/qwen3/model.py:338-347)
+and the vocab-chunked selected-token log-prob (tensor_utils.py:167-186).
+
 Per decoder layer the forward is ~10 kernels:
 
     add_rmsnorm -> [dropout] -> U = x A^T (tcgen05, N=64) -> QKV GEMM with the

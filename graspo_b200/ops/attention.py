@@ -1,5 +1,9 @@
 """Prefill / training attention over padded batches (sm_100a flash attention).
 
+Reference counterpart: SDPA with a boolean causal + padding mask
+(src/graspo/backends/graspoflow/models/common/layers_qwen3.py:252-257,
+src/graspo/backends/graspoflow/tensor_utils.py:452-468).
+
 Layout: q [T, nq, D], k/v [T, nkv, D] with T = B*S tokens; ``meta.key_mask``
 marks valid tokens.  A row's valid tokens form one contiguous range
 [start, end) -- left padding before the prompt, right padding after EOS --

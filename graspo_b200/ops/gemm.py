@@ -1,5 +1,9 @@
 """Python face of the tcgen05 GEMM (csrc/gemm_tc.cu).
 
+Reference counterpart: the LoRA linears ``y = x W^T + s (drop(x) A^T) B^T``
+(src/graspo/backends/graspoflow/lora.py:208-213) and the LM head / log-prob
+chunks (src/graspo/backends/graspoflow/tensor_utils.py:167-186), cuBLAS there.
+
 ``gemm(a, b)`` computes ``a @ b.T`` for row-major bf16 ``a [M, K]`` and
 ``b [N, K]`` with fp32 accumulation, plus optional fused pieces:
 
