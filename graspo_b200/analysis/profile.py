@@ -89,9 +89,8 @@ def rank_summary(run_dir: Path) -> dict[str, Any]:
     latest: dict[int, dict[str, Any]] = {}
     for path in sorted(run_dir.glob("logs/rank_metrics.rank_*.jsonl")) + sorted(run_dir.glob("rank_metrics.rank_*.jsonl")):
         for row in json_lines(path):
-            metrics = row.get("metrics") or row
-            if "rank" in metrics:
-                latest[int(metrics["rank"])] = metrics
+            if "rank" in row:   # the last event of each rank: phase, memory snapshot, metrics
+                latest[int(row["rank"])] = row
     return {"per_rank": {str(r): m for r, m in sorted(latest.items())}}
 
 

@@ -210,6 +210,7 @@ class Qwen3Adapter:
             fn = lr_lambda(sched.type, int(sched.warmup_steps), total, float(sched.min_lr_ratio))
         self.optimizer = FlatAdamW(self.model.lora, lr=tr.learning_rate, weight_decay=tr.weight_decay,
                                    schedule=fn, ps=self.ps)
+        self._rank_event("setup_after")
 
     def _print_rank0(self, payload: dict) -> None:
         if self.rank == 0:
@@ -255,10 +256,14 @@ class Qwen3Adapter:
         return self._generations(res, tokenize_sec, time.monotonic() - t0)
 
     def generate_sample_groups(self, *, samples: list[Any], **kwargs: Any) -> list[NativeGeneration]:
+        self._rank_event("rollout_before", {"samples": len(samples)})
         if any(getattr(s, "media", None) for s in samples):
-            return self._generate_multimodal(samples, **kwargs)
-        return self.generate_groups(message_batches=[s.messages for s in samples],
-                                    tool_batches=[s.tools for s in samples], **kwargs)
+            out = self._generate_multimodal(samples, **kwargs)
+        else:
+            out = self.generate_groups(message_batches=[s.messages for s in samples],
+                                       tool_batches=[s.tools for s in samples], **kwargs)
+        self._rank_event("rollout_after", {"groups": len(out)})
+        return out
 
     # ------------------------------------------------------------ images
     @property
@@ -586,6 +591,7 @@ class Qwen3Adapter:
             "current_lr": self.optimizer.lr,
             "activation_checkpointing_enabled": bool(self.model.gradient_checkpointing),
         }
+        self._rank_event("train_batch_after", {"metrics": metrics})
         return self._aggregate_rank_metrics(metrics)
 
     def train_batch_sft(self, sft_batches: list[dict[str, Any]], *, optimize_iterations_per_step: int,
@@ -647,6 +653,23 @@ class Qwen3Adapter:
         loss.backward()
         lora.accumulate_grads()
         return loss.detach().reshape(1)
+
+    def _rank_event(self, phase: str, extra: dict[str, Any] | None = None) -> None:
+        """Per-rank memory snapshot (and metrics) to logs/rank_metrics.rank_NNNNN.jsonl
+        (reference: transformer_adapter.py:704-721)."""
+        from graspo_b200.train.logger import append_rank_metrics, memory_snapshot
+
+        ps = self.ps
+        payload = {"event": "rank_memory", "phase": phase, "rank": self.rank,
+                   "tp_rank": ps.tp_rank if ps else 0, "pp_rank": ps.pp_rank if ps else 0,
+                   "dp_rank": ps.dp_rank if ps else 0, "device": str(self.device),
+                   "memory": memory_snapshot(self.device)}
+        if extra:
+            payload.update(extra)
+        try:
+            append_rank_metrics(self.config.training.output_dir, self.rank, payload)
+        except OSError:
+            pass  # metrics are best effort; training goes on
 
     def _aggregate_rank_metrics(self, metrics: dict[str, Any]) -> dict[str, Any]:
         local = {"rank": self.rank, "tp_rank": self.tp_rank, **metrics}

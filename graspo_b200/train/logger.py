@@ -132,3 +132,28 @@ def append_event(output_dir: str | Path, payload: dict[str, Any]) -> None:
     path.parent.mkdir(parents=True, exist_ok=True)
     with path.open("a", encoding="utf-8") as handle:
         handle.write(json.dumps(payload, ensure_ascii=False, default=str) + "\n")
+
+
+def memory_snapshot(device: Any) -> dict[str, Any]:
+    """Allocator and device memory of ``device`` in MiB (empty on CPU)."""
+    import torch
+
+    if getattr(device, "type", "cpu") != "cuda" or not torch.cuda.is_available():
+        return {}
+    mib = 1 << 20
+    free, total = torch.cuda.mem_get_info(device)
+    return {
+        "allocated_mib": torch.cuda.memory_allocated(device) / mib,
+        "reserved_mib": torch.cuda.memory_reserved(device) / mib,
+        "max_allocated_mib": torch.cuda.max_memory_allocated(device) / mib,
+        "device_free_mib": free / mib,
+        "device_total_mib": total / mib,
+    }
+
+
+def append_rank_metrics(output_dir: str | Path, rank: int, payload: dict[str, Any]) -> None:
+    """One line of ``<output_dir>/logs/rank_metrics.rank_NNNNN.jsonl`` (every rank writes its own)."""
+    path = Path(output_dir) / "logs" / f"rank_metrics.rank_{int(rank):05d}.jsonl"
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with path.open("a", encoding="utf-8") as handle:
+        handle.write(json.dumps(to_jsonable(payload), ensure_ascii=False) + "\n")

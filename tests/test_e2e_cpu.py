@@ -56,6 +56,13 @@ def test_config0_tp2_gloo_end_to_end(tmp_path):
     assert sorted(p.name for p in final.glob("rank_*.pt")) == ["rank_00000_tp_00_pp_00.pt", "rank_00001_tp_01_pp_00.pt"]
     logs = tmp_path / "run" / "logs"
     assert (logs / "rollouts.readable.jsonl").exists() and (logs / "timing_events.jsonl").exists()
+    # per-rank memory / metrics lines from both ranks, and the primary rank's event log
+    for rank in (0, 1):
+        lines = [json.loads(x) for x in (logs / f"rank_metrics.rank_{rank:05d}.jsonl").read_text().splitlines()]
+        phases = {x["phase"] for x in lines}
+        assert {"setup_after", "rollout_before", "rollout_after", "train_batch_after"} <= phases, phases
+        assert all(x["rank"] == rank for x in lines)
+    assert any(json.loads(x).get("event") == "train_step" for x in (logs / "events.jsonl").read_text().splitlines())
 
     # PEFT export through the CLI
     cfg = yaml.safe_load(config.read_text())
