@@ -263,6 +263,9 @@ def compact_timing_summary(timings: list[dict[str, Any]], *, optimize_sec: float
     out["decode_tokens"] = int(_sum(timings, "decode_tokens"))
     out["rollout_generation_split_count"] = int(_sum(timings, "rollout_generation_split_count"))
     out["total_observed_sec"] = round(total, 6)
+    # throughput: generated tokens per rollout second and per observed step second
+    out["decode_tokens_per_sec"] = round(out["decode_tokens"] / out["rollout_sec"], 3) if out["rollout_sec"] > 0 else None
+    out["step_decode_tokens_per_sec"] = round(out["decode_tokens"] / total, 3) if total > 0 else None
     return out
 
 

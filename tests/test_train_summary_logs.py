@@ -125,6 +125,8 @@ def test_timing_and_optimize_roll_ups():
     t = compact_timing_summary(timings, optimize_sec=4.0, checkpoint_sec=0.5, metrics={"micro_batch_count": 3})
     assert t["rollout_sec"] == 3.0 and t["decode_tokens"] == 150 and t["micro_batch_count"] == 3
     assert t["total_observed_sec"] == pytest.approx(7.75)
+    assert t["decode_tokens_per_sec"] == pytest.approx(50.0)
+    assert t["step_decode_tokens_per_sec"] == pytest.approx(150 / 7.75, rel=1e-3)
     o = compact_optimize_metrics({"optimized": True, "optimizer_steps": 2, "global_loss_mean": 0.3,
                                   "loss_mean": 9.0, "grad_norm_mean": 1.5, "skipped_nonfinite": 1})
     assert o["loss_mean"] == 0.3 and o["grad_norm_mean"] == 1.5 and o["global_optimizer_steps_sum"] == 2
