@@ -20,6 +20,7 @@ gradients of column-parallel projections are all-reduced.
 from __future__ import annotations
 
 import json
+import logging
 import math
 import os
 import random
@@ -43,6 +44,8 @@ from graspo_b200.models.loader import SafetensorIndex
 from graspo_b200.models.qwen3 import EagerLoRA, Qwen3Model, eager_stage_forward, eager_token_logprobs
 from graspo_b200.parallel import state as pstate
 from graspo_b200.parallel.placement import build_placement_plan, placement_summary
+
+log = logging.getLogger("graspo.adapter")
 
 
 def _dtype(name: str) -> torch.dtype:
@@ -210,6 +213,9 @@ class Qwen3Adapter:
             fn = lr_lambda(sched.type, int(sched.warmup_steps), total, float(sched.min_lr_ratio))
         self.optimizer = FlatAdamW(self.model.lora, lr=tr.learning_rate, weight_decay=tr.weight_decay,
                                    schedule=fn, ps=self.ps)
+        if not self.config.graspoflow.use_kv_cache_for_rollout:
+            log.warning("graspoflow.use_kv_cache_for_rollout=false: rollouts always decode from the paged KV "
+                        "cache here (recomputing the whole prefix for every token is not implemented)")
         self._rank_event("setup_after")
 
     def _print_rank0(self, payload: dict) -> None:
@@ -238,9 +244,20 @@ class Qwen3Adapter:
         seed = int(self.config.training.seed) * 1_000_003 + self._train_batch_call_index if seed is None else seed
         # every TP rank must draw the same tokens: derive the seed from the DP replica only
         seed += 7919 * (self.ps.dp_rank if self.ps else 0)
-        return self._engine.generate(prompts, group_size=rollout_group_size, max_new_tokens=max_new_tokens,
-                                     temperature=temperature, top_p=top_p, eos_id=eos, pad_id=pad,
-                                     ignore_eos=bool(flow.benchmark_ignore_eos), seed=seed)
+        # graspoflow.rollout_engine_batch bounds the rows decoded together (0: all at once)
+        limit = int(flow.rollout_engine_batch)
+        per = max(1, limit // max(1, rollout_group_size)) if limit > 0 else max(1, len(prompts))
+        parts = []
+        for ci, start in enumerate(range(0, len(prompts), per)):
+            parts.append(self._engine.generate(
+                prompts[start : start + per], group_size=rollout_group_size, max_new_tokens=max_new_tokens,
+                temperature=temperature, top_p=top_p, eos_id=eos, pad_id=pad,
+                ignore_eos=bool(flow.benchmark_ignore_eos), seed=seed + 104729 * ci))
+            if flow.empty_cache_after_rollout_split and self.device.type == "cuda":
+                torch.cuda.empty_cache()
+        from graspo_b200.engine.rollout import merge_results
+
+        return merge_results(parts, pad)
 
     def generate_groups(self, *, message_batches=None, tool_batches=None, rollout_group_size: int,
                         max_new_tokens: int, max_prompt_length: int | None = None, temperature: float = 1.0,
@@ -371,6 +388,9 @@ class Qwen3Adapter:
                     "adapter": "graspoflow", "rollout_group_size": G, "prefill_len": P,
                     "prompt_lens": [res.prompt_lens[i]], "generated_tokens_max": max_new,
                     "rollout_use_kv_cache": True, "rollout_paged_kv": self.fused,
+                    "rollout_generation_split_count": int(getattr(res, "splits", 1)),
+                    "rollout_generation_micro_batch_size": int(self.config.graspoflow.rollout_engine_batch) or n * G,
+                    "rollout_empty_cache_after_split": bool(self.config.graspoflow.empty_cache_after_rollout_split),
                     "tokenize_sec": round(tokenize_sec / n, 6), "prefill_sec": round(res.prefill_sec / n, 6),
                     "decode_sec": round(res.decode_sec / n, 6), "decode_tokens": decode_tokens // n,
                     "decode_steps": res.decode_steps, "rollout_elapsed_sec": round(elapsed, 6),
@@ -547,6 +567,8 @@ class Qwen3Adapter:
         tok = self.tokenizer
         pad = int(tok.pad_token_id if tok.pad_token_id is not None else tok.eos_token_id)
         bs = int(self.config.training.optimize_prompt_batch_size)
+        if self.config.graspoflow.empty_cache_before_train and self.device.type == "cuda":
+            torch.cuda.empty_cache()
         t0 = time.monotonic()
         lora_before = self.model.lora.parameter_norm()
         losses, norms = [], []

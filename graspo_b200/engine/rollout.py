@@ -53,6 +53,21 @@ class RolloutResult:
     prefill_sec: float = 0.0
     decode_sec: float = 0.0
     decode_steps: int = 0
+    splits: int = 1               # engine calls the rows were decoded in
+
+
+def merge_results(parts: list[RolloutResult], pad_id: int) -> RolloutResult:
+    """Concatenate the results of successive engine calls (prompt ids re-padded on the left)."""
+    if len(parts) == 1:
+        return parts[0]
+    P = max(int(p.prompt_ids.shape[1]) for p in parts)
+    ids = [torch.nn.functional.pad(p.prompt_ids, (P - p.prompt_ids.shape[1], 0), value=pad_id) for p in parts]
+    return RolloutResult(
+        prompt_ids=torch.cat(ids, 0), prompt_lens=[n for p in parts for n in p.prompt_lens],
+        tokens=torch.cat([p.tokens for p in parts], 0), gen_lens=[n for p in parts for n in p.gen_lens],
+        group_size=parts[0].group_size, prefill_sec=sum(p.prefill_sec for p in parts),
+        decode_sec=sum(p.decode_sec for p in parts), decode_steps=max(p.decode_steps for p in parts),
+        splits=len(parts))
 
 
 def _sync(dev: torch.device) -> None:

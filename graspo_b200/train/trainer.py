@@ -174,6 +174,14 @@ class GraspoTrainer:
     def ps(self):
         return getattr(self.runtime, "ps", None)
 
+    def _now(self) -> float:
+        """Phase clock; with ``graspoflow.synchronize_cuda_timing`` the device is
+        synchronised first so each phase owns its GPU work (reference:
+        transformer_adapter.py:685-691)."""
+        if self.config.graspoflow.synchronize_cuda_timing and torch.cuda.is_available():
+            torch.cuda.synchronize()
+        return time.monotonic()
+
     def _is_primary(self) -> bool:
         fn = getattr(self.runtime, "is_primary", None)
         return bool(fn()) if callable(fn) else True
@@ -301,7 +309,7 @@ class GraspoTrainer:
     def _rollout_attempt(self, active: list[_Queued], *, epoch: int) -> list[dict[str, Any]]:
         tr = self.config.training
         self.faults.hit("rollout")
-        t0 = time.monotonic()
+        t0 = self._now()
         gens = self.runtime.generate_sample_groups(
             samples=[s.sample for s in active], rollout_group_size=tr.rollout_group_size,
             max_new_tokens=tr.max_new_tokens, max_prompt_length=self.config.data.max_prompt_length,
@@ -309,16 +317,16 @@ class GraspoTrainer:
         )
         if len(gens) != len(active):
             raise RuntimeError(f"generate_sample_groups returned {len(gens)} groups for {len(active)} samples")
-        per_prompt = (time.monotonic() - t0) / max(1, len(gens))
+        per_prompt = (self._now() - t0) / max(1, len(gens))
         records = []
         self.faults.hit("reward")
         for st, gen in zip(active, gens, strict=True):
-            t1 = time.monotonic()
+            t1 = self._now()
             parse = getattr(self.runtime, "parse_completion", None)
             parsed = [parse(t, st.sample) if callable(parse) else raw_parsed_completion(t) for t in gen.completions]
             results = [self.reward.score_parsed(p, st.sample.targets, is_tool_call=st.sample.expects_tool_calls)
                        for p in parsed]
-            reward_sec = time.monotonic() - t1
+            reward_sec = self._now() - t1
             rewards = [float(r.reward) for r in results]
             content = [float(r.content_score) for r in results]
             best = max(range(len(rewards)), key=lambda i: rewards[i])
@@ -384,10 +392,10 @@ class GraspoTrainer:
                                          "prompt_preview": readable.get("prompt_preview"),
                                          "group_stats": readable.get("group_stats")})
         else:
-            t0 = time.monotonic()
+            t0 = self._now()
             old = self.runtime.sequence_log_probs(gen.sequences, gen.attention_mask, metadata=gen.metadata)
             old = old.detach().float().cpu()
-            timing["old_logprob_sec"] = time.monotonic() - t0
+            timing["old_logprob_sec"] = self._now() - t0
             adv = group_advantages(rewards, eps=self.config.graspoflow.advantage_eps)
             items = []
             for j in range(len(rewards)):
@@ -457,11 +465,11 @@ class GraspoTrainer:
             return False
         self.faults.hit("optimize")
         data = self.replay_buffer.take(usable)
-        t0 = time.monotonic()
+        t0 = self._now()
         metrics = self.runtime.train_batch(data, policy_ratio_clip_eps=tr.policy_ratio_clip_eps,
                                            optimize_iterations_per_step=tr.optimize_iterations_per_step,
                                            max_grad_norm=tr.max_grad_norm)
-        optimize_sec = time.monotonic() - t0
+        optimize_sec = self._now() - t0
         batch = reward_batch_summary(self.pending_attempts, rollout_group_size=tr.rollout_group_size,
                                      optimize_prompt_batch_size=tr.optimize_prompt_batch_size)
         metrics.update({
@@ -479,9 +487,9 @@ class GraspoTrainer:
         ckpt_sec, ckpt_dir = 0.0, None
         if tr.save_steps > 0 and self.global_step % tr.save_steps == 0:
             ckpt_dir = Path(tr.output_dir) / f"step_{self.global_step}"
-            t1 = time.monotonic()
+            t1 = self._now()
             self._save_checkpoint(ckpt_dir, epoch=epoch)
-            ckpt_sec = time.monotonic() - t1
+            ckpt_sec = self._now() - t1
         window = reward_window_summary(self.recent_groups)
         health = training_health(metrics, batch, window)
         optimize = compact_optimize_metrics(metrics)

@@ -23,6 +23,8 @@ def _config(tmp: Path, **training) -> Path:
     cfg["training"]["output_dir"] = str(tmp / "run")
     cfg["training"].update(training)
     cfg["launch"]["master_port"] = 29000 + os.getpid() % 2000
+    # decode the 2 prompts of a step in two engine calls (one group of 4 rows each)
+    cfg["graspoflow"].update(rollout_engine_batch=4, synchronize_cuda_timing=True)
     path = tmp / "config.yaml"
     path.write_text(yaml.safe_dump(cfg))
     return path
@@ -63,6 +65,9 @@ def test_config0_tp2_gloo_end_to_end(tmp_path):
         assert {"setup_after", "rollout_before", "rollout_after", "train_batch_after"} <= phases, phases
         assert all(x["rank"] == rank for x in lines)
     assert any(json.loads(x).get("event") == "train_step" for x in (logs / "events.jsonl").read_text().splitlines())
+    groups = [json.loads(x) for x in (logs / "rollouts.readable.jsonl").read_text().splitlines()]
+    assert groups and all(g["completions"] for g in groups)
+    assert steps[0]["timing"]["rollout_generation_split_count"] >= 2
 
     # PEFT export through the CLI
     cfg = yaml.safe_load(config.read_text())

@@ -137,3 +137,22 @@ def test_attention_cache_gives_the_recompute_values(model, monkeypatch):
         got, dgot, cached = _fused_grads(model, monkeypatch, mode)
         assert all(cached), mode
         assert torch.equal(got, ref) and torch.equal(dgot, dref), mode
+
+
+def test_split_rollout_merges_to_the_unsplit_result(model):
+    """Decoding the prompts in several engine calls (graspoflow.rollout_engine_batch)
+    and merging gives the rows, prompt padding and lengths of one call (greedy)."""
+    from graspo_b200.engine.rollout import EagerRolloutEngine, merge_results
+
+    prompts = [[5, 6, 7, 8, 9], list(range(20, 50)), [300]]
+    kw = dict(group_size=2, max_new_tokens=5, temperature=0.0, top_p=1.0, eos_id=4095, pad_id=4095,
+              ignore_eos=True, seed=0)
+    eng = EagerRolloutEngine(model)
+    whole = eng.generate(prompts, **kw)
+    parts = [eng.generate(prompts[:1], **kw), eng.generate(prompts[1:], **kw)]
+    merged = merge_results(parts, pad_id=4095)
+    assert merged.splits == 2 and merged.group_size == 2
+    assert torch.equal(merged.tokens, whole.tokens)
+    assert merged.prompt_lens == whole.prompt_lens and merged.gen_lens == whole.gen_lens
+    assert torch.equal(merged.prompt_ids, whole.prompt_ids)
+    assert merge_results(parts[:1], pad_id=4095) is parts[0]
