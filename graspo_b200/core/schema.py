@@ -42,7 +42,14 @@ class LoRAConfig(BaseModel):
 
 
 class ModelConfig(BaseModel):
-    """Where the frozen base model lives and how it is materialised."""
+    """Where the frozen base model lives and how it is materialised.
+
+    ``trust_remote_code`` and ``attn_implementation`` configure Hugging Face
+    model classes in the reference; here the weights are read from the
+    safetensors files by this framework's own loader and attention always
+    runs on its own kernels, so both keys are accepted (reference YAMLs load
+    unchanged) and have no effect.
+    """
 
     model_config = _STRICT
 
