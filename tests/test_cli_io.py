@@ -176,3 +176,17 @@ def test_every_shipped_config_loads_and_plans(tmp_path, monkeypatch):
         if flow.dp_size:
             assert plan.nproc_per_node == cell * flow.dp_size, f.name
         assert plan.uses_torchrun == (plan.nproc_per_node > 1), f.name
+
+
+@pytest.mark.parametrize("command", ["train", "prepare-data", "analyze"])
+def test_removed_commands_are_not_public(command):
+    """Only launch / export / validate-reward are public (validate-reward is kept:
+    the reference README documents it and the baseline asks for it)."""
+    with pytest.raises(SystemExit):
+        build_parser().parse_args([command])
+
+
+def test_world_size_one_runs_in_process(tmp_path):
+    plan = build_launch_plan(_write_cfg(tmp_path, tp_size=1))
+    assert not plan.uses_torchrun and plan.nproc_per_node == 1
+    assert "torchrun" not in " ".join(plan.command)
