@@ -136,6 +136,9 @@ class GraspoFlowConfig(BaseModel):
       all-reduces run inside the o_proj / down_proj GEMMs (tile push into the
       peers' memory over NVLink) and the following RMSNorm kernel; ``"nccl"``:
       an NCCL all-reduce after each of those GEMMs.
+    * ``async_checkpoint`` – intermediate checkpoints (``step_N``, ``epoch_N``)
+      are snapshotted to host memory and written by a background thread while
+      training continues; the final checkpoint is always written in place.
     """
 
     model_config = _STRICT
@@ -166,6 +169,7 @@ class GraspoFlowConfig(BaseModel):
     cuda_graph_decode: bool = True
     pg_timeout_sec: float = 600.0
     decode_tp_allreduce: Literal["fused", "nccl"] = "fused"
+    async_checkpoint: bool = False
 
     @field_validator("adapter")
     @classmethod

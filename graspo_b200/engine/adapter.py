@@ -712,16 +712,36 @@ class Qwen3Adapter:
 
     # ------------------------------------------------------------ checkpoints
     def save_checkpoint(self, path: str | Path, *, trainer_state: dict[str, Any] | None = None) -> None:
-        from graspo_b200.train.checkpoint import save_rank_checkpoint
+        from graspo_b200.train.checkpoint import AsyncCheckpointWriter, save_rank_checkpoint
 
-        save_rank_checkpoint(self, Path(path), trainer_state=trainer_state)
+        path = Path(path)
+        writer = self.__dict__.setdefault("_ckpt_writer", AsyncCheckpointWriter())
+        if self.config.graspoflow.async_checkpoint and path.name != "final":
+            writer.submit(self, path, trainer_state=trainer_state)
+            return
+        writer.wait(self)
+        save_rank_checkpoint(self, path, trainer_state=trainer_state)
+
+    def flush_checkpoints(self) -> None:
+        """Finish a background checkpoint write, if one is in flight (all ranks call it)."""
+        writer = self.__dict__.get("_ckpt_writer")
+        if writer is not None:
+            writer.wait(self)
+
+    def abandon_checkpoints(self) -> None:
+        """Stop waiting for an in-flight background checkpoint without completing it."""
+        writer = self.__dict__.get("_ckpt_writer")
+        if writer is not None:
+            writer.abandon()
 
     def load_checkpoint(self, path: str | Path) -> dict[str, Any] | None:
         from graspo_b200.train.checkpoint import load_rank_checkpoint
 
+        self.flush_checkpoints()
         return load_rank_checkpoint(self, Path(path))
 
     def close(self) -> None:
+        self.flush_checkpoints()
         self._engine = None
         pstate.destroy()
 

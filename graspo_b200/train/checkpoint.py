@@ -44,13 +44,25 @@ def _atomic_write_text(path: Path, text: str) -> None:
     os.replace(tmp, path)
 
 
-def save_rank_checkpoint(adapter, path: Path, *, trainer_state: dict | None = None) -> None:
+def _to_cpu(obj: Any) -> Any:
+    """Deep copy with every tensor cloned to host memory (a snapshot that later
+    training steps cannot change)."""
+    if isinstance(obj, torch.Tensor):
+        return obj.detach().to("cpu", copy=True)
+    if isinstance(obj, dict):
+        return {k: _to_cpu(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(_to_cpu(v) for v in obj)
+    return obj
+
+
+def build_rank_payload(adapter, trainer_state: dict | None) -> dict | None:
+    """This rank's shard payload (None on data-parallel replicas other than 0)."""
     ps = adapter.ps
     model = adapter.model
-    path.mkdir(parents=True, exist_ok=True)
     cell_rank = ps.rank_of(tp=ps.tp_rank, pp=ps.pp_rank, dp=0)
     if ps.dp_rank == 0:
-        payload = {
+        return {
             "adapter": "graspoflow",
             "rank": cell_rank,
             "tp_rank": ps.tp_rank,
@@ -70,7 +82,28 @@ def save_rank_checkpoint(adapter, path: Path, *, trainer_state: dict | None = No
             "trainer_state": trainer_state,
             "config": adapter.config.model_dump(),
         }
-        _atomic_save(payload, path / rank_file_name(cell_rank, ps.tp_rank, ps.pp_rank))
+    return None
+
+
+def shard_path(adapter, path: Path) -> Path:
+    ps = adapter.ps
+    cell_rank = ps.rank_of(tp=ps.tp_rank, pp=ps.pp_rank, dp=0)
+    return path / rank_file_name(cell_rank, ps.tp_rank, ps.pp_rank)
+
+
+def save_rank_checkpoint(adapter, path: Path, *, trainer_state: dict | None = None) -> None:
+    path.mkdir(parents=True, exist_ok=True)
+    payload = build_rank_payload(adapter, trainer_state)
+    if payload is not None:
+        _atomic_save(payload, shard_path(adapter, path))
+    finish_checkpoint(adapter, path, has_trainer_state=trainer_state is not None)
+
+
+def finish_checkpoint(adapter, path: Path, *, has_trainer_state: bool) -> None:
+    """Barrier over every rank, then rank 0 writes the manifest (the checkpoint
+    counts as complete only once the manifest exists)."""
+    ps = adapter.ps
+    model = adapter.model
     if ps.distributed:
         dist.barrier()
     if ps.rank == 0:
@@ -83,9 +116,68 @@ def save_rank_checkpoint(adapter, path: Path, *, trainer_state: dict | None = No
             "lora_target_signature": model.lora_target_signature(),
             "world_size": ps.tp_size * ps.pp_size,
             "checkpoint_type": "recoverable_lora_training_state",
-            "has_trainer_state": trainer_state is not None,
+            "has_trainer_state": bool(has_trainer_state),
         }
         _atomic_write_text(path / "manifest.json", json.dumps(manifest, ensure_ascii=False, indent=2))
+
+
+class AsyncCheckpointWriter:
+    """Background shard writer (``graspoflow.async_checkpoint``).
+
+    ``submit`` snapshots the shard payload into host memory on the calling
+    thread (so later optimizer steps cannot leak into it) and serialises it on
+    a worker thread while training continues.  ``wait`` joins the worker, then
+    runs the cross-rank barrier and the manifest write of ``finish_checkpoint``;
+    every rank calls it at the same program points (the next save, the final
+    save, shutdown), so at most one checkpoint is in flight and a checkpoint
+    without its manifest is never taken for a finished one."""
+
+    def __init__(self) -> None:
+        self._thread = None
+        self._error: BaseException | None = None
+        self._pending: tuple[Path, bool] | None = None
+
+    def submit(self, adapter, path: Path, *, trainer_state: dict | None = None) -> None:
+        import threading
+
+        self.wait(adapter)
+        path.mkdir(parents=True, exist_ok=True)
+        payload = build_rank_payload(adapter, trainer_state)
+        payload = _to_cpu(payload) if payload is not None else None
+        target = shard_path(adapter, path)
+
+        def work() -> None:
+            try:
+                if payload is not None:
+                    _atomic_save(payload, target)
+            except BaseException as exc:  # noqa: BLE001 - re-raised by wait()
+                self._error = exc
+
+        self._thread = threading.Thread(target=work, name="graspo-checkpoint", daemon=True)
+        self._thread.start()
+        self._pending = (path, trainer_state is not None)
+
+    @property
+    def pending(self) -> bool:
+        return self._pending is not None
+
+    def abandon(self) -> None:
+        """Join the worker without the barrier and manifest (error paths: the other
+        ranks may never reach the barrier); the directory stays without a manifest."""
+        if self._thread is not None:
+            self._thread.join()
+        self._thread, self._pending, self._error = None, None, None
+
+    def wait(self, adapter) -> None:
+        if self._pending is None:
+            return
+        self._thread.join()
+        path, has_state = self._pending
+        self._pending, self._thread = None, None
+        if self._error is not None:
+            err, self._error = self._error, None
+            raise RuntimeError(f"background checkpoint write to {path} failed") from err
+        finish_checkpoint(adapter, path, has_trainer_state=has_state)
 
 
 def load_rank_checkpoint(adapter, path: Path) -> dict | None:

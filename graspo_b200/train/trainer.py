@@ -24,6 +24,7 @@ import json
 import logging
 import os
 import random
+import sys
 import time
 from collections import deque
 from dataclasses import asdict, dataclass, field
@@ -271,6 +272,14 @@ class GraspoTrainer:
             self._maybe_optimize(epoch=tr.max_epochs - 1, force=True)
             self._save_checkpoint(out / "final", epoch=tr.max_epochs - 1)
         finally:
+            if sys.exc_info()[0] is not None:
+                # failing: do not wait at a checkpoint barrier the other ranks may never reach
+                abandon = getattr(self.runtime, "abandon_checkpoints", None)
+                if callable(abandon):
+                    try:
+                        abandon()
+                    except RuntimeError:
+                        pass
             self.runtime.close()
 
     # ------------------------------------------------------------ rollout

@@ -26,7 +26,7 @@ import yaml
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def _config(tmp: Path, name: str, **training) -> Path:
+def _config(tmp: Path, name: str, flow: dict | None = None, **training) -> Path:
     from graspo_b200.utils.make_smoke_assets import make
 
     assets = make(tmp / "assets")
@@ -36,6 +36,7 @@ def _config(tmp: Path, name: str, **training) -> Path:
     cfg["training"]["output_dir"] = str(tmp / name)
     cfg["training"].update(training)
     cfg["graspoflow"]["pg_timeout_sec"] = 60.0
+    cfg["graspoflow"].update(flow or {})
     cfg["launch"]["master_port"] = 29000 + (os.getpid() * 7 + len(name)) % 2000
     path = tmp / f"{name}.yaml"
     path.write_text(yaml.safe_dump(cfg))
@@ -89,3 +90,23 @@ def test_resume_reproduces_the_uninterrupted_run(tmp_path):
             va, vb = sa[key], sb[key]
             if isinstance(va, torch.Tensor):
                 assert torch.equal(va, vb), key
+
+
+@pytest.mark.slow
+def test_background_checkpoint_is_a_snapshot(tmp_path):
+    """With graspoflow.async_checkpoint the step-1 shards are written by a
+    background thread while step 2 trains; they must still hold the step-1
+    state: resuming from them reproduces the uninterrupted run."""
+    full = _config(tmp_path, "full", {"async_checkpoint": True}, max_steps=2, save_steps=1)
+    proc = _launch(full)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    step1 = tmp_path / "full" / "step_1"
+    assert (step1 / "manifest.json").exists()
+    resumed = _config(tmp_path, "resumed", max_steps=2, resume_from_checkpoint=str(step1))
+    proc = _launch(resumed)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    for rank in (0, 1):
+        a = _rank_state(tmp_path / "full" / "final", rank)
+        b = _rank_state(tmp_path / "resumed" / "final", rank)
+        for key, ta in a["lora_state_dict"].items():
+            assert torch.equal(ta, b["lora_state_dict"][key]), key
