@@ -753,7 +753,9 @@ class Qwen35Adapter(Qwen3Adapter):
     Training and log-probs run the model's autograd path (chunked delta rule,
     gradient checkpointing per layer), rollout runs ``HybridRolloutEngine``
     (per-row KV / conv / recurrent caches, the delta-rule decode step on the
-    sm_100a kernel).  Text prompts only; TP = 1 per replica.
+    sm_100a kernel).  Heads are split over the tensor-parallel group (the
+    model sums the row-parallel outputs, the adapter sums the replicated LoRA
+    factors' gradients); text prompts only.
     """
 
     families = ("qwen3_5_text",)

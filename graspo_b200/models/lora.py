@@ -10,8 +10,10 @@ adapted module owns two views into it:
 
 so the adapter starts as an exact no-op (reference: lora.py:76-213).  Shard
 kinds follow the reference checkpoint format: ``out`` (column parallel: rows of
-W and B are split, A is replicated), ``in`` (row parallel: columns of W and A
-are split, B is replicated), ``none``.  The initial A of a module is drawn for
+W and B are split, A is replicated), ``rows`` (a head-row selection or a row
+block of a fused HF matrix, ``row_start:row_stop`` in that matrix's rows; A is
+replicated), ``in`` (row parallel: columns of W and A are split, B is
+replicated), ``none``.  The initial A of a module is drawn for
 the *full* matrix from a generator seeded by (seed, module name) and then
 sliced, so a TP=2 run starts from exactly the TP=1 adapter.
 
@@ -52,6 +54,9 @@ class LoRAModule:
     b_grad: torch.Tensor | None = None
     offset_a: int = 0
     offset_b: int = 0
+    # False for a target that is a row block of a larger HF module (DeltaNet
+    # q/k/v inside in_proj_qkv): PEFT export combines the blocks into one pair
+    peft_exportable: bool = True
 
     @property
     def replicated_factor(self) -> str:
@@ -160,7 +165,7 @@ class LoRAAdapter:
                 "col_start": m.col_start,
                 "col_stop": m.col_stop,
                 "row_indices": None,
-                "peft_exportable": True,
+                "peft_exportable": m.peft_exportable,
                 "r": self.r,
                 "alpha": int(self.alpha) if float(self.alpha).is_integer() else self.alpha,
             }

@@ -13,6 +13,13 @@ adapters move between frameworks and into PEFT / vLLM):
   the replicated A must agree across ranks and B rows are placed by
   ``row_start:row_stop``; for row-parallel (``in``) the replicated B must agree
   and A columns are placed by ``col_start:col_stop``.
+* Row blocks of one HF module (the DeltaNet ``q/k/v_proj`` targets inside
+  ``in_proj_qkv``, records with ``peft_exportable: false``) become ONE PEFT
+  pair: the targets' A factors stacked along the rank axis, their B factors
+  placed on their rows with the LoRA scale folded in, ``r = lora_alpha`` =
+  the summed rank (PEFT scale 1).  ``graspo_adapter_metadata.json`` records
+  each target's rank slice and B scale so the import can split the pair again
+  (reference: lora_io.py:313-350, 432-499).
 * Merged Hugging Face export: every base safetensors file is streamed,
   ``W += (alpha / r) * B @ A`` is added on the rows/columns the shard covered,
   and non-weight sidecar files are copied.
@@ -30,6 +37,7 @@ from safetensors import safe_open
 from safetensors.torch import load_file, save_file
 
 PEFT_PREFIX = "base_model.model."
+METADATA_FILE = "graspo_adapter_metadata.json"
 
 
 def _payloads(checkpoint_dir: str | Path) -> list[dict[str, Any]]:
@@ -91,6 +99,39 @@ def reconstruct_pair(module: str, items) -> tuple[torch.Tensor, torch.Tensor]:
     return a, b
 
 
+def combine_row_blocks(module: str, items) -> tuple[torch.Tensor, torch.Tensor, list[dict[str, Any]]]:
+    """One PEFT pair for several row-block targets of one HF module (and the
+    rank slices that undo it)."""
+    by_target: dict[str, list] = {}
+    for rec, pair in items:
+        by_target.setdefault(str(rec["target_name"]), []).append((rec, pair))
+    rows = max(int(rec["row_stop"]) for rec, _ in items)
+    parts = []
+    for target, group in sorted(by_target.items()):
+        kinds = {rec["shard_kind"] for rec, _ in group}
+        if not kinds <= {"rows", "out"}:
+            raise ValueError(f"row-block target {target} of {module} has shard kinds {sorted(kinds)}")
+        a = _same(module, [p["A"] for _, p in group], f"{target} lora_A")
+        b = torch.zeros(rows, a.shape[0], dtype=group[0][1]["B"].dtype)
+        for rec, p in group:
+            b[rec["row_start"] : rec["row_stop"]] = p["B"]
+        rec = group[0][0]
+        scale = float(rec["alpha"]) / float(rec["r"])
+        parts.append((rec, a, b * scale, scale))
+    total = sum(a.shape[0] for _, a, _, _ in parts)
+    comb_a = torch.zeros(total, parts[0][1].shape[1], dtype=parts[0][1].dtype)
+    comb_b = torch.zeros(rows, total, dtype=parts[0][2].dtype)
+    slices, start = [], 0
+    for rec, a, b, scale in parts:
+        stop = start + a.shape[0]
+        comb_a[start:stop], comb_b[:, start:stop] = a, b
+        slices.append({"target_name": str(rec["target_name"]), "base_weight_name": str(rec["base_weight_name"]),
+                       "rank_start": start, "rank_stop": stop, "native_r": int(rec["r"]),
+                       "native_alpha": rec["alpha"], "adapter_b_scale": scale})
+        start = stop
+    return comb_a, comb_b, slices
+
+
 def export_peft_adapter(checkpoint_dir, output_dir, *, base_model_path=None) -> Path:
     payloads = _payloads(checkpoint_dir)
     cfg = payloads[0].get("config") or {}
@@ -98,7 +139,14 @@ def export_peft_adapter(checkpoint_dir, output_dir, *, base_model_path=None) -> 
     base = str(base_model_path or (cfg.get("model") or {}).get("model_path") or "")
     tensors: dict[str, torch.Tensor] = {}
     specs: dict[str, tuple[int, int]] = {}
+    combined: dict[str, list[dict[str, Any]]] = {}
     for module, items in sorted(_grouped(payloads).items()):
+        if any(not rec.get("peft_exportable", True) for rec, _ in items):
+            a, b, combined[module] = combine_row_blocks(module, items)
+            tensors[f"{PEFT_PREFIX}{module}.lora_A.weight"] = a.contiguous()
+            tensors[f"{PEFT_PREFIX}{module}.lora_B.weight"] = b.contiguous()
+            specs[module] = (int(a.shape[0]), int(a.shape[0]))
+            continue
         a, b = reconstruct_pair(module, items)
         tensors[f"{PEFT_PREFIX}{module}.lora_A.weight"] = a.contiguous()
         tensors[f"{PEFT_PREFIX}{module}.lora_B.weight"] = b.contiguous()
@@ -127,6 +175,9 @@ def export_peft_adapter(checkpoint_dir, output_dir, *, base_model_path=None) -> 
     out = _fresh_dir(output_dir)
     save_file(tensors, str(out / "adapter_model.safetensors"))
     (out / "adapter_config.json").write_text(json.dumps(config, indent=2) + "\n", encoding="utf-8")
+    if combined:
+        meta = {"format": "graspo-peft-adapter-metadata", "version": 1, "modules": combined}
+        (out / METADATA_FILE).write_text(json.dumps(meta, indent=2) + "\n", encoding="utf-8")
     return out
 
 
@@ -239,11 +290,30 @@ def load_peft_adapter(model, adapter_path, *, base_model_path: str | None = None
     if incomplete:
         raise ValueError("PEFT adapter has incomplete LoRA A/B pairs: " + ", ".join(incomplete))
     adapter = model.lora
+    meta_file = path / METADATA_FILE
+    combined = json.loads(meta_file.read_text(encoding="utf-8")).get("modules", {}) if meta_file.exists() else {}
     consumed = set()
     for mod in adapter.modules:
         pair = grouped.get(mod.hf_module_path)
         if pair is None:
             raise ValueError(f"PEFT adapter is missing LoRA tensors for {mod.hf_module_path}")
+        if not mod.peft_exportable:
+            base_name = f"{mod.hf_module_path}.weight"
+            hits = [s for s in combined.get(mod.hf_module_path, [])
+                    if s.get("target_name") == mod.target_name and s.get("base_weight_name") == base_name]
+            if len(hits) != 1:
+                raise ValueError(f"PEFT adapter has no unique {METADATA_FILE} slice for {mod.target_name} "
+                                 f"in {mod.hf_module_path}")
+            rs, re_ = int(hits[0]["rank_start"]), int(hits[0]["rank_stop"])
+            scale = float(hits[0].get("adapter_b_scale") or 1.0)
+            a = pair["A"][rs:re_]
+            b = pair["B"][mod.row_start : mod.row_stop, rs:re_] / scale
+            if tuple(a.shape) != tuple(mod.a.shape) or tuple(b.shape) != tuple(mod.b.shape):
+                raise ValueError(f"shape mismatch for {mod.target_name} in {mod.hf_module_path}")
+            mod.a.copy_(a.float())
+            mod.b.copy_(b.float())
+            consumed.add(mod.hf_module_path)
+            continue
         r = _module_int(config, mod.hf_module_path, "rank_pattern", "r")
         if r is not None and r != adapter.r:
             raise ValueError(f"PEFT adapter r={r} does not match native LoRA r={adapter.r}")
@@ -253,7 +323,7 @@ def load_peft_adapter(model, adapter_path, *, base_model_path: str | None = None
         a, b = pair["A"], pair["B"]
         if mod.shard_kind == "in":
             a = a[:, mod.col_start : mod.col_stop]
-        elif mod.shard_kind == "out":
+        elif mod.shard_kind in ("out", "rows"):
             b = b[mod.row_start : mod.row_stop]
         if tuple(a.shape) != tuple(mod.a.shape) or tuple(b.shape) != tuple(mod.b.shape):
             raise ValueError(f"shape mismatch for {mod.hf_module_path}: adapter A{tuple(a.shape)} B{tuple(b.shape)}, "

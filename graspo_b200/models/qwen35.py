@@ -22,8 +22,8 @@ in-chunk triangular system is solved with one batched ``solve_triangular``
 one-token decode step of the recurrence runs in the ``gated_delta_step``
 kernel on GPUs.  LoRA is applied on the reference's targets
 (``language.full_attn.*``, ``language.linear_attn.{q,k,v}_proj`` (row blocks of
-``in_proj_qkv``), ``in_proj_z``, ``out_proj``, ``language.mlp.*``).  This family
-runs with TP = 1 (one process per pipeline / data replica).
+``in_proj_qkv``), ``in_proj_z``, ``out_proj``, ``language.mlp.*``).  Heads
+are split over the tensor-parallel group (``Qwen35Model``).
 """
 
 from __future__ import annotations
@@ -32,6 +32,7 @@ import math
 from dataclasses import dataclass, field
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from graspo_b200.core.lora_targets import lora_target_enabled
@@ -40,6 +41,7 @@ from graspo_b200.models.loader import SafetensorIndex
 from graspo_b200.models.lora import LoRAAdapter, LoRAModule
 from graspo_b200.models.qwen3 import EagerLoRA
 from graspo_b200.parallel.state import ParallelState
+from graspo_b200.parallel.tp import copy_to_tp, reduce_from_tp
 
 CHUNK = 64
 
@@ -134,7 +136,21 @@ _TARGETS = {
 
 
 class Qwen35Model:
-    """Weights and LoRA state of the hybrid decoder (TP = 1)."""
+    """Weights and LoRA state of the hybrid decoder, sharded over the TP group.
+
+    Tensor parallelism splits heads (reference: models/common/layers.py:145-633):
+    full attention keeps ``nq/tp`` query heads (their query+gate rows of
+    ``q_proj``) and ``nkv/tp`` key/value heads, DeltaNet keeps ``lk/tp`` key
+    heads and ``lv/tp`` value heads (rows of ``in_proj_qkv`` in each of its
+    q / k / v blocks, the matching conv channels, rows of ``in_proj_z/b/a``,
+    ``dt_bias``, ``A_log``), the MLP keeps ``I/tp`` intermediate rows;
+    ``o_proj`` / ``out_proj`` / ``down_proj`` keep the matching input columns
+    and their outputs are summed over the group.  Embedding, norms and LM head
+    are replicated.  LoRA shard kinds follow the reference checkpoint format:
+    ``rows`` for head-row selections (A replicated), ``out`` for
+    ``in_proj_z`` / gate / up, ``in`` for the row-parallel projections (B
+    replicated).
+    """
 
     supports_kv_cache = True
 
@@ -143,8 +159,6 @@ class Qwen35Model:
                  lora_targets=frozenset(), lora_r: int = 8, lora_alpha: float = 16, lora_dropout: float = 0.0,
                  dtype: torch.dtype = torch.bfloat16, device: torch.device = torch.device("cpu"), seed: int = 42,
                  gradient_checkpointing: bool = True) -> None:
-        if ps.tp_size != 1:
-            raise NotImplementedError("the qwen3_5_text family runs with tp_size=1")
         t = cfg.extra["text_config"]
         self.cfg, self.ps, self.dtype, self.device = cfg, ps, dtype, device
         self.gradient_checkpointing = gradient_checkpointing
@@ -161,12 +175,40 @@ class Qwen35Model:
         self.dk, self.dv = int(t["linear_key_head_dim"]), int(t["linear_value_head_dim"])
         self.conv_k = int(t["linear_conv_kernel_dim"])
         self.key_dim, self.value_dim = self.lk_heads * self.dk, self.lv_heads * self.dv
+        tp, tr = ps.tp_size, ps.tp_rank
+        self.tp_group = ps.tp_group if tp > 1 else None
+        for n, what in ((self.nq, "attention heads"), (self.nkv, "key/value heads"),
+                        (self.lk_heads, "linear-attention key heads"), (self.lv_heads, "linear-attention value heads"),
+                        (cfg.intermediate_size, "intermediate size")):
+            if n % tp:
+                raise ValueError(f"qwen3_5_text: {what} ({n}) must be divisible by tp_size={tp}")
+        # local head counts and widths
+        self.nq_l, self.nkv_l = self.nq // tp, self.nkv // tp
+        self.lk_l, self.lv_l = self.lk_heads // tp, self.lv_heads // tp
+        self.kd_l, self.vd_l = self.lk_l * self.dk, self.lv_l * self.dv
+        self.inter_l = cfg.intermediate_size // tp
+        H, D, kd = cfg.hidden_size, self.D, self.key_dim
         pre = cfg.key_prefix
         dev, dt = device, dtype
 
         def load(name):
             return loader.get(name).to(device=dev, dtype=dt)
 
+        def rows(name, a, b):
+            return loader.get_rows(name, a, b).to(device=dev, dtype=dt)
+
+        def cols(name, a, b):
+            return loader.get_cols(name, a, b).to(device=dev, dtype=dt)
+
+        qr = (tr * self.nq_l * 2 * D, (tr + 1) * self.nq_l * 2 * D)          # query+gate rows of q_proj
+        kvr = (tr * self.nkv_l * D, (tr + 1) * self.nkv_l * D)
+        oc = (tr * self.nq_l * D, (tr + 1) * self.nq_l * D)
+        lqr = (tr * self.kd_l, (tr + 1) * self.kd_l)                          # q block of in_proj_qkv
+        lkr = (kd + lqr[0], kd + lqr[1])                                      # k block
+        lvr = (2 * kd + tr * self.vd_l, 2 * kd + (tr + 1) * self.vd_l)        # v block
+        zr = (tr * self.vd_l, (tr + 1) * self.vd_l)
+        hr = (tr * self.lv_l, (tr + 1) * self.lv_l)                           # value heads
+        ir = (tr * self.inter_l, (tr + 1) * self.inter_l)
         self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
         self.vocab_local, self.vocab_start = cfg.vocab_size, 0
         self.layers: list[HybridLayer] = []
@@ -175,34 +217,51 @@ class Qwen35Model:
             p = f"{pre}.layers.{idx}"
             kind = cfg.layer_kind(idx)
             lay = HybridLayer(idx, kind, load(f"{p}.input_layernorm.weight"), load(f"{p}.post_attention_layernorm.weight"))
+            # kind -> (shard kind, full rows, (row range), full cols, (col range), exportable as its own PEFT module)
             if kind == "full_attention":
-                for n in ("q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm"):
-                    lay.w[n] = load(f"{p}.self_attn.{n}.weight")
-                sizes = {"fq": (cfg.hidden_size, 2 * self.nq * self.D), "fk": (cfg.hidden_size, self.nkv * self.D),
-                         "fv": (cfg.hidden_size, self.nkv * self.D), "fo": (self.nq * self.D, cfg.hidden_size)}
+                a = f"{p}.self_attn"
+                lay.w["q_proj"] = rows(f"{a}.q_proj.weight", *qr)
+                lay.w["k_proj"] = rows(f"{a}.k_proj.weight", *kvr)
+                lay.w["v_proj"] = rows(f"{a}.v_proj.weight", *kvr)
+                lay.w["o_proj"] = cols(f"{a}.o_proj.weight", *oc)
+                lay.w["q_norm"], lay.w["k_norm"] = load(f"{a}.q_norm.weight"), load(f"{a}.k_norm.weight")
+                shards = {"fq": ("rows", 2 * self.nq * D, qr, H, (0, H), True),
+                          "fk": ("rows", self.nkv * D, kvr, H, (0, H), True),
+                          "fv": ("rows", self.nkv * D, kvr, H, (0, H), True),
+                          "fo": ("in", H, (0, H), self.nq * D, oc, True)}
             else:
-                for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
-                    lay.w[n] = load(f"{p}.linear_attn.{n}.weight")
-                lay.w["conv"] = load(f"{p}.linear_attn.conv1d.weight").reshape(-1, self.conv_k)
-                lay.w["dt_bias"] = loader.get(f"{p}.linear_attn.dt_bias").float().to(dev)
-                lay.w["A_log"] = loader.get(f"{p}.linear_attn.A_log").float().to(dev)
-                lay.w["norm"] = load(f"{p}.linear_attn.norm.weight")
-                H = cfg.hidden_size
-                sizes = {"lq": (H, self.key_dim), "lk": (H, self.key_dim), "lv": (H, self.value_dim),
-                         "lz": (H, self.value_dim), "lo": (self.value_dim, H)}
-            for n in ("gate_proj", "up_proj", "down_proj"):
-                lay.w[n] = load(f"{p}.mlp.{n}.weight")
-            sizes.update({"gate": (cfg.hidden_size, cfg.intermediate_size), "up": (cfg.hidden_size, cfg.intermediate_size),
-                          "down": (cfg.intermediate_size, cfg.hidden_size)})
+                a = f"{p}.linear_attn"
+                lay.w["in_proj_qkv"] = torch.cat([rows(f"{a}.in_proj_qkv.weight", *r) for r in (lqr, lkr, lvr)])
+                lay.w["in_proj_z"] = rows(f"{a}.in_proj_z.weight", *zr)
+                lay.w["in_proj_b"] = rows(f"{a}.in_proj_b.weight", *hr)
+                lay.w["in_proj_a"] = rows(f"{a}.in_proj_a.weight", *hr)
+                lay.w["out_proj"] = cols(f"{a}.out_proj.weight", *zr)
+                conv = loader.get(f"{a}.conv1d.weight").reshape(-1, self.conv_k)
+                lay.w["conv"] = torch.cat([conv[r0:r1] for r0, r1 in (lqr, lkr, lvr)]).to(device=dev, dtype=dt)
+                lay.w["dt_bias"] = loader.get(f"{a}.dt_bias")[hr[0]:hr[1]].float().to(dev)
+                lay.w["A_log"] = loader.get(f"{a}.A_log")[hr[0]:hr[1]].float().to(dev)
+                lay.w["norm"] = load(f"{a}.norm.weight")
+                qkv_rows = 2 * kd + self.value_dim
+                shards = {"lq": ("rows", qkv_rows, lqr, H, (0, H), False),
+                          "lk": ("rows", qkv_rows, lkr, H, (0, H), False),
+                          "lv": ("rows", qkv_rows, lvr, H, (0, H), False),
+                          "lz": ("out", self.value_dim, zr, H, (0, H), True),
+                          "lo": ("in", H, (0, H), self.value_dim, zr, True)}
+            lay.w["gate_proj"] = rows(f"{p}.mlp.gate_proj.weight", *ir)
+            lay.w["up_proj"] = rows(f"{p}.mlp.up_proj.weight", *ir)
+            lay.w["down_proj"] = cols(f"{p}.mlp.down_proj.weight", *ir)
+            I = cfg.intermediate_size
+            shards.update({"gate": ("out", I, ir, H, (0, H), True), "up": ("out", I, ir, H, (0, H), True),
+                           "down": ("in", H, (0, H), I, ir, True)})
             self.layers.append(lay)
-            for k, (fan_in, fan_out) in sizes.items():
+            for k, (sk, out_full, (r0, r1), in_full, (c0, c1), exportable) in shards.items():
                 target, sub = _TARGETS[k]
                 if not lora_target_enabled(self.lora_targets, target):
                     continue
                 modules.append(LoRAModule(
                     module_name=f"layers.{idx}.{k}", target_name=target, hf_module_path=f"{p}.{sub}", layer=idx,
-                    kind=k, shard_kind="none", in_full=fan_in, out_full=fan_out, in_local=fan_in, out_local=fan_out,
-                    row_start=0, row_stop=fan_out, col_start=0, col_stop=fan_in))
+                    kind=k, shard_kind=sk, in_full=in_full, out_full=out_full, in_local=c1 - c0, out_local=r1 - r0,
+                    row_start=r0, row_stop=r1, col_start=c0, col_stop=c1, peft_exportable=exportable))
         if include_head:
             self.norm = load(f"{pre}.norm.weight")
             name = "lm_head.weight" if loader.has("lm_head.weight") else f"{pre}.embed_tokens.weight"
@@ -229,12 +288,21 @@ class Qwen35Model:
         return self.lora.target_names()
 
     def estimate_kv_cache_bytes(self, *, batch_size: int, sequence_len: int) -> int:
+        """Bytes of this rank's decoding caches (local heads of the local layers)."""
         full = sum(1 for lay in self.layers if lay.kind == "full_attention")
         lin = len(self.layers) - full
-        kv = batch_size * full * 2 * self.nkv * self.D * sequence_len * self.dtype.itemsize
-        state = batch_size * lin * (self.lv_heads * self.dk * self.dv * 4
-                                    + (2 * self.key_dim + self.value_dim) * self.conv_k * self.dtype.itemsize)
+        kv = batch_size * full * 2 * self.nkv_l * self.D * sequence_len * self.dtype.itemsize
+        state = batch_size * lin * (self.lv_l * self.dk * self.dv * 4
+                                    + (2 * self.kd_l + self.vd_l) * self.conv_k * self.dtype.itemsize)
         return kv + state
+
+    def _f(self, x):
+        """Identity forward, all-reduce backward (input of the column-parallel projections)."""
+        return copy_to_tp(x, self.tp_group) if self.tp_group is not None else x
+
+    def _g(self, x):
+        """All-reduce forward, identity backward (output of the row-parallel projections)."""
+        return reduce_from_tp(x, self.tp_group) if self.tp_group is not None else x
 
     # ---------------------------------------------------------------- pieces
     def _lin(self, x, w, lay, kind, lora, training):
@@ -260,10 +328,11 @@ class Qwen35Model:
     def _full_attn(self, lay, h, pos, key_mask, lora, training, cache=None):
         B, S, _ = h.shape
         D = self.D
-        qg = self._lin(h, lay.w["q_proj"], lay, "fq", lora, training).view(B, S, self.nq, 2 * D)
-        q, gate = qg[..., :D], qg[..., D:].reshape(B, S, self.nq * D)
-        k = self._lin(h, lay.w["k_proj"], lay, "fk", lora, training).view(B, S, self.nkv, D)
-        v = self._lin(h, lay.w["v_proj"], lay, "fv", lora, training).view(B, S, self.nkv, D)
+        nq, nkv = self.nq_l, self.nkv_l
+        qg = self._lin(h, lay.w["q_proj"], lay, "fq", lora, training).view(B, S, nq, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(B, S, nq * D)
+        k = self._lin(h, lay.w["k_proj"], lay, "fk", lora, training).view(B, S, nkv, D)
+        v = self._lin(h, lay.w["v_proj"], lay, "fv", lora, training).view(B, S, nkv, D)
         q = self._rope(norm1p(q, lay.w["q_norm"], self.cfg.rms_norm_eps), pos)
         k = self._rope(norm1p(k, lay.w["k_norm"], self.cfg.rms_norm_eps), pos)
         if cache is not None:
@@ -272,7 +341,7 @@ class Qwen35Model:
                 v = torch.cat([cache["v"], v], 1)
             cache["k"], cache["v"] = k, v
         Sk = k.shape[1]
-        G = self.nq // self.nkv
+        G = nq // nkv
         qh = q.transpose(1, 2)
         kh = k.transpose(1, 2).repeat_interleave(G, 1)
         vh = v.transpose(1, 2).repeat_interleave(G, 1)
@@ -282,14 +351,14 @@ class Qwen35Model:
         # a padding query attends to itself, so no softmax row is empty
         allowed = allowed | (qpos[:, None] == kpos[None])[None]
         o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=allowed[:, None], scale=1.0 / math.sqrt(D))
-        o = o.transpose(1, 2).reshape(B, S, self.nq * D)
-        return self._lin(o * torch.sigmoid(gate), lay.w["o_proj"], lay, "fo", lora, training)
+        o = o.transpose(1, 2).reshape(B, S, nq * D)
+        return self._lin(o * torch.sigmoid(gate), lay.w["o_proj"], lay, "fo", lora, training)   # partial over TP
 
     def _linear_attn(self, lay, h, key_mask, lora, training, cache=None):
         B, S, _ = h.shape
         h = h * key_mask[:, -S:, None].to(h.dtype)
         W = lay.w["in_proj_qkv"]
-        kd, vd = self.key_dim, self.value_dim
+        kd, vd = self.kd_l, self.vd_l
         q = self._lin(h, W[:kd], lay, "lq", lora, training)
         k = self._lin(h, W[kd : 2 * kd], lay, "lk", lora, training)
         v = self._lin(h, W[2 * kd :], lay, "lv", lora, training)
@@ -302,10 +371,10 @@ class Qwen35Model:
         conv = F.conv1d(ext, lay.w["conv"][:, None, :], groups=mixed.shape[1])
         mixed = F.silu(conv).transpose(1, 2)                               # [B, S, C]
         q, k, v = mixed[..., :kd], mixed[..., kd : 2 * kd], mixed[..., 2 * kd :]
-        q = q.reshape(B, S, self.lk_heads, self.dk)
-        k = k.reshape(B, S, self.lk_heads, self.dk)
-        v = v.reshape(B, S, self.lv_heads, self.dv)
-        z = self._lin(h, lay.w["in_proj_z"], lay, "lz", lora, training).reshape(B, S, self.lv_heads, self.dv)
+        q = q.reshape(B, S, self.lk_l, self.dk)
+        k = k.reshape(B, S, self.lk_l, self.dk)
+        v = v.reshape(B, S, self.lv_l, self.dv)
+        z = self._lin(h, lay.w["in_proj_z"], lay, "lz", lora, training).reshape(B, S, self.lv_l, self.dv)
         beta = torch.sigmoid(F.linear(h, lay.w["in_proj_b"]).float())
         g = -lay.w["A_log"].exp() * F.softplus(F.linear(h, lay.w["in_proj_a"]).float() + lay.w["dt_bias"])
         rep = self.lv_heads // self.lk_heads
@@ -322,19 +391,19 @@ class Qwen35Model:
                 cache["state"] = fin.detach().clone()
         o = gated_norm(o.to(h.dtype).reshape(-1, self.dv), z.reshape(-1, self.dv), lay.w["norm"],
                        self.cfg.rms_norm_eps).reshape(B, S, vd)
-        return self._lin(o, lay.w["out_proj"], lay, "lo", lora, training)
+        return self._lin(o, lay.w["out_proj"], lay, "lo", lora, training)   # partial over TP
 
     def layer(self, lay, x, pos, key_mask, lora=None, training=False, cache=None):
         eps = self.cfg.rms_norm_eps
-        h = norm1p(x, lay.ln1, eps)
+        h = self._f(norm1p(x, lay.ln1, eps))
         if lay.kind == "full_attention":
-            x = x + self._full_attn(lay, h, pos, key_mask, lora, training, cache)
+            x = x + self._g(self._full_attn(lay, h, pos, key_mask, lora, training, cache))
         else:
-            x = x + self._linear_attn(lay, h, key_mask, lora, training, cache)
-        h2 = norm1p(x, lay.ln2, eps)
+            x = x + self._g(self._linear_attn(lay, h, key_mask, lora, training, cache))
+        h2 = self._f(norm1p(x, lay.ln2, eps))
         gate = self._lin(h2, lay.w["gate_proj"], lay, "gate", lora, training)
         up = self._lin(h2, lay.w["up_proj"], lay, "up", lora, training)
-        return x + self._lin(F.silu(gate) * up, lay.w["down_proj"], lay, "down", lora, training)
+        return x + self._g(self._lin(F.silu(gate) * up, lay.w["down_proj"], lay, "down", lora, training))
 
     def forward(self, ids, mask, *, lora=None, training=False, caches=None, pos=None, key_mask=None):
         """[B, S] ids -> final hidden [B, S, H] (whole-sequence; caches fill for decoding)."""
@@ -424,6 +493,9 @@ class HybridRolloutEngine:
         steps = 0
         for t in range(max_new_tokens):
             tok = EagerRolloutEngine._sample(logits, temperature, top_p, gen)
+            if m.tp_group is not None:
+                # TP ranks hold the same logits and noise; the leader's draw settles any last-bit difference
+                dist.broadcast(tok, src=m.ps.rank_of(tp=0, pp=m.ps.pp_rank, dp=m.ps.dp_rank), group=m.tp_group)
             tok = torch.where(finished, torch.full_like(tok, pad_id), tok)
             out[:, t] = tok
             if not ignore_eos:
