@@ -78,6 +78,8 @@ def collate(items: list[Experience], device: torch.device, pad_id: int):
 class Qwen3Adapter:
     families: tuple[str, ...] = ("qwen3",)
     model_class = Qwen3Model
+    # pipeline stages through the autograd forward (families without the fused path)
+    autograd_pipeline = False
 
     def __new__(cls, config: Any = None, *args: Any, **kwargs: Any):
         # the default adapter serves both families: a qwen3_5 checkpoint gets the hybrid adapter
@@ -130,8 +132,8 @@ class Qwen3Adapter:
         from graspo_b200.parallel.p2p import StageComm
 
         self._comm = StageComm(self.ps)
-        if self.ps.pp_size > 1 and not self.fused:
-            raise NotImplementedError("pipeline parallelism runs on the fused sm_100a kernels (GPUs)")
+        if self.ps.pp_size > 1 and not (self.fused or self.autograd_pipeline):
+            raise NotImplementedError("pipeline parallelism of this family runs on the fused sm_100a kernels (GPUs)")
         model_path = Path(cfg.model.model_path)
         if not model_path.exists():
             raise FileNotFoundError(f"model.model_path does not exist: {model_path}")
@@ -161,7 +163,13 @@ class Qwen3Adapter:
             gradient_checkpointing=cfg.model.gradient_checkpointing,
         )
         loader.close()
-        missing = sorted(set(targets.resolved) - set(self.model.enabled_lora_target_names()))
+        enabled = set(self.model.enabled_lora_target_names())
+        if self.ps.pp_size > 1 and self.ps.distributed:
+            # a stage holds some layer kinds only: the targets must be covered by the whole pipeline
+            parts: list = [None] * self.ps.pp_size
+            dist.all_gather_object(parts, sorted(enabled), group=self.ps.pp_group)
+            enabled = set().union(*map(set, parts))
+        missing = sorted(set(targets.resolved) - enabled)
         if missing:
             raise ValueError("Resolved LoRA target(s) are not implemented by this model: " + ", ".join(missing))
         if cfg.lora.adapter_path:
@@ -419,8 +427,11 @@ class Qwen3Adapter:
         if media_rows and any(media_rows):
             return self._logprobs(seq, mask, train=False, embed_hook=self._image_hook(media_rows))[0]
         if self.ps.pp_size > 1:
-            from graspo_b200.engine.pipeline import pp_logprobs
+            from graspo_b200.engine.pipeline import pp_logprobs, pp_logprobs_autograd
 
+            if not self.fused:
+                return pp_logprobs_autograd(self.model, self._comm, seq, mask, seq[:, 1:],
+                                            chunk_rows=self._pp_chunk_rows(seq))
             return pp_logprobs(self._fused, self._comm, seq, mask, seq[:, 1:], chunk_rows=self._pp_chunk_rows(seq))
         outs = []
         for sl in self._token_budget_chunks(seq.shape[0], seq.shape[1]):
@@ -520,6 +531,18 @@ class Qwen3Adapter:
     def _backward_grpo(self, seq, mask, old, adv, act, clip_eps: float, seed: int, embed_hook=None):
         """Forward + GRPO loss + backward into the flat grad buffer; returns loss (device)."""
         B, S = seq.shape
+        if self.ps.pp_size > 1 and not self.fused:
+            from graspo_b200.engine.pipeline import pp_train_autograd
+
+            if embed_hook is not None:
+                raise NotImplementedError("image inputs with pipeline stages are not supported")
+            self.loss_fn.policy_ratio_clip_eps = clip_eps
+
+            def chunk_loss(logp_c, sl):
+                return self.loss_fn(logp_c, old[sl], adv[sl], act[sl]) * ((sl.stop - sl.start) / B)
+
+            return pp_train_autograd(self.model, self._comm, seq, mask, seq[:, 1:], chunk_loss,
+                                     chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
             from graspo_b200.ops._ext import ext
@@ -656,6 +679,14 @@ class Qwen3Adapter:
         valid = tgt.ne(-100)
         denom = valid.sum().clamp_min(1)
         safe = torch.where(valid, tgt, torch.zeros_like(tgt))
+        if self.ps.pp_size > 1 and not self.fused:
+            from graspo_b200.engine.pipeline import pp_train_autograd
+
+            def chunk_loss(logp_c, sl):
+                return -(logp_c * valid[sl]).sum() / denom
+
+            return pp_train_autograd(self.model, self._comm, ids, mask, safe, chunk_loss,
+                                     chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
 
@@ -759,6 +790,7 @@ class Qwen35Adapter(Qwen3Adapter):
     """
 
     families = ("qwen3_5_text",)
+    autograd_pipeline = True
 
     @property
     def model_class(self):
@@ -773,4 +805,4 @@ class Qwen35Adapter(Qwen3Adapter):
     def _eager_engine(self):
         from graspo_b200.models.qwen35 import HybridRolloutEngine
 
-        return HybridRolloutEngine(self.model)
+        return HybridRolloutEngine(self.model, comm=self._comm)

@@ -123,3 +123,85 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
                 comm.send_prev(dx_in)
     comm.flush()
     return comm.broadcast_from_last(total)
+
+
+# ---------------------------------------------------------------- autograd stages
+# Families without the fused kernel path (the Qwen3.5 hybrid) pipeline their
+# autograd forward instead: a stage runs ``model.forward(..., x=<previous
+# stage output>)`` with per-layer gradient checkpointing, the last stage turns
+# the hidden states into log-probs and the micro-batch loss, and the backward of
+# a micro-batch is one ``backward`` call whose input gradient goes upstream.
+# Same chunking, schedules and transfers as the fused functions above
+# (reference: models/qwen35_36/training.py:567-1043, logprobs.py:65-121).
+
+
+def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor, *,
+                         chunk_rows: int) -> torch.Tensor:
+    """log p(targets) [B, S-1] on every stage of the column (forward only)."""
+    from graspo_b200.models.qwen3 import EagerLoRA
+
+    ps = comm.ps
+    B, S = seq.shape
+    H = model.cfg.hidden_size
+    outs = []
+    lora = EagerLoRA(model.lora, requires_grad=False)
+    with torch.no_grad():
+        for sl in _chunks(B, chunk_rows):
+            rows = sl.stop - sl.start
+            x = None if ps.is_first_stage else comm.recv_prev((rows, S, H), model.dtype)
+            xL = model.forward(seq[sl], mask[sl], x=x, lora=lora)
+            if ps.is_last_stage:
+                outs.append(model.token_logprobs(xL[:, :-1], targets[sl]).float())
+            else:
+                comm.send_next(xL)
+    comm.flush()
+    logp = torch.cat(outs, 0).contiguous() if ps.is_last_stage else \
+        torch.empty(B, S - 1, device=seq.device, dtype=torch.float32)
+    return comm.broadcast_from_last(logp)
+
+
+def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
+                      loss_fn: Callable[[torch.Tensor, slice], torch.Tensor], *, chunk_rows: int,
+                      schedule: str = "one_f_one_b") -> torch.Tensor:
+    """Forward + backward of one optimizer step into ``model.lora.grads``.
+
+    ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
+    returns the chunk's differentiable loss, already weighted by its share.
+    Returns the summed loss on every stage."""
+    from graspo_b200.models.qwen3 import EagerLoRA
+
+    ps = comm.ps
+    B, S = seq.shape
+    H = model.cfg.hidden_size
+    chunks = _chunks(B, chunk_rows)
+    plan = get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank).plan(len(chunks))
+    lora = EagerLoRA(model.lora, requires_grad=True)
+    saved: dict[int, tuple] = {}
+    total = torch.zeros(1, device=seq.device, dtype=torch.float32)
+    for step in plan:
+        c = step.microbatch_idx
+        sl = chunks[c]
+        rows = sl.stop - sl.start
+        if step.action == PipelineAction.FORWARD:
+            x = None
+            if not ps.is_first_stage:
+                x = comm.recv_prev((rows, S, H), model.dtype).requires_grad_(True)
+            with torch.enable_grad():
+                xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, training=True)
+                if ps.is_last_stage:
+                    out = loss_fn(model.token_logprobs(xL[:, :-1], targets[sl]).float(), sl).reshape(1)
+                    total += out.detach()
+                else:
+                    comm.send_next(xL.detach())
+                    out = xL
+            saved[c] = (x, out)
+        else:
+            x, out = saved.pop(c)
+            grad = None if ps.is_last_stage else comm.recv_next((rows, S, H), model.dtype)
+            if out.requires_grad:
+                out.backward(grad)
+            if not ps.is_first_stage:
+                comm.send_prev(x.grad if x.grad is not None else torch.zeros_like(x))
+    comm.flush()
+    lora.accumulate_grads()
+    return comm.broadcast_from_last(total)

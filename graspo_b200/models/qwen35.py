@@ -405,9 +405,12 @@ class Qwen35Model:
         up = self._lin(h2, lay.w["up_proj"], lay, "up", lora, training)
         return x + self._g(self._lin(F.silu(gate) * up, lay.w["down_proj"], lay, "down", lora, training))
 
-    def forward(self, ids, mask, *, lora=None, training=False, caches=None, pos=None, key_mask=None):
-        """[B, S] ids -> final hidden [B, S, H] (whole-sequence; caches fill for decoding)."""
-        x = F.embedding(ids, self.embed)
+    def forward(self, ids, mask, *, x=None, lora=None, training=False, caches=None, pos=None, key_mask=None):
+        """[B, S] ids -> hidden [B, S, H] after this stage's layers (whole-sequence;
+        caches fill for decoding).  On a later pipeline stage ``x`` is the
+        previous stage's output and ``ids`` is unused."""
+        if x is None:
+            x = F.embedding(ids, self.embed)
         pos = (mask.long().cumsum(-1) - 1).clamp_min(0) if pos is None else pos
         key_mask = mask if key_mask is None else key_mask
         for i, lay in enumerate(self.layers):
@@ -453,10 +456,30 @@ def gated_delta_step(q, k, v, g, beta, state):
 class HybridRolloutEngine:
     """Grouped sampling for the hybrid decoder: each prompt is prefilled once,
     its caches (KV for attention layers, conv + recurrent state for DeltaNet
-    layers) are copied to its G rows, then tokens are decoded one at a time."""
+    layers) are copied to its G rows, then tokens are decoded one at a time.
 
-    def __init__(self, model: Qwen35Model) -> None:
+    With pipeline stages (``comm`` over a column of stages, each holding the
+    caches of its own layers) the hidden states of the prefill and of every
+    decoding step travel stage to stage, the last stage samples, and the token
+    is broadcast to the column so every stage embeds / tracks the same rows
+    (the reference has no pipelined rollout: qwen35_36/generation.py:645-685).
+    """
+
+    def __init__(self, model: Qwen35Model, comm=None) -> None:
         self.m = model
+        self.comm = comm if comm is not None and comm.active else None
+
+    def _stage(self, ids, mask, **kw):
+        """This stage's layers: input from the previous stage (or the embedding), output to the next."""
+        m, comm = self.m, self.comm
+        x = None
+        if comm is not None and not m.ps.is_first_stage:
+            x = comm.recv_prev((ids.shape[0], ids.shape[1], m.cfg.hidden_size), m.dtype)
+        y = m.forward(ids, mask, x=x, **kw)
+        if comm is not None and not m.ps.is_last_stage:
+            comm.send_next(y)
+            comm.flush()
+        return y
 
     @torch.no_grad()
     def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
@@ -465,7 +488,8 @@ class HybridRolloutEngine:
 
         from graspo_b200.engine.rollout import EagerRolloutEngine, RolloutResult, _gen_lengths
 
-        m, dev = self.m, self.m.device
+        m, dev, comm = self.m, self.m.device, self.comm
+        last = comm is None or m.ps.is_last_stage
         n, G = len(prompts), int(group_size)
         lens = [max(1, len(p)) for p in prompts]
         P = max(lens)
@@ -478,13 +502,14 @@ class HybridRolloutEngine:
         t0 = time.perf_counter()
         ids_d, mask_d = ids.to(dev), mask.to(dev)
         caches = [dict() for _ in m.layers]
-        hidden = m.forward(ids_d, mask_d, caches=caches)
+        lora = EagerLoRA(m.lora, requires_grad=False)      # the current policy's adapter (views of the master)
+        hidden = self._stage(ids_d, mask_d, caches=caches, lora=lora)
         for c in caches:
             for key, val in list(c.items()):
                 c[key] = val.repeat_interleave(G, 0)
         key_mask = mask_d.repeat_interleave(G, 0)
         pos = (mask_d.long().sum(-1) - 1).repeat_interleave(G, 0)
-        logits = m.logits(hidden[:, -1]).repeat_interleave(G, 0)
+        logits = m.logits(hidden[:, -1]).repeat_interleave(G, 0) if last else None
         gen = torch.Generator(device=dev).manual_seed(int(seed))
         rows = n * G
         out = torch.full((rows, max_new_tokens), pad_id, dtype=torch.long, device=dev)
@@ -492,10 +517,15 @@ class HybridRolloutEngine:
         t1 = time.perf_counter()
         steps = 0
         for t in range(max_new_tokens):
-            tok = EagerRolloutEngine._sample(logits, temperature, top_p, gen)
-            if m.tp_group is not None:
-                # TP ranks hold the same logits and noise; the leader's draw settles any last-bit difference
-                dist.broadcast(tok, src=m.ps.rank_of(tp=0, pp=m.ps.pp_rank, dp=m.ps.dp_rank), group=m.tp_group)
+            if last:
+                tok = EagerRolloutEngine._sample(logits, temperature, top_p, gen)
+                if m.tp_group is not None:
+                    # TP ranks hold the same logits and noise; the leader's draw settles any last-bit difference
+                    dist.broadcast(tok, src=m.ps.rank_of(tp=0, pp=m.ps.pp_rank, dp=m.ps.dp_rank), group=m.tp_group)
+            else:
+                tok = torch.empty(rows, dtype=torch.long, device=dev)
+            if comm is not None:
+                comm.broadcast_from_last(tok)
             tok = torch.where(finished, torch.full_like(tok, pad_id), tok)
             out[:, t] = tok
             if not ignore_eos:
@@ -505,8 +535,9 @@ class HybridRolloutEngine:
                 break
             key_mask = torch.cat([key_mask, torch.ones(rows, 1, dtype=torch.bool, device=dev)], 1)
             pos = pos + 1
-            x = m.forward(tok[:, None], key_mask[:, -1:], caches=caches, pos=pos[:, None], key_mask=key_mask)
-            logits = m.logits(x[:, -1])
+            x = self._stage(tok[:, None], key_mask[:, -1:], caches=caches, pos=pos[:, None], key_mask=key_mask,
+                            lora=lora)
+            logits = m.logits(x[:, -1]) if last else None
         tokens = out.cpu()
         return RolloutResult(prompt_ids=ids, prompt_lens=lens, tokens=tokens,
                              gen_lens=_gen_lengths(tokens, eos_id, ignore_eos), group_size=G,

@@ -4,7 +4,9 @@ The eager forward of both model families is compared with the
 ``transformers`` modules of the same architecture on the same random-init
 checkpoint: ``Qwen3ForCausalLM`` for the dense family and
 ``Qwen3_5ForCausalLM`` (gated DeltaNet + gated attention, partial RoPE,
-(1 + w) norms) for the hybrid one.  Left-padded rows get the positions that
+(1 + w) norms) for the hybrid one, ``Qwen3_5VisionModel`` for the vision
+tower (patch embedding, resampled position table, 2-D rotary, merger) on
+images of two grid sizes.  Left-padded rows get the positions that
 the training and rollout paths use (count of real tokens before them).
 Reference behaviour: models/qwen3/model.py:250-365 and
 models/qwen35_36/model.py:486-543, both built to reproduce the HF modules.
@@ -94,3 +96,37 @@ def test_qwen35_hybrid_matches_transformers(tmp_path):
     lp = m.sequence_logprobs(ids, mask)
     valid = mask[:, :-1] & mask[:, 1:]
     assert (lp - _hf_logprobs(ref, ids)).abs()[valid].max().item() < 1e-3
+
+
+def test_vision_tower_matches_transformers(tmp_path):
+    """The native ViT + 2x2 merger equals ``Qwen3_5VisionModel`` on the same weights and patches."""
+    from safetensors.torch import load_file
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5VisionConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5VisionModel
+
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.vision import VisionConfig, VisionTower, preprocess
+    from graspo_b200.utils.synth import TINY, VIT_TINY, add_vision_tower, write_qwen3_checkpoint
+
+    path = add_vision_tower(write_qwen3_checkpoint(tmp_path / "vl", TINY, seed=1, device="cpu", dtype=torch.float32,
+                                                   with_tokenizer=False), VIT_TINY, seed=2, std=0.2,
+                            dtype=torch.float32)
+    vc = json.loads((path / "config.json").read_text())["vision_config"]
+    hc = Qwen3_5VisionConfig(**vc)
+    hc._attn_implementation = "eager"
+    hf = Qwen3_5VisionModel(hc).float().eval()
+    state = {k[len("model.visual."):]: v for k, v in load_file(str(path / "model-vision.safetensors")).items()}
+    missing, unexpected = hf.load_state_dict(state, strict=False)
+    assert not missing and not unexpected, (missing, unexpected)
+    cfg = VisionConfig.from_dict(vc)
+    vt = VisionTower(cfg, SafetensorIndex(path), "model.visual", dtype=torch.float32, device=torch.device("cpu"))
+    g = torch.Generator().manual_seed(0)
+    images = [torch.randint(0, 256, (96, 128, 3), dtype=torch.uint8, generator=g),
+              torch.randint(0, 256, (64, 64, 3), dtype=torch.uint8, generator=g)]
+    pre = [preprocess(img, cfg) for img in images]
+    with torch.no_grad():
+        mine = vt.encode([p for p, _ in pre], [grid for _, grid in pre])
+        out = hf(torch.cat([p for p, _ in pre]), grid_thw=torch.tensor([list(grid) for _, grid in pre]))
+    ref = out.pooler_output
+    assert mine.shape == ref.shape
+    assert (mine - ref).abs().max().item() < 1e-3 * ref.abs().max().item()
