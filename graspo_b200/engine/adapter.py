@@ -296,7 +296,8 @@ class Qwen3Adapter:
         return int(self.tokenizer.convert_tokens_to_ids("<|vision_pad|>"))
 
     def _image_features(self, media_rows: list[list[dict]]):
-        """Vision-tower features of every image of every row, rows in order (cached per image path)."""
+        """Vision-tower features of every image of every row, rows in order (cached
+        per image path), and the merged grid of each image."""
         from graspo_b200.models.vision import load_image, preprocess
 
         vt = getattr(self.model, "vision", None)
@@ -305,27 +306,28 @@ class Qwen3Adapter:
         cache = self.__dict__.setdefault("_image_cache", {})
         if len(cache) > 512:
             cache.clear()
-        feats = []
+        feats, grids = [], []
+        m = vt.cfg.spatial_merge_size
         for media in media_rows:
             for item in media or []:
                 if item.get("type") != "image":
                     raise NotImplementedError("video inputs are not supported")
                 path = item["path"]
                 if path not in cache:
-                    patches, grid = preprocess(load_image(path), vt.cfg)
-                    cache[path] = vt.encode([patches], [grid])
-                feats.append(cache[path])
-        return torch.cat(feats, 0) if feats else None
+                    patches, (t, gh, gw) = preprocess(load_image(path), vt.cfg)
+                    cache[path] = (vt.encode([patches], [(t, gh, gw)]), (t, gh // m, gw // m))
+                feats.append(cache[path][0])
+                grids.append(cache[path][1])
+        return (torch.cat(feats, 0), grids) if feats else (None, [])
 
     def _image_hook(self, media_rows: list[list[dict]]):
         """embed_hook placing image features on the image placeholder tokens."""
-        from graspo_b200.models.vision import scatter_image_features
+        from graspo_b200.models.vision import ImageInputs
 
-        feats = self._image_features(media_rows)
+        feats, grids = self._image_features(media_rows)
         if feats is None:
             return None
-        pad = self._vision_pad_id
-        return lambda ids, x: scatter_image_features(x, ids, pad, feats)
+        return ImageInputs(feats, self._vision_pad_id, grids)
 
     def _generate_multimodal(self, samples, *, rollout_group_size: int, max_new_tokens: int,
                              max_prompt_length: int | None = None, temperature: float = 1.0, top_p: float = 1.0,
@@ -475,7 +477,8 @@ class Qwen3Adapter:
         lora = EagerLoRA(self.model.lora, requires_grad=train)
         with torch.set_grad_enabled(train):
             if hasattr(self.model, "sequence_logprobs"):
-                logp = self.model.sequence_logprobs(seq, mask, lora=lora, training=train, targets=tgt)
+                logp = self.model.sequence_logprobs(seq, mask, lora=lora, training=train, targets=tgt,
+                                                    embed_hook=embed_hook)
             else:
                 hidden = eager_stage_forward(self.model, seq, mask, lora=lora, training=train, embed_hook=embed_hook)
                 logp = eager_token_logprobs(self.model, hidden[:, :-1], tgt)

@@ -171,6 +171,14 @@ class Qwen35Model:
         theta = float(rp.get("rope_theta", t.get("rope_theta", 1e6)))
         self.inv_freq = (1.0 / theta ** (torch.arange(0, self.rotary_dim, 2, dtype=torch.float32) / self.rotary_dim)
                          ).to(device)
+        # interleaved multimodal RoPE: frequency j follows the height position if j % 3 == 1 and
+        # j < 3 * sections[1], the width position if j % 3 == 2 and j < 3 * sections[2], else time
+        sec = [int(v) for v in (rp.get("mrope_section") or (11, 11, 10))]
+        j = torch.arange(self.rotary_dim // 2)
+        comp = torch.zeros_like(j)
+        comp[(j % 3 == 1) & (j < 3 * sec[1])] = 1
+        comp[(j % 3 == 2) & (j < 3 * sec[2])] = 2
+        self.mrope_component = comp.to(device)
         self.lk_heads, self.lv_heads = int(t["linear_num_key_heads"]), int(t["linear_num_value_heads"])
         self.dk, self.dv = int(t["linear_key_head_dim"]), int(t["linear_value_head_dim"])
         self.conv_k = int(t["linear_conv_kernel_dim"])
@@ -211,6 +219,14 @@ class Qwen35Model:
         ir = (tr * self.inter_l, (tr + 1) * self.inter_l)
         self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
         self.vocab_local, self.vocab_start = cfg.vocab_size, 0
+        # frozen vision tower on the stage that embeds the tokens (replicated over TP)
+        self.vision = None
+        if include_embed and cfg.has_vision:
+            from graspo_b200.models.vision import VisionConfig, VisionTower
+
+            vc = dict(cfg.extra["vision_config"])
+            vc.setdefault("out_hidden_size", cfg.hidden_size)
+            self.vision = VisionTower(VisionConfig.from_dict(vc), loader, "model.visual", dtype=dtype, device=device)
         self.layers: list[HybridLayer] = []
         modules: list[LoRAModule] = []
         for idx in self.local_layers:
@@ -316,9 +332,13 @@ class Qwen35Model:
         return y + (F.linear(F.linear(xin.to(a.dtype), a), b) * ad.scaling).to(y.dtype)
 
     def _rope(self, x, pos):
-        """Partial rotary embedding (rotate-half on the first rotary_dim dims). x [B, S, h, D]; pos [B, S]."""
+        """Partial rotary embedding (rotate-half on the first rotary_dim dims). x [B, S, h, D]; pos [B, S]
+        (text) or [3, B, S] (time / height / width positions of multimodal RoPE)."""
         rd = self.rotary_dim
-        f = pos.float()[..., None] * self.inv_freq                     # [B, S, rd/2]
+        f = pos.float()[..., None] * self.inv_freq                     # [B, S, rd/2] or [3, B, S, rd/2]
+        if pos.dim() == 3:
+            idx = self.mrope_component.view(1, 1, 1, -1).expand(1, *f.shape[1:])
+            f = f.gather(0, idx)[0]
         cos, sin = torch.cat([f, f], -1).cos()[:, :, None], torch.cat([f, f], -1).sin()[:, :, None]
         xr, xp = x[..., :rd].float(), x[..., rd:]
         half = rd // 2
@@ -405,12 +425,52 @@ class Qwen35Model:
         up = self._lin(h2, lay.w["up_proj"], lay, "up", lora, training)
         return x + self._g(self._lin(F.silu(gate) * up, lay.w["down_proj"], lay, "down", lora, training))
 
-    def forward(self, ids, mask, *, x=None, lora=None, training=False, caches=None, pos=None, key_mask=None):
+    def mrope_positions(self, ids, mask, images) -> torch.Tensor:
+        """[3, B, S] time / height / width positions of a batch with image placeholders.
+
+        Text tokens advance one position (all three equal); the ``t * h * w``
+        placeholders of an image (``images.grids``: merged grids in row order)
+        take ``start + (0, row, col)`` and the text after it resumes at
+        ``start + max(h, w)``.  Padding gets 0 (reference:
+        models/qwen35_36/model.py:289-330, 372-461)."""
+        B, S = ids.shape
+        out = torch.zeros(3, B, S, dtype=torch.long)
+        grids = iter(images.grids)
+        ids_c, mask_c = ids.cpu(), mask.cpu()
+        for b in range(B):
+            cols = torch.nonzero(mask_c[b]).flatten().tolist()
+            toks = ids_c[b, cols].tolist()
+            pos, i, rows = 0, 0, []
+            while i < len(toks):
+                if toks[i] != images.pad_id:
+                    rows.append((pos, pos, pos))
+                    pos, i = pos + 1, i + 1
+                    continue
+                t, h, w = next(grids)
+                for ti in range(t):
+                    for hi in range(h):
+                        for wi in range(w):
+                            rows.append((pos + ti, pos + hi, pos + wi))
+                i += t * h * w
+                pos += max(h, w)
+            if len(rows) != len(cols):
+                raise ValueError("image placeholder count does not match the image grids")
+            out[:, b, cols] = torch.tensor(rows, dtype=torch.long).T
+        return out.to(ids.device)
+
+    def forward(self, ids, mask, *, x=None, lora=None, training=False, caches=None, pos=None, key_mask=None,
+                embed_hook=None):
         """[B, S] ids -> hidden [B, S, H] after this stage's layers (whole-sequence;
         caches fill for decoding).  On a later pipeline stage ``x`` is the
-        previous stage's output and ``ids`` is unused."""
+        previous stage's output and ``ids`` is unused.  ``embed_hook`` places
+        image features on the placeholder embeddings; with it the positions
+        are the multimodal RoPE ones unless ``pos`` is given."""
         if x is None:
             x = F.embedding(ids, self.embed)
+            if embed_hook is not None:
+                x = embed_hook(ids, x)
+                if pos is None and getattr(embed_hook, "grids", None):
+                    pos = self.mrope_positions(ids, mask, embed_hook)
         pos = (mask.long().cumsum(-1) - 1).clamp_min(0) if pos is None else pos
         key_mask = mask if key_mask is None else key_mask
         for i, lay in enumerate(self.layers):
@@ -435,8 +495,8 @@ class Qwen35Model:
             out.append(lg.gather(-1, tg[i : i + chunk, None]).squeeze(-1) - torch.logsumexp(lg, -1))
         return torch.cat(out).view(targets.shape)
 
-    def sequence_logprobs(self, seq, mask, *, lora=None, training=False, targets=None):
-        hidden = self.forward(seq, mask, lora=lora, training=training)
+    def sequence_logprobs(self, seq, mask, *, lora=None, training=False, targets=None, embed_hook=None):
+        hidden = self.forward(seq, mask, lora=lora, training=training, embed_hook=embed_hook)
         tgt = seq[:, 1:] if targets is None else targets
         return self.token_logprobs(hidden[:, :-1], tgt)
 
@@ -483,12 +543,16 @@ class HybridRolloutEngine:
 
     @torch.no_grad()
     def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
-                 ignore_eos=False, seed=0):
+                 ignore_eos=False, seed=0, embed_hook=None):
+        """``embed_hook`` (``ImageInputs``) places image features on the prompts' placeholders;
+        decoding then continues from each prompt's largest multimodal position."""
         import time
 
         from graspo_b200.engine.rollout import EagerRolloutEngine, RolloutResult, _gen_lengths
 
         m, dev, comm = self.m, self.m.device, self.comm
+        if embed_hook is not None and comm is not None:
+            raise NotImplementedError("image inputs with pipeline stages are not supported")
         last = comm is None or m.ps.is_last_stage
         n, G = len(prompts), int(group_size)
         lens = [max(1, len(p)) for p in prompts]
@@ -503,12 +567,18 @@ class HybridRolloutEngine:
         ids_d, mask_d = ids.to(dev), mask.to(dev)
         caches = [dict() for _ in m.layers]
         lora = EagerLoRA(m.lora, requires_grad=False)      # the current policy's adapter (views of the master)
-        hidden = self._stage(ids_d, mask_d, caches=caches, lora=lora)
+        if getattr(embed_hook, "grids", None):
+            pos3 = m.mrope_positions(ids_d, mask_d, embed_hook)
+            hidden = self._stage(ids_d, mask_d, caches=caches, lora=lora, embed_hook=embed_hook, pos=pos3)
+            last_pos = pos3.amax(dim=(0, 2))
+        else:
+            hidden = self._stage(ids_d, mask_d, caches=caches, lora=lora, embed_hook=embed_hook)
+            last_pos = mask_d.long().sum(-1) - 1
         for c in caches:
             for key, val in list(c.items()):
                 c[key] = val.repeat_interleave(G, 0)
         key_mask = mask_d.repeat_interleave(G, 0)
-        pos = (mask_d.long().sum(-1) - 1).repeat_interleave(G, 0)
+        pos = last_pos.repeat_interleave(G, 0)
         logits = m.logits(hidden[:, -1]).repeat_interleave(G, 0) if last else None
         gen = torch.Generator(device=dev).manual_seed(int(seed))
         rows = n * G

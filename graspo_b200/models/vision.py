@@ -190,3 +190,19 @@ def scatter_image_features(x: torch.Tensor, ids: torch.Tensor, pad_id: int, feat
         raise ValueError(f"{n} image placeholder tokens for {feats.shape[0]} image features")
     x[sel] = feats.to(x.dtype)
     return x
+
+
+class ImageInputs:
+    """``embed_hook`` of a batch with images: places the features of every
+    image (rows in order, images in order) on the placeholder embeddings, and
+    carries each image's merged grid ``(t, h, w)`` so a decoder with
+    multimodal RoPE can give the placeholders their 3-D positions."""
+
+    def __init__(self, feats: torch.Tensor, pad_id: int, grids: list[tuple[int, int, int]]) -> None:
+        self.feats, self.pad_id, self.grids = feats, int(pad_id), list(grids)
+
+    def __call__(self, ids: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() == 2:
+            return scatter_image_features(x, ids, self.pad_id, self.feats)
+        scatter_image_features(x.view(-1, x.shape[-1]), ids, self.pad_id, self.feats)
+        return x

@@ -282,7 +282,7 @@ VIT_TINY = dict(depth=2, hidden_size=64, intermediate_size=128, num_heads=4, in_
 
 def add_vision_tower(model_dir: str | Path, vdims: dict, *, seed: int = 0, std: float = 0.02,
                      dtype: torch.dtype = torch.bfloat16) -> Path:
-    """Add a random-init vision tower (``model.visual.*``) to a synthetic Qwen3 checkpoint."""
+    """Add a random-init vision tower (``model.visual.*``) to a synthetic Qwen3 or Qwen3.5 checkpoint."""
     from safetensors.torch import save_file
 
     out = Path(model_dir)
@@ -292,7 +292,8 @@ def add_vision_tower(model_dir: str | Path, vdims: dict, *, seed: int = 0, std: 
     Hd, I = vdims["hidden_size"], vdims["intermediate_size"]
     pdim = vdims["in_channels"] * vdims["temporal_patch_size"] * vdims["patch_size"] ** 2
     merged = Hd * vdims["spatial_merge_size"] ** 2
-    out_h = config["hidden_size"]
+    text = config.get("text_config") or config
+    out_h = text["hidden_size"]
     gen = torch.Generator().manual_seed(seed)
     specs = [("patch_embed.proj.weight", (Hd, vdims["in_channels"], vdims["temporal_patch_size"], vdims["patch_size"],
                                           vdims["patch_size"]), "n"),
@@ -318,6 +319,10 @@ def add_vision_tower(model_dir: str | Path, vdims: dict, *, seed: int = 0, std: 
     index["weight_map"].update({k: "model-vision.safetensors" for k in tensors})
     (out / "model.safetensors.index.json").write_text(json.dumps(index, indent=2))
     config["vision_config"] = {**vdims, "out_hidden_size": out_h}
+    if config.get("image_token_id") is None:
+        from graspo_b200.utils.tokenizer import special_token_ids
+
+        config["image_token_id"] = special_token_ids(text["vocab_size"])["<|vision_pad|>"]
     (out / "config.json").write_text(json.dumps(config, indent=2))
     return out
 

@@ -1,7 +1,9 @@
 """Vision tower + multimodal GRASPO on CPU: patch layout, placeholder expansion,
 and an image-conditioned rollout / old log-probs / training round trip
-through the public runtime API (Qwen3 decoder with a ViT, eager backend)."""
+through the public runtime API (Qwen3 and Qwen3.5 decoders with a ViT, eager
+backend)."""
 
+import pytest
 import torch
 
 from graspo_b200.models.vision import VisionConfig, expand_image_placeholders, merged_tokens, preprocess
@@ -20,22 +22,32 @@ def test_patch_layout_and_token_counts():
     assert expand_image_placeholders([1, 9, 2, 9, 3], 9, [2, 3]) == [1, 9, 9, 2, 9, 9, 9, 3]
 
 
-def test_multimodal_grpo_round_trip(tmp_path):
+@pytest.mark.parametrize("family", ["qwen3", "qwen3_5"])
+def test_multimodal_grpo_round_trip(tmp_path, family):
+    """Image prompts through the public runtime API on both families (the
+    Qwen3.5 hybrid with multimodal RoPE positions): rollout, old log-probs
+    that the image changes, one GRPO step."""
     from graspo_b200.core.buffer import Experience
     from graspo_b200.core.data import sample_from_record
     from graspo_b200.core.schema import GraspoConfig
     from graspo_b200.engine.runtime import GraspoFlowRuntime
-    from graspo_b200.utils.synth import (TINY, VIT_TINY, add_vision_tower, synthetic_image_records,
-                                         write_qwen3_checkpoint)
+    from graspo_b200.utils.synth import (QWEN35_TINY, TINY, VIT_TINY, add_vision_tower, synthetic_image_records,
+                                         write_qwen3_checkpoint, write_qwen35_checkpoint)
 
-    dims = dict(TINY, vocab_size=2048)
-    path = add_vision_tower(write_qwen3_checkpoint(tmp_path / "vl", dims, seed=1, device="cpu"), VIT_TINY, seed=2)
+    if family == "qwen3":
+        dims = dict(TINY, vocab_size=2048)
+        base = write_qwen3_checkpoint(tmp_path / "vl", dims, seed=1, device="cpu")
+        targets = ["language.self_attn.q_proj", "language.mlp.down_proj"]
+    else:
+        dims = dict(QWEN35_TINY, vocab_size=2048, head_dim=64)
+        base = write_qwen35_checkpoint(tmp_path / "vl35", dims, seed=1, std=0.05)
+        targets = ["language.full_attn.q_proj", "language.linear_attn.out_proj", "language.mlp.down_proj"]
+    path = add_vision_tower(base, VIT_TINY, seed=2)
     cfg = GraspoConfig.from_dict({
         "train_method": "graspo",
         "model": {"model_path": str(path), "torch_dtype": "float32"},
         "data": {"train_path": "", "max_prompt_length": 600},
-        "lora": {"r": 4, "alpha": 8, "dropout": 0.0, "target_modules": ["language.self_attn.q_proj",
-                                                                         "language.mlp.down_proj"]},
+        "lora": {"r": 4, "alpha": 8, "dropout": 0.0, "target_modules": targets},
         "training": {"output_dir": str(tmp_path / "run"), "run_name": "t", "rollout_group_size": 2,
                      "optimize_prompt_batch_size": 2, "learning_rate": 1e-3, "max_new_tokens": 4},
         "graspoflow": {"tp_size": 1, "pp_size": 1, "raw_log_enabled": False, "readable_log_enabled": False},
