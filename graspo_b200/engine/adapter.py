@@ -44,6 +44,7 @@ from graspo_b200.models.loader import SafetensorIndex
 from graspo_b200.models.qwen3 import EagerLoRA, Qwen3Model, eager_stage_forward, eager_token_logprobs
 from graspo_b200.parallel import state as pstate
 from graspo_b200.parallel.placement import build_placement_plan, placement_summary
+from graspo_b200.utils.timing import NULL_CLOCK
 
 log = logging.getLogger("graspo.adapter")
 
@@ -80,6 +81,8 @@ class Qwen3Adapter:
     model_class = Qwen3Model
     # pipeline stages through the autograd forward (families without the fused path)
     autograd_pipeline = False
+    # phase clock of the running train_batch call (no timing outside one)
+    _clock = NULL_CLOCK
 
     def __new__(cls, config: Any = None, *args: Any, **kwargs: Any):
         # the default adapter serves both families: a qwen3_5 checkpoint gets the hybrid adapter
@@ -545,7 +548,8 @@ class Qwen3Adapter:
                 return self.loss_fn(logp_c, old[sl], adv[sl], act[sl]) * ((sl.stop - sl.start) / B)
 
             return pp_train_autograd(self.model, self._comm, seq, mask, seq[:, 1:], chunk_loss,
-                                     chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule)
+                                     chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
+                                     clock=self._clock)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
             from graspo_b200.ops._ext import ext
@@ -563,23 +567,29 @@ class Qwen3Adapter:
                 return loss * (rows / B), dlogp
 
             return pp_train(self._fused, self._comm, seq, mask, seq[:, 1:], loss_fn, seed=seed,
-                            chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule)
+                            chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
+                            clock=self._clock)
+        clock = self._clock
         if self.fused:
             from graspo_b200.ops._ext import ext
 
-            logp, ctx = self._logprobs(seq, mask, train=True, seed=seed, embed_hook=embed_hook)
-            loss = torch.zeros(1, device=seq.device, dtype=torch.float32)
-            dlogp = torch.empty_like(logp)
-            ext().grpo_loss(logp, old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous(), clip_eps,
-                            1.0, loss, dlogp, None)
-            self._fused_backward_from_logp_grad(ctx, dlogp, seed)
+            with clock.time("micro_batch_forward_sec"):
+                logp, ctx = self._logprobs(seq, mask, train=True, seed=seed, embed_hook=embed_hook)
+            with clock.time("backward_sec"):
+                loss = torch.zeros(1, device=seq.device, dtype=torch.float32)
+                dlogp = torch.empty_like(logp)
+                ext().grpo_loss(logp, old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous(), clip_eps,
+                                1.0, loss, dlogp, None)
+                self._fused_backward_from_logp_grad(ctx, dlogp, seed)
             return loss
-        logp, lora = self._logprobs(seq, mask, train=True, embed_hook=embed_hook)
-        self.loss_fn.policy_ratio_clip_eps = clip_eps
-        loss = self.loss_fn(logp, old, adv, act)
-        if torch.isfinite(loss):
-            loss.backward()
-            lora.accumulate_grads()
+        with clock.time("micro_batch_forward_sec"):
+            logp, lora = self._logprobs(seq, mask, train=True, embed_hook=embed_hook)
+            self.loss_fn.policy_ratio_clip_eps = clip_eps
+            loss = self.loss_fn(logp, old, adv, act)
+        with clock.time("backward_sec"):
+            if torch.isfinite(loss):
+                loss.backward()
+                lora.accumulate_grads()
         return loss.detach().reshape(1)
 
     def _shared_training_indices(self, count: int, optimize_round: int) -> list[int]:
@@ -596,10 +606,15 @@ class Qwen3Adapter:
         if self.config.graspoflow.empty_cache_before_train and self.device.type == "cuda":
             torch.cuda.empty_cache()
         t0 = time.monotonic()
+        from graspo_b200.utils.timing import PhaseClock
+
+        self._clock = clock = PhaseClock(sync=self.config.graspoflow.synchronize_cuda_timing)
         lora_before = self.model.lora.parameter_norm()
         losses, norms = [], []
+        round_secs = []
         steps = 0
         for rnd in range(int(optimize_iterations_per_step)):
+            t_round = clock.now() if clock.sync else time.monotonic()
             idx = self._shared_training_indices(len(experiences), rnd)
             for start in range(0, len(idx) - bs + 1, bs):
                 batch = [experiences[i] for i in idx[start : start + bs]]
@@ -609,12 +624,15 @@ class Qwen3Adapter:
                 media_rows = [((e.metadata or {}).get("_media") or []) for e in batch]
                 hook = self._image_hook(media_rows) if any(media_rows) else None
                 loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed, embed_hook=hook)
-                self._tp_sync_replicated_grads()
-                self._dp_average_grads()
-                norm = self.optimizer.step(max_grad_norm, loss)
+                with clock.time("grad_sync_sec"):
+                    self._tp_sync_replicated_grads()
+                    self._dp_average_grads()
+                with clock.time("optimizer_step_sec"):
+                    norm = self.optimizer.step(max_grad_norm, loss)
                 losses.append(loss)
                 norms.append(norm)
                 steps += 1
+            round_secs.append(round((clock.now() if clock.sync else time.monotonic()) - t_round, 6))
         self._train_batch_call_index += 1
         if os.environ.get("GRASPO_CHECK_REPLICAS", "0") == "1":
             self.check_replicas()
@@ -638,7 +656,11 @@ class Qwen3Adapter:
             "micro_batch_count": steps,
             "current_lr": self.optimizer.lr,
             "activation_checkpointing_enabled": bool(self.model.gradient_checkpointing),
+            "optimize_round_sec": round_secs,
+            **clock.summary(),
         }
+        if clock.calls.get("pipeline_forward_calls"):
+            metrics["pipeline_forward_calls"] = int(clock.calls["pipeline_forward_calls"])
         self._rank_event("train_batch_after", {"metrics": metrics})
         return self._aggregate_rank_metrics(metrics)
 

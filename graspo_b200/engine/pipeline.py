@@ -27,6 +27,7 @@ from graspo_b200.models.fused import AttnMeta, FusedQwen3
 from graspo_b200.ops._ext import ext
 from graspo_b200.parallel.p2p import StageComm
 from graspo_b200.parallel.schedule import PipelineAction, get_scheduler
+from graspo_b200.utils.timing import NULL_CLOCK, PhaseClock, schedule_phases
 
 # the fused layers produce bf16 activations (the GEMMs store bf16)
 ACT_DTYPE = torch.bfloat16
@@ -72,12 +73,15 @@ LossFn = Callable[[torch.Tensor, slice], tuple[torch.Tensor, torch.Tensor]]
 
 
 def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
-             loss_fn: LossFn, *, seed: int, chunk_rows: int, schedule: str = "one_f_one_b") -> torch.Tensor:
+             loss_fn: LossFn, *, seed: int, chunk_rows: int, schedule: str = "one_f_one_b",
+             clock: PhaseClock = NULL_CLOCK) -> torch.Tensor:
     """Forward + backward of one optimizer step into the LoRA gradient buffer.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
     returns (loss contribution [1], d loss / d logp_chunk); contributions must
     already carry the chunk's weight.  Returns the summed loss on every stage.
+    ``clock`` collects the stage timers (recv / send / compute / head / loss /
+    backward, and the fill / steady / drain phases of the schedule).
     """
     m, ps = f.m, comm.ps
     C = ext()
@@ -85,42 +89,57 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     H = m.cfg.hidden_size
     full = _full_targets(targets)
     chunks = _chunks(B, chunk_rows)
-    plan = get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank).plan(len(chunks))
+    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
-    for step in plan:
+    for phase, step in plan:
+        t_step = clock.now()
         c = step.microbatch_idx
         sl = chunks[c]
         rows = sl.stop - sl.start
         if step.action == PipelineAction.FORWARD:
             meta = AttnMeta.from_mask(mask[sl])
-            x = f.embed(seq[sl]) if ps.is_first_stage else comm.recv_prev((rows * S, H), ACT_DTYPE)
-            xL, inputs = f.stage_forward(x, meta, train=True, seed=seed, keep_inputs=True)
+            if ps.is_first_stage:
+                x = f.embed(seq[sl])
+            else:
+                with clock.time("pipeline_recv_sec"):
+                    x = comm.recv_prev((rows * S, H), ACT_DTYPE)
+            with clock.time("pipeline_stage_compute_sec"):
+                xL, inputs = f.stage_forward(x, meta, train=True, seed=seed, keep_inputs=True)
+            clock.calls["pipeline_forward_calls"] += 1
             if ps.is_last_stage:
-                hn, rstd = f.final_norm(xL)
-                fc = full[sl].reshape(-1).contiguous()
-                lp, lse = f.token_logprobs(hn, fc)
-                loss_c, dlogp = loss_fn(lp.view(rows, S)[:, :-1], sl)
-                total += loss_c.reshape(1)
+                with clock.time("pipeline_lm_head_sec"):
+                    hn, rstd = f.final_norm(xL)
+                    fc = full[sl].reshape(-1).contiguous()
+                    lp, lse = f.token_logprobs(hn, fc)
+                with clock.time("pipeline_loss_sec"):
+                    loss_c, dlogp = loss_fn(lp.view(rows, S)[:, :-1], sl)
+                    total += loss_c.reshape(1)
                 saved[c] = (meta, inputs, xL, hn, rstd, fc, lse, dlogp)
             else:
-                comm.send_next(xL)
+                with clock.time("pipeline_send_sec"):
+                    comm.send_next(xL)
                 saved[c] = (meta, inputs)
         else:
             if ps.is_last_stage:
                 meta, inputs, xL, hn, rstd, fc, lse, dlogp = saved.pop(c)
-                g = torch.zeros(rows, S, device=seq.device, dtype=torch.float32)
-                g[:, :-1] = dlogp
-                dhn = f.token_logprobs_backward(hn, fc, lse, g.view(-1))
-                dx = torch.empty_like(xL)
-                C.rmsnorm_bwd(dhn, xL, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
+                with clock.time("pipeline_backward_autograd_sec"):
+                    g = torch.zeros(rows, S, device=seq.device, dtype=torch.float32)
+                    g[:, :-1] = dlogp
+                    dhn = f.token_logprobs_backward(hn, fc, lse, g.view(-1))
+                    dx = torch.empty_like(xL)
+                    C.rmsnorm_bwd(dhn, xL, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
                 del dhn, hn, xL
             else:
                 meta, inputs = saved.pop(c)
-                dx = comm.recv_next((rows * S, H), ACT_DTYPE)
-            dx_in = f.stage_backward(inputs, dx, meta, train=True, seed=seed)
+                with clock.time("pipeline_grad_recv_sec"):
+                    dx = comm.recv_next((rows * S, H), ACT_DTYPE)
+            with clock.time("pipeline_backward_autograd_sec"):
+                dx_in = f.stage_backward(inputs, dx, meta, train=True, seed=seed)
             if not ps.is_first_stage:
-                comm.send_prev(dx_in)
+                with clock.time("pipeline_grad_send_sec"):
+                    comm.send_prev(dx_in)
+        clock.add(f"{phase}_sec", clock.now() - t_step)
     comm.flush()
     return comm.broadcast_from_last(total)
 
@@ -162,7 +181,7 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
 
 def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
                       loss_fn: Callable[[torch.Tensor, slice], torch.Tensor], *, chunk_rows: int,
-                      schedule: str = "one_f_one_b") -> torch.Tensor:
+                      schedule: str = "one_f_one_b", clock: PhaseClock = NULL_CLOCK) -> torch.Tensor:
     """Forward + backward of one optimizer step into ``model.lora.grads``.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
@@ -174,34 +193,48 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
     B, S = seq.shape
     H = model.cfg.hidden_size
     chunks = _chunks(B, chunk_rows)
-    plan = get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank).plan(len(chunks))
+    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
     lora = EagerLoRA(model.lora, requires_grad=True)
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
-    for step in plan:
+    for phase, step in plan:
+        t_step = clock.now()
         c = step.microbatch_idx
         sl = chunks[c]
         rows = sl.stop - sl.start
         if step.action == PipelineAction.FORWARD:
             x = None
             if not ps.is_first_stage:
-                x = comm.recv_prev((rows, S, H), model.dtype).requires_grad_(True)
+                with clock.time("pipeline_recv_sec"):
+                    x = comm.recv_prev((rows, S, H), model.dtype).requires_grad_(True)
             with torch.enable_grad():
-                xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, training=True)
+                with clock.time("pipeline_stage_compute_sec"):
+                    xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, training=True)
+                clock.calls["pipeline_forward_calls"] += 1
                 if ps.is_last_stage:
-                    out = loss_fn(model.token_logprobs(xL[:, :-1], targets[sl]).float(), sl).reshape(1)
-                    total += out.detach()
+                    with clock.time("pipeline_lm_head_sec"):
+                        lp = model.token_logprobs(xL[:, :-1], targets[sl]).float()
+                    with clock.time("pipeline_loss_sec"):
+                        out = loss_fn(lp, sl).reshape(1)
+                        total += out.detach()
                 else:
-                    comm.send_next(xL.detach())
+                    with clock.time("pipeline_send_sec"):
+                        comm.send_next(xL.detach())
                     out = xL
             saved[c] = (x, out)
         else:
             x, out = saved.pop(c)
-            grad = None if ps.is_last_stage else comm.recv_next((rows, S, H), model.dtype)
-            if out.requires_grad:
-                out.backward(grad)
+            grad = None
+            if not ps.is_last_stage:
+                with clock.time("pipeline_grad_recv_sec"):
+                    grad = comm.recv_next((rows, S, H), model.dtype)
+            with clock.time("pipeline_backward_autograd_sec"):
+                if out.requires_grad:
+                    out.backward(grad)
             if not ps.is_first_stage:
-                comm.send_prev(x.grad if x.grad is not None else torch.zeros_like(x))
+                with clock.time("pipeline_grad_send_sec"):
+                    comm.send_prev(x.grad if x.grad is not None else torch.zeros_like(x))
+        clock.add(f"{phase}_sec", clock.now() - t_step)
     comm.flush()
     lora.accumulate_grads()
     return comm.broadcast_from_last(total)

@@ -29,6 +29,17 @@ def test_gpipe_and_1f1b_plans():
         get_scheduler("nope", pp_size=2, pp_rank=0)
 
 
+def test_schedule_phases_keep_the_plan_order():
+    from graspo_b200.utils.timing import schedule_phases
+
+    for name in ("simple", "one_f_one_b"):
+        for rank in range(4):
+            sch = get_scheduler(name, pp_size=4, pp_rank=rank)
+            pairs = schedule_phases(sch, 6)
+            assert [step for _, step in pairs] == sch.plan(6)
+            assert {p for p, _ in pairs} <= {"fill", "steady", "drain"}
+
+
 def test_minimax_placement():
     ranges = minimax_contiguous_ranges([1.0] * 8, [0.0, 0.0])
     assert ranges == [(0, 4), (4, 8)]

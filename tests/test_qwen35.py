@@ -116,4 +116,7 @@ def test_hybrid_adapter_grpo_round_trip(tmp_path):
     before = api.adapter.model.lora.params.clone()
     metrics = api.train_batch(exps, policy_ratio_clip_eps=0.2, optimize_iterations_per_step=1, max_grad_norm=1.0)
     assert metrics["optimizer_steps"] == 2 and metrics["loss_mean"] is not None
+    for key in ("micro_batch_forward_sec", "backward_sec", "optimizer_step_sec"):
+        assert metrics[key] > 0, key
+    assert len(metrics["optimize_round_sec"]) == 1
     assert not torch.equal(before, api.adapter.model.lora.params)

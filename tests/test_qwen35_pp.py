@@ -87,10 +87,22 @@ def _worker(rank, world, path, ref_file, tp):
     valid = mask[:, :-1] & mask[:, 1:]
     lp = pp_logprobs_autograd(m, comm, ids, mask, ids[:, 1:], chunk_rows=2)
     assert (lp - ref["lp"]).abs()[valid].max().item() < 1e-4
+    from graspo_b200.utils.timing import PhaseClock
+
     for schedule in ("one_f_one_b", "simple"):
         m.lora.grads.zero_()
+        clock = PhaseClock()
         loss = pp_train_autograd(m, comm, ids, mask, ids[:, 1:], lambda lp_c, sl: (lp_c * w[sl]).sum(),
-                                 chunk_rows=1, schedule=schedule)
+                                 chunk_rows=1, schedule=schedule, clock=clock)
+        # stage timers in the reference's key names
+        want = {"pipeline_stage_compute_sec", "pipeline_backward_autograd_sec",
+                "pipeline_send_sec" if first else "pipeline_recv_sec"}
+        assert want <= set(clock.sec), (schedule, sorted(clock.sec))
+        # 1F1B: the first stage warms up (fill), the last runs steady only; GPipe: fill then drain
+        phases = {"fill_sec", "drain_sec"} if schedule == "simple" else ({"fill_sec", "steady_sec", "drain_sec"}
+                                                                         if first else {"steady_sec"})
+        assert {k for k in clock.sec if k in ("fill_sec", "steady_sec", "drain_sec")} == phases, sorted(clock.sec)
+        assert clock.calls["pipeline_forward_calls"] == 3
         assert abs(loss.item() - (ref["lp"] * w).sum().item()) < 1e-3
         if tp > 1:
             torch.distributed.all_reduce(m.lora.grads[: m.lora.replicated_numel], group=ps.tp_group)
