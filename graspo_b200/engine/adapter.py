@@ -528,6 +528,8 @@ class Qwen3Adapter:
         rep = self.model.lora.replicated_numel
         if ps.tp_size > 1 and ps.distributed and rep:
             dist.all_reduce(self.model.lora.grads[:rep], group=ps.tp_group)
+        if ps.tp_size > 1 and ps.distributed and hasattr(self.model, "sync_partial_grads"):
+            self.model.sync_partial_grads()
 
     def _pp_chunk_rows(self, seq) -> int:
         """Rows per pipeline micro-batch (graspoflow.pp_micro_batch_size, bounded by a token budget)."""

@@ -140,7 +140,9 @@ class Qwen35Model:
 
     Tensor parallelism splits heads (reference: models/common/layers.py:145-633):
     full attention keeps ``nq/tp`` query heads (their query+gate rows of
-    ``q_proj``) and ``nkv/tp`` key/value heads, DeltaNet keeps ``lk/tp`` key
+    ``q_proj``) and ``nkv/tp`` key/value heads (when TP is a multiple of
+    ``nkv`` above it: the one head its query heads read, copied on ``tp/nkv``
+    ranks, whose LoRA B gradients ``sync_partial_grads`` sums), DeltaNet keeps ``lk/tp`` key
     heads and ``lv/tp`` value heads (rows of ``in_proj_qkv`` in each of its
     q / k / v blocks, the matching conv channels, rows of ``in_proj_z/b/a``,
     ``dt_bias``, ``A_log``), the MLP keeps ``I/tp`` intermediate rows;
@@ -185,13 +187,16 @@ class Qwen35Model:
         self.key_dim, self.value_dim = self.lk_heads * self.dk, self.lv_heads * self.dv
         tp, tr = ps.tp_size, ps.tp_rank
         self.tp_group = ps.tp_group if tp > 1 else None
-        for n, what in ((self.nq, "attention heads"), (self.nkv, "key/value heads"),
+        # key/value heads: split when TP divides them, else each rank keeps the one head its query
+        # heads read and the tp/nkv ranks of a group hold copies (reference: layers.py:182-188)
+        self.kv_replicas = tp // self.nkv if (tp > self.nkv and tp % self.nkv == 0) else 1
+        for n, what in ((self.nq, "attention heads"), (self.nkv * self.kv_replicas, "key/value heads (or TP multiple)"),
                         (self.lk_heads, "linear-attention key heads"), (self.lv_heads, "linear-attention value heads"),
                         (cfg.intermediate_size, "intermediate size")):
             if n % tp:
                 raise ValueError(f"qwen3_5_text: {what} ({n}) must be divisible by tp_size={tp}")
         # local head counts and widths
-        self.nq_l, self.nkv_l = self.nq // tp, self.nkv // tp
+        self.nq_l, self.nkv_l = self.nq // tp, self.nkv * self.kv_replicas // tp
         self.lk_l, self.lv_l = self.lk_heads // tp, self.lv_heads // tp
         self.kd_l, self.vd_l = self.lk_l * self.dk, self.lv_l * self.dv
         self.inter_l = cfg.intermediate_size // tp
@@ -209,7 +214,8 @@ class Qwen35Model:
             return loader.get_cols(name, a, b).to(device=dev, dtype=dt)
 
         qr = (tr * self.nq_l * 2 * D, (tr + 1) * self.nq_l * 2 * D)          # query+gate rows of q_proj
-        kvr = (tr * self.nkv_l * D, (tr + 1) * self.nkv_l * D)
+        kv0 = tr // self.kv_replicas * self.nkv_l
+        kvr = (kv0 * D, (kv0 + self.nkv_l) * D)
         oc = (tr * self.nq_l * D, (tr + 1) * self.nq_l * D)
         lqr = (tr * self.kd_l, (tr + 1) * self.kd_l)                          # q block of in_proj_qkv
         lkr = (kd + lqr[0], kd + lqr[1])                                      # k block
@@ -311,6 +317,25 @@ class Qwen35Model:
         state = batch_size * lin * (self.lv_l * self.dk * self.dv * 4
                                     + (2 * self.kd_l + self.vd_l) * self.conv_k * self.dtype.itemsize)
         return kv + state
+
+    def sync_partial_grads(self) -> None:
+        """Sum the LoRA B gradients of key/value heads held by several TP ranks over those ranks.
+
+        With replicated key/value heads each copy only sees the gradient of
+        its own rank's query heads; the B rows of one head must get the sum.
+        The rows are placed in a whole-module buffer, summed over the TP group
+        (other groups contribute zeros) and read back."""
+        if self.kv_replicas == 1 or self.tp_group is None:
+            return
+        mods = [m for m in self.lora.modules if m.kind in ("fk", "fv")]
+        if not mods:
+            return
+        full = torch.zeros(len(mods), mods[0].out_full, self.lora.r, device=self.device, dtype=torch.float32)
+        for i, m in enumerate(mods):
+            full[i, m.row_start : m.row_stop] = m.b_grad
+        dist.all_reduce(full, group=self.tp_group)
+        for i, m in enumerate(mods):
+            m.b_grad.copy_(full[i, m.row_start : m.row_stop])
 
     def _f(self, x):
         """Identity forward, all-reduce backward (input of the column-parallel projections)."""

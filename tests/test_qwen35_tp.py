@@ -13,6 +13,7 @@ pairs for the DeltaNet q/k/v row blocks).
 import os
 import zlib
 
+import pytest
 import torch
 
 from tests.dist_util import run_world
@@ -74,12 +75,13 @@ def _local(mod, fac, full):
 
 
 def _worker(rank, world, path, ref_file, out_dir):
+    tp = world
     from graspo_b200.models.lora_io import export_peft_adapter
     from graspo_b200.models.qwen35 import HybridRolloutEngine
     from graspo_b200.parallel import state as pstate
     from graspo_b200.train.checkpoint import rank_file_name
 
-    ps = pstate.initialize(2, 1, 0, timeout_sec=120, device="cpu")
+    ps = pstate.initialize(tp, 1, 0, timeout_sec=120, device="cpu")
     m = _model(path, ps)
     ref = torch.load(ref_file)
     ids, mask = _batch()
@@ -88,6 +90,7 @@ def _worker(rank, world, path, ref_file, out_dir):
     assert (lp - ref["lp"]).abs()[valid].max().item() < 1e-4
     rep = m.lora.replicated_numel
     torch.distributed.all_reduce(m.lora.grads[:rep], group=ps.tp_group)
+    m.sync_partial_grads()        # key/value heads held by several ranks (TP above the KV head count)
     for mod in m.lora.modules:
         for fac, g in (("a", mod.a_grad), ("b", mod.b_grad)):
             want = _local(mod, fac, ref["grads"][mod.module_name][fac])
@@ -107,7 +110,10 @@ def _worker(rank, world, path, ref_file, out_dir):
     pstate.destroy()
 
 
-def test_qwen35_tp2_matches_tp1(tmp_path):
+@pytest.mark.parametrize("tp", [2, 4])
+def test_qwen35_tp_matches_tp1(tmp_path, tp):
+    """TP = 2 splits every head kind; TP = 4 exceeds the 2 key/value heads, so
+    pairs of ranks hold copies of one head and sum their B gradients."""
     from graspo_b200.models.lora_io import load_peft_adapter
     from graspo_b200.models.qwen35 import HybridRolloutEngine
     from graspo_b200.parallel import state as pstate
@@ -115,8 +121,10 @@ def test_qwen35_tp2_matches_tp1(tmp_path):
     from graspo_b200.utils.synth import QWEN35_TINY, write_qwen35_checkpoint
 
     os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
-    path = write_qwen35_checkpoint(tmp_path / "q35", QWEN35_TINY, seed=1, std=0.05, with_tokenizer=False)
+    dims = dict(QWEN35_TINY, linear_num_key_heads=4, linear_num_value_heads=4)   # DeltaNet heads divide by 4
+    path = write_qwen35_checkpoint(tmp_path / "q35", dims, seed=1, std=0.05, with_tokenizer=False)
     m = _model(path, ParallelState())
+    assert m.nkv < 4
     ids, mask = _batch()
     lp = _grads(m, ids, mask)
     grads = {mod.module_name: {"a": _to_full(mod, "a", mod.a_grad), "b": _to_full(mod, "b", mod.b_grad)}
@@ -129,7 +137,7 @@ def test_qwen35_tp2_matches_tp1(tmp_path):
     pstate.destroy()
     ckpt = tmp_path / "ckpt"
     ckpt.mkdir()
-    run_world(2, _worker, path, ref_file, str(ckpt), timeout=600)
+    run_world(tp, _worker, path, ref_file, str(ckpt), timeout=600)
     # the TP = 2 shards exported as one PEFT adapter give back the TP = 1 LoRA state
     fresh = _model(path, ParallelState())
     with torch.no_grad():
