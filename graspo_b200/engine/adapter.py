@@ -674,6 +674,9 @@ class Qwen3Adapter:
         fbs = int(self.config.graspoflow.forward_batch_size)
         losses, steps = [], 0
         t0 = time.monotonic()
+        from graspo_b200.utils.timing import PhaseClock
+
+        self._clock = clock = PhaseClock(sync=self.config.graspoflow.synchronize_cuda_timing)
         for _ in range(int(optimize_iterations_per_step)):
             for start in range(0, len(sft_batches), fbs):
                 chunk = sft_batches[start : start + fbs]
@@ -687,9 +690,11 @@ class Qwen3Adapter:
                 ids, labels, mask = ids.to(self.device), labels.to(self.device), mask.to(self.device)
                 self.optimizer.zero_grad()
                 loss = self._backward_sft(ids, mask, labels, steps)
-                self._tp_sync_replicated_grads()
-                self._dp_average_grads()
-                self.optimizer.step(max_grad_norm, loss)
+                with clock.time("grad_sync_sec"):
+                    self._tp_sync_replicated_grads()
+                    self._dp_average_grads()
+                with clock.time("optimizer_step_sec"):
+                    self.optimizer.step(max_grad_norm, loss)
                 losses.append(loss)
                 steps += 1
         vals = [float(x) for x in torch.cat(losses).cpu()] if losses else []
@@ -697,6 +702,7 @@ class Qwen3Adapter:
             "optimized": steps > 0, "optimizer_steps": steps,
             "loss_mean": sum(vals) / len(vals) if vals else None,
             "train_batch_total_sec": time.monotonic() - t0, "current_lr": self.optimizer.lr,
+            **clock.summary(),
         })
 
     def _backward_sft(self, ids, mask, labels, step: int):
@@ -713,7 +719,8 @@ class Qwen3Adapter:
                 return -(logp_c * valid[sl]).sum() / denom
 
             return pp_train_autograd(self.model, self._comm, ids, mask, safe, chunk_loss,
-                                     chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule)
+                                     chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
+                                     clock=self._clock)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
 
@@ -722,16 +729,22 @@ class Qwen3Adapter:
                 return -(logp_c * v).sum().reshape(1) / denom, -(v / denom)
 
             return pp_train(self._fused, self._comm, ids, mask, safe, loss_fn, seed=step,
-                            chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule)
+                            chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
+                            clock=self._clock)
+        clock = self._clock
         if self.fused:
-            logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe)
-            loss = -(logp * valid).sum() / denom
-            self._fused_backward_from_logp_grad(ctx, -(valid.float() / denom), step)
+            with clock.time("micro_batch_forward_sec"):
+                logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe)
+                loss = -(logp * valid).sum() / denom
+            with clock.time("backward_sec"):
+                self._fused_backward_from_logp_grad(ctx, -(valid.float() / denom), step)
             return loss.detach().reshape(1)
-        logp, lora = self._logprobs(ids, mask, train=True, targets=safe)
-        loss = -(logp * valid).sum() / denom
-        loss.backward()
-        lora.accumulate_grads()
+        with clock.time("micro_batch_forward_sec"):
+            logp, lora = self._logprobs(ids, mask, train=True, targets=safe)
+            loss = -(logp * valid).sum() / denom
+        with clock.time("backward_sec"):
+            loss.backward()
+            lora.accumulate_grads()
         return loss.detach().reshape(1)
 
     def _rank_event(self, phase: str, extra: dict[str, Any] | None = None) -> None:
