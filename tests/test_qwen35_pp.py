@@ -130,8 +130,10 @@ def test_qwen35_pipeline_matches_single_process(tmp_path, tp):
 
 
 @pytest.mark.slow
-def test_qwen35_tp2_pp2_grpo_launch(tmp_path):
-    """`graspo launch` at TP = 2 x PP = 2 (4 CPU ranks, 1F1B): one GRPO step and a final checkpoint."""
+@pytest.mark.parametrize("method", ["graspo", "sft"])
+def test_qwen35_tp2_pp2_launch(tmp_path, method):
+    """`graspo launch` at TP = 2 x PP = 2 (4 CPU ranks, 1F1B): one GRPO step (or one
+    supervised step) and a final checkpoint."""
     import subprocess
     import sys
     from pathlib import Path
@@ -153,6 +155,9 @@ def test_qwen35_tp2_pp2_grpo_launch(tmp_path):
     cfg["graspoflow"].update(tp_size=2, pp_size=2, pg_timeout_sec=60.0, pp_schedule="one_f_one_b",
                              pp_micro_batch_size=1)
     cfg["launch"].update(nproc_per_node=4, master_port=29000 + (os.getpid() * 3) % 2000)
+    cfg["train_method"] = method
+    if method == "sft":
+        cfg.pop("reward", None)
     path = tmp_path / "q35_tp2_pp2.yaml"
     path.write_text(yaml.safe_dump(cfg))
     env = {k: v for k, v in os.environ.items() if not k.startswith("GRASPO_FAULT")}
