@@ -98,3 +98,40 @@ def test_qwen35_image_decoding_continues_the_positions(tmp_path):
     P = res.prompt_ids.shape[1]
     greedy = logits[:, P - 1 : P - 1 + 5].argmax(-1)
     assert torch.equal(greedy, res.tokens), (greedy, res.tokens)
+
+
+def _tp2_image_worker(rank, world, tmp, ref_file):
+    from graspo_b200.models.config import load_decoder_config
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen35 import Qwen35Model
+    from graspo_b200.models.vision import ImageInputs
+    from graspo_b200.parallel import state as pstate
+
+    ps = pstate.initialize(2, 1, 0, timeout_sec=120, device="cpu")
+    ref = torch.load(ref_file)
+    path = ref["path"]
+    hook = ImageInputs(ref["feats"], int(ref["pad_id"]), [tuple(g) for g in ref["grids"].tolist()])
+    m = Qwen35Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, dtype=torch.float32)
+    assert m.vision is not None and m.nq_l * 2 == m.nq
+    with torch.no_grad():
+        got = m.logits(m.forward(ref["ids"], ref["mask"], embed_hook=hook))
+    mask = ref["mask"]
+    assert (got - ref["logits"]).abs()[mask].max().item() < 1e-4
+    pstate.destroy()
+
+
+def test_qwen35_image_prompt_tp2_matches_tp1(tmp_path):
+    """Heads split over two CPU ranks, vision tower and multimodal positions
+    replicated on each: the image-prompt logits of TP = 1."""
+    import os
+
+    from tests.dist_util import run_world
+
+    os.environ.setdefault("GLOO_SOCKET_IFNAME", "lo")
+    path, m, ids, mask, pre, hook, pad_id = _setup(tmp_path)
+    with torch.no_grad():
+        logits = m.logits(m.forward(ids, mask, embed_hook=hook))
+    ref_file = tmp_path / "ref.pt"
+    torch.save({"path": str(path), "ids": ids, "mask": mask, "feats": hook.feats, "pad_id": pad_id,
+                "grids": torch.tensor(hook.grids), "logits": logits}, ref_file)
+    run_world(2, _tp2_image_worker, str(tmp_path), str(ref_file), timeout=600)
