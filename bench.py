@@ -44,6 +44,10 @@ MAX_NEW = 2048
 GROUP = 8
 PROMPTS_PER_REPLICA_PER_TP = 8
 BASELINE_VALUE = None  # the reference publishes no throughput number
+MIN_WARMUP = 3
+# wall-clock budget of one run (set-up + warm-up + timed steps); see StepBudget
+TIME_BUDGET_S = 760.0
+_T_IMPORT = time.time()
 
 
 def layout(n: int) -> tuple[int, int]:
@@ -139,6 +143,53 @@ class PhaseTimer:
         return (b - a) * 1e3
 
 
+class StepBudget:
+    """Fits the warm-up and timed steps into a wall-clock budget for the whole run.
+
+    The budget counts from the process start (model set-up included).  Every
+    rank takes the slowest rank's step time (a MAX all-reduce), so all ranks
+    agree on the number of steps.  At least ``MIN_WARMUP`` warm-up steps and
+    one timed step always run; steps are never shortened, only counted.
+    """
+
+    def __init__(self, budget_s: float, cuda: bool) -> None:
+        self.budget_s = float(budget_s)
+        self.cuda = cuda
+        self.last_step_s = 0.0
+
+    @staticmethod
+    def elapsed() -> float:
+        try:
+            import psutil
+
+            return time.time() - psutil.Process().create_time()
+        except Exception:  # noqa: BLE001 - psutil missing: count from import
+            return time.time() - _T_IMPORT
+
+    def _agree(self, values: list[float]) -> list[float]:
+        import torch.distributed as dist
+
+        if not (dist.is_available() and dist.is_initialized()):
+            return values
+        t = torch.tensor(values, dtype=torch.float64, device="cuda" if self.cuda else "cpu")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(v) for v in t.tolist()]
+
+    def step_done(self, seconds: float) -> None:
+        self.last_step_s, self._elapsed = self._agree([seconds, self.elapsed()])
+
+    def room_for(self, n_steps: int) -> bool:
+        if self.budget_s <= 0:
+            return True
+        return self._elapsed + n_steps * self.last_step_s <= self.budget_s
+
+    def timed_steps(self, requested: int) -> int:
+        if self.budget_s <= 0 or self.last_step_s <= 0:
+            return requested
+        fit = int((self.budget_s - self._elapsed) // self.last_step_s)
+        return max(1, min(requested, fit))
+
+
 def grpo_step(api, samples, reward, *, group: int, max_new: int, prompt_len: int, iters: int, timer: PhaseTimer,
               reward_cls_adv, experience_cls, counters: dict) -> int:
     """One GRASPO step through ``api`` (this framework's or the reference's runtime)."""
@@ -204,7 +255,7 @@ def run(args) -> dict:
     model_path = ensure_checkpoint(args.model, local_rank)
     per_replica = PROMPTS_PER_REPLICA_PER_TP * tp if args.prompts is None else args.prompts
     n_total = per_replica * (dp if args.impl == "ours" else 1)
-    all_records = records(n_total * (args.warmup + args.steps))
+    all_records = records(n_total * (max(args.warmup, MIN_WARMUP) + args.steps))
     out_dir = CKPT_ROOT / f"run_{args.impl}_{world}"
     # the runtimes append per-rank JSONL under <output_dir>/logs (normally created
     # by the trainer's logging setup, which the harness does not run)
@@ -260,12 +311,24 @@ def run(args) -> dict:
     counters = {"h2d": 0, "d2h": 0}
     kw = dict(group=args.group, max_new=args.max_new, prompt_len=args.prompt_len, iters=args.iters,
               reward_cls_adv=adv_fn, experience_cls=Experience)
-    for w in range(args.warmup):
+    budget = StepBudget(args.time_budget, cuda)
+    warm_done = 0
+    while warm_done < args.warmup:
         wt = PhaseTimer(cuda)
-        grpo_step(api, step_samples(w), reward, timer=wt, counters={"h2d": 0, "d2h": 0}, **kw)
+        t0 = time.monotonic()
+        grpo_step(api, step_samples(warm_done), reward, timer=wt, counters={"h2d": 0, "d2h": 0}, **kw)
+        warm_done += 1
         if rank == 0:
             phases = {k: round(v / 1e3 if not k.endswith("_s") else v, 2) for k, v in wt.phases.items()}
-            print(f"[bench] warm-up step {w + 1}/{args.warmup}: {phases}", file=sys.stderr, flush=True)
+            print(f"[bench] warm-up step {warm_done}/{args.warmup}: {phases}", file=sys.stderr, flush=True)
+        budget.step_done(time.monotonic() - t0)
+        if warm_done >= MIN_WARMUP and warm_done < args.warmup and not budget.room_for(2):
+            # one more warm-up and one timed step would not fit: stop warming up
+            break
+    steps = budget.timed_steps(args.steps)
+    if rank == 0 and (steps != args.steps or warm_done != args.warmup):
+        print(f"[bench] time budget {args.time_budget:.0f} s: {warm_done} warm-up and {steps} timed steps "
+              f"(requested {args.warmup} and {args.steps})", file=sys.stderr, flush=True)
 
     from graspo_b200.bench.clocks import ClockSampler
 
@@ -278,8 +341,8 @@ def run(args) -> dict:
     timer = PhaseTimer(cuda)
     tokens = 0
     with ClockSampler(gpu_index=None) as clocks:
-        for k in range(args.steps):
-            tokens += grpo_step(api, step_samples(args.warmup + k), reward, timer=timer, counters=counters, **kw)
+        for k in range(steps):
+            tokens += grpo_step(api, step_samples(warm_done + k), reward, timer=timer, counters=counters, **kw)
         if cuda:
             torch.cuda.synchronize()
     if dist.is_available() and dist.is_initialized():
@@ -307,9 +370,12 @@ def run(args) -> dict:
         "value": round(value, 2),
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(device_ms / args.steps, 2),
+        "steps": steps,
+        "warmup": warm_done,
+        "requested_steps": args.steps,
+        "requested_warmup": args.warmup,
+        "time_budget_s": args.time_budget,
+        "ms_per_step": round(device_ms / steps, 2),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 4),
@@ -323,8 +389,8 @@ def run(args) -> dict:
             "l2": "inputs larger than L2 (weights 16 GB, KV cache > 10 GB per step)",
             "fixed_length_decode": args.impl == "ours",
         },
-        "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": counters["h2d"] // max(1, args.steps),
-                "d2h_bytes_per_step": counters["d2h"] // max(1, args.steps)},
+        "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": counters["h2d"] // max(1, steps),
+                "d2h_bytes_per_step": counters["d2h"] // max(1, steps)},
         "gpu_launches": int(float(maxes[3])),
         "clocks": clocks.summary() if rank == 0 else None,
     }
@@ -345,10 +411,13 @@ def main() -> None:
     p.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
     p.add_argument("--max-new", type=int, default=MAX_NEW)
     p.add_argument("--iters", type=int, default=1, help="optimize_iterations_per_step")
+    p.add_argument("--time-budget", type=float, default=TIME_BUDGET_S,
+                   help="wall-clock seconds for the whole run; fewer timed steps (>= 1) run when the requested "
+                        "ones would not fit, and warm-up stops early (after at least 3); 0 disables")
     args = p.parse_args()
-    if args.warmup < 3:
-        print("[bench] warm-up raised to 3 steps", file=sys.stderr)
-        args.warmup = 3
+    if args.warmup < MIN_WARMUP:
+        print(f"[bench] warm-up raised to {MIN_WARMUP} steps", file=sys.stderr)
+        args.warmup = MIN_WARMUP
     rank, world, _ = dist_env()
     if args.gpus != world:
         print(f"[bench] --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)

@@ -28,6 +28,7 @@
 
 #include <mutex>
 
+#include "graspo_noalloc.h"
 #include "sm100_common.cuh"
 
 namespace gb {
@@ -951,8 +952,8 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
 //    without ordering) race on the array and must not be issued.
 // ===========================================================================
 
-constexpr long kNoAllocScratchFloats = 1L << 20;
-constexpr int kNoAllocMaxCounters = 8192;
+constexpr long kNoAllocScratchFloats = GRASPO_NOALLOC_SCRATCH_FLOATS;
+constexpr int kNoAllocMaxCounters = GRASPO_NOALLOC_MAX_COUNTERS;
 
 // File-scope scratch for the allocation-free entry point (see above).  In host
 // code these names are host-side stand-ins, not device addresses: the device
@@ -993,29 +994,18 @@ static int resolve_slots(int device, DeviceSlots** out) {
 }  // namespace noalloc
 }  // namespace gb
 
-enum GbNoAllocStatus : int {
-  GB_NOALLOC_OK = 0,
-  GB_NOALLOC_TOO_LARGE = 1,
-  GB_NOALLOC_BAD_ARGUMENT = 2,
-  GB_NOALLOC_SETUP_FAILED = 3,
-  GB_NOALLOC_LAUNCH_FAILED = 4,
-  GB_NOALLOC_BAD_DEVICE = 5,
-};
-
 // Paged decode attention, split over the key range, scratch from the library's
-// fixed array.  Same layouts and semantics as paged_decode_attention():
-//   q [rows, nq, 128] bf16, k_pool / v_pool [pages, nkv, page_size, 128] bf16,
-//   block_table [rows, max_pages] int32, start / len [rows] int32,
-//   out [rows, nq * 128] bf16.
-// Returns a GbNoAllocStatus; nothing is launched unless it returns GB_NOALLOC_OK.
+// fixed array.  Same layouts and semantics as paged_decode_attention(); the
+// declaration and its contract are in graspo_noalloc.h.
 extern "C" int graspo_paged_decode_attention_noalloc(const void* q, const void* k_pool, const void* v_pool,
                                                      const int* block_table, const int* start, const int* len,
                                                      void* out, int rows, int nq, int nkv, int page_size,
-                                                     int max_pages, int splits, float scale, cudaStream_t stream) {
+                                                     int max_pages, int num_pages, int splits, float scale, int* err,
+                                                     cudaStream_t stream) {
   using namespace gb;
   if (q == nullptr || k_pool == nullptr || v_pool == nullptr || block_table == nullptr || start == nullptr ||
       len == nullptr || out == nullptr || rows <= 0 || nq <= 0 || nkv <= 0 || nq % nkv != 0 || page_size <= 0 ||
-      max_pages <= 0 || splits < 2) {
+      max_pages <= 0 || num_pages <= 0 || splits < 2) {
     return GB_NOALLOC_BAD_ARGUMENT;
   }
   const int G = nq / nkv;
@@ -1034,7 +1024,8 @@ extern "C" int graspo_paged_decode_attention_noalloc(const void* q, const void* 
     return GB_NOALLOC_LAUNCH_FAILED;
   }
   DecodeAttnArgs a{};
-  a.num_pages = 0x7fffffff;  // the C entry point has no pool size: block-table entries are trusted
+  a.num_pages = num_pages;
+  a.err = err;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k_pool = static_cast<const __nv_bfloat16*>(k_pool);
   a.v_pool = static_cast<const __nv_bfloat16*>(v_pool);

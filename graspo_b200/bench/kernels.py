@@ -313,6 +313,8 @@ def bench_profile(args) -> None:
         runs.append(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, 1 / math.sqrt(D), 4, scratch,
                                                          P, G, 2))
     elif k in ("flash_fwd", "flash_bwd", "flash_fwd_tc", "flash_bwd_tc"):
+        from graspo_b200.ops._ext import err_word
+
         B, S, nq, nkv, D = 4, 3072, 32, 8, 128
         T = B * S
         q = torch.randn(T, nq, D, device="cuda").bfloat16()
@@ -322,25 +324,15 @@ def bench_profile(args) -> None:
         end = torch.full((B,), S, device="cuda", dtype=torch.int32)
         o = torch.empty_like(q)
         lse = torch.empty(T, nq, device="cuda")
-        ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D))
-        if k == "flash_fwd":
-            runs.append(lambda: ext().flash_attn_fwd(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D)))
-        elif k == "flash_fwd_tc":
-            from graspo_b200.ops._ext import err_word
-
-            runs.append(lambda: ext().flash_attn_fwd_tc(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D),
-                                                        err_word(q.device)))
+        ew = err_word(q.device)
+        ext().flash_attn_fwd_tc(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D), ew)
+        if k in ("flash_fwd", "flash_fwd_tc"):
+            runs.append(lambda: ext().flash_attn_fwd_tc(q, kk, v, o, lse, start, end, B, S, 1 / math.sqrt(D), ew))
         else:
             do = torch.randn_like(q)
             dq, dk, dv = torch.empty_like(q), torch.empty_like(kk), torch.empty_like(v)
-            if k == "flash_bwd_tc":
-                from graspo_b200.ops._ext import err_word
-
-                runs.append(lambda: ext().flash_attn_bwd_tc(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
-                                                            1 / math.sqrt(D), err_word(q.device)))
-            else:
-                runs.append(lambda: ext().flash_attn_bwd(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
-                                                         1 / math.sqrt(D)))
+            runs.append(lambda: ext().flash_attn_bwd_tc(do, q, kk, v, o, lse, dq, dk, dv, start, end, B, S,
+                                                        1 / math.sqrt(D), ew))
     else:
         raise SystemExit(f"unknown kernel {k}")
     for _ in range(args.iters):

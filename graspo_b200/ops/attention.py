@@ -19,21 +19,16 @@ dK and dV in TMEM (dQ is added into an fp32 buffer with vector atomics).  The
 forward also returns the per-(token, head) log-sum-exp (log2 domain, fp32),
 which the backward uses to rebuild the probabilities without a second softmax
 pass (FlashAttention-2, Dao 2023).  GQA is handled inside the kernels: a query
-head reads KV head ``h // (nq // nkv)``.  ``GRASPO_FA_TC=0`` / ``GRASPO_FA_TC_BWD=0``
-select the mma.sync kernels (csrc/flash_attn.cu) instead.
+head reads KV head ``h // (nq // nkv)``.  On the CPU the entry points run their
+emulation (graspo_b200/ops/emulate.py), used by the CPU tests.
 Head dim 128 (every Qwen3 size) is the supported kernel shape.
 """
 
 from __future__ import annotations
 
-import os
-
 import torch
 
 from graspo_b200.ops._ext import err_word, ext
-
-USE_TC_FORWARD = os.environ.get("GRASPO_FA_TC", "1") != "0"
-USE_TC_BACKWARD = os.environ.get("GRASPO_FA_TC_BWD", "1") != "0"
 
 
 def row_ranges(meta) -> tuple[torch.Tensor, torch.Tensor]:
@@ -64,12 +59,8 @@ def attention_forward(q, k, v, meta, scale: float, need_ctx: bool = False):
     start, end = row_ranges(meta)
     out = torch.empty(T, nq * D, device=q.device, dtype=q.dtype)
     lse = torch.empty(T, nq, device=q.device, dtype=torch.float32)
-    if USE_TC_FORWARD and q.is_cuda:
-        ext().flash_attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
-                                meta.B, meta.S, float(scale), err_word(q.device))
-    else:
-        ext().flash_attn_fwd(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
-                             meta.B, meta.S, float(scale))
+    ext().flash_attn_fwd_tc(q.contiguous(), k.contiguous(), v.contiguous(), out.view(T, nq, D), lse, start, end,
+                            meta.B, meta.S, float(scale), err_word(q.device))
     return out, (lse if need_ctx else None)
 
 
@@ -85,8 +76,5 @@ def attention_backward(dout, q, k, v, out, ctx, meta, scale: float):
     dv = torch.empty_like(v)
     args = (dout.contiguous().view(T, nq, D), q.contiguous(), k.contiguous(), v.contiguous(),
             out.contiguous().view(T, nq, D), ctx.contiguous(), dq, dk, dv, start, end, meta.B, meta.S, float(scale))
-    if USE_TC_BACKWARD and q.is_cuda:
-        ext().flash_attn_bwd_tc(*args, err_word(q.device))
-    else:
-        ext().flash_attn_bwd(*args)
+    ext().flash_attn_bwd_tc(*args, err_word(q.device))
     return dq, dk, dv
