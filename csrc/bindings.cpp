@@ -9,7 +9,14 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
              c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
              int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
-             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout);
+             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout,
+             c10::optional<torch::Tensor> push_out, c10::optional<torch::Tensor> push_sig, int64_t push_self,
+             int64_t push_rows);
+void tp_reduce(torch::Tensor srcs, int64_t counter, int64_t expected, c10::optional<torch::Tensor> residual,
+               torch::Tensor out, int64_t ld_src, torch::Tensor err, int64_t spin_limit);
+void lse_push(torch::Tensor partials, torch::Tensor tgt, torch::Tensor dst, torch::Tensor sig, int64_t self);
+void lse_merge(torch::Tensor srcs, int64_t counter, int64_t expected, torch::Tensor lse, torch::Tensor logp,
+               torch::Tensor err, int64_t spin_limit);
 std::vector<torch::Tensor> symm_alloc(int64_t nbytes, int64_t device);
 int64_t symm_open(torch::Tensor handle, int64_t device);
 void symm_close(int64_t ptr, int64_t device);
@@ -36,13 +43,8 @@ void gated_delta_step(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::
                       torch::Tensor state, torch::Tensor out);
 void embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 bool kernel_checks();
-void flash_attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
-                    torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale);
 void flash_attn_fwd_tc(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out, torch::Tensor lse,
                        torch::Tensor start, torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err);
-void flash_attn_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
-                    torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
-                    torch::Tensor end, int64_t B, int64_t S, double scale);
 void flash_attn_bwd_tc(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor out,
                        torch::Tensor lse, torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor start,
                        torch::Tensor end, int64_t B, int64_t S, double scale, torch::Tensor err);
@@ -74,7 +76,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("B2"), py::arg("C"), py::arg("R"), py::arg("aux"), py::arg("targets"), py::arg("tgt_logit"),
         py::arg("row_lse"), py::arg("row_scale"), py::arg("epilogue"), py::arg("swap"), py::arg("bn"),
         py::arg("splits"), py::arg("err"), py::arg("max_ctas"), py::arg("push_dst") = py::none(),
-        py::arg("push_flag") = py::none(), py::arg("tile_ctr") = py::none(), py::arg("layout") = 0);
+        py::arg("push_flag") = py::none(), py::arg("tile_ctr") = py::none(), py::arg("layout") = 0,
+        py::arg("push_out") = py::none(), py::arg("push_sig") = py::none(), py::arg("push_self") = 0,
+        py::arg("push_rows") = 0);
+  m.def("tp_reduce", &gb::tp_reduce,
+        "sum of the tensor-parallel receive slots (rank order) + optional residual, after a bounded wait "
+        "on the arrival counter",
+        py::arg("srcs"), py::arg("counter"), py::arg("expected"), py::arg("residual"), py::arg("out"),
+        py::arg("ld_src"), py::arg("err"), py::arg("spin_limit") = 0);
+  m.def("lse_push", &gb::lse_push,
+        "vocab-parallel log-prob: this shard's (log-sum-exp, target logit) per token into every rank's slot");
+  m.def("lse_merge", &gb::lse_merge,
+        "vocab-parallel log-prob: bounded wait, then merge every shard's pair into lse and log-prob",
+        py::arg("srcs"), py::arg("counter"), py::arg("expected"), py::arg("lse"), py::arg("logp"), py::arg("err"),
+        py::arg("spin_limit") = 0);
   m.def("symm_alloc", &gb::symm_alloc, "zeroed device buffer + its CUDA IPC handle");
   m.def("symm_open", &gb::symm_open, "map a peer's buffer from its IPC handle; returns the device address");
   m.def("symm_close", &gb::symm_close);
@@ -101,8 +116,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("block_table"), py::arg("start"), py::arg("len"), py::arg("out"), py::arg("scale"),
         py::arg("splits"), py::arg("scratch"), py::arg("prefix_len") = 0, py::arg("group_rows") = 1,
         py::arg("prefix_splits") = 1, py::arg("err") = py::none());
-  m.def("flash_attn_fwd", &gb::flash_attn_fwd, "causal flash attention forward over row ranges");
-  m.def("flash_attn_bwd", &gb::flash_attn_bwd, "causal flash attention backward over row ranges");
   m.def("flash_attn_fwd_tc", &gb::flash_attn_fwd_tc, "causal flash attention forward on tcgen05 / TMEM");
   m.def("flash_attn_bwd_tc", &gb::flash_attn_bwd_tc, "causal flash attention backward on tcgen05 / TMEM");
   m.def("sample_append", &gb::sample_append);

@@ -13,7 +13,7 @@ namespace gb {
 
 bool& pdl_enabled() {
   // Off by default: on the decode loop (captured in a CUDA graph) it measured
-  // slower than plain stream order.  GRASPO_PDL=1 turns it on.
+  // slower than plain stream order.  _C.set_pdl(True) turns it on for measurements.
   static bool on = false;
   return on;
 }
@@ -69,7 +69,9 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              c10::optional<torch::Tensor> tgt_logit, c10::optional<torch::Tensor> row_lse,
              c10::optional<torch::Tensor> row_scale, int64_t epilogue, bool swap, int64_t bn,
              int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
-             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout) {
+             c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout,
+             c10::optional<torch::Tensor> push_out, c10::optional<torch::Tensor> push_sig, int64_t push_self,
+             int64_t push_rows) {
   check_operand(A, "A");
   check_operand(B, "B");
   // layout bit 1: A given as [K, M] (MN-major); bit 0: B given as [K, N]
@@ -185,6 +187,34 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
     args.tile_ctr = tile_ctr->data_ptr<int>();
     TORCH_CHECK(layout == 0 && C.scalar_type() == torch::kFloat32 && C.size(0) == Ndim && C.size(1) == Mdim,
                 "tile push writes C [tokens, features] in full");
+  }
+  if (push_out.has_value() && push_out->defined()) {
+    // fused all-reduce / reduce-scatter of a non-swap bf16 GEMM: C only supplies the row stride
+    TORCH_CHECK(!swap && epilogue == kStoreBF16 && (layout == 0 || layout == 1),
+                "slot push needs the non-swap bf16 store epilogue with a K-major A");
+    TORCH_CHECK(C.scalar_type() == torch::kBFloat16 && C.stride(1) == 1 && C.stride(0) >= Ndim &&
+                    (C.stride(0) * 2) % 16 == 0 && Ndim % 8 == 0,
+                "slot push: bf16 slots with 16-byte aligned rows and N a multiple of 8");
+    TORCH_CHECK(push_sig.has_value() && push_sig->defined(), "slot push needs arrival counters");
+    TORCH_CHECK(push_out->device().is_cpu() && push_out->scalar_type() == torch::kInt64 &&
+                    push_sig->device().is_cpu() && push_sig->scalar_type() == torch::kInt64 &&
+                    push_out->numel() == push_sig->numel() && push_out->numel() >= 1 && push_out->numel() <= kMaxPeers,
+                "push_out / push_sig: CPU int64 address tables of equal length in [1, 8]");
+    const int np = static_cast<int>(push_out->numel());
+    TORCH_CHECK(push_self >= 0 && push_self < np, "push_self must index the address tables");
+    TORCH_CHECK(push_rows == 0 || static_cast<int64_t>(push_rows) * np == Mdim,
+                "reduce-scatter push needs rows = M / ranks");
+    auto po = push_out->contiguous();
+    auto ps = push_sig->contiguous();
+    for (int q = 0; q < np; ++q) {
+      args.out_push[q] = reinterpret_cast<__nv_bfloat16*>(po.data_ptr<int64_t>()[q]);
+      args.sig_push[q] = reinterpret_cast<unsigned long long*>(ps.data_ptr<int64_t>()[q]);
+      TORCH_CHECK(args.out_push[q] != nullptr && reinterpret_cast<uintptr_t>(args.out_push[q]) % 16 == 0,
+                  "slot push: 16-byte aligned destination slots");
+    }
+    args.npush = np;
+    args.push_self = static_cast<int>(push_self);
+    args.push_rows = static_cast<int>(push_rows);
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   const int mc = static_cast<int>(max_ctas);

@@ -89,6 +89,22 @@ struct GemmArgs {
   // remaining tiles are split `splits` ways (split-K SwiGLU: the last wave of a
   // persistent grid is filled without splitting every tile).  0: all tiles split.
   int full_tiles;
+  // Tensor-parallel all-reduce / reduce-scatter of a non-swap bf16 GEMM
+  // (prefill and training, row-parallel projections and column-parallel
+  // dgrads).  With npush > 0 the epilogue stores every finished bf16 tile
+  // straight into the receive slot out_push[q] of each destination rank q
+  // (this rank's own slot included; row stride ldc) instead of C, and after
+  // the tile the 64-bit arrival counter sig_push[q] of each remote
+  // destination grows by the number of elements it received (release at
+  // system scope).  push_rows > 0 selects reduce-scatter: row m goes only to
+  // rank m / push_rows, at row m % push_rows of its slot; push_rows == 0 is
+  // all-reduce (every rank receives every row).  The consumer kernel
+  // (tp_reduce) waits for the counters and sums the slots in rank order.
+  __nv_bfloat16* out_push[kMaxPeers];
+  unsigned long long* sig_push[kMaxPeers];
+  int npush;
+  int push_self;
+  int push_rows;
 };
 
 template <int BN_>
@@ -190,6 +206,66 @@ __device__ __forceinline__ void push_tile_impl(const GemmArgs& args, const Unit&
     }
   }
   epi_bar();  // last_split is rewritten by the next unit
+}
+
+// One 32-column chunk of output row m (fp32 values v) to its destination
+// slot(s) of the fused all-reduce / reduce-scatter (see GemmArgs::out_push).
+__device__ __forceinline__ void push_chunk_bf16(const GemmArgs& args, int m, int nc, bool full_chunk,
+                                                const float (&v)[32]) {
+  int q0 = 0, q1 = args.npush;
+  long row = m;
+  if (args.push_rows > 0) {
+    q0 = m / args.push_rows;
+    q1 = q0 + 1;
+    row = m - static_cast<long>(q0) * args.push_rows;
+  }
+  uint4 pk[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk[q]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[q * 8 + 2 * e], v[q * 8 + 2 * e + 1]);
+  }
+  for (int q = q0; q < q1; ++q) {
+    __nv_bfloat16* D = args.out_push[q] + row * args.ldc + nc;
+    if (full_chunk) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reinterpret_cast<uint4*>(D)[c] = pk[c];
+    } else {
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(pk);
+      for (int j = 0; j < 32; ++j)
+        if (nc + j < args.N) D[j] = b[j];
+    }
+  }
+}
+
+// After the 128 epilogue threads stored a tile to its destinations: make the
+// stores visible system-wide, then one thread adds the element counts to the
+// remote destinations' arrival counters (release).  Every epilogue thread
+// reaches the barrier, also after a timed-out accumulator wait, so the peers'
+// consumers are never left waiting on a tile that will not be signalled.
+template <int BN>
+__device__ __forceinline__ void push_signal(const GemmArgs& args, const Unit& w, int row_in_tile) {
+  __threadfence_system();
+  epi_bar();
+  if (row_in_tile == 0) {
+    const int m0 = w.m_block * BM;
+    const int mm = min(BM, args.M - m0);
+    const int nn = min(BN, args.N - w.n_block * BN);
+    for (int q = 0; q < args.npush; ++q) {
+      if (q == args.push_self || args.sig_push[q] == nullptr) continue;
+      long rows_q = mm;
+      if (args.push_rows > 0) {
+        const long lo = max(static_cast<long>(m0), static_cast<long>(q) * args.push_rows);
+        const long hi = min(static_cast<long>(m0 + mm), static_cast<long>(q + 1) * args.push_rows);
+        rows_q = hi > lo ? hi - lo : 0;
+      }
+      if (rows_q > 0) {
+        const unsigned long long cnt = static_cast<unsigned long long>(rows_q) * nn;
+        asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(args.sig_push[q]), "l"(cnt) : "memory");
+      }
+    }
+  }
 }
 
 // Split-K SwiGLU (swap layout): every split stores its fp32 partial tile into
@@ -521,6 +597,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const bool full_chunk = (nc + 32 <= args.N);
           if constexpr (EPI == kStoreBF16) {
+            if (args.npush > 0) {
+              if (args.R != nullptr) {
+                const __nv_bfloat16* R = args.R + static_cast<long>(m) * args.ldr + nc;
+                for (int j = 0; j < 32; ++j)
+                  if (nc + j < args.N) v[j] += __bfloat162float(R[j]);
+              }
+              push_chunk_bf16(args, m, nc, full_chunk, v);
+              continue;
+            }
             __nv_bfloat16* C = static_cast<__nv_bfloat16*>(args.C) + static_cast<long>(m) * args.ldc + nc;
             if (args.R != nullptr) {
               const __nv_bfloat16* R = args.R + static_cast<long>(m) * args.ldr + nc;
@@ -667,6 +752,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if constexpr (SWAP && EPI == kSwiGLU) {
         if (w.partial) swiglu_fixup_impl<BN>(args, w, num_n, m, row_in_tile);
+      }
+      if constexpr (!SWAP && EPI == kStoreBF16) {
+        if (args.npush > 0) push_signal<BN>(args, w, row_in_tile);
       }
     }
   }

@@ -441,7 +441,28 @@ class Qwen3Adapter:
         outs = []
         for sl in self._token_budget_chunks(seq.shape[0], seq.shape[1]):
             outs.append(self._logprobs(seq[sl], mask[sl], train=False)[0])
-        return torch.cat(outs, 0)
+        out = torch.cat(outs, 0)
+        self._check_kernels()
+        return out
+
+    def _check_kernels(self) -> None:
+        """Raise ``KernelTimeout`` if a bounded device wait gave up since the last check.
+
+        A wait that ran out leaves the fused collective sites' arrival counters
+        out of step with the host's expectations, so the sites are retired
+        first (the next use builds fresh, zeroed buffers)."""
+        if self.device.type != "cuda" or not self.fused:
+            return
+        from graspo_b200.ops._ext import KernelTimeout, check_errors
+
+        try:
+            check_errors(self.device)
+        except KernelTimeout:
+            red = getattr(self._fused, "_tp_red", None)
+            if red is not None:
+                red.close()
+                self._fused._tp_red = None
+            raise
 
     def _logprobs(self, seq, mask, *, train: bool, seed: int = 0, targets=None, embed_hook=None):
         """log p(targets) per position, [B, S-1] fp32 (targets default to seq[:, 1:]).
@@ -639,6 +660,7 @@ class Qwen3Adapter:
         if os.environ.get("GRASPO_CHECK_REPLICAS", "0") == "1":
             self.check_replicas()
         loss_vals = [float(x) for x in torch.cat(losses).cpu()] if losses else []
+        self._check_kernels()
         norm_vals = [float(x) for x in torch.cat([n.reshape(1) for n in norms]).cpu()] if norms else []
         skipped = int(self.optimizer.skipped.item())
         finite = [v for v in loss_vals if math.isfinite(v)]

@@ -339,7 +339,15 @@ class FusedRolloutEngine:
             comm.broadcast_from_last(st["out"])
         _sync(dev)
         t2 = time.perf_counter()
-        check_errors(dev)
+        try:
+            check_errors(dev)
+        except Exception:
+            # a peer wait that ran out leaves the decode sites' arrival counters
+            # out of step: retire them so the next call builds zeroed ones
+            for site in self._peer_sites.values():
+                site.close()
+            self._peer_sites.clear()
+            raise
         tokens = st["out"].cpu()
         return RolloutResult(
             prompt_ids=ids, prompt_lens=lens, tokens=tokens, gen_lens=_gen_lengths(tokens, eos_id, ignore_eos),

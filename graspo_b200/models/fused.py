@@ -17,7 +17,12 @@ the backward kernels.  LoRA gradients are tensor-core reductions over tokens
 (``dB = dY^T U``, ``dA = s * dU^T X``) written straight into the adapter's
 flat fp32 gradient buffer.  Under tensor parallelism the input gradients of
 column-parallel projections are all-reduced over the TP group (the conjugate
-of the forward all-reduce after row-parallel projections).
+of the forward all-reduce after row-parallel projections).  On B200s both
+directions are fused collectives: the GEMM epilogue stores its bf16 partial
+tiles into every rank's receive slot over NVLink and ``tp_reduce`` sums the
+slots once the peers' tiles have arrived (``parallel/symm.py`` TPAllReduce);
+with sequence parallelism each row goes only to the rank that owns its token
+(reduce-scatter).
 
 The selected-token log-prob never materialises logits: the LM-head GEMM's
 epilogue emits per-tile (max, sum-exp) partials, a small kernel merges them
@@ -132,6 +137,20 @@ class FusedQwen3:
         self.eps = model.cfg.rms_norm_eps
         self.scale = 1.0 / math.sqrt(model.D)
         self.sp = bool(sequence_parallel) and model.ps.tp_size > 1
+        self._tp_red = None
+
+    def tp_reducer(self):
+        """The fused GEMM + all-reduce / reduce-scatter sites (CUDA with TP > 1), made on first use.
+
+        On the CPU (gloo process groups in tests) the collectives stay library calls."""
+        m = self.m
+        if m.ps.tp_size == 1 or m.device.type != "cuda" or not dist.is_initialized():
+            return None
+        if self._tp_red is None:
+            from graspo_b200.parallel.symm import TPAllReduce
+
+            self._tp_red = TPAllReduce(m.ps.tp_group, m.device, m.cfg.hidden_size)
+        return self._tp_red
 
     # ------------------------------------------------------------ sequence parallel
     def sp_shard(self, x: torch.Tensor) -> torch.Tensor:
@@ -153,10 +172,6 @@ class FusedQwen3:
         y = torch.empty_like(x)
         self.C.dropout(x, y, p, seed, layer * 8 + _DROP_SITES[site], None)
         return y
-
-    def _dropout_add(self, x, base, site, layer, seed):
-        """base + mask(x) with the forward's mask (in place into base)."""
-        self.C.dropout(x, base, self.m.lora.dropout, seed, layer * 8 + _DROP_SITES[site], base)
 
     def _layouts(self, lw: LayerWeights):
         return self.m.lora.layer_layouts(lw.index, self.m.sizes)
@@ -215,6 +230,13 @@ class FusedQwen3:
         elif tp == 1:
             gemm(attn, lw.w_o, x1, ext_ab=ext_o, residual=x)
             C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
+        elif self.tp_reducer() is not None:
+            # the o_proj GEMM pushes its partial tiles to every rank; x1 = x + sum
+            red = self.tp_reducer()
+            push = red.begin(T, scatter=sp)
+            gemm(attn, lw.w_o, push.pop("out"), ext_ab=ext_o, push=push)
+            x1 = red.finish(residual=x)
+            C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
         else:
             o = gemm(attn, lw.w_o, ext_ab=ext_o)
             o = _sp_scatter(o, tp_group) if sp else _tp_all_reduce(o, tp_group)
@@ -244,6 +266,11 @@ class FusedQwen3:
             x2 = None  # every TP rank skips the same GEMM and collective
         elif tp == 1:
             x2 = gemm(act, lw.w_down, ext_ab=ext_d, residual=x1)
+        elif self.tp_reducer() is not None:
+            red = self.tp_reducer()
+            push = red.begin(T, scatter=sp)
+            gemm(act, lw.w_down, push.pop("out"), ext_ab=ext_d, push=push)
+            x2 = red.finish(residual=x1)
         else:
             d = gemm(act, lw.w_down, ext_ab=ext_d)
             d = _sp_scatter(d, tp_group) if sp else _tp_all_reduce(d, tp_group)
@@ -262,32 +289,51 @@ class FusedQwen3:
         return x2, s
 
     # ------------------------------------------------------------ backward
-    def _lora_linear_backward(self, dy, w, saved_u, saved_xd, b_ext, a_ext, site, layer, seed, train):
+    def _lora_linear_backward(self, dy, w, saved_u, saved_xd, b_ext, a_ext, site, layer, seed, train,
+                              reduce: str | None = None):
         """d(input) of y = x W^T + U B^T with U = drop(x) (sA)^T, plus LoRA grads.
 
         Every operand is read as stored: ``W`` [N, K], ``B`` [N, 64k] and ``sA``
         [64k, K] are the MN-major B operand of ``dy @ W`` / ``dy @ B`` /
         ``du @ sA``, and the gradients contract over tokens with both operands
         MN-major (split-K fp32 atomics), so no transposed copy is made.
+        ``reduce`` ("all" or "scatter") sums d(input) over the TP group: the
+        dgrad GEMM pushes its tiles to the peers (fused all-reduce /
+        reduce-scatter) on CUDA, an NCCL / gloo collective follows it elsewhere.
         Returns (dx, db_full [N, 64k] fp32, da_full [64k, K] fp32) -- the
         gradient w.r.t. the padded layouts (caller scatters into parameters).
         """
+        red = self.tp_reducer() if reduce is not None else None
+        push, out = None, None
+        if red is not None:
+            push = red.begin(dy.shape[0], scatter=reduce == "scatter")
+            out = push.pop("out")
         if saved_u is None:
-            return gemm(dy, w, b_mn=True), None, None
-        du = gemm(dy, b_ext, b_mn=True, bn=64)            # [T, 64k]
-        p = self.m.lora.dropout
-        if train and p > 0:
-            dx = gemm(dy, w, b_mn=True)
-            tmp = gemm(du, a_ext, b_mn=True)
-            self._dropout_add(tmp, dx, site, layer, seed)
+            dx = gemm(dy, w, out, b_mn=True, push=push)
+            db = da = None
         else:
-            dx = gemm(dy, w, b_mn=True, ext_ab=(du, a_ext))
-        n_out, width, k_in = dy.shape[1], saved_u.shape[1], saved_xd.shape[1]
-        db = torch.zeros(n_out, width, device=dy.device, dtype=torch.float32)
-        gemm(dy, saved_u, db, epilogue="atomic", a_mn=True, b_mn=True, bn=64, splits=_grad_splits(n_out))
-        da = torch.zeros(width, k_in, device=dy.device, dtype=torch.float32)
-        gemm(saved_xd, du, da, epilogue="atomic", a_mn=True, b_mn=True, bn=64, swap=True,
-             splits=_grad_splits(k_in))
+            du = gemm(dy, b_ext, b_mn=True, bn=64)            # [T, 64k]
+            p = self.m.lora.dropout
+            if train and p > 0:
+                # the LoRA path's dgrad, masked like the forward, enters the
+                # frozen dgrad's epilogue as a residual
+                tmp = self._dropout(gemm(du, a_ext, b_mn=True), site, layer, seed, train)
+                dx = gemm(dy, w, out, b_mn=True, residual=tmp, push=push)
+                del tmp
+            else:
+                dx = gemm(dy, w, out, b_mn=True, ext_ab=(du, a_ext), push=push)
+            n_out, width, k_in = dy.shape[1], saved_u.shape[1], saved_xd.shape[1]
+            db = torch.zeros(n_out, width, device=dy.device, dtype=torch.float32)
+            gemm(dy, saved_u, db, epilogue="atomic", a_mn=True, b_mn=True, bn=64, splits=_grad_splits(n_out))
+            da = torch.zeros(width, k_in, device=dy.device, dtype=torch.float32)
+            gemm(saved_xd, du, da, epilogue="atomic", a_mn=True, b_mn=True, bn=64, swap=True,
+                 splits=_grad_splits(k_in))
+        if red is not None:
+            dx = red.finish()
+        elif reduce == "scatter":
+            dx = _sp_scatter(dx, self.m.ps.tp_group)
+        elif reduce == "all":
+            dx = _tp_all_reduce(dx, self.m.ps.tp_group)
         return dx, db, da
 
     def _scatter_grads(self, layer: int, group: str, db, da) -> None:
@@ -331,12 +377,12 @@ class FusedQwen3:
         C.swiglu_bwd(s.gu, dact, dgu)
         del dact
         # --- gate/up
+        tp_reduce = None if m.ps.tp_size == 1 else ("scatter" if sp else "all")
         dxn2, db, da = self._lora_linear_backward(dgu, lw.w_gu, s.u_gu, s.xd2, L.get("b_gu"), L.get("a_gu"),
-                                                  "gu", li, seed, train)
+                                                  "gu", li, seed, train, reduce=tp_reduce)
         if db is not None:
             self._scatter_grads(li, "gu", db, da)
         del dgu, dy2
-        dxn2 = _sp_scatter(dxn2, tp_group) if sp else _tp_all_reduce(dxn2, tp_group)
         dx1 = torch.empty_like(dx2)
         C.rmsnorm_bwd(dxn2, s.x1, lw.ln2, s.rstd2, dx2, dx1, self.eps)
         # --- o projection
@@ -352,10 +398,9 @@ class FusedQwen3:
         del dq, dk, dv
         # --- qkv projection
         dxn, db, da = self._lora_linear_backward(dqkv, lw.w_qkv, s.u_qkv, s.xd, L.get("b_qkv"), L.get("a_qkv"),
-                                                 "qkv", li, seed, train)
+                                                 "qkv", li, seed, train, reduce=tp_reduce)
         if db is not None:
             self._scatter_grads(li, "qkv", db, da)
-        dxn = _sp_scatter(dxn, tp_group) if sp else _tp_all_reduce(dxn, tp_group)
         dx = torch.empty_like(dx2)
         C.rmsnorm_bwd(dxn, s.x, lw.ln1, s.rstd1, dx1, dx, self.eps)
         return dx
@@ -462,6 +507,10 @@ class FusedQwen3:
         tl = torch.zeros(T, device=h.device, dtype=torch.float32)
         gemm(h, m.lm_head, torch.empty(0, device=h.device), epilogue="lse", aux=part.view(T, nblk * 2),
              targets=local_t, tgt_logit=tl, bn=bn)
+        red = self.tp_reducer()
+        if red is not None:
+            # vocab shards merged through peer memory (no library collective)
+            return red.lse_exchange(part, tl)
         lse = torch.empty(T, device=h.device, dtype=torch.float32)
         logp = torch.empty(T, device=h.device, dtype=torch.float32)
         self.C.lse_combine(part, tl, lse, logp)
@@ -486,12 +535,22 @@ class FusedQwen3:
         T, H = h.shape
         dh = torch.empty_like(h)
         local_t = (targets - m.vocab_start).contiguous()
+        # without SP the vocab shards' partial d(hidden) are summed by the fused
+        # GEMM + all-reduce, chunk by chunk
+        red = self.tp_reducer() if not self.sp else None
         for t0 in range(0, T, chunk_tokens):
             t1 = min(T, t0 + chunk_tokens)
             dlog = gemm(h[t0:t1], m.lm_head, epilogue="softmax_grad", targets=local_t[t0:t1],
                         row_lse=lse[t0:t1].contiguous(), row_scale=g[t0:t1].contiguous())
-            gemm(dlog, m.lm_head, dh[t0:t1], b_mn=True)
+            if red is not None:
+                push = red.begin(t1 - t0)
+                gemm(dlog, m.lm_head, push.pop("out"), b_mn=True, push=push)
+                red.finish(out=dh[t0:t1])
+            else:
+                gemm(dlog, m.lm_head, dh[t0:t1], b_mn=True)
             del dlog
+        if red is not None:
+            return dh
         if self.sp:
             return _sp_scatter(dh, m.ps.tp_group)
         _tp_all_reduce(dh, m.ps.tp_group)

@@ -21,6 +21,7 @@ ERROR_NAMES = {
     4: "accumulator never released (TMEM empty timeout)",
     5: "peer GPU never signalled (cross-GPU flag timeout)",
     6: "bad shape",
+    7: "index outside its table (kernel-checks build; the access was clamped)",
 }
 
 
@@ -78,9 +79,6 @@ def ext():
                 "graspo_b200._C (the sm_100a kernel library) is not built; run "
                 "`python setup.py build_ext --inplace` in the repository root"
             ) from exc
-        import os
-
-        module.set_pdl(os.environ.get("GRASPO_PDL", "0") == "1")
         _C = _Counting(module)
     return _C
 

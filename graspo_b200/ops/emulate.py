@@ -24,8 +24,9 @@ def _f(x):
 
 
 def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epilogue, swap, bn, splits, err,
-            max_ctas, push_dst=None, push_flag=None, tile_ctr=None, layout=0):
-    if push_dst is not None:
+            max_ctas, push_dst=None, push_flag=None, tile_ctr=None, layout=0, push_out=None, push_sig=None,
+            push_self=0, push_rows=0):
+    if push_dst is not None or push_out is not None:
         raise NotImplementedError("the peer-memory tile push needs GPUs")
     a_mn, b_mn = bool(layout & 2), bool(layout & 1)
 
@@ -370,3 +371,15 @@ def use_emulation():
 
 def kernel_checks():
     return False
+
+
+def tp_reduce(srcs, counter, expected, residual, out, ld_src, err, spin_limit=0):
+    raise NotImplementedError("the fused tensor-parallel reduction reads peer memory and needs GPUs")
+
+
+def lse_push(partials, tgt, dst, sig, self_rank):
+    raise NotImplementedError("the vocab-parallel log-prob exchange writes peer memory and needs GPUs")
+
+
+def lse_merge(srcs, counter, expected, lse, logp, err, spin_limit=0):
+    raise NotImplementedError("the vocab-parallel log-prob exchange reads peer memory and needs GPUs")

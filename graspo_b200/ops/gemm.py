@@ -95,7 +95,9 @@ def gemm(
     bn = bn or pick_bn(narrow, swap)
     if b_mn:
         bn = max(bn, 64)
-    kw = push.gemm_kwargs() if push is not None else {}
+    # push: the decode all-reduce site (PeerReduce) or the slot-push tables of a
+    # prefill / training site (TPAllReduce.begin's keyword arguments)
+    kw = push.gemm_kwargs() if hasattr(push, "gemm_kwargs") else dict(push or {})
     if tile_ctr is not None:
         kw["tile_ctr"] = tile_ctr
     layout = (2 if a_mn else 0) | (1 if b_mn else 0)

@@ -85,3 +85,139 @@ class PeerReduce:
 
     def close(self) -> None:
         self.sym.close()
+
+
+class TPAllReduce:
+    """Fused all-reduce / reduce-scatter sites of prefill and training.
+
+    The row-parallel projections (o_proj, down_proj) and the dgrads of the
+    column-parallel ones produce per-rank partial sums that the tensor-parallel
+    group must add.  Instead of a GEMM followed by an NCCL call, the GEMM's
+    epilogue stores each finished bf16 tile straight into this rank's receive
+    slot on every destination rank (NVLink stores into CUDA-IPC mapped
+    memory), signalling a 64-bit arrival counter per tile; ``tp_reduce`` then
+    waits (bounded) for the peers' tiles and sums the slots in rank order, so
+    the transfer overlaps the GEMM's remaining tiles and all ranks hold the same
+    bits.  Reduce-scatter (sequence parallelism) sends each row only to the rank
+    that owns its token.
+
+    Two slot sets alternate between consecutive sites.  A rank writes site s+2
+    into a peer's set (s mod 2) only after it has consumed site s+1, which
+    needed the peer's site s+1 tiles, which the peer produced after consuming
+    site s -- so a set is never overwritten while its owner still reads it.
+    Every rank of the group must call ``begin`` / ``finish`` for the same sites
+    in the same order (the model's program order guarantees it).
+
+    Buffer of each rank: [0, 16) the two sets' arrival counters (u64), then
+    ``2 x tp`` slots of ``capacity x hidden`` bf16 (set b, source rank q at
+    ``256 + (b * tp + q) * slot_bytes``).  The capacity grows on demand (a
+    collective of the group: every rank sees the same token counts).
+
+    Reference counterpart: the NCCL all-reduce of
+    src/graspo/backends/graspoflow/tensor_utils.py:146-164 (called from
+    models/common/layers_qwen3.py:263-264, 333-335).
+    """
+
+    def __init__(self, group, device: torch.device, hidden: int, capacity: int = 0) -> None:
+        self.group = group
+        self.device = device
+        self.hidden = int(hidden)
+        self.tp = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.capacity = 0
+        self.slot_bytes = 0
+        self.sym = None
+        self.site = 0
+        self.expected = [0, 0]
+        self._pending = None
+        self.err = err_word(device)
+        if capacity:
+            self._alloc(capacity)
+
+    def _alloc(self, capacity: int) -> None:
+        if self.sym is not None:
+            # every rank has finished with the old buffers (its kernels and the
+            # peers' pushes into it) before any rank unmaps or frees them
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            self.sym.close()
+            dist.barrier(group=self.group)
+            self.sym = None
+        self.capacity = int(capacity)
+        self.slot_bytes = self.capacity * self.hidden * 2
+        self.sym = SymmetricBuffer(_HEADER + 2 * self.tp * self.slot_bytes, self.group, self.device)
+        self.site = 0
+        self.expected = [0, 0]
+
+    def _slot_addr(self, rank: int, buf: int, src: int) -> int:
+        return self.sym.ptrs[rank] + _HEADER + (buf * self.tp + src) * self.slot_bytes
+
+    def begin(self, tokens: int, scatter: bool = False) -> dict:
+        """GEMM keyword arguments (``out`` and the push tables) for the next site.
+
+        ``out`` is this rank's own slot viewed as [tokens (or tokens / tp), hidden]."""
+        if self._pending is not None:
+            raise RuntimeError("TPAllReduce: begin() called twice without finish()")
+        if scatter and tokens % self.tp:
+            raise ValueError("reduce-scatter needs tokens divisible by the TP size")
+        if tokens > self.capacity:
+            self._alloc(max(tokens, 2 * self.capacity))
+        b = self.site & 1
+        rows = tokens // self.tp if scatter else tokens
+        r = self.rank
+        out_tab = torch.tensor([self._slot_addr(q, b, r) for q in range(self.tp)], dtype=torch.int64)
+        sig_tab = torch.tensor([self.sym.ptrs[q] + 8 * b if q != r else 0 for q in range(self.tp)],
+                               dtype=torch.int64)
+        own = self.sym.buf[_HEADER + (b * self.tp + r) * self.slot_bytes:]
+        out = own[: rows * self.hidden * 2].view(torch.bfloat16).view(rows, self.hidden)
+        self.expected[b] += rows * self.hidden * (self.tp - 1)
+        self._pending = (b, rows)
+        return {"out": out, "push_out": out_tab, "push_sig": sig_tab, "push_self": r,
+                "push_rows": rows if scatter else 0}
+
+    def finish(self, residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
+               spin_limit: int = 0) -> torch.Tensor:
+        """Sum of the site's slots in rank order (+ residual) into ``out`` (bf16 [rows, hidden])."""
+        if self._pending is None:
+            raise RuntimeError("TPAllReduce: finish() without begin()")
+        b, rows = self._pending
+        self._pending = None
+        self.site += 1
+        if out is None:
+            out = torch.empty(rows, self.hidden, device=self.device, dtype=torch.bfloat16)
+        srcs = torch.tensor([self._slot_addr(self.rank, b, q) for q in range(self.tp)], dtype=torch.int64)
+        ext().tp_reduce(srcs, self.sym.ptrs[self.rank] + 8 * b, self.expected[b], residual, out, self.hidden,
+                        self.err, spin_limit)
+        return out
+
+    def lse_exchange(self, partials: torch.Tensor, tgt_logit: torch.Tensor, spin_limit: int = 0):
+        """Vocab-parallel log-prob merge as one more site: this shard's per-token
+        (log-sum-exp, target logit) pair goes to every rank (``lse_push``), and
+        ``lse_merge`` combines all shards' pairs -> (lse [T], logp [T]) fp32.
+
+        ``partials`` are the LM-head GEMM's per-tile (max, sum-exp) pairs
+        [T, blocks, 2]; ``tgt_logit`` is zero where the target is outside this
+        shard.  Replaces an NCCL all-gather and all-reduce per log-prob chunk."""
+        if self._pending is not None:
+            raise RuntimeError("TPAllReduce: lse_exchange inside an open site")
+        T = partials.shape[0]
+        if self.slot_bytes < 8 * T:
+            self._alloc(max(2 * self.capacity, -(-8 * T // (2 * self.hidden))))
+        b = self.site & 1
+        self.site += 1
+        r = self.rank
+        dst = torch.tensor([self._slot_addr(q, b, r) for q in range(self.tp)], dtype=torch.int64)
+        sig = torch.tensor([self.sym.ptrs[q] + 8 * b if q != r else 0 for q in range(self.tp)], dtype=torch.int64)
+        self.expected[b] += T * (self.tp - 1)
+        C = ext()
+        C.lse_push(partials, tgt_logit.contiguous(), dst, sig, r)
+        lse = torch.empty(T, device=self.device, dtype=torch.float32)
+        logp = torch.empty(T, device=self.device, dtype=torch.float32)
+        srcs = torch.tensor([self._slot_addr(r, b, q) for q in range(self.tp)], dtype=torch.int64)
+        C.lse_merge(srcs, self.sym.ptrs[r] + 8 * b, self.expected[b], lse, logp, self.err, spin_limit)
+        return lse, logp
+
+    def close(self) -> None:
+        if self.sym is not None:
+            self.sym.close()
+            self.sym = None

@@ -147,6 +147,74 @@ def test_fused_tp_allreduce_matches_nccl():
     run_world(2, _peer_reduce_worker, timeout=300)
 
 
+def _tp_reduce_worker(rank, world):
+    """GEMM slot push + tp_reduce over real peers == the NCCL sum of the same partials."""
+    import torch.distributed as dist
+
+    from graspo_b200.ops._ext import check_errors
+    from graspo_b200.ops.gemm import gemm
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.symm import TPAllReduce
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ps = pstate.initialize(world, 1, 0, timeout_sec=120)
+    H = 1024
+    red = TPAllReduce(ps.tp_group, ps.device, H)
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    shared = torch.Generator(device="cuda").manual_seed(7)
+    # the 4096-token site outgrows the slots: the buffers are re-made mid-sequence
+    for T, scatter in [(512, False), (256, True), (4096, False), (640, True), (300, False), (1024, True)]:
+        rows = T // world if scatter else T
+        a = (torch.randn(T, 384, device="cuda", generator=g) * 0.5).bfloat16()
+        w = (torch.randn(H, 384, device="cuda", generator=g) * 0.5).bfloat16()
+        res = torch.randn(rows, H, device="cuda", generator=shared).bfloat16()
+        push = red.begin(T, scatter=scatter)
+        gemm(a, w, push.pop("out"), push=push)
+        y = red.finish(residual=res)
+        part = (a.float() @ w.float().T).bfloat16().float()
+        parts = [torch.empty_like(part) for _ in range(world)]
+        dist.all_gather(parts, part)
+        total = parts[0]
+        for q in range(1, world):
+            total = total + parts[q]
+        if scatter:
+            total = total[rank * rows : (rank + 1) * rows]
+        want = total + res.float()
+        err = (y.float() - want).abs().max().item() / want.abs().max().item()
+        assert err < 1e-2, (T, scatter, err)
+        if not scatter:
+            other = [torch.empty_like(y) for _ in range(world)]
+            dist.all_gather(other, y)
+            assert all(torch.equal(o, y) for o in other), "ranks must hold bit-identical sums"
+    # vocab-parallel log-prob: each rank holds a vocabulary shard of the head
+    T, Hd, V = 300, 256, 4096
+    h = (torch.randn(T, Hd, device="cuda", generator=shared)).bfloat16()
+    head = (torch.randn(V, Hd, device="cuda", generator=shared) * 0.2).bfloat16()
+    tgt = torch.randint(0, V, (T,), device="cuda", generator=shared)
+    vs = V // world
+    local = head[rank * vs : (rank + 1) * vs].contiguous()
+    nblk = -(-vs // 256)
+    part = torch.empty(T, nblk, 2, device="cuda")
+    tl = torch.zeros(T, device="cuda")
+    gemm(h, local, torch.empty(0, device="cuda"), epilogue="lse", aux=part.view(T, nblk * 2),
+         targets=(tgt - rank * vs).contiguous(), tgt_logit=tl, bn=256)
+    lse, logp = red.lse_exchange(part, tl)
+    logits = h.float() @ head.float().T
+    want_lse = torch.logsumexp(logits, -1)
+    want = logits.gather(1, tgt[:, None]).squeeze(1) - want_lse
+    assert (lse - want_lse).abs().max().item() < 2e-3
+    assert (logp - want).abs().max().item() < 2e-3
+    torch.cuda.synchronize()
+    check_errors()
+    red.close()
+    pstate.destroy()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_gemm_tp_reduce_matches_nccl():
+    run_world(2, _tp_reduce_worker, timeout=300)
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tp2_fused_matches_tp1(tmp_path):
     from graspo_b200.utils.synth import write_qwen3_checkpoint
