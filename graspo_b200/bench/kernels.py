@@ -290,6 +290,50 @@ def bench_profile(args) -> None:
         ctr = torch.zeros(192, device="cuda", dtype=torch.int32)
         kw = dict(aux=ws, tile_ctr=ctr) if splits > 1 else {}
         runs.append(lambda: gemm(w, x, out, swap=True, epilogue="swiglu", splits=splits, **kw))
+    elif k in ("lse", "softmax_grad"):
+        # LM head over the full vocabulary: per-tile log-sum-exp partials + target logit (old log-probs,
+        # 8192 tokens), or the softmax-grad epilogue of its backward
+        T, H, V = 8192, 4096, 151936
+        h = torch.randn(T, H, device="cuda").bfloat16()
+        head = (torch.randn(V, H, device="cuda") * 0.02).bfloat16()
+        tgt = torch.randint(0, V, (T,), device="cuda")
+        nblk = -(-V // 256)
+        part = torch.empty(T, nblk * 2, device="cuda")
+        tl = torch.zeros(T, device="cuda")
+        if k == "lse":
+            runs.append(lambda: gemm(h, head, torch.empty(0, device="cuda"), epilogue="lse", aux=part, targets=tgt,
+                                     tgt_logit=tl, bn=256))
+        else:
+            lse = torch.full((T,), 12.0, device="cuda")
+            g = torch.full((T,), 1e-3, device="cuda")
+            runs.append(lambda: gemm(h, head, epilogue="softmax_grad", targets=tgt, row_lse=lse, row_scale=g))
+    elif k == "gemm_qkv_decode":
+        # decode q/k/v projection with its LoRA A rows: 64 tokens, swap layout, split-K 3, fp32 atomics
+        w, x = torch.randn(6144 + 64, 4096, device="cuda").bfloat16(), torch.randn(64, 4096, device="cuda").bfloat16()
+        ws = torch.zeros(64, 6144 + 64, device="cuda")
+        runs.append(lambda: gemm(w, x, ws, swap=True, epilogue="atomic", splits=3))
+    elif k == "adamw":
+        # clipped AdamW over the flat LoRA buffer of the Qwen3-8B config (r=16, all linears)
+        n = 43646976
+        p, g = torch.randn(n, device="cuda") * 0.01, torch.randn(n, device="cuda") * 1e-3
+        m1, m2 = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+        sumsq, loss = torch.ones(1, device="cuda"), torch.zeros(1, device="cuda")
+        skipped = torch.zeros(1, dtype=torch.int32, device="cuda")
+        runs.append(lambda: ext().adamw(p, g, m1, m2, 5e-6, 0.9, 0.999, 1e-8, 0.01, 1, sumsq, 1.0, loss, skipped))
+    elif k == "sample":
+        # Gumbel-max sampling + decode-state update, 64 rows x 151936 vocabulary (top-p 1 and 0.9)
+        rows, V = 64, 151936
+        logits = torch.randn(rows, V, device="cuda") * 3
+        st = dict(next_ids=torch.zeros(rows, dtype=torch.long, device="cuda"),
+                  slot=torch.full((rows,), 1023, dtype=torch.long, device="cuda"),
+                  pos=torch.zeros(rows, dtype=torch.long, device="cuda"),
+                  kv_len=torch.full((rows,), 1024, dtype=torch.int32, device="cuda"),
+                  finished=torch.zeros(rows, dtype=torch.uint8, device="cuda"),
+                  out=torch.zeros(rows, 4096, dtype=torch.long, device="cuda"))
+        for top_p in (1.0, 0.9):
+            runs.append(lambda top_p=top_p: ext().sample_append(
+                logits, 1.0, top_p, 7, st["next_ids"], st["slot"], st["pos"], st["kv_len"], st["finished"],
+                st["out"], 1024, -1, 0, True, None))
     elif k == "gemm_mn":
         dy, w = torch.randn(8192, 24576, device="cuda").bfloat16(), torch.randn(24576, 4096, device="cuda").bfloat16()
         runs.append(lambda: gemm(dy, w, b_mn=True))
