@@ -14,6 +14,23 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              int64_t push_rows);
 void tp_reduce(torch::Tensor srcs, int64_t counter, int64_t expected, c10::optional<torch::Tensor> residual,
                torch::Tensor out, int64_t ld_src, torch::Tensor err, int64_t spin_limit);
+void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
+                               torch::Tensor block_table, torch::Tensor start, torch::Tensor len,
+                               torch::Tensor out, double scale, int64_t splits, torch::Tensor scratch,
+                               int64_t prefix_len, int64_t group_rows, int64_t prefix_splits,
+                               torch::Tensor err);
+void peer_copy(int64_t dst, torch::Tensor src, int64_t src_offset_bytes, int64_t nbytes);
+void signal_counters(torch::Tensor counters, int64_t count);
+void dp_reduce(torch::Tensor grads, torch::Tensor srcs, int64_t counter, int64_t expected, double scale,
+               torch::Tensor err, int64_t spin_limit);
+void conv_silu_fwd(torch::Tensor x, c10::optional<torch::Tensor> prev, torch::Tensor w, torch::Tensor y);
+void conv_silu_bwd(torch::Tensor x, c10::optional<torch::Tensor> prev, torch::Tensor w, torch::Tensor dy,
+                   torch::Tensor dx);
+void gated_rmsnorm_fwd(torch::Tensor x, torch::Tensor z, torch::Tensor w, torch::Tensor y, double eps);
+void gated_rmsnorm_bwd(torch::Tensor x, torch::Tensor z, torch::Tensor w, torch::Tensor dy, torch::Tensor dx,
+                       torch::Tensor dz, double eps);
+void sigmoid_gate_fwd(torch::Tensor o, torch::Tensor g, torch::Tensor y);
+void sigmoid_gate_bwd(torch::Tensor o, torch::Tensor g, torch::Tensor dy, torch::Tensor dout, torch::Tensor dg);
 void lse_push(torch::Tensor partials, torch::Tensor tgt, torch::Tensor dst, torch::Tensor sig, int64_t self);
 void lse_merge(torch::Tensor srcs, int64_t counter, int64_t expected, torch::Tensor lse, torch::Tensor logp,
                torch::Tensor err, int64_t spin_limit);
@@ -53,6 +70,13 @@ void paged_decode_attention(torch::Tensor q, torch::Tensor k_pool, torch::Tensor
                             torch::Tensor out, double scale, int64_t splits,
                             c10::optional<torch::Tensor> scratch, int64_t prefix_len, int64_t group_rows,
                             int64_t prefix_splits, c10::optional<torch::Tensor> err);
+void sample_append_split(torch::Tensor logits, double temperature, int64_t seed, torch::Tensor next_ids,
+                         torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len, torch::Tensor finished,
+                         torch::Tensor out_tokens, int64_t prompt_slots, int64_t eos_id, int64_t pad_id,
+                         bool ignore_eos, int64_t vocab_start, torch::Tensor scratch, int64_t chunk,
+                         torch::Tensor err, c10::optional<torch::Tensor> exch_dst,
+                         c10::optional<torch::Tensor> exch_sig, int64_t exch_self, int64_t exch_slots,
+                         int64_t exch_arrivals, int64_t spin_limit);
 void sample_append(torch::Tensor logits, double temperature, double top_p, int64_t seed,
                    torch::Tensor next_ids, torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len,
                    torch::Tensor finished, torch::Tensor out_tokens, int64_t prompt_slots,
@@ -84,6 +108,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "on the arrival counter",
         py::arg("srcs"), py::arg("counter"), py::arg("expected"), py::arg("residual"), py::arg("out"),
         py::arg("ld_src"), py::arg("err"), py::arg("spin_limit") = 0);
+  m.def("paged_decode_attention_tc", &gb::paged_decode_attention_tc,
+        "paged decode attention on tcgen05 / TMA: prompt keys once per group, per-row keys split, merged "
+        "by the last arriving CTA");
+  m.def("peer_copy", &gb::peer_copy, "copy-engine copy of a local byte range to a (peer) device address");
+  m.def("signal_counters", &gb::signal_counters, "add a count to peers' 64-bit arrival counters (release)");
+  m.def("dp_reduce", &gb::dp_reduce,
+        "data-parallel gradient sum in rank order times a scale, after a bounded wait on the arrival counter",
+        py::arg("grads"), py::arg("srcs"), py::arg("counter"), py::arg("expected"), py::arg("scale"), py::arg("err"),
+        py::arg("spin_limit") = 0);
+  m.def("conv_silu_fwd", &gb::conv_silu_fwd, "causal depthwise conv1d + SiLU, channels-last");
+  m.def("conv_silu_bwd", &gb::conv_silu_bwd, "input gradient of the causal conv1d + SiLU (frozen weight)");
+  m.def("gated_rmsnorm_fwd", &gb::gated_rmsnorm_fwd, "w * rmsnorm(x) * silu(z)");
+  m.def("gated_rmsnorm_bwd", &gb::gated_rmsnorm_bwd, "gradients of the gated RMSNorm for x and z");
+  m.def("sigmoid_gate_fwd", &gb::sigmoid_gate_fwd, "o * sigmoid(g)");
+  m.def("sigmoid_gate_bwd", &gb::sigmoid_gate_bwd, "gradients of o * sigmoid(g)");
   m.def("lse_push", &gb::lse_push,
         "vocab-parallel log-prob: this shard's (log-sum-exp, target logit) per token into every rank's slot");
   m.def("lse_merge", &gb::lse_merge,
@@ -119,6 +158,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_fwd_tc", &gb::flash_attn_fwd_tc, "causal flash attention forward on tcgen05 / TMEM");
   m.def("flash_attn_bwd_tc", &gb::flash_attn_bwd_tc, "causal flash attention backward on tcgen05 / TMEM");
   m.def("sample_append", &gb::sample_append);
+  m.def("sample_append_split", &gb::sample_append_split,
+        "Gumbel-max sampling over vocabulary chunks on every SM (top-p 1), optionally vocab-parallel with the "
+        "shards' winners exchanged through peer memory",
+        py::arg("logits"), py::arg("temperature"), py::arg("seed"), py::arg("next_ids"), py::arg("slot"),
+        py::arg("pos"), py::arg("kv_len"), py::arg("finished"), py::arg("out_tokens"), py::arg("prompt_slots"),
+        py::arg("eos_id"), py::arg("pad_id"), py::arg("ignore_eos"), py::arg("vocab_start"), py::arg("scratch"),
+        py::arg("chunk"), py::arg("err"), py::arg("exch_dst") = py::none(), py::arg("exch_sig") = py::none(),
+        py::arg("exch_self") = 0, py::arg("exch_slots") = 0, py::arg("exch_arrivals") = 0,
+        py::arg("spin_limit") = 0);
   m.def("lse_combine", &gb::lse_combine);
   m.def("grpo_loss", &gb::grpo_loss);
   m.def("dropout", &gb::dropout);

@@ -600,8 +600,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (args.npush > 0) {
               if (args.R != nullptr) {
                 const __nv_bfloat16* R = args.R + static_cast<long>(m) * args.ldr + nc;
-                for (int j = 0; j < 32; ++j)
-                  if (nc + j < args.N) v[j] += __bfloat162float(R[j]);
+                if (full_chunk) {
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    uint4 rv = *reinterpret_cast<const uint4*>(R + q * 8);
+                    const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[q * 8 + e] += __bfloat162float(rb[e]);
+                  }
+                } else {
+                  for (int j = 0; j < 32; ++j)
+                    if (nc + j < args.N) v[j] += __bfloat162float(R[j]);
+                }
               }
               push_chunk_bf16(args, m, nc, full_chunk, v);
               continue;

@@ -28,6 +28,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <algorithm>
+#include <cmath>
+
 #include "sm100_common.cuh"
 
 namespace gb {
@@ -220,6 +223,133 @@ __global__ void sample_append_kernel(SampleArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Split sampler (top-p = 1): the vocabulary of each row is cut into chunks, one
+// CTA per (chunk, row) draws the same Gumbel noise as sample_append (Philox
+// counter = global vocabulary index / 4, the row's cache slot and the row) and
+// keeps its chunk's best (key, index); the CTA that completes a row (arrival
+// counter) takes the best chunk.  With one vocabulary shard it then updates the
+// decode state; with several (vocab-parallel LM head), it stores the shard's
+// winner into every rank's exchange slot over NVLink and signals the peers, and
+// sample_exchange_kernel picks the best of all shards -- the same token on
+// every rank, without gathering the logits.
+struct SplitSampleArgs {
+  SampleArgs s;           // logits = this shard's [rows, V_local], V = V_local
+  int vocab_start;        // global index of this shard's first entry (a multiple of 4)
+  int chunk;              // entries per CTA (a multiple of 4)
+  int nchunks;
+  float2* part;           // [rows, nchunks]: (key, index as float bits)
+  int* counters;          // [rows], left at zero
+  // exchange (ntp > 1): this shard's winner -> slot `self` of every rank
+  float2* xdst[8];        // per rank: its exchange slots + rank `self`'s block ([rows] float2)
+  int* xsig[8];           // per rank: its arrival counters [rows] (nullptr for this rank)
+  int ntp, self;
+};
+
+__device__ __forceinline__ void sample_update(const SampleArgs& a, int row, int64_t best_i) {
+  const int64_t slot = a.slot[row];
+  const bool live = (a.active == nullptr || a.active[row]) && !a.finished[row];
+  const int64_t tok = live ? best_i : a.pad_id;
+  const int64_t col = slot + 1 - a.prompt_slots;
+  if (col >= 0 && col < a.max_new) a.out_tokens[static_cast<long>(row) * a.max_new + col] = tok;
+  if (live && !a.ignore_eos && tok == a.eos_id) a.finished[row] = 1;
+  a.next_ids[row] = tok;
+  a.slot[row] = slot + 1;
+  a.pos[row] = a.pos[row] + 1;
+  a.kv_len[row] = static_cast<int>(slot + 2);
+}
+
+__global__ void __launch_bounds__(256) sample_chunk_kernel(SplitSampleArgs x) {
+  const SampleArgs& a = x.s;
+  const int c = blockIdx.x, row = blockIdx.y;
+  __shared__ int last;
+  pdl_wait();
+  const float* lg = a.logits + static_cast<long>(row) * a.ld;
+  const int64_t slot = a.slot[row];
+  const int v0 = c * x.chunk, v1 = min(a.V, v0 + x.chunk);
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int v4 = v0 + 4 * threadIdx.x; v4 < v1; v4 += 4 * blockDim.x) {
+    const int g4 = x.vocab_start + v4;  // global index of the group's first entry
+    U4 r{0, 0, 0, 0};
+    if (a.inv_temp > 0.f) {
+      r = philox4x32_10(U4{static_cast<uint32_t>(g4 >> 2), static_cast<uint32_t>(slot), static_cast<uint32_t>(row),
+                           0x5A3F1u},
+                        a.seed_lo, a.seed_hi);
+    }
+    const uint32_t bits[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int v = v4 + e;
+      if (v >= v1) break;
+      const float key = a.inv_temp > 0.f ? lg[v] * a.inv_temp + gumbel(bits[e]) : lg[v];
+      best = better(best, ArgMax{key, x.vocab_start + v});
+    }
+  }
+  best = block_argmax(best);
+  if (threadIdx.x == 0) {
+    x.part[static_cast<long>(row) * x.nchunks + c] = make_float2(best.v, __int_as_float(best.i));
+    __threadfence();
+    const int prev = atomicAdd(x.counters + row, 1);
+    last = prev == x.nchunks - 1;
+    if (last) x.counters[row] = 0;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  ArgMax w{-INFINITY, 0x7fffffff};
+  for (int k = 0; k < x.nchunks; ++k) {
+    const float2 p = __ldcg(x.part + static_cast<long>(row) * x.nchunks + k);
+    w = better(w, ArgMax{p.x, __float_as_int(p.y)});
+  }
+  if (x.ntp <= 1) {
+    sample_update(a, row, w.i);
+    return;
+  }
+  const float2 mine = make_float2(w.v, __int_as_float(w.i));
+  for (int q = 0; q < x.ntp; ++q) x.xdst[q][row] = mine;
+  __threadfence_system();
+  for (int q = 0; q < x.ntp; ++q)
+    if (x.xsig[q] != nullptr) asm volatile("red.release.sys.global.add.s32 [%0], 1;" ::"l"(x.xsig[q] + row) : "memory");
+}
+
+// One thread per row: bounded wait for the other shards' winners, the best of
+// all shards (ties -> smaller index, as in a single full-vocabulary pass), the
+// decode-state update, and the arrival counter back to zero for the next step.
+struct ExchangeArgs {
+  SampleArgs s;
+  const float2* slots;   // this rank's [ntp, rows] exchange slots
+  int* arrivals;         // this rank's [rows] counters
+  int ntp, rows;
+  int* err;
+  long long spin_limit;
+};
+
+__global__ void sample_exchange_kernel(ExchangeArgs x) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (row >= x.rows) return;
+  const long long t0 = clock64();
+  bool ok = true;
+  for (;;) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(x.arrivals + row) : "memory");
+    if (v >= x.ntp - 1) break;
+    if (clock64() - t0 > x.spin_limit) {
+      record_error(x.err, kErrPeerTimeout);
+      ok = false;
+      break;
+    }
+    __nanosleep(64);
+  }
+  ArgMax w{-INFINITY, 0x7fffffff};
+  for (int q = 0; q < x.ntp; ++q) {
+    const float2 p = __ldcg(x.slots + static_cast<long>(q) * x.rows + row);
+    w = better(w, ArgMax{p.x, __float_as_int(p.y)});
+  }
+  if (ok) x.arrivals[row] = 0;
+  sample_update(x.s, row, ok ? w.i : x.s.pad_id);
+}
+
 // one warp per token
 __global__ void lse_combine_kernel(const float2* __restrict__ part, long ld, int nblk,
                                    const float* __restrict__ tgt, float* __restrict__ lse,
@@ -298,23 +428,60 @@ __global__ void grpo_loss_kernel(const float* __restrict__ logp, const float* __
   }
 }
 
-// y = (add ? add : 0) + x * mask / (1 - p)
+// y = (add ? add : 0) + x * mask / (1 - p).  One Philox4x32-10 draw per 8
+// elements: each 32-bit output word supplies two 16-bit uniforms, and an element
+// is kept when its uniform is >= round(p * 2^16) (keep probability within 2^-17
+// of 1 - p).  Threads move 16-byte vectors (8 bf16); the mask of element i
+// depends only on (seed, stream_id, i), so the backward recomputes the forward's
+// mask exactly.  Any tail of n % 8 elements goes through the same draw.
 __global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* y,
-                               const __nv_bfloat16* add, long n, float p, uint32_t seed_lo,
-                               uint32_t seed_hi, uint32_t stream_id) {
-  const long q = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x;  // group of 4
-  if (q * 4 >= n) return;
-  const U4 r = philox4x32_10(U4{static_cast<uint32_t>(q), static_cast<uint32_t>(q >> 32), stream_id, 0xD0u},
-                             seed_lo, seed_hi);
-  const uint32_t bits[4] = {r.x, r.y, r.z, r.w};
-  const float keep = 1.f / (1.f - p);
+                               const __nv_bfloat16* add, long n, uint32_t thresh16, float keep_scale,
+                               uint32_t seed_lo, uint32_t seed_hi, uint32_t stream_id) {
+  const long groups = (n + 7) / 8;
+  for (long q = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; q < groups;
+       q += static_cast<long>(gridDim.x) * blockDim.x) {
+    const U4 r = philox4x32_10(U4{static_cast<uint32_t>(q), static_cast<uint32_t>(q >> 32), stream_id, 0xD1u},
+                               seed_lo, seed_hi);
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+    const long i0 = q * 8;
+    float v[8];
+    const bool full = i0 + 8 <= n;
+    if (full) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(x + i0);
+      const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const long i = q * 4 + e;
-    if (i < n) {
-      float val = u01(bits[e]) >= p ? __bfloat162float(x[i]) * keep : 0.f;
-      if (add != nullptr) val += __bfloat162float(add[i]);
-      y[i] = __float2bfloat16(val);
+      for (int e = 0; e < 8; ++e) v[e] = __bfloat162float(b[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = i0 + e < n ? __bfloat162float(x[i0 + e]) : 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t u16 = (w[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
+      v[e] = u16 >= thresh16 ? v[e] * keep_scale : 0.f;
+    }
+    if (add != nullptr) {
+      if (full) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(add + i0);
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] += __bfloat162float(b[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (i0 + e < n) v[e] += __bfloat162float(add[i0 + e]);
+      }
+    }
+    if (full) {
+      uint4 pk;
+      __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+      *reinterpret_cast<uint4*>(y + i0) = pk;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (i0 + e < n) y[i0 + e] = __float2bfloat16(v[e]);
     }
   }
 }
@@ -389,6 +556,80 @@ void sample_append(torch::Tensor logits, double temperature, double top_p, int64
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Split sampler (temperature > 0 or greedy, no nucleus): see sample_chunk_kernel.
+// scratch: int32 [rows] counters (zeroed once, left zeroed) followed by fp32
+// [rows * nchunks * 2] partials.  exch_dst / exch_sig: CPU int64 tables (one
+// entry per rank) for the vocab-parallel exchange; exch_slots / exch_arrivals:
+// this rank's own exchange slots and counters.
+void sample_append_split(torch::Tensor logits, double temperature, int64_t seed, torch::Tensor next_ids,
+                         torch::Tensor slot, torch::Tensor pos, torch::Tensor kv_len, torch::Tensor finished,
+                         torch::Tensor out_tokens, int64_t prompt_slots, int64_t eos_id, int64_t pad_id,
+                         bool ignore_eos, int64_t vocab_start, torch::Tensor scratch, int64_t chunk,
+                         torch::Tensor err, c10::optional<torch::Tensor> exch_dst,
+                         c10::optional<torch::Tensor> exch_sig, int64_t exch_self, int64_t exch_slots,
+                         int64_t exch_arrivals, int64_t spin_limit) {
+  const c10::cuda::CUDAGuard guard(logits.device());
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.stride(1) == 1, "logits must be fp32 row-major");
+  TORCH_CHECK(vocab_start % 4 == 0 && chunk % 4 == 0 && chunk > 0, "vocab_start and chunk must be multiples of 4");
+  SplitSampleArgs x{};
+  SampleArgs& a = x.s;
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.V = static_cast<int>(logits.size(1));
+  a.inv_temp = temperature > 0 ? static_cast<float>(1.0 / std::max(temperature, 1e-6)) : 0.f;
+  a.top_p = 1.f;
+  a.seed_lo = static_cast<uint32_t>(seed & 0xffffffff);
+  a.seed_hi = static_cast<uint32_t>((seed >> 32) & 0xffffffff);
+  a.next_ids = next_ids.data_ptr<int64_t>();
+  a.slot = slot.data_ptr<int64_t>();
+  a.pos = pos.data_ptr<int64_t>();
+  a.kv_len = kv_len.data_ptr<int>();
+  a.finished = finished.data_ptr<uint8_t>();
+  a.out_tokens = out_tokens.data_ptr<int64_t>();
+  a.max_new = static_cast<int>(out_tokens.size(1));
+  a.prompt_slots = prompt_slots;
+  a.eos_id = eos_id;
+  a.pad_id = pad_id;
+  a.ignore_eos = ignore_eos ? 1 : 0;
+  const int rows = static_cast<int>(logits.size(0));
+  if (rows == 0) return;
+  x.vocab_start = static_cast<int>(vocab_start);
+  x.chunk = static_cast<int>(chunk);
+  x.nchunks = (a.V + x.chunk - 1) / x.chunk;
+  TORCH_CHECK(scratch.is_cuda() && scratch.scalar_type() == torch::kFloat32 &&
+                  scratch.numel() >= static_cast<long>(rows) * (1 + 2L * x.nchunks),
+              "sampler scratch: fp32 with rows * (1 + 2 * chunks) entries");
+  x.counters = reinterpret_cast<int*>(scratch.data_ptr<float>());
+  x.part = reinterpret_cast<float2*>(scratch.data_ptr<float>() + ((rows + 1) / 2) * 2);
+  x.ntp = 1;
+  if (exch_dst.has_value() && exch_dst->defined()) {
+    TORCH_CHECK(exch_sig.has_value() && exch_dst->device().is_cpu() && exch_sig->device().is_cpu() &&
+                    exch_dst->numel() == exch_sig->numel() && exch_dst->numel() <= 8,
+                "exchange tables: CPU int64, one entry per rank (<= 8)");
+    x.ntp = static_cast<int>(exch_dst->numel());
+    x.self = static_cast<int>(exch_self);
+    auto d = exch_dst->contiguous(), g = exch_sig->contiguous();
+    for (int q = 0; q < x.ntp; ++q) {
+      x.xdst[q] = reinterpret_cast<float2*>(d.data_ptr<int64_t>()[q]);
+      x.xsig[q] = reinterpret_cast<int*>(g.data_ptr<int64_t>()[q]);
+    }
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(launch_kernel(sample_chunk_kernel, dim3(x.nchunks, rows), dim3(256), 0, stream, x));
+  if (x.ntp > 1) {
+    ExchangeArgs e{};
+    e.s = a;
+    e.slots = reinterpret_cast<const float2*>(exch_slots);
+    e.arrivals = reinterpret_cast<int*>(exch_arrivals);
+    e.ntp = x.ntp;
+    e.rows = rows;
+    e.err = err.data_ptr<int>();
+    e.spin_limit = spin_limit > 0 ? spin_limit : 10 * kSpinLimitCycles;
+    C10_CUDA_CHECK(launch_kernel(sample_exchange_kernel, dim3((rows + 127) / 128), dim3(128), 0, stream, e));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void lse_combine(torch::Tensor partials, torch::Tensor tgt, torch::Tensor lse, torch::Tensor logp) {
   const c10::cuda::CUDAGuard guard(partials.device());
   TORCH_CHECK(partials.scalar_type() == torch::kFloat32 && partials.dim() == 3 && partials.size(2) == 2,
@@ -428,11 +669,23 @@ void dropout(torch::Tensor x, torch::Tensor y, double p, int64_t seed, int64_t s
   TORCH_CHECK(x.is_contiguous() && y.is_contiguous(), "dropout tensors must be contiguous");
   const long n = x.numel();
   if (n == 0) return;
-  const long groups = (n + 3) / 4;
-  dropout_kernel<<<(groups + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && y.scalar_type() == torch::kBFloat16 && y.numel() == n,
+              "dropout takes bf16 tensors of equal size");
+  const bool has_add = add.has_value() && add->defined();
+  if (has_add) TORCH_CHECK(add->is_contiguous() && add->numel() == n && add->scalar_type() == torch::kBFloat16,
+                           "dropout add must match x");
+  for (const void* ptr : {x.data_ptr(), y.data_ptr(), has_add ? add->data_ptr() : x.data_ptr()})
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "dropout tensors must be 16-byte aligned");
+  TORCH_CHECK(p >= 0.0 && p < 1.0, "dropout probability must be in [0, 1)");
+  const long groups = (n + 7) / 8;
+  const uint32_t thresh16 = static_cast<uint32_t>(std::lround(p * 65536.0));
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.get_device());
+  const int blocks = static_cast<int>(std::min<long>((groups + 255) / 256, 16L * sms));
+  dropout_kernel<<<std::max(blocks, 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
-      (add.has_value() && add->defined()) ? reinterpret_cast<const __nv_bfloat16*>(add->data_ptr()) : nullptr, n,
-      static_cast<float>(p), static_cast<uint32_t>(seed & 0xffffffff),
+      has_add ? reinterpret_cast<const __nv_bfloat16*>(add->data_ptr()) : nullptr, n, thresh16,
+      static_cast<float>(1.0 / (1.0 - p)), static_cast<uint32_t>(seed & 0xffffffff),
       static_cast<uint32_t>((seed >> 32) & 0xffffffff), static_cast<uint32_t>(stream_id));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -203,7 +203,140 @@ __global__ void lse_merge_kernel(PairMergeArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Data-parallel LoRA-gradient all-reduce.  During the backward each layer's
+// finished gradient slices are copied into every DP peer's receive slot by the
+// copy engines on a side stream (cudaMemcpyAsync to the CUDA-IPC mapped
+// address, overlapping the remaining layers' backward), followed by
+// signal_kernel, which adds the copied element count to the peers' 64-bit
+// arrival counters.  dp_reduce_kernel then waits (bounded) for all peers'
+// slices and writes g = scale * sum over ranks of g_q, in rank order (this
+// rank's own term read from its gradient buffer), so every DP replica holds the
+// same bits.
+struct SignalArgs {
+  unsigned long long* ctr[kMaxRanks];
+  int n;
+  unsigned long long count;
+};
+
+__global__ void signal_kernel(SignalArgs a) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  for (int q = 0; q < a.n; ++q)
+    if (a.ctr[q] != nullptr)
+      asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(a.ctr[q]), "l"(a.count) : "memory");
+}
+
+struct DPReduceArgs {
+  float* grads;                     // this rank's gradients (its own term, overwritten with the result)
+  const float* src[kMaxRanks];      // per rank: receive slot, or nullptr for this rank
+  int nranks;
+  long n;
+  float scale;
+  const unsigned long long* counter;
+  unsigned long long expected;
+  int* err;
+  long long spin_limit;
+};
+
+__global__ void __launch_bounds__(256) dp_reduce_kernel(DPReduceArgs a) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    int good = 1;
+    const long long t0 = clock64();
+    while (ld_acquire_sys_u64(a.counter) < a.expected) {
+      if (clock64() - t0 > a.spin_limit) {
+        record_error(a.err, kErrPeerTimeout);
+        good = 0;
+        break;
+      }
+      __nanosleep(128);
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const long n4 = a.n / 4;
+  for (long i = blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = 0; q < a.nranks; ++q) {
+      const float4 v = a.src[q] != nullptr ? __ldcg(reinterpret_cast<const float4*>(a.src[q]) + i)
+                                           : reinterpret_cast<const float4*>(a.grads)[i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(a.grads)[i] =
+        make_float4(acc.x * a.scale, acc.y * a.scale, acc.z * a.scale, acc.w * a.scale);
+  }
+  for (long i = n4 * 4 + blockIdx.x * static_cast<long>(blockDim.x) + threadIdx.x; i < a.n;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int q = 0; q < a.nranks; ++q) acc += a.src[q] != nullptr ? __ldcg(a.src[q] + i) : a.grads[i];
+    a.grads[i] = acc * a.scale;
+  }
+}
+
 }  // namespace
+
+// Copy `nbytes` from a local tensor (at a byte offset) to a device address on
+// the current stream -- a CUDA-IPC mapped peer buffer -- with the copy engines.
+void peer_copy(int64_t dst, torch::Tensor src, int64_t src_offset_bytes, int64_t nbytes) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "peer_copy source must be a contiguous CUDA tensor");
+  TORCH_CHECK(src_offset_bytes >= 0 && nbytes >= 0 &&
+                  src_offset_bytes + nbytes <= static_cast<int64_t>(src.numel() * src.element_size()),
+              "peer_copy range outside the source");
+  if (nbytes == 0) return;
+  const c10::cuda::CUDAGuard guard(src.device());
+  C10_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<void*>(dst),
+                                 static_cast<const uint8_t*>(src.data_ptr()) + src_offset_bytes,
+                                 static_cast<size_t>(nbytes), cudaMemcpyDeviceToDevice,
+                                 at::cuda::getCurrentCUDAStream()));
+}
+
+// Add `count` to each 64-bit counter of the CPU int64 address table (0 entries are skipped).
+void signal_counters(torch::Tensor counters, int64_t count) {
+  TORCH_CHECK(counters.device().is_cpu() && counters.scalar_type() == torch::kInt64 && counters.numel() <= kMaxRanks,
+              "counters: CPU int64 address table of <= 8 entries");
+  SignalArgs a{};
+  auto c = counters.contiguous();
+  a.n = static_cast<int>(c.numel());
+  for (int q = 0; q < a.n; ++q) a.ctr[q] = reinterpret_cast<unsigned long long*>(c.data_ptr<int64_t>()[q]);
+  a.count = static_cast<unsigned long long>(count);
+  signal_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_CHECK(cudaGetLastError());
+}
+
+// grads = scale * sum_q slot_q in rank order (srcs[q] == 0 for this rank: its grads), after a
+// bounded wait until this rank's counter reaches `expected`.
+void dp_reduce(torch::Tensor grads, torch::Tensor srcs, int64_t counter, int64_t expected, double scale,
+               torch::Tensor err, int64_t spin_limit) {
+  TORCH_CHECK(grads.is_cuda() && grads.scalar_type() == torch::kFloat32 && grads.is_contiguous(),
+              "grads must be a contiguous fp32 CUDA tensor");
+  TORCH_CHECK(srcs.device().is_cpu() && srcs.scalar_type() == torch::kInt64 && srcs.numel() >= 1 &&
+                  srcs.numel() <= kMaxRanks, "srcs: CPU int64 table of 1..8 addresses");
+  const c10::cuda::CUDAGuard guard(grads.device());
+  DPReduceArgs a{};
+  a.grads = grads.data_ptr<float>();
+  auto s = srcs.contiguous();
+  a.nranks = static_cast<int>(s.numel());
+  for (int q = 0; q < a.nranks; ++q) {
+    a.src[q] = reinterpret_cast<const float*>(s.data_ptr<int64_t>()[q]);
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(a.src[q]) % 16 == 0, "16-byte aligned slots");
+  }
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.grads) % 16 == 0, "16-byte aligned gradients");
+  a.n = grads.numel();
+  a.scale = static_cast<float>(scale);
+  a.counter = reinterpret_cast<const unsigned long long*>(counter);
+  a.expected = static_cast<unsigned long long>(expected);
+  a.err = err.data_ptr<int>();
+  a.spin_limit = spin_limit > 0 ? spin_limit : 10 * kSpinLimitCycles;
+  if (a.n == 0) return;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, grads.get_device());
+  const int blocks = static_cast<int>(std::min<long>((a.n / 4 + 255) / 256 + 1, 8L * sms));
+  dp_reduce_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_CHECK(cudaGetLastError());
+}
 
 // Vocab-parallel log-prob exchange, producer half (see lse_push_kernel).
 void lse_push(torch::Tensor partials, torch::Tensor tgt, torch::Tensor dst, torch::Tensor sig, int64_t self) {

@@ -156,6 +156,58 @@ def bench_decode(args) -> None:
         }), flush=True)
 
 
+def bench_attn(args) -> None:
+    """Decode attention on the GRASPO shape: ``--prompts`` groups of ``--group`` rows sharing a
+    ``--prompt-len`` prompt, each row with ``--new`` generated keys (32 / 8 heads, page 64).
+
+    Times the mma.sync split kernel (prompt keys re-read per row) and the tcgen05 / TMA kernel
+    (prompt keys once per group), with the bytes each must read and the fraction of the measured
+    HBM copy rate."""
+    from graspo_b200.engine.rollout import decode_attention_splits, decode_tc_splits
+    from graspo_b200.ops._ext import check_errors, err_word, ext
+
+    peaks = measured_peaks()
+    timer = Timer(iters=args.iters)
+    nq, nkv, D, page = 32, 8, 128, 64
+    n, G, P, gen = args.prompts, args.group, args.prompt_len, args.new
+    rows = n * G
+    pp, gp = P // page, -(-gen // page)
+    num_pages = n * pp + rows * gp
+    kp = torch.randn(num_pages, nkv, page, D, device="cuda").bfloat16()
+    vp = torch.randn_like(kp)
+    bt = torch.empty(rows, pp + gp, dtype=torch.int32)
+    for r in range(rows):
+        bt[r, :pp] = torch.arange((r // G) * pp, (r // G + 1) * pp)
+        bt[r, pp:] = torch.arange(n * pp + r * gp, n * pp + (r + 1) * gp)
+    bt = bt.cuda()
+    q = torch.randn(rows, nq, D, device="cuda").bfloat16()
+    start = torch.zeros(rows, device="cuda", dtype=torch.int32)
+    ln = torch.full((rows,), P + gen, device="cuda", dtype=torch.int32)
+    out = torch.empty(rows, nq * D, device="cuda", dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(D)
+    kv_row = nkv * D * 2 * 2  # K and V bytes per key position
+    bytes_per_row = rows * (P + gen) * kv_row
+    bytes_shared = (n * P + rows * gen) * kv_row
+    splits = decode_attention_splits(rows, nkv, P + gp * page)
+    scr = torch.zeros(rows * nq * splits * (D + 2) + rows * nkv, device="cuda")
+    old = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, scale, splits, scr))
+    ref = out.clone()
+    sp, psp = decode_tc_splits(rows, nkv, gp * page, n, P)
+    scr2 = torch.zeros(rows * nq * (sp + psp) * (D + 2) + rows * nkv, device="cuda")
+    ew = err_word(q.device)
+    new = timer(lambda: ext().paged_decode_attention_tc(q, kp, vp, bt, start, ln, out, scale, sp, scr2, P, G, psp,
+                                                        ew))
+    check_errors()
+    err = (out.float() - ref.float()).abs().max().item()
+    for name, ms, nbytes in (("split_mma_sync", old, bytes_per_row), ("tcgen05_shared_prompt", new, bytes_shared)):
+        print(json.dumps({
+            "kernel": name, "rows": rows, "prompt": P, "generated": gen, "ms": round(ms, 4),
+            "bytes": nbytes, "GBps": round(nbytes / ms / 1e6, 1),
+            "frac_of_measured_hbm": round(nbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
+            "floor_ms_shared": round(bytes_shared / peaks["hbm_gbs"] / 1e6, 4), "max_abs_diff": err,
+        }), flush=True)
+
+
 def bench_step(args) -> None:
     from graspo_b200.engine.rollout import FusedRolloutEngine
     from graspo_b200.models.fused import FusedQwen3
@@ -389,7 +441,7 @@ def bench_profile(args) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "step", "train", "profile", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "attn", "step", "train", "profile", "all"])
     parser.add_argument("--kernel", default="gemm")
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
@@ -408,6 +460,8 @@ def main() -> None:
         bench_gemm(args)
     if args.what in ("decode", "all"):
         bench_decode(args)
+    if args.what == "attn":
+        bench_attn(args)
     if args.what == "step":
         bench_step(args)
     if args.what == "train":

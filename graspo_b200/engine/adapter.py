@@ -520,7 +520,7 @@ class Qwen3Adapter:
         dxL = torch.empty_like(xL)
         ext().rmsnorm_bwd(dhn, xL, self.model.norm, rstd, None, dxL, self.model.cfg.rms_norm_eps)
         del dhn
-        self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed)
+        self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed, on_layer_done=self._dp_layer_hook())
 
     # ------------------------------------------------------------ training
     def check_replicas(self) -> None:
@@ -537,10 +537,34 @@ class Qwen3Adapter:
         if bad:
             raise RuntimeError("replicated LoRA state diverged: " + "; ".join(bad))
 
+    def _dp_reducer(self):
+        """The overlapped peer-memory DP gradient all-reduce (CUDA, DP > 1, fused
+        path without pipeline stages); None where a library all-reduce is used."""
+        ps = self.ps
+        if not (ps.dp_size > 1 and ps.distributed and self.device.type == "cuda" and self.fused
+                and ps.pp_size == 1):
+            return None
+        red = getattr(self, "_dp_red", None)
+        if red is None:
+            from graspo_b200.parallel.symm import DPGradReduce
+
+            red = self._dp_red = DPGradReduce(self.model.lora.numel, ps.dp_group, self.device)
+        return red
+
+    def _dp_layer_hook(self):
+        red = self._dp_reducer()
+        if red is None:
+            return None
+        lora = self.model.lora
+        return lambda layer: red.push(lora.grads, lora.layer_ranges(layer))
+
     def _dp_average_grads(self) -> None:
         ps = self.ps
         g = self.model.lora.grads
-        if ps.dp_size > 1 and ps.distributed:
+        red = self._dp_reducer()
+        if red is not None:
+            red.finish(g)
+        elif ps.dp_size > 1 and ps.distributed:
             dist.all_reduce(g, group=ps.dp_group)
             g.div_(ps.dp_size)
 
@@ -648,8 +672,10 @@ class Qwen3Adapter:
                 hook = self._image_hook(media_rows) if any(media_rows) else None
                 loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed, embed_hook=hook)
                 with clock.time("grad_sync_sec"):
-                    self._tp_sync_replicated_grads()
+                    # both are sums (they commute); the DP slices were already sent
+                    # layer by layer during the backward
                     self._dp_average_grads()
+                    self._tp_sync_replicated_grads()
                 with clock.time("optimizer_step_sec"):
                     norm = self.optimizer.step(max_grad_norm, loss)
                 losses.append(loss)

@@ -83,6 +83,24 @@ def decode_attention_splits(rows: int, nkv: int, capacity: int, sms: int = 148) 
     return int(max(1, min(want, capacity // 256, 16)))
 
 
+def decode_tc_splits(rows: int, nkv: int, gen_capacity: int, groups: int, prompt: int,
+                     sms: int = 148) -> tuple[int, int]:
+    """(row splits, prompt splits) of the tcgen05 decode attention.
+
+    Row units (one per row, KV head and split) take at most 16 key tiles (1024
+    keys) of a row's own keys and are at least two per SM; prompt units (one
+    per group, KV head and split) together fill the SMs once, with at least
+    four tiles each."""
+    tiles = max(1, -(-gen_capacity // 64))
+    units = max(1, rows * nkv)
+    splits = max(-(-tiles // 16), -(-2 * sms // units))
+    splits = int(max(1, min(splits, tiles, 16)))
+    psplits = 1
+    if prompt > 0:
+        psplits = int(max(1, min(round(sms / max(1, groups * nkv)), prompt // 256, 8)))
+    return splits, psplits
+
+
 def swap_gemm_splits(out_features: int, rows: int, sms: int = 148, max_splits: int = 4) -> int:
     """Split-K factor for a swap-layout decode GEMM: the fewest splits that
     minimise the time of the last wave (units = 128-feature tiles x splits,
@@ -137,8 +155,10 @@ class FusedRolloutEngine:
         # the tokens to its column (no CUDA graph across the p2p boundary)
         self.comm = comm if (comm is not None and comm.active) else None
         # attend the prompt keys once per group (shared-prefix kernel).  Off by
-        # default: with the current split kernel its fixed per-CTA cost outweighs
-        # the saved prompt reads at 1k-3k keys; True runs it
+        # default: the rows of a group run next to each other, so the prompt pages
+        # they share are read from DRAM once and served from L2, and the
+        # one-launch split kernel measured faster than both shared-prompt variants
+        # (the mma.sync prefix + split pair and the tcgen05 kernel with prompt units)
         self.prefix_attention = False
 
     def _ensure_pool(self, num_pages: int) -> None:
@@ -163,16 +183,42 @@ class FusedRolloutEngine:
         dist.all_gather_into_tensor(parts, local.contiguous(), group=ps.tp_group)
         return parts.permute(1, 0, 2).reshape(local.shape[0], -1).contiguous()
 
-    def _lm_logits(self, xn: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def _lm_local(self, xn: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """fp32 logits of this rank's vocabulary shard [rows, vocab / tp]."""
         from graspo_b200.ops.gemm import gemm
 
         m = self.m
-        rows = xn.shape[0]
-        if rows <= 128:
-            local = gemm(m.lm_head, xn, out, swap=True, epilogue="store_f32")
-        else:
-            local = gemm(xn, m.lm_head, out, epilogue="store_f32")
-        return self._vocab_gather(local)
+        if xn.shape[0] <= 128:
+            return gemm(m.lm_head, xn, out, swap=True, epilogue="store_f32")
+        return gemm(xn, m.lm_head, out, epilogue="store_f32")
+
+    def _lm_logits(self, xn: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        return self._vocab_gather(self._lm_local(xn, out))
+
+    def _sampler_plan(self, rows: int, top_p: float) -> None:
+        """Split sampler (every SM, no nucleus restriction): with a vocab-parallel
+        head the shards' winners are exchanged through peer memory instead of
+        gathering the logits.  Nucleus sampling keeps the single-pass sampler
+        over the gathered logits."""
+        m = self.m
+        self._split_sample = m.device.type == "cuda" and m.include_head and top_p >= 1.0 and (
+            m.ps.tp_size == 1 or self.fused_tp)
+        self._sx = None
+        if not self._split_sample:
+            return
+        want = max(1, -(-4 * 148 // max(1, rows)))
+        self._samp_chunk = _round_up(-(-m.vocab_local // want), 4)
+        if m.ps.tp_size > 1:
+            key = ("sample", rows, 0)
+            sx = self._peer_sites.get(key)
+            if sx is None:
+                from graspo_b200.parallel.symm import SampleExchange
+
+                for k in [k for k in self._peer_sites if k[0] == "sample"]:
+                    self._peer_sites.pop(k).close()
+                sx = SampleExchange(rows, m.ps.tp_group, m.device)
+                self._peer_sites[key] = sx
+            self._sx = sx
 
     @torch.no_grad()
     def generate(
@@ -294,6 +340,10 @@ class FusedRolloutEngine:
         slots = self._splits + (self._prefix_splits if self._prefix else 0)
         bufs["attn_scratch"] = torch.zeros(rows * m.nq * slots * (m.D + 2) + rows * m.nkv,
                                            device=dev, dtype=torch.float32)
+        self._sampler_plan(rows, top_p)
+        if self._split_sample:
+            nch = -(-m.vocab_local // self._samp_chunk)
+            bufs["samp_scratch"] = torch.zeros(rows * (1 + 2 * nch) + 2, device=dev, dtype=torch.float32)
         row_ids = torch.arange(rows, dtype=torch.long, device=dev)
 
         def step() -> None:
@@ -538,9 +588,17 @@ class FusedRolloutEngine:
                           b_down_prev, r if b_down_prev is not None else 0, **d_norm)
         else:
             C.add_rmsnorm(b["x_a"], None, None, m.norm, b["xn"], None, None, None, 1.0, eps)
-        logits = self._lm_logits(b["xn"], b["logits"])
-        C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"], st["pos"],
-                        st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos), None)
+        if self._split_sample:
+            local = self._lm_local(b["xn"], b["logits"])
+            C.sample_append_split(local, float(temperature), int(seed), st["next_ids"], st["slot"], st["pos"],
+                                  st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos),
+                                  m.vocab_start, b["samp_scratch"], self._samp_chunk, ew["err"],
+                                  **(self._sx.kwargs() if self._sx is not None else {}))
+        else:
+            logits = self._lm_logits(b["xn"], b["logits"])
+            C.sample_append(logits, float(temperature), float(top_p), int(seed), st["next_ids"], st["slot"],
+                            st["pos"], st["kv_len"], st["finished"], st["out"], P, eos_id, pad_id, bool(ignore_eos),
+                            None)
         self._sync_stages(st)
 
 

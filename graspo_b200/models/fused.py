@@ -472,11 +472,13 @@ class FusedQwen3:
                 inputs.append((x_in, keep))
         return x, inputs
 
-    def stage_backward(self, inputs, dout: torch.Tensor, meta: AttnMeta, *, train=True, seed=0):
+    def stage_backward(self, inputs, dout: torch.Tensor, meta: AttnMeta, *, train=True, seed=0,
+                       on_layer_done=None):
         """Recompute-and-backprop through this rank's layers; returns d(input).
 
         ``inputs`` (from ``stage_forward``) is consumed: each layer's entry is
-        released once its backward ran."""
+        released once its backward ran.  ``on_layer_done(layer)`` runs after a
+        layer's LoRA gradients are complete (the data-parallel gradient push)."""
         g = dout
         for lw in reversed(self.m.layers):
             x, cache = inputs.pop()
@@ -485,6 +487,8 @@ class FusedQwen3:
             del x, cache
             g = self.layer_backward(lw, saved, g, meta, train=train, seed=seed)
             del saved
+            if on_layer_done is not None:
+                on_layer_done(lw.index)
         if inputs:
             raise ValueError("stage_backward: more saved inputs than local layers")
         return g
@@ -510,7 +514,8 @@ class FusedQwen3:
         red = self.tp_reducer()
         if red is not None:
             # vocab shards merged through peer memory (no library collective)
-            return red.lse_exchange(part, tl)
+            lse, logp = red.lse_exchange(part, tl)
+            return logp, lse
         lse = torch.empty(T, device=h.device, dtype=torch.float32)
         logp = torch.empty(T, device=h.device, dtype=torch.float32)
         self.C.lse_combine(part, tl, lse, logp)

@@ -114,6 +114,25 @@ class LoRAAdapter:
         self.by_name = {m.module_name: m for m in modules}
         self.layouts: dict[int, dict[str, torch.Tensor]] = {}
 
+    def layer_ranges(self, layer: int) -> list[tuple[int, int]]:
+        """(start, count) ranges of the flat buffer that hold one layer's factors,
+        adjacent ranges merged (a layer's factors sit in the replicated and in the
+        sharded part of the buffer)."""
+        spans = []
+        for mod in self.modules:
+            if mod.layer != layer:
+                continue
+            spans.append((mod.offset_a, self.r * mod.in_local))
+            spans.append((mod.offset_b, mod.out_local * self.r))
+        spans.sort()
+        merged: list[list[int]] = []
+        for start, count in spans:
+            if merged and merged[-1][0] + merged[-1][1] == start:
+                merged[-1][1] += count
+            else:
+                merged.append([start, count])
+        return [(a, b) for a, b in merged]
+
     def _bind(self, mod: LoRAModule) -> None:
         a_n = self.r * mod.in_local
         b_n = mod.out_local * self.r

@@ -40,6 +40,7 @@ from graspo_b200.models.config import DecoderConfig
 from graspo_b200.models.loader import SafetensorIndex
 from graspo_b200.models.lora import LoRAAdapter, LoRAModule
 from graspo_b200.models.qwen3 import EagerLoRA
+from graspo_b200.ops.hybrid import conv_silu, sigmoid_gate
 from graspo_b200.parallel.state import ParallelState
 from graspo_b200.parallel.tp import copy_to_tp, reduce_from_tp
 
@@ -54,9 +55,10 @@ def norm1p(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def gated_norm(x: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    xf = x.float()
-    y = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
-    return (w * y * F.silu(z.float())).to(x.dtype)
+    """w * rmsnorm(x) * silu(z); one kernel each way on CUDA (graspo_b200/ops/hybrid.py)."""
+    from graspo_b200.ops.hybrid import gated_rmsnorm
+
+    return gated_rmsnorm(x, z, w, eps)
 
 
 def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
@@ -397,7 +399,7 @@ class Qwen35Model:
         allowed = allowed | (qpos[:, None] == kpos[None])[None]
         o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=allowed[:, None], scale=1.0 / math.sqrt(D))
         o = o.transpose(1, 2).reshape(B, S, nq * D)
-        return self._lin(o * torch.sigmoid(gate), lay.w["o_proj"], lay, "fo", lora, training)   # partial over TP
+        return self._lin(sigmoid_gate(o, gate), lay.w["o_proj"], lay, "fo", lora, training)   # partial over TP
 
     def _linear_attn(self, lay, h, key_mask, lora, training, cache=None):
         B, S, _ = h.shape
@@ -407,14 +409,15 @@ class Qwen35Model:
         q = self._lin(h, W[:kd], lay, "lq", lora, training)
         k = self._lin(h, W[kd : 2 * kd], lay, "lk", lora, training)
         v = self._lin(h, W[2 * kd :], lay, "lv", lora, training)
-        mixed = torch.cat([q, k, v], -1).transpose(1, 2)                   # [B, C, S]
+        mixed_in = torch.cat([q, k, v], -1)                                # [B, S, C]
         K = self.conv_k
         prev = cache.get("conv") if cache is not None else None
-        ext = torch.cat([prev, mixed], -1) if prev is not None else F.pad(mixed, (K - 1, 0))
         if cache is not None:
-            cache["conv"] = ext[..., -(K - 1):].detach().clone()
-        conv = F.conv1d(ext, lay.w["conv"][:, None, :], groups=mixed.shape[1])
-        mixed = F.silu(conv).transpose(1, 2)                               # [B, S, C]
+            # the last K-1 inputs [B, C, K-1] carry the convolution into the next call
+            xt = mixed_in.detach().transpose(1, 2)
+            ext = torch.cat([prev, xt], -1) if prev is not None else F.pad(xt, (K - 1, 0))
+            cache["conv"] = ext[..., -(K - 1):].contiguous().clone()
+        mixed = conv_silu(mixed_in, prev, lay.w["conv"])                   # causal conv1d + SiLU, [B, S, C]
         q, k, v = mixed[..., :kd], mixed[..., kd : 2 * kd], mixed[..., 2 * kd :]
         q = q.reshape(B, S, self.lk_l, self.dk)
         k = k.reshape(B, S, self.lk_l, self.dk)

@@ -383,3 +383,17 @@ def lse_push(partials, tgt, dst, sig, self_rank):
 
 def lse_merge(srcs, counter, expected, lse, logp, err, spin_limit=0):
     raise NotImplementedError("the vocab-parallel log-prob exchange reads peer memory and needs GPUs")
+
+
+def paged_decode_attention_tc(q, k_pool, v_pool, block_table, start, length, out, scale, splits, scratch,
+                              prefix_len, group_rows, prefix_splits, err):
+    paged_decode_attention(q, k_pool, v_pool, block_table, start, length, out, scale, splits, scratch)
+
+
+def sample_append_split(logits, temperature, seed, next_ids, slot, pos, kv_len, finished, out_tokens, prompt_slots,
+                        eos_id, pad_id, ignore_eos, vocab_start, scratch, chunk, err, exch_dst=None, exch_sig=None,
+                        exch_self=0, exch_slots=0, exch_arrivals=0, spin_limit=0):
+    if exch_dst is not None:
+        raise NotImplementedError("the vocab-parallel sampler exchange writes peer memory and needs GPUs")
+    sample_append(logits, temperature, 1.0, seed, next_ids, slot, pos, kv_len, finished, out_tokens, prompt_slots,
+                  eos_id, pad_id, ignore_eos, None)

@@ -221,3 +221,120 @@ class TPAllReduce:
         if self.sym is not None:
             self.sym.close()
             self.sym = None
+
+
+class SampleExchange:
+    """Vocab-parallel sampling without gathering the logits.
+
+    Every rank draws Gumbel noise for its own vocabulary shard (the same
+    counters as a full-vocabulary pass) and keeps the shard's best (key,
+    token); the winner goes into slot ``rank`` of every rank's buffer over
+    NVLink with a per-row arrival counter, and each rank then takes the best of
+    all shards -- the same token everywhere.  The consumer resets a row's
+    counter after reading it, so the buffers serve every decode step (and a
+    captured CUDA graph) without host bookkeeping.  Two consecutive uses must
+    be separated by a collective of the group -- a decode step has one per
+    layer -- so that no rank overwrites a slot or signals a counter that a
+    slower peer has not consumed yet.  Layout of each rank's
+    buffer: ``[0, 4 * rows)`` int32 arrival counters, then ``tp x rows`` float2
+    slots at offset 256-aligned.
+
+    Replaces the all-gather of ``[rows, vocab / tp]`` fp32 logits before the
+    sampler (reference counterpart: the replicated head and sampling of
+    src/graspo/backends/graspoflow/tensor_utils.py:649-683).
+    """
+
+    def __init__(self, rows: int, group, device: torch.device) -> None:
+        self.rows = int(rows)
+        self.tp = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slot_off = -(-4 * self.rows // 256) * 256
+        nbytes = self.slot_off + self.tp * self.rows * 8
+        self.sym = SymmetricBuffer(nbytes, group, device)
+        p, r = self.sym.ptrs, self.rank
+        self.dst = torch.tensor([p[q] + self.slot_off + r * self.rows * 8 for q in range(self.tp)], dtype=torch.int64)
+        self.sig = torch.tensor([0 if q == r else p[q] for q in range(self.tp)], dtype=torch.int64)
+        self.slots = p[r] + self.slot_off
+        self.arrivals = p[r]
+
+    def kwargs(self) -> dict:
+        return {"exch_dst": self.dst, "exch_sig": self.sig, "exch_self": self.rank, "exch_slots": self.slots,
+                "exch_arrivals": self.arrivals}
+
+    def close(self) -> None:
+        self.sym.close()
+
+
+class DPGradReduce:
+    """Data-parallel LoRA-gradient all-reduce overlapped with the backward.
+
+    As soon as a layer's backward has finished its LoRA gradients, ``push``
+    copies those slices into this rank's receive slot on every DP peer with the
+    copy engines, on a side stream (so the transfer runs under the remaining
+    layers' backward), and a one-thread kernel adds the element count to the
+    peers' 64-bit arrival counters.  ``finish`` waits (bounded, on the device)
+    for the peers' slices and writes ``scale * sum`` in rank order straight into
+    the gradient buffer -- the 1/dp scaling is part of the same pass -- so every
+    replica holds the same bits before the clipped AdamW.
+
+    Two slot sets alternate between optimizer steps: a rank writes step s+2
+    into a peer's set only after its own ``finish`` of step s+1, which needed
+    the peer's step s+1 slices, pushed after the peer's ``finish`` of step s.
+
+    Reference counterpart: the DP-free reference has no such reduction; the
+    LoRA-gradient all-reduce of src/graspo/backends/graspoflow/models/qwen35_36/
+    training.py:428-441 (over TP) is its closest relative.
+    """
+
+    def __init__(self, numel: int, group, device: torch.device) -> None:
+        self.n = int(numel)
+        self.dp = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slot_bytes = -(-self.n * 4 // 256) * 256
+        self.sym = SymmetricBuffer(_HEADER + 2 * self.dp * self.slot_bytes, group, device)
+        self.set = 0
+        self.expected = [0, 0]
+        self.pushed = 0
+        self.stream = torch.cuda.Stream(device=device)
+        self.err = err_word(device)
+
+    def _slot(self, rank: int, s: int, src: int) -> int:
+        return self.sym.ptrs[rank] + _HEADER + (s * self.dp + src) * self.slot_bytes
+
+    def push(self, grads: torch.Tensor, ranges: list[tuple[int, int]]) -> None:
+        """Send the finished gradient ranges [(start, count), ...] to every peer."""
+        C = ext()
+        ev = torch.cuda.Event()
+        ev.record()
+        total = 0
+        peers = [q for q in range(self.dp) if q != self.rank]
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_event(ev)
+            for start, count in ranges:
+                for q in peers:
+                    C.peer_copy(self._slot(q, self.set, self.rank) + 4 * start, grads, 4 * start, 4 * count)
+                total += count
+            sig = torch.tensor([self.sym.ptrs[q] + 8 * self.set for q in peers], dtype=torch.int64)
+            C.signal_counters(sig, total)
+        # the gradient buffer must outlive the side-stream copies that read it
+        grads.record_stream(self.stream)
+        self.pushed += total
+
+    def finish(self, grads: torch.Tensor, spin_limit: int = 0) -> None:
+        """grads <- (1 / dp) * sum over replicas, after every range has been pushed."""
+        if self.pushed == 0:
+            self.push(grads, [(0, self.n)])
+        if self.pushed != self.n:
+            raise RuntimeError(f"DPGradReduce: {self.pushed} of {self.n} gradient entries were pushed this step")
+        torch.cuda.current_stream().wait_stream(self.stream)
+        s = self.set
+        self.expected[s] += self.n * (self.dp - 1)
+        srcs = torch.tensor([0 if q == self.rank else self._slot(self.rank, s, q) for q in range(self.dp)],
+                            dtype=torch.int64)
+        ext().dp_reduce(grads, srcs, self.sym.ptrs[self.rank] + 8 * s, self.expected[s], 1.0 / self.dp, self.err,
+                        spin_limit)
+        self.set ^= 1
+        self.pushed = 0
+
+    def close(self) -> None:
+        self.sym.close()

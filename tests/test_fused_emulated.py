@@ -156,3 +156,29 @@ def test_split_rollout_merges_to_the_unsplit_result(model):
     assert merged.prompt_lens == whole.prompt_lens and merged.gen_lens == whole.gen_lens
     assert torch.equal(merged.prompt_ids, whole.prompt_ids)
     assert merge_results(parts[:1], pad_id=4095) is parts[0]
+
+
+def test_layer_gradient_ranges_cover_the_buffer_once(model):
+    """The data-parallel push sends each layer's LoRA factors as merged ranges of the flat
+    buffer; over all layers they cover every entry exactly once."""
+    lora = model.lora
+    seen = torch.zeros(lora.numel, dtype=torch.int32)
+    for lw in model.layers:
+        ranges = lora.layer_ranges(lw.index)
+        assert ranges == sorted(ranges)
+        for start, count in ranges:
+            seen[start : start + count] += 1
+    assert bool((seen == 1).all())
+
+
+def test_stage_backward_reports_each_finished_layer(model):
+    from graspo_b200.models.fused import AttnMeta, FusedQwen3
+
+    with use_emulation():
+        f = FusedQwen3(model)
+        seq, mask = _batch()
+        meta = AttnMeta.from_mask(mask)
+        x, inputs = f.stage_forward(f.embed(seq), meta, train=True, keep_inputs=True)
+        done = []
+        f.stage_backward(inputs, torch.randn_like(x) * 1e-3, meta, train=True, on_layer_done=done.append)
+    assert done == [lw.index for lw in reversed(model.layers)]

@@ -521,6 +521,39 @@ def test_adamw_matches_torch():
     _close(p, ref.detach(), 1e-5)
 
 
+@pytest.mark.parametrize("temperature", [1.0, 0.0])
+def test_split_sampler_matches_single_pass(temperature):
+    """The split sampler draws the same noise per vocabulary entry as the one-CTA-per-row sampler,
+    so both pick the same tokens and leave the same decode state."""
+    rows, V = 5, 151936
+    logits = torch.randn(rows, V, device="cuda") * 2
+
+    def state():
+        return dict(next_ids=torch.zeros(rows, dtype=torch.long, device="cuda"),
+                    slot=torch.arange(rows, device="cuda", dtype=torch.long) + 40,
+                    pos=torch.zeros(rows, dtype=torch.long, device="cuda"),
+                    kv_len=torch.zeros(rows, dtype=torch.int32, device="cuda"),
+                    finished=torch.zeros(rows, dtype=torch.uint8, device="cuda"),
+                    out=torch.zeros(rows, 64, dtype=torch.long, device="cuda"))
+
+    from graspo_b200.ops._ext import check_errors, err_word
+
+    a, b = state(), state()
+    chunk = 15196
+    nch = -(-V // chunk)
+    scratch = torch.zeros(rows * (1 + 2 * nch) + 2, device="cuda")
+    for step in range(3):
+        _ext().sample_append(logits, temperature, 1.0, 11, a["next_ids"], a["slot"], a["pos"], a["kv_len"],
+                             a["finished"], a["out"], 32, -1, 0, True, None)
+        _ext().sample_append_split(logits, temperature, 11, b["next_ids"], b["slot"], b["pos"], b["kv_len"],
+                                   b["finished"], b["out"], 32, -1, 0, True, 0, scratch, chunk, err_word())
+    torch.cuda.synchronize()
+    check_errors()
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
+    assert int(scratch[:rows].view(torch.int32).abs().sum().item()) == 0, "row counters are left at zero"
+
+
 def test_dropout_statistics():
     x = torch.ones(100000, device="cuda", dtype=torch.bfloat16)
     y = torch.empty_like(x)
@@ -531,6 +564,24 @@ def test_dropout_statistics():
     y2 = torch.empty_like(x)
     _ext().dropout(x, y2, 0.1, 5, 3, None)
     assert torch.equal(y, y2), "same seed and stream must regenerate the same mask"
+
+
+def test_dropout_tail_add_and_streams():
+    n = 100003  # not a multiple of the 8-element vectors
+    x = (torch.randn(n, device="cuda") + 3).bfloat16()
+    a = torch.randn(n, device="cuda").bfloat16()
+    y0, y = torch.empty_like(x), torch.empty_like(x)
+    _ext().dropout(x, y0, 0.25, 9, 1, None)
+    _ext().dropout(x, y, 0.25, 9, 1, a)
+    keep = y0 != 0
+    assert abs(keep.float().mean().item() - 0.75) < 0.01
+    want = (x.float() * keep.float() * (1.0 / 0.75) + a.float()).bfloat16()
+    assert torch.equal(y, want), "the added variant applies the same mask"
+    tail = (x[-3:].float() * keep[-3:].float() * (1.0 / 0.75)).bfloat16()
+    assert torch.equal(y0[-3:], tail), "the tail elements are masked and scaled like the rest"
+    y3 = torch.empty_like(x)
+    _ext().dropout(x, y3, 0.25, 9, 2, None)
+    assert ((y3 != 0) != keep).float().mean().item() > 0.2, "another stream id draws another mask"
 
 
 @pytest.mark.parametrize("dk,dv", [(64, 64), (128, 128), (128, 96)])

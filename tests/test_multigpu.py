@@ -204,10 +204,105 @@ def _tp_reduce_worker(rank, world):
     want = logits.gather(1, tgt[:, None]).squeeze(1) - want_lse
     assert (lse - want_lse).abs().max().item() < 2e-3
     assert (logp - want).abs().max().item() < 2e-3
+    # vocab-parallel sampling: the shards' winners through peer memory == one full-vocabulary pass
+    from graspo_b200.ops._ext import ext, err_word
+    from graspo_b200.parallel.symm import SampleExchange
+
+    rows, V = 6, 151936
+    logits = torch.randn(rows, V, device="cuda", generator=shared) * 2
+    vs = V // world
+    sx = SampleExchange(rows, ps.tp_group, ps.device)
+
+    def state():
+        return [torch.zeros(rows, dtype=torch.long, device="cuda"),
+                torch.arange(rows, device="cuda", dtype=torch.long) + 7,
+                torch.zeros(rows, dtype=torch.long, device="cuda"), torch.zeros(rows, dtype=torch.int32, device="cuda"),
+                torch.zeros(rows, dtype=torch.uint8, device="cuda"), torch.zeros(rows, 16, dtype=torch.long, device="cuda")]
+
+    full, part = state(), state()
+    chunk = 4096
+    scratch = torch.zeros(rows * (1 + 2 * (-(-vs // chunk))) + 2, device="cuda")
+    local = logits[:, rank * vs : (rank + 1) * vs].contiguous()
+    tick = torch.zeros(1, device="cuda")
+    for _ in range(4):
+        ext().sample_append(logits, 1.0, 1.0, 5, *full, 3, -1, 0, True, None)
+        ext().sample_append_split(local, 1.0, 5, *part, 3, -1, 0, True, rank * vs, scratch, chunk, err_word(),
+                                  **sx.kwargs())
+        dist.all_reduce(tick)  # consecutive exchanges are separated by a collective (a decode step has several)
+    torch.cuda.synchronize()
+    check_errors()
+    for x, y in zip(full, part):
+        assert torch.equal(x, y)
+    sx.close()
     torch.cuda.synchronize()
     check_errors()
     red.close()
     pstate.destroy()
+
+
+def _dp_worker(rank, world, path):
+    """DP=2: LoRA gradients sent layer by layer during the backward and summed by dp_reduce
+    equal (1/2 x) the DP=1 gradients of the whole batch, bit-identical on both replicas."""
+    import torch.distributed as dist
+
+    from graspo_b200.models.fused import AttnMeta, FusedQwen3
+    from graspo_b200.ops._ext import check_errors, ext
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.state import ParallelState
+    from graspo_b200.parallel.symm import DPGradReduce
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ps = pstate.initialize(1, 1, world, timeout_sec=120)
+    g = torch.Generator().manual_seed(0)
+    B, S = 4, 80
+    seq = torch.randint(0, 4088, (B, S), generator=g).cuda()
+    mask = torch.ones(B, S, dtype=torch.bool, device="cuda")
+    mask[1, :9] = False
+    w = torch.randn(B, S - 1, generator=g).cuda() * (mask[:, :-1] & mask[:, 1:])
+
+    def grads_of(m, rows, hook=None):
+        f = FusedQwen3(m)
+        sq, mk = seq[rows], mask[rows]
+        meta = AttnMeta.from_mask(mk)
+        m.lora.grads.zero_()
+        x, inputs = f.stage_forward(f.embed(sq), meta, train=True, keep_inputs=True)
+        hn, rstd = f.final_norm(x)
+        tgt = torch.zeros_like(sq)
+        tgt[:, :-1] = sq[:, 1:]
+        lp, lse = f.token_logprobs(hn, tgt.reshape(-1))
+        gg = torch.zeros(sq.shape, device="cuda")
+        gg[:, :-1] = w[rows]
+        dhn = f.token_logprobs_backward(hn, tgt.reshape(-1), lse, gg.view(-1))
+        dx = torch.empty_like(x)
+        ext().rmsnorm_bwd(dhn, x, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
+        f.stage_backward(inputs, dx, meta, train=True, on_layer_done=hook)
+        return m.lora.grads
+
+    m2 = _build(path, ps)
+    red = DPGradReduce(m2.lora.numel, ps.dp_group, ps.device)
+    half = slice(rank * B // world, (rank + 1) * B // world)
+    for step in range(3):  # both slot sets, twice
+        gr = grads_of(m2, half, hook=lambda layer: red.push(m2.lora.grads, m2.lora.layer_ranges(layer)))
+        red.finish(gr)
+        torch.cuda.synchronize()
+        check_errors()
+        other = [torch.empty_like(gr) for _ in range(world)]
+        dist.all_gather(other, gr)
+        assert all(torch.equal(o, gr) for o in other), "replicas must hold bit-identical gradients"
+    m1 = _build(path, ParallelState(device=ps.device))
+    full = grads_of(m1, slice(0, B)) / world
+    err = (gr - full).abs().max().item() / full.abs().max().item()
+    assert err < 2e-2, err
+    red.close()
+    pstate.destroy()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_dp2_overlapped_grad_reduce_matches_dp1(tmp_path):
+    from graspo_b200.utils.synth import write_qwen3_checkpoint
+
+    path = write_qwen3_checkpoint(tmp_path / "small", SMALL, seed=4, std=0.05, with_tokenizer=False)
+    run_world(2, _dp_worker, path, timeout=600)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
