@@ -11,7 +11,7 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
              c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout,
              c10::optional<torch::Tensor> push_out, c10::optional<torch::Tensor> push_sig, int64_t push_self,
-             int64_t push_rows);
+             int64_t push_rows, int64_t push_fence_once);
 void tp_reduce(torch::Tensor srcs, int64_t counter, int64_t expected, c10::optional<torch::Tensor> residual,
                torch::Tensor out, int64_t ld_src, torch::Tensor err, int64_t spin_limit);
 void paged_decode_attention_tc(torch::Tensor q, torch::Tensor k_pool, torch::Tensor v_pool,
@@ -37,6 +37,7 @@ void lse_merge(torch::Tensor srcs, int64_t counter, int64_t expected, torch::Ten
 std::vector<torch::Tensor> symm_alloc(int64_t nbytes, int64_t device);
 int64_t symm_open(torch::Tensor handle, int64_t device);
 void symm_close(int64_t ptr, int64_t device);
+bool enable_peer_access(int64_t device, int64_t peer);
 void add_rmsnorm(torch::Tensor h, c10::optional<torch::Tensor> delta, c10::optional<torch::Tensor> h_out,
                  torch::Tensor w, torch::Tensor y, c10::optional<torch::Tensor> rstd,
                  c10::optional<torch::Tensor> lora_a, c10::optional<torch::Tensor> lora_u, double scale,
@@ -102,7 +103,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("splits"), py::arg("err"), py::arg("max_ctas"), py::arg("push_dst") = py::none(),
         py::arg("push_flag") = py::none(), py::arg("tile_ctr") = py::none(), py::arg("layout") = 0,
         py::arg("push_out") = py::none(), py::arg("push_sig") = py::none(), py::arg("push_self") = 0,
-        py::arg("push_rows") = 0);
+        py::arg("push_rows") = 0, py::arg("push_fence_once") = 0);
   m.def("tp_reduce", &gb::tp_reduce,
         "sum of the tensor-parallel receive slots (rank order) + optional residual, after a bounded wait "
         "on the arrival counter",
@@ -132,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &gb::symm_alloc, "zeroed device buffer + its CUDA IPC handle");
   m.def("symm_open", &gb::symm_open, "map a peer's buffer from its IPC handle; returns the device address");
   m.def("symm_close", &gb::symm_close);
+  m.def("enable_peer_access", &gb::enable_peer_access, "direct access from one GPU to another's memory");
   m.def("set_pdl", [](bool on) { gb::pdl_enabled() = on; },
         "launch the decode-chain kernels with programmatic dependent launch (default on)");
   m.def("pdl_enabled", []() { return gb::pdl_enabled(); });

@@ -71,7 +71,7 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
              int64_t splits, torch::Tensor err, int64_t max_ctas, c10::optional<torch::Tensor> push_dst,
              c10::optional<torch::Tensor> push_flag, c10::optional<torch::Tensor> tile_ctr, int64_t layout,
              c10::optional<torch::Tensor> push_out, c10::optional<torch::Tensor> push_sig, int64_t push_self,
-             int64_t push_rows) {
+             int64_t push_rows, int64_t push_fence_once) {
   check_operand(A, "A");
   check_operand(B, "B");
   // layout bit 1: A given as [K, M] (MN-major); bit 0: B given as [K, N]
@@ -215,6 +215,7 @@ void gemm_tc(torch::Tensor A, torch::Tensor B, c10::optional<torch::Tensor> A2,
     args.npush = np;
     args.push_self = static_cast<int>(push_self);
     args.push_rows = static_cast<int>(push_rows);
+    args.push_fence_once = push_fence_once ? 1 : 0;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   const int mc = static_cast<int>(max_ctas);

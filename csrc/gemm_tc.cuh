@@ -105,6 +105,7 @@ struct GemmArgs {
   int npush;
   int push_self;
   int push_rows;
+  int push_fence_once;  // 1: one system fence per tile by the signalling thread (after the barrier)
 };
 
 template <int BN_>
@@ -246,9 +247,12 @@ __device__ __forceinline__ void push_chunk_bf16(const GemmArgs& args, int m, int
 // consumers are never left waiting on a tile that will not be signalled.
 template <int BN>
 __device__ __forceinline__ void push_signal(const GemmArgs& args, const Unit& w, int row_in_tile) {
-  __threadfence_system();
+  if (!args.push_fence_once) __threadfence_system();
   epi_bar();
   if (row_in_tile == 0) {
+    // the barrier orders the other epilogue threads' stores before this thread's
+    // release (release is cumulative); the fence makes them visible system-wide
+    if (args.push_fence_once) __threadfence_system();
     const int m0 = w.m_block * BM;
     const int mm = min(BM, args.M - m0);
     const int nn = min(BN, args.N - w.n_block * BN);

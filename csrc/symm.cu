@@ -58,6 +58,23 @@ int64_t symm_open(torch::Tensor handle, int64_t device) {
   return reinterpret_cast<int64_t>(ptr);
 }
 
+// Let kernels on `device` read and write `peer`'s memory directly (one process
+// driving several GPUs: profiling and single-process tests of the peer paths).
+// Returns false when the two devices cannot reach each other.
+bool enable_peer_access(int64_t device, int64_t peer) {
+  int ok = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&ok, static_cast<int>(device), static_cast<int>(peer)));
+  if (!ok) return false;
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const cudaError_t e = cudaDeviceEnablePeerAccess(static_cast<int>(peer), 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  C10_CUDA_CHECK(e);
+  return true;
+}
+
 void symm_close(int64_t ptr, int64_t device) {
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));

@@ -208,6 +208,50 @@ def bench_attn(args) -> None:
         }), flush=True)
 
 
+def bench_push(args) -> None:
+    """One process, two GPUs: the TP=2 training o_proj GEMM (24576 x 4096 x 2048) plain, with its
+    tiles pushed to a second local slot, and pushed to GPU 1 over NVLink; plus a copy-engine copy
+    of the same 201 MB to GPU 1 and the rank-order sum (tp_reduce)."""
+    from graspo_b200.ops._ext import check_errors, err_word, ext
+    from graspo_b200.ops.gemm import gemm
+
+    if not ext().enable_peer_access(0, 1):
+        raise SystemExit("GPU 0 cannot reach GPU 1")
+    timer = Timer(iters=args.iters)
+    T, H, K = 24576, 4096, 2048
+    a = torch.randn(T, K, device="cuda:0").bfloat16()
+    w = (torch.randn(H, K, device="cuda:0") * 0.02).bfloat16()
+    own = torch.empty(T, H, device="cuda:0", dtype=torch.bfloat16)
+    local2 = torch.empty_like(own)
+    peer = torch.empty(T, H, device="cuda:1", dtype=torch.bfloat16)
+    ctr0 = torch.zeros(2, device="cuda:0", dtype=torch.int64)
+    ctr1 = torch.zeros(2, device="cuda:1", dtype=torch.int64)
+
+    def push(dst, ctr):
+        return {"push_out": torch.tensor([own.data_ptr(), dst.data_ptr()], dtype=torch.int64),
+                "push_sig": torch.tensor([0, ctr.data_ptr()], dtype=torch.int64), "push_self": 0, "push_rows": 0}
+
+    nbytes = T * H * 2
+    flops = 2.0 * T * H * K
+    res = {}
+    res["gemm"] = timer(lambda: gemm(a, w, own))
+    res["gemm_push_local"] = timer(lambda: gemm(a, w, own, push=push(local2, ctr0)))
+    res["gemm_push_peer"] = timer(lambda: gemm(a, w, own, push=push(peer, ctr1)))
+    res["gemm_push_peer_fence_once"] = timer(lambda: gemm(a, w, own, push={**push(peer, ctr1), "push_fence_once": 1}))
+    res["gemm_push_local_fence_once"] = timer(lambda: gemm(a, w, own, push={**push(local2, ctr0),
+                                                                             "push_fence_once": 1}))
+    res["copy_engine_to_peer"] = timer(lambda: ext().peer_copy(peer.data_ptr(), own, 0, nbytes))
+    done = torch.ones(1, device="cuda:0", dtype=torch.int64)
+    out = torch.empty_like(own)
+    srcs = torch.tensor([own.data_ptr(), local2.data_ptr()], dtype=torch.int64)
+    res["tp_reduce"] = timer(lambda: ext().tp_reduce(srcs, done.data_ptr(), 1, own, out, H, err_word(out.device), 0))
+    check_errors(0)
+    for name, ms in res.items():
+        extra = {"tflops": round(flops / ms / 1e9, 1)} if name.startswith("gemm") else {}
+        print(json.dumps({"case": name, "ms": round(ms, 4), "GBps_201MB": round(nbytes / ms / 1e6, 1), **extra}),
+              flush=True)
+
+
 def bench_step(args) -> None:
     from graspo_b200.engine.rollout import FusedRolloutEngine
     from graspo_b200.models.fused import FusedQwen3
@@ -359,6 +403,31 @@ def bench_profile(args) -> None:
             lse = torch.full((T,), 12.0, device="cuda")
             g = torch.full((T,), 1e-3, device="cuda")
             runs.append(lambda: gemm(h, head, epilogue="softmax_grad", targets=tgt, row_lse=lse, row_scale=g))
+    elif k in ("gemm_push_peer", "tp_reduce"):
+        # one process, two GPUs: the training o_proj GEMM at TP=2 (24576 tokens x 4096 x 2048) whose
+        # epilogue stores every bf16 tile into this GPU's own slot and into the slot on GPU 1
+        # (NVLink), then the rank-order sum of the two slots with the residual
+        if not ext().enable_peer_access(0, 1):
+            raise SystemExit("GPU 0 cannot reach GPU 1")
+        T, H, K = 24576, 4096, 2048
+        a = torch.randn(T, K, device="cuda:0").bfloat16()
+        w = (torch.randn(H, K, device="cuda:0") * 0.02).bfloat16()
+        own = torch.empty(T, H, device="cuda:0", dtype=torch.bfloat16)
+        peer = torch.empty(T, H, device="cuda:1", dtype=torch.bfloat16)
+        ctr = torch.zeros(2, device="cuda:1", dtype=torch.int64)
+        push = {"push_out": torch.tensor([own.data_ptr(), peer.data_ptr()], dtype=torch.int64),
+                "push_sig": torch.tensor([0, ctr.data_ptr()], dtype=torch.int64), "push_self": 0, "push_rows": 0}
+        if k == "gemm_push_peer":
+            runs.append(lambda: gemm(a, w, own, push=dict(push)))
+        else:
+            from graspo_b200.ops._ext import err_word
+
+            other = torch.randn(T, H, device="cuda:0").bfloat16()
+            res = torch.randn(T, H, device="cuda:0").bfloat16()
+            out = torch.empty(T, H, device="cuda:0", dtype=torch.bfloat16)
+            done = torch.ones(1, device="cuda:0", dtype=torch.int64)  # every arrival already counted
+            srcs = torch.tensor([own.data_ptr(), other.data_ptr()], dtype=torch.int64)
+            runs.append(lambda: ext().tp_reduce(srcs, done.data_ptr(), 1, res, out, H, err_word(out.device), 0))
     elif k == "gemm_qkv_decode":
         # decode q/k/v projection with its LoRA A rows: 64 tokens, swap layout, split-K 3, fp32 atomics
         w, x = torch.randn(6144 + 64, 4096, device="cuda").bfloat16(), torch.randn(64, 4096, device="cuda").bfloat16()
@@ -441,7 +510,7 @@ def bench_profile(args) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "attn", "step", "train", "profile", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "attn", "push", "step", "train", "profile", "all"])
     parser.add_argument("--kernel", default="gemm")
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
@@ -462,6 +531,8 @@ def main() -> None:
         bench_decode(args)
     if args.what == "attn":
         bench_attn(args)
+    if args.what == "push":
+        bench_push(args)
     if args.what == "step":
         bench_step(args)
     if args.what == "train":

@@ -25,7 +25,7 @@ def _f(x):
 
 def gemm_tc(A, B, A2, B2, C, R, aux, targets, tgt_logit, row_lse, row_scale, epilogue, swap, bn, splits, err,
             max_ctas, push_dst=None, push_flag=None, tile_ctr=None, layout=0, push_out=None, push_sig=None,
-            push_self=0, push_rows=0):
+            push_self=0, push_rows=0, push_fence_once=0):
     if push_dst is not None or push_out is not None:
         raise NotImplementedError("the peer-memory tile push needs GPUs")
     a_mn, b_mn = bool(layout & 2), bool(layout & 1)
