@@ -33,6 +33,11 @@ namespace {
 
 constexpr int kReduceThreads = 256;
 constexpr int kMaxRanks = 8;
+// Kernels that spin on arrival counters keep their grid to two 256-thread CTAs
+// per SM, so a kernel that signals a peer (sent from this GPU's side stream) is
+// never starved of an SM by them: the peers' waits can only end once this
+// GPU's own signals have run.
+constexpr long kWaitCtasPerSm = 2;
 
 struct ReduceArgs {
   const __nv_bfloat16* src[kMaxRanks];
@@ -333,7 +338,8 @@ void dp_reduce(torch::Tensor grads, torch::Tensor srcs, int64_t counter, int64_t
   if (a.n == 0) return;
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, grads.get_device());
-  const int blocks = static_cast<int>(std::min<long>((a.n / 4 + 255) / 256 + 1, 8L * sms));
+  // two waiting CTAs per SM at most: the side stream's signal kernel must find room (see tp_reduce)
+  const int blocks = static_cast<int>(std::min<long>((a.n / 4 + 255) / 256 + 1, kWaitCtasPerSm * sms));
   dp_reduce_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_CHECK(cudaGetLastError());
 }
@@ -394,7 +400,7 @@ void lse_merge(torch::Tensor srcs, int64_t counter, int64_t expected, torch::Ten
   if (a.T == 0) return;
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, lse.get_device());
-  const int blocks = std::min((a.T + 255) / 256, 4 * sms);
+  const int blocks = std::min((a.T + 255) / 256, static_cast<int>(kWaitCtasPerSm) * sms);
   lse_merge_kernel<<<std::max(blocks, 1), 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_CHECK(cudaGetLastError());
 }
@@ -441,7 +447,9 @@ void tp_reduce(torch::Tensor srcs, int64_t counter, int64_t expected, c10::optio
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, out.get_device());
   const long vecs = static_cast<long>(rows) * (cols / 8);
-  const int blocks = static_cast<int>(std::min<long>((vecs + kReduceThreads - 1) / kReduceThreads, 8L * sms));
+  // at most two waiting CTAs per SM: the peers' arrivals may come from a signal kernel on this
+  // GPU's side stream, which needs room on an SM while these CTAs spin
+  const int blocks = static_cast<int>(std::min<long>((vecs + kReduceThreads - 1) / kReduceThreads, kWaitCtasPerSm * sms));
   tp_reduce_kernel<<<std::max(blocks, 1), kReduceThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_CHECK(cudaGetLastError());
 }

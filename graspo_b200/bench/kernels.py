@@ -189,9 +189,13 @@ def bench_attn(args) -> None:
     bytes_per_row = rows * (P + gen) * kv_row
     bytes_shared = (n * P + rows * gen) * kv_row
     splits = decode_attention_splits(rows, nkv, P + gp * page)
-    scr = torch.zeros(rows * nq * splits * (D + 2) + rows * nkv, device="cuda")
+    scr = torch.zeros(rows * nq * 8 * (D + 2) + rows * nkv, device="cuda")
     old = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, scale, splits, scr))
     ref = out.clone()
+    for sp in (1, 2, 3, 4, 6, 8):
+        ms = timer(lambda: ext().paged_decode_attention(q, kp, vp, bt, start, ln, out, scale, sp, scr))  # noqa: B023
+        print(json.dumps({"kernel": "split_mma_sync", "splits": sp, "chosen": sp == splits, "ms": round(ms, 4)}),
+              flush=True)
     sp, psp = decode_tc_splits(rows, nkv, gp * page, n, P)
     scr2 = torch.zeros(rows * nq * (sp + psp) * (D + 2) + rows * nkv, device="cuda")
     ew = err_word(q.device)
@@ -241,6 +245,25 @@ def bench_push(args) -> None:
     res["gemm_push_local_fence_once"] = timer(lambda: gemm(a, w, own, push={**push(local2, ctr0),
                                                                              "push_fence_once": 1}))
     res["copy_engine_to_peer"] = timer(lambda: ext().peer_copy(peer.data_ptr(), own, 0, nbytes))
+    side = torch.cuda.Stream(device="cuda:0")
+
+    def chunked(nch):
+        # the GEMM in row chunks; the copy engines send each finished chunk to GPU 1 on a side
+        # stream while the next chunk computes
+        rows = T // nch
+        for c in range(nch):
+            sl = slice(c * rows, (c + 1) * rows)
+            gemm(a[sl], w, own[sl])
+            ev = torch.cuda.Event()
+            ev.record()
+            side.wait_event(ev)
+            with torch.cuda.stream(side):
+                ext().peer_copy(peer[sl].data_ptr(), own, c * rows * H * 2, rows * H * 2)
+        torch.cuda.current_stream().wait_stream(side)
+
+    res["gemm_chunked_copy2"] = timer(lambda: chunked(2))
+    res["gemm_chunked_copy4"] = timer(lambda: chunked(4))
+    res["gemm_chunked_copy8"] = timer(lambda: chunked(8))
     done = torch.ones(1, device="cuda:0", dtype=torch.int64)
     out = torch.empty_like(own)
     srcs = torch.tensor([own.data_ptr(), local2.data_ptr()], dtype=torch.int64)
@@ -250,6 +273,35 @@ def bench_push(args) -> None:
         extra = {"tflops": round(flops / ms / 1e9, 1)} if name.startswith("gemm") else {}
         print(json.dumps({"case": name, "ms": round(ms, 4), "GBps_201MB": round(nbytes / ms / 1e6, 1), **extra}),
               flush=True)
+
+
+def bench_dsweep(args) -> None:
+    """Decode GEMM shapes (``--tokens`` rows, swap layout): tile width x split-K sweep with the
+    fraction of the measured HBM copy rate reached on the weight bytes."""
+    from graspo_b200.ops._ext import check_errors
+    from graspo_b200.ops.gemm import gemm
+
+    peaks = measured_peaks()
+    timer = Timer(iters=args.iters)
+    T = args.tokens
+    x = torch.randn(T, 4096, device="cuda").bfloat16()
+    for name, n, k in [("qkv", 6144 + 64, 4096), ("o", 4096 + 64, 4096), ("down", 4096 + 64, 12288),
+                       ("gate_up", 24576, 4096)]:
+        w = torch.randn(n, k, device="cuda").bfloat16()
+        xx = x if k == 4096 else torch.randn(T, k, device="cuda").bfloat16()
+        for bn in (32, 64):
+            for sp in ((1,) if name == "gate_up" else (1, 2, 3, 4, 6, 8)):
+                if name == "gate_up":
+                    act = torch.empty(T, n // 2, device="cuda", dtype=torch.bfloat16)
+                    ms = timer(lambda: gemm(w, xx, act, swap=True, epilogue="swiglu", bn=bn))  # noqa: B023
+                else:
+                    ws = torch.zeros(T, n, device="cuda")
+                    ms = timer(lambda: gemm(w, xx, ws, swap=True, epilogue="atomic", splits=sp, bn=bn))  # noqa: B023
+                print(json.dumps({"case": name, "bn": bn, "splits": sp, "us": round(ms * 1e3, 1),
+                                  "frac_of_measured_hbm": round(n * k * 2 / ms / 1e6 / peaks["hbm_gbs"], 3)}),
+                      flush=True)
+        del w
+    check_errors()
 
 
 def bench_step(args) -> None:
@@ -510,7 +562,8 @@ def bench_profile(args) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "attn", "push", "step", "train", "profile", "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "dsweep", "attn", "push", "step", "train", "profile",
+                                         "all"])
     parser.add_argument("--kernel", default="gemm")
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
@@ -533,6 +586,8 @@ def main() -> None:
         bench_attn(args)
     if args.what == "push":
         bench_push(args)
+    if args.what == "dsweep":
+        bench_dsweep(args)
     if args.what == "step":
         bench_step(args)
     if args.what == "train":

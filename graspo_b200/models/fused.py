@@ -18,11 +18,12 @@ the backward kernels.  LoRA gradients are tensor-core reductions over tokens
 flat fp32 gradient buffer.  Under tensor parallelism the input gradients of
 column-parallel projections are all-reduced over the TP group (the conjugate
 of the forward all-reduce after row-parallel projections).  On B200s both
-directions are fused collectives: the GEMM epilogue stores its bf16 partial
-tiles into every rank's receive slot over NVLink and ``tp_reduce`` sums the
-slots once the peers' tiles have arrived (``parallel/symm.py`` TPAllReduce);
-with sequence parallelism each row goes only to the rank that owns its token
-(reduce-scatter).
+directions overlap the transfer with the GEMM: the row-parallel GEMM runs in
+row chunks into this rank's receive slot, the copy engines send each finished
+chunk to the other ranks over NVLink on a side stream, and ``tp_reduce`` sums
+the slots in rank order once the peers' chunks have arrived
+(``parallel/symm.py`` TPAllReduce.gemm_reduce); with sequence parallelism each
+chunk goes only to the rank that owns its tokens (reduce-scatter).
 
 The selected-token log-prob never materialises logits: the LM-head GEMM's
 epilogue emits per-tile (max, sum-exp) partials, a small kernel merges them
@@ -231,11 +232,11 @@ class FusedQwen3:
             gemm(attn, lw.w_o, x1, ext_ab=ext_o, residual=x)
             C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
         elif self.tp_reducer() is not None:
-            # the o_proj GEMM pushes its partial tiles to every rank; x1 = x + sum
-            red = self.tp_reducer()
-            push = red.begin(T, scatter=sp)
-            gemm(attn, lw.w_o, push.pop("out"), ext_ab=ext_o, push=push)
-            x1 = red.finish(residual=x)
+            # the o_proj GEMM's row chunks go to every rank as they finish; x1 = x + sum
+            def o_rows(rows, dst):
+                gemm(attn[rows], lw.w_o, dst, ext_ab=(ext_o[0][rows], ext_o[1]) if ext_o else None)
+
+            x1 = self.tp_reducer().gemm_reduce(o_rows, T, scatter=sp, residual=x)
             C.add_rmsnorm(x1, None, None, lw.ln2, xn2, rstd2, None, None, 1.0, self.eps)
         else:
             o = gemm(attn, lw.w_o, ext_ab=ext_o)
@@ -267,10 +268,10 @@ class FusedQwen3:
         elif tp == 1:
             x2 = gemm(act, lw.w_down, ext_ab=ext_d, residual=x1)
         elif self.tp_reducer() is not None:
-            red = self.tp_reducer()
-            push = red.begin(T, scatter=sp)
-            gemm(act, lw.w_down, push.pop("out"), ext_ab=ext_d, push=push)
-            x2 = red.finish(residual=x1)
+            def down_rows(rows, dst):
+                gemm(act[rows], lw.w_down, dst, ext_ab=(ext_d[0][rows], ext_d[1]) if ext_d else None)
+
+            x2 = self.tp_reducer().gemm_reduce(down_rows, T, scatter=sp, residual=x1)
         else:
             d = gemm(act, lw.w_down, ext_ab=ext_d)
             d = _sp_scatter(d, tp_group) if sp else _tp_all_reduce(d, tp_group)
@@ -297,42 +298,48 @@ class FusedQwen3:
         [64k, K] are the MN-major B operand of ``dy @ W`` / ``dy @ B`` /
         ``du @ sA``, and the gradients contract over tokens with both operands
         MN-major (split-K fp32 atomics), so no transposed copy is made.
-        ``reduce`` ("all" or "scatter") sums d(input) over the TP group: the
-        dgrad GEMM pushes its tiles to the peers (fused all-reduce /
-        reduce-scatter) on CUDA, an NCCL / gloo collective follows it elsewhere.
+        ``reduce`` ("all" or "scatter") sums d(input) over the TP group: on CUDA
+        the dgrad runs in row chunks whose results the copy engines send to the
+        peers while the next chunk computes (``TPAllReduce.gemm_reduce``), an
+        NCCL / gloo collective follows it elsewhere.
         Returns (dx, db_full [N, 64k] fp32, da_full [64k, K] fp32) -- the
         gradient w.r.t. the padded layouts (caller scatters into parameters).
         """
         red = self.tp_reducer() if reduce is not None else None
-        push, out = None, None
-        if red is not None:
-            push = red.begin(dy.shape[0], scatter=reduce == "scatter")
-            out = push.pop("out")
-        if saved_u is None:
-            dx = gemm(dy, w, out, b_mn=True, push=push)
-            db = da = None
-        else:
+        du = tmp = None
+        if saved_u is not None:
             du = gemm(dy, b_ext, b_mn=True, bn=64)            # [T, 64k]
-            p = self.m.lora.dropout
-            if train and p > 0:
+            if train and self.m.lora.dropout > 0:
                 # the LoRA path's dgrad, masked like the forward, enters the
                 # frozen dgrad's epilogue as a residual
                 tmp = self._dropout(gemm(du, a_ext, b_mn=True), site, layer, seed, train)
-                dx = gemm(dy, w, out, b_mn=True, residual=tmp, push=push)
-                del tmp
+
+        def dgrad_rows(rows, dst):
+            if saved_u is None:
+                gemm(dy[rows], w, dst, b_mn=True)
+            elif tmp is not None:
+                gemm(dy[rows], w, dst, b_mn=True, residual=tmp[rows])
             else:
-                dx = gemm(dy, w, out, b_mn=True, ext_ab=(du, a_ext), push=push)
+                gemm(dy[rows], w, dst, b_mn=True, ext_ab=(du[rows], a_ext))
+
+        if red is not None:
+            # the dgrad's row chunks go to every rank (or their owner) as they finish
+            dx = red.gemm_reduce(dgrad_rows, dy.shape[0], scatter=reduce == "scatter")
+        else:
+            dx = torch.empty(dy.shape[0], w.shape[1], device=dy.device, dtype=dy.dtype)
+            dgrad_rows(slice(0, dy.shape[0]), dx)
+        del tmp
+        db = da = None
+        if saved_u is not None:
             n_out, width, k_in = dy.shape[1], saved_u.shape[1], saved_xd.shape[1]
             db = torch.zeros(n_out, width, device=dy.device, dtype=torch.float32)
             gemm(dy, saved_u, db, epilogue="atomic", a_mn=True, b_mn=True, bn=64, splits=_grad_splits(n_out))
             da = torch.zeros(width, k_in, device=dy.device, dtype=torch.float32)
             gemm(saved_xd, du, da, epilogue="atomic", a_mn=True, b_mn=True, bn=64, swap=True,
                  splits=_grad_splits(k_in))
-        if red is not None:
-            dx = red.finish()
-        elif reduce == "scatter":
+        if red is None and reduce == "scatter":
             dx = _sp_scatter(dx, self.m.ps.tp_group)
-        elif reduce == "all":
+        elif red is None and reduce == "all":
             dx = _tp_all_reduce(dx, self.m.ps.tp_group)
         return dx, db, da
 
@@ -548,9 +555,8 @@ class FusedQwen3:
             dlog = gemm(h[t0:t1], m.lm_head, epilogue="softmax_grad", targets=local_t[t0:t1],
                         row_lse=lse[t0:t1].contiguous(), row_scale=g[t0:t1].contiguous())
             if red is not None:
-                push = red.begin(t1 - t0)
-                gemm(dlog, m.lm_head, push.pop("out"), b_mn=True, push=push)
-                red.finish(out=dh[t0:t1])
+                red.gemm_reduce(lambda rows, dst: gemm(dlog[rows], m.lm_head, dst, b_mn=True), t1 - t0,
+                                out=dh[t0:t1])
             else:
                 gemm(dlog, m.lm_head, dh[t0:t1], b_mn=True)
             del dlog
