@@ -298,16 +298,23 @@ class Qwen3Adapter:
     def _vision_pad_id(self) -> int:
         return int(self.tokenizer.convert_tokens_to_ids("<|vision_pad|>"))
 
-    def _image_features(self, media_rows: list[list[dict]]):
-        """Vision-tower features of every image of every row, rows in order (cached
-        per image path), and the merged grid of each image."""
-        from graspo_b200.models.vision import load_image, preprocess
+    def _image_features(self, media_rows: list[list[dict]], vision_lora=None):
+        """Vision-tower features of every image of every row, rows in order, and
+        the merged grid of each image.  Features are cached per image path while
+        the tower is frozen; with vision LoRA targets they follow the current
+        factors (``vision_lora``: the pass's LoRA leaves, with gradients when training).
+
+        Video inputs are rejected, as in the reference, whose data path blocks
+        them (src/graspo/backends/graspoflow/multimodal.py:224, 253)."""
+        from graspo_b200.models.vision import VisionLoRA, load_image, preprocess
 
         vt = getattr(self.model, "vision", None)
         if vt is None:
             raise NotImplementedError("this checkpoint has no vision tower (config.json vision_config)")
+        if vision_lora is None and self.model.lora.vision_modules():
+            vision_lora = VisionLoRA(self.model.lora, training=False)
         cache = self.__dict__.setdefault("_image_cache", {})
-        if len(cache) > 512:
+        if len(cache) > 512 or vision_lora is not None:
             cache.clear()
         feats, grids = [], []
         m = vt.cfg.spatial_merge_size
@@ -316,21 +323,43 @@ class Qwen3Adapter:
                 if item.get("type") != "image":
                     raise NotImplementedError("video inputs are not supported")
                 path = item["path"]
-                if path not in cache:
+                if vision_lora is not None or path not in cache:
                     patches, (t, gh, gw) = preprocess(load_image(path), vt.cfg)
-                    cache[path] = (vt.encode([patches], [(t, gh, gw)]), (t, gh // m, gw // m))
+                    entry = (vt.encode([patches], [(t, gh, gw)], lora=vision_lora), (t, gh // m, gw // m))
+                    if vision_lora is not None:
+                        feats.append(entry[0])
+                        grids.append(entry[1])
+                        continue
+                    cache[path] = entry
                 feats.append(cache[path][0])
                 grids.append(cache[path][1])
         return (torch.cat(feats, 0), grids) if feats else (None, [])
 
-    def _image_hook(self, media_rows: list[list[dict]]):
-        """embed_hook placing image features on the image placeholder tokens."""
-        from graspo_b200.models.vision import ImageInputs
+    def _image_hook(self, media_rows: list[list[dict]], train: bool = False):
+        """embed_hook placing image features on the image placeholder tokens.
 
-        feats, grids = self._image_features(media_rows)
+        With vision LoRA targets and ``train``, the features carry an autograd
+        graph to the tower's LoRA leaves (kept in ``self._vision_pass`` until
+        the backward has run, see ``_finish_vision_pass``)."""
+        from graspo_b200.models.vision import ImageInputs, VisionLoRA
+
+        vlora = None
+        if self.model.lora.vision_modules():
+            vlora = VisionLoRA(self.model.lora, training=train)
+            if train:
+                self._vision_pass = vlora
+        feats, grids = self._image_features(media_rows, vision_lora=vlora)
         if feats is None:
             return None
         return ImageInputs(feats, self._vision_pad_id, grids)
+
+    def _finish_vision_pass(self) -> None:
+        """Add the vision-tower LoRA gradients of the pass that just ran backward
+        (only on the first rank of the TP group: every rank ran the same tower)."""
+        vlora = getattr(self, "_vision_pass", None)
+        if vlora is not None:
+            vlora.accumulate(enabled=self.ps.tp_rank == 0)
+            self._vision_pass = None
 
     def _generate_multimodal(self, samples, *, rollout_group_size: int, max_new_tokens: int,
                              max_prompt_length: int | None = None, temperature: float = 1.0, top_p: float = 1.0,
@@ -487,8 +516,13 @@ class Qwen3Adapter:
                 tgt = torch.cat([tgt, tgt.new_zeros(B, pad)], 1)
             meta = AttnMeta.from_mask(mask)
             x0 = f.embed(seq)
+            x0_graph = None
             if embed_hook is not None:
                 x0 = embed_hook(seq, x0)
+                if x0.requires_grad:
+                    # image features with vision LoRA: the kernels see a plain tensor, the
+                    # graph to the tower's LoRA leaves is kept for the backward
+                    x0_graph, x0 = x0, x0.detach()
             xL, inputs = f.stage_forward(f.sp_shard(x0), meta, train=train, seed=seed, keep_inputs=train)
             hn, rstd = f.final_norm(xL)
             hn_all = f.sp_gather(hn)
@@ -497,7 +531,7 @@ class Qwen3Adapter:
             full = full.reshape(-1)
             logp_full, lse = f.token_logprobs(hn_all, full)
             logp = logp_full.view(B, S)[:, : S_in - 1].contiguous()
-            return logp, ((meta, inputs, xL, hn_all, rstd, full, lse) if train else None)
+            return logp, ((meta, inputs, xL, hn_all, rstd, full, lse, x0_graph) if train else None)
         lora = EagerLoRA(self.model.lora, requires_grad=train)
         with torch.set_grad_enabled(train):
             if hasattr(self.model, "sequence_logprobs"):
@@ -512,7 +546,7 @@ class Qwen3Adapter:
         """Backprop d(loss)/d(logp) [B, S-1] through the head and all layers."""
         from graspo_b200.ops._ext import ext
 
-        meta, inputs, xL, hn, rstd, full_targets, lse = ctx
+        meta, inputs, xL, hn, rstd, full_targets, lse, x0_graph = ctx
         B, S = meta.B, meta.S
         g = torch.zeros(B, S, device=dlogp.device, dtype=torch.float32)
         g[:, : dlogp.shape[1]] = dlogp
@@ -520,7 +554,11 @@ class Qwen3Adapter:
         dxL = torch.empty_like(xL)
         ext().rmsnorm_bwd(dhn, xL, self.model.norm, rstd, None, dxL, self.model.cfg.rms_norm_eps)
         del dhn
-        self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed, on_layer_done=self._dp_layer_hook())
+        dx0 = self._fused.stage_backward(inputs, dxL, meta, train=True, seed=seed,
+                                         on_layer_done=self._dp_layer_hook())
+        if x0_graph is not None:
+            # into the vision tower through the image-feature rows of the embeddings
+            torch.autograd.backward(x0_graph, self._fused.sp_gather(dx0).view_as(x0_graph))
 
     # ------------------------------------------------------------ training
     def check_replicas(self) -> None:
@@ -628,6 +666,7 @@ class Qwen3Adapter:
                 ext().grpo_loss(logp, old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous(), clip_eps,
                                 1.0, loss, dlogp, None)
                 self._fused_backward_from_logp_grad(ctx, dlogp, seed)
+                self._finish_vision_pass()
             return loss
         with clock.time("micro_batch_forward_sec"):
             logp, lora = self._logprobs(seq, mask, train=True, embed_hook=embed_hook)
@@ -637,6 +676,7 @@ class Qwen3Adapter:
             if torch.isfinite(loss):
                 loss.backward()
                 lora.accumulate_grads()
+            self._finish_vision_pass()
         return loss.detach().reshape(1)
 
     def _shared_training_indices(self, count: int, optimize_round: int) -> list[int]:
@@ -669,7 +709,7 @@ class Qwen3Adapter:
                 self.optimizer.zero_grad()
                 seed = (int(self.config.training.seed) << 20) ^ (self._train_batch_call_index << 10) ^ steps
                 media_rows = [((e.metadata or {}).get("_media") or []) for e in batch]
-                hook = self._image_hook(media_rows) if any(media_rows) else None
+                hook = self._image_hook(media_rows, train=True) if any(media_rows) else None
                 loss = self._backward_grpo(seq, att, old, adv, act, policy_ratio_clip_eps, seed, embed_hook=hook)
                 with clock.time("grad_sync_sec"):
                     # both are sums (they commute); the DP slices were already sent

@@ -60,7 +60,10 @@ class LoRAModule:
 
     @property
     def replicated_factor(self) -> str:
-        """Which factor is replicated across the TP group ('a' or 'b')."""
+        """Which factor is replicated across the TP group ('a' or 'b'; 'ab' for a
+        module that is not sharded at all, such as a vision-tower linear)."""
+        if self.shard_kind == "none":
+            return "ab"
         return "b" if self.shard_kind == "in" else "a"
 
 
@@ -93,7 +96,7 @@ class LoRAAdapter:
         for replicated_pass in (True, False):
             for mod in modules:
                 for fac in ("a", "b"):
-                    if (mod.replicated_factor == fac) != replicated_pass:
+                    if (fac in mod.replicated_factor) != replicated_pass:
                         continue
                     size = self.r * mod.in_local if fac == "a" else mod.out_local * self.r
                     setattr(mod, f"offset_{fac}", total)
@@ -204,11 +207,15 @@ class LoRAAdapter:
         """1.0 for elements that are replicated across the TP group, else 0.0."""
         mask = torch.zeros(self.numel, dtype=torch.float32, device=self.device)
         for m in self.modules:
-            if m.replicated_factor == "a":
+            if "a" in m.replicated_factor:
                 mask[m.offset_a : m.offset_a + self.r * m.in_local] = 1.0
-            else:
+            if "b" in m.replicated_factor:
                 mask[m.offset_b : m.offset_b + m.out_local * self.r] = 1.0
         return mask
+
+    def vision_modules(self) -> list[LoRAModule]:
+        """LoRA modules of the vision tower (replicated over TP, outside the decoder layers)."""
+        return [m for m in self.modules if m.kind == "vision"]
 
     # ------------------------------------------------------------ fused layouts
     def invalidate(self) -> None:

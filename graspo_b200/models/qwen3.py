@@ -205,6 +205,10 @@ class Qwen3Model:
         else:
             self.norm = None
             self.lm_head = None
+        if self.vision is not None:
+            from graspo_b200.models.vision import vision_lora_modules
+
+            modules += vision_lora_modules(self.vision.cfg, self.lora_targets)
         self.lora = LoRAAdapter(
             modules, r=lora_r, alpha=lora_alpha, dropout=lora_dropout, device=dev, seed=seed, tp_rank=tr
         )

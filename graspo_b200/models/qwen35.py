@@ -292,6 +292,10 @@ class Qwen35Model:
             self.lm_head = load(name)
         else:
             self.norm = self.lm_head = None
+        if self.vision is not None:
+            from graspo_b200.models.vision import vision_lora_modules
+
+            modules += vision_lora_modules(self.vision.cfg, self.lora_targets)
         self.lora = LoRAAdapter(modules, r=lora_r, alpha=lora_alpha, dropout=lora_dropout, device=dev, seed=seed)
         self._mods = {(m.layer, m.kind): m for m in modules}
 

@@ -83,8 +83,70 @@ def load_image(path: str) -> torch.Tensor:
         return torch.from_numpy(__import__("numpy").asarray(im.convert("RGB"), dtype="uint8").copy())
 
 
+_VISION_LINEARS = ("attn.qkv", "attn.proj", "mlp.linear_fc1", "mlp.linear_fc2")
+
+
+def vision_lora_modules(cfg: VisionConfig, targets) -> list:
+    """LoRA modules of the vision tower for the enabled targets (reference names
+    ``visual.blocks.<i>.attn.qkv`` ... and ``visual.merger.linear_fc1/2``; presets
+    ``vision_merger`` and ``vision_common``).  The tower is replicated over
+    tensor parallelism, so both factors are unsharded."""
+    from graspo_b200.core.lora_targets import lora_target_enabled
+    from graspo_b200.models.lora import LoRAModule
+
+    H, inter = cfg.hidden_size, cfg.intermediate_size
+    merged = H * cfg.spatial_merge_size ** 2
+    dims = {"attn.qkv": (H, 3 * H), "attn.proj": (H, H), "mlp.linear_fc1": (H, inter), "mlp.linear_fc2": (inter, H)}
+    spec = [(f"blocks.{i}.{name}", *dims[name]) for i in range(cfg.depth) for name in _VISION_LINEARS]
+    spec += [("merger.linear_fc1", merged, merged), ("merger.linear_fc2", merged, cfg.out_hidden_size)]
+    out = []
+    for path, d_in, d_out in spec:
+        target = f"visual.{path}"
+        if not lora_target_enabled(targets, target):
+            continue
+        out.append(LoRAModule(module_name=target, target_name=target, hf_module_path=f"model.visual.{path}",
+                              layer=-1, kind="vision", shard_kind="none", in_full=d_in, out_full=d_out,
+                              in_local=d_in, out_local=d_out))
+    return out
+
+
+class VisionLoRA:
+    """Autograd leaves of the vision-tower LoRA factors for one training pass.
+
+    The leaves share storage with the adapter's fp32 master weights; after the
+    backward, ``accumulate`` adds their gradients into the flat gradient
+    buffer.  Every tensor-parallel rank runs the same tower on the same images,
+    so only one rank of the group adds them (the group's gradient sum of the
+    replicated factors then yields the gradient once)."""
+
+    def __init__(self, adapter, *, training: bool) -> None:
+        self.adapter = adapter
+        self.training = training
+        self.modules = {m.module_name: m for m in adapter.vision_modules()}
+        self.leaves = {name: (m.a.detach().requires_grad_(training), m.b.detach().requires_grad_(training))
+                       for name, m in self.modules.items()}
+
+    def delta(self, name: str, x: torch.Tensor) -> torch.Tensor | None:
+        pair = self.leaves.get(name)
+        if pair is None:
+            return None
+        a, b = pair
+        p = self.adapter.dropout
+        xin = F.dropout(x, p, True) if (self.training and p > 0) else x
+        return F.linear(F.linear(xin.float(), a), b) * self.adapter.scaling
+
+    def accumulate(self, enabled: bool = True) -> None:
+        for name, m in self.modules.items():
+            a, b = self.leaves[name]
+            if enabled and a.grad is not None:
+                m.a_grad.add_(a.grad)
+            if enabled and b.grad is not None:
+                m.b_grad.add_(b.grad)
+            a.grad = b.grad = None
+
+
 class VisionTower:
-    """Frozen vision encoder (weights under ``<prefix>.``)."""
+    """Vision encoder (weights under ``<prefix>.``), frozen; LoRA on its linears when enabled."""
 
     def __init__(self, cfg: VisionConfig, loader, prefix: str, *, dtype: torch.dtype, device: torch.device) -> None:
         self.cfg, self.dtype, self.device = cfg, dtype, device
@@ -133,33 +195,49 @@ class VisionTower:
         rot = torch.cat([-x[..., half:], x[..., :half]], -1)
         return x * cos[:, None] + rot * sin[:, None]
 
-    @torch.no_grad()
-    def encode(self, patches: list[torch.Tensor], grids: list[tuple[int, int, int]]) -> torch.Tensor:
-        """Per-image patches -> merged features [sum(gh * gw / 4), out_hidden], images in order."""
+    def encode(self, patches: list[torch.Tensor], grids: list[tuple[int, int, int]],
+               lora: VisionLoRA | None = None) -> torch.Tensor:
+        """Per-image patches -> merged features [sum(gh * gw / 4), out_hidden], images in order.
+
+        Without ``lora`` (or with LoRA leaves that need no gradient) this runs
+        without an autograd graph."""
+        if lora is None or not lora.training:
+            with torch.no_grad():
+                return self._encode(patches, grids, lora)
+        return self._encode(patches, grids, lora)
+
+    def _encode(self, patches, grids, lora):
         cfg = self.cfg
         outs = []
+
+        def lin(x, w, bias, name):
+            y = F.linear(x, w, bias)
+            d = lora.delta(name, x) if lora is not None else None
+            return y if d is None else y + d.to(y.dtype)
         for pt, (_, gh, gw) in zip(patches, grids, strict=True):
             x = F.linear(pt.to(self.device, self.dtype), self.patch_w, self.patch_b)
             x = (x.float() + self._pos_embed(gh, gw)).to(self.dtype)
             cos, sin = self._rotary(gh, gw)
             N = x.shape[0]
-            for blk in self.blocks:
+            for bi, blk in enumerate(self.blocks):
+                pre = f"visual.blocks.{bi}."
                 h = F.layer_norm(x, (cfg.hidden_size,), blk["norm1.weight"], blk["norm1.bias"], 1e-6)
-                qkv = F.linear(h, blk["attn.qkv.weight"], blk["attn.qkv.bias"]).view(N, 3, cfg.num_heads, -1)
+                qkv = lin(h, blk["attn.qkv.weight"], blk["attn.qkv.bias"], pre + "attn.qkv").view(N, 3, cfg.num_heads, -1)
                 q = self._rope(qkv[:, 0].float(), cos, sin).to(self.dtype)
                 k = self._rope(qkv[:, 1].float(), cos, sin).to(self.dtype)
                 v = qkv[:, 2]
                 o = F.scaled_dot_product_attention(q.transpose(0, 1)[None], k.transpose(0, 1)[None],
                                                    v.transpose(0, 1)[None])[0].transpose(0, 1).reshape(N, -1)
-                x = x + F.linear(o, blk["attn.proj.weight"], blk["attn.proj.bias"])
+                x = x + lin(o, blk["attn.proj.weight"], blk["attn.proj.bias"], pre + "attn.proj")
                 h = F.layer_norm(x, (cfg.hidden_size,), blk["norm2.weight"], blk["norm2.bias"], 1e-6)
-                h = F.gelu(F.linear(h, blk["mlp.linear_fc1.weight"], blk["mlp.linear_fc1.bias"]), approximate="tanh")
-                x = x + F.linear(h, blk["mlp.linear_fc2.weight"], blk["mlp.linear_fc2.bias"])
+                h = F.gelu(lin(h, blk["mlp.linear_fc1.weight"], blk["mlp.linear_fc1.bias"], pre + "mlp.linear_fc1"),
+                           approximate="tanh")
+                x = x + lin(h, blk["mlp.linear_fc2.weight"], blk["mlp.linear_fc2.bias"], pre + "mlp.linear_fc2")
             mg = self.merger
             h = F.layer_norm(x, (cfg.hidden_size,), mg["norm.weight"], mg["norm.bias"], 1e-6)
             h = h.reshape(-1, cfg.hidden_size * cfg.spatial_merge_size ** 2)
-            h = F.gelu(F.linear(h, mg["linear_fc1.weight"], mg["linear_fc1.bias"]))
-            outs.append(F.linear(h, mg["linear_fc2.weight"], mg["linear_fc2.bias"]))
+            h = F.gelu(lin(h, mg["linear_fc1.weight"], mg["linear_fc1.bias"], "visual.merger.linear_fc1"))
+            outs.append(lin(h, mg["linear_fc2.weight"], mg["linear_fc2.bias"], "visual.merger.linear_fc2"))
         return torch.cat(outs, 0)
 
 

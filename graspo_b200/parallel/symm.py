@@ -385,6 +385,7 @@ class DPGradReduce:
         self.set = 0
         self.expected = [0, 0]
         self.pushed = 0
+        self._ranges: list[tuple[int, int]] = []
         self.stream = torch.cuda.Stream(device=device)
         self.err = err_word(device)
 
@@ -409,11 +410,20 @@ class DPGradReduce:
         # the gradient buffer must outlive the side-stream copies that read it
         grads.record_stream(self.stream)
         self.pushed += total
+        self._ranges.extend(ranges)
 
     def finish(self, grads: torch.Tensor, spin_limit: int = 0) -> None:
-        """grads <- (1 / dp) * sum over replicas, after every range has been pushed."""
-        if self.pushed == 0:
-            self.push(grads, [(0, self.n)])
+        """grads <- (1 / dp) * sum over replicas.  Ranges no layer hook pushed (a
+        step without hooks, the vision tower's factors) are sent now."""
+        rest, cursor = [], 0
+        for start, count in sorted(self._ranges):
+            if start > cursor:
+                rest.append((cursor, start - cursor))
+            cursor = max(cursor, start + count)
+        if cursor < self.n:
+            rest.append((cursor, self.n - cursor))
+        if rest:
+            self.push(grads, rest)
         if self.pushed != self.n:
             raise RuntimeError(f"DPGradReduce: {self.pushed} of {self.n} gradient entries were pushed this step")
         torch.cuda.current_stream().wait_stream(self.stream)
@@ -425,6 +435,7 @@ class DPGradReduce:
                         spin_limit)
         self.set ^= 1
         self.pushed = 0
+        self._ranges = []
 
     def close(self) -> None:
         self.sym.close()
