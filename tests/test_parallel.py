@@ -181,7 +181,7 @@ def _dp2_worker(rank, world, path, batch, ref_file):
     w = mask[rows, 1:].float()
     ((lp * w).sum() / w.sum()).backward()
     lora.accumulate_grads()
-    fake = SimpleNamespace(ps=ps, model=m)
+    fake = SimpleNamespace(ps=ps, model=m, _dp_reducer=lambda: None)  # CPU ranks: the library all-reduce
     Qwen3Adapter._dp_average_grads(fake)
     ref = torch.load(ref_file)["grads"]
     assert torch.allclose(m.lora.grads, ref, atol=1e-6, rtol=1e-4), (m.lora.grads - ref).abs().max()
