@@ -252,6 +252,10 @@ def run(args) -> dict:
     if torch.cuda.is_available():
         torch.cuda.set_device(local_rank)
     tp, dp = layout(world) if args.impl == "ours" else (world, 1)
+    if args.tp and args.impl == "ours":
+        if world % args.tp:
+            raise SystemExit(f"--tp {args.tp} does not divide {world} GPUs")
+        tp, dp = args.tp, world // args.tp
     model_path = ensure_checkpoint(args.model, local_rank)
     per_replica = PROMPTS_PER_REPLICA_PER_TP * tp if args.prompts is None else args.prompts
     n_total = per_replica * (dp if args.impl == "ours" else 1)
@@ -411,6 +415,8 @@ def main() -> None:
     p.add_argument("--prompt-len", type=int, default=PROMPT_LEN)
     p.add_argument("--max-new", type=int, default=MAX_NEW)
     p.add_argument("--iters", type=int, default=1, help="optimize_iterations_per_step")
+    p.add_argument("--tp", type=int, default=0,
+                   help="tensor-parallel size of this framework's arm (default: 1 on one GPU, else 2; DP = N / TP)")
     p.add_argument("--time-budget", type=float, default=TIME_BUDGET_S,
                    help="wall-clock seconds for the whole run; fewer timed steps (>= 1) run when the requested "
                         "ones would not fit, and warm-up stops early (after at least 3); 0 disables")
