@@ -9,7 +9,8 @@ from graspo_b200.core.schema import GraspoConfig
 
 def main() -> None:
     parser = argparse.ArgumentParser(prog="python -m graspo_b200.cli.train_worker",
-                                     description="Internal GRASPO training worker. Use `graspo launch --config ...`.")
+                                     description=("Per-rank process started by `graspo launch` (directly or through torchrun); "
+                                                  "not meant to be run by hand."))
     parser.add_argument("--config", "-c", required=True)
     args = parser.parse_args()
     config = GraspoConfig.from_yaml(args.config)

@@ -1,12 +1,18 @@
-"""Completion-level replay buffer (reference: src/graspo/core/buffer.py:5-36).
+"""Completion-level replay buffer.
 
-Experiences hold host tensors so the device keeps only what the current step
-needs; the buffer is drained after every optimize step.
+Reference counterpart: src/graspo/core/buffer.py:5-36.  ``Experience`` is the
+record both runtimes exchange (``train_batch`` consumes a list of them), so
+its fields and their order are kept as the reference defines them; the buffer
+around it is a bounded FIFO of host-side records that the trainer fills with
+finalized groups and drains after every optimize step.
 """
 
 from __future__ import annotations
 
+from collections import deque
+from collections.abc import Iterable
 from dataclasses import dataclass
+from itertools import islice
 from typing import Any
 
 
@@ -22,24 +28,36 @@ class Experience:
 
 
 class ReplayBuffer:
-    def __init__(self, limit: int = 0) -> None:
-        self.limit = int(limit)
-        self.items: list[Experience] = []
+    """FIFO of experiences waiting for an optimize step.
 
-    def append_many(self, items: list[Experience]) -> None:
-        self.items.extend(items)
-        if self.limit > 0 and len(self.items) > self.limit:
-            del self.items[: len(self.items) - self.limit]
+    ``limit`` > 0 bounds the buffer: appending past it drops the oldest
+    records.  ``take(n)`` returns the oldest ``n`` without removing them;
+    ``consume(n)`` removes them once they have been trained on."""
+
+    def __init__(self, limit: int = 0) -> None:
+        self.limit = max(0, int(limit))
+        self._fifo: deque[Experience] = deque(maxlen=self.limit or None)
+
+    @property
+    def items(self) -> list[Experience]:
+        """A snapshot of the buffered records, oldest first."""
+        return list(self._fifo)
+
+    def append_many(self, records: Iterable[Experience]) -> None:
+        self._fifo.extend(records)
 
     def take(self, count: int) -> list[Experience]:
-        """The ``count`` oldest experiences (not removed)."""
-        return self.items[:count]
+        return list(islice(self._fifo, max(0, int(count))))
+
+    def consume(self, count: int) -> None:
+        for _ in range(min(max(0, int(count)), len(self._fifo))):
+            self._fifo.popleft()
 
     def clear(self) -> None:
-        self.items.clear()
+        self._fifo.clear()
 
     def __len__(self) -> int:
-        return len(self.items)
+        return len(self._fifo)
 
     def __getitem__(self, index: int) -> Experience:
-        return self.items[index]
+        return self._fifo[index]

@@ -487,7 +487,7 @@ class GraspoTrainer:
             "optimize_prompt_batch_size": tr.optimize_prompt_batch_size,
             "optimize_iterations_per_step": tr.optimize_iterations_per_step, "force_flush": bool(force),
         })
-        self.replay_buffer.items = self.replay_buffer.items[usable:]
+        self.replay_buffer.consume(usable)
         attempts, timings = list(self.pending_attempts), list(self.pending_timings)
         self.pending_attempts.clear()
         self.pending_timings.clear()
