@@ -4,7 +4,9 @@ A batch of rows is cut into micro-batches of ``chunk_rows`` rows.  Stage 0
 embeds, every stage runs its local layers, the last stage normalises and
 computes the selected-token log-probs (and the loss); hidden states travel
 forward and their gradients backward between neighbouring stages over
-``StageComm`` (NCCL p2p on GPUs).
+``StageComm`` (NCCL p2p on GPUs, one stream per direction).  Every receive
+is posted one receiving step ahead of the step that consumes it, so the
+transfer runs under the computation before it instead of between the two.
 
 * ``pp_logprobs``: forward only (old log-probs), GPipe order; the last stage
   broadcasts the log-probs to its pipeline column so every rank returns them
@@ -45,6 +47,42 @@ def _full_targets(tgt: torch.Tensor) -> torch.Tensor:
     return full
 
 
+class _RecvAhead:
+    """Posts every step's receive one receiving step early.
+
+    ``needs[k]`` is the receive of plan step ``k``: ("prev", shape) for a
+    forward step past the first stage, ("next", shape) for a backward step
+    before the last, or None.  ``advance(k)``, called as step ``k`` starts,
+    posts in plan order every receive up to the first receiving step after
+    ``k``, so that step's transfer runs while step ``k`` computes.  Plan order
+    is the order the neighbour sends in (forward micro-batches ascending,
+    backward micro-batches ascending), which keeps each direction's queue
+    matched."""
+
+    def __init__(self, comm: StageComm, needs: list, dtype: torch.dtype) -> None:
+        self.comm, self.dtype = comm, dtype
+        self.order = [(k, n) for k, n in enumerate(needs) if n is not None]
+        self.posted = 0
+
+    def advance(self, k: int) -> None:
+        last = next((i for i, (step, _) in enumerate(self.order) if step > k), len(self.order) - 1)
+        while self.posted <= last:
+            side, shape = self.order[self.posted][1]
+            (self.comm.prefetch_prev if side == "prev" else self.comm.prefetch_next)(shape, self.dtype)
+            self.posted += 1
+
+
+def _plan_needs(plan, chunks: list[slice], ps, shape_of) -> list:
+    needs = []
+    for _, step in plan:
+        rows = chunks[step.microbatch_idx].stop - chunks[step.microbatch_idx].start
+        if step.action == PipelineAction.FORWARD:
+            needs.append(None if ps.is_first_stage else ("prev", shape_of(rows)))
+        else:
+            needs.append(None if ps.is_last_stage else ("next", shape_of(rows)))
+    return needs
+
+
 def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor,
                 targets: torch.Tensor, *, chunk_rows: int) -> torch.Tensor:
     """log p(targets) [B, S-1] on every stage of the column (forward only)."""
@@ -53,8 +91,12 @@ def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.T
     H = m.cfg.hidden_size
     full = _full_targets(targets)
     outs = []
-    for sl in _chunks(B, chunk_rows):
+    chunks = _chunks(B, chunk_rows)
+    ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", ((c.stop - c.start) * S, H))
+                              for c in chunks], ACT_DTYPE)
+    for k, sl in enumerate(chunks):
         rows = sl.stop - sl.start
+        ahead.advance(k)
         meta = AttnMeta.from_mask(mask[sl])
         x = f.embed(seq[sl]) if ps.is_first_stage else comm.recv_prev((rows * S, H), ACT_DTYPE)
         xL, _ = f.stage_forward(x, meta)
@@ -90,13 +132,15 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     full = _full_targets(targets)
     chunks = _chunks(B, chunk_rows)
     plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
+    ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows * S, H)), ACT_DTYPE)
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
-    for phase, step in plan:
+    for k, (phase, step) in enumerate(plan):
         t_step = clock.now()
         c = step.microbatch_idx
         sl = chunks[c]
         rows = sl.stop - sl.start
+        ahead.advance(k)
         if step.action == PipelineAction.FORWARD:
             meta = AttnMeta.from_mask(mask[sl])
             if ps.is_first_stage:
@@ -164,9 +208,13 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
     H = model.cfg.hidden_size
     outs = []
     lora = EagerLoRA(model.lora, requires_grad=False)
+    chunks = _chunks(B, chunk_rows)
+    ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", (c.stop - c.start, S, H))
+                              for c in chunks], model.dtype)
     with torch.no_grad():
-        for sl in _chunks(B, chunk_rows):
+        for k, sl in enumerate(chunks):
             rows = sl.stop - sl.start
+            ahead.advance(k)
             x = None if ps.is_first_stage else comm.recv_prev((rows, S, H), model.dtype)
             xL = model.forward(seq[sl], mask[sl], x=x, lora=lora)
             if ps.is_last_stage:
@@ -195,13 +243,15 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
     chunks = _chunks(B, chunk_rows)
     plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
     lora = EagerLoRA(model.lora, requires_grad=True)
+    ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows, S, H)), model.dtype)
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
-    for phase, step in plan:
+    for k, (phase, step) in enumerate(plan):
         t_step = clock.now()
         c = step.microbatch_idx
         sl = chunks[c]
         rows = sl.stop - sl.start
+        ahead.advance(k)
         if step.action == PipelineAction.FORWARD:
             x = None
             if not ps.is_first_stage:

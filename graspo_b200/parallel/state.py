@@ -40,6 +40,10 @@ class ParallelState:
     tp_ranks: list[int] = field(default_factory=list)
     pp_ranks: list[int] = field(default_factory=list)
     dp_ranks: list[int] = field(default_factory=list)
+    # one two-rank group per stage boundary and direction: "send_next" /
+    # "recv_prev" carry activations forward, "send_prev" / "recv_next" carry
+    # their gradients back (see ``initialize``)
+    stage_groups: dict[str, object] = field(default_factory=dict)
     owns_process_group: bool = False
 
     @property
@@ -146,6 +150,25 @@ def initialize(
                 group = dist.new_group(ranks, timeout=timeout)
                 if rank in ranks:
                     state.dp_group, state.dp_ranks = group, ranks
+        # Stage-boundary links.  Each boundary of each pipeline column gets two
+        # groups, one per direction, so the activations going forward and the
+        # gradients coming back queue on different NCCL streams.  On one
+        # stream, a large send posted ahead of a receive that the peer must
+        # complete first (1F1B: stage s sends micro-batch i+1 forward while
+        # stage s+1 sends the gradient of micro-batch i back) waits forever;
+        # with one direction per stream both ends post in the same order.
+        for d in range(dp):
+            for t in range(tp):
+                for p in range(pp - 1):
+                    pair = [state.rank_of(tp=t, pp=p, dp=d), state.rank_of(tp=t, pp=p + 1, dp=d)]
+                    fwd = dist.new_group(pair, timeout=timeout)
+                    bwd = dist.new_group(pair, timeout=timeout)
+                    if rank == pair[0]:
+                        state.stage_groups["send_next"] = fwd
+                        state.stage_groups["recv_next"] = bwd
+                    elif rank == pair[1]:
+                        state.stage_groups["recv_prev"] = fwd
+                        state.stage_groups["send_prev"] = bwd
     else:
         state.tp_ranks, state.pp_ranks, state.dp_ranks = [0], [0], [0]
     _STATE = state
