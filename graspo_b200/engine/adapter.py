@@ -186,8 +186,6 @@ class Qwen3Adapter:
             from graspo_b200.engine.rollout import FusedRolloutEngine
             from graspo_b200.models.fused import FusedQwen3
 
-            if flow.sequence_parallel and self.ps.pp_size > 1:
-                raise NotImplementedError("sequence parallelism together with pipeline stages is not supported")
             # training / log-prob passes (optionally sequence-parallel); the rollout
             # engine keeps whole-sequence prefill
             self._fused = FusedQwen3(self.model, sequence_parallel=flow.sequence_parallel)

@@ -31,13 +31,28 @@ from graspo_b200.parallel.p2p import StageComm
 from graspo_b200.parallel.schedule import PipelineAction, get_scheduler
 from graspo_b200.utils.timing import NULL_CLOCK, PhaseClock, schedule_phases
 
-# the fused layers produce bf16 activations (the GEMMs store bf16)
+# the fused layers produce bf16 activations (the GEMMs store bf16); stage
+# transfers use it on the wire whatever the model's parameter dtype
 ACT_DTYPE = torch.bfloat16
 
 
 def _chunks(B: int, rows: int) -> list[slice]:
     rows = max(1, int(rows))
     return [slice(i, min(B, i + rows)) for i in range(0, B, rows)]
+
+
+def _sp_pad(f: FusedQwen3, seq, mask, targets):
+    """Under sequence parallelism every micro-batch's tokens split evenly over the
+    TP ranks: pad the sequence dimension to a multiple of TP with masked pad
+    tokens.  Returns the padded seq, mask and targets and the token divisor
+    (``tp`` with SP, else 1)."""
+    tp = f.m.ps.tp_size if f.sp else 1
+    pad = (-seq.shape[1]) % tp
+    if pad:
+        seq = torch.cat([seq, seq.new_zeros(seq.shape[0], pad)], 1)
+        mask = torch.cat([mask, mask.new_zeros(mask.shape[0], pad)], 1)
+        targets = torch.cat([targets, targets.new_zeros(targets.shape[0], pad)], 1)
+    return seq, mask, targets, tp
 
 
 def _full_targets(tgt: torch.Tensor) -> torch.Tensor:
@@ -85,29 +100,34 @@ def _plan_needs(plan, chunks: list[slice], ps, shape_of) -> list:
 
 def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor,
                 targets: torch.Tensor, *, chunk_rows: int) -> torch.Tensor:
-    """log p(targets) [B, S-1] on every stage of the column (forward only)."""
+    """log p(targets) [B, S-1] on every stage of the column (forward only).
+
+    With sequence parallelism each TP rank carries, and sends to the same TP
+    rank of the next stage, its 1/tp share of a micro-batch's tokens."""
     m, ps = f.m, comm.ps
-    B, S = seq.shape
+    B, S_in = seq.shape
+    seq, mask, targets, tp = _sp_pad(f, seq, mask, targets)
+    S = seq.shape[1]
     H = m.cfg.hidden_size
     full = _full_targets(targets)
     outs = []
     chunks = _chunks(B, chunk_rows)
-    ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", ((c.stop - c.start) * S, H))
+    ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", ((c.stop - c.start) * S // tp, H))
                               for c in chunks], ACT_DTYPE)
     for k, sl in enumerate(chunks):
         rows = sl.stop - sl.start
         ahead.advance(k)
         meta = AttnMeta.from_mask(mask[sl])
-        x = f.embed(seq[sl]) if ps.is_first_stage else comm.recv_prev((rows * S, H), ACT_DTYPE)
+        x = f.sp_shard(f.embed(seq[sl])) if ps.is_first_stage else comm.recv_prev((rows * S // tp, H), ACT_DTYPE)
         xL, _ = f.stage_forward(x, meta)
         if ps.is_last_stage:
             hn, _ = f.final_norm(xL)
-            lp, _ = f.token_logprobs(hn, full[sl].reshape(-1))
-            outs.append(lp.view(rows, S)[:, :-1])
+            lp, _ = f.token_logprobs(f.sp_gather(hn), full[sl].reshape(-1))
+            outs.append(lp.view(rows, S)[:, : S_in - 1])
         else:
-            comm.send_next(xL)
+            comm.send_next(xL.to(ACT_DTYPE))
     comm.flush()
-    logp = torch.cat(outs, 0).contiguous() if ps.is_last_stage else torch.empty(B, S - 1, device=seq.device)
+    logp = torch.cat(outs, 0).contiguous() if ps.is_last_stage else torch.empty(B, S_in - 1, device=seq.device)
     return comm.broadcast_from_last(logp)
 
 
@@ -127,12 +147,14 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     """
     m, ps = f.m, comm.ps
     C = ext()
-    B, S = seq.shape
+    B, S_in = seq.shape
+    seq, mask, targets, tp = _sp_pad(f, seq, mask, targets)
+    S = seq.shape[1]
     H = m.cfg.hidden_size
     full = _full_targets(targets)
     chunks = _chunks(B, chunk_rows)
     plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
-    ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows * S, H)), ACT_DTYPE)
+    ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows * S // tp, H)), ACT_DTYPE)
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
     for k, (phase, step) in enumerate(plan):
@@ -144,32 +166,34 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
         if step.action == PipelineAction.FORWARD:
             meta = AttnMeta.from_mask(mask[sl])
             if ps.is_first_stage:
-                x = f.embed(seq[sl])
+                x = f.sp_shard(f.embed(seq[sl]))
             else:
                 with clock.time("pipeline_recv_sec"):
-                    x = comm.recv_prev((rows * S, H), ACT_DTYPE)
+                    x = comm.recv_prev((rows * S // tp, H), ACT_DTYPE)
             with clock.time("pipeline_stage_compute_sec"):
                 xL, inputs = f.stage_forward(x, meta, train=True, seed=seed, keep_inputs=True)
             clock.calls["pipeline_forward_calls"] += 1
             if ps.is_last_stage:
                 with clock.time("pipeline_lm_head_sec"):
                     hn, rstd = f.final_norm(xL)
+                    hn = f.sp_gather(hn)
                     fc = full[sl].reshape(-1).contiguous()
                     lp, lse = f.token_logprobs(hn, fc)
                 with clock.time("pipeline_loss_sec"):
-                    loss_c, dlogp = loss_fn(lp.view(rows, S)[:, :-1], sl)
+                    loss_c, dlogp = loss_fn(lp.view(rows, S)[:, : S_in - 1], sl)
                     total += loss_c.reshape(1)
                 saved[c] = (meta, inputs, xL, hn, rstd, fc, lse, dlogp)
             else:
                 with clock.time("pipeline_send_sec"):
-                    comm.send_next(xL)
+                    comm.send_next(xL.to(ACT_DTYPE))
                 saved[c] = (meta, inputs)
         else:
             if ps.is_last_stage:
                 meta, inputs, xL, hn, rstd, fc, lse, dlogp = saved.pop(c)
                 with clock.time("pipeline_backward_autograd_sec"):
                     g = torch.zeros(rows, S, device=seq.device, dtype=torch.float32)
-                    g[:, :-1] = dlogp
+                    g[:, : S_in - 1] = dlogp
+                    # the head's input gradient, this rank's token shard under SP
                     dhn = f.token_logprobs_backward(hn, fc, lse, g.view(-1))
                     dx = torch.empty_like(xL)
                     C.rmsnorm_bwd(dhn, xL, m.norm, rstd, None, dx, m.cfg.rms_norm_eps)
@@ -177,12 +201,12 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
             else:
                 meta, inputs = saved.pop(c)
                 with clock.time("pipeline_grad_recv_sec"):
-                    dx = comm.recv_next((rows * S, H), ACT_DTYPE)
+                    dx = comm.recv_next((rows * S // tp, H), ACT_DTYPE)
             with clock.time("pipeline_backward_autograd_sec"):
                 dx_in = f.stage_backward(inputs, dx, meta, train=True, seed=seed)
             if not ps.is_first_stage:
                 with clock.time("pipeline_grad_send_sec"):
-                    comm.send_prev(dx_in)
+                    comm.send_prev(dx_in.to(ACT_DTYPE))
         clock.add(f"{phase}_sec", clock.now() - t_step)
     comm.flush()
     return comm.broadcast_from_last(total)

@@ -14,13 +14,14 @@ TARGETS = {"language.self_attn.q_proj", "language.self_attn.k_proj", "language.s
            "language.self_attn.o_proj", "language.mlp.gate_proj", "language.mlp.up_proj", "language.mlp.down_proj"}
 
 
-def _model(path, ps):
+def _model(path, ps, **stage):
     from graspo_b200.models.config import load_decoder_config
     from graspo_b200.models.loader import SafetensorIndex
     from graspo_b200.models.qwen3 import Qwen3Model
 
     m = Qwen3Model(load_decoder_config(path), SafetensorIndex(path), ps=ps, lora_targets=TARGETS, lora_r=8,
-                   lora_alpha=16, lora_dropout=0.0, dtype=torch.float32, device=torch.device("cpu"), seed=3)
+                   lora_alpha=16, lora_dropout=0.0, dtype=torch.float32, device=torch.device("cpu"), seed=3,
+                   **stage)
     with torch.no_grad():
         for mod in m.lora.modules:
             g = torch.Generator().manual_seed(zlib.crc32(mod.module_name.encode()))
@@ -99,3 +100,58 @@ def test_sequence_parallel_tp2_matches_tp1(tmp_path):
 
     path = write_qwen3_checkpoint(tmp_path / "sp", SMALL, seed=2, std=0.05, with_tokenizer=False)
     run_world(2, _worker, path, timeout=600)
+
+
+def _pp_worker(rank, world, path):
+    """TP=2 with SP x PP=2: pipelined log-probs and 1F1B gradients equal the
+    unsharded model's; each stage sends its TP rank's token shard."""
+    from graspo_b200.engine.pipeline import pp_logprobs, pp_train
+    from graspo_b200.models.fused import FusedQwen3
+    from graspo_b200.ops.emulate import use_emulation
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.p2p import StageComm
+    from graspo_b200.parallel.state import ParallelState
+
+    ps = pstate.initialize(2, 2, 0, timeout_sec=60, device="cpu")
+    comm = StageComm(ps)
+    g = torch.Generator().manual_seed(1)
+    seq = torch.randint(0, 500, (3, 23), generator=g)   # odd length: padded to 24 under SP
+    mask = torch.ones(3, 23, dtype=torch.bool)
+    mask[0, :4] = False
+    mask[2, -3:] = False
+    w = torch.randn(3, 22, generator=g) * (mask[:, :-1] & mask[:, 1:])
+    first, last = ps.pp_rank == 0, ps.pp_rank == 1
+    with use_emulation():
+        stage = _model(path, ps, local_layers=[0] if first else [1], include_embed=first, include_head=last)
+        f = FusedQwen3(stage, sequence_parallel=True)
+        lp = pp_logprobs(f, comm, seq, mask, seq[:, 1:], chunk_rows=1)
+        stage.lora.grads.zero_()
+
+        def loss_fn(lp_c, sl):
+            return (lp_c * w[sl]).sum().reshape(1), w[sl].clone()
+
+        loss = pp_train(f, comm, seq, mask, seq[:, 1:], loss_fn, seed=0, chunk_rows=1, schedule="one_f_one_b")
+        dist.all_reduce(stage.lora.grads[: stage.lora.replicated_numel], group=ps.tp_group)
+        m1 = _model(path, ParallelState())
+        lp1 = _run(FusedQwen3(m1), seq, mask, w)
+    valid = mask[:, :-1] & mask[:, 1:]
+    assert lp.shape == lp1.shape
+    assert (lp - lp1).abs()[valid].max().item() < 3e-2
+    assert abs(loss.item() - (lp1 * w).sum().item()) < 5e-2 * (1 + abs(loss.item()))
+    for mod2 in stage.lora.modules:
+        mod1 = m1.lora.by_name[mod2.module_name]
+        if mod2.shard_kind == "out":
+            a1, b1 = mod1.a_grad, mod1.b_grad[mod2.row_start : mod2.row_stop]
+        else:
+            a1, b1 = mod1.a_grad[:, mod2.col_start : mod2.col_stop], mod1.b_grad
+        for x1, x2 in ((a1, mod2.a_grad), (b1, mod2.b_grad)):
+            cos = torch.nn.functional.cosine_similarity(x1.flatten(), x2.flatten(), dim=0).item()
+            assert cos > 0.99, (mod2.module_name, cos)
+    pstate.destroy()
+
+
+def test_sequence_parallel_with_pipeline_stages(tmp_path):
+    from graspo_b200.utils.synth import write_qwen3_checkpoint
+
+    path = write_qwen3_checkpoint(tmp_path / "sp_pp", SMALL, seed=2, std=0.05, with_tokenizer=False)
+    run_world(4, _pp_worker, path, timeout=600)
