@@ -294,7 +294,43 @@ class Qwen3Adapter:
     # ------------------------------------------------------------ images
     @property
     def _vision_pad_id(self) -> int:
-        return int(self.tokenizer.convert_tokens_to_ids("<|vision_pad|>"))
+        """The image placeholder token: config.json ``image_token_id`` (the Qwen-VL
+        chat templates write ``<|image_pad|>``), else the tokenizer's own."""
+        tid = (getattr(self.model.cfg, "extra", None) or {}).get("image_token_id")
+        if tid is not None:
+            return int(tid)
+        unk = getattr(self.tokenizer, "unk_token_id", None)
+        for name in ("<|image_pad|>", "<|vision_pad|>"):
+            i = self.tokenizer.convert_tokens_to_ids(name)
+            if i is not None and i != unk:
+                return int(i)
+        raise ValueError("no image placeholder token (config.json image_token_id)")
+
+    def _sft_images(self, item: dict[str, Any]) -> tuple[torch.Tensor, torch.Tensor, list[dict]]:
+        """An SFT item's ids and labels with each image placeholder repeated once per
+        merged vision token (labels -100 there), and the item's images."""
+        from graspo_b200.models.vision import expand_image_placeholders, image_grid, image_size, merged_tokens
+
+        row = item.get("_multimodal_row")
+        vc = getattr(self.model, "vision_cfg", None)
+        if not row or vc is None:
+            return item["input_ids"], item["labels"], []
+        media = [m for m in row.get("media") or [] if m.get("type") == "image"]
+        if len(media) != len(row.get("media") or []):
+            raise NotImplementedError("video inputs are not supported")
+        pad = self._vision_pad_id
+        counts = [merged_tokens(image_grid(*image_size(m["path"]), vc), vc) for m in media]
+        ids = item["input_ids"].tolist()
+        labels = item["labels"].tolist()
+        out_ids = expand_image_placeholders(ids, pad, counts)
+        out_labels, k = [], 0
+        for t, lab in zip(ids, labels, strict=True):
+            if t == pad and k < len(counts):
+                out_labels.extend([-100] * counts[k])
+                k += 1
+            else:
+                out_labels.append(lab)
+        return torch.tensor(out_ids), torch.tensor(out_labels), media
 
     def _image_features(self, media_rows: list[list[dict]], vision_lora=None):
         """Vision-tower features of every image of every row, rows in order, and
@@ -339,8 +375,21 @@ class Qwen3Adapter:
         With vision LoRA targets and ``train``, the features carry an autograd
         graph to the tower's LoRA leaves (kept in ``self._vision_pass`` until
         the backward has run, see ``_finish_vision_pass``)."""
-        from graspo_b200.models.vision import ImageInputs, VisionLoRA
+        from graspo_b200.models.vision import ImageInputs, VisionLoRA, image_grid, image_size
 
+        if getattr(self.model, "vision", None) is None and getattr(self.model, "vision_cfg", None) is not None:
+            # a pipeline stage after the first: the grids only (placeholder
+            # counts and multimodal positions), no tower and no features
+            vc = self.model.vision_cfg
+            m = vc.spatial_merge_size
+            grids = []
+            for media in media_rows:
+                for item in media or []:
+                    if item.get("type") != "image":
+                        raise NotImplementedError("video inputs are not supported")
+                    t, gh, gw = image_grid(*image_size(item["path"]), vc)
+                    grids.append((t, gh // m, gw // m))
+            return ImageInputs(None, self._vision_pad_id, grids) if grids else None
         vlora = None
         if self.model.lora.vision_modules():
             vlora = VisionLoRA(self.model.lora, training=train)
@@ -362,10 +411,10 @@ class Qwen3Adapter:
     def _generate_multimodal(self, samples, *, rollout_group_size: int, max_new_tokens: int,
                              max_prompt_length: int | None = None, temperature: float = 1.0, top_p: float = 1.0,
                              chat_template_kwargs: dict | None = None, **_: Any) -> list[NativeGeneration]:
-        from graspo_b200.models.vision import expand_image_placeholders, load_image, merged_tokens, preprocess
+        from graspo_b200.models.vision import expand_image_placeholders, image_grid, image_size, merged_tokens
 
-        vt = getattr(self.model, "vision", None)
-        if vt is None:
+        vc = getattr(self.model, "vision_cfg", None)
+        if vc is None:
             raise NotImplementedError("this checkpoint has no vision tower (config.json vision_config)")
         t0 = time.monotonic()
         max_len = int(max_prompt_length or self.config.data.max_prompt_length)
@@ -375,7 +424,7 @@ class Qwen3Adapter:
         prompts, media_rows = [], []
         for s, ids in zip(samples, enc["input_ids"], strict=True):
             media = [m for m in (s.media or []) if m.get("type") == "image"]
-            counts = [merged_tokens(preprocess(load_image(m["path"]), vt.cfg)[1], vt.cfg) for m in media]
+            counts = [merged_tokens(image_grid(*image_size(m["path"]), vc), vc) for m in media]
             ids = expand_image_placeholders(list(ids), pad, counts)
             if len(ids) > max_len:
                 # keep the image tokens: drop text from the front of the prompt
@@ -456,15 +505,17 @@ class Qwen3Adapter:
         seq = sequences.to(dev)
         mask = attention_mask.to(dev).bool()
         media_rows = (metadata or {}).get("_media_rows") if isinstance(metadata, dict) else None
-        if media_rows and any(media_rows):
-            return self._logprobs(seq, mask, train=False, embed_hook=self._image_hook(media_rows))[0]
+        hook = self._image_hook(media_rows) if media_rows and any(media_rows) else None
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_logprobs, pp_logprobs_autograd
 
             if not self.fused:
                 return pp_logprobs_autograd(self.model, self._comm, seq, mask, seq[:, 1:],
-                                            chunk_rows=self._pp_chunk_rows(seq))
-            return pp_logprobs(self._fused, self._comm, seq, mask, seq[:, 1:], chunk_rows=self._pp_chunk_rows(seq))
+                                            chunk_rows=self._pp_chunk_rows(seq), embed_hook=hook)
+            return pp_logprobs(self._fused, self._comm, seq, mask, seq[:, 1:], chunk_rows=self._pp_chunk_rows(seq),
+                               embed_hook=hook)
+        if hook is not None:
+            return self._logprobs(seq, mask, train=False, embed_hook=hook)[0]
         outs = []
         for sl in self._token_budget_chunks(seq.shape[0], seq.shape[1]):
             outs.append(self._logprobs(seq[sl], mask[sl], train=False)[0])
@@ -623,22 +674,20 @@ class Qwen3Adapter:
         if self.ps.pp_size > 1 and not self.fused:
             from graspo_b200.engine.pipeline import pp_train_autograd
 
-            if embed_hook is not None:
-                raise NotImplementedError("image inputs with pipeline stages are not supported")
             self.loss_fn.policy_ratio_clip_eps = clip_eps
 
             def chunk_loss(logp_c, sl):
                 return self.loss_fn(logp_c, old[sl], adv[sl], act[sl]) * ((sl.stop - sl.start) / B)
 
-            return pp_train_autograd(self.model, self._comm, seq, mask, seq[:, 1:], chunk_loss,
+            loss = pp_train_autograd(self.model, self._comm, seq, mask, seq[:, 1:], chunk_loss,
                                      chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
-                                     clock=self._clock)
+                                     clock=self._clock, embed_hook=embed_hook)
+            self._finish_vision_pass()
+            return loss
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
             from graspo_b200.ops._ext import ext
 
-            if embed_hook is not None:
-                raise NotImplementedError("image inputs with pipeline stages are not supported")
             old_c, adv_c, act_c = old.contiguous(), adv.contiguous(), act.to(torch.uint8).contiguous()
 
             def loss_fn(logp_c, sl):
@@ -649,9 +698,11 @@ class Qwen3Adapter:
                                 dlogp, None)
                 return loss * (rows / B), dlogp
 
-            return pp_train(self._fused, self._comm, seq, mask, seq[:, 1:], loss_fn, seed=seed,
+            loss = pp_train(self._fused, self._comm, seq, mask, seq[:, 1:], loss_fn, seed=seed,
                             chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
-                            clock=self._clock)
+                            clock=self._clock, embed_hook=embed_hook)
+            self._finish_vision_pass()
+            return loss
         clock = self._clock
         if self.fused:
             from graspo_b200.ops._ext import ext
@@ -765,17 +816,19 @@ class Qwen3Adapter:
         self._clock = clock = PhaseClock(sync=self.config.graspoflow.synchronize_cuda_timing)
         for _ in range(int(optimize_iterations_per_step)):
             for start in range(0, len(sft_batches), fbs):
-                chunk = sft_batches[start : start + fbs]
-                S = max(int(b["input_ids"].shape[0]) for b in chunk)
+                chunk = [self._sft_images(b) for b in sft_batches[start : start + fbs]]
+                S = max(int(b_ids.shape[0]) for b_ids, _, _ in chunk)
                 ids = torch.full((len(chunk), S), pad, dtype=torch.long)
                 labels = torch.full((len(chunk), S), -100, dtype=torch.long)
                 mask = torch.zeros((len(chunk), S), dtype=torch.bool)
-                for i, b in enumerate(chunk):
-                    n = int(b["input_ids"].shape[0])
-                    ids[i, :n], labels[i, :n], mask[i, :n] = b["input_ids"], b["labels"], True
+                for i, (b_ids, b_labels, _) in enumerate(chunk):
+                    n = int(b_ids.shape[0])
+                    ids[i, :n], labels[i, :n], mask[i, :n] = b_ids, b_labels, True
                 ids, labels, mask = ids.to(self.device), labels.to(self.device), mask.to(self.device)
+                media_rows = [media for _, _, media in chunk]
+                hook = self._image_hook(media_rows, train=True) if any(media_rows) else None
                 self.optimizer.zero_grad()
-                loss = self._backward_sft(ids, mask, labels, steps)
+                loss = self._backward_sft(ids, mask, labels, steps, embed_hook=hook)
                 with clock.time("grad_sync_sec"):
                     self._tp_sync_replicated_grads()
                     self._dp_average_grads()
@@ -791,9 +844,16 @@ class Qwen3Adapter:
             **clock.summary(),
         })
 
-    def _backward_sft(self, ids, mask, labels, step: int):
+    def _backward_sft(self, ids, mask, labels, step: int, embed_hook=None):
         """Token cross-entropy = -mean log p(label) over labelled positions
-        (the quantity of core.loss.sft_cross_entropy_loss, without logits)."""
+        (the quantity of core.loss.sft_cross_entropy_loss, without logits).
+        ``embed_hook`` places the batch's image features (multimodal SFT,
+        reference: models/qwen35_36/training.py:75-90)."""
+        loss = self._backward_sft_pass(ids, mask, labels, step, embed_hook)
+        self._finish_vision_pass()
+        return loss
+
+    def _backward_sft_pass(self, ids, mask, labels, step: int, embed_hook):
         tgt = labels[:, 1:]
         valid = tgt.ne(-100)
         denom = valid.sum().clamp_min(1)
@@ -806,7 +866,7 @@ class Qwen3Adapter:
 
             return pp_train_autograd(self.model, self._comm, ids, mask, safe, chunk_loss,
                                      chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
-                                     clock=self._clock)
+                                     clock=self._clock, embed_hook=embed_hook)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
 
@@ -816,17 +876,17 @@ class Qwen3Adapter:
 
             return pp_train(self._fused, self._comm, ids, mask, safe, loss_fn, seed=step,
                             chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
-                            clock=self._clock)
+                            clock=self._clock, embed_hook=embed_hook)
         clock = self._clock
         if self.fused:
             with clock.time("micro_batch_forward_sec"):
-                logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe)
+                logp, ctx = self._logprobs(ids, mask, train=True, seed=step, targets=safe, embed_hook=embed_hook)
                 loss = -(logp * valid).sum() / denom
             with clock.time("backward_sec"):
                 self._fused_backward_from_logp_grad(ctx, -(valid.float() / denom), step)
             return loss.detach().reshape(1)
         with clock.time("micro_batch_forward_sec"):
-            logp, lora = self._logprobs(ids, mask, train=True, targets=safe)
+            logp, lora = self._logprobs(ids, mask, train=True, targets=safe, embed_hook=embed_hook)
             loss = -(logp * valid).sum() / denom
         with clock.time("backward_sec"):
             loss.backward()

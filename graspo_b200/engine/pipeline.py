@@ -99,11 +99,13 @@ def _plan_needs(plan, chunks: list[slice], ps, shape_of) -> list:
 
 
 def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor,
-                targets: torch.Tensor, *, chunk_rows: int) -> torch.Tensor:
+                targets: torch.Tensor, *, chunk_rows: int, embed_hook=None) -> torch.Tensor:
     """log p(targets) [B, S-1] on every stage of the column (forward only).
 
     With sequence parallelism each TP rank carries, and sends to the same TP
-    rank of the next stage, its 1/tp share of a micro-batch's tokens."""
+    rank of the next stage, its 1/tp share of a micro-batch's tokens.
+    ``embed_hook`` (image inputs) edits the first stage's embeddings, one
+    micro-batch's rows at a time."""
     m, ps = f.m, comm.ps
     B, S_in = seq.shape
     seq, mask, targets, tp = _sp_pad(f, seq, mask, targets)
@@ -112,13 +114,18 @@ def pp_logprobs(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.T
     full = _full_targets(targets)
     outs = []
     chunks = _chunks(B, chunk_rows)
+    hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None and ps.is_first_stage else None
     ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", ((c.stop - c.start) * S // tp, H))
                               for c in chunks], ACT_DTYPE)
     for k, sl in enumerate(chunks):
         rows = sl.stop - sl.start
         ahead.advance(k)
         meta = AttnMeta.from_mask(mask[sl])
-        x = f.sp_shard(f.embed(seq[sl])) if ps.is_first_stage else comm.recv_prev((rows * S // tp, H), ACT_DTYPE)
+        if ps.is_first_stage:
+            x = f.embed(seq[sl])
+            x = f.sp_shard(hooks[k](seq[sl], x).detach() if hooks is not None else x)
+        else:
+            x = comm.recv_prev((rows * S // tp, H), ACT_DTYPE)
         xL, _ = f.stage_forward(x, meta)
         if ps.is_last_stage:
             hn, _ = f.final_norm(xL)
@@ -136,7 +143,7 @@ LossFn = Callable[[torch.Tensor, slice], tuple[torch.Tensor, torch.Tensor]]
 
 def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
              loss_fn: LossFn, *, seed: int, chunk_rows: int, schedule: str = "one_f_one_b",
-             clock: PhaseClock = NULL_CLOCK) -> torch.Tensor:
+             clock: PhaseClock = NULL_CLOCK, embed_hook=None) -> torch.Tensor:
     """Forward + backward of one optimizer step into the LoRA gradient buffer.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
@@ -144,6 +151,10 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     already carry the chunk's weight.  Returns the summed loss on every stage.
     ``clock`` collects the stage timers (recv / send / compute / head / loss /
     backward, and the fill / steady / drain phases of the schedule).
+    ``embed_hook`` (image inputs) edits the first stage's embeddings per
+    micro-batch; with LoRA on the vision tower, the embedding gradient of
+    each micro-batch's image rows is collected and sent through the tower
+    once, after the last backward.
     """
     m, ps = f.m, comm.ps
     C = ext()
@@ -155,6 +166,8 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     chunks = _chunks(B, chunk_rows)
     plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
     ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows * S // tp, H)), ACT_DTYPE)
+    hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None and ps.is_first_stage else None
+    graphs: dict[int, torch.Tensor] = {}  # micro-batch -> embeddings carrying the image-feature graph
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
     for k, (phase, step) in enumerate(plan):
@@ -166,7 +179,12 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
         if step.action == PipelineAction.FORWARD:
             meta = AttnMeta.from_mask(mask[sl])
             if ps.is_first_stage:
-                x = f.sp_shard(f.embed(seq[sl]))
+                x = f.embed(seq[sl])
+                if hooks is not None:
+                    x = hooks[c](seq[sl], x)
+                    if x.requires_grad:
+                        graphs[c], x = x, x.detach()
+                x = f.sp_shard(x)
             else:
                 with clock.time("pipeline_recv_sec"):
                     x = comm.recv_prev((rows * S // tp, H), ACT_DTYPE)
@@ -204,12 +222,24 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
                     dx = comm.recv_next((rows * S // tp, H), ACT_DTYPE)
             with clock.time("pipeline_backward_autograd_sec"):
                 dx_in = f.stage_backward(inputs, dx, meta, train=True, seed=seed)
+                g0 = graphs.pop(c, None)
+                if g0 is not None:
+                    torch.autograd.backward(g0, f.sp_gather(dx_in).view_as(g0).to(g0.dtype))
             if not ps.is_first_stage:
                 with clock.time("pipeline_grad_send_sec"):
                     comm.send_prev(dx_in.to(ACT_DTYPE))
         clock.add(f"{phase}_sec", clock.now() - t_step)
     comm.flush()
+    if hooks is not None:
+        embed_hook.backward_into_tower()
     return comm.broadcast_from_last(total)
+
+
+def _mrope(model, seq, mask, hook):
+    """Multimodal positions of a micro-batch with images (every stage needs them)."""
+    if hook is None or not hook.grids or not hasattr(model, "mrope_positions"):
+        return None
+    return model.mrope_positions(seq, mask, hook)
 
 
 # ---------------------------------------------------------------- autograd stages
@@ -223,8 +253,11 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
 
 
 def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor, *,
-                         chunk_rows: int) -> torch.Tensor:
-    """log p(targets) [B, S-1] on every stage of the column (forward only)."""
+                         chunk_rows: int, embed_hook=None) -> torch.Tensor:
+    """log p(targets) [B, S-1] on every stage of the column (forward only).
+
+    With ``embed_hook`` (image inputs) the first stage places the image
+    features and every stage uses the multimodal positions of its micro-batch."""
     from graspo_b200.models.qwen3 import EagerLoRA
 
     ps = comm.ps
@@ -233,6 +266,7 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
     outs = []
     lora = EagerLoRA(model.lora, requires_grad=False)
     chunks = _chunks(B, chunk_rows)
+    hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None else [None] * len(chunks)
     ahead = _RecvAhead(comm, [None if ps.is_first_stage else ("prev", (c.stop - c.start, S, H))
                               for c in chunks], model.dtype)
     with torch.no_grad():
@@ -240,7 +274,8 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
             rows = sl.stop - sl.start
             ahead.advance(k)
             x = None if ps.is_first_stage else comm.recv_prev((rows, S, H), model.dtype)
-            xL = model.forward(seq[sl], mask[sl], x=x, lora=lora)
+            xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, pos=_mrope(model, seq[sl], mask[sl], hooks[k]),
+                               embed_hook=hooks[k] if ps.is_first_stage else None)
             if ps.is_last_stage:
                 outs.append(model.token_logprobs(xL[:, :-1], targets[sl]).float())
             else:
@@ -253,7 +288,8 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
 
 def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
                       loss_fn: Callable[[torch.Tensor, slice], torch.Tensor], *, chunk_rows: int,
-                      schedule: str = "one_f_one_b", clock: PhaseClock = NULL_CLOCK) -> torch.Tensor:
+                      schedule: str = "one_f_one_b", clock: PhaseClock = NULL_CLOCK,
+                      embed_hook=None) -> torch.Tensor:
     """Forward + backward of one optimizer step into ``model.lora.grads``.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
@@ -268,6 +304,7 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
     plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
     lora = EagerLoRA(model.lora, requires_grad=True)
     ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows, S, H)), model.dtype)
+    hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None else [None] * len(chunks)
     saved: dict[int, tuple] = {}
     total = torch.zeros(1, device=seq.device, dtype=torch.float32)
     for k, (phase, step) in enumerate(plan):
@@ -283,7 +320,9 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
                     x = comm.recv_prev((rows, S, H), model.dtype).requires_grad_(True)
             with torch.enable_grad():
                 with clock.time("pipeline_stage_compute_sec"):
-                    xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, training=True)
+                    xL = model.forward(seq[sl], mask[sl], x=x, lora=lora, training=True,
+                                       pos=_mrope(model, seq[sl], mask[sl], hooks[c]),
+                                       embed_hook=hooks[c] if ps.is_first_stage else None)
                 clock.calls["pipeline_forward_calls"] += 1
                 if ps.is_last_stage:
                     with clock.time("pipeline_lm_head_sec"):
@@ -311,4 +350,6 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
         clock.add(f"{phase}_sec", clock.now() - t_step)
     comm.flush()
     lora.accumulate_grads()
+    if embed_hook is not None:
+        embed_hook.backward_into_tower()
     return comm.broadcast_from_last(total)

@@ -134,14 +134,17 @@ class Qwen3Model:
             return loader.get_cols(name, a, b).to(device=dev, dtype=dt)
 
         self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
-        # frozen vision tower on the stage that embeds the tokens
-        self.vision = None
-        if include_embed and cfg.has_vision:
+        # frozen vision tower on the stage that embeds the tokens; every stage
+        # keeps its config (image grids give placeholder counts and positions)
+        self.vision = self.vision_cfg = None
+        if cfg.has_vision:
             from graspo_b200.models.vision import VisionConfig, VisionTower
 
             vc = dict(cfg.extra["vision_config"])
             vc.setdefault("out_hidden_size", cfg.hidden_size)
-            self.vision = VisionTower(VisionConfig.from_dict(vc), loader, "model.visual", dtype=dtype, device=self.device)
+            self.vision_cfg = VisionConfig.from_dict(vc)
+            if include_embed:
+                self.vision = VisionTower(self.vision_cfg, loader, "model.visual", dtype=dtype, device=self.device)
         self.layers: list[LayerWeights] = []
         modules: list[LoRAModule] = []
         H = cfg.hidden_size

@@ -227,14 +227,18 @@ class Qwen35Model:
         ir = (tr * self.inter_l, (tr + 1) * self.inter_l)
         self.embed = load(f"{pre}.embed_tokens.weight") if include_embed else None
         self.vocab_local, self.vocab_start = cfg.vocab_size, 0
-        # frozen vision tower on the stage that embeds the tokens (replicated over TP)
-        self.vision = None
-        if include_embed and cfg.has_vision:
+        # frozen vision tower on the stage that embeds the tokens (replicated over
+        # TP); every stage keeps its config (image grids give placeholder counts
+        # and the multimodal positions)
+        self.vision = self.vision_cfg = None
+        if cfg.has_vision:
             from graspo_b200.models.vision import VisionConfig, VisionTower
 
             vc = dict(cfg.extra["vision_config"])
             vc.setdefault("out_hidden_size", cfg.hidden_size)
-            self.vision = VisionTower(VisionConfig.from_dict(vc), loader, "model.visual", dtype=dtype, device=device)
+            self.vision_cfg = VisionConfig.from_dict(vc)
+            if include_embed:
+                self.vision = VisionTower(self.vision_cfg, loader, "model.visual", dtype=dtype, device=device)
         self.layers: list[HybridLayer] = []
         modules: list[LoRAModule] = []
         for idx in self.local_layers:
@@ -577,14 +581,15 @@ class HybridRolloutEngine:
     def generate(self, prompts, *, group_size, max_new_tokens, temperature, top_p, eos_id, pad_id,
                  ignore_eos=False, seed=0, embed_hook=None):
         """``embed_hook`` (``ImageInputs``) places image features on the prompts' placeholders;
-        decoding then continues from each prompt's largest multimodal position."""
+        decoding then continues from each prompt's largest multimodal position.
+        With pipeline stages the first stage's hook carries the features and
+        every stage's hook the image grids, from which each stage derives the
+        same multimodal positions."""
         import time
 
         from graspo_b200.engine.rollout import EagerRolloutEngine, RolloutResult, _gen_lengths
 
         m, dev, comm = self.m, self.m.device, self.comm
-        if embed_hook is not None and comm is not None:
-            raise NotImplementedError("image inputs with pipeline stages are not supported")
         last = comm is None or m.ps.is_last_stage
         n, G = len(prompts), int(group_size)
         lens = [max(1, len(p)) for p in prompts]

@@ -57,12 +57,33 @@ class VisionConfig:
         return self.in_channels * self.temporal_patch_size * self.patch_size ** 2
 
 
+def _resized(H: int, W: int, cfg: VisionConfig) -> tuple[int, int]:
+    """The image size ``preprocess`` resamples to: each side rounded to a whole
+    number of merge blocks (at least one)."""
+    unit = cfg.patch_size * cfg.spatial_merge_size
+    return max(unit, round(H / unit) * unit), max(unit, round(W / unit) * unit)
+
+
+def image_grid(height: int, width: int, cfg: VisionConfig) -> tuple[int, int, int]:
+    """The patch grid ``(1, gh, gw)`` that ``preprocess`` gives an image of this size."""
+    h2, w2 = _resized(int(height), int(width), cfg)
+    return 1, h2 // cfg.patch_size, w2 // cfg.patch_size
+
+
+def image_size(path: str) -> tuple[int, int]:
+    """(height, width) of an image file, read from its header."""
+    from PIL import Image
+
+    with Image.open(path) as im:
+        w, h = im.size
+    return h, w
+
+
 def preprocess(image: torch.Tensor, cfg: VisionConfig) -> tuple[torch.Tensor, tuple[int, int, int]]:
     """uint8 [H, W, 3] -> (patches [gh * gw, patch_dim] in merge-block order, (1, gh, gw))."""
-    unit = cfg.patch_size * cfg.spatial_merge_size
     img = image.permute(2, 0, 1).float()[None] / 255.0                       # [1, 3, H, W]
     H, W = img.shape[-2:]
-    h2, w2 = max(unit, round(H / unit) * unit), max(unit, round(W / unit) * unit)
+    h2, w2 = _resized(H, W, cfg)
     if (h2, w2) != (H, W):
         img = F.interpolate(img, size=(h2, w2), mode="bicubic", align_corners=False)
     mean = torch.tensor(MEAN).view(1, 3, 1, 1)
@@ -276,8 +297,48 @@ class ImageInputs:
     carries each image's merged grid ``(t, h, w)`` so a decoder with
     multimodal RoPE can give the placeholders their 3-D positions."""
 
-    def __init__(self, feats: torch.Tensor, pad_id: int, grids: list[tuple[int, int, int]]) -> None:
+    def __init__(self, feats: torch.Tensor | None, pad_id: int, grids: list[tuple[int, int, int]]) -> None:
+        # feats is None on pipeline stages after the first: they only need the
+        # grids (multimodal positions), the features enter with the embeddings
         self.feats, self.pad_id, self.grids = feats, int(pad_id), list(grids)
+        self._cut: list[tuple[torch.Tensor, torch.Tensor]] = []
+
+    def rows(self, ids: torch.Tensor, sl: slice) -> "ImageInputs":
+        """The images of rows ``sl`` of the batch ``ids`` [B, S]: each row's
+        placeholders take the next images' features, in row order."""
+        per_row = (ids == self.pad_id).sum(1).tolist()
+        f0 = sum(per_row[: sl.start])
+        f1 = f0 + sum(per_row[sl])
+        bounds, acc = [0], 0
+        for t, h, w in self.grids:
+            acc += t * h * w
+            bounds.append(acc)
+        if f0 not in bounds or f1 not in bounds:
+            raise ValueError("image placeholder counts do not match the image grids")
+        feats = self.feats[f0:f1] if self.feats is not None else None
+        return ImageInputs(feats, self.pad_id, self.grids[bounds.index(f0) : bounds.index(f1)])
+
+    def split_rows(self, ids: torch.Tensor, chunks: list[slice]) -> list["ImageInputs"]:
+        """One ``rows`` view per micro-batch.  Features that carry a graph to
+        the vision tower (LoRA on the tower, training) are cut from it here:
+        each micro-batch gets leaf features, and ``backward_into_tower`` sends
+        their gradients through the tower in one pass after the last
+        micro-batch's backward."""
+        parts = []
+        for sl in chunks:
+            sub = self.rows(ids, sl)
+            if sub.feats is not None and sub.feats.requires_grad:
+                leaf = sub.feats.detach().requires_grad_(True)
+                self._cut.append((sub.feats, leaf))
+                sub.feats = leaf
+            parts.append(sub)
+        return parts
+
+    def backward_into_tower(self) -> None:
+        pairs = [(g, leaf.grad) for g, leaf in self._cut if leaf.grad is not None]
+        self._cut = []
+        if pairs:
+            torch.autograd.backward([g for g, _ in pairs], [d.to(g.dtype) for g, d in pairs])
 
     def __call__(self, ids: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
         if x.dim() == 2:
