@@ -19,65 +19,34 @@ import argparse
 import json
 import time
 from pathlib import Path
-from statistics import mean
 from typing import Any
 
+from graspo_b200.analysis.scoring import score_row, summarize, write_report
 from graspo_b200.core.completion import raw_parsed_completion
 from graspo_b200.core.reward import GraspoReward
-
-
-def _scrubbed_metadata(sample) -> dict[str, Any]:
-    meta = {k: v for k, v in (sample.metadata or {}).items() if k not in ("image", "images", "video", "videos")}
-    meta["media"] = [{"type": m.get("type")} for m in (sample.media or [])]
-    return meta
 
 
 def evaluate_samples(runtime, config, samples: list, output_dir: str | Path, *,
                      checkpoint: str | None = None) -> dict[str, Any]:
     """Score ``rollout_group_size`` completions per sample; returns the summary."""
-    out = Path(output_dir)
-    out.mkdir(parents=True, exist_ok=True)
     tr = config.training
     reward = GraspoReward(config.reward)
     primary = bool(getattr(runtime, "is_primary", lambda: True)())
+    parse = getattr(runtime, "parse_completion", None)
     t0 = time.monotonic()
-    rows, group_rewards, group_ranges = [], [], []
+    rows = []
     for idx, sample in enumerate(samples):
         (gen,) = runtime.generate_sample_groups(
             samples=[sample], rollout_group_size=tr.rollout_group_size, max_new_tokens=tr.max_new_tokens,
             max_prompt_length=config.data.max_prompt_length, temperature=tr.temperature, top_p=tr.top_p,
             chat_template_kwargs=config.model.chat_template_kwargs)
-        parse = getattr(runtime, "parse_completion", None)
-        rewards = []
-        for text in gen.completions:
+        for j, text in enumerate(gen.completions):
             parsed = parse(text, sample) if callable(parse) else raw_parsed_completion(text)
-            res = reward.score_parsed(parsed, sample.targets, is_tool_call=sample.expects_tool_calls)
-            rewards.append(float(res.reward))
-            rows.append({"sample_index": idx, "completion": text, "reward": float(res.reward),
-                         "content_score": float(res.content_score), "all_right": bool(res.all_right),
-                         "matched_target_index": res.matched_target_index, "matched_target_id": res.matched_target_id,
-                         "parse_errors": list(parsed.parse_errors), "targets": sample.targets,
-                         "metadata": _scrubbed_metadata(sample)})
-        group_rewards.append(rewards)
-        group_ranges.append(max(rewards) - min(rewards) if rewards else 0.0)
-    flat = [r["reward"] for r in rows]
-    summary = {
-        "checkpoint": checkpoint,
-        "count": len(samples),
-        "completion_count": len(rows),
-        "rollout_group_size": int(tr.rollout_group_size),
-        "reward_mean": mean(flat) if flat else 0.0,
-        "reward_max_mean": mean(max(g) for g in group_rewards if g) if group_rewards else 0.0,
-        "reward_range_mean": mean(group_ranges) if group_ranges else 0.0,
-        "content_mean": mean(r["content_score"] for r in rows) if rows else 0.0,
-        "all_right_rate": (sum(r["all_right"] for r in rows) / len(rows)) if rows else 0.0,
-        "elapsed_sec": round(time.monotonic() - t0, 3),
-    }
+            rows.append(score_row(reward, parsed, sample, sample_index=idx, completion_index=j))
+    summary = summarize(rows, len(samples), checkpoint=checkpoint, rollout_group_size=int(tr.rollout_group_size),
+                        elapsed_sec=round(time.monotonic() - t0, 3))
     if primary:
-        with (out / "completions.jsonl").open("w", encoding="utf-8") as fh:
-            for row in rows:
-                fh.write(json.dumps(row, ensure_ascii=False) + "\n")
-        (out / "summary.json").write_text(json.dumps(summary, indent=2) + "\n", encoding="utf-8")
+        write_report(output_dir, rows, summary)
     return summary
 
 

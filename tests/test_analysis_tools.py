@@ -5,6 +5,7 @@ import json
 from pathlib import Path
 
 import pytest
+import torch
 
 from graspo_b200.analysis.datasets import split_jsonl, synth_image_records
 from graspo_b200.analysis.evaluate import evaluate_samples
@@ -116,3 +117,92 @@ def test_split_and_synthetic_images(tmp_path):
     assert split_jsonl(src, tmp_path / "t2.jsonl", tmp_path / "e2.jsonl", eval_count=3, seed=5)["eval_indices"] == e
     with pytest.raises(ValueError):
         split_jsonl(src, tmp_path / "a", tmp_path / "b", eval_count=10)
+
+
+def test_endpoint_eval_against_a_local_server(tmp_path):
+    """The OpenAI-compatible endpoint evaluator: wire format (image parts as data
+    URLs, tools, per-completion seeds), structured tool-call replies and text
+    replies both scored with the reward."""
+    import threading
+    from http.server import BaseHTTPRequestHandler, HTTPServer
+
+    from graspo_b200.analysis.endpoint_eval import EndpointClient, evaluate_endpoint
+
+    seen = []
+
+    class Handler(BaseHTTPRequestHandler):
+        def log_message(self, *a):
+            pass
+
+        def do_POST(self):
+            body = json.loads(self.rfile.read(int(self.headers["Content-Length"])))
+            seen.append((self.path, body))
+            if body.get("tools"):
+                msg = {"role": "assistant", "content": "",
+                       "tool_calls": [{"type": "function", "function": {"name": "set_status",
+                                                                         "arguments": json.dumps({"status": "ok"})}}]}
+            else:
+                status = "ok" if body["seed"] % 2 == 0 else "fail"
+                msg = {"role": "assistant", "content": '```json\n{"status": "%s"}\n```' % status}
+            data = json.dumps({"choices": [{"index": 0, "message": msg}]}).encode()
+            self.send_response(200)
+            self.send_header("Content-Type", "application/json")
+            self.send_header("Content-Length", str(len(data)))
+            self.end_headers()
+            self.wfile.write(data)
+
+    server = HTTPServer(("127.0.0.1", 0), Handler)
+    threading.Thread(target=server.serve_forever, daemon=True).start()
+    try:
+        (tmp_path / "img.png").write_bytes(b"\x89PNG fake")
+        tools = [{"type": "function", "function": {"name": "set_status", "parameters": {
+            "type": "object", "properties": {"status": {"type": "string"}}, "required": ["status"]}}}]
+        plain = Sample(messages=[{"role": "user", "content": [{"type": "image", "image": "img.png"},
+                                                              {"type": "text", "text": "status?"}]}],
+                       targets=[{"id": "t", "output": {"content": {"status": "ok"}}}])
+        tool = Sample(messages=[{"role": "user", "content": "set it"}], tools=tools,
+                      targets=[{"id": "c", "output": {"tool_calls": [{"name": "set_status",
+                                                                      "arguments": {"status": "ok"}}]}}])
+        cfg = GraspoConfig.from_dict({"training": {"output_dir": str(tmp_path), "max_new_tokens": 64}})
+        client = EndpointClient(f"http://127.0.0.1:{server.server_port}/v1", "m", timeout=10)
+        summary = evaluate_endpoint(cfg, [plain, tool], client, tmp_path / "ep", base_dir=tmp_path,
+                                    samples_per_prompt=2, seed=10, chat_template_kwargs={"enable_thinking": False})
+    finally:
+        server.shutdown()
+    assert [p for p, _ in seen] == ["/v1/chat/completions"] * 4
+    first = seen[0][1]
+    part = first["messages"][0]["content"][0]
+    assert part["type"] == "image_url" and part["image_url"]["url"].startswith("data:image/png;base64,")
+    assert [b["seed"] for _, b in seen] == [10, 11, 10, 11]
+    assert first["max_tokens"] == 64 and first["chat_template_kwargs"] == {"enable_thinking": False}
+    rows = [json.loads(x) for x in (tmp_path / "ep" / "completions.jsonl").read_text().splitlines()]
+    assert [r["all_right"] for r in rows] == [True, False, True, True]
+    assert rows[2]["parser_name"] == "endpoint_tool_calls" and rows[2]["tool_calls"][0]["name"] == "set_status"
+    assert summary["completion_count"] == 4 and summary["all_right_rate"] == 0.75
+
+
+def test_hf_baseline_generates_and_scores(tmp_path):
+    """The transformers baseline on a tiny checkpoint: prompts through the chat
+    template, sampled completions scored, EOS / length bookkeeping."""
+    from graspo_b200.analysis.hf_baseline import HFGenerator, run_baseline
+    from graspo_b200.utils.synth import TINY, write_qwen3_checkpoint
+
+    path = write_qwen3_checkpoint(tmp_path / "m", TINY, seed=1, device="cpu", dtype=torch.float32)
+    gen = HFGenerator(str(path), device="cpu", dtype=torch.float32)
+    sample = Sample(messages=[{"role": "user", "content": "read"}],
+                    targets=[{"id": "ok", "output": {"content": {"status": "ok"}}}])
+    cfg = GraspoConfig.from_dict({"training": {"output_dir": str(tmp_path), "max_new_tokens": 6,
+                                               "temperature": 1.0, "top_p": 1.0}})
+    summary = run_baseline(cfg, [sample, sample], gen, tmp_path / "hf", base_dir=tmp_path, samples_per_prompt=2,
+                           seed=3)
+    rows = [json.loads(x) for x in (tmp_path / "hf" / "completions.jsonl").read_text().splitlines()]
+    assert len(rows) == 4 and summary["completion_count"] == 4
+    for r in rows:
+        assert r["prompt_len"] > 0 and 0 <= r["completion_len"] <= 6
+        assert r["truncated"] == (not r["hit_eos"] and r["completion_len"] == 6)
+    assert "eos_rate" in summary and "truncated_rate" in summary
+    # the same seeds give the same completions
+    again = run_baseline(cfg, [sample, sample], gen, tmp_path / "hf2", base_dir=tmp_path, samples_per_prompt=2,
+                         seed=3)
+    assert again["reward_mean"] == summary["reward_mean"]
+    assert (tmp_path / "hf2" / "completions.jsonl").read_text() == (tmp_path / "hf" / "completions.jsonl").read_text()
