@@ -681,6 +681,7 @@ class Qwen3Adapter:
 
             loss = pp_train_autograd(self.model, self._comm, seq, mask, seq[:, 1:], chunk_loss,
                                      chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
+                                     max_inflight=int(self.config.graspoflow.pp_max_inflight_microbatches),
                                      clock=self._clock, embed_hook=embed_hook)
             self._finish_vision_pass()
             return loss
@@ -700,6 +701,7 @@ class Qwen3Adapter:
 
             loss = pp_train(self._fused, self._comm, seq, mask, seq[:, 1:], loss_fn, seed=seed,
                             chunk_rows=self._pp_chunk_rows(seq), schedule=self.config.graspoflow.pp_schedule,
+                            max_inflight=int(self.config.graspoflow.pp_max_inflight_microbatches),
                             clock=self._clock, embed_hook=embed_hook)
             self._finish_vision_pass()
             return loss
@@ -800,6 +802,15 @@ class Qwen3Adapter:
         }
         if clock.calls.get("pipeline_forward_calls"):
             metrics["pipeline_forward_calls"] = int(clock.calls["pipeline_forward_calls"])
+        if self.ps.pp_size > 1:
+            flow = self.config.graspoflow
+            metrics.update({
+                "pp_size": self.ps.pp_size, "pipeline_stage_rank": self.ps.pp_rank, "pp_schedule": flow.pp_schedule,
+                "placement_strategy": flow.placement_strategy,
+                "pipeline_pp_micro_batch_size": int(flow.pp_micro_batch_size),
+                "pp_max_inflight_microbatches": int(flow.pp_max_inflight_microbatches),
+                **clock.peaks,  # micro-batches per step and the most held at once on this stage
+            })
         self._rank_event("train_batch_after", {"metrics": metrics})
         return self._aggregate_rank_metrics(metrics)
 
@@ -866,6 +877,7 @@ class Qwen3Adapter:
 
             return pp_train_autograd(self.model, self._comm, ids, mask, safe, chunk_loss,
                                      chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
+                                     max_inflight=int(self.config.graspoflow.pp_max_inflight_microbatches),
                                      clock=self._clock, embed_hook=embed_hook)
         if self.ps.pp_size > 1:
             from graspo_b200.engine.pipeline import pp_train
@@ -876,6 +888,7 @@ class Qwen3Adapter:
 
             return pp_train(self._fused, self._comm, ids, mask, safe, loss_fn, seed=step,
                             chunk_rows=self._pp_chunk_rows(ids), schedule=self.config.graspoflow.pp_schedule,
+                            max_inflight=int(self.config.graspoflow.pp_max_inflight_microbatches),
                             clock=self._clock, embed_hook=embed_hook)
         clock = self._clock
         if self.fused:

@@ -28,7 +28,7 @@ import torch
 from graspo_b200.models.fused import AttnMeta, FusedQwen3
 from graspo_b200.ops._ext import ext
 from graspo_b200.parallel.p2p import StageComm
-from graspo_b200.parallel.schedule import PipelineAction, get_scheduler
+from graspo_b200.parallel.schedule import PipelineAction, get_scheduler, peak_inflight
 from graspo_b200.utils.timing import NULL_CLOCK, PhaseClock, schedule_phases
 
 # the fused layers produce bf16 activations (the GEMMs store bf16); stage
@@ -143,7 +143,7 @@ LossFn = Callable[[torch.Tensor, slice], tuple[torch.Tensor, torch.Tensor]]
 
 def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
              loss_fn: LossFn, *, seed: int, chunk_rows: int, schedule: str = "one_f_one_b",
-             clock: PhaseClock = NULL_CLOCK, embed_hook=None) -> torch.Tensor:
+             clock: PhaseClock = NULL_CLOCK, embed_hook=None, max_inflight: int = 0) -> torch.Tensor:
     """Forward + backward of one optimizer step into the LoRA gradient buffer.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
@@ -151,6 +151,8 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     already carry the chunk's weight.  Returns the summed loss on every stage.
     ``clock`` collects the stage timers (recv / send / compute / head / loss /
     backward, and the fill / steady / drain phases of the schedule).
+    ``max_inflight`` > 0 caps the micro-batches a stage holds activations for
+    (``graspoflow.pp_max_inflight_microbatches``).
     ``embed_hook`` (image inputs) edits the first stage's embeddings per
     micro-batch; with LoRA on the vision tower, the embedding gradient of
     each micro-batch's image rows is collected and sent through the tower
@@ -164,7 +166,10 @@ def pp_train(f: FusedQwen3, comm: StageComm, seq: torch.Tensor, mask: torch.Tens
     H = m.cfg.hidden_size
     full = _full_targets(targets)
     chunks = _chunks(B, chunk_rows)
-    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
+    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks),
+                           max_inflight)
+    clock.peak("pipeline_chunks_per_optimizer_step", len(chunks))
+    clock.peak("pipeline_peak_inflight_microbatches", peak_inflight([st for _, st in plan]))
     ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows * S // tp, H)), ACT_DTYPE)
     hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None and ps.is_first_stage else None
     graphs: dict[int, torch.Tensor] = {}  # micro-batch -> embeddings carrying the image-feature graph
@@ -289,7 +294,7 @@ def pp_logprobs_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.
 def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Tensor, targets: torch.Tensor,
                       loss_fn: Callable[[torch.Tensor, slice], torch.Tensor], *, chunk_rows: int,
                       schedule: str = "one_f_one_b", clock: PhaseClock = NULL_CLOCK,
-                      embed_hook=None) -> torch.Tensor:
+                      embed_hook=None, max_inflight: int = 0) -> torch.Tensor:
     """Forward + backward of one optimizer step into ``model.lora.grads``.
 
     ``loss_fn(logp_chunk [rows, S-1], row_slice)`` runs on the last stage and
@@ -301,7 +306,10 @@ def pp_train_autograd(model, comm: StageComm, seq: torch.Tensor, mask: torch.Ten
     B, S = seq.shape
     H = model.cfg.hidden_size
     chunks = _chunks(B, chunk_rows)
-    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks))
+    plan = schedule_phases(get_scheduler(schedule, pp_size=ps.pp_size, pp_rank=ps.pp_rank), len(chunks),
+                           max_inflight)
+    clock.peak("pipeline_chunks_per_optimizer_step", len(chunks))
+    clock.peak("pipeline_peak_inflight_microbatches", peak_inflight([st for _, st in plan]))
     lora = EagerLoRA(model.lora, requires_grad=True)
     ahead = _RecvAhead(comm, _plan_needs(plan, chunks, ps, lambda rows: (rows, S, H)), model.dtype)
     hooks = embed_hook.split_rows(seq, chunks) if embed_hook is not None else [None] * len(chunks)

@@ -9,9 +9,10 @@ compute and communicate (reference: backends/graspoflow/schedule.py:19-207).
   max_inflight)`` forwards, then alternating forward(k + warmup) /
   backward(k), then the remaining backwards; at most ``warmup + 1``
   micro-batches hold activations on a stage.
-* ``async_1f1b``: the 1F1B order; the executor posts receives one step ahead
-  and sends asynchronously on a communication stream, so transfers overlap
-  the next compute step (the reference's async variant is a placeholder).
+* ``async_1f1b``: the 1F1B order under its own name (the reference's async
+  variant is a placeholder).  Every schedule's executor already posts each
+  receive one step ahead and sends without blocking, on one communicator per
+  direction, so transfers overlap the neighbouring compute steps.
 """
 
 from __future__ import annotations

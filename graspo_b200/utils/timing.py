@@ -26,6 +26,7 @@ class PhaseClock:
         self.sync = bool(sync) and torch.cuda.is_available()
         self.sec: dict[str, float] = defaultdict(float)
         self.calls: dict[str, int] = defaultdict(int)
+        self.peaks: dict[str, int] = {}
 
     def now(self) -> float:
         if self.sync:
@@ -44,6 +45,10 @@ class PhaseClock:
     def add(self, key: str, seconds: float) -> None:
         self.sec[key] += seconds
 
+    def peak(self, key: str, value: int) -> None:
+        """Keep the largest ``value`` seen under ``key``."""
+        self.peaks[key] = max(int(value), self.peaks.get(key, int(value)))
+
     def summary(self, *, digits: int = 6) -> dict[str, float]:
         return {k: round(v, digits) for k, v in sorted(self.sec.items()) if v}
 
@@ -59,14 +64,19 @@ class _NullClock(PhaseClock):
     def add(self, key: str, seconds: float) -> None:
         return None
 
+    def peak(self, key: str, value: int) -> None:
+        return None
+
 
 NULL_CLOCK = _NullClock()
 
 
-def schedule_phases(scheduler, chunk_count: int) -> list[tuple[str, object]]:
+def schedule_phases(scheduler, chunk_count: int, max_inflight: int | None = None) -> list[tuple[str, object]]:
     """(phase, step) pairs of a pipeline plan: ``fill`` / ``steady`` / ``drain``
-    for 1F1B; GPipe's all-forwards run as ``fill`` and its backwards as ``drain``."""
-    phases = scheduler.plan_phases(chunk_count)
+    for 1F1B; GPipe's all-forwards run as ``fill`` and its backwards as ``drain``.
+    ``max_inflight`` (> 0) caps the 1F1B warm-up forwards, and with them the
+    micro-batches whose activations a stage holds at once."""
+    phases = scheduler.plan_phases(chunk_count, max_inflight=max_inflight or None)
     rename = {"forward": "fill", "backward": "drain", "all": "steady"}
     return [(rename.get(name, name), step) for name, steps in phases.items() for step in steps]
 

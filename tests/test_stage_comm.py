@@ -115,7 +115,7 @@ class _Recorder:
         self.program.append(("send", side, None))
 
 
-def _programs(pp, n_micro, schedule):
+def _programs(pp, n_micro, schedule, max_inflight=0):
     from graspo_b200.engine.pipeline import _plan_needs, _RecvAhead
     from graspo_b200.parallel.schedule import PipelineAction, get_scheduler
     from graspo_b200.utils.timing import schedule_phases
@@ -125,7 +125,7 @@ def _programs(pp, n_micro, schedule):
     for s in range(pp):
         rec = _Recorder(s, pp)
         ps = type("PS", (), {"is_first_stage": s == 0, "is_last_stage": s == pp - 1})()
-        plan = schedule_phases(get_scheduler(schedule, pp_size=pp, pp_rank=s), n_micro)
+        plan = schedule_phases(get_scheduler(schedule, pp_size=pp, pp_rank=s), n_micro, max_inflight)
         ahead = _RecvAhead(rec, _plan_needs(plan, chunks, ps, lambda rows: (rows,)), torch.float32)
         for k, (_, step) in enumerate(plan):
             ahead.advance(k)
@@ -191,10 +191,24 @@ def _runs_to_completion(progs, per_direction: bool) -> bool:
     return all(pc[r] == len(progs[r]) for r in range(pp)) and not any(queues.values())
 
 
-@pytest.mark.parametrize("pp,n_micro", [(2, 4), (4, 8), (8, 16)])
+@pytest.mark.parametrize("pp,n_micro", [(2, 4), (4, 8), (8, 16), (4, 3)])
 def test_direction_queues_cannot_deadlock(pp, n_micro):
     for schedule in ("one_f_one_b", "gpipe"):
         assert _runs_to_completion(_programs(pp, n_micro, schedule), per_direction=True), schedule
+    # graspoflow.pp_max_inflight_microbatches caps the 1F1B warm-up
+    for cap in (1, 2):
+        assert _runs_to_completion(_programs(pp, n_micro, "one_f_one_b", cap), per_direction=True), cap
+
+
+def test_inflight_cap_bounds_live_microbatches():
+    from graspo_b200.parallel.schedule import get_scheduler, peak_inflight
+    from graspo_b200.utils.timing import schedule_phases
+
+    for cap in (1, 2, 3):
+        plan = [step for _, step in schedule_phases(get_scheduler("one_f_one_b", pp_size=8, pp_rank=0), 16, cap)]
+        assert peak_inflight(plan) == cap + 1
+        assert sorted((s.action, s.microbatch_idx) for s in plan) == sorted(
+            [(a, i) for a in ("forward", "backward") for i in range(16)])
 
 
 def test_one_shared_queue_per_boundary_deadlocks_under_1f1b():
