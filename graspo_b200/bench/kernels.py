@@ -413,6 +413,79 @@ def bench_train(args) -> None:
     }), flush=True)
 
 
+def bench_hybrid(args) -> None:
+    """Training micro-batch of the Qwen3.5 hybrid family (``--layers`` layers of
+    the 9B shape, every fourth a gated-attention layer; ``--tiny`` for the test
+    shape): autograd forward to the selected-token log-probs with LoRA r=16 on
+    every linear of the decoder, then the backward into the LoRA factors, on
+    ``--rows`` x ``--seq`` tokens.  CUDA-event timed on a GPU, wall-clock
+    otherwise."""
+    import time
+
+    from graspo_b200.models.config import load_decoder_config, lora_available_targets
+    from graspo_b200.models.loader import SafetensorIndex
+    from graspo_b200.models.qwen3 import EagerLoRA
+    from graspo_b200.models.qwen35 import Qwen35Model
+    from graspo_b200.parallel.state import ParallelState
+    from graspo_b200.utils.synth import QWEN35_9B, QWEN35_TINY, write_qwen35_checkpoint
+
+    cuda = torch.cuda.is_available()
+    dev = torch.device("cuda", 0) if cuda else torch.device("cpu")
+    dims = dict(QWEN35_TINY if args.tiny else QWEN35_9B, num_hidden_layers=args.layers)
+    name = f"qwen35-{'tiny' if args.tiny else '9b'}-{args.layers}l"
+    path = write_qwen35_checkpoint(Path(args.ckpt) / name, dims, seed=7, with_tokenizer=False)
+    cfg = load_decoder_config(path)
+    model = Qwen35Model(cfg, SafetensorIndex(path), ps=ParallelState(device=dev),
+                        lora_targets=set(lora_available_targets(cfg)), lora_r=16, lora_alpha=32,
+                        lora_dropout=args.dropout, dtype=torch.bfloat16 if cuda else torch.float32, device=dev,
+                        seed=1)
+    B, S = args.rows, args.seq
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, dims["vocab_size"] - 8, (B, S), generator=g).to(dev)
+    mask = torch.ones(B, S, dtype=torch.bool, device=dev)
+    mask[0, : S // 8] = False
+    w = (torch.randn(B, S - 1, generator=g) * 1e-3).to(dev)
+
+    def mark():
+        if cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            return e
+        return time.perf_counter()
+
+    def ms(a, b):
+        return a.elapsed_time(b) if cuda else (b - a) * 1e3
+
+    def step():
+        lora = EagerLoRA(model.lora, requires_grad=True)
+        lp = model.sequence_logprobs(ids, mask, lora=lora, training=True)
+        mid = mark()
+        (lp.float() * w).sum().backward()
+        lora.accumulate_grads()
+        return mid
+
+    for _ in range(2):
+        step()
+    if cuda:
+        torch.cuda.synchronize()
+    times = []
+    for _ in range(args.iters):
+        t0 = mark()
+        t1 = step()
+        t2 = mark()
+        if cuda:
+            torch.cuda.synchronize()
+        times.append((ms(t0, t1), ms(t1, t2)))
+    times.sort(key=lambda t: t[0] + t[1])
+    fw, bw = times[len(times) // 2]
+    print(json.dumps({
+        "kernel": "hybrid_train_microbatch", "shape": "tiny" if args.tiny else "qwen3.5-9b", "layers": args.layers,
+        "rows": B, "seq": S, "device": str(dev), "fwd_ms": round(fw, 2), "bwd_ms": round(bw, 2),
+        "fwd_ms_per_layer": round(fw / args.layers, 3), "bwd_ms_per_layer": round(bw / args.layers, 3),
+        "tokens_per_s": round(B * S / ((fw + bw) / 1e3), 1),
+    }), flush=True)
+
+
 def bench_profile(args) -> None:
     """Small, fixed launches of one kernel family for an ncu capture (no timing).
 
@@ -560,10 +633,10 @@ def bench_profile(args) -> None:
     print(json.dumps({"profile": k, "launches": args.iters * len(runs)}), flush=True)
 
 
-def main() -> None:
+def main(argv: list[str] | None = None) -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("what", choices=["gemm", "decode", "dsweep", "attn", "push", "step", "train", "profile",
-                                         "all"])
+    parser.add_argument("what", choices=["gemm", "decode", "dsweep", "attn", "push", "step", "train", "hybrid",
+                                         "profile", "all"])
     parser.add_argument("--kernel", default="gemm")
     parser.add_argument("--iters", type=int, default=10)
     parser.add_argument("--tokens", type=int, default=64)
@@ -577,7 +650,8 @@ def main() -> None:
     parser.add_argument("--rows", type=int, default=8)
     parser.add_argument("--seq", type=int, default=3072)
     parser.add_argument("--dropout", type=float, default=0.1)
-    args = parser.parse_args()
+    parser.add_argument("--tiny", action="store_true", help="hybrid: the small test shape")
+    args = parser.parse_args(argv)
     if args.what in ("gemm", "all"):
         bench_gemm(args)
     if args.what in ("decode", "all"):
@@ -592,6 +666,8 @@ def main() -> None:
         bench_step(args)
     if args.what == "train":
         bench_train(args)
+    if args.what == "hybrid":
+        bench_hybrid(args)
     if args.what == "profile":
         bench_profile(args)
 

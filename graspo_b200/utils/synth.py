@@ -83,6 +83,15 @@ QWEN35_TINY = dict(
     linear_conv_kernel_dim=4, full_attention_interval=4, partial_rotary_factor=0.25,
 )
 
+# Qwen3.5-9B-shaped hybrid decoder (the dimensions transformers' Qwen3_5TextConfig
+# defaults to): three gated-DeltaNet layers per gated-attention layer
+QWEN35_9B = dict(
+    vocab_size=248320, hidden_size=4096, intermediate_size=12288, num_hidden_layers=32,
+    num_attention_heads=16, num_key_value_heads=4, head_dim=256,
+    linear_num_key_heads=16, linear_num_value_heads=32, linear_key_head_dim=128, linear_value_head_dim=128,
+    linear_conv_kernel_dim=4, full_attention_interval=4, partial_rotary_factor=0.25,
+)
+
 
 def _qwen35_tensor_specs(dims: dict) -> list[tuple[str, tuple[int, ...], str]]:
     H, I, V = dims["hidden_size"], dims["intermediate_size"], dims["vocab_size"]
