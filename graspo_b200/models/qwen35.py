@@ -92,15 +92,23 @@ def chunk_gated_delta(q, k, v, g, beta, state=None):
     u, w = sol[..., :dv], sol[..., dv:]
     S_t = torch.zeros(B, h, dk, dv, device=q.device, dtype=torch.float32) if state is None else state.float()
     attn = (q @ k.transpose(-1, -2)) * decay                                      # [B, h, n, C, C] (causal)
+    # Everything that does not depend on the carried state is computed for all
+    # chunks at once; the loop over chunks keeps only the state recurrence, as
+    # five batched products per chunk over the (batch, head) pairs.
+    BH = B * h
+    last = g[..., -1]                                                             # [B, h, n] log decay of a chunk
+    qg = (q * g.exp()[..., None]).reshape(BH, n, CHUNK, dk)                       # queries decayed to chunk start
+    kd = (k * (last[..., None] - g).exp()[..., None]).transpose(-1, -2).reshape(BH, n, dk, CHUNK)
+    el = last.exp().reshape(BH, n, 1, 1)
+    u, w, attn = u.reshape(BH, n, CHUNK, dv), w.reshape(BH, n, CHUNK, dk), attn.reshape(BH, n, CHUNK, CHUNK)
+    S_t = S_t.reshape(BH, dk, dv)
     outs = []
     for c in range(n):
-        u_c = u[:, :, c] - w[:, :, c] @ S_t                                       # new values after the state
-        outs.append((q[:, :, c] * g[:, :, c].exp()[..., None]) @ S_t + attn[:, :, c] @ u_c)
-        last = g[:, :, c, -1]
-        S_t = S_t * last.exp()[..., None, None] + \
-            (k[:, :, c] * (last[..., None] - g[:, :, c]).exp()[..., None]).transpose(-1, -2) @ u_c
-    o = torch.stack(outs, 2).reshape(B, h, n * CHUNK, dv)[:, :, :S]
-    return o.transpose(1, 2), S_t
+        u_c = torch.baddbmm(u[:, c], w[:, c], S_t, alpha=-1.0)                    # new values after the state
+        outs.append(torch.baddbmm(torch.bmm(attn[:, c], u_c), qg[:, c], S_t))
+        S_t = torch.baddbmm(S_t * el[:, c], kd[:, c], u_c)
+    o = torch.stack(outs, 1).reshape(B, h, n * CHUNK, dv)[:, :, :S]
+    return o.transpose(1, 2), S_t.reshape(B, h, dk, dv)
 
 
 def recurrent_gated_delta(q, k, v, g, beta, state):

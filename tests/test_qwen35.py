@@ -120,3 +120,39 @@ def test_hybrid_adapter_grpo_round_trip(tmp_path):
         assert metrics[key] > 0, key
     assert len(metrics["optimize_round_sec"]) == 1
     assert not torch.equal(before, api.adapter.model.lora.params)
+
+
+def test_chunked_delta_rule_gradients_match_recurrence():
+    """Gradients of the chunked form (the training path) equal those of a
+    functional token-by-token recurrence, initial state included."""
+    g = torch.Generator().manual_seed(1)
+    B, S, h, dk, dv = 1, 140, 2, 8, 12
+    qi = torch.randn(B, S, h, dk, generator=g)
+    ki = torch.randn(B, S, h, dk, generator=g)
+    v = torch.randn(B, S, h, dv, generator=g)
+    gl = -torch.rand(B, S, h, generator=g) * 0.5
+    beta = torch.rand(B, S, h, generator=g)
+    s0 = torch.randn(B, h, dk, dv, generator=g) * 0.1
+    wo = torch.randn(B, S, h, dv, generator=g)
+    wf = torch.randn(B, h, dk, dv, generator=g)
+    leaves = [t.clone().requires_grad_(True) for t in (qi, ki, v, gl, beta, s0)]
+
+    def loss_chunked(qi, ki, v, gl, beta, s0):
+        o, fin = chunk_gated_delta(l2norm(qi) / dk ** 0.5, l2norm(ki), v, gl, beta, s0)
+        return (o * wo).sum() + (fin * wf).sum()
+
+    def loss_recurrent(qi, ki, v, gl, beta, s0):
+        q, k = l2norm(qi) / dk ** 0.5, l2norm(ki)
+        st, outs = s0, []
+        for t in range(S):
+            st = st * gl[:, t].exp()[..., None, None]
+            mem = (st * k[:, t, :, :, None]).sum(-2)
+            delta = (v[:, t] - mem) * beta[:, t, :, None]
+            st = st + k[:, t, :, :, None] * delta[:, :, None, :]
+            outs.append((st * q[:, t, :, :, None]).sum(-2))
+        return (torch.stack(outs, 1) * wo).sum() + (st * wf).sum()
+
+    ga = torch.autograd.grad(loss_chunked(*leaves), leaves)
+    gb = torch.autograd.grad(loss_recurrent(*leaves), leaves)
+    for name, a, b in zip(("q", "k", "v", "g", "beta", "state"), ga, gb):
+        assert (a - b).abs().max().item() <= 1e-4 * (1 + b.abs().max().item()), name
