@@ -530,9 +530,15 @@ class Qwen35Model:
         return F.linear(norm1p(hidden, self.norm, self.cfg.rms_norm_eps).float(), self.lm_head.float())
 
     def token_logprobs(self, hidden, targets, chunk: int = 8192):
-        """log p(targets) from final hidden states, computed in token chunks."""
+        """log p(targets) from final hidden states.  On the GPU the vocabulary
+        GEMM keeps only per-row (max, sum-exp) partials and the target logit
+        (``ops/head.py``); on the CPU fp32 logits are formed in token chunks."""
+        from graspo_b200.ops.head import kernel_head_ok, selected_token_logprobs
+
         hn = norm1p(hidden, self.norm, self.cfg.rms_norm_eps)
         flat, tg = hn.reshape(-1, hn.shape[-1]), targets.reshape(-1)
+        if kernel_head_ok(flat, self.lm_head):
+            return selected_token_logprobs(flat, self.lm_head, tg, chunk_tokens=chunk).view(targets.shape)
         out = []
         for i in range(0, flat.shape[0], chunk):
             lg = F.linear(flat[i : i + chunk].float(), self.lm_head.float())
