@@ -102,11 +102,14 @@ def chunk_gated_delta(q, k, v, g, beta, state=None):
     el = last.exp().reshape(BH, n, 1, 1)
     u, w, attn = u.reshape(BH, n, CHUNK, dv), w.reshape(BH, n, CHUNK, dk), attn.reshape(BH, n, CHUNK, CHUNK)
     S_t = S_t.reshape(BH, dk, dv)
+    # unbind (one stack in the backward) rather than indexing chunk c of each
+    # tensor, whose backward would fill and add a full-size gradient per chunk
+    u, w, attn, qg, kd, el = (t.unbind(1) for t in (u, w, attn, qg, kd, el))
     outs = []
     for c in range(n):
-        u_c = torch.baddbmm(u[:, c], w[:, c], S_t, alpha=-1.0)                    # new values after the state
-        outs.append(torch.baddbmm(torch.bmm(attn[:, c], u_c), qg[:, c], S_t))
-        S_t = torch.baddbmm(S_t * el[:, c], kd[:, c], u_c)
+        u_c = torch.baddbmm(u[c], w[c], S_t, alpha=-1.0)                          # new values after the state
+        outs.append(torch.baddbmm(torch.bmm(attn[c], u_c), qg[c], S_t))
+        S_t = torch.baddbmm(S_t * el[c], kd[c], u_c)
     o = torch.stack(outs, 1).reshape(B, h, n * CHUNK, dv)[:, :, :S]
     return o.transpose(1, 2), S_t.reshape(B, h, dk, dv)
 
@@ -406,6 +409,13 @@ class Qwen35Model:
         Sk = k.shape[1]
         G = nq // nkv
         qh = q.transpose(1, 2)
+        if cache is None and Sk == S and bool(key_mask.all()):
+            # no padding: plain causal attention, which SDPA runs without a mask
+            # (and without copying the key / value heads for the query groups)
+            o = F.scaled_dot_product_attention(qh, k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                               scale=1.0 / math.sqrt(D), enable_gqa=G > 1)
+            o = o.transpose(1, 2).reshape(B, S, nq * D)
+            return self._lin(sigmoid_gate(o, gate), lay.w["o_proj"], lay, "fo", lora, training)
         kh = k.transpose(1, 2).repeat_interleave(G, 1)
         vh = v.transpose(1, 2).repeat_interleave(G, 1)
         qpos = torch.arange(Sk - S, Sk, device=h.device)
