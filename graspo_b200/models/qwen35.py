@@ -54,6 +54,19 @@ def norm1p(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return (y * (1.0 + w.float())).to(x.dtype)
 
 
+def _valid_span_start(mask: torch.Tensor) -> torch.Tensor | None:
+    """Per row, the first valid position when each row's valid tokens are one
+    contiguous span (None otherwise, or when a row has none)."""
+    B, S = mask.shape
+    lens = mask.sum(1)
+    start = mask.int().argmax(1)
+    ar = torch.arange(S, device=mask.device)
+    span = (ar[None] >= start[:, None]) & (ar[None] < (start + lens)[:, None])
+    if not bool(torch.equal(span, mask.bool()) and (lens > 0).all()):
+        return None
+    return start
+
+
 def gated_norm(x: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """w * rmsnorm(x) * silu(z); one kernel each way on CUDA (graspo_b200/ops/hybrid.py)."""
     from graspo_b200.ops.hybrid import gated_rmsnorm
@@ -409,12 +422,25 @@ class Qwen35Model:
         Sk = k.shape[1]
         G = nq // nkv
         qh = q.transpose(1, 2)
-        if cache is None and Sk == S and bool(key_mask.all()):
-            # no padding: plain causal attention, which SDPA runs without a mask
-            # (and without copying the key / value heads for the query groups)
-            o = F.scaled_dot_product_attention(qh, k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
-                                               scale=1.0 / math.sqrt(D), enable_gqa=G > 1)
-            o = o.transpose(1, 2).reshape(B, S, nq * D)
+        shift = _valid_span_start(key_mask) if cache is None and Sk == S else None
+        if shift is not None:
+            # Every row's valid tokens form one span (left-padded prompt, right-
+            # padded completion): rotate each row so its span starts at 0, run
+            # plain causal attention, which SDPA does without a mask (and without
+            # copying the key / value heads for the query groups), rotate back.
+            # Valid queries see exactly the valid keys before them; the outputs at
+            # padding positions differ from the masked form, and nothing reads them
+            # (the DeltaNet layers zero padding inputs, attention masks padding keys).
+            ar = torch.arange(S, device=h.device)
+            fwd = None if not bool(shift.any()) else (ar[None] + shift[:, None]) % S
+            qs, ks, vs = ((t if fwd is None else t.gather(1, fwd[:, :, None, None].expand_as(t))).transpose(1, 2)
+                          for t in (q, k, v))
+            o = F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, scale=1.0 / math.sqrt(D),
+                                               enable_gqa=G > 1).transpose(1, 2)
+            if fwd is not None:
+                back = (ar[None] - shift[:, None]) % S
+                o = o.gather(1, back[:, :, None, None].expand_as(o))
+            o = o.reshape(B, S, nq * D)
             return self._lin(sigmoid_gate(o, gate), lay.w["o_proj"], lay, "fo", lora, training)
         kh = k.transpose(1, 2).repeat_interleave(G, 1)
         vh = v.transpose(1, 2).repeat_interleave(G, 1)

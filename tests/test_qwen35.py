@@ -156,3 +156,44 @@ def test_chunked_delta_rule_gradients_match_recurrence():
     gb = torch.autograd.grad(loss_recurrent(*leaves), leaves)
     for name, a, b in zip(("q", "k", "v", "g", "beta", "state"), ga, gb):
         assert (a - b).abs().max().item() <= 1e-4 * (1 + b.abs().max().item()), name
+
+
+def test_full_attention_span_rotation_matches_masked(tmp_path):
+    """Rows whose valid tokens form one span (left and right padding) take the
+    rotated causal-attention path; their valid positions equal the explicitly
+    masked attention's, in values and LoRA gradients."""
+    from graspo_b200.models import qwen35 as q35
+    from graspo_b200.models.qwen3 import EagerLoRA
+
+    m = _model(tmp_path)
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 500, (3, 30), generator=g)
+    mask = torch.ones(3, 30, dtype=torch.bool)
+    mask[0, :6] = False
+    mask[1, -5:] = False
+    mask[2, :3] = False
+    mask[2, -4:] = False
+    assert q35._valid_span_start(mask).tolist() == [6, 0, 3]
+    w = torch.randn(3, 29, generator=g)
+    valid = mask[:, :-1] & mask[:, 1:]
+
+    def run():
+        m.lora.grads.zero_()
+        lora = EagerLoRA(m.lora, requires_grad=True)
+        lp = m.sequence_logprobs(ids, mask, lora=lora, training=True)
+        (lp * w * valid).sum().backward()
+        lora.accumulate_grads()
+        return lp.detach(), m.lora.grads.clone()
+
+    lp_rot, g_rot = run()
+    orig = q35._valid_span_start
+    q35._valid_span_start = lambda mask: None        # force the masked form
+    try:
+        lp_mask, g_mask = run()
+    finally:
+        q35._valid_span_start = orig
+    assert (lp_rot - lp_mask).abs()[valid].max().item() < 1e-4
+    assert (g_rot - g_mask).abs().max().item() <= 1e-4 * (1 + g_mask.abs().max().item())
+    holes = mask.clone()
+    holes[1, 10] = False
+    assert q35._valid_span_start(holes) is None
