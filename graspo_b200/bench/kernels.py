@@ -443,7 +443,8 @@ def bench_hybrid(args) -> None:
     g = torch.Generator().manual_seed(0)
     ids = torch.randint(0, dims["vocab_size"] - 8, (B, S), generator=g).to(dev)
     mask = torch.ones(B, S, dtype=torch.bool, device=dev)
-    mask[0, : S // 8] = False
+    if not args.no_pad:
+        mask[0, : S // 8] = False        # a left-padded first row
     w = (torch.randn(B, S - 1, generator=g) * 1e-3).to(dev)
 
     def mark():
@@ -478,11 +479,20 @@ def bench_hybrid(args) -> None:
         times.append((ms(t0, t1), ms(t1, t2)))
     times.sort(key=lambda t: t[0] + t[1])
     fw, bw = times[len(times) // 2]
+    if args.torch_profile and cuda:
+        # one more step under torch.profiler: a per-kernel breakdown, not a timing
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=30, max_name_column_width=70),
+              flush=True)
     print(json.dumps({
         "kernel": "hybrid_train_microbatch", "shape": "tiny" if args.tiny else "qwen3.5-9b", "layers": args.layers,
-        "rows": B, "seq": S, "device": str(dev), "fwd_ms": round(fw, 2), "bwd_ms": round(bw, 2),
-        "fwd_ms_per_layer": round(fw / args.layers, 3), "bwd_ms_per_layer": round(bw / args.layers, 3),
-        "tokens_per_s": round(B * S / ((fw + bw) / 1e3), 1),
+        "rows": B, "seq": S, "padded_first_row": not args.no_pad, "device": str(dev), "fwd_ms": round(fw, 2),
+        "bwd_ms": round(bw, 2), "fwd_ms_per_layer": round(fw / args.layers, 3),
+        "bwd_ms_per_layer": round(bw / args.layers, 3), "tokens_per_s": round(B * S / ((fw + bw) / 1e3), 1),
     }), flush=True)
 
 
@@ -651,6 +661,8 @@ def main(argv: list[str] | None = None) -> None:
     parser.add_argument("--seq", type=int, default=3072)
     parser.add_argument("--dropout", type=float, default=0.1)
     parser.add_argument("--tiny", action="store_true", help="hybrid: the small test shape")
+    parser.add_argument("--no-pad", action="store_true", help="hybrid: no left-padded row")
+    parser.add_argument("--torch-profile", action="store_true", help="hybrid: print a torch.profiler kernel table")
     args = parser.parse_args(argv)
     if args.what in ("gemm", "all"):
         bench_gemm(args)
