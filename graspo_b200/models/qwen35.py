@@ -563,7 +563,14 @@ class Qwen35Model:
         return x
 
     def logits(self, hidden):
-        return F.linear(norm1p(hidden, self.norm, self.cfg.rms_norm_eps).float(), self.lm_head.float())
+        """fp32 logits of the last hidden states (sampling); the head GEMM on the GPU."""
+        from graspo_b200.ops.head import kernel_head_ok, vocab_logits
+
+        hn = norm1p(hidden, self.norm, self.cfg.rms_norm_eps)
+        flat = hn.reshape(-1, hn.shape[-1])
+        if kernel_head_ok(flat, self.lm_head):
+            return vocab_logits(flat, self.lm_head).view(*hn.shape[:-1], -1)
+        return F.linear(hn.float(), self.lm_head.float())
 
     def token_logprobs(self, hidden, targets, chunk: int = 8192):
         """log p(targets) from final hidden states.  On the GPU the vocabulary

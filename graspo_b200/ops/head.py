@@ -12,6 +12,10 @@ for normed hidden states ``h`` [T, H] and a vocabulary projection ``weight`` [V,
   epilogue writes ``g * (onehot(target) - softmax)`` in bf16, which a second
   GEMM multiplies by ``weight``.
 
+``vocab_logits(h, weight)`` gives the fp32 logits of a few rows (sampling):
+the same GEMM with an fp32 store, the vocabulary on the MMA rows when there
+are at most 128 tokens.
+
 The reference computes fp32 logits chunk by chunk and takes gather - logsumexp
 (src/graspo/backends/graspoflow/tensor_utils.py:167-186).  The families whose
 decoder is a PyTorch module (the Qwen3.5 hybrid) use this for their LM head;
@@ -81,3 +85,13 @@ def selected_token_logprobs(h: torch.Tensor, weight: torch.Tensor, targets: torc
         raise ValueError("selected_token_logprobs takes bf16 CUDA tensors with H and V multiples of 64")
     return _SelectedTokenLogprob.apply(h.contiguous(), weight.contiguous(), targets.reshape(-1).long().contiguous(),
                                        chunk_tokens)
+
+
+def vocab_logits(h: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """fp32 logits ``h @ weight^T`` [T, V] (bf16 operands, fp32 accumulation and store)."""
+    if not kernel_head_ok(h, weight):
+        raise ValueError("vocab_logits takes bf16 CUDA tensors with H and V multiples of 64")
+    h = h.contiguous()
+    if h.shape[0] <= _ROWS:
+        return gemm(weight.contiguous(), h, swap=True, epilogue="store_f32")
+    return gemm(h, weight.contiguous(), epilogue="store_f32")

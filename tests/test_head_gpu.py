@@ -28,3 +28,17 @@ def test_selected_token_logprobs_matches_fp32():
     # the backward's softmax-grad chunk is stored in bf16
     err = (hk.grad.float() - hr.grad).abs().max().item()
     assert err < 2e-2 * hr.grad.abs().max().item(), err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows", [5, 200])
+def test_vocab_logits_matches_fp32(rows):
+    from graspo_b200.ops.head import vocab_logits
+
+    g = torch.Generator().manual_seed(rows)
+    h = (torch.randn(rows, 256, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    w = (torch.randn(1024, 256, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    out = vocab_logits(h, w)
+    ref = h.float() @ w.float().T
+    assert out.dtype == torch.float32 and out.shape == (rows, 1024)
+    assert (out - ref).abs().max().item() < 1e-3
