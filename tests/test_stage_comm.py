@@ -216,3 +216,32 @@ def test_one_shared_queue_per_boundary_deadlocks_under_1f1b():
     # single queue, 1F1B stalls (stage 0's gradient receive sits in front of
     # its next forward send while stage 1 waits for that send)
     assert not _runs_to_completion(_programs(2, 4, "one_f_one_b"), per_direction=False)
+
+
+def _leaving_stage_worker(rank, world, timeout_sec):
+    """Stage 1 leaves between steps (exits without posting its receive); stage 0's
+    next transfer with it must end with an error, not wait for ever."""
+    import time
+
+    from graspo_b200.parallel import state as pstate
+    from graspo_b200.parallel.p2p import StageComm
+
+    ps = pstate.initialize(1, 2, 0, timeout_sec=timeout_sec, device="cpu")
+    comm = StageComm(ps)
+    comm.send_next(torch.ones(8))                    # one completed step
+    if rank == 1:
+        assert torch.equal(comm.recv_prev((8,), torch.float32), torch.ones(8))
+        return                                       # leaves; no destroy, no further collectives
+    comm.flush()
+    t0 = time.monotonic()
+    try:
+        comm.recv_next((1 << 16,), torch.float32)    # the gradient that never comes
+    except RuntimeError:
+        elapsed = time.monotonic() - t0
+        assert elapsed < timeout_sec + 30, elapsed
+        return
+    raise AssertionError("a receive from a stage that left returned normally")
+
+
+def test_stage_that_leaves_ends_the_neighbours_transfer():
+    run_world(2, _leaving_stage_worker, 10.0, timeout=120)
