@@ -1,5 +1,5 @@
 """The ``graspo`` standard-library logging channel (reference: ``logs/training.log``,
-README.md:491-513).
+described at lines 491-513 of the reference project's own README).
 
 Console output (INFO) on every rank; ``<output_dir>/logs/training.log`` (DEBUG)
 on rank 0.  Calling it again for the same directory is harmless.
