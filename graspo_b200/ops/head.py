@@ -83,6 +83,8 @@ def selected_token_logprobs(h: torch.Tensor, weight: torch.Tensor, targets: torc
     """log p(targets) [T] (fp32) of ``h`` [T, H] under the vocabulary projection ``weight`` [V, H]."""
     if not kernel_head_ok(h, weight):
         raise ValueError("selected_token_logprobs takes bf16 CUDA tensors with H and V multiples of 64")
+    if h.shape[0] == 0:
+        return (h.sum(-1) * 0).float()                    # no tokens: an empty result tied to h
     return _SelectedTokenLogprob.apply(h.contiguous(), weight.contiguous(), targets.reshape(-1).long().contiguous(),
                                        chunk_tokens)
 
