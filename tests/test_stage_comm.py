@@ -11,9 +11,10 @@ from tests.dist_util import run_world
 
 
 def _expected(c: int, stage: int, backward: bool) -> float:
-    # forward: micro-batch c leaves stage s carrying c * 100 + s + 1;
-    # backward: its gradient leaves stage s carrying -(c * 100 + s + 1)
-    v = float(c * 100 + stage + 1)
+    # forward: micro-batch c leaves stage s carrying c * 16 + s + 1;
+    # backward: its gradient leaves stage s carrying -(c * 16 + s + 1)
+    # (small integers, exact in bf16)
+    v = float(c * 16 + stage + 1)
     return -v if backward else v
 
 
